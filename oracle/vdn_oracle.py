@@ -1,0 +1,623 @@
+"""CPU float64 restatement of the VDN-H3 hybrid attention block forward.
+
+TEST INFRASTRUCTURE ONLY.  This module is the parity checker for the CUDA path.
+Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` / ``--impl
+reference`` legs of ``bench.py`` may import it, and only to check or to time a CPU
+baseline.  The product path (the ``comfyui-kirei-vdn-h3_b200`` package and its C-ABI
+library) never calls into it.
+
+Every function restates the algorithm of hyukudan/ComfyUI-Kirei-VDN-H3 v0.3.3; the
+reference file:line it follows is cited in each docstring (paths inside that project).
+Arithmetic is float64 throughout so the oracle is an upper-precision stand-in for the
+reference's fp32 CPU path and bf16 GPU path alike.
+
+Pinning: ``tests/golden/make_golden.py`` runs the reference itself (its own torch code,
+imported read-only where it is mounted) on seeded config-0 inputs and stores the outputs
+under ``tests/golden/``; ``tests/test_oracle_golden.py`` checks this module against them.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+F64 = torch.float64
+ANCHOR_MODES = ("none", "columns", "rows", "both")
+TEXT_STATE_SCALE = 0.5  # branch.py:23
+FP8_MAX = 448.0  # fp8.py:30 (float8_e4m3fn max)
+
+
+def _t(x) -> torch.Tensor:
+    if isinstance(x, np.ndarray):
+        x = torch.from_numpy(x)
+    return x.detach().to("cpu", F64)
+
+
+# ---------------------------------------------------------------------------------------
+# Geometry (window.py:141-178, layout.py:19-41)
+# ---------------------------------------------------------------------------------------
+
+def window_bounds(num_frames: int, radius: int, chunk: int = 0) -> list[tuple[int, int]]:
+    """Per-frame inclusive key-frame range (window.py:141-153)."""
+    if num_frames < 0 or radius < 0:
+        raise ValueError("num_frames and radius must be non-negative")
+    out = []
+    for f in range(num_frames):
+        if chunk <= 0:
+            out.append((f - radius, f + radius))
+        else:
+            base = f // chunk
+            out.append(((base - radius) * chunk, (base + radius + 1) * chunk - 1))
+    return out
+
+
+def full_coverage(bounds, num_frames) -> bool:
+    """window.py:156-159."""
+    return all(lo <= 0 and hi >= num_frames - 1 for lo, hi in bounds)
+
+
+@dataclass(frozen=True)
+class Layout:
+    """Packed-sequence geometry (layout.py:19-41)."""
+
+    seq_len: int
+    video_start: int
+    video_end: int
+    num_frames: int
+    tokens_per_frame: int
+    frame_size: tuple[int, int]
+    text_start: int
+    text_len: int
+    bounds: tuple = ()
+    full_cover: bool = False
+    anchor_frames: str = "both"
+
+
+def make_layout(text_len, num_frames, grid, *, radius=1, chunk=5, anchor_frames="both",
+                text_first=True) -> Layout:
+    gh, gw = grid
+    tpf = gh * gw
+    video = num_frames * tpf
+    if text_first:
+        ts, vs = 0, text_len
+    else:
+        vs, ts = 0, video
+    bounds = tuple(window_bounds(num_frames, radius, chunk))
+    return Layout(
+        seq_len=text_len + video, video_start=vs, video_end=vs + video,
+        num_frames=num_frames, tokens_per_frame=tpf, frame_size=(gh, gw),
+        text_start=ts, text_len=text_len, bounds=bounds,
+        full_cover=full_coverage(bounds, num_frames), anchor_frames=anchor_frames,
+    )
+
+
+# ---------------------------------------------------------------------------------------
+# Window softmax (window.py:277-344; tests/test_window.py:41-69)
+# ---------------------------------------------------------------------------------------
+
+def allowed_mask(seq, vs, ve, num_frames, tpf, bounds, anchors) -> torch.Tensor:
+    """Boolean [seq, seq] mask of allowed (query, key) pairs (window.py:327-344)."""
+    rows = torch.arange(seq)
+    glob = (rows < vs) | (rows >= ve)
+    frame = torch.div(rows - vs, tpf, rounding_mode="floor")
+    lo = torch.zeros(seq, dtype=torch.long)
+    hi = torch.full((seq,), num_frames - 1, dtype=torch.long)
+    for f, (a, b) in enumerate(bounds):
+        s = vs + f * tpf
+        lo[s:s + tpf] = max(a, 0)
+        hi[s:s + tpf] = min(b, num_frames - 1)
+    kf = frame[None, :]
+    allowed = glob[:, None] | glob[None, :] | ((kf >= lo[:, None]) & (kf <= hi[:, None]))
+    if anchors in ("columns", "both"):
+        allowed = allowed | ((kf == 0) | (kf == num_frames - 1))
+    if anchors in ("rows", "both"):
+        qf = frame[:, None]
+        allowed = allowed | ((qf == 0) | (qf == num_frames - 1))
+    return allowed
+
+
+def window_attention(q, k, v, vs, ve, num_frames, tpf, bounds, scale, anchors="none",
+                     rows=None) -> torch.Tensor:
+    """Exact masked softmax attention, float64 (window.py:277-313 semantics).
+
+    ``q,k,v``: [S, H, D].  ``rows`` optionally restricts which query rows are computed
+    (a 1-D index tensor); the result then has one entry per requested row.
+    """
+    q, k, v = _t(q), _t(k), _t(v)
+    seq = q.shape[0]
+    mask = allowed_mask(seq, vs, ve, num_frames, tpf, bounds, anchors)
+    if rows is not None:
+        rows = torch.as_tensor(rows, dtype=torch.long)
+        q = q[rows]
+        mask = mask[rows]
+    logits = torch.einsum("qhd,khd->hqk", q, k) * scale
+    logits = logits.masked_fill(~mask[None], float("-inf"))
+    p = torch.softmax(logits, dim=-1)
+    return torch.einsum("hqk,khd->qhd", p, v)
+
+
+def key_count_per_row(seq, vs, ve, num_frames, tpf, bounds, anchors) -> np.ndarray:
+    """Allowed keys per query row, computed from intervals (no [S,S] mask)."""
+    out = np.empty(seq, dtype=np.int64)
+    glob = vs + (seq - ve)
+    out[:vs] = seq
+    out[ve:] = seq
+    last = num_frames - 1
+    for f in range(num_frames):
+        s = vs + f * tpf
+        if anchors in ("rows", "both") and f in (0, last):
+            out[s:s + tpf] = seq
+            continue
+        lo, hi = max(bounds[f][0], 0), min(bounds[f][1], last)
+        frames = set(range(lo, hi + 1))
+        if anchors in ("columns", "both"):
+            frames.update((0, last))
+        out[s:s + tpf] = glob + len(frames) * tpf
+    return out
+
+
+# ---------------------------------------------------------------------------------------
+# Branch pieces (kernels.py, branch.py, runtime.py)
+# ---------------------------------------------------------------------------------------
+
+def activate(x, l2norm: bool) -> torch.Tensor:
+    """SiLU then optional L2 over the last dim, eps 1e-6 (kernels.py:47-51)."""
+    y = F.silu(_t(x))
+    if l2norm:
+        y = y / y.norm(dim=-1, keepdim=True).clamp_min(1e-6)
+    return y
+
+
+def temporal_shift(x, w) -> torch.Tensor:
+    """Zero-padded depthwise temporal conv over axis 0 (kernels.py:59-68).
+
+    ``x``: [T, S_frame, C]; ``w``: [C, taps] with taps odd.
+    """
+    x, w = _t(x), _t(w)
+    taps = w.shape[-1]
+    pad = taps // 2
+    xp = F.pad(x, (0, 0, 0, 0, pad, pad))
+    out = torch.zeros_like(x)
+    for dt in range(taps):
+        out += xp[dt:dt + x.shape[0]] * w[:, dt].view(1, 1, -1)
+    return out
+
+
+def conv_features(tokens, spatial_w, temporal_w, num_frames, frame_size, l2norm) -> torch.Tensor:
+    """Depthwise spatial conv per frame, temporal 5-tap conv, SiLU, L2 (branch.py:443-480).
+
+    ``tokens``: [F*gh*gw, H, D]; returns [F, H, gh*gw, D] (the FHSD layout).
+    """
+    tokens = _t(tokens)
+    heads, dim = tokens.shape[-2:]
+    gh, gw = frame_size
+    ch = heads * dim
+    vol = tokens.reshape(num_frames, gh, gw, ch).permute(0, 3, 1, 2)
+    sw = _t(spatial_w)
+    kh, kw = sw.shape[-2:]
+    vol = F.conv2d(vol, sw, padding=(kh // 2, kw // 2), groups=ch)
+    flat = vol.permute(0, 2, 3, 1).reshape(num_frames, gh * gw, ch)
+    tm = temporal_shift(flat, _t(temporal_w).reshape(ch, -1))
+    y = activate(tm.reshape(num_frames, gh * gw, heads, dim), l2norm)
+    return y.permute(0, 2, 1, 3).contiguous()
+
+
+def to_fhsd(tokens, num_frames) -> torch.Tensor:
+    t = _t(tokens)
+    rows, h, d = t.shape
+    return t.reshape(num_frames, rows // num_frames, h, d).permute(0, 2, 1, 3).contiguous()
+
+
+def frame_statistics(key, value, beta) -> tuple[torch.Tensor, torch.Tensor]:
+    """A = sym((beta*K)^T K), B = (beta*V)^T K per frame/head (branch.py:197-243)."""
+    key, value, beta = _t(key), _t(value), _t(beta)
+    a = torch.einsum("fhsk,fhsl,fhs->fhkl", key, key, beta)
+    a = 0.5 * (a + a.transpose(-1, -2))
+    b = torch.einsum("fhsv,fhsk,fhs->fhvk", value, key, beta)
+    return a, b
+
+
+def alpha_gate(frame_mean, w_down, w_up, dt_bias, a_log, heads, dim) -> torch.Tensor:
+    """alpha = exp(-exp(A_log) * softplus(up(down(mean)) + dt_bias)) (branch.py:483-491)."""
+    m = _t(frame_mean)
+    delta = m @ _t(w_down).T
+    delta = delta @ _t(w_up).T + _t(dt_bias)
+    decay = torch.exp(_t(a_log)).reshape(heads, 1)
+    return torch.exp(-decay * F.softplus(delta.reshape(-1, heads, dim)))
+
+
+def cholesky_info(a) -> torch.Tensor:
+    """First failing leading-minor order per matrix of I+A (0 = SPD); cholesky_ex semantics."""
+    m = _t(a)
+    n = m.shape[-1]
+    flat = (m + torch.eye(n, dtype=F64)).reshape(-1, n, n)
+    info = torch.zeros(flat.shape[0], dtype=torch.int32)
+    for i in range(flat.shape[0]):
+        _, inf = torch.linalg.cholesky_ex(flat[i])
+        info[i] = int(inf)
+    return info.reshape(m.shape[:-2])
+
+
+def factor_apply(alpha, a, b) -> tuple[torch.Tensor, torch.Tensor]:
+    """T = alpha[...,None] * (I+A)^-1, Inj = B (I+A)^-1 via Cholesky (branch.py:148-160)."""
+    a, b, alpha = _t(a), _t(b), _t(alpha)
+    n = a.shape[-1]
+    eye = torch.eye(n, dtype=F64).expand_as(a)
+    chol = torch.linalg.cholesky(a + eye)
+    inv_chol = torch.linalg.solve_triangular(chol, eye, upper=False, left=True)
+    inverse = inv_chol.transpose(-1, -2) @ inv_chol
+    return alpha.unsqueeze(-1) * inverse, b @ inverse
+
+
+def sana_factor_apply(alpha, a, b, tokens) -> tuple[torch.Tensor, torch.Tensor]:
+    """T = alpha*(I - A/tpf), Inj = B/sqrt(tpf) (branch.py:163-177)."""
+    a, b, alpha = _t(a), _t(b), _t(alpha)
+    eye = torch.eye(a.shape[-1], dtype=F64)
+    return alpha.unsqueeze(-1) * (eye - a / tokens), b / math.sqrt(tokens)
+
+
+def run_scans(transition, injection, initial) -> tuple[torch.Tensor, torch.Tensor]:
+    """prefix_t = Inj_t + prefix_{t-1} T_t (t up), suffix likewise (t down) (branch.py:297-312)."""
+    frames = transition.shape[0]
+    prefix = torch.empty_like(injection)
+    suffix = torch.empty_like(injection)
+    state = initial
+    for f in range(frames):
+        state = injection[f] + state @ transition[f]
+        prefix[f] = state
+    state = initial
+    for f in range(frames - 1, -1, -1):
+        state = injection[f] + state @ transition[f]
+        suffix[f] = state
+    return prefix, suffix
+
+
+def gather_linear_state(prefix, suffix, alpha, bounds, bridge="alpha", text_state=None):
+    """Window-bridged linear state per frame (branch.py:345-396)."""
+    frames = prefix.shape[0]
+    log_prefix = torch.cat((torch.zeros_like(alpha[:1]), alpha.clamp_min(1e-12).log().cumsum(0)))
+    zero = torch.zeros_like(prefix[0])
+    out = []
+    for f, (raw_lo, raw_hi) in enumerate(bounds):
+        lo, hi = max(raw_lo, 0), min(raw_hi, frames - 1)
+        has_before, has_after = raw_lo - 1 >= 0, raw_hi + 1 < frames
+        fallback = zero if text_state is None else text_state
+        before = prefix[lo - 1] if has_before else fallback
+        after = suffix[hi + 1] if has_after else fallback
+        if bridge == "alpha":
+            before = before * torch.exp(log_prefix[f + 1] - log_prefix[lo]).unsqueeze(1)
+            after = after * torch.exp(log_prefix[hi + 1] - log_prefix[f]).unsqueeze(1)
+        out.append(before + after)
+    return torch.stack(out)
+
+
+def rms_norm(x, weight, eps=1e-6) -> torch.Tensor:
+    """x * rsqrt(mean(x^2) + eps) * weight over the last dim (branch.py:494-498)."""
+    x = _t(x)
+    ms = x.square().mean(dim=-1, keepdim=True)
+    return x * torch.rsqrt(ms + eps) * _t(weight)
+
+
+@dataclass
+class BranchConfig:
+    """Released-lineage branch structure (docs/ARCHITECTURE.md:70-82, spec.py:297-353)."""
+
+    delta_rule: str = "vdn_solve"
+    bridge: str = "alpha"
+    short_conv: tuple = ("k", "v")
+    enable_text_state: bool = True
+
+
+def text_state(weights, text_x, text_k, text_v, heads, dim, cfg: BranchConfig):
+    """Text rows as one extra 'frame', alpha = 1, S0 = 0.5 * Inj (branch.py:649-670)."""
+    if not cfg.enable_text_state or text_x is None:
+        return None
+    length = text_x.shape[0]
+    key = activate(text_k, True).reshape(1, length, heads, dim).permute(0, 2, 1, 3)
+    val = activate(text_v, False).reshape(1, length, heads, dim).permute(0, 2, 1, 3)
+    beta = torch.sigmoid(_t(text_x) @ _t(weights["beta_proj.weight"]).T)
+    beta = beta.reshape(1, length, heads).permute(0, 2, 1)
+    a, b = frame_statistics(key, val, beta)
+    ones = torch.ones(1, heads, dim, dtype=F64)
+    if cfg.delta_rule == "vdn_solve":
+        _, inj = factor_apply(ones, a, b)
+    else:
+        _, inj = sana_factor_apply(ones, a, b, length)
+    return TEXT_STATE_SCALE * inj[0]
+
+
+def branch_readout(weights, xv, q_raw, k_raw, v_raw, num_frames, tpf, bounds, frame_size,
+                   heads, dim, cfg: BranchConfig, text_x=None, text_k=None, text_v=None,
+                   skip_ends=False, return_parts=False):
+    """Linear-branch readout before ``to_out_linear`` (branch.py:672-785; runtime.py:545-607).
+
+    Returns [F*tpf, H*D] (rows of skipped end frames are zero).
+    """
+    xv = _t(xv)
+    rows_total = num_frames * tpf
+    if skip_ends:
+        if num_frames <= 2:
+            return torch.zeros(rows_total, heads * dim, dtype=F64)
+        inner = slice(tpf, (num_frames - 1) * tpf)
+        inner_out = branch_readout(
+            weights, xv[inner], _t(q_raw)[inner], _t(k_raw)[inner], _t(v_raw)[inner],
+            num_frames - 2, tpf, [(lo - 1, hi - 1) for lo, hi in bounds[1:-1]], frame_size,
+            heads, dim, cfg, text_x, text_k, text_v, skip_ends=False, return_parts=return_parts,
+        )
+        parts = None
+        if return_parts:
+            inner_out, parts = inner_out
+        out = torch.zeros(rows_total, heads * dim, dtype=F64)
+        out[inner] = inner_out
+        return (out, parts) if return_parts else out
+    w = weights
+
+    def feature(tokens, name):
+        l2 = name != "v"
+        if name in cfg.short_conv:
+            return conv_features(tokens, w[f"short_conv.{name}_sp.weight"],
+                                 w[f"short_conv.{name}_tm.weight"], num_frames, frame_size, l2)
+        return to_fhsd(activate(tokens, l2), num_frames)
+
+    qf, kf, vf = feature(q_raw, "q"), feature(k_raw, "k"), feature(v_raw, "v")
+    beta = torch.sigmoid(xv @ _t(w["beta_proj.weight"]).T)
+    beta = beta.reshape(num_frames, tpf, heads).permute(0, 2, 1)
+    a, b = frame_statistics(kf, vf, beta)
+    frame_mean = xv.reshape(num_frames, tpf, -1).mean(dim=1)
+    alpha = alpha_gate(frame_mean, w["alpha.down.weight"], w["alpha.up.weight"],
+                       w["alpha.dt_bias"], w["alpha.A_log"], heads, dim)
+    s0 = text_state(w, text_x, text_k, text_v, heads, dim, cfg)
+    if cfg.delta_rule == "vdn_solve":
+        trans, inj = factor_apply(alpha, a, b)
+    else:
+        trans, inj = sana_factor_apply(alpha, a, b, tpf)
+    init = torch.zeros_like(inj[0]) if s0 is None else s0
+    prefix, suffix = run_scans(trans, inj, init)
+    gate = torch.sigmoid(
+        (xv @ _t(w["output_gate.down.weight"]).T) @ _t(w["output_gate.up.weight"]).T
+        + _t(w["output_gate.up.bias"])
+    )
+    state = gather_linear_state(prefix, suffix, alpha, bounds, cfg.bridge, s0)
+    readout = qf @ state.transpose(-1, -2)
+    normed = rms_norm(readout, w["norm.weight"], 1e-6)
+    out = normed.permute(0, 2, 1, 3).reshape(rows_total, heads * dim) * gate
+    if return_parts:
+        parts = dict(q=qf, k=kf, v=vf, beta=beta, A=a, B=b, alpha=alpha, text_state=s0,
+                     prefix=prefix, suffix=suffix, state=state, gate=gate, readout=readout)
+        return out, parts
+    return out
+
+
+# ---------------------------------------------------------------------------------------
+# Projections (projection.py:259-268, fp8.py:84-266) and the config-2 INT8 scheme
+# ---------------------------------------------------------------------------------------
+
+def round_half_even(x: torch.Tensor) -> torch.Tensor:
+    return torch.round(x)  # torch.round is round-half-to-even
+
+
+def int8_quantize_weight(w) -> tuple[torch.Tensor, torch.Tensor]:
+    """Symmetric per-output-channel int8: scale = amax/127, q = rne(w/scale) (config 2)."""
+    w32 = _t(w).to(torch.float32)
+    scale = (w32.abs().amax(dim=1) / 127.0).clamp_min(1e-12)
+    q = round_half_even(w32 / scale[:, None]).clamp(-127, 127).to(torch.int8)
+    return q, scale
+
+
+def int8_quantize_rows(x) -> tuple[torch.Tensor, torch.Tensor]:
+    """Dynamic per-token int8 of fp32 rows, same rule as the weights (config 2).
+
+    The scale is computed and applied in fp32 (amax * (1/127) and x * (1/scale) are
+    not used): scale = max(amax / 127, 1e-12); q = rne(x / scale) clamped to +-127.
+    """
+    x32 = _t(x).to(torch.float32)
+    scale = (x32.abs().amax(dim=1) / 127.0).clamp_min(1e-12)
+    q = round_half_even(x32 / scale[:, None]).clamp(-127, 127).to(torch.int8)
+    return q, scale
+
+
+def int8_accumulate(qa: torch.Tensor, qw: torch.Tensor) -> torch.Tensor:
+    """Exact int32 accumulator of int8 operands, computed in int64 then checked to fit."""
+    acc = qa.to(torch.int64) @ qw.to(torch.int64).T
+    if acc.abs().max() >= 2**31:
+        raise OverflowError("int8 accumulator exceeds int32")
+    return acc.to(torch.int32)
+
+
+def fp8_quantize_tensor(x) -> tuple[torch.Tensor, float]:
+    """Per-tensor e4m3: scale = max(amax/448, 1e-12); q = clamp(x/scale) (fp8.py:88-105)."""
+    x32 = _t(x).to(torch.float32)
+    scale = max(float(x32.abs().max()) / FP8_MAX, 1e-12)
+    q = (x32 / torch.tensor(scale, dtype=torch.float32)).clamp(-FP8_MAX, FP8_MAX)
+    return q.to(torch.float8_e4m3fn), scale
+
+
+def project(rows, w, precision="bf16"):
+    """``rows @ W^T`` under the chosen precision; float64 result (projection.py:259-268)."""
+    if precision == "bf16" or precision == "fp64":
+        return _t(rows) @ _t(w).T
+    if precision == "int8":
+        qa, sa = int8_quantize_rows(rows)
+        qw, sw = int8_quantize_weight(w)
+        acc = int8_accumulate(qa, qw).to(F64)
+        return acc * sa.to(F64)[:, None] * sw.to(F64)[None, :]
+    if precision == "fp8":
+        qa, sa = fp8_quantize_tensor(rows)
+        qw, sw = fp8_quantize_tensor(w)
+        return (qa.to(F64) @ qw.to(F64).T) * (sa * sw)
+    raise ValueError(f"unknown precision {precision!r}")
+
+
+# ---------------------------------------------------------------------------------------
+# Whole block (hybrid.py:409-579)
+# ---------------------------------------------------------------------------------------
+
+@dataclass
+class BlockWeights:
+    """One H3 attention block plus its VDN branch weights (spec.py:471-486)."""
+
+    qkv: torch.Tensor  # [3*H*D, hidden]
+    q_norm: torch.Tensor  # [D]
+    k_norm: torch.Tensor  # [D]
+    out: torch.Tensor  # [hidden, H*D]
+    branch: dict = field(default_factory=dict)
+
+
+def block_forward(x, bw: BlockWeights, lay: Layout, heads, dim, cfg: BranchConfig,
+                  *, enable_softmax_gate=True, linear_enabled=True, precision="bf16",
+                  return_parts=False):
+    """VDN hybrid block forward: QKV, branch on raw video q/k/v, q/k RMSNorm, window
+    softmax, per-token head gate, out_proj, delta add on video rows (hybrid.py:409-579).
+
+    ``precision`` selects the projection arithmetic of qkv/out_proj/to_out_linear
+    (``bf16`` = exact float64 here; ``int8``/``fp8`` = the config-2 quantised schemes).
+    """
+    x = _t(x)
+    seq = x.shape[0]
+    inner = heads * dim
+    qkv = project(x, bw.qkv, precision)
+    q_raw = qkv[:, :inner].reshape(seq, heads, dim)
+    k_raw = qkv[:, inner:2 * inner].reshape(seq, heads, dim)
+    v = qkv[:, 2 * inner:].reshape(seq, heads, dim)
+    w = bw.branch
+    linear_active = linear_enabled and not lay.full_cover
+    delta = None
+    parts = {}
+    if linear_active:
+        va, vb = lay.video_start, lay.video_end
+        ta, tb = lay.text_start, lay.text_start + lay.text_len
+        text = cfg.enable_text_state and lay.text_len > 0
+        readout = branch_readout(
+            w, x[va:vb], q_raw[va:vb], k_raw[va:vb], v[va:vb], lay.num_frames,
+            lay.tokens_per_frame, list(lay.bounds), lay.frame_size, heads, dim, cfg,
+            text_x=x[ta:tb] if text else None, text_k=k_raw[ta:tb] if text else None,
+            text_v=v[ta:tb] if text else None, skip_ends=(lay.anchor_frames == "both"),
+        )
+        delta = project(readout, w["to_out_linear.weight"], precision)
+        parts["readout"] = readout
+    qn = rms_norm(q_raw, bw.q_norm, 1e-6)
+    kn = rms_norm(k_raw, bw.k_norm, 1e-6)
+    scale = dim ** -0.5
+    if lay.full_cover:
+        soft = window_attention(qn, kn, v, 0, seq, 1, seq, [(0, 0)], scale, "none")
+    else:
+        soft = window_attention(qn, kn, v, lay.video_start, lay.video_end, lay.num_frames,
+                                lay.tokens_per_frame, list(lay.bounds), scale, lay.anchor_frames)
+    parts["softmax"] = soft
+    if enable_softmax_gate:
+        g = torch.sigmoid(x @ _t(w["softmax_gate.up.weight"]).T + _t(w["softmax_gate.up.bias"]))
+        flat = (soft * g.reshape(seq, heads, 1)).reshape(seq, inner)
+        parts["gate"] = g
+    else:
+        flat = soft.reshape(seq, inner)
+    out = project(flat, bw.out, precision)
+    if delta is not None:
+        out[lay.video_start:lay.video_end] += delta
+        parts["delta"] = delta
+    return (out, parts) if return_parts else out
+
+
+# ---------------------------------------------------------------------------------------
+# Seeded synthetic inputs (SURVEY-free restatement of the shapes)
+# ---------------------------------------------------------------------------------------
+
+def make_branch_weights(gen, hidden, heads, dim, *, std=0.02, kernel=5, gate=True,
+                        short_conv=("k", "v")) -> dict:
+    ch = heads * dim
+
+    def n(*shape, s=std, mean=0.0):
+        return torch.randn(*shape, generator=gen, dtype=torch.float32) * s + mean
+
+    w = {
+        "to_out_linear.weight": n(hidden, ch),
+        "beta_proj.weight": n(heads, hidden),
+        "norm.weight": 1.0 + n(dim, s=0.1),
+        "alpha.A_log": n(heads, s=0.3),
+        "alpha.dt_bias": n(ch, s=0.5, mean=-2.0),
+        "alpha.down.weight": n(dim, hidden),
+        "alpha.up.weight": n(ch, dim, s=0.1),
+        "output_gate.down.weight": n(dim, hidden),
+        "output_gate.up.weight": n(ch, dim, s=0.1),
+        "output_gate.up.bias": n(ch, s=0.1),
+    }
+    if gate:
+        w["softmax_gate.up.weight"] = n(heads, hidden)
+        w["softmax_gate.up.bias"] = n(heads, s=0.5)
+    for t in short_conv:
+        w[f"short_conv.{t}_sp.weight"] = n(ch, 1, kernel, kernel, s=0.2)
+        w[f"short_conv.{t}_tm.weight"] = n(ch, 1, 5, s=0.45)
+    return w
+
+
+def make_block(seed, hidden, heads, dim, *, std=0.02) -> BlockWeights:
+    gen = torch.Generator().manual_seed(seed)
+    inner = heads * dim
+    qkv = torch.randn(3 * inner, hidden, generator=gen) * std
+    out = torch.randn(hidden, inner, generator=gen) * std
+    qn = 1.0 + torch.randn(dim, generator=gen) * 0.1
+    kn = 1.0 + torch.randn(dim, generator=gen) * 0.1
+    branch = make_branch_weights(gen, hidden, heads, dim, std=std)
+    return BlockWeights(qkv=qkv, q_norm=qn, k_norm=kn, out=out, branch=branch)
+
+
+def make_x(seed, seq, hidden) -> torch.Tensor:
+    gen = torch.Generator().manual_seed(seed + 7919)
+    return torch.randn(seq, hidden, generator=gen)
+
+
+def make_kernel_inputs(seed, lay: Layout, heads, dim):
+    """Config-0 kernel-level inputs: q,k,v ~ N(0,1) with k L2-normalised per head,
+    beta = sigmoid(N(0,1)) [F,H,tpf], alpha = sigmoid(N(2,1)) [F,H,D],
+    gate = sigmoid(N(0,1)) [S,H,1]."""
+    gen = torch.Generator().manual_seed(seed)
+    s = lay.seq_len
+    q = torch.randn(s, heads, dim, generator=gen)
+    k = torch.randn(s, heads, dim, generator=gen)
+    k = k / k.norm(dim=-1, keepdim=True)
+    v = torch.randn(s, heads, dim, generator=gen)
+    beta = torch.sigmoid(torch.randn(lay.num_frames, heads, lay.tokens_per_frame, generator=gen))
+    alpha = torch.sigmoid(torch.randn(lay.num_frames, heads, dim, generator=gen) + 2.0)
+    gate = torch.sigmoid(torch.randn(s, heads, 1, generator=gen))
+    return dict(q=q, k=k, v=v, beta=beta, alpha=alpha, gate=gate)
+
+
+CONFIG0 = dict(text=32, frames=15, grid=(4, 4), heads=4, dim=64, hidden=256)
+CONFIG1 = dict(text=512, frames=31, grid=(38, 22), heads=40, dim=128, hidden=5120)
+CONFIG3 = dict(text=512, frames=31, grid=(80, 48), heads=40, dim=128, hidden=5120)
+
+
+def config_layout(cfg: dict, **kw) -> Layout:
+    return make_layout(cfg["text"], cfg["frames"], cfg["grid"], **kw)
+
+
+def attention_pairs(lay: Layout) -> int:
+    """Allowed (query, key) pairs per head (used for the algorithmic FLOP count)."""
+    return int(key_count_per_row(lay.seq_len, lay.video_start, lay.video_end, lay.num_frames,
+                                 lay.tokens_per_frame, list(lay.bounds), lay.anchor_frames).sum())
+
+
+def block_flops(lay: Layout, heads, dim, hidden, *, branch=True) -> dict:
+    """Algorithmic FLOPs of one block forward (allowed attention pairs only)."""
+    s = lay.seq_len
+    inner = heads * dim
+    fl = {}
+    fl["attention"] = 4.0 * attention_pairs(lay) * dim * heads
+    fl["qkv"] = 2.0 * s * hidden * 3 * inner
+    fl["out_proj"] = 2.0 * s * inner * hidden
+    fl["gates"] = 2.0 * s * hidden * heads
+    if branch and not lay.full_cover:
+        fb = lay.num_frames - 2 if lay.anchor_frames == "both" else lay.num_frames
+        rows = fb * lay.tokens_per_frame
+        tpf = lay.tokens_per_frame
+        fl["to_out_linear"] = 2.0 * rows * inner * hidden
+        fl["branch_gates"] = 2.0 * rows * hidden * (heads + 2 * dim) + 2.0 * rows * dim * inner
+        fl["frame_stats"] = 2.0 * 2 * fb * heads * tpf * dim * dim
+        fl["factor"] = (fb + 1) * heads * (dim ** 3) * 3.0
+        fl["scan"] = 2.0 * 2 * fb * heads * dim ** 3
+        fl["readout"] = 2.0 * rows * heads * dim * dim
+    fl["total"] = sum(fl.values())
+    return fl

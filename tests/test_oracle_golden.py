@@ -1,0 +1,145 @@
+"""Pin the float64 oracle against golden vectors produced by the reference itself.
+
+The fixture ``tests/golden/config0.npz`` holds outputs of the reference's own torch
+path (window.py, branch.py, runtime.py, hybrid.py of hyukudan/ComfyUI-Kirei-VDN-H3)
+on seeded config-0 inputs; ``tests/golden/make_golden.py`` made it.  Inputs are
+rebuilt here from the same seeds and checked by digest first, so a drift of the
+torch RNG shows up as a clear failure rather than as a numerical mismatch.
+"""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import vdn_oracle as vo
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "config0.npz")
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return dict(np.load(GOLDEN))
+
+
+@pytest.fixture(scope="module")
+def setup():
+    c = vo.CONFIG0
+    lay = vo.config_layout(c)
+    ki = vo.make_kernel_inputs(0, lay, c["heads"], c["dim"])
+    return c, lay, ki
+
+
+def _close(got, want, rtol, atol):
+    got = got.detach().cpu().numpy() if isinstance(got, torch.Tensor) else got
+    np.testing.assert_allclose(got, want, rtol=rtol, atol=atol)
+
+
+def test_inputs_are_the_golden_inputs(golden, setup):
+    from tests.golden.make_golden import tensor_digest
+
+    _, _, ki = setup
+    assert str(golden["input_digest"]) == tensor_digest(ki["q"], ki["k"], ki["v"], ki["beta"], ki["alpha"])
+
+
+@pytest.mark.parametrize("mode", vo.ANCHOR_MODES)
+def test_window_attention_matches_reference(golden, setup, mode):
+    c, lay, ki = setup
+    got = vo.window_attention(ki["q"], ki["k"], ki["v"], lay.video_start, lay.video_end,
+                              lay.num_frames, lay.tokens_per_frame, list(lay.bounds),
+                              c["dim"] ** -0.5, mode)
+    if mode != "both":
+        got = got[::4]
+    _close(got, golden[f"window_{mode}"], 2e-5, 2e-6)
+
+
+def test_window_sliding_geometry_matches_reference(golden):
+    lay2 = vo.Layout(seq_len=24 + 9 * 16 + 8, video_start=24, video_end=24 + 9 * 16,
+                     num_frames=9, tokens_per_frame=16, frame_size=(4, 4), text_start=0,
+                     text_len=24, bounds=tuple(vo.window_bounds(9, 2, 0)), anchor_frames="columns")
+    ki2 = vo.make_kernel_inputs(5, lay2, 2, 64)
+    got = vo.window_attention(ki2["q"], ki2["k"], ki2["v"], lay2.video_start, lay2.video_end,
+                              9, 16, list(lay2.bounds), 64 ** -0.5, "columns")
+    _close(got, golden["window_sliding_columns"], 2e-5, 2e-6)
+
+
+def _branch_inputs(setup):
+    c, lay, ki = setup
+    heads, dim = c["heads"], c["dim"]
+    fb, tpf = lay.num_frames - 2, lay.tokens_per_frame
+    inner = slice(lay.video_start + tpf, lay.video_end - tpf)
+    kf = ki["k"][inner].reshape(fb, tpf, heads, dim).permute(0, 2, 1, 3)
+    vf = ki["v"][inner].reshape(fb, tpf, heads, dim).permute(0, 2, 1, 3)
+    text = torch.randn(heads, dim, dim, generator=torch.Generator().manual_seed(11)) * 0.1
+    bounds_b = [(lo - 1, hi - 1) for lo, hi in lay.bounds[1:-1]]
+    return kf, vf, ki["beta"][1:-1], ki["alpha"][1:-1], text, bounds_b
+
+
+def test_statistics_factor_scan_gather_match_reference(golden, setup):
+    kf, vf, beta, alpha, text, bounds_b = _branch_inputs(setup)
+    a, b = vo.frame_statistics(kf, vf, beta)
+    _close(a[:4, 1], golden["stats_A_f03_h1"], 1e-5, 1e-5)
+    _close(b[:4, 1], golden["stats_B_f03_h1"], 1e-5, 1e-5)
+    trans, inj = vo.factor_apply(alpha, a, b)
+    _close(trans[0], golden["inverse_T_f0"], 1e-4, 2e-6)
+    _close(inj[0], golden["inj_f0"], 1e-4, 2e-6)
+    prefix, suffix = vo.run_scans(trans, inj, vo._t(text))
+    _close(prefix[-1], golden["prefix_last"], 1e-4, 1e-5)
+    _close(suffix[0], golden["suffix_first"], 1e-4, 1e-5)
+    state = vo.gather_linear_state(prefix, suffix, vo._t(alpha), bounds_b, "alpha", vo._t(text))
+    _close(state[::2, 0], golden["state_h0"], 1e-4, 1e-5)
+    state_nt = vo.gather_linear_state(prefix, suffix, vo._t(alpha), bounds_b, "alpha", None)
+    _close(state_nt[1::3, 1], golden["state_notext_h1"], 1e-4, 1e-5)
+
+
+def test_conv_features_match_reference(golden, setup):
+    c, lay, ki = setup
+    bw = vo.make_block(0, c["hidden"], c["heads"], c["dim"])
+    w = bw.branch
+    got = vo.conv_features(ki["k"][lay.video_start:lay.video_end], w["short_conv.k_sp.weight"],
+                           w["short_conv.k_tm.weight"], lay.num_frames, lay.frame_size, True)
+    _close(got[3], golden["conv_k_f3"], 1e-5, 1e-6)
+
+
+def test_block_forward_matches_reference(golden, setup):
+    c, lay, _ = setup
+    bw = vo.make_block(0, c["hidden"], c["heads"], c["dim"])
+    x = vo.make_x(0, lay.seq_len, c["hidden"])
+    out, parts = vo.block_forward(x, bw, lay, c["heads"], c["dim"], vo.BranchConfig(), return_parts=True)
+    _close(out, golden["block_out"], 1e-4, 2e-6)
+    delta = torch.zeros(lay.video_end - lay.video_start, c["hidden"], dtype=torch.float64)
+    delta[:] = parts["delta"]
+    _close(delta, golden["branch_delta"], 1e-4, 2e-6)
+    # skip_ends: the anchor frames get no branch contribution (runtime.py:603-607).
+    tpf = lay.tokens_per_frame
+    assert float(parts["delta"][:tpf].abs().max()) == 0.0
+    assert float(parts["delta"][-tpf:].abs().max()) == 0.0
+
+
+def test_window_geometry_known_answers():
+    # Known answers of the reference's own geometry tests (tests/test_window.py:193-202).
+    assert vo.window_bounds(4, 1) == [(-1, 1), (0, 2), (1, 3), (2, 4)]
+    assert vo.window_bounds(6, 1, 5)[0] == (-5, 9)
+    assert vo.window_bounds(6, 1, 5)[5] == (0, 14)
+    assert vo.full_coverage(vo.window_bounds(6, 1, 5), 6)
+    assert not vo.full_coverage(vo.window_bounds(16, 1, 5), 16)
+
+
+def test_int8_scheme_is_exact_integer_arithmetic():
+    gen = torch.Generator().manual_seed(3)
+    x = torch.randn(37, 256, generator=gen).to(torch.bfloat16).float()
+    w = torch.randn(48, 256, generator=gen) * 0.02
+    qa, sa = vo.int8_quantize_rows(x)
+    qw, sw = vo.int8_quantize_weight(w)
+    assert qa.dtype == torch.int8 and int(qa.abs().max()) <= 127
+    acc = vo.int8_accumulate(qa, qw)
+    want = (qa.double() @ qw.double().T)
+    assert torch.equal(acc.double(), want)
+    # The dequantised product approximates the float product within int8 resolution.
+    approx = acc.double() * sa.double()[:, None] * sw.double()[None, :]
+    exact = x.double() @ w.double().T
+    rel = (approx - exact).norm() / exact.norm()
+    assert rel < 2e-2
