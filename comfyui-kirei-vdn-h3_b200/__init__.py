@@ -1,0 +1,24 @@
+"""B200-native (sm_100a) VDN-H3 hybrid attention hot path.
+
+Drop-in for the hot path of hyukudan/ComfyUI-Kirei-VDN-H3: the exact local window
+softmax, the Video Delta Attention branch, the gated sum and the bf16 / fp8 / int8
+projections, behind the reference's operator API (``make_vdn_forward`` ->
+``attn.forward(x, rope_freqs, transformer_options)``).  Compute runs in hand-written
+CUDA for sm_100a loaded from the in-tree C-ABI library ``libvdn_b200.so``; there is no
+CPU or library fallback.
+"""
+
+from . import _lib
+from .branch import B200LinearBranch, cholesky_runtime_scope
+from .hybrid import B200State, FusedBlock, make_vdn_forward, run_forward_checked
+from .layout import (ANCHOR_FRAME_MODES, VDNLayout, current_layout, full_coverage, make_layout, publish_layout,
+                     window_bounds, with_window)
+from .projection import gemm, prepare_projection_maps, project, quantize_rows_int8, quantize_tensor_fp8
+from .window import WindowPlanCache, build_window_plan, window_softmax_b200
+
+__all__ = [
+    "ANCHOR_FRAME_MODES", "B200LinearBranch", "B200State", "FusedBlock", "VDNLayout", "WindowPlanCache",
+    "build_window_plan", "cholesky_runtime_scope", "current_layout", "full_coverage", "gemm", "make_layout",
+    "make_vdn_forward", "prepare_projection_maps", "project", "publish_layout", "quantize_rows_int8",
+    "quantize_tensor_fp8", "run_forward_checked", "window_bounds", "window_softmax_b200", "with_window", "_lib",
+]

@@ -1,0 +1,365 @@
+"""Video Delta Attention branch on sm_100a (replaces vdn_h3/branch.py + vdn_h3/runtime.py).
+
+``B200LinearBranch`` keeps the reference's constructor knobs (delta_rule, bridge,
+a_fp32, short_conv, enable_text_state) and its two entry points:
+
+* ``readout(weights, xv, q_raw, k_raw, v_raw, num_frames, tokens_per_frame, bounds,
+  frame_size, text_x, text_k_raw, text_v_raw, skip_ends, *, inference)``
+  (branch.py:672-722), returning the branch output before ``to_out_linear``;
+* ``projected_delta(..., projector=None)`` (runtime.py:545-607), returning it after.
+
+Both run the same kernel sequence as the fused block (``run_branch``): features, alpha,
+frame statistics (+ the text frame), Cholesky inverse, the fused bidirectional scan
+and the gather/readout/RMSNorm/gate kernel.  Only the ``vdn_solve`` rule with the
+``alpha`` or ``none`` bridge is implemented on the device (the released lineage,
+docs/ARCHITECTURE.md:70-82); ``sana_scaled`` raises.
+"""
+
+from __future__ import annotations
+
+from contextlib import contextmanager
+from contextvars import ContextVar
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+TEXT_STATE_SCALE = 0.5  # branch.py:23
+DELTA_RULES = ("vdn_solve",)
+_CHOLESKY_CHECKS: ContextVar = ContextVar("vdn_b200_cholesky_checks", default=None)
+
+
+class _CholeskyChecks:
+    """Deferred SPD validation of every factorisation of one forward (branch.py:27-45)."""
+
+    def __init__(self):
+        self.statuses: list[torch.Tensor] = []
+        self.factor_calls = 0
+
+    def validate(self):
+        if not self.statuses:
+            return
+        flat = torch.cat([s.reshape(-1) for s in self.statuses])
+        bad = torch.nonzero(flat != 0)
+        if bad.numel():
+            failed = int(bad[0].item())
+            for index, status in enumerate(self.statuses):
+                if failed < status.numel():
+                    minor = int(status.reshape(-1)[failed].item())
+                    raise torch.linalg.LinAlgError(
+                        f"VDN-H3 Cholesky factor {index}, batch {failed}: "
+                        f"leading minor of order {minor} is not positive-definite")
+                failed -= status.numel()
+
+
+@contextmanager
+def cholesky_runtime_scope():
+    """Collect factor statuses and validate them once when the scope exits (branch.py:48-59)."""
+    checks = _CholeskyChecks()
+    token = _CHOLESKY_CHECKS.set(checks)
+    try:
+        yield checks
+        checks.validate()
+    finally:
+        checks.statuses.clear()
+        _CHOLESKY_CHECKS.reset(token)
+
+
+def record_factor_status(info: torch.Tensor):
+    checks = _CHOLESKY_CHECKS.get()
+    if checks is None:
+        tmp = _CholeskyChecks()
+        tmp.statuses.append(info)
+        tmp.factor_calls = 1
+        tmp.validate()
+    else:
+        checks.statuses.append(info)
+        checks.factor_calls += 1
+
+
+@dataclass
+class BranchDeviceWeights:
+    """Branch weights in the layouts the kernels read (fp32 for the small tensors,
+    matching the reference's fp32 policy for A_log/dt_bias, weights.py)."""
+
+    heads: int
+    dim: int
+    og_up: torch.Tensor  # [H*D, D] bf16
+    og_bias: torch.Tensor  # [H*D] fp32
+    alpha_up: torch.Tensor  # [H*D, D] fp32
+    dt_bias: torch.Tensor  # [H*D] fp32
+    a_log: torch.Tensor  # [H] fp32
+    norm_w: torch.Tensor  # [D] fp32
+    conv: dict  # name -> (spatial [C, kh*kw] fp32, kh, kw, temporal [C, taps] fp32, taps)
+    beta_w: torch.Tensor  # [H, hidden] bf16
+    og_down: torch.Tensor  # [D, hidden] bf16
+    alpha_down: torch.Tensor  # [D, hidden] bf16
+    to_out: torch.Tensor | None  # [hidden, H*D] bf16
+
+    @staticmethod
+    def from_dict(w: dict, heads: int, dim: int, device, head_slice: slice | None = None,
+                  short_conv=("k", "v")) -> "BranchDeviceWeights":
+        dev = torch.device(device)
+        hs = head_slice or slice(0, heads)
+        h0, h1 = hs.start, hs.stop
+        cs = slice(h0 * dim, h1 * dim)
+
+        def f32(t):
+            return t.detach().to(dev, torch.float32).contiguous()
+
+        def b16(t):
+            return t.detach().to(dev, torch.bfloat16).contiguous()
+
+        conv = {}
+        for name in short_conv:
+            sp = w[f"short_conv.{name}_sp.weight"][cs]
+            tm = w[f"short_conv.{name}_tm.weight"][cs]
+            kh, kw = int(sp.shape[-2]), int(sp.shape[-1])
+            conv[name] = (f32(sp.reshape(sp.shape[0], -1)), kh, kw, f32(tm.reshape(tm.shape[0], -1)),
+                          int(tm.shape[-1]))
+        to_out = w.get("to_out_linear.weight")
+        return BranchDeviceWeights(
+            heads=h1 - h0, dim=dim,
+            og_up=b16(w["output_gate.up.weight"][cs]),
+            og_bias=f32(w.get("output_gate.up.bias", torch.zeros(heads * dim))[cs]),
+            alpha_up=f32(w["alpha.up.weight"][cs]),
+            dt_bias=f32(w["alpha.dt_bias"][cs]),
+            a_log=f32(w["alpha.A_log"][hs]),
+            norm_w=f32(w["norm.weight"]),
+            conv=conv,
+            beta_w=b16(w["beta_proj.weight"][hs]),
+            og_down=b16(w["output_gate.down.weight"]),
+            alpha_down=b16(w["alpha.down.weight"]),
+            to_out=b16(to_out) if to_out is not None and not isinstance(to_out, tuple) else None,
+        )
+
+
+class BranchWorkspace:
+    """Device buffers of one branch geometry, reused across calls."""
+
+    def __init__(self, device, Fb, tpf, heads, dim, text_len):
+        dev = torch.device(device)
+        inner = heads * dim
+        rows = Fb * tpf
+        bf = dict(device=dev, dtype=torch.bfloat16)
+        f32 = dict(device=dev, dtype=torch.float32)
+        self.key = (str(dev), Fb, tpf, heads, dim, text_len)
+        self.conv_tmp = torch.empty(rows, inner, **bf)
+        self.qf = torch.empty(Fb, heads, tpf, dim, **bf)
+        self.kf = torch.empty(Fb, heads, tpf, dim, **bf)
+        self.vf = torch.empty(Fb, heads, tpf, dim, **bf)
+        nt = 1 if text_len > 0 else 0
+        self.tk = torch.empty(1, heads, max(text_len, 1), dim, **bf)
+        self.tv = torch.empty(1, heads, max(text_len, 1), dim, **bf)
+        self.alpha = torch.empty(Fb, heads, dim, **f32)
+        self.A = torch.empty(Fb + nt, heads, dim, dim, **f32)
+        self.B = torch.empty(Fb + nt, heads, dim, dim, **f32)
+        self.inv = torch.empty(Fb + nt, heads, dim, dim, **f32)
+        self.info = torch.zeros(Fb + nt, heads, device=dev, dtype=torch.int32)
+        self.s0 = torch.empty(heads, dim, dim, **f32)
+        self.prefix = torch.empty(Fb, heads, dim, dim, **f32)
+        self.suffix = torch.empty(Fb, heads, dim, dim, **f32)
+        self.ogd = torch.empty(rows, dim, **bf)
+        self.og = torch.empty(rows, inner, **bf)
+        self.lohi: dict = {}
+
+    def bounds_arrays(self, bounds):
+        key = tuple(bounds)
+        if key not in self.lohi:
+            dev = self.alpha.device
+            lo = torch.tensor([int(b[0]) for b in bounds], dtype=torch.int32, device=dev)
+            hi = torch.tensor([int(b[1]) for b in bounds], dtype=torch.int32, device=dev)
+            self.lohi[key] = (lo, hi)
+        return self.lohi[key]
+
+
+def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_raw, aux, beta_col0, ogd_col0,
+               ad_col0, Fb, tpf, frame_size, bounds, bridge, text_k=None, text_v=None, text_aux=None,
+               out, out_row0, status: _lib.DeviceStatus, short_conv=("k", "v")):
+    """Run the branch kernels on the current stream.
+
+    q_raw / k_raw / v_raw: [Fb*tpf, H*D] bf16 row views (pitch = stride(0)) of the raw
+    projections of the branch frames; aux: [Fb*tpf, *] fp32 rows holding the beta logits
+    (column beta_col0 + h), the output-gate bottleneck (ogd_col0 + j) and the alpha
+    bottleneck (ad_col0 + j); text_k / text_v / text_aux: the same for the text rows.
+    Writes out[out_row0 + f*tpf + s, h*D + v] (bf16).
+    """
+    H, D = bw.heads, bw.dim
+    inner = H * D
+    rows = Fb * tpf
+    stream = _lib.stream_handle(out.device)
+    gh, gw = frame_size
+    call = _lib.call
+
+    def feature(raw, name, dst, l2):
+        if name in bw.conv and name in short_conv:
+            sp, kh, kw, tm, taps = bw.conv[name]
+            call("vdn_spatial_conv", raw.data_ptr(), raw.stride(0), sp.data_ptr(), kh, kw, Fb, gh, gw, inner,
+                 ws.conv_tmp.data_ptr(), ws.conv_tmp.stride(0), stream)
+            call("vdn_temporal_act", ws.conv_tmp.data_ptr(), ws.conv_tmp.stride(0), tm.data_ptr(), taps, Fb, tpf,
+                 H, D, int(l2), dst.data_ptr(), stream)
+        else:
+            call("vdn_temporal_act", raw.data_ptr(), raw.stride(0), None, 0, Fb, tpf, H, D, int(l2), dst.data_ptr(),
+                 stream)
+
+    feature(k_raw, "k", ws.kf, True)
+    feature(v_raw, "v", ws.vf, False)
+    feature(q_raw, "q", ws.qf, True)
+    aux_ld = aux.stride(0)
+    call("vdn_alpha_gate", aux.data_ptr() + 4 * ad_col0, aux_ld, Fb, tpf, D, bw.alpha_up.data_ptr(),
+         bw.dt_bias.data_ptr(), bw.a_log.data_ptr(), H, D, ws.alpha.data_ptr(), stream)
+    call("vdn_frame_stats", ws.kf.data_ptr(), ws.vf.data_ptr(), Fb, H, tpf, D, aux.data_ptr(), aux_ld, beta_col0,
+         ws.A.data_ptr(), ws.B.data_ptr(), stream)
+    has_text = text_k is not None
+    if has_text:
+        L = text_k.shape[0]
+        call("vdn_temporal_act", text_k.data_ptr(), text_k.stride(0), None, 0, 1, L, H, D, 1, ws.tk.data_ptr(), stream)
+        call("vdn_temporal_act", text_v.data_ptr(), text_v.stride(0), None, 0, 1, L, H, D, 0, ws.tv.data_ptr(), stream)
+        mat = D * D * H
+        call("vdn_frame_stats", ws.tk.data_ptr(), ws.tv.data_ptr(), 1, H, L, D, text_aux.data_ptr(),
+             text_aux.stride(0), beta_col0, ws.A.data_ptr() + 4 * Fb * mat, ws.B.data_ptr() + 4 * Fb * mat, stream)
+        call("vdn_delta_factor", ws.A.data_ptr(), ws.B.data_ptr(), Fb + 1, H, D, ws.inv.data_ptr(),
+             ws.info.data_ptr(), Fb, TEXT_STATE_SCALE, ws.s0.data_ptr(), stream)
+        s0 = ws.s0
+    else:
+        call("vdn_delta_factor", ws.A.data_ptr(), ws.B.data_ptr(), Fb, H, D, ws.inv.data_ptr(), ws.info.data_ptr(),
+             -1, 0.0, None, stream)
+        s0 = None
+    record_factor_status(ws.info)
+    call("vdn_bidir_scan", ws.inv.data_ptr(), ws.B.data_ptr(), ws.alpha.data_ptr(), _lib.ptr(s0), Fb, H, D,
+         ws.prefix.data_ptr(), ws.suffix.data_ptr(), stream)
+    # output gate: sigmoid(bf16(x W_down^T) W_up^T + b)  (branch.py:754-758)
+    call("vdn_cast_rows", aux.data_ptr(), aux_ld, ogd_col0, rows, D, ws.ogd.data_ptr(), ws.ogd.stride(0), stream)
+    call("vdn_gemm", 0, ws.ogd.data_ptr(), D, None, 0, 0, bw.og_up.data_ptr(), D, ws.og.data_ptr(), inner, 0,
+         rows, inner, D, 1.0, None, None, None, None, bw.og_bias.data_ptr(), 1, None, 0, status.err_ptr, stream)
+    lo, hi = ws.bounds_arrays(bounds)
+    call("vdn_readout", ws.qf.data_ptr(), Fb, H, tpf, D, ws.prefix.data_ptr(), ws.suffix.data_ptr(),
+         ws.alpha.data_ptr(), _lib.ptr(s0), lo.data_ptr(), hi.data_ptr(), int(bridge == "alpha"),
+         bw.norm_w.data_ptr(), ws.og.data_ptr(), inner, out.data_ptr(), out.stride(0), int(out_row0), stream)
+
+
+class B200LinearBranch:
+    """Drop-in for ``LinearBranch`` / ``OptimizedLinearBranch`` (branch.py:533-571,
+    runtime.py:237-245) running the sm_100a kernels."""
+
+    def __init__(self, weights, num_heads, head_dim, delta_rule="vdn_solve", bridge="alpha", a_fp32=True,
+                 short_conv=("k", "v"), enable_text_state=True, **_runtime):
+        if delta_rule not in ("vdn_solve", "sana_scaled"):
+            raise ValueError(f"unknown delta rule: {delta_rule!r}")
+        if bridge not in ("alpha", "none"):
+            raise ValueError("bridge must be 'alpha' or 'none'")
+        targets = tuple(short_conv)
+        if len(set(targets)) != len(targets) or any(t not in ("q", "k", "v") for t in targets):
+            raise ValueError("short_conv must be a distinct subset of ('q', 'k', 'v')")
+        self.w = weights
+        self.num_heads = int(num_heads)
+        self.head_dim = int(head_dim)
+        self.delta_rule = delta_rule
+        self.bridge = bridge
+        self.a_fp32 = bool(a_fp32)
+        self.short_conv = targets
+        self.enable_text_state = bool(enable_text_state)
+        self._dev_weights: dict = {}
+        self._workspaces: dict = {}
+        self.status = None
+
+    def detach_weights(self):
+        self.w = None
+
+    def release(self):
+        self._dev_weights.clear()
+        self._workspaces.clear()
+
+    clear = release
+
+    def device_weights(self, weights, device) -> BranchDeviceWeights:
+        key = (str(device), id(weights))
+        if key not in self._dev_weights:
+            self._dev_weights[key] = BranchDeviceWeights.from_dict(weights, self.num_heads, self.head_dim, device,
+                                                                   short_conv=self.short_conv)
+        return self._dev_weights[key]
+
+    def workspace(self, device, Fb, tpf, text_len) -> BranchWorkspace:
+        key = (str(device), Fb, tpf, text_len)
+        if key not in self._workspaces:
+            self._workspaces[key] = BranchWorkspace(device, Fb, tpf, self.num_heads, self.head_dim, text_len)
+        return self._workspaces[key]
+
+    def readout(self, weights, xv, q_raw, k_raw, v_raw, num_frames, tokens_per_frame, bounds, frame_size=None,
+                text_x=None, text_k_raw=None, text_v_raw=None, skip_ends=False, *, inference=False):
+        if self.delta_rule != "vdn_solve":
+            raise NotImplementedError("the B200 branch implements the released vdn_solve rule only")
+        expected_rows = num_frames * tokens_per_frame
+        if xv.ndim != 2 or xv.shape[0] != expected_rows:
+            raise ValueError("xv rows must equal num_frames * tokens_per_frame")
+        H, D = self.num_heads, self.head_dim
+        expected_qkv = (expected_rows, H, D)
+        if q_raw.shape != expected_qkv or k_raw.shape != expected_qkv or v_raw.shape != expected_qkv:
+            raise ValueError("raw q/k/v have incompatible video row/head geometry")
+        if len(bounds) != num_frames:
+            raise ValueError("bounds must contain one entry per frame")
+        if frame_size is None and self.short_conv:
+            raise ValueError("short convolution requires frame_size")
+        _lib.require_cuda(xv, q_raw, k_raw, v_raw)
+        dev = xv.device
+        out = torch.zeros(expected_rows, H * D, device=dev, dtype=torch.bfloat16)
+        if skip_ends:
+            if num_frames <= 2:
+                return out
+            F_b, r0 = num_frames - 2, tokens_per_frame
+            bounds_b = [(lo - 1, hi - 1) for lo, hi in bounds[1:-1]]
+        else:
+            F_b, r0 = num_frames, 0
+            bounds_b = list(bounds)
+        rows = slice(r0, r0 + F_b * tokens_per_frame)
+        bw = self.device_weights(weights, dev)
+        text = self.enable_text_state and text_x is not None
+        if text and (text_k_raw is None or text_v_raw is None):
+            raise ValueError("text state needs both raw text key and value")
+        ws = self.workspace(dev, F_b, tokens_per_frame, text_x.shape[0] if text else 0)
+        # side projections [beta | og_down | alpha_down] as fp32 (branch.py:736, :743-751, :755)
+        w_side = torch.cat([bw.beta_w, bw.og_down, bw.alpha_down], 0).contiguous()
+        n_side = w_side.shape[0]
+        n_pad = (n_side + 255) // 256 * 256
+        st = self.status or _lib.DeviceStatus(dev)
+
+        def side(x):
+            xb = x.to(torch.bfloat16).contiguous()
+            o = torch.empty(xb.shape[0], n_pad, device=dev, dtype=torch.float32)
+            _lib.call("vdn_gemm", 0, xb.data_ptr(), xb.shape[1], None, 0, 0, w_side.data_ptr(), w_side.shape[1],
+                      o.data_ptr(), n_pad, 1, xb.shape[0], n_side, xb.shape[1], 1.0, None, None, None, None, None, 0,
+                      None, 0, st.err_ptr, _lib.stream_handle(dev))
+            return o
+
+        aux = side(xv[rows])
+
+        def flat(t):
+            t = t.reshape(t.shape[0], H * D) if t.is_contiguous() else t.contiguous().reshape(t.shape[0], H * D)
+            return t.to(torch.bfloat16)
+
+        kw = dict(q_raw=flat(q_raw[rows]), k_raw=flat(k_raw[rows]), v_raw=flat(v_raw[rows]), aux=aux, beta_col0=0,
+                  ogd_col0=H, ad_col0=H + D, Fb=F_b, tpf=tokens_per_frame, frame_size=frame_size, bounds=bounds_b,
+                  bridge=self.bridge, out=out, out_row0=r0, status=st, short_conv=self.short_conv)
+        if text:
+            kw.update(text_k=flat(text_k_raw), text_v=flat(text_v_raw), text_aux=side(text_x))
+        run_branch(ws, bw, **kw)
+        if self.status is None:
+            st.raise_if_failed()
+        return out
+
+    def projected_delta(self, weights, xv, q_raw, k_raw, v_raw, num_frames, tokens_per_frame, bounds, *,
+                        frame_size=None, text_x=None, text_k_raw=None, text_v_raw=None, skip_ends=False,
+                        inference=False, projector=None, tile_frames=None):
+        """Branch output after ``to_out_linear`` (runtime.py:545-607)."""
+        readout = self.readout(weights, xv, q_raw, k_raw, v_raw, num_frames, tokens_per_frame, bounds,
+                               frame_size=frame_size, text_x=text_x, text_k_raw=text_k_raw, text_v_raw=text_v_raw,
+                               skip_ends=skip_ends, inference=inference)
+        if projector is None:
+            from .projection import project
+            return project(readout.to(xv.dtype), weights)
+        return projector(readout.to(xv.dtype))
+
+
+__all__ = ["B200LinearBranch", "BranchDeviceWeights", "BranchWorkspace", "TEXT_STATE_SCALE",
+           "cholesky_runtime_scope", "run_branch"]

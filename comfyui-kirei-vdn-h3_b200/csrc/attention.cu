@@ -1,0 +1,470 @@
+// Exact block-sparse window softmax attention for VDN-H3 on sm_100a (tcgen05 + TMA).
+//
+// Semantics (window.py:277-344): a query row may attend to key row k iff
+//     global(q) or global(k) or lo[frame(q)] <= frame(k) <= hi[frame(q)]
+//     or (anchor columns and frame(k) in {0, F-1}) or (anchor rows and frame(q) in {0, F-1}),
+// softmax over the allowed keys with scale D^-0.5, then the per-token head gate
+// sigmoid(x W_g^T + b) (hybrid.py:518-528) is applied and the result is stored in the
+// flattened [S, H*D] layout the out-projection reads (softmax_kernels.py:8-9).
+//
+// B200 design:
+//   * persistent CTAs walk a cost-sorted list of (head, 128-row query tile) items;
+//   * the host plan gives each query tile the merged key intervals its rows can see, cut
+//     into 128-key tiles at arbitrary row offsets (TMA rows have no alignment rule); only
+//     tiles where some row of the query tile is excluded carry a mask flag, and for those
+//     the mask is rebuilt per element from the frame index (never materialised);
+//   * warp 4 streams K and V tiles with TMA into a 2-stage ring; warp 5 issues
+//     S = Q K^T (M=128, N=128) into one of two TMEM buffers and O += P V (V MN-major);
+//   * warps 0..3 own one query row per thread: they read S from TMEM, run the online
+//     softmax in registers (exp2 in log2 units), rescale O in TMEM, write P as bf16 into
+//     a 128-byte-swizzled shared-memory tile and finally apply 1/l and the gate.
+#include "host_common.h"
+#include "sm100.cuh"
+
+namespace vdn {
+namespace attn {
+
+constexpr int kThreads = 192;
+constexpr int BQ = 128;
+constexpr int BKV = 128;
+constexpr int kStages = 2;
+
+struct Params {
+  int S, H, D;
+  int vs, ve, F, tpf;
+  int anchor_rows, anchor_cols;
+  float scale_log2;
+  const int* frame_lo;              // [F] first visible key frame (clamped)
+  const int* frame_hi;              // [F] last visible key frame (clamped)
+  const int* items;                 // [n_items] (head << 20) | q_tile
+  int n_items;
+  const int* tile_off;              // [n_qtiles + 1]
+  const int* ktile;                 // [n_ktiles] (k0 << 9) | (masked << 8) | (valid - 1)
+  __nv_bfloat16* out;
+  long long ld_out;
+  const float* gate_logits;         // [S, ld_gate] fp32 or null
+  long long ld_gate;
+  int gate_col0;
+  const float* gate_bias;           // [H] or null
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int D>
+struct Layout {
+  static constexpr int kQBytes = BQ * D * 2;
+  static constexpr int kKBytes = BKV * D * 2;
+  static constexpr int kVBytes = BKV * D * 2;
+  static constexpr int kPBytes = BQ * BKV * 2;
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + kQBytes;
+  static constexpr int kOffV = kOffK + kStages * kKBytes;
+  static constexpr int kOffP = kOffV + kStages * kVBytes;
+  static constexpr int kOffBar = kOffP + kPBytes;
+  static constexpr int kSmem = kOffBar + 256 + 1024;
+};
+
+// Barrier slots.
+enum {
+  B_QFULL = 0, B_QEMPTY, B_KFULL0, B_KFULL1, B_VFULL0, B_VFULL1, B_KEMPTY0, B_KEMPTY1,
+  B_VEMPTY0, B_VEMPTY1, B_SFULL0, B_SFULL1, B_SEMPTY0, B_SEMPTY1, B_PFULL, B_ODONE, B_OFREE, B_COUNT
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    window_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                            const __grid_constant__ CUtensorMap tv, Params p, int* err) {
+  using L = Layout<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + B_COUNT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  auto B = [&](int i) { return smem_u32(&bar[i]); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(B(B_QFULL), 1);
+    mbar_init(B(B_QEMPTY), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(B(B_KFULL0 + s), 1);
+      mbar_init(B(B_VFULL0 + s), 1);
+      mbar_init(B(B_KEMPTY0 + s), 1);
+      mbar_init(B(B_VEMPTY0 + s), 1);
+      mbar_init(B(B_SFULL0 + s), 1);
+      mbar_init(B(B_SEMPTY0 + s), 4);
+    }
+    mbar_init(B(B_PFULL), 4);
+    mbar_init(B(B_ODONE), 1);
+    mbar_init(B(B_OFREE), 4);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch(&tq);
+    tma_prefetch(&tk);
+    tma_prefetch(&tv);
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t sQ = smem_u32(smem + L::kOffQ);
+  const uint32_t sK = smem_u32(smem + L::kOffK);
+  const uint32_t sV = smem_u32(smem + L::kOffV);
+  const uint32_t sP = smem_u32(smem + L::kOffP);
+  constexpr int kDBlocks = D / 64;  // 64-element (128 B) column blocks per row
+
+  if (warp == 4) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int g = 0;  // global kv tile counter
+      int it = 0;
+      for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++it) {
+        const int code = p.items[item];
+        const int h = code >> 20, qt = code & 0xFFFFF;
+        if (!mbar_wait(B(B_QEMPTY), (it & 1) ^ 1, abort_flag, err, kErrWaitProducer)) break;
+        mbar_arrive_expect_tx(B(B_QFULL), L::kQBytes);
+        for (int b = 0; b < kDBlocks; ++b)
+          tma_load_2d(sQ + b * (BQ * 128), &tq, B(B_QFULL), h * D + b * 64, qt * BQ);
+        const int t0 = p.tile_off[qt], t1 = p.tile_off[qt + 1];
+        bool ok = true;
+        for (int t = t0; t < t1; ++t, ++g) {
+          const int st = g & 1;
+          const uint32_t ph = (g >> 1) & 1;
+          const int k0 = p.ktile[t] >> 9;
+          const uint32_t kb = sK + st * L::kKBytes, vb = sV + st * L::kVBytes;
+          if (!mbar_wait(B(B_KEMPTY0 + st), ph ^ 1, abort_flag, err, kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(B(B_KFULL0 + st), L::kKBytes);
+          for (int b = 0; b < kDBlocks; ++b)
+            tma_load_2d(kb + b * (BKV * 128), &tk, B(B_KFULL0 + st), h * D + b * 64, k0);
+          if (!mbar_wait(B(B_VEMPTY0 + st), ph ^ 1, abort_flag, err, kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(B(B_VFULL0 + st), L::kVBytes);
+          for (int b = 0; b < kDBlocks; ++b)
+            tma_load_2d(vb + b * (BKV * 128), &tv, B(B_VFULL0 + st), h * D + b * 64, k0);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc_s = make_idesc(1, 1, 1, 0, 0, BQ, BKV);
+      constexpr uint32_t idesc_o = make_idesc(1, 1, 1, 0, 1, BQ, D);
+      const uint32_t o_tmem = tmem_base + 256;
+      int g = 0;
+      int it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++it) {
+        const int qt = p.items[item] & 0xFFFFF;
+        const int n = p.tile_off[qt + 1] - p.tile_off[qt];
+        if (!mbar_wait(B(B_QFULL), it & 1, abort_flag, err, kErrWaitMma)) break;
+        tc_fence_after();
+        const int g0 = g;
+        for (int j = 0; j <= n && ok; ++j) {
+          if (j < n) {
+            // S_j = Q K_j^T into S buffer (g0 + j) & 1
+            const int gj = g0 + j, st = gj & 1;
+            const uint32_t ph = (gj >> 1) & 1;
+            if (!mbar_wait(B(B_KFULL0 + st), ph, abort_flag, err, kErrWaitMma) ||
+                !mbar_wait(B(B_SEMPTY0 + st), ph ^ 1, abort_flag, err, kErrWaitMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t kb = sK + st * L::kKBytes;
+#pragma unroll
+            for (int s = 0; s < D / 16; ++s) {
+              const uint32_t off = (s >> 2) * (BQ * 128) + (s & 3) * 32;
+              mma_f16(tmem_base + st * 128, make_sdesc(sQ + off, 16, 1024), make_sdesc(kb + off, 16, 1024),
+                      idesc_s, s > 0 ? 1u : 0u);
+            }
+            tc_commit(B(B_SFULL0 + st));
+            tc_commit(B(B_KEMPTY0 + st));
+            if (j == n - 1) tc_commit(B(B_QEMPTY));
+          }
+          if (j > 0) {
+            // O += P_{j-1} V_{j-1}
+            const int gj = g0 + j - 1, st = gj & 1;
+            const uint32_t ph = (gj >> 1) & 1;
+            if (!mbar_wait(B(B_PFULL), gj & 1, abort_flag, err, kErrWaitMma) ||
+                !mbar_wait(B(B_VFULL0 + st), ph, abort_flag, err, kErrWaitMma)) {
+              ok = false;
+              break;
+            }
+            if (j == 1 && !mbar_wait(B(B_OFREE), (it & 1) ^ 1, abort_flag, err, kErrWaitMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t vb = sV + st * L::kVBytes;
+#pragma unroll
+            for (int s = 0; s < BKV / 16; ++s) {
+              const uint32_t aoff = (s >> 2) * (BQ * 128) + (s & 3) * 32;
+              mma_f16(o_tmem, make_sdesc(sP + aoff, 16, 1024), make_sdesc(vb + s * 2048, BKV * 128, 1024),
+                      idesc_o, (j > 1 || s > 0) ? 1u : 0u);
+            }
+            tc_commit(B(B_ODONE));
+            tc_commit(B(B_VEMPTY0 + st));
+          }
+        }
+        g = g0 + n;
+      }
+    }
+  } else {
+    // ---------------- softmax / correction / epilogue (warps 0..3) ----------------
+    const int row_in_tile = warp * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    int g = 0;
+    int it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++it) {
+      const int code = p.items[item];
+      const int h = code >> 20, qt = code & 0xFFFFF;
+      const int t0 = p.tile_off[qt], n = p.tile_off[qt + 1] - t0;
+      const int qrow = qt * BQ + row_in_tile;
+      // Per-row visibility (window.py:327-344).
+      bool dense = (qrow < p.vs) || (qrow >= p.ve);
+      int wlo = 0, whi = 0;
+      if (!dense && qrow < p.S) {
+        const int f = (qrow - p.vs) / p.tpf;
+        if (p.anchor_rows && (f == 0 || f == p.F - 1)) dense = true;
+        wlo = p.vs + p.frame_lo[f] * p.tpf;
+        whi = p.vs + (p.frame_hi[f] + 1) * p.tpf;
+      }
+      const int acol_lo = p.anchor_cols ? p.vs + p.tpf : p.vs;   // keys < acol_lo are anchor frame 0
+      const int acol_hi = p.anchor_cols ? p.ve - p.tpf : p.ve;   // keys >= acol_hi are anchor frame F-1
+      float m_run = -INFINITY, l_run = 0.f;
+      const int g0 = g;
+      for (int j = 0; j < n; ++j) {
+        const int gj = g0 + j, st = gj & 1;
+        const uint32_t ph = (gj >> 1) & 1;
+        if (!mbar_wait(B(B_SFULL0 + st), ph, abort_flag, err, kErrWaitEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float s[BKV];
+        {
+          uint32_t r[32];
+#pragma unroll
+          for (int c = 0; c < BKV / 32; ++c) {
+            tmem_ld32(tmem_base + lane_base + st * 128 + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(B(B_SEMPTY0 + st));
+        const int info = p.ktile[t0 + j];
+        const int k0 = info >> 9;
+        const int valid = (info & 0xFF) + 1;
+        const bool masked = (info >> 8) & 1;
+        float mt = -INFINITY;
+        if (masked || valid < BKV) {
+#pragma unroll
+          for (int c = 0; c < BKV; ++c) {
+            const int key = k0 + c;
+            bool allow = c < valid;
+            if (masked && allow) {
+              allow = dense || key < p.vs || key >= p.ve || (key >= wlo && key < whi) || key < acol_lo ||
+                      key >= acol_hi;
+            }
+            s[c] = allow ? s[c] * p.scale_log2 : -INFINITY;
+            mt = fmaxf(mt, s[c]);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < BKV; ++c) {
+            s[c] *= p.scale_log2;
+            mt = fmaxf(mt, s[c]);
+          }
+        }
+        const float m_new = fmaxf(m_run, mt);
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+        const float corr = ex2(m_run - m_use);  // m_run = -inf gives 0
+        float rs = 0.f;
+        uint32_t pk[BKV / 2];
+#pragma unroll
+        for (int c = 0; c < BKV; c += 2) {
+          const float a = ex2(s[c] - m_use), b = ex2(s[c + 1] - m_use);
+          rs += a + b;
+          pk[c / 2] = pack_bf16(a, b);
+        }
+        l_run = l_run * corr + rs;
+        m_run = m_new;
+        if (j > 0) {
+          // The previous PV must be done before O is rescaled and P is overwritten.
+          if (!mbar_wait(B(B_ODONE), (gj - 1) & 1, abort_flag, err, kErrWaitEpilogue)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, corr != 1.0f)) {
+            uint32_t r[32];
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              const uint32_t ta = tmem_base + lane_base + 256 + c * 32;
+              tmem_ld32(ta, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+              tmem_st32(ta, r);
+            }
+            tmem_st_wait();
+          }
+        }
+        // P (bf16) -> shared memory, K-major 128-byte swizzle: 2 blocks of 64 keys.
+        {
+          const uint32_t rbase = sP + row_in_tile * 128;
+          const uint32_t sw = row_in_tile & 7;
+#pragma unroll
+          for (int c = 0; c < BKV / 8; ++c) {
+            const uint32_t addr = rbase + (c >> 3) * (BQ * 128) + (((c & 7) ^ sw) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[c * 4]),
+                         "r"(pk[c * 4 + 1]), "r"(pk[c * 4 + 2]), "r"(pk[c * 4 + 3])
+                         : "memory");
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(B(B_PFULL));
+      }
+      if (!ok) break;
+      g = g0 + n;
+      // Epilogue: wait for the last PV, normalise, gate, store.
+      if (!mbar_wait(B(B_ODONE), (g - 1) & 1, abort_flag, err, kErrWaitEpilogue)) break;
+      tc_fence_after();
+      float gate = 1.f;
+      if (p.gate_logits && qrow < p.S) {
+        float z = p.gate_logits[(long long)qrow * p.ld_gate + p.gate_col0 + h];
+        if (p.gate_bias) z += p.gate_bias[h];
+        gate = 1.f / (1.f + __expf(-z));
+      }
+      const float inv_l = (l_run > 0.f) ? gate / l_run : 0.f;
+      __nv_bfloat16* dst = p.out + (long long)qrow * p.ld_out + h * D;
+      uint32_t r[32];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        tmem_ld32(tmem_base + lane_base + 256 + c * 32, r);
+        tmem_ld_wait();
+        if (qrow < p.S) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 v;
+            v.x = pack_bf16(__uint_as_float(r[i]) * inv_l, __uint_as_float(r[i + 1]) * inv_l);
+            v.y = pack_bf16(__uint_as_float(r[i + 2]) * inv_l, __uint_as_float(r[i + 3]) * inv_l);
+            v.z = pack_bf16(__uint_as_float(r[i + 4]) * inv_l, __uint_as_float(r[i + 5]) * inv_l);
+            v.w = pack_bf16(__uint_as_float(r[i + 6]) * inv_l, __uint_as_float(r[i + 7]) * inv_l);
+            *reinterpret_cast<uint4*>(dst + c * 32 + i) = v;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(B(B_OFREE));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) abort_drain();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+template <int D>
+int launch(const void* q, long long ld_q, const void* k, long long ld_k, const void* v, long long ld_v, Params p,
+           int* err, cudaStream_t stream) {
+  CUtensorMap tq, tk, tv;
+  const uint64_t width = (uint64_t)p.H * D;
+  int rc = make_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, width, (uint64_t)p.S, (uint64_t)ld_q, 64, 128);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, width, (uint64_t)p.S, (uint64_t)ld_k, 64, 128);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tv, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, width, (uint64_t)p.S, (uint64_t)ld_v, 64, 128);
+  if (rc) return rc;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(window_attention_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Layout<D>::kSmem);
+    attr = true;
+  }
+  const int grid = p.n_items < sm_count() ? p.n_items : sm_count();
+  if (grid <= 0) return kOk;
+  window_attention_kernel<D><<<grid, kThreads, Layout<D>::kSmem, stream>>>(tq, tk, tv, p, err);
+  return launch_status();
+}
+
+}  // namespace attn
+}  // namespace vdn
+
+extern "C" {
+
+// Window softmax attention with the fused per-token head gate.
+//   q, k, v  [S, H*D] bf16 row-major views with row pitches ld_q / ld_k / ld_v (elements);
+//            q and k already RMS-normalised (hybrid.py:271-273)
+//   out      [S, ld_out] bf16: gated output at columns h*D
+//   frame_lo / frame_hi [F] int32 device arrays: clamped visible key-frame range per frame
+//   items / tile_off / ktile: the block-sparse plan built by the host package
+//   gate_logits [S, ld_gate] fp32 (column gate_col0 + h) and gate_bias [H]: optional
+// Replaces window.py:277-313 (window_softmax_grouped) + hybrid.py:518-528.
+int vdn_window_attention(const void* q, long long ld_q, const void* k, long long ld_k, const void* v, long long ld_v,
+                         int S, int H, int D, int video_start, int video_end, int num_frames, int tokens_per_frame,
+                         int anchor_rows, int anchor_cols, float scale, const int* frame_lo, const int* frame_hi,
+                         const int* items, int n_items, const int* tile_off, const int* ktile, void* out,
+                         long long ld_out, const float* gate_logits, long long ld_gate, int gate_col0,
+                         const float* gate_bias, int* dev_err, void* stream) {
+  if (!q || !k || !v || !out || !items || !tile_off || !ktile || !frame_lo || !frame_hi) return vdn::kBadArgument;
+  if (D != 64 && D != 128) return vdn::kUnsupported;
+  if (S <= 0 || H <= 0 || H >= 2048 || num_frames <= 0 || tokens_per_frame <= 0) return vdn::kBadArgument;
+  if (S >= (1 << 22)) return vdn::kUnsupported;
+  if ((ld_out * 2) % 16) return vdn::kMisaligned;
+  vdn::attn::Params p{};
+  p.S = S;
+  p.H = H;
+  p.D = D;
+  p.vs = video_start;
+  p.ve = video_end;
+  p.F = num_frames;
+  p.tpf = tokens_per_frame;
+  p.anchor_rows = anchor_rows;
+  p.anchor_cols = anchor_cols;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.frame_lo = frame_lo;
+  p.frame_hi = frame_hi;
+  p.items = items;
+  p.n_items = n_items;
+  p.tile_off = tile_off;
+  p.ktile = ktile;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ld_out = ld_out;
+  p.gate_logits = gate_logits;
+  p.ld_gate = ld_gate;
+  p.gate_col0 = gate_col0;
+  p.gate_bias = gate_bias;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return D == 128 ? vdn::attn::launch<128>(q, ld_q, k, ld_k, v, ld_v, p, dev_err, s)
+                  : vdn::attn::launch<64>(q, ld_q, k, ld_k, v, ld_v, p, dev_err, s);
+}
+
+}  // extern "C"

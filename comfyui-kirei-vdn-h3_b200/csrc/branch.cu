@@ -1,0 +1,587 @@
+// Video Delta Attention (VDA) linear branch of VDN-H3 on sm_100a.
+//
+// Pipeline for the F' = F-2 inner frames of one block (branch.py:672-816, runtime.py:545-607):
+//   1. vdn_spatial_conv   depthwise kxk conv per frame on the (gh, gw) grid      (branch.py:469-471)
+//   2. vdn_temporal_act   5-tap temporal conv (zero pad), SiLU, L2 over D, FHSD  (kernels.py:99-129)
+//                         (taps = 0: plain activation for q and text rows, kernels.py:47-51)
+//   3. vdn_alpha_gate     alpha = exp(-exp(A_log) softplus(up(mean_t down x) + dt_bias)) (branch.py:483-491)
+//   4. vdn_frame_stats    A = sym((beta K)^T K), B = (beta V)^T K per frame/head  (branch.py:197-243)
+//   5. vdn_delta_factor   Cholesky of I+A, L^-1, (I+A)^-1 = L^-T L^-1, info    (branch.py:148-160, :62-71)
+//   6. vdn_bidir_scan     s_t = (B_t + s_{t-1} diag(alpha_t)) (I+A_t)^-1, both directions
+//                         (= Inj_t + s_{t-1} T_t of branch.py:297-312, fused so neither T nor
+//                          Inj is ever materialised)
+//   7. vdn_readout        gather + alpha bridge (branch.py:372-396), Q S^T, RMSNorm(D),
+//                         x output gate (branch.py:494-530, :754-758)
+// Every kernel reads and writes device buffers through plain pointers and strides.
+#include "host_common.h"
+#include "sm100.cuh"
+
+namespace vdn {
+namespace branch {
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
+
+// ---------------------------------------------------------------------------------
+// 1. Spatial depthwise conv.  in: rows (f*gh + y)*gw + x at row pitch ld_in; out [rows, C] bf16.
+// grid (gh, F, ceil(C/256)), block 256: one channel per thread, sliding along x.
+// ---------------------------------------------------------------------------------
+__global__ void spatial_conv_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in,
+                                    const float* __restrict__ w, int kh, int kw, int gh, int gw, int C,
+                                    __nv_bfloat16* __restrict__ out, long long ld_out) {
+  const int y = blockIdx.x, f = blockIdx.y;
+  const int c = blockIdx.z * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  float wr[49];
+  const int taps = kh * kw;
+  for (int i = 0; i < taps; ++i) wr[i] = w[(long long)c * taps + i];
+  const int ph = kh / 2, pw = kw / 2;
+  const long long frame0 = (long long)f * gh * gw;
+  for (int x = 0; x < gw; ++x) {
+    float acc = 0.f;
+    for (int dy = 0; dy < kh; ++dy) {
+      const int yy = y + dy - ph;
+      if (yy < 0 || yy >= gh) continue;
+      for (int dx = 0; dx < kw; ++dx) {
+        const int xx = x + dx - pw;
+        if (xx < 0 || xx >= gw) continue;
+        acc += wr[dy * kw + dx] * __bfloat162float(in[(frame0 + (long long)yy * gw + xx) * ld_in + c]);
+      }
+    }
+    out[(frame0 + (long long)y * gw + x) * ld_out + c] = __float2bfloat16_rn(acc);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// 2. Temporal conv + SiLU + optional L2, output FHSD [F, H, T, D] bf16.
+// One warp per (token s, head h), looping over frames with a 5-frame register ring.
+// taps == 0 means no temporal conv (plain activation).
+// ---------------------------------------------------------------------------------
+template <int D>
+__global__ void temporal_act_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in, const float* __restrict__ w,
+                                    int taps, int F, int T, int H, int l2, __nv_bfloat16* __restrict__ out) {
+  constexpr int V = D / 32;  // channels per lane
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= T * H) return;
+  const int s = gw / H, h = gw % H;
+  const int c0 = h * D + lane * V;
+  float wt[5][V];
+  const int pad = taps / 2;
+  for (int dt = 0; dt < 5; ++dt)
+    for (int i = 0; i < V; ++i) wt[dt][i] = (dt < taps) ? w[(long long)(c0 + i) * taps + dt] : 0.f;
+  auto load = [&](int t, float (&v)[V]) {
+    if (t < 0 || t >= F) {
+#pragma unroll
+      for (int i = 0; i < V; ++i) v[i] = 0.f;
+      return;
+    }
+    const __nv_bfloat16* src = in + ((long long)t * T + s) * ld_in + c0;
+#pragma unroll
+    for (int i = 0; i < V; ++i) v[i] = __bfloat162float(src[i]);
+  };
+  float ring[5][V];
+  if (taps > 0) {
+    for (int k = 0; k < 5; ++k) load(k - pad, ring[k]);
+  }
+  for (int t = 0; t < F; ++t) {
+    float y[V];
+    if (taps > 0) {
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        float a = 0.f;
+#pragma unroll
+        for (int dt = 0; dt < 5; ++dt) a += wt[dt][i] * ring[dt][i];
+        y[i] = a;
+      }
+    } else {
+      load(t, y);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      y[i] = silu(y[i]);
+      ss += y[i] * y[i];
+    }
+    if (l2) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-6f);
+#pragma unroll
+      for (int i = 0; i < V; ++i) y[i] *= inv;
+    }
+    __nv_bfloat16* dst = out + (((long long)t * H + h) * T + s) * D + lane * V;
+#pragma unroll
+    for (int i = 0; i < V; i += 2) *reinterpret_cast<uint32_t*>(dst + i) = pack_bf16(y[i], y[i + 1]);
+    if (taps > 0) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int i = 0; i < V; ++i) ring[k][i] = ring[k + 1][i];
+      load(t + 1 - pad + 4, ring[4]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// 3. alpha gate.  down[rows, ld_down] fp32 (the x W_down^T columns, computed by the
+// projection GEMM), mean over the T rows of each frame, then up + dt_bias, softplus.
+// grid F, block 256.  alpha out [F, H, D] fp32.
+// ---------------------------------------------------------------------------------
+__global__ void alpha_gate_kernel(const float* __restrict__ down, long long ld_down, int T, int R,
+                                  const float* __restrict__ w_up, const float* __restrict__ dt_bias,
+                                  const float* __restrict__ a_log, int H, int D, float* __restrict__ alpha) {
+  extern __shared__ float mean[];
+  const int f = blockIdx.x;
+  for (int j = threadIdx.x; j < R; j += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < T; ++s) acc += down[((long long)f * T + s) * ld_down + j];
+    mean[j] = acc / (float)T;
+  }
+  __syncthreads();
+  const int inner = H * D;
+  for (int c = threadIdx.x; c < inner; c += blockDim.x) {
+    float d = dt_bias[c];
+    const float* wr = w_up + (long long)c * R;
+    for (int j = 0; j < R; ++j) d += wr[j] * mean[j];
+    const int h = c / D;
+    alpha[(long long)f * inner + c] = __expf(-__expf(a_log[h]) * softplusf_(d));
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// 4. Frame statistics.  K, V FHSD bf16 [F, H, T, D]; beta logits [rows, ld_beta] fp32 with
+// row = f*T + s, column beta_col0 + h.  A, B out [F, H, D, D] fp32.  grid (H, F), 256 thr.
+// ---------------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(256) frame_stats_kernel(const __nv_bfloat16* __restrict__ K,
+                                                          const __nv_bfloat16* __restrict__ V, int T, int H,
+                                                          const float* __restrict__ beta_logits,
+                                                          long long ld_beta, int beta_col0,
+                                                          float* __restrict__ A, float* __restrict__ Bm) {
+  constexpr int CH = 32;        // tokens per chunk
+  constexpr int TB = D / 16;    // per-thread block edge: 8 for D=128, 4 for D=64
+  __shared__ float sk[CH][D];
+  __shared__ float sv[CH][D];
+  __shared__ float sb[CH];
+  const int h = blockIdx.x, f = blockIdx.y;
+  const int ti = threadIdx.x / 16, tj = threadIdx.x % 16;  // 16 x 16 thread grid
+  const int i0 = ti * TB, j0 = tj * TB;
+  float a[TB][TB], b[TB][TB];
+#pragma unroll
+  for (int i = 0; i < TB; ++i)
+#pragma unroll
+    for (int j = 0; j < TB; ++j) a[i][j] = b[i][j] = 0.f;
+  const long long base = ((long long)f * H + h) * T * D;
+  for (int s0 = 0; s0 < T; s0 += CH) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < CH * D; e += 256) {
+      const int s = e / D, d = e % D;
+      const bool in = s0 + s < T;
+      sk[s][d] = in ? __bfloat162float(K[base + (long long)(s0 + s) * D + d]) : 0.f;
+      sv[s][d] = in ? __bfloat162float(V[base + (long long)(s0 + s) * D + d]) : 0.f;
+    }
+    if (threadIdx.x < CH) {
+      const int s = s0 + threadIdx.x;
+      sb[threadIdx.x] = s < T ? sigmoidf_(beta_logits[((long long)f * T + s) * ld_beta + beta_col0 + h]) : 0.f;
+    }
+    __syncthreads();
+    const int n = min(CH, T - s0);
+    for (int s = 0; s < n; ++s) {
+      const float bt = sb[s];
+      float ki[TB], vi[TB], kj[TB];
+#pragma unroll
+      for (int i = 0; i < TB; ++i) {
+        ki[i] = sk[s][i0 + i] * bt;
+        vi[i] = sv[s][i0 + i] * bt;
+        kj[i] = sk[s][j0 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < TB; ++i)
+#pragma unroll
+        for (int j = 0; j < TB; ++j) {
+          a[i][j] += ki[i] * kj[j];
+          b[i][j] += vi[i] * kj[j];
+        }
+    }
+  }
+  const long long ob = ((long long)f * H + h) * D * D;
+#pragma unroll
+  for (int i = 0; i < TB; ++i)
+#pragma unroll
+    for (int j = 0; j < TB; ++j) {
+      A[ob + (long long)(i0 + i) * D + j0 + j] = a[i][j];
+      Bm[ob + (long long)(i0 + i) * D + j0 + j] = b[i][j];
+    }
+}
+
+// ---------------------------------------------------------------------------------
+// 5. Delta factor: inv = (I + sym(A))^-1 by Cholesky (lower), L^-1 by forward substitution,
+// inv = L^-T L^-1.  info[batch] = order of the first non-positive leading minor (0 = SPD).
+// For batches listed as text frames, also s0 = scale * B inv.  grid (H, F), 256 threads.
+// ---------------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(256) delta_factor_kernel(const float* __restrict__ A, const float* __restrict__ Bm,
+                                                           int H, float* __restrict__ inv_out,
+                                                           int* __restrict__ info, int text_frame,
+                                                           float text_scale, float* __restrict__ s0_out) {
+  constexpr int P = D + 1;  // padded pitch
+  extern __shared__ float sm[];
+  float* Lm = sm;            // [D][P]  M -> L (lower)
+  float* X = sm + D * P;     // [D][P]  X = L^-1 (lower)
+  __shared__ int bad;
+  const int h = blockIdx.x, f = blockIdx.y;
+  const long long mb = ((long long)f * H + h) * D * D;
+  const int tid = threadIdx.x;
+  for (int e = tid; e < D * D; e += 256) {
+    const int i = e / D, j = e % D;
+    float v = 0.5f * (A[mb + (long long)i * D + j] + A[mb + (long long)j * D + i]);
+    if (i == j) v += 1.0f;
+    Lm[i * P + j] = v;
+  }
+  if (tid == 0) bad = 0;
+  __syncthreads();
+  // Right-looking Cholesky, lower triangle in place.
+  for (int k = 0; k < D; ++k) {
+    const float dkk = Lm[k * P + k];
+    if (dkk <= 0.f || !(dkk == dkk)) {
+      if (tid == 0 && bad == 0) bad = k + 1;
+      break;  // uniform: every thread reads the same value
+    }
+    const float d = sqrtf(dkk);
+    __syncthreads();
+    if (tid == 0) Lm[k * P + k] = d;
+    for (int i = k + 1 + tid; i < D; i += 256) Lm[i * P + k] /= d;
+    __syncthreads();
+    // trailing update of the lower triangle: rows i > k, columns k < j <= i
+    const int n = D - k - 1;
+    for (int e = tid; e < n * n; e += 256) {
+      const int i = k + 1 + e / n, j = k + 1 + e % n;
+      if (j <= i) Lm[i * P + j] -= Lm[i * P + k] * Lm[j * P + k];
+    }
+    __syncthreads();
+  }
+  __syncthreads();
+  if (tid == 0) info[(long long)f * H + h] = bad;
+  if (bad) {
+    for (int e = tid; e < D * D; e += 256) inv_out[mb + e] = __int_as_float(0x7fc00000);
+    return;
+  }
+  // X = L^-1, one column j per thread (threads >= D idle).
+  if (tid < D) {
+    const int j = tid;
+    for (int i = 0; i < D; ++i) {
+      if (i < j) {
+        X[i * P + j] = 0.f;
+        continue;
+      }
+      float acc = (i == j) ? 1.f : 0.f;
+      for (int k = j; k < i; ++k) acc -= Lm[i * P + k] * X[k * P + j];
+      X[i * P + j] = acc / Lm[i * P + i];
+    }
+  }
+  __syncthreads();
+  // inv[i][j] = sum_k X[k][i] X[k][j], k >= max(i, j)
+  for (int e = tid; e < D * D; e += 256) {
+    const int i = e / D, j = e % D;
+    float acc = 0.f;
+    for (int k = max(i, j); k < D; ++k) acc += X[k * P + i] * X[k * P + j];
+    inv_out[mb + e] = acc;
+  }
+  if (f == text_frame && s0_out) {
+    __syncthreads();
+    // reuse Lm for inv (full, symmetric)
+    for (int e = tid; e < D * D; e += 256) Lm[(e / D) * P + (e % D)] = inv_out[mb + e];
+    __syncthreads();
+    for (int e = tid; e < D * D; e += 256) {
+      const int r = e / D, c = e % D;
+      float acc = 0.f;
+      for (int k = 0; k < D; ++k) acc += Bm[mb + (long long)r * D + k] * Lm[k * P + c];
+      s0_out[(long long)h * D * D + e] = text_scale * acc;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// 6. Bidirectional scan, state rows split across CTAs (the rows of s evolve independently).
+// grid (H, 2 directions, D / RB), 256 threads.  states out [F, H, D, D] fp32 (prefix, suffix).
+// ---------------------------------------------------------------------------------
+template <int D, int RB>
+__global__ void __launch_bounds__(256) bidir_scan_kernel(const float* __restrict__ inv, const float* __restrict__ Bm,
+                                                         const float* __restrict__ alpha, const float* __restrict__ s0,
+                                                         int F, int H, float* __restrict__ prefix,
+                                                         float* __restrict__ suffix) {
+  extern __shared__ float sm[];
+  float* sinv = sm;             // [D][D]
+  float* u = sm + D * D;        // [RB][D]
+  const int h = blockIdx.x, dir = blockIdx.y, r0 = blockIdx.z * RB;
+  const int tid = threadIdx.x;
+  constexpr int OUT = RB * D / 256;  // outputs per thread
+  const int r = (tid * OUT) / D, c0 = (tid * OUT) % D;
+  float s[OUT];
+#pragma unroll
+  for (int o = 0; o < OUT; ++o) s[o] = s0 ? s0[((long long)h * D + r0 + r) * D + c0 + o] : 0.f;
+  float* dst_all = dir == 0 ? prefix : suffix;
+  for (int step = 0; step < F; ++step) {
+    const int t = dir == 0 ? step : F - 1 - step;
+    const long long mb = ((long long)t * H + h) * D * D;
+    __syncthreads();
+    for (int e = tid * 4; e < D * D; e += 256 * 4)
+      *reinterpret_cast<float4*>(sinv + e) = *reinterpret_cast<const float4*>(inv + mb + e);
+    const float* al = alpha + ((long long)t * H + h) * D;
+#pragma unroll
+    for (int o = 0; o < OUT; ++o)
+      u[r * D + c0 + o] = Bm[mb + (long long)(r0 + r) * D + c0 + o] + s[o] * al[c0 + o];
+    __syncthreads();
+#pragma unroll
+    for (int o = 0; o < OUT; ++o) s[o] = 0.f;
+    for (int i = 0; i < D; ++i) {
+      const float ui = u[r * D + i];
+#pragma unroll
+      for (int o = 0; o < OUT; ++o) s[o] += ui * sinv[i * D + c0 + o];
+    }
+#pragma unroll
+    for (int o = 0; o < OUT; ++o) dst_all[mb + (long long)(r0 + r) * D + c0 + o] = s[o];
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// 7. Readout: state (gather + alpha bridge, cast to bf16) -> R = Q S^T -> bf16 ->
+// RMSNorm(D) x norm_w -> bf16 -> x output gate -> out rows.
+// grid (ceil(T/64), H, F), 256 threads: thread = (token s = tid/4, v = g + 4*vi).
+// ---------------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(256) readout_kernel(
+    const __nv_bfloat16* __restrict__ Q, int T, int F, int H, const float* __restrict__ prefix,
+    const float* __restrict__ suffix, const float* __restrict__ alpha, const float* __restrict__ s0,
+    const int* __restrict__ lo_arr, const int* __restrict__ hi_arr, int use_alpha,
+    const float* __restrict__ norm_w, const __nv_bfloat16* __restrict__ gate, long long ld_gate,
+    __nv_bfloat16* __restrict__ out, long long ld_out, long long out_row0) {
+  constexpr int P = D + 1;
+  extern __shared__ float sm[];
+  float* st = sm;            // [D][P] state (v, k)
+  float* sq = sm + D * P;    // [64][P] q tile
+  __shared__ float dec_b[D], dec_a[D];
+  const int tile = blockIdx.x, h = blockIdx.y, f = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int raw_lo = lo_arr[f], raw_hi = hi_arr[f];
+  const int lo = max(raw_lo, 0), hi = min(raw_hi, F - 1);
+  const bool has_before = raw_lo - 1 >= 0, has_after = raw_hi + 1 < F;
+  // decays
+  for (int k = tid; k < D; k += 256) {
+    float lb = 0.f, la = 0.f;
+    if (use_alpha) {
+      for (int j = lo; j <= f; ++j) lb += __logf(fmaxf(alpha[((long long)j * H + h) * D + k], 1e-12f));
+      for (int j = f; j <= hi; ++j) la += __logf(fmaxf(alpha[((long long)j * H + h) * D + k], 1e-12f));
+    }
+    dec_b[k] = __expf(lb);
+    dec_a[k] = __expf(la);
+  }
+  __syncthreads();
+  const float* pb = has_before ? prefix + (((long long)(lo - 1) * H + h) * D * D) : (s0 ? s0 + (long long)h * D * D : nullptr);
+  const float* pa = has_after ? suffix + (((long long)(hi + 1) * H + h) * D * D) : (s0 ? s0 + (long long)h * D * D : nullptr);
+  for (int e = tid; e < D * D; e += 256) {
+    const int v = e / D, k = e % D;
+    float val = 0.f;
+    if (pb) val += pb[e] * dec_b[k];
+    if (pa) val += pa[e] * dec_a[k];
+    st[v * P + k] = bf16_round(val);
+  }
+  const int s_base = tile * 64;
+  for (int e = tid; e < 64 * D; e += 256) {
+    const int s = e / D, k = e % D;
+    sq[s * P + k] = (s_base + s < T) ? __bfloat162float(Q[(((long long)f * H + h) * T + s_base + s) * D + k]) : 0.f;
+  }
+  __syncthreads();
+  const int s = tid / 4, g = tid % 4;
+  constexpr int NV = D / 4;
+  float acc[NV];
+#pragma unroll
+  for (int vi = 0; vi < NV; ++vi) acc[vi] = 0.f;
+  for (int k = 0; k < D; ++k) {
+    const float qk = sq[s * P + k];
+#pragma unroll
+    for (int vi = 0; vi < NV; ++vi) acc[vi] += qk * st[(g + 4 * vi) * P + k];
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int vi = 0; vi < NV; ++vi) {
+    acc[vi] = bf16_round(acc[vi]);
+    ss += acc[vi] * acc[vi];
+  }
+  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+  const float inv = rsqrtf(ss / (float)D + 1e-6f);
+  const int tok = s_base + s;
+  if (tok < T) {
+    const long long row = out_row0 + (long long)f * T + tok;
+#pragma unroll
+    for (int vi = 0; vi < NV; ++vi) {
+      const int v = g + 4 * vi;
+      const float nv = bf16_round(acc[vi] * inv * norm_w[v]);
+      const float gv = __bfloat162float(gate[row * ld_gate + h * D + v]);
+      out[row * ld_out + h * D + v] = __float2bfloat16_rn(nv * gv);
+    }
+  }
+}
+
+// fp32 [rows, ld_in] (columns col0..col0+cols) -> bf16 [rows, ld_out]
+__global__ void cast_rows_kernel(const float* __restrict__ in, long long ld_in, int col0, int rows, int cols,
+                                 __nv_bfloat16* __restrict__ out, long long ld_out) {
+  const long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= (long long)rows * cols) return;
+  const long long r = e / cols;
+  const int c = (int)(e % cols);
+  out[r * ld_out + c] = __float2bfloat16_rn(in[r * ld_in + col0 + c]);
+}
+
+}  // namespace branch
+}  // namespace vdn
+
+using namespace vdn::branch;
+
+extern "C" {
+
+// 1. Depthwise spatial conv (branch.py:469-471).  in rows f*gh*gw + y*gw + x, channels [0, C).
+int vdn_spatial_conv(const void* in, long long ld_in, const float* w, int kh, int kw, int F, int gh, int gw, int C,
+                     void* out, long long ld_out, void* stream) {
+  if (!in || !w || !out || kh <= 0 || kw <= 0 || kh * kw > 49 || (kh % 2) == 0 || (kw % 2) == 0)
+    return vdn::kBadArgument;
+  if (F <= 0 || gh <= 0 || gw <= 0 || C <= 0) return vdn::kBadArgument;
+  dim3 grid(gh, F, (C + 255) / 256);
+  spatial_conv_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, kh, kw, gh, gw, C,
+      reinterpret_cast<__nv_bfloat16*>(out), ld_out);
+  return vdn::launch_status();
+}
+
+// 2. Temporal 5-tap conv (taps = 5) or none (taps = 0), SiLU, optional L2; FHSD output.
+// Replaces kernels.py:99-162 (temporal) and kernels.py:47-51 + the FHSD permute.
+int vdn_temporal_act(const void* in, long long ld_in, const float* w, int taps, int F, int T, int H, int D,
+                     int l2norm, void* out, void* stream) {
+  if (!in || !out || (taps != 0 && taps != 1 && taps != 3 && taps != 5) || (taps && !w)) return vdn::kBadArgument;
+  if (D != 64 && D != 128) return vdn::kUnsupported;
+  const long long warps = (long long)T * H;
+  const int blocks = (int)((warps * 32 + 255) / 256);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (D == 128)
+    temporal_act_kernel<128><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, taps, F,
+                                                     T, H, l2norm, reinterpret_cast<__nv_bfloat16*>(out));
+  else
+    temporal_act_kernel<64><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, taps, F, T,
+                                                    H, l2norm, reinterpret_cast<__nv_bfloat16*>(out));
+  return vdn::launch_status();
+}
+
+// 3. alpha gate (branch.py:483-491, frame mean :743-745).  down: [F*T, ld_down] fp32 holding
+// x W_down^T (R columns); w_up [H*D, R] fp32; alpha out [F, H, D] fp32.
+int vdn_alpha_gate(const float* down, long long ld_down, int F, int T, int R, const float* w_up,
+                   const float* dt_bias, const float* a_log, int H, int D, float* alpha, void* stream) {
+  if (!down || !w_up || !dt_bias || !a_log || !alpha || F <= 0 || T <= 0 || R <= 0) return vdn::kBadArgument;
+  alpha_gate_kernel<<<F, 256, R * sizeof(float), reinterpret_cast<cudaStream_t>(stream)>>>(
+      down, ld_down, T, R, w_up, dt_bias, a_log, H, D, alpha);
+  return vdn::launch_status();
+}
+
+// 4. Frame statistics (branch.py:197-243).  K, V FHSD [F, H, T, D] bf16.
+int vdn_frame_stats(const void* K, const void* V, int F, int H, int T, int D, const float* beta_logits,
+                    long long ld_beta, int beta_col0, float* A, float* B, void* stream) {
+  if (!K || !V || !beta_logits || !A || !B) return vdn::kBadArgument;
+  dim3 grid(H, F);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (D == 128)
+    frame_stats_kernel<128><<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(K),
+                                                 reinterpret_cast<const __nv_bfloat16*>(V), T, H, beta_logits,
+                                                 ld_beta, beta_col0, A, B);
+  else if (D == 64)
+    frame_stats_kernel<64><<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(K),
+                                                reinterpret_cast<const __nv_bfloat16*>(V), T, H, beta_logits,
+                                                ld_beta, beta_col0, A, B);
+  else
+    return vdn::kUnsupported;
+  return vdn::launch_status();
+}
+
+// 5. Delta factor (branch.py:148-160, info semantics of cholesky_ex as in :62-71).
+// A, B: [F, H, D, D] fp32.  inv out [F, H, D, D]; info [F, H] int32.  If text_frame >= 0,
+// s0 [H, D, D] = text_scale * B[text_frame] inv[text_frame] (branch.py:649-670).
+int vdn_delta_factor(const float* A, const float* B, int F, int H, int D, float* inv, int* info, int text_frame,
+                     float text_scale, float* s0, void* stream) {
+  if (!A || !inv || !info || (text_frame >= 0 && (!B || !s0))) return vdn::kBadArgument;
+  dim3 grid(H, F);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  const size_t smem = 2 * (size_t)D * (D + 1) * sizeof(float);
+  if (D == 128) {
+    cudaFuncSetAttribute(delta_factor_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    delta_factor_kernel<128><<<grid, 256, smem, s>>>(A, B, H, inv, info, text_frame, text_scale, s0);
+  } else if (D == 64) {
+    delta_factor_kernel<64><<<grid, 256, smem, s>>>(A, B, H, inv, info, text_frame, text_scale, s0);
+  } else {
+    return vdn::kUnsupported;
+  }
+  return vdn::launch_status();
+}
+
+// 6. Bidirectional scan (branch.py:297-312 with the factor applied on the fly).
+// inv, B: [F, H, D, D]; alpha [F, H, D]; s0 [H, D, D] or NULL (zero start).
+int vdn_bidir_scan(const float* inv, const float* B, const float* alpha, const float* s0, int F, int H, int D,
+                   float* prefix, float* suffix, void* stream) {
+  if (!inv || !B || !alpha || !prefix || !suffix) return vdn::kBadArgument;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  constexpr int RB = 16;
+  if (D == 128) {
+    const size_t smem = (size_t)(128 * 128 + RB * 128) * sizeof(float);
+    cudaFuncSetAttribute(bidir_scan_kernel<128, RB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    bidir_scan_kernel<128, RB><<<dim3(H, 2, 128 / RB), 256, smem, s>>>(inv, B, alpha, s0, F, H, prefix, suffix);
+  } else if (D == 64) {
+    const size_t smem = (size_t)(64 * 64 + 2 * RB * 64) * sizeof(float);
+    bidir_scan_kernel<64, 2 * RB><<<dim3(H, 2, 64 / (2 * RB)), 256, smem, s>>>(inv, B, alpha, s0, F, H, prefix,
+                                                                               suffix);
+  } else {
+    return vdn::kUnsupported;
+  }
+  return vdn::launch_status();
+}
+
+// 7. Readout + epilogue (branch.py:372-396, :494-530, :780).  Q FHSD [F, H, T, D] bf16;
+// lo/hi [F] int32 raw window bounds of the branch frames; gate [rows, ld_gate] bf16 holding
+// sigmoid(up(down x) + b); out rows out_row0 + f*T + s, columns h*D + v.
+int vdn_readout(const void* Q, int F, int H, int T, int D, const float* prefix, const float* suffix,
+                const float* alpha, const float* s0, const int* lo, const int* hi, int use_alpha,
+                const float* norm_w, const void* gate, long long ld_gate, void* out, long long ld_out,
+                long long out_row0, void* stream) {
+  if (!Q || !prefix || !suffix || !alpha || !lo || !hi || !norm_w || !gate || !out) return vdn::kBadArgument;
+  dim3 grid((T + 63) / 64, H, F);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  const size_t smem = (size_t)(D + 64) * (D + 1) * sizeof(float);
+  if (D == 128) {
+    cudaFuncSetAttribute(readout_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    readout_kernel<128><<<grid, 256, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(Q), T, F, H, prefix, suffix,
+                                                alpha, s0, lo, hi, use_alpha, norm_w,
+                                                reinterpret_cast<const __nv_bfloat16*>(gate), ld_gate,
+                                                reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0);
+  } else if (D == 64) {
+    readout_kernel<64><<<grid, 256, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(Q), T, F, H, prefix, suffix,
+                                               alpha, s0, lo, hi, use_alpha, norm_w,
+                                               reinterpret_cast<const __nv_bfloat16*>(gate), ld_gate,
+                                               reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0);
+  } else {
+    return vdn::kUnsupported;
+  }
+  return vdn::launch_status();
+}
+
+// fp32 -> bf16 copy of a column block (used for the output-gate bottleneck, which the
+// reference rounds to the activation dtype: branch.py:755).
+int vdn_cast_rows(const float* in, long long ld_in, int col0, int rows, int cols, void* out, long long ld_out,
+                  void* stream) {
+  if (!in || !out || rows < 0 || cols <= 0) return vdn::kBadArgument;
+  const long long n = (long long)rows * cols;
+  if (n == 0) return vdn::kOk;
+  cast_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      in, ld_in, col0, rows, cols, reinterpret_cast<__nv_bfloat16*>(out), ld_out);
+  return vdn::launch_status();
+}
+
+}  // extern "C"

@@ -1,0 +1,69 @@
+// Host-side helpers shared by the C-ABI entry points: TMA tensor-map encoding through
+// the driver entry point (no -lcuda link), status codes and SM-count caching.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+
+namespace vdn {
+
+// C-ABI status codes (the host wrapper maps them to Python exceptions).
+enum : int {
+  kOk = 0,
+  kBadArgument = -1,      // ValueError
+  kUnsupported = -2,      // ValueError (geometry outside what the kernels handle)
+  kTensorMapFailed = -3,  // RuntimeError
+  kLaunchFailed = -4,     // RuntimeError (cudaGetLastError after launch)
+  kMisaligned = -5,       // ValueError (pointer / stride not 16-byte aligned)
+};
+
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  }
+  return fn;
+}
+
+// 2-D row-major tensor [outer][inner] with a row pitch of `row_stride_elems`.
+inline int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                        int elem_bytes, uint64_t inner, uint64_t outer,
+                        uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return kTensorMapFailed;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((row_stride_elems * elem_bytes) & 15))
+    return kMisaligned;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estride,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kTensorMapFailed;
+}
+
+inline int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev] > 0 ? n[dev] : 148;
+}
+
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+}  // namespace vdn

@@ -1,0 +1,330 @@
+"""The VDN-H3 hybrid attention block on sm_100a (replaces vdn_h3/hybrid.py's operator).
+
+``make_vdn_forward(attn, state, block_index)`` returns the same patched
+``attn.forward(x, rope_freqs=None, transformer_options=None)`` the reference installs
+(hybrid.py:409-579): layout from the request ContextVar, QKV, the linear branch on the
+raw video q/k/v, q/k RMSNorm, exact window softmax, per-token head gate, out_proj and
+the branch delta added on the video rows.
+
+On the device one block forward is four phases, all on the caller's stream:
+
+1. one tcgen05 GEMM of x against [W_qkv; W_gate; W_beta; W_og_down; W_alpha_down]
+   writing raw q/k/v (bf16), per-head RMS-normalised q/k (bf16) and the side
+   projections (fp32) from a single pass over x;
+2. the branch kernels (features, alpha, statistics, Cholesky inverse, fused scan,
+   gather/readout/RMSNorm/output gate) writing the branch rows of a [S, H*D] buffer;
+3. the block-sparse window attention kernel with the gate fused in its epilogue;
+4. one tcgen05 GEMM over K = 2*H*D of [gated softmax | branch] against
+   [W_out | W_to_out]: out_proj, to_out_linear and the delta add in one pass (bf16);
+   the quantised precisions run out_proj then to_out_linear with an addend epilogue.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Mapping
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .branch import BranchDeviceWeights, BranchWorkspace, cholesky_runtime_scope, run_branch
+from .layout import VDNLayout, current_layout
+from .projection import KIND, QuantizedMatrix, quantize_rows_int8, quantize_tensor_fp8, quantize_weight
+from .window import ATTENTION_BACKENDS, WindowPlanCache, launch_window_attention
+
+AUX_ALIGN = 256
+
+
+def _weight_of(module_or_tensor):
+    w = getattr(module_or_tensor, "weight", module_or_tensor)
+    return w.detach()
+
+
+@dataclass
+class BlockGeometry:
+    heads: int
+    dim: int
+    hidden: int
+
+    @property
+    def inner(self):
+        return self.heads * self.dim
+
+
+class FusedBlock:
+    """Device weights of one H3 attention block + its VDN branch, laid out for the kernels."""
+
+    def __init__(self, qkv_w, q_norm_w, k_norm_w, out_w, branch_w: Mapping, heads, dim, device, *,
+                 precision="bf16", eps=1e-6, enable_gate=True, short_conv=("k", "v")):
+        dev = torch.device(device)
+        H, D = int(heads), int(dim)
+        inner = H * D
+        hidden = int(qkv_w.shape[1])
+        if qkv_w.shape[0] != 3 * inner or out_w.shape != (hidden, inner):
+            raise ValueError("attention weights do not match the head geometry")
+        self.geo = BlockGeometry(H, D, hidden)
+        self.device = dev
+        self.precision = precision
+        self.eps = float(eps)
+        self.enable_gate = bool(enable_gate)
+        self.short_conv = tuple(short_conv)
+
+        def f32(t):
+            return t.detach().to(dev, torch.float32).contiguous()
+
+        def b16(t):
+            return t.detach().to(dev, torch.bfloat16).contiguous()
+
+        zeros_h = torch.zeros(H, hidden)
+        gate_w = branch_w.get("softmax_gate.up.weight", zeros_h) if enable_gate else zeros_h
+        self.gate_bias = f32(branch_w.get("softmax_gate.up.bias", torch.zeros(H))) if enable_gate else None
+        side = [gate_w, branch_w.get("beta_proj.weight", zeros_h), branch_w.get("output_gate.down.weight",
+                torch.zeros(D, hidden)), branch_w.get("alpha.down.weight", torch.zeros(D, hidden))]
+        n_side = 2 * H + 2 * D
+        self.n_aux = (n_side + AUX_ALIGN - 1) // AUX_ALIGN * AUX_ALIGN
+        pad = torch.zeros(self.n_aux - n_side, hidden)
+        side_w = torch.cat([s.detach().float().cpu() for s in side] + [pad], 0)
+        # aux column offsets
+        self.col_gate, self.col_beta, self.col_ogd, self.col_ad = 0, H, 2 * H, 2 * H + D
+        self.norm_w = torch.cat([f32(q_norm_w), f32(k_norm_w)]).contiguous()
+        self.has_branch = "to_out_linear.weight" in branch_w or "to_out_linear.weight_fp8" in branch_w
+        to_out = branch_w.get("to_out_linear.weight")
+        if precision == "bf16":
+            self.w_big = torch.cat([b16(qkv_w), side_w.to(dev, torch.bfloat16)], 0).contiguous()
+            if self.has_branch and to_out is not None:
+                self.w_out_cat = torch.cat([b16(out_w), b16(to_out)], 1).contiguous()
+            else:
+                self.w_out_cat = torch.cat([b16(out_w), torch.zeros(hidden, inner, device=dev,
+                                                                    dtype=torch.bfloat16)], 1).contiguous()
+        else:
+            self.w_qkv_q = quantize_weight(qkv_w, precision, dev)
+            self.w_side = side_w.to(dev, torch.bfloat16).contiguous()
+            self.w_out_q = quantize_weight(out_w, precision, dev)
+            self.w_to_q = quantize_weight(to_out, precision, dev) if to_out is not None else None
+        self.bw = BranchDeviceWeights.from_dict(branch_w, H, D, dev, short_conv=self.short_conv) if self.has_branch \
+            else None
+        self._ws: dict = {}
+
+    # ------------------------------------------------------------------ workspaces
+    def workspace(self, S: int, layout: VDNLayout | None):
+        key = (S, None if layout is None else (layout.num_frames, layout.tokens_per_frame, layout.text_len,
+                                               layout.anchor_frames))
+        ws = self._ws.get(key)
+        if ws is None:
+            g = self.geo
+            dev = self.device
+            bf = dict(device=dev, dtype=torch.bfloat16)
+            ws = {
+                "qkv": torch.empty(S, 3 * g.inner, **bf),
+                "qkn": torch.empty(S, 2 * g.inner, **bf),
+                "aux": torch.empty(S, self.n_aux, device=dev, dtype=torch.float32),
+                "flat": torch.empty(S, g.inner, **bf),
+                "branch": torch.zeros(S, g.inner, **bf),
+            }
+            if self.precision != "bf16":
+                qdt = torch.int8 if self.precision == "int8" else torch.float8_e4m3fn
+                sdim = S if self.precision == "int8" else 1
+                for name, k in (("xq", g.hidden), ("fq", g.inner), ("bq", g.inner)):
+                    ws[name] = QuantizedMatrix(torch.empty(S, k, device=dev, dtype=qdt),
+                                               torch.empty(sdim, device=dev, dtype=torch.float32), self.precision)
+                ws["work"] = torch.empty(1, device=dev, dtype=torch.float32)
+            if layout is not None and self.bw is not None and not layout.full_cover:
+                skip = layout.anchor_frames == "both"
+                Fb = layout.num_frames - 2 if skip else layout.num_frames
+                if Fb > 0:
+                    ws["bws"] = BranchWorkspace(dev, Fb, layout.tokens_per_frame, g.heads, g.dim, layout.text_len)
+            self._ws[key] = ws
+        return ws
+
+    # ------------------------------------------------------------------ phases
+    def _qkv(self, x, ws, status, stream):
+        g = self.geo
+        S = x.shape[0]
+        if self.precision == "bf16":
+            _lib.call("vdn_qkv_gemm", 0, x.data_ptr(), x.stride(0), self.w_big.data_ptr(), self.w_big.stride(0), S,
+                      g.hidden, g.inner, self.n_aux, g.dim, self.norm_w.data_ptr(), self.eps, 1.0, None, None, None,
+                      None, ws["qkv"].data_ptr(), ws["qkv"].stride(0), ws["qkn"].data_ptr(), ws["qkn"].stride(0),
+                      ws["aux"].data_ptr(), ws["aux"].stride(0), status.err_ptr, stream)
+            return
+        kind = KIND[self.precision]
+        if self.precision == "int8":
+            xq = quantize_rows_int8(x, ws["xq"])
+            rs, cs, d0, d1 = xq.scale, self.w_qkv_q.scale, None, None
+        else:
+            xq = quantize_tensor_fp8(x, ws["xq"], ws["work"])
+            rs, cs, d0, d1 = None, None, xq.scale, self.w_qkv_q.scale
+        _lib.call("vdn_qkv_gemm", kind, xq.data.data_ptr(), xq.data.stride(0), self.w_qkv_q.data.data_ptr(),
+                  self.w_qkv_q.data.stride(0), S, g.hidden, g.inner, 0, g.dim, self.norm_w.data_ptr(), self.eps, 1.0,
+                  _lib.ptr(d0), _lib.ptr(d1), _lib.ptr(rs), _lib.ptr(cs), ws["qkv"].data_ptr(), ws["qkv"].stride(0),
+                  ws["qkn"].data_ptr(), ws["qkn"].stride(0), None, 0, status.err_ptr, stream)
+        # side projections stay bf16 -> fp32 (gates, beta, alpha are never quantised: fp8.py:1-12)
+        _lib.call("vdn_gemm", 0, x.data_ptr(), x.stride(0), None, 0, 0, self.w_side.data_ptr(),
+                  self.w_side.stride(0), ws["aux"].data_ptr(), ws["aux"].stride(0), 1, S, self.n_aux, g.hidden, 1.0,
+                  None, None, None, None, None, 0, None, 0, status.err_ptr, stream)
+
+    def _out(self, ws, out, with_branch, status, stream):
+        g = self.geo
+        S = out.shape[0]
+        if self.precision == "bf16":
+            K = 2 * g.inner if with_branch else g.inner
+            a2 = ws["branch"] if with_branch else None
+            _lib.call("vdn_gemm", 0, ws["flat"].data_ptr(), ws["flat"].stride(0), _lib.ptr(a2),
+                      ws["branch"].stride(0) if with_branch else 0, g.inner if with_branch else 0,
+                      self.w_out_cat.data_ptr(), self.w_out_cat.stride(0), out.data_ptr(), out.stride(0), 0, S,
+                      g.hidden, K, 1.0, None, None, None, None, None, 0, None, 0, status.err_ptr, stream)
+            return
+        kind = KIND[self.precision]
+
+        def quantized_gemm(src, buf, w: QuantizedMatrix, addend):
+            if self.precision == "int8":
+                qa = quantize_rows_int8(src, buf)
+                rs, cs, d0, d1 = qa.scale, w.scale, None, None
+            else:
+                qa = quantize_tensor_fp8(src, buf, ws["work"])
+                rs, cs, d0, d1 = None, None, qa.scale, w.scale
+            _lib.call("vdn_gemm", kind, qa.data.data_ptr(), qa.data.stride(0), None, 0, 0, w.data.data_ptr(),
+                      w.data.stride(0), out.data_ptr(), out.stride(0), 0, S, g.hidden, g.inner, 1.0, _lib.ptr(d0),
+                      _lib.ptr(d1), _lib.ptr(rs), _lib.ptr(cs), None, 0, _lib.ptr(addend),
+                      addend.stride(0) if addend is not None else 0, status.err_ptr, stream)
+
+        quantized_gemm(ws["flat"], ws["fq"], self.w_out_q, None)
+        if with_branch and self.w_to_q is not None:
+            quantized_gemm(ws["branch"], ws["bq"], self.w_to_q, out)
+
+    def forward(self, x: torch.Tensor, layout: VDNLayout, plans: WindowPlanCache, status: _lib.DeviceStatus,
+                *, linear_enabled=True, bridge="alpha", enable_text_state=True, out=None) -> torch.Tensor:
+        g = self.geo
+        S = x.shape[0]
+        if x.dtype != torch.bfloat16 or x.stride(-1) != 1:
+            x = x.to(torch.bfloat16).contiguous()
+        stream = _lib.stream_handle(x.device)
+        ws = self.workspace(S, layout)
+        self._qkv(x, ws, status, stream)
+        linear_active = linear_enabled and not layout.full_cover and self.bw is not None and "bws" in ws
+        if linear_active:
+            skip = layout.anchor_frames == "both"
+            tpf = layout.tokens_per_frame
+            Fb = layout.num_frames - 2 if skip else layout.num_frames
+            r0 = layout.video_start + (tpf if skip else 0)
+            rows = slice(r0, r0 + Fb * tpf)
+            bounds_b = [(lo - 1, hi - 1) for lo, hi in layout.bounds[1:-1]] if skip else list(layout.bounds)
+            qkv, aux = ws["qkv"], ws["aux"]
+            kw = dict(q_raw=qkv[rows, :g.inner], k_raw=qkv[rows, g.inner:2 * g.inner],
+                      v_raw=qkv[rows, 2 * g.inner:], aux=aux[rows], beta_col0=self.col_beta, ogd_col0=self.col_ogd,
+                      ad_col0=self.col_ad, Fb=Fb, tpf=tpf, frame_size=layout.frame_size, bounds=bounds_b,
+                      bridge=bridge, out=ws["branch"], out_row0=r0, status=status, short_conv=self.short_conv)
+            if enable_text_state and layout.text_len > 0:
+                ts = slice(layout.text_start, layout.text_start + layout.text_len)
+                kw.update(text_k=qkv[ts, g.inner:2 * g.inner], text_v=qkv[ts, 2 * g.inner:], text_aux=aux[ts])
+            run_branch(ws["bws"], self.bw, **kw)
+        # window softmax with the fused gate
+        if layout.full_cover:
+            plan = plans.get(S, 0, S, 1, S, [(0, 0)], "none")
+        else:
+            plan = plans.get(S, layout.video_start, layout.video_end, layout.num_frames, layout.tokens_per_frame,
+                             layout.bounds, layout.anchor_frames)
+        qkn, qkv = ws["qkn"], ws["qkv"]
+        launch_window_attention(qkn[:, :g.inner], qkn[:, g.inner:], qkv[:, 2 * g.inner:], ws["flat"], plan, g.heads,
+                                g.dim, g.dim ** -0.5, status,
+                                gate_logits=ws["aux"] if self.enable_gate else None, gate_col0=self.col_gate,
+                                gate_bias=self.gate_bias)
+        if out is None:
+            out = torch.empty(S, g.hidden, device=x.device, dtype=torch.bfloat16)
+        self._out(ws, out, linear_active, status, stream)
+        return out
+
+
+class B200State:
+    """Runtime state of one patched model on the B200 path (counterpart of VDNState,
+    hybrid.py:33-150).  ``branches`` holds one weight mapping (or an object exposing it
+    as ``.w``) per block."""
+
+    def __init__(self, name, config: Mapping, branches, num_heads, head_dim, *, attention_backend="b200",
+                 projection_precision="bf16", inference=True, weight_maps=None, **_ignored):
+        if attention_backend not in ATTENTION_BACKENDS:
+            raise ValueError(f"unsupported attention backend {attention_backend!r}")
+        if projection_precision not in ("bf16", "fp8", "int8"):
+            raise ValueError(f"unsupported projection precision {projection_precision!r}")
+        self.name = str(name)
+        self.config = dict(config)
+        self.num_heads = int(num_heads)
+        self.head_dim = int(head_dim)
+        self.attention_backend = attention_backend
+        self.projection_precision = projection_precision
+        self.inference = bool(inference)
+        maps = list(weight_maps) if weight_maps is not None else [
+            b if isinstance(b, Mapping) else getattr(b, "w") for b in branches]
+        self.branches = list(branches)
+        self.weight_maps = maps
+        self.window_plans = WindowPlanCache(limit=24)
+        self.blocks: dict[int, FusedBlock] = {}
+        self.status: dict[str, _lib.DeviceStatus] = {}
+        self.forwards = 0
+        self.last_attention_backend = None
+
+    def device_status(self, device) -> _lib.DeviceStatus:
+        key = str(device)
+        if key not in self.status:
+            self.status[key] = _lib.DeviceStatus(device)
+        return self.status[key]
+
+    def fused_block(self, attn, index, device) -> FusedBlock:
+        fb = self.blocks.get(index)
+        if fb is None:
+            cfg = self.config
+            fb = FusedBlock(_weight_of(attn.qkv_proj), _weight_of(attn.q_norm), _weight_of(attn.k_norm),
+                            _weight_of(attn.out_proj), self.weight_maps[index], self.num_heads, self.head_dim,
+                            device, precision=self.projection_precision, eps=float(getattr(attn.q_norm, "eps", 1e-6)),
+                            enable_gate=bool(cfg.get("enable_softmax_gate", True)),
+                            short_conv=tuple(cfg.get("short_conv", ("k", "v"))))
+            self.blocks[index] = fb
+        return fb
+
+    def release(self):
+        self.blocks.clear()
+        self.window_plans.clear()
+        return self
+
+
+def make_vdn_forward(attn, state: B200State, block_index: int):
+    """Patched ``attn.forward`` (hybrid.py:409-579) running the sm_100a block."""
+    original_forward = attn.forward
+    heads, head_dim = int(attn.heads), int(attn.head_dim)
+    if heads != state.num_heads or head_dim != state.head_dim:
+        raise RuntimeError("attention geometry disagrees with the VDN state")
+    config = state.config
+
+    def vdn_forward(x, rope_freqs=None, transformer_options=None):
+        layout = current_layout(required=False)
+        if layout is None:
+            return original_forward(x, rope_freqs=rope_freqs, transformer_options=transformer_options or {})
+        if int(x.shape[0]) != layout.seq_len:
+            raise RuntimeError(f"VDN layout has {layout.seq_len} rows but attention received {x.shape[0]}")
+        if rope_freqs is not None:
+            raise NotImplementedError("RoPE is not implemented on the B200 path (rope_freqs must be None)")
+        _lib.require_cuda(x)
+        status = state.device_status(x.device)
+        block = state.fused_block(attn, block_index, x.device)
+        out = block.forward(x, layout, state.window_plans, status,
+                            linear_enabled=bool(config.get("linear_enabled", True)),
+                            bridge=str(config.get("bridge", "alpha")),
+                            enable_text_state=bool(config.get("enable_text_state", True)))
+        state.last_attention_backend = "b200_dense" if layout.full_cover else "b200"
+        return out.to(x.dtype)
+
+    vdn_forward._vdn_h3_forward = True
+    vdn_forward._vdn_h3_original = original_forward
+    return vdn_forward
+
+
+def run_forward_checked(state: B200State, fn, *args, **kwargs):
+    """Run one model forward inside the deferred Cholesky scope and check the kernels'
+    device status once at the end (the reference's layout wrapper, hybrid.py:216-241)."""
+    with cholesky_runtime_scope():
+        result = fn(*args, **kwargs)
+    for st in state.status.values():
+        st.raise_if_failed()
+    return result
+
+
+__all__ = ["B200State", "FusedBlock", "make_vdn_forward", "run_forward_checked"]

@@ -1,0 +1,158 @@
+"""Projections on sm_100a tensor cores (replaces vdn_h3/projection.py + vdn_h3/fp8.py).
+
+``project(rows, weights)`` keeps the reference dispatch on the stored weight
+(projection.py:259-268): a bf16 ``to_out_linear.weight`` runs the bf16 tcgen05 GEMM; a
+quantised ``to_out_linear.weight_fp8`` with ``to_out_linear.weight_scale`` runs the
+e4m3 (per-tensor) or int8 (per-output-channel weight, per-token activation) GEMM with
+the dequantisation fused into the epilogue.  ``prepare_projection_maps`` builds those
+quantised masters (fp8.py:168-222, projection.py:139-232); the int8 scheme is the
+config-2 one (symmetric, round-half-even, fp32 scales), not comfy-kitchen's ConvRot.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+BF16_WEIGHT_KEY = "to_out_linear.weight"
+QUANT_WEIGHT_KEY = "to_out_linear.weight_fp8"
+QUANT_SCALE_KEY = "to_out_linear.weight_scale"
+PROJECTION_PRECISIONS = ("bf16", "fp8", "int8")
+DEFAULT_FP8_SKIP_END_BLOCKS = 4  # fp8.py:35
+
+KIND = {"bf16": 0, "fp8": 1, "int8": 2}
+
+
+@dataclass
+class QuantizedMatrix:
+    """A [N, K] weight (or [M, K] activation) quantised for the tcgen05 GEMM."""
+
+    data: torch.Tensor  # int8 / float8_e4m3fn, row-major [rows, K]
+    scale: torch.Tensor  # int8: [rows] fp32; fp8: [1] fp32 (device scalar)
+    precision: str
+
+
+def _stream(t):
+    return _lib.stream_handle(t.device)
+
+
+def quantize_rows_int8(x: torch.Tensor, out: QuantizedMatrix | None = None) -> QuantizedMatrix:
+    """Per-row symmetric int8 of a bf16/fp32 [rows, K] tensor (round half to even)."""
+    _lib.require_cuda(x)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    rows, K = x.shape
+    if out is None:
+        out = QuantizedMatrix(torch.empty(rows, K, device=x.device, dtype=torch.int8),
+                              torch.empty(rows, device=x.device, dtype=torch.float32), "int8")
+    src = 0 if x.dtype == torch.bfloat16 else 1
+    if src == 1 and x.dtype != torch.float32:
+        x = x.float()
+    _lib.call("vdn_quant_int8_rows", src, x.data_ptr(), x.stride(0), rows, K, out.data.data_ptr(),
+              out.data.stride(0), out.scale.data_ptr(), _stream(x))
+    return out
+
+
+def quantize_tensor_fp8(x: torch.Tensor, out: QuantizedMatrix | None = None,
+                        work: torch.Tensor | None = None) -> QuantizedMatrix:
+    """Per-tensor e4m3 of a bf16/fp32 [rows, K] tensor (fp8.py:99-133, per_tensor=True)."""
+    _lib.require_cuda(x)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    rows, K = x.shape
+    if out is None:
+        out = QuantizedMatrix(torch.empty(rows, K, device=x.device, dtype=torch.float8_e4m3fn),
+                              torch.empty(1, device=x.device, dtype=torch.float32), "fp8")
+    if work is None:
+        work = torch.empty(1, device=x.device, dtype=torch.float32)
+    src = 0 if x.dtype == torch.bfloat16 else 1
+    if src == 1 and x.dtype != torch.float32:
+        x = x.float()
+    _lib.call("vdn_quant_fp8_tensor", src, x.data_ptr(), x.stride(0), rows, K, out.data.data_ptr(),
+              out.data.stride(0), work.data_ptr(), out.scale.data_ptr(), _stream(x))
+    return out
+
+
+def quantize_weight(w: torch.Tensor, precision: str, device) -> QuantizedMatrix:
+    w = w.detach().to(device=device, dtype=torch.float32).contiguous()
+    if precision == "int8":
+        return quantize_rows_int8(w)
+    if precision == "fp8":
+        return quantize_tensor_fp8(w)
+    raise ValueError(f"unknown quantised precision {precision!r}")
+
+
+def gemm(a, b, *, out=None, out_dtype=torch.bfloat16, alpha=1.0, a2=None, k_split=None, row_scale=None,
+         col_scale=None, dev_scale0=None, dev_scale1=None, col_bias=None, sigmoid=False, addend=None,
+         status: _lib.DeviceStatus | None = None, kind=0):
+    """out = epilogue(a @ b^T) on the tcgen05 GEMM.  a: [M, K1] (and a2 [M, K-K1]); b: [N, K]."""
+    _lib.require_cuda(a, b)
+    M = a.shape[0]
+    N, K = b.shape
+    if out is None:
+        out = torch.empty(M, N, device=a.device, dtype=out_dtype)
+    okind = {torch.bfloat16: 0, torch.float32: 1, torch.int32: 2}[out.dtype]
+    st = status or _lib.DeviceStatus(a.device)
+    _lib.call("vdn_gemm", kind, a.data_ptr(), a.stride(0), _lib.ptr(a2), a2.stride(0) if a2 is not None else 0,
+              int(k_split or 0), b.data_ptr(), b.stride(0), out.data_ptr(), out.stride(0), okind, M, N, K,
+              float(alpha), _lib.ptr(dev_scale0), _lib.ptr(dev_scale1), _lib.ptr(row_scale), _lib.ptr(col_scale),
+              _lib.ptr(col_bias), int(sigmoid), _lib.ptr(addend), addend.stride(0) if addend is not None else 0,
+              st.err_ptr, _stream(a))
+    if status is None:
+        st.raise_if_failed()
+    return out
+
+
+def project(rows: torch.Tensor, weights) -> torch.Tensor:
+    """Dispatch bf16 / fp8 / int8 like projection.py:259-268 (output dtype = rows.dtype)."""
+    _lib.require_cuda(rows)
+    x = rows.to(torch.bfloat16)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    if BF16_WEIGHT_KEY in weights and not isinstance(weights[BF16_WEIGHT_KEY], tuple):
+        w = weights[BF16_WEIGHT_KEY].to(device=x.device, dtype=torch.bfloat16).contiguous()
+        return gemm(x, w).to(rows.dtype)
+    if QUANT_WEIGHT_KEY not in weights:
+        raise KeyError("VDN projection state has no supported weight representation")
+    q = weights[QUANT_WEIGHT_KEY].to(x.device)
+    s = weights[QUANT_SCALE_KEY].to(device=x.device, dtype=torch.float32).reshape(-1).contiguous()
+    if q.dtype == torch.int8:
+        xa = quantize_rows_int8(x)
+        return gemm(xa.data, q.contiguous(), row_scale=xa.scale, col_scale=s, kind=2).to(rows.dtype)
+    xa = quantize_tensor_fp8(x)
+    return gemm(xa.data, q.contiguous(), dev_scale0=xa.scale, dev_scale1=s, kind=1).to(rows.dtype)
+
+
+def prepare_projection_maps(branch_maps, device, precision, *, skip_end_blocks=None):
+    """Quantised ``to_out_linear`` masters per block; edge blocks stay bf16 (fp8.py:168-222)."""
+    if precision not in PROJECTION_PRECISIONS:
+        raise ValueError(f"unknown VDN projection precision {precision!r}")
+    if precision == "bf16":
+        return tuple(dict(b) for b in branch_maps), None
+    skip = (DEFAULT_FP8_SKIP_END_BLOCKS if precision == "fp8" else 0) if skip_end_blocks is None else int(skip_end_blocks)
+    count = len(branch_maps)
+    if count == 0:
+        raise ValueError("branch_maps cannot be empty")
+    if skip and skip * 2 >= count:
+        raise ValueError(f"skip_end_blocks={skip} leaves no quantised interior blocks for {count} branches")
+    out = []
+    for i, block in enumerate(branch_maps):
+        if BF16_WEIGHT_KEY not in block:
+            raise KeyError(f"VDN block {i} has no {BF16_WEIGHT_KEY!r}")
+        if i < skip or i >= count - skip:
+            out.append(dict(block))
+            continue
+        qm = quantize_weight(block[BF16_WEIGHT_KEY], precision, device)
+        copied = dict(block)
+        copied.pop(BF16_WEIGHT_KEY)
+        copied[QUANT_WEIGHT_KEY] = qm.data
+        copied[QUANT_SCALE_KEY] = qm.scale.reshape(1, 1) if precision == "fp8" else qm.scale
+        out.append(copied)
+    return tuple(out), {"precision": precision, "skip_end_blocks": skip}
+
+
+__all__ = ["PROJECTION_PRECISIONS", "QuantizedMatrix", "gemm", "prepare_projection_maps", "project",
+           "quantize_rows_int8", "quantize_tensor_fp8", "quantize_weight"]

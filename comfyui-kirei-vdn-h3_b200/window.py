@@ -1,0 +1,241 @@
+"""Block-sparse window softmax on sm_100a (replaces vdn_h3/window.py's backends).
+
+``window_softmax_b200`` keeps the argument list of ``window_softmax_grouped``
+(window.py:277-280) and its exact semantics (window.py:327-344), but runs one persistent
+tcgen05 kernel over a host-built plan instead of per-group K/V gathers and SDPA calls.
+
+Plan (built once per geometry, cached like the reference's ``_DecomposedPlan``,
+window.py:726-797): query rows are cut into 128-row tiles; for each tile the key rows
+visible to any of its rows are merged into intervals and cut into 128-key tiles that
+may start at any row.  A key tile carries a mask flag only when some row of the query
+tile cannot see all of its keys; the kernel then rebuilds that row's visibility from
+the frame index.  Work items (head, query tile) are sorted by key-tile count so the
+persistent CTAs stay balanced.
+"""
+
+from __future__ import annotations
+
+from collections import OrderedDict
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from .layout import ANCHOR_FRAME_MODES, validate_layout
+
+BQ = 128
+BKV = 128
+ATTENTION_BACKENDS = ("auto", "grouped", "flex", "flash2", "decomposed", "reference", "compat", "b200")
+
+
+def _merge(intervals):
+    out = []
+    for a, b in sorted(i for i in intervals if i[0] < i[1]):
+        if out and out[-1][1] >= a:
+            out[-1] = (out[-1][0], max(out[-1][1], b))
+        else:
+            out.append((a, b))
+    return out
+
+
+def _contained(a, b, ivs) -> bool:
+    return any(x <= a and b <= y for x, y in ivs)
+
+
+@dataclass
+class WindowPlan:
+    seq_len: int
+    video_start: int
+    video_end: int
+    num_frames: int
+    tokens_per_frame: int
+    anchor_rows: bool
+    anchor_cols: bool
+    frame_lo: np.ndarray  # [F] int32, clamped
+    frame_hi: np.ndarray  # [F] int32, clamped
+    tile_off: np.ndarray  # [nq + 1] int32
+    ktile: np.ndarray  # [n_ktiles] int32 packed (k0 << 9) | (masked << 8) | (valid - 1)
+    tiles_per_q: np.ndarray  # [nq]
+    masked_tiles: int
+    _device: dict | None = None
+
+    @property
+    def n_qtiles(self) -> int:
+        return len(self.tiles_per_q)
+
+    def items(self, heads: int) -> np.ndarray:
+        """(head << 20) | q_tile, most expensive first, heads interleaved."""
+        qt = np.arange(self.n_qtiles, dtype=np.int64)
+        order = np.argsort(-self.tiles_per_q, kind="stable")
+        codes = (np.arange(heads, dtype=np.int64)[None, :] << 20) | qt[order][:, None]
+        return codes.reshape(-1).astype(np.int32)
+
+    def key_tiles_total(self, heads: int) -> int:
+        return int(self.tiles_per_q.sum()) * heads
+
+    def device_arrays(self, device, heads: int) -> dict:
+        key = (str(device), heads)
+        if self._device is None:
+            self._device = {}
+        if key not in self._device:
+            dev = torch.device(device)
+            self._device[key] = {
+                "frame_lo": torch.from_numpy(self.frame_lo).to(dev),
+                "frame_hi": torch.from_numpy(self.frame_hi).to(dev),
+                "tile_off": torch.from_numpy(self.tile_off).to(dev),
+                "ktile": torch.from_numpy(self.ktile).to(dev),
+                "items": torch.from_numpy(self.items(heads)).to(dev),
+            }
+        return self._device[key]
+
+
+def build_window_plan(seq_len, video_start, video_end, num_frames, tokens_per_frame, bounds,
+                      anchor_frames) -> WindowPlan:
+    validate_layout(seq_len, video_start, video_end, num_frames, tokens_per_frame, bounds, anchor_frames)
+    S, vs, ve, F, tpf = int(seq_len), int(video_start), int(video_end), int(num_frames), int(tokens_per_frame)
+    a_rows = anchor_frames in ("rows", "both")
+    a_cols = anchor_frames in ("columns", "both")
+    last = F - 1
+    lo = np.array([max(int(b[0]), 0) for b in bounds], dtype=np.int32)
+    hi = np.array([min(int(b[1]), last) for b in bounds], dtype=np.int32)
+    cls_cache: dict[int, list] = {}
+
+    def class_iv(c):
+        if c not in cls_cache:
+            if c < 0:
+                cls_cache[c] = [(0, S)]
+            else:
+                iv = [(0, vs), (ve, S), (vs + int(lo[c]) * tpf, vs + (int(hi[c]) + 1) * tpf)]
+                if a_cols:
+                    iv += [(vs, vs + tpf), (ve - tpf, ve)]
+                cls_cache[c] = _merge(iv)
+        return cls_cache[c]
+
+    nq = (S + BQ - 1) // BQ
+    tile_off = np.zeros(nq + 1, dtype=np.int64)
+    ktiles = []
+    tiles_per_q = np.zeros(nq, dtype=np.int64)
+    masked = 0
+    for qt in range(nq):
+        r0, r1 = qt * BQ, min(S, qt * BQ + BQ)
+        classes = set()
+        if r0 < vs or r1 > ve:
+            classes.add(-1)
+        a, b = max(r0, vs), min(r1, ve)
+        if a < b:
+            for f in range((a - vs) // tpf, (b - 1 - vs) // tpf + 1):
+                classes.add(-1 if (a_rows and f in (0, last)) else f)
+        ivs = {c: class_iv(c) for c in classes}
+        union = _merge([iv for c in classes for iv in ivs[c]])
+        n = 0
+        for x, y in union:
+            for k0 in range(x, y, BKV):
+                kend = min(k0 + BKV, y)
+                m = any(not _contained(k0, kend, ivs[c]) for c in classes)
+                masked += int(m)
+                ktiles.append((k0 << 9) | (int(m) << 8) | (kend - k0 - 1))
+                n += 1
+        if n == 0:
+            raise ValueError(f"query tile {qt} sees no keys")
+        tiles_per_q[qt] = n
+        tile_off[qt + 1] = tile_off[qt] + n
+    return WindowPlan(S, vs, ve, F, tpf, a_rows, a_cols, lo, hi, tile_off.astype(np.int32),
+                      np.asarray(ktiles, dtype=np.int64).astype(np.int32), tiles_per_q, masked)
+
+
+class WindowPlanCache:
+    """LRU of plans, owned by one state object (window.py:77-138 keeps plans per model)."""
+
+    def __init__(self, limit: int = 16):
+        self.limit = int(limit)
+        self._plans: OrderedDict = OrderedDict()
+
+    def get(self, seq_len, video_start, video_end, num_frames, tokens_per_frame, bounds, anchor_frames):
+        key = (int(seq_len), int(video_start), int(video_end), int(num_frames), int(tokens_per_frame),
+               tuple((int(a), int(b)) for a, b in bounds), str(anchor_frames))
+        plan = self._plans.get(key)
+        if plan is None:
+            plan = build_window_plan(*key)
+            self._plans[key] = plan
+            while len(self._plans) > self.limit:
+                self._plans.popitem(last=False)
+        else:
+            self._plans.move_to_end(key)
+        return plan
+
+    def clear(self):
+        self._plans.clear()
+
+    release = clear
+
+
+_DEFAULT_PLANS = WindowPlanCache()
+
+
+def _rows_view(t: torch.Tensor, heads: int, dim: int) -> int:
+    """Row pitch of a [S, H, D] view whose heads and dims are packed (row-major [S, H*D])."""
+    if t.dtype != torch.bfloat16:
+        raise ValueError("window attention operands must be bfloat16")
+    if t.stride(-1) != 1 or t.stride(-2) != dim:
+        raise ValueError("q/k/v must have contiguous [heads, dim] inner layout")
+    return t.stride(0)
+
+
+def launch_window_attention(q, k, v, out, plan: WindowPlan, heads, dim, scale, status: _lib.DeviceStatus,
+                            gate_logits=None, gate_col0=0, gate_bias=None):
+    """Launch the kernel on the current stream (no validation beyond the C-ABI's)."""
+    d = plan.device_arrays(q.device, heads)
+    n_items = heads * plan.n_qtiles
+    _lib.call(
+        "vdn_window_attention",
+        q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+        plan.seq_len, heads, dim, plan.video_start, plan.video_end, plan.num_frames, plan.tokens_per_frame,
+        int(plan.anchor_rows), int(plan.anchor_cols), float(scale),
+        d["frame_lo"].data_ptr(), d["frame_hi"].data_ptr(), d["items"].data_ptr(), n_items,
+        d["tile_off"].data_ptr(), d["ktile"].data_ptr(), out.data_ptr(), out.stride(0),
+        _lib.ptr(gate_logits), gate_logits.stride(0) if gate_logits is not None else 0, int(gate_col0),
+        _lib.ptr(gate_bias), status.err_ptr, _lib.stream_handle(q.device),
+    )
+
+
+def window_softmax_b200(query, key, value, video_start, video_end, num_frames, tokens_per_frame, bounds, scale,
+                        anchor_frames="none", *, gate=None, cache: WindowPlanCache | None = None,
+                        status: _lib.DeviceStatus | None = None):
+    """Exact window softmax attention, same contract as window_softmax_grouped
+    (window.py:277-313).  ``query/key/value``: [S, H, D] bf16 CUDA tensors (strided row
+    views of a fused projection are accepted).  ``gate`` optionally fuses the per-token
+    head gate: a tuple (logits [S, >=H] fp32 view, bias [H] fp32 or None); the result is
+    then ``softmax_out * sigmoid(logits + bias)``.  Returns [S, H, D] bf16.
+    """
+    if query.ndim != 3 or query.shape != key.shape or query.shape != value.shape:
+        raise ValueError("query, key and value must share shape [sequence, heads, dim]")
+    _lib.require_cuda(query, key, value)
+    S, H, D = query.shape
+    plan = (cache or _DEFAULT_PLANS).get(S, video_start, video_end, num_frames, tokens_per_frame, bounds,
+                                         anchor_frames)
+    for t in (query, key, value):
+        _rows_view(t, H, D)
+    out = torch.empty(S, H, D, device=query.device, dtype=torch.bfloat16)
+    st = status or _lib.DeviceStatus(query.device)
+    logits, bias, col0 = None, None, 0
+    if gate is not None:
+        logits, bias = gate
+        if logits.dtype != torch.float32 or logits.stride(-1) != 1:
+            raise ValueError("gate logits must be an fp32 row-major view")
+        col0 = 0
+    launch_window_attention(query, key, value, out, plan, H, D, scale, st, logits, col0, bias)
+    if status is None:
+        st.raise_if_failed()
+    return out
+
+
+__all__ = [
+    "ANCHOR_FRAME_MODES",
+    "ATTENTION_BACKENDS",
+    "WindowPlan",
+    "WindowPlanCache",
+    "build_window_plan",
+    "launch_window_attention",
+    "window_softmax_b200",
+]

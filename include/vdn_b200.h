@@ -1,0 +1,135 @@
+/*
+ * vdn_b200.h - C ABI of libvdn_b200.so, the sm_100a hot path of the VDN-H3 hybrid
+ * attention block (hyukudan/ComfyUI-Kirei-VDN-H3 v0.3.3).
+ *
+ * Conventions for every entry point:
+ *   - pointers are CUDA device pointers (row-major, pitches in elements), sizes are
+ *     plain ints; `stream` is a cudaStream_t passed as void*; all work is stream-ordered;
+ *   - the return value is a status: 0 ok, -1 invalid argument, -2 unsupported geometry,
+ *     -3 TMA tensor-map encoding failed, -4 launch failed, -5 misaligned pointer/pitch;
+ *   - `dev_err` (where present) is a device int that receives the first kernel abort
+ *     code (1..4: a bounded wait timed out); the host checks it once per forward;
+ *   - bf16 = __nv_bfloat16, fp8 = e4m3 (float8_e4m3fn), int8 = signed char.
+ *
+ * The reference is pure Python/torch; each function below names the reference code it
+ * replaces (file:line inside the reference project).  A Python host binds them with
+ * ctypes.
+ */
+#ifndef VDN_B200_H
+#define VDN_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- projections ---- */
+
+/* C = epilogue(A * B^T).  kind: 0 bf16, 1 fp8 e4m3, 2 int8.  A: [M, K] (pitch lda), or
+ * split along K: A for k < k_split, A2 (pitch lda2) for the rest (A2 = NULL: one source).
+ * B: [N, K] (pitch ldb).  out_kind: 0 bf16, 1 fp32, 2 raw int32 (int8 only).
+ * epilogue: v = acc * alpha * dev_scale0 * dev_scale1 * row_scale[m] * col_scale[n]
+ *           (+ col_bias[n]) (sigmoid if act == 1) (+ addend[m, n] bf16).
+ * Replaces: hybrid.py:263 and :535 (ComfyUI qkv_proj / out_proj linears),
+ *           projection.py:259-268 (project), fp8.py:239-266 (_scaled_mm),
+ *           projection.py:243-256 (ck.int8_linear), branch.py:754-758 (output gate). */
+int vdn_gemm(int kind, const void* A, long long lda, const void* A2, long long lda2, long long k_split,
+             const void* B, long long ldb, void* C, long long ldc, int out_kind, int M, int N, int K,
+             float alpha, const float* dev_scale0, const float* dev_scale1, const float* row_scale,
+             const float* col_scale, const float* col_bias, int act, const void* addend, long long ld_add,
+             int* dev_err, void* stream);
+
+/* Fused QKV projection of x [S, hidden] against [W_qkv; W_side] ([3*inner + n_aux, hidden]):
+ * raw q/k/v -> qkv_out [S, 3*inner] bf16; RMSNorm(q), RMSNorm(k) per head with weights
+ * norm_w [2, head_dim] fp32 -> qk_norm [S, 2*inner] bf16; side columns -> aux_out [S, n_aux] fp32.
+ * kind / scales as in vdn_gemm (int8: row_scale per token, col_scale per channel).
+ * Replaces: hybrid.py:260-268 (_qkv), hybrid.py:271-273 (q_norm / k_norm, rope_freqs=None),
+ *           hybrid.py:520-522 (gate logits), branch.py:736 (beta), :743-751 (alpha down),
+ *           :755 (output-gate down). */
+int vdn_qkv_gemm(int kind, const void* x, long long ldx, const void* w, long long ldw, int S, int hidden,
+                 int inner, int n_aux, int head_dim, const float* norm_w, float eps, float alpha,
+                 const float* dev_scale0, const float* dev_scale1, const float* row_scale,
+                 const float* col_scale, void* qkv_out, long long ld_qkv, void* qk_norm, long long ld_norm,
+                 float* aux_out, long long ld_aux, int* dev_err, void* stream);
+
+/* Per-row symmetric int8 (scale = max(amax/127, 1e-12), round half to even).
+ * src_kind: 0 bf16, 1 fp32.  Replaces: projection.py:74-97 (TensorWiseINT8 quantisation,
+ * here without ConvRot: the config-2 scheme). */
+int vdn_quant_int8_rows(int src_kind, const void* x, long long ldx, int rows, int K, void* q, long long ldq,
+                        float* scale, void* stream);
+
+/* Per-tensor e4m3 (scale = max(amax/448, 1e-12)); work: one fp32 device scalar.
+ * Replaces: fp8.py:108-133 (quantize_activation, per_tensor=True). */
+int vdn_quant_fp8_tensor(int src_kind, const void* x, long long ldx, int rows, int K, void* q, long long ldq,
+                         float* work, float* scale_out, void* stream);
+
+/* ---------------------------------------------------------------- window softmax -- */
+
+/* Exact block-sparse window softmax attention with the per-token head gate fused.
+ * q, k, v: [S, H*D] bf16 views (pitches ld_q/ld_k/ld_v); q, k already RMS-normalised.
+ * frame_lo/frame_hi [F]: clamped visible key-frame range; items/tile_off/ktile: host plan
+ * (window.py in the package).  out [S, ld_out] bf16 at columns h*D.
+ * gate_logits [S, ld_gate] fp32 (column gate_col0 + h) + gate_bias [H]: optional.
+ * Replaces: window.py:277-313 (window_softmax_grouped), window.py:327-344 (mask),
+ *           window.py:694-861 (flex / FA2 / FA4 backends), hybrid.py:518-528 and
+ *           softmax_kernels.py:8-37 (gate and flatten). */
+int vdn_window_attention(const void* q, long long ld_q, const void* k, long long ld_k, const void* v,
+                         long long ld_v, int S, int H, int D, int video_start, int video_end, int num_frames,
+                         int tokens_per_frame, int anchor_rows, int anchor_cols, float scale,
+                         const int* frame_lo, const int* frame_hi, const int* items, int n_items,
+                         const int* tile_off, const int* ktile, void* out, long long ld_out,
+                         const float* gate_logits, long long ld_gate, int gate_col0, const float* gate_bias,
+                         int* dev_err, void* stream);
+
+/* ---------------------------------------------------------------- VDA branch ------ */
+
+/* Depthwise kh x kw conv per frame on the (gh, gw) grid, zero padding; out bf16.
+ * Replaces: branch.py:469-471, runtime.py:329-333 (F.conv2d groups=channels). */
+int vdn_spatial_conv(const void* in, long long ld_in, const float* w, int kh, int kw, int F, int gh, int gw,
+                     int C, void* out, long long ld_out, void* stream);
+
+/* Temporal depthwise conv (taps 5, zero pad; taps 0 = none), SiLU, optional L2 over D,
+ * output FHSD [F, H, T, D] bf16.  Replaces: kernels.py:99-162 (_tconv_act_kernel),
+ * kernels.py:59-68 (temporal_shift_eager), kernels.py:47-51 (activate). */
+int vdn_temporal_act(const void* in, long long ld_in, const float* w, int taps, int F, int T, int H, int D,
+                     int l2norm, void* out, void* stream);
+
+/* alpha [F, H, D] = exp(-exp(A_log) * softplus(W_up mean_t(down) + dt_bias)), down being the
+ * per-row x W_down^T columns.  Replaces: branch.py:483-491 (alpha_gate), :743-751. */
+int vdn_alpha_gate(const float* down, long long ld_down, int F, int T, int R, const float* w_up,
+                   const float* dt_bias, const float* a_log, int H, int D, float* alpha, void* stream);
+
+/* A = sym((beta K)^T K), B = (beta V)^T K per frame and head, beta = sigmoid(logit).
+ * Replaces: branch.py:197-282 (frame_statistics). */
+int vdn_frame_stats(const void* K, const void* V, int F, int H, int T, int D, const float* beta_logits,
+                    long long ld_beta, int beta_col0, float* A, float* B, void* stream);
+
+/* inv = (I + A)^-1 via Cholesky + triangular inverse; info[f, h] = order of the first
+ * non-positive leading minor (0 = SPD).  text_frame >= 0: s0 = text_scale * B inv of it.
+ * Replaces: branch.py:148-160 (VdnDelta.factor_apply), :62-71 (cholesky_ex info),
+ *           :649-670 (_text_state). */
+int vdn_delta_factor(const float* A, const float* B, int F, int H, int D, float* inv, int* info,
+                     int text_frame, float text_scale, float* s0, void* stream);
+
+/* prefix_t = (B_t + prefix_{t-1} diag(alpha_t)) inv_t (t up), suffix likewise (t down),
+ * both from s0 (NULL = zero).  Replaces: branch.py:297-333 (run_scans_*),
+ * runtime.py:118-150 (_run_scans_shared). */
+int vdn_bidir_scan(const float* inv, const float* B, const float* alpha, const float* s0, int F, int H, int D,
+                   float* prefix, float* suffix, void* stream);
+
+/* Gather with alpha bridge, readout Q S^T, RMSNorm over D, x output gate, into
+ * out[out_row0 + f*T + s, h*D + v].  Replaces: branch.py:345-396 (gather_linear_state),
+ * branch.py:780, :494-530 (readout, linear_epilogue). */
+int vdn_readout(const void* Q, int F, int H, int T, int D, const float* prefix, const float* suffix,
+                const float* alpha, const float* s0, const int* lo, const int* hi, int use_alpha,
+                const float* norm_w, const void* gate, long long ld_gate, void* out, long long ld_out,
+                long long out_row0, void* stream);
+
+/* fp32 column block -> bf16 (output-gate bottleneck rounding, branch.py:755). */
+int vdn_cast_rows(const float* in, long long ld_in, int col0, int rows, int cols, void* out, long long ld_out,
+                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VDN_B200_H */

@@ -31,10 +31,21 @@ TEXT_STATE_SCALE = 0.5  # branch.py:23
 FP8_MAX = 448.0  # fp8.py:30 (float8_e4m3fn max)
 
 
+_COMPUTE = [F64]
+
+
+def set_compute_dtype(dtype) -> torch.dtype:
+    """Switch the arithmetic dtype (float64 for parity checks; float32 reproduces the
+    reference's CPU path for the timed CPU baseline).  Returns the previous dtype."""
+    prev = _COMPUTE[0]
+    _COMPUTE[0] = dtype
+    return prev
+
+
 def _t(x) -> torch.Tensor:
     if isinstance(x, np.ndarray):
         x = torch.from_numpy(x)
-    return x.detach().to("cpu", F64)
+    return x.detach().to("cpu", _COMPUTE[0])
 
 
 # ---------------------------------------------------------------------------------------
@@ -99,45 +110,48 @@ def make_layout(text_len, num_frames, grid, *, radius=1, chunk=5, anchor_frames=
 # Window softmax (window.py:277-344; tests/test_window.py:41-69)
 # ---------------------------------------------------------------------------------------
 
-def allowed_mask(seq, vs, ve, num_frames, tpf, bounds, anchors) -> torch.Tensor:
-    """Boolean [seq, seq] mask of allowed (query, key) pairs (window.py:327-344)."""
-    rows = torch.arange(seq)
-    glob = (rows < vs) | (rows >= ve)
-    frame = torch.div(rows - vs, tpf, rounding_mode="floor")
-    lo = torch.zeros(seq, dtype=torch.long)
-    hi = torch.full((seq,), num_frames - 1, dtype=torch.long)
-    for f, (a, b) in enumerate(bounds):
-        s = vs + f * tpf
-        lo[s:s + tpf] = max(a, 0)
-        hi[s:s + tpf] = min(b, num_frames - 1)
-    kf = frame[None, :]
-    allowed = glob[:, None] | glob[None, :] | ((kf >= lo[:, None]) & (kf <= hi[:, None]))
+def allowed_mask(seq, vs, ve, num_frames, tpf, bounds, anchors, rows=None) -> torch.Tensor:
+    """Boolean [rows, seq] mask of allowed (query, key) pairs (window.py:327-344);
+    all rows when ``rows`` is None."""
+    keys = torch.arange(seq)
+    qrows = keys if rows is None else torch.as_tensor(rows, dtype=torch.long)
+    kglob = (keys < vs) | (keys >= ve)
+    qglob = (qrows < vs) | (qrows >= ve)
+    kf = torch.div(keys - vs, tpf, rounding_mode="floor")[None, :]
+    qf = torch.div(qrows - vs, tpf, rounding_mode="floor")
+    lo_f = torch.tensor([max(a, 0) for a, _ in bounds], dtype=torch.long)
+    hi_f = torch.tensor([min(b, num_frames - 1) for _, b in bounds], dtype=torch.long)
+    qfc = qf.clamp(0, num_frames - 1)
+    lo = torch.where(qglob, 0, lo_f[qfc])
+    hi = torch.where(qglob, num_frames - 1, hi_f[qfc])
+    allowed = qglob[:, None] | kglob[None, :] | ((kf >= lo[:, None]) & (kf <= hi[:, None]))
     if anchors in ("columns", "both"):
         allowed = allowed | ((kf == 0) | (kf == num_frames - 1))
     if anchors in ("rows", "both"):
-        qf = frame[:, None]
-        allowed = allowed | ((qf == 0) | (qf == num_frames - 1))
+        allowed = allowed | ((qf[:, None] == 0) | (qf[:, None] == num_frames - 1))
     return allowed
 
 
 def window_attention(q, k, v, vs, ve, num_frames, tpf, bounds, scale, anchors="none",
-                     rows=None) -> torch.Tensor:
-    """Exact masked softmax attention, float64 (window.py:277-313 semantics).
+                     rows=None, chunk=512) -> torch.Tensor:
+    """Exact masked softmax attention (window.py:277-313 semantics), computed in blocks
+    of ``chunk`` query rows so memory stays bounded.
 
     ``q,k,v``: [S, H, D].  ``rows`` optionally restricts which query rows are computed
     (a 1-D index tensor); the result then has one entry per requested row.
     """
     q, k, v = _t(q), _t(k), _t(v)
     seq = q.shape[0]
-    mask = allowed_mask(seq, vs, ve, num_frames, tpf, bounds, anchors)
-    if rows is not None:
-        rows = torch.as_tensor(rows, dtype=torch.long)
-        q = q[rows]
-        mask = mask[rows]
-    logits = torch.einsum("qhd,khd->hqk", q, k) * scale
-    logits = logits.masked_fill(~mask[None], float("-inf"))
-    p = torch.softmax(logits, dim=-1)
-    return torch.einsum("hqk,khd->qhd", p, v)
+    rows = torch.arange(seq) if rows is None else torch.as_tensor(rows, dtype=torch.long)
+    out = torch.empty(len(rows), q.shape[1], q.shape[2], dtype=q.dtype)
+    for i in range(0, len(rows), chunk):
+        r = rows[i:i + chunk]
+        mask = allowed_mask(seq, vs, ve, num_frames, tpf, bounds, anchors, rows=r)
+        logits = torch.einsum("qhd,khd->hqk", q[r], k) * scale
+        logits = logits.masked_fill(~mask[None], float("-inf"))
+        p = torch.softmax(logits, dim=-1)
+        out[i:i + chunk] = torch.einsum("hqk,khd->qhd", p, v)
+    return out
 
 
 def key_count_per_row(seq, vs, ve, num_frames, tpf, bounds, anchors) -> np.ndarray:
@@ -234,7 +248,7 @@ def cholesky_info(a) -> torch.Tensor:
     """First failing leading-minor order per matrix of I+A (0 = SPD); cholesky_ex semantics."""
     m = _t(a)
     n = m.shape[-1]
-    flat = (m + torch.eye(n, dtype=F64)).reshape(-1, n, n)
+    flat = (m + torch.eye(n, dtype=m.dtype)).reshape(-1, n, n)
     info = torch.zeros(flat.shape[0], dtype=torch.int32)
     for i in range(flat.shape[0]):
         _, inf = torch.linalg.cholesky_ex(flat[i])
@@ -246,7 +260,7 @@ def factor_apply(alpha, a, b) -> tuple[torch.Tensor, torch.Tensor]:
     """T = alpha[...,None] * (I+A)^-1, Inj = B (I+A)^-1 via Cholesky (branch.py:148-160)."""
     a, b, alpha = _t(a), _t(b), _t(alpha)
     n = a.shape[-1]
-    eye = torch.eye(n, dtype=F64).expand_as(a)
+    eye = torch.eye(n, dtype=a.dtype).expand_as(a)
     chol = torch.linalg.cholesky(a + eye)
     inv_chol = torch.linalg.solve_triangular(chol, eye, upper=False, left=True)
     inverse = inv_chol.transpose(-1, -2) @ inv_chol
@@ -256,7 +270,7 @@ def factor_apply(alpha, a, b) -> tuple[torch.Tensor, torch.Tensor]:
 def sana_factor_apply(alpha, a, b, tokens) -> tuple[torch.Tensor, torch.Tensor]:
     """T = alpha*(I - A/tpf), Inj = B/sqrt(tpf) (branch.py:163-177)."""
     a, b, alpha = _t(a), _t(b), _t(alpha)
-    eye = torch.eye(a.shape[-1], dtype=F64)
+    eye = torch.eye(a.shape[-1], dtype=a.dtype)
     return alpha.unsqueeze(-1) * (eye - a / tokens), b / math.sqrt(tokens)
 
 
@@ -322,7 +336,7 @@ def text_state(weights, text_x, text_k, text_v, heads, dim, cfg: BranchConfig):
     beta = torch.sigmoid(_t(text_x) @ _t(weights["beta_proj.weight"]).T)
     beta = beta.reshape(1, length, heads).permute(0, 2, 1)
     a, b = frame_statistics(key, val, beta)
-    ones = torch.ones(1, heads, dim, dtype=F64)
+    ones = torch.ones(1, heads, dim, dtype=_COMPUTE[0])
     if cfg.delta_rule == "vdn_solve":
         _, inj = factor_apply(ones, a, b)
     else:
@@ -341,7 +355,7 @@ def branch_readout(weights, xv, q_raw, k_raw, v_raw, num_frames, tpf, bounds, fr
     rows_total = num_frames * tpf
     if skip_ends:
         if num_frames <= 2:
-            return torch.zeros(rows_total, heads * dim, dtype=F64)
+            return torch.zeros(rows_total, heads * dim, dtype=_COMPUTE[0])
         inner = slice(tpf, (num_frames - 1) * tpf)
         inner_out = branch_readout(
             weights, xv[inner], _t(q_raw)[inner], _t(k_raw)[inner], _t(v_raw)[inner],
@@ -351,7 +365,7 @@ def branch_readout(weights, xv, q_raw, k_raw, v_raw, num_frames, tpf, bounds, fr
         parts = None
         if return_parts:
             inner_out, parts = inner_out
-        out = torch.zeros(rows_total, heads * dim, dtype=F64)
+        out = torch.zeros(rows_total, heads * dim, dtype=_COMPUTE[0])
         out[inner] = inner_out
         return (out, parts) if return_parts else out
     w = weights
@@ -396,28 +410,22 @@ def branch_readout(weights, xv, q_raw, k_raw, v_raw, num_frames, tpf, bounds, fr
 # Projections (projection.py:259-268, fp8.py:84-266) and the config-2 INT8 scheme
 # ---------------------------------------------------------------------------------------
 
-def round_half_even(x: torch.Tensor) -> torch.Tensor:
-    return torch.round(x)  # torch.round is round-half-to-even
+def _int8_rows_np(x32: np.ndarray) -> tuple[torch.Tensor, torch.Tensor]:
+    """IEEE fp32 arithmetic throughout: scale = max(amax / 127, 1e-12); q = rne(x / scale)."""
+    amax = np.abs(x32).max(axis=1)
+    scale = np.maximum(amax / np.float32(127.0), np.float32(1e-12)).astype(np.float32)
+    q = np.clip(np.rint(x32 / scale[:, None]), -127, 127).astype(np.int8)
+    return torch.from_numpy(q), torch.from_numpy(scale)
 
 
 def int8_quantize_weight(w) -> tuple[torch.Tensor, torch.Tensor]:
-    """Symmetric per-output-channel int8: scale = amax/127, q = rne(w/scale) (config 2)."""
-    w32 = _t(w).to(torch.float32)
-    scale = (w32.abs().amax(dim=1) / 127.0).clamp_min(1e-12)
-    q = round_half_even(w32 / scale[:, None]).clamp(-127, 127).to(torch.int8)
-    return q, scale
+    """Symmetric per-output-channel int8 (config 2): one fp32 scale per row of W [N, K]."""
+    return _int8_rows_np(_t(w).to(torch.float32).numpy())
 
 
 def int8_quantize_rows(x) -> tuple[torch.Tensor, torch.Tensor]:
-    """Dynamic per-token int8 of fp32 rows, same rule as the weights (config 2).
-
-    The scale is computed and applied in fp32 (amax * (1/127) and x * (1/scale) are
-    not used): scale = max(amax / 127, 1e-12); q = rne(x / scale) clamped to +-127.
-    """
-    x32 = _t(x).to(torch.float32)
-    scale = (x32.abs().amax(dim=1) / 127.0).clamp_min(1e-12)
-    q = round_half_even(x32 / scale[:, None]).clamp(-127, 127).to(torch.int8)
-    return q, scale
+    """Dynamic per-token int8 (config 2), the same rule as the weights: one scale per row."""
+    return _int8_rows_np(_t(x).to(torch.float32).numpy())
 
 
 def int8_accumulate(qa: torch.Tensor, qw: torch.Tensor) -> torch.Tensor:
@@ -429,11 +437,12 @@ def int8_accumulate(qa: torch.Tensor, qw: torch.Tensor) -> torch.Tensor:
 
 
 def fp8_quantize_tensor(x) -> tuple[torch.Tensor, float]:
-    """Per-tensor e4m3: scale = max(amax/448, 1e-12); q = clamp(x/scale) (fp8.py:88-105)."""
-    x32 = _t(x).to(torch.float32)
-    scale = max(float(x32.abs().max()) / FP8_MAX, 1e-12)
-    q = (x32 / torch.tensor(scale, dtype=torch.float32)).clamp(-FP8_MAX, FP8_MAX)
-    return q.to(torch.float8_e4m3fn), scale
+    """Per-tensor e4m3: scale = max(amax/448, 1e-12) in fp32; q = rn(clamp(x/scale))
+    (fp8.py:88-105 with per_tensor=True)."""
+    x32 = _t(x).to(torch.float32).numpy()
+    scale = np.maximum(np.float32(np.abs(x32).max()) / np.float32(FP8_MAX), np.float32(1e-12)).astype(np.float32)
+    q = np.clip(x32 / scale, -FP8_MAX, FP8_MAX).astype(np.float32)
+    return torch.from_numpy(q).to(torch.float8_e4m3fn), float(scale)
 
 
 def project(rows, w, precision="bf16"):
@@ -443,12 +452,12 @@ def project(rows, w, precision="bf16"):
     if precision == "int8":
         qa, sa = int8_quantize_rows(rows)
         qw, sw = int8_quantize_weight(w)
-        acc = int8_accumulate(qa, qw).to(F64)
-        return acc * sa.to(F64)[:, None] * sw.to(F64)[None, :]
+        acc = int8_accumulate(qa, qw).to(_COMPUTE[0])
+        return acc * sa.to(_COMPUTE[0])[:, None] * sw.to(_COMPUTE[0])[None, :]
     if precision == "fp8":
         qa, sa = fp8_quantize_tensor(rows)
         qw, sw = fp8_quantize_tensor(w)
-        return (qa.to(F64) @ qw.to(F64).T) * (sa * sw)
+        return (qa.to(_COMPUTE[0]) @ qw.to(_COMPUTE[0]).T) * (sa * sw)
     raise ValueError(f"unknown precision {precision!r}")
 
 

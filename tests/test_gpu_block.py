@@ -1,0 +1,108 @@
+"""GPU parity of the whole hybrid block (drop-in operator) against the oracle and the
+reference's golden block output; bf16 within 2e-2 relative L2."""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from __graft_entry__ import _Attn, load_package
+from oracle import vdn_oracle as vo
+
+pytestmark = pytest.mark.gpu
+
+pkg = load_package()
+DEV = torch.device("cuda:0") if torch.cuda.is_available() else None
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "config0.npz")
+
+
+def rel_l2(got, want):
+    got = got.double().cpu()
+    want = want.double().cpu()
+    return float((got - want).norm() / want.norm())
+
+
+def _run_block(bw, lay, heads, dim, x, precision="bf16", config=None):
+    state = pkg.B200State("t", config or {"enable_softmax_gate": True}, [bw.branch], heads, dim,
+                          projection_precision=precision)
+    attn = _Attn(bw, heads, dim)
+    fwd = pkg.make_vdn_forward(attn, state, 0)
+    with pkg.publish_layout(lay):
+        out = pkg.run_forward_checked(state, fwd, x.to(DEV, torch.bfloat16))
+    torch.cuda.synchronize()
+    return out
+
+
+def _layout(c, **kw):
+    return pkg.make_layout(c["text"], c["frames"], c["grid"], **kw)
+
+
+def test_block_config0_matches_oracle_and_golden():
+    c = vo.CONFIG0
+    bw = vo.make_block(0, c["hidden"], c["heads"], c["dim"])
+    lay_o = vo.config_layout(c)
+    x = vo.make_x(0, lay_o.seq_len, c["hidden"])
+    got = _run_block(bw, _layout(c), c["heads"], c["dim"], x)
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig())
+    assert rel_l2(got, want) < 2e-2
+    golden = torch.from_numpy(dict(np.load(GOLDEN))["block_out"])
+    assert rel_l2(got, golden) < 2e-2
+
+
+@pytest.mark.parametrize("anchors", ["none", "columns", "rows"])
+def test_block_other_anchor_modes(anchors):
+    c = dict(vo.CONFIG0, frames=12)
+    bw = vo.make_block(1, c["hidden"], c["heads"], c["dim"])
+    lay_o = vo.config_layout(c, anchor_frames=anchors)
+    x = vo.make_x(1, lay_o.seq_len, c["hidden"])
+    got = _run_block(bw, _layout(c, anchor_frames=anchors), c["heads"], c["dim"], x)
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig())
+    assert rel_l2(got, want) < 2e-2
+
+
+def test_block_full_cover_runs_dense_attention_without_branch():
+    c = dict(vo.CONFIG0, frames=5)
+    bw = vo.make_block(2, c["hidden"], c["heads"], c["dim"])
+    lay_o = vo.config_layout(c)
+    assert lay_o.full_cover
+    x = vo.make_x(2, lay_o.seq_len, c["hidden"])
+    got = _run_block(bw, _layout(c), c["heads"], c["dim"], x)
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig())
+    assert rel_l2(got, want) < 2e-2
+
+
+@pytest.mark.parametrize("precision", ["int8", "fp8"])
+def test_block_quantised_projections_match_oracle(precision):
+    c = dict(vo.CONFIG0, heads=2, dim=128)
+    bw = vo.make_block(3, c["hidden"], c["heads"], c["dim"])
+    lay_o = vo.config_layout(c)
+    x = vo.make_x(3, lay_o.seq_len, c["hidden"]).to(torch.bfloat16).float()
+    got = _run_block(bw, _layout(c), c["heads"], c["dim"], x, precision=precision)
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(), precision=precision)
+    exact = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig())
+    # quantised block vs its own CPU restatement; and both near the unquantised block
+    assert rel_l2(got, want) < 2e-2
+    assert rel_l2(got, exact) < (3e-2 if precision == "int8" else 8e-2)
+
+
+def test_block_d128_ragged_frames_matches_oracle():
+    c = dict(text=64, frames=7, grid=(9, 14), heads=2, dim=128, hidden=512)
+    bw = vo.make_block(4, c["hidden"], c["heads"], c["dim"])
+    lay_o = vo.config_layout(c)
+    x = vo.make_x(4, lay_o.seq_len, c["hidden"])
+    got = _run_block(bw, _layout(c), c["heads"], c["dim"], x)
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig())
+    assert rel_l2(got, want) < 2e-2
+
+
+def test_repeated_forward_is_deterministic():
+    c = vo.CONFIG0
+    bw = vo.make_block(0, c["hidden"], c["heads"], c["dim"])
+    lay = _layout(c)
+    x = vo.make_x(0, lay.seq_len, c["hidden"])
+    a = _run_block(bw, lay, c["heads"], c["dim"], x)
+    b = _run_block(bw, lay, c["heads"], c["dim"], x)
+    assert torch.equal(a, b)

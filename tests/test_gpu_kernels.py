@@ -1,0 +1,283 @@
+"""GPU parity of the individual sm_100a kernels against the float64 oracle / fp32 torch.
+
+Tolerances: bf16 outputs within 2e-2 relative L2 (most checks are far tighter), int8
+quantisation codes and int32 accumulators bit-exact."""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from __graft_entry__ import load_package
+from oracle import vdn_oracle as vo
+
+pytestmark = pytest.mark.gpu
+
+pkg = load_package()
+DEV = torch.device("cuda:0") if torch.cuda.is_available() else None
+
+
+def rel_l2(got, want):
+    got = got.double().cpu()
+    want = want.double().cpu()
+    return float((got - want).norm() / want.norm().clamp_min(1e-30))
+
+
+def _randn(*shape, seed=0, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=g) * scale
+
+
+# --------------------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (257, 520, 192), (1000, 768, 1024), (3000, 1024, 5120)])
+def test_gemm_bf16_matches_fp32(M, N, K):
+    a = _randn(M, K, seed=1).to(torch.bfloat16)
+    b = _randn(N, K, seed=2, scale=0.05).to(torch.bfloat16)
+    got = pkg.gemm(a.to(DEV), b.to(DEV), out_dtype=torch.float32)
+    want = a.float() @ b.float().T
+    assert rel_l2(got, want) < 1e-5
+
+
+def test_gemm_k_concat_equals_single_operand():
+    M, K1, K2, N = 300, 256, 512, 256
+    a1 = _randn(M, K1, seed=3).to(torch.bfloat16)
+    a2 = _randn(M, K2, seed=4).to(torch.bfloat16)
+    b = _randn(N, K1 + K2, seed=5, scale=0.05).to(torch.bfloat16)
+    got = pkg.gemm(a1.to(DEV), b.to(DEV), a2=a2.to(DEV), k_split=K1, out_dtype=torch.float32)
+    want = torch.cat([a1, a2], 1).float() @ b.float().T
+    assert rel_l2(got, want) < 1e-5
+
+
+def test_gemm_epilogue_scale_bias_sigmoid_addend():
+    M, N, K = 200, 512, 128
+    a = _randn(M, K, seed=6).to(torch.bfloat16)
+    b = _randn(N, K, seed=7, scale=0.05).to(torch.bfloat16)
+    rs = torch.rand(M) + 0.5
+    cs = torch.rand(N) + 0.5
+    bias = _randn(N, seed=8)
+    add = _randn(M, N, seed=9).to(torch.bfloat16)
+    got = pkg.gemm(a.to(DEV), b.to(DEV), alpha=0.7, row_scale=rs.to(DEV), col_scale=cs.to(DEV),
+                   col_bias=bias.to(DEV), sigmoid=True, addend=add.to(DEV), out_dtype=torch.float32)
+    want = torch.sigmoid((a.float() @ b.float().T) * 0.7 * rs[:, None] * cs[None] + bias) + add.float()
+    assert rel_l2(got, want) < 1e-5
+
+
+def test_int8_quantisation_and_accumulator_bit_exact():
+    M, N, K = 333, 512, 1024
+    x = _randn(M, K, seed=10).to(torch.bfloat16)
+    w = _randn(N, K, seed=11, scale=0.02)
+    qa = pkg.quantize_rows_int8(x.to(DEV))
+    qw = pkg.quantize_rows_int8(w.to(DEV))
+    oa, sa = vo.int8_quantize_rows(x.float())
+    ow, sw = vo.int8_quantize_weight(w)
+    assert torch.equal(qa.data.cpu(), oa) and torch.equal(qa.scale.cpu(), sa)
+    assert torch.equal(qw.data.cpu(), ow) and torch.equal(qw.scale.cpu(), sw)
+    acc = pkg.gemm(qa.data, qw.data, kind=2, out_dtype=torch.int32)
+    assert torch.equal(acc.cpu(), vo.int8_accumulate(oa, ow))
+    deq = pkg.gemm(qa.data, qw.data, kind=2, row_scale=qa.scale, col_scale=qw.scale, out_dtype=torch.float32)
+    want = acc.cpu().double() * sa.double()[:, None] * sw.double()[None]
+    assert rel_l2(deq, want) < 1e-6
+
+
+def test_fp8_gemm_matches_oracle():
+    M, N, K = 500, 768, 2048
+    x = _randn(M, K, seed=12).to(torch.bfloat16)
+    w = _randn(N, K, seed=13, scale=0.02)
+    qa = pkg.quantize_tensor_fp8(x.to(DEV))
+    qw = pkg.quantize_tensor_fp8(w.to(DEV))
+    oa, sa = vo.fp8_quantize_tensor(x.float())
+    ow, sw = vo.fp8_quantize_tensor(w)
+    assert abs(float(qa.scale) - sa) <= 1e-7 * sa and abs(float(qw.scale) - sw) <= 1e-7 * sw
+    assert torch.equal(qa.data.cpu().view(torch.uint8), oa.view(torch.uint8))
+    got = pkg.gemm(qa.data, qw.data, kind=1, dev_scale0=qa.scale, dev_scale1=qw.scale, out_dtype=torch.float32)
+    want = vo.project(x.float(), w, "fp8")
+    assert rel_l2(got, want) < 1e-5
+    # and the fp8 product stays within 2e-2 of the exact product
+    assert rel_l2(got, x.double() @ w.double().T) < 5e-2
+
+
+def test_qkv_gemm_epilogue():
+    S, hidden, H, D = 300, 256, 2, 128
+    inner = H * D
+    n_aux = 256
+    x = _randn(S, hidden, seed=14).to(torch.bfloat16)
+    w = _randn(3 * inner + n_aux, hidden, seed=15, scale=0.05).to(torch.bfloat16)
+    nw = (1 + 0.1 * _randn(2 * D, seed=16)).float()
+    qkv = torch.empty(S, 3 * inner, device=DEV, dtype=torch.bfloat16)
+    qkn = torch.empty(S, 2 * inner, device=DEV, dtype=torch.bfloat16)
+    aux = torch.empty(S, n_aux, device=DEV, dtype=torch.float32)
+    st = pkg._lib.DeviceStatus(DEV)
+    xd, wd = x.to(DEV), w.to(DEV)
+    pkg._lib.call("vdn_qkv_gemm", 0, xd.data_ptr(), hidden, wd.data_ptr(), hidden, S, hidden, inner, n_aux, D,
+                  nw.to(DEV).data_ptr(), 1e-6, 1.0, None, None, None, None, qkv.data_ptr(), 3 * inner,
+                  qkn.data_ptr(), 2 * inner, aux.data_ptr(), n_aux, st.err_ptr, pkg._lib.stream_handle(DEV))
+    torch.cuda.synchronize()
+    st.raise_if_failed()
+    full = x.float() @ w.float().T
+    assert rel_l2(qkv, full[:, :3 * inner]) < 5e-3
+    assert rel_l2(aux, full[:, 3 * inner:]) < 1e-5
+    raw = full[:, :2 * inner].to(torch.bfloat16).float().reshape(S, 2, H, D)
+    normed = raw * torch.rsqrt(raw.square().mean(-1, keepdim=True) + 1e-6) * nw.reshape(2, 1, D)
+    assert rel_l2(qkn, normed.reshape(S, 2 * inner)) < 5e-3
+
+
+# --------------------------------------------------------------------------- window attention
+def _attention_case(lay, heads, dim, seed, gate=True):
+    ki = vo.make_kernel_inputs(seed, lay, heads, dim)
+    q, k, v = (ki[n].to(torch.bfloat16) for n in ("q", "k", "v"))
+    logits = _randn(lay.seq_len, heads, seed=seed + 1)
+    bias = _randn(heads, seed=seed + 2) * 0.5
+    return q, k, v, logits, bias
+
+
+@pytest.mark.parametrize("mode", vo.ANCHOR_MODES)
+def test_window_attention_config0(mode):
+    lay = vo.config_layout(vo.CONFIG0)
+    H, D = 4, 64
+    q, k, v, logits, bias = _attention_case(lay, H, D, 20)
+    got = pkg.window_softmax_b200(q.to(DEV), k.to(DEV), v.to(DEV), lay.video_start, lay.video_end, lay.num_frames,
+                                  lay.tokens_per_frame, list(lay.bounds), D ** -0.5, mode,
+                                  gate=(logits.to(DEV), bias.to(DEV)))
+    want = vo.window_attention(q.float(), k.float(), v.float(), lay.video_start, lay.video_end, lay.num_frames,
+                               lay.tokens_per_frame, list(lay.bounds), D ** -0.5, mode)
+    want = want * torch.sigmoid(logits.double() + bias.double())[:, :, None]
+    assert rel_l2(got, want) < 1e-2
+
+
+def test_window_attention_golden_vector():
+    g = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "config0.npz")))
+    lay = vo.config_layout(vo.CONFIG0)
+    ki = vo.make_kernel_inputs(0, lay, 4, 64)
+    got = pkg.window_softmax_b200(*(ki[n].to(DEV, torch.bfloat16) for n in ("q", "k", "v")), lay.video_start,
+                                  lay.video_end, lay.num_frames, lay.tokens_per_frame, list(lay.bounds), 64 ** -0.5,
+                                  "both")
+    assert rel_l2(got, torch.from_numpy(g["window_both"])) < 1e-2
+
+
+@pytest.mark.parametrize("geom", [(24, 9, (4, 4), 8, 2, 0, "columns", 2, 64),
+                                  (512, 7, (38, 22), 0, 1, 5, "both", 2, 128),
+                                  (100, 5, (20, 13), 37, 1, 2, "rows", 3, 128)])
+def test_window_attention_ragged_tiles(geom):
+    before, F, grid, after, radius, chunk, mode, H, D = geom
+    tpf = grid[0] * grid[1]
+    vs, ve = before, before + F * tpf
+    S = ve + after
+    lay = vo.Layout(seq_len=S, video_start=vs, video_end=ve, num_frames=F, tokens_per_frame=tpf, frame_size=grid,
+                    text_start=0, text_len=before, bounds=tuple(vo.window_bounds(F, radius, chunk)),
+                    anchor_frames=mode)
+    q, k, v, logits, bias = _attention_case(lay, H, D, 30)
+    got = pkg.window_softmax_b200(q.to(DEV), k.to(DEV), v.to(DEV), vs, ve, F, tpf, list(lay.bounds), D ** -0.5, mode)
+    rows = torch.unique(torch.cat([torch.arange(0, S, 37), torch.arange(max(0, vs - 3), min(S, vs + 130)),
+                                   torch.tensor([S - 1])]))
+    want = vo.window_attention(q.float(), k.float(), v.float(), vs, ve, F, tpf, list(lay.bounds), D ** -0.5, mode,
+                               rows=rows)
+    assert rel_l2(got[rows], want) < 1e-2
+
+
+# --------------------------------------------------------------------------- branch kernels
+def _branch_setup(seed=40, Fb=6, grid=(4, 5), H=2, D=64, text=9):
+    tpf = grid[0] * grid[1]
+    rows = Fb * tpf
+    g = torch.Generator().manual_seed(seed)
+    w = vo.make_branch_weights(g, 96, H, D)
+    q = torch.randn(rows, H * D, generator=g).to(torch.bfloat16)
+    k = torch.randn(rows, H * D, generator=g).to(torch.bfloat16)
+    v = torch.randn(rows, H * D, generator=g).to(torch.bfloat16)
+    return w, q, k, v, tpf, rows
+
+
+def test_conv_features_match_oracle():
+    w, q, k, v, tpf, rows = _branch_setup()
+    Fb, H, D, grid = 6, 2, 64, (4, 5)
+    bwt = pkg.branch.BranchDeviceWeights.from_dict(w, H, D, DEV)
+    ws = pkg.branch.BranchWorkspace(DEV, Fb, tpf, H, D, 0)
+    kd = k.to(DEV)
+    sp, kh, kw, tm, taps = bwt.conv["k"]
+    s = pkg._lib.stream_handle(DEV)
+    pkg._lib.call("vdn_spatial_conv", kd.data_ptr(), kd.stride(0), sp.data_ptr(), kh, kw, Fb, grid[0], grid[1],
+                  H * D, ws.conv_tmp.data_ptr(), ws.conv_tmp.stride(0), s)
+    pkg._lib.call("vdn_temporal_act", ws.conv_tmp.data_ptr(), ws.conv_tmp.stride(0), tm.data_ptr(), taps, Fb, tpf, H,
+                  D, 1, ws.kf.data_ptr(), s)
+    qd = q.to(DEV)
+    pkg._lib.call("vdn_temporal_act", qd.data_ptr(), qd.stride(0), None, 0, Fb, tpf, H, D, 1, ws.qf.data_ptr(), s)
+    torch.cuda.synchronize()
+    want_k = vo.conv_features(k.float().reshape(rows, H, D), w["short_conv.k_sp.weight"], w["short_conv.k_tm.weight"],
+                              Fb, grid, True)
+    want_q = vo.to_fhsd(vo.activate(q.float().reshape(rows, H, D), True), Fb)
+    assert rel_l2(ws.kf, want_k) < 1e-2
+    assert rel_l2(ws.qf, want_q) < 5e-3
+
+
+def test_statistics_factor_scan_match_oracle_and_report_non_spd():
+    Fb, H, T, D = 5, 3, 70, 128
+    g = torch.Generator().manual_seed(50)
+    kf = torch.nn.functional.normalize(torch.randn(Fb, H, T, D, generator=g), dim=-1).to(torch.bfloat16)
+    vf = torch.randn(Fb, H, T, D, generator=g).to(torch.bfloat16)
+    logits = torch.randn(Fb * T, 8, generator=g)
+    alpha = torch.sigmoid(torch.randn(Fb, H, D, generator=g) + 2)
+    A = torch.empty(Fb, H, D, D, device=DEV)
+    B = torch.empty_like(A)
+    s = pkg._lib.stream_handle(DEV)
+    ld = logits.to(DEV)
+    pkg._lib.call("vdn_frame_stats", kf.to(DEV).data_ptr(), vf.to(DEV).data_ptr(), Fb, H, T, D, ld.data_ptr(), 8, 2,
+                  A.data_ptr(), B.data_ptr(), s)
+    beta = torch.sigmoid(logits[:, 2:2 + H]).reshape(Fb, T, H).permute(0, 2, 1)
+    wa, wb = vo.frame_statistics(kf.float(), vf.float(), beta)
+    torch.cuda.synchronize()
+    assert rel_l2(A, wa) < 1e-5 and rel_l2(B, wb) < 1e-5
+    inv = torch.empty_like(A)
+    info = torch.zeros(Fb, H, device=DEV, dtype=torch.int32)
+    pkg._lib.call("vdn_delta_factor", A.data_ptr(), B.data_ptr(), Fb, H, D, inv.data_ptr(), info.data_ptr(), -1, 0.0,
+                  None, s)
+    eye = torch.eye(D, dtype=torch.float64)
+    want_inv = torch.linalg.inv(eye + wa)
+    torch.cuda.synchronize()
+    assert int(info.abs().sum()) == 0
+    assert rel_l2(inv, want_inv) < 1e-5
+    prefix = torch.empty_like(A)
+    suffix = torch.empty_like(A)
+    s0 = (torch.randn(H, D, D, generator=g) * 0.1)
+    ad = alpha.to(DEV)
+    pkg._lib.call("vdn_bidir_scan", inv.data_ptr(), B.data_ptr(), ad.data_ptr(), s0.to(DEV).data_ptr(), Fb, H, D,
+                  prefix.data_ptr(), suffix.data_ptr(), s)
+    trans, inj = vo.factor_apply(alpha, wa, wb)
+    wp, wsf = vo.run_scans(trans, inj, s0.double())
+    torch.cuda.synchronize()
+    assert rel_l2(prefix, wp) < 1e-4 and rel_l2(suffix, wsf) < 1e-4
+    # a matrix that is not SPD reports the order of its first bad leading minor
+    bad = wa.clone().float()
+    bad[2, 1] = -3.0 * torch.eye(D)
+    bd = bad.to(DEV)
+    pkg._lib.call("vdn_delta_factor", bd.data_ptr(), B.data_ptr(), Fb, H, D, inv.data_ptr(), info.data_ptr(), -1, 0.0,
+                  None, s)
+    torch.cuda.synchronize()
+    want_info = vo.cholesky_info(bad.double())
+    assert torch.equal(info.cpu(), want_info)
+    assert int(info[2, 1]) == 1
+
+
+def test_branch_readout_matches_oracle_with_and_without_text():
+    H, D, hidden = 2, 64, 96
+    F, grid = 8, (4, 5)
+    tpf = grid[0] * grid[1]
+    rows = F * tpf
+    g = torch.Generator().manual_seed(60)
+    w = vo.make_branch_weights(g, hidden, H, D)
+    xv = torch.randn(rows, hidden, generator=g).to(torch.bfloat16)
+    q, k, v = (torch.randn(rows, H, D, generator=g).to(torch.bfloat16) for _ in range(3))
+    tx = torch.randn(11, hidden, generator=g).to(torch.bfloat16)
+    tk, tv = (torch.randn(11, H, D, generator=g).to(torch.bfloat16) for _ in range(2))
+    bounds = vo.window_bounds(F, 1, 2)
+    br = pkg.B200LinearBranch(w, H, D)
+    for text in (True, False):
+        got = br.readout(w, xv.to(DEV), q.to(DEV), k.to(DEV), v.to(DEV), F, tpf, bounds, frame_size=grid,
+                         text_x=tx.to(DEV) if text else None, text_k_raw=tk.to(DEV), text_v_raw=tv.to(DEV),
+                         skip_ends=True)
+        want = vo.branch_readout(w, xv.float(), q.float(), k.float(), v.float(), F, tpf, bounds, grid, H, D,
+                                 vo.BranchConfig(), text_x=tx.float() if text else None, text_k=tk.float(),
+                                 text_v=tv.float(), skip_ends=True)
+        assert rel_l2(got, want) < 2e-2, (text, rel_l2(got, want))
+        assert float(got[:tpf].abs().max()) == 0.0 and float(got[-tpf:].abs().max()) == 0.0

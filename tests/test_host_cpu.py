@@ -1,0 +1,181 @@
+"""CPU tests of the host side: the block-sparse window plan, layout mirrors, the C-ABI
+library exports and the deferred Cholesky scope.  No GPU compute is called."""
+
+from __future__ import annotations
+
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from __graft_entry__ import ROOT, load_package
+from oracle import vdn_oracle as vo
+
+pkg = load_package()
+from vdn_b200 import window as bw  # noqa: E402
+from vdn_b200 import branch as bbr  # noqa: E402
+
+
+def _expand_plan(plan, S):
+    """Emulate the kernel's key-tile walk and mask formula: returns a bool [S, S] matrix
+    and asserts that no (row, key) pair is visited twice."""
+    vs, ve, F, tpf = plan.video_start, plan.video_end, plan.num_frames, plan.tokens_per_frame
+    allowed = np.zeros((S, S), dtype=bool)
+    for qt in range(plan.n_qtiles):
+        rows = np.arange(qt * 128, min(S, qt * 128 + 128))
+        dense = (rows < vs) | (rows >= ve)
+        f = np.clip((rows - vs) // tpf, 0, F - 1)
+        if plan.anchor_rows:
+            dense |= (~dense) & ((f == 0) | (f == F - 1))
+        wlo = vs + plan.frame_lo[f] * tpf
+        whi = vs + (plan.frame_hi[f] + 1) * tpf
+        acol_lo = vs + tpf if plan.anchor_cols else vs
+        acol_hi = ve - tpf if plan.anchor_cols else ve
+        seen = np.zeros((len(rows), S), dtype=np.int32)
+        for t in range(plan.tile_off[qt], plan.tile_off[qt + 1]):
+            code = int(plan.ktile[t])
+            k0, masked, valid = code >> 9, (code >> 8) & 1, (code & 0xFF) + 1
+            keys = np.arange(k0, k0 + valid)
+            assert keys.max() < S
+            if masked:
+                ok = (dense[:, None] | (keys[None] < vs) | (keys[None] >= ve)
+                      | ((keys[None] >= wlo[:, None]) & (keys[None] < whi[:, None]))
+                      | (keys[None] < acol_lo) | (keys[None] >= acol_hi))
+            else:
+                ok = np.ones((len(rows), len(keys)), dtype=bool)
+            seen[:, keys] += 1
+            allowed[rows[:, None], keys[None, :]] |= ok
+        assert seen.max() <= 1, "a key tile overlaps another one"
+    return allowed
+
+
+GEOMS = [
+    # (text_before, frames, tpf, text_after, radius, chunk)
+    (32, 15, 16, 0, 1, 5),
+    (4, 11, 3, 2, 1, 3),
+    (4, 11, 3, 2, 2, 4),
+    (4, 11, 3, 2, 2, 0),
+    (24, 9, 16, 8, 2, 0),
+    (0, 7, 40, 0, 1, 2),
+    (130, 6, 200, 70, 0, 1),
+    (512, 31, 836, 0, 1, 5),
+]
+
+
+@pytest.mark.parametrize("geom", GEOMS)
+@pytest.mark.parametrize("anchors", vo.ANCHOR_MODES)
+def test_window_plan_covers_exactly_the_reference_mask(geom, anchors):
+    before, F, tpf, after, radius, chunk = geom
+    vs, ve = before, before + F * tpf
+    S = ve + after
+    if S > 8192 and anchors != "both":
+        pytest.skip("large geometry checked in the released anchor mode only")
+    bounds = vo.window_bounds(F, radius, chunk)
+    plan = bw.build_window_plan(S, vs, ve, F, tpf, bounds, anchors)
+    if S > 8192:
+        # spot-check rows instead of the full [S, S] mask
+        got = _expand_plan(plan, S)
+        rows = np.unique(np.linspace(0, S - 1, 97).astype(int))
+        want = vo.allowed_mask(S, vs, ve, F, tpf, bounds, anchors)[torch.as_tensor(rows)].numpy()
+        np.testing.assert_array_equal(got[rows], want)
+        return
+    got = _expand_plan(plan, S)
+    want = vo.allowed_mask(S, vs, ve, F, tpf, bounds, anchors).numpy()
+    np.testing.assert_array_equal(got, want)
+
+
+def test_plan_items_sorted_by_cost_and_cover_all_heads():
+    lay = vo.config_layout(vo.CONFIG0)
+    plan = bw.build_window_plan(lay.seq_len, lay.video_start, lay.video_end, lay.num_frames,
+                                lay.tokens_per_frame, list(lay.bounds), lay.anchor_frames)
+    items = plan.items(4)
+    assert len(items) == 4 * plan.n_qtiles
+    heads = items >> 20
+    qts = items & 0xFFFFF
+    costs = plan.tiles_per_q[qts]
+    assert np.all(np.diff(costs) <= 0)
+    assert sorted(zip(heads.tolist(), qts.tolist())) == [(h, q) for h in range(4) for q in range(plan.n_qtiles)]
+
+
+def test_plan_at_config1_is_block_sparse():
+    lay = vo.config_layout(vo.CONFIG1)
+    plan = bw.build_window_plan(lay.seq_len, lay.video_start, lay.video_end, lay.num_frames,
+                                lay.tokens_per_frame, list(lay.bounds), lay.anchor_frames)
+    dense_tiles = plan.n_qtiles * ((lay.seq_len + 127) // 128)
+    visited = int(plan.tiles_per_q.sum())
+    pairs = vo.attention_pairs(lay)
+    # visited key tiles carry at most ~12 % more work than the allowed pairs, and far less than dense
+    assert visited * 128 * 128 < 1.12 * pairs
+    assert visited < 0.6 * dense_tiles
+    assert plan.masked_tiles < 0.25 * visited
+
+
+def test_layout_mirrors_reference_geometry():
+    assert pkg.window_bounds(4, 1) == [(-1, 1), (0, 2), (1, 3), (2, 4)]
+    assert pkg.window_bounds(6, 1, 5)[0] == (-5, 9)
+    assert pkg.full_coverage(pkg.window_bounds(6, 1, 5), 6)
+    lay = pkg.make_layout(512, 31, (38, 22))
+    assert lay.seq_len == 26428 and lay.video_start == 512 and lay.tokens_per_frame == 836
+    with pytest.raises(ValueError):
+        pkg.window_bounds(3, -1)
+    with pytest.raises(RuntimeError):
+        pkg.current_layout()
+    with pkg.publish_layout(lay):
+        assert pkg.current_layout() is lay
+    assert pkg.current_layout(required=False) is None
+
+
+def test_library_exports_every_declared_symbol():
+    header = open(os.path.join(ROOT, "include", "vdn_b200.h")).read()
+    declared = set(re.findall(r"^int (vdn_\w+)\(", header, flags=re.M))
+    assert declared, "no declarations found"
+    lib_path = os.path.join(ROOT, "comfyui-kirei-vdn-h3_b200", "libvdn_b200.so")
+    if not os.path.exists(lib_path):
+        import __graft_entry__
+
+        __graft_entry__.build()
+    lib = pkg._lib.library()
+    for name in sorted(declared):
+        assert hasattr(lib, name), name
+    assert declared == set(pkg._lib.SIGNATURES), "ctypes table and header disagree"
+
+
+def test_missing_library_fails_loudly(monkeypatch):
+    monkeypatch.setattr(pkg._lib, "_lib", None)
+    monkeypatch.setattr(pkg._lib, "LIB_PATH", "/nonexistent/libvdn_b200.so")
+    with pytest.raises(RuntimeError, match="no CPU or library fallback"):
+        pkg._lib.library()
+
+
+def test_cpu_tensors_are_rejected():
+    q = torch.zeros(16, 2, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        pkg.window_softmax_b200(q, q, q, 0, 16, 1, 16, [(0, 0)], 0.125)
+
+
+def test_deferred_cholesky_scope_reports_factor_and_batch():
+    good = torch.zeros(3, 2, dtype=torch.int32)
+    bad = torch.zeros(3, 2, dtype=torch.int32)
+    bad.view(-1)[3] = 7
+    with pytest.raises(torch.linalg.LinAlgError, match="factor 1, batch 3: leading minor of order 7"):
+        with bbr.cholesky_runtime_scope() as checks:
+            bbr.record_factor_status(good)
+            bbr.record_factor_status(bad)
+            assert checks.factor_calls == 2
+    with bbr.cholesky_runtime_scope() as checks:
+        bbr.record_factor_status(good)
+    # outside a scope the check is immediate
+    with pytest.raises(torch.linalg.LinAlgError):
+        bbr.record_factor_status(bad)
+
+
+def test_status_codes_map_to_reference_exceptions():
+    with pytest.raises(ValueError):
+        pkg._lib.check(-1, "x")
+    with pytest.raises(ValueError):
+        pkg._lib.check(-2, "x")
+    with pytest.raises(RuntimeError):
+        pkg._lib.check(-3, "x")
+    pkg._lib.check(0, "x")
