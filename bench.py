@@ -203,6 +203,43 @@ def run_reference_arm(args, c, world, rank):
 METRIC = "VDN hybrid block fwd TFLOP/s at 31x836+512 tokens (ms in ms_per_step)"
 
 
+def run_attention_only(args, c):
+    """The window attention kernel alone on the config geometry (profiling / roofline)."""
+    from __graft_entry__ import load_package
+    from oracle import vdn_oracle as vo  # FLOP model only
+
+    pkg = load_package()
+    dev = torch.device("cuda", 0)
+    H, D = c["heads"], c["dim"]
+    lay = pkg.make_layout(c["text"], c["frames"], c["grid"])
+    flops = 4.0 * vo.attention_pairs(vo.config_layout(c)) * D * H
+    g = torch.Generator().manual_seed(0)
+    S = lay.seq_len
+    q = torch.randn(S, H, D, generator=g).to(dev, torch.bfloat16)
+    k = torch.randn(S, H, D, generator=g).to(dev, torch.bfloat16)
+    v = torch.randn(S, H, D, generator=g).to(dev, torch.bfloat16)
+    plans = pkg.WindowPlanCache()
+    st = pkg._lib.DeviceStatus(dev)
+    call = lambda: pkg.window_softmax_b200(q, k, v, lay.video_start, lay.video_end, lay.num_frames,  # noqa: E731
+                                           lay.tokens_per_frame, lay.bounds, D ** -0.5, lay.anchor_frames,
+                                           cache=plans, status=st)
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    st.raise_if_failed()
+    ms = e0.elapsed_time(e1) / max(args.steps, 1)
+    pk, src = peaks()
+    print(json.dumps({"kernel": "window_attention_kernel", "heads": H, "tokens": S, "ms": ms,
+                      "tflops": flops / (ms * 1e-3) / 1e12, "frac_of_burst_peak": flops / (ms * 1e-3) / 1e12 /
+                      pk["bf16_tflops"], "peak_source": src}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -211,10 +248,18 @@ def main():
     ap.add_argument("--impl", default="b200")
     ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["attention"], default=None,
+                    help="run one kernel alone on the config geometry (profiling small cases)")
+    ap.add_argument("--heads", type=int, default=None, help="override the head count (profiling small cases)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
-    c = CONFIGS[args.config]
+    c = dict(CONFIGS[args.config])
+    if args.heads:
+        c["heads"] = args.heads
+    if args.only == "attention":
+        run_attention_only(args, c)
+        return
     if args.impl == "reference":
         run_reference_arm(args, c, world, rank)
         if world > 1:

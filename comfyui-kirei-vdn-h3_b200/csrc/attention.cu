@@ -54,6 +54,19 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x for x <= 0 on the FMA/ALU pipes: x = n + f with n = round(x) (added-magic-number
+// rounding) and f in [-0.5, 0.5]; 2^f by a cubic fitted here for minimum relative error
+// (max 1.0e-4, far below the bf16 rounding P receives); 2^n added to the exponent bits.
+__device__ __forceinline__ float exp2_poly(float x) {
+  const float xc = fmaxf(x, -126.0f);
+  const float t = xc + 12582912.0f;  // 1.5 * 2^23: rounds xc to an integer in the low bits
+  const int n = __float_as_int(t) - 0x4B400000;
+  const float f = xc - (t - 12582912.0f);
+  const float p = fmaf(fmaf(fmaf(0.05500844f, f, 0.24220988f), f, 0.69328284f), f, 1.0f);
+  const float y = __int_as_float(__float_as_int(p) + (n << 23));
+  return x < -125.0f ? 0.0f : y;
+}
+
 template <int D>
 struct Layout {
   static constexpr int kQBytes = BQ * D * 2;
@@ -258,17 +271,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        float s[BKV];
-        {
-          uint32_t r[32];
+        uint32_t sr[BKV];  // raw scores of this row (fp32 bits)
 #pragma unroll
-          for (int c = 0; c < BKV / 32; ++c) {
-            tmem_ld32(tmem_base + lane_base + st * 128 + c * 32, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
-          }
-        }
+        for (int c = 0; c < BKV / 32; ++c)
+          tmem_ld32(tmem_base + lane_base + st * 128 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
+        tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(B(B_SEMPTY0 + st));
@@ -276,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int k0 = info >> 9;
         const int valid = (info & 0xFF) + 1;
         const bool masked = (info >> 8) & 1;
-        float mt = -INFINITY;
+        float mt = -INFINITY;  // tile max of the raw scores
         if (masked || valid < BKV) {
 #pragma unroll
           for (int c = 0; c < BKV; ++c) {
@@ -286,24 +293,29 @@ __global__ void __launch_bounds__(kThreads, 1)
               allow = dense || key < p.vs || key >= p.ve || (key >= wlo && key < whi) || key < acol_lo ||
                       key >= acol_hi;
             }
-            s[c] = allow ? s[c] * p.scale_log2 : -INFINITY;
-            mt = fmaxf(mt, s[c]);
+            if (!allow) sr[c] = __float_as_uint(-INFINITY);
+            mt = fmaxf(mt, __uint_as_float(sr[c]));
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < BKV; ++c) {
-            s[c] *= p.scale_log2;
-            mt = fmaxf(mt, s[c]);
-          }
+          for (int c = 0; c < BKV; ++c) mt = fmaxf(mt, __uint_as_float(sr[c]));
         }
-        const float m_new = fmaxf(m_run, mt);
+        // The reference max only moves when the tile max exceeds it by more than 2^8 (in
+        // log2 units), so exponents stay <= 8 and O is rescaled rarely; the result is exact.
+        const float mts = mt * p.scale_log2;
+        const bool grow = mts > m_run + 8.0f;
+        const float m_new = grow ? mts : m_run;
         const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        const float corr = ex2(m_run - m_use);  // m_run = -inf gives 0
+        const float corr = grow ? ex2(m_run - m_use) : 1.0f;  // m_run = -inf gives 0
         float rs = 0.f;
         uint32_t pk[BKV / 2];
 #pragma unroll
         for (int c = 0; c < BKV; c += 2) {
-          const float a = ex2(s[c] - m_use), b = ex2(s[c + 1] - m_use);
+          const float xa = fmaf(__uint_as_float(sr[c]), p.scale_log2, -m_use);
+          const float xb = fmaf(__uint_as_float(sr[c + 1]), p.scale_log2, -m_use);
+          // a quarter of the exponentials run on the FMA pipe to relieve the MUFU unit
+          const float a = ex2(xa);
+          const float b = ((c & 3) == 2) ? exp2_poly(xb) : ex2(xb);
           rs += a + b;
           pk[c / 2] = pack_bf16(a, b);
         }
@@ -316,17 +328,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          if (__any_sync(0xffffffffu, corr != 1.0f)) {
-            uint32_t r[32];
+          if (__any_sync(0xffffffffu, grow)) {
+            uint32_t o[D];
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-              const uint32_t ta = tmem_base + lane_base + 256 + c * 32;
-              tmem_ld32(ta, r);
-              tmem_ld_wait();
+            for (int c = 0; c < D / 32; ++c)
+              tmem_ld32(tmem_base + lane_base + 256 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(o + c * 32));
+            tmem_ld_wait();
 #pragma unroll
-              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
-              tmem_st32(ta, r);
-            }
+            for (int i = 0; i < D; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c)
+              tmem_st32(tmem_base + lane_base + 256 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(o + c * 32));
             tmem_st_wait();
           }
         }

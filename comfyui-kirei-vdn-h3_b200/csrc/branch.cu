@@ -6,7 +6,7 @@
 //                         (taps = 0: plain activation for q and text rows, kernels.py:47-51)
 //   3. vdn_alpha_gate     alpha = exp(-exp(A_log) softplus(up(mean_t down x) + dt_bias)) (branch.py:483-491)
 //   4. vdn_frame_stats    A = sym((beta K)^T K), B = (beta V)^T K per frame/head  (branch.py:197-243)
-//   5. vdn_delta_factor   Cholesky of I+A, L^-1, (I+A)^-1 = L^-T L^-1, info    (branch.py:148-160, :62-71)
+//   5. vdn_delta_factor   (I+A)^-1 of every SPD frame matrix, leading-minor info (branch.py:148-160, :62-71)
 //   6. vdn_bidir_scan     s_t = (B_t + s_{t-1} diag(alpha_t)) (I+A_t)^-1, both directions
 //                         (= Inj_t + s_{t-1} T_t of branch.py:297-312, fused so neither T nor
 //                          Inj is ever materialised)
@@ -24,18 +24,70 @@ __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __ex
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 
 // ---------------------------------------------------------------------------------
-// 1. Spatial depthwise conv.  in: rows (f*gh + y)*gw + x at row pitch ld_in; out [rows, C] bf16.
-// grid (gh, F, ceil(C/256)), block 256: one channel per thread, sliding along x.
+// 1. Spatial depthwise 5x5 conv.  in: rows (f*gh + y)*gw + x at row pitch ld_in; out
+// [rows, C] bf16 (rounded like the reference's bf16 conv2d output).
+// One thread per (channel pair, grid row); it slides along x keeping the 5x5 window of
+// both channels in registers, so each output costs 5 paired loads and 50 FMAs.
+// grid (ceil(C/256), gh, F), block 128.
 // ---------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) spatial_conv5_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in,
+                                                            const float* __restrict__ w, int gh, int gw, int C,
+                                                            __nv_bfloat16* __restrict__ out, long long ld_out) {
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
+  const int y = blockIdx.y, f = blockIdx.z;
+  if (c >= C) return;
+  float2 wr[5][5];
+#pragma unroll
+  for (int dy = 0; dy < 5; ++dy)
+#pragma unroll
+    for (int dx = 0; dx < 5; ++dx)
+      wr[dy][dx] = make_float2(w[(long long)c * 25 + dy * 5 + dx], w[(long long)(c + 1) * 25 + dy * 5 + dx]);
+  const long long frame0 = (long long)f * gh * gw;
+  auto load_col = [&](int x, float2 (&col)[5]) {
+#pragma unroll
+    for (int dy = 0; dy < 5; ++dy) {
+      const int yy = y + dy - 2;
+      if (x >= 0 && x < gw && yy >= 0 && yy < gh) {
+        const __nv_bfloat162 v =
+            *reinterpret_cast<const __nv_bfloat162*>(in + (frame0 + (long long)yy * gw + x) * ld_in + c);
+        col[dy] = __bfloat1622float2(v);
+      } else {
+        col[dy] = make_float2(0.f, 0.f);
+      }
+    }
+  };
+  float2 win[5][5];  // win[slot][dy]; slot (u + k) % 5 holds column x - 2 + k
+#pragma unroll
+  for (int s = 0; s < 5; ++s) load_col(s - 2, win[s]);
+  for (int x0 = 0; x0 < gw; x0 += 5) {
+#pragma unroll
+    for (int u = 0; u < 5; ++u) {
+      const int x = x0 + u;
+      if (x < gw) {
+        float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 5; ++k)
+#pragma unroll
+          for (int dy = 0; dy < 5; ++dy) {
+            acc.x += wr[dy][k].x * win[(u + k) % 5][dy].x;
+            acc.y += wr[dy][k].y * win[(u + k) % 5][dy].y;
+          }
+        *reinterpret_cast<__nv_bfloat162*>(out + (frame0 + (long long)y * gw + x) * ld_out + c) =
+            __floats2bfloat162_rn(acc.x, acc.y);
+        load_col(x + 3, win[u]);  // replaces column x - 2
+      }
+    }
+  }
+}
+
+// Generic odd kernel sizes (kh*kw <= 49): one thread per channel, direct sum.
 __global__ void spatial_conv_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in,
                                     const float* __restrict__ w, int kh, int kw, int gh, int gw, int C,
                                     __nv_bfloat16* __restrict__ out, long long ld_out) {
   const int y = blockIdx.x, f = blockIdx.y;
   const int c = blockIdx.z * blockDim.x + threadIdx.x;
   if (c >= C) return;
-  float wr[49];
   const int taps = kh * kw;
-  for (int i = 0; i < taps; ++i) wr[i] = w[(long long)c * taps + i];
   const int ph = kh / 2, pw = kw / 2;
   const long long frame0 = (long long)f * gh * gw;
   for (int x = 0; x < gw; ++x) {
@@ -46,7 +98,7 @@ __global__ void spatial_conv_kernel(const __nv_bfloat16* __restrict__ in, long l
       for (int dx = 0; dx < kw; ++dx) {
         const int xx = x + dx - pw;
         if (xx < 0 || xx >= gw) continue;
-        acc += wr[dy * kw + dx] * __bfloat162float(in[(frame0 + (long long)yy * gw + xx) * ld_in + c]);
+        acc += w[(long long)c * taps + dy * kw + dx] * __bfloat162float(in[(frame0 + (long long)yy * gw + xx) * ld_in + c]);
       }
     }
     out[(frame0 + (long long)y * gw + x) * ld_out + c] = __float2bfloat16_rn(acc);
@@ -132,16 +184,27 @@ __global__ void temporal_act_kernel(const __nv_bfloat16* __restrict__ in, long l
 __global__ void alpha_gate_kernel(const float* __restrict__ down, long long ld_down, int T, int R,
                                   const float* __restrict__ w_up, const float* __restrict__ dt_bias,
                                   const float* __restrict__ a_log, int H, int D, float* __restrict__ alpha) {
-  extern __shared__ float mean[];
+  extern __shared__ float mean[];  // [R] then [256] partials
+  float* part = mean + R;
   const int f = blockIdx.x;
-  for (int j = threadIdx.x; j < R; j += blockDim.x) {
+  // frame mean: thread t sums column t % R over rows t / R, t / R + G, ... (G = 256 / R)
+  const int G = max(1, 256 / R);
+  for (int j0 = 0; j0 < R; j0 += 256 / G) {
+    const int j = j0 + (int)threadIdx.x % (256 / G), r0 = (int)threadIdx.x / (256 / G);
     float acc = 0.f;
-    for (int s = 0; s < T; ++s) acc += down[((long long)f * T + s) * ld_down + j];
-    mean[j] = acc / (float)T;
+    if (j < R && r0 < G)
+      for (int s = r0; s < T; s += G) acc += down[((long long)f * T + s) * ld_down + j];
+    part[threadIdx.x] = acc;
+    __syncthreads();
+    if ((int)threadIdx.x < 256 / G && j0 + (int)threadIdx.x < R) {
+      float tot = 0.f;
+      for (int r = 0; r < G; ++r) tot += part[r * (256 / G) + threadIdx.x];
+      mean[j0 + threadIdx.x] = tot / (float)T;
+    }
+    __syncthreads();
   }
-  __syncthreads();
   const int inner = H * D;
-  for (int c = threadIdx.x; c < inner; c += blockDim.x) {
+  for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < inner; c += blockDim.x * gridDim.y) {
     float d = dt_bias[c];
     const float* wr = w_up + (long long)c * R;
     for (int j = 0; j < R; ++j) d += wr[j] * mean[j];
@@ -217,90 +280,117 @@ __global__ void __launch_bounds__(256) frame_stats_kernel(const __nv_bfloat16* _
 }
 
 // ---------------------------------------------------------------------------------
-// 5. Delta factor: inv = (I + sym(A))^-1 by Cholesky (lower), L^-1 by forward substitution,
-// inv = L^-T L^-1.  info[batch] = order of the first non-positive leading minor (0 = SPD).
-// For batches listed as text frames, also s0 = scale * B inv.  grid (H, F), 256 threads.
+// 5. Delta factor: inv = (I + sym(A))^-1 by in-place Gauss-Jordan elimination without
+// pivoting, the matrix held in registers (one TBxTB block per thread of a 16x16 grid).
+// For a symmetric matrix the step-k pivot is the ratio of the k-th and (k-1)-th leading
+// principal minors, so the first non-positive pivot gives exactly cholesky_ex's info
+// (order of the first leading minor that is not positive definite, branch.py:62-71).
+// grid (H, F), 256 threads.  info[f, h] = 0 when SPD.
 // ---------------------------------------------------------------------------------
 template <int D>
-__global__ void __launch_bounds__(256) delta_factor_kernel(const float* __restrict__ A, const float* __restrict__ Bm,
-                                                           int H, float* __restrict__ inv_out,
-                                                           int* __restrict__ info, int text_frame,
-                                                           float text_scale, float* __restrict__ s0_out) {
-  constexpr int P = D + 1;  // padded pitch
-  extern __shared__ float sm[];
-  float* Lm = sm;            // [D][P]  M -> L (lower)
-  float* X = sm + D * P;     // [D][P]  X = L^-1 (lower)
-  __shared__ int bad;
+__global__ void __launch_bounds__(256) spd_inverse_kernel(const float* __restrict__ A, int H, float* __restrict__ inv_out,
+                                                          int* __restrict__ info) {
+  constexpr int TB = D / 16;
+  __shared__ float colk[D];
+  __shared__ float rowk[D];
   const int h = blockIdx.x, f = blockIdx.y;
   const long long mb = ((long long)f * H + h) * D * D;
-  const int tid = threadIdx.x;
-  for (int e = tid; e < D * D; e += 256) {
-    const int i = e / D, j = e % D;
-    float v = 0.5f * (A[mb + (long long)i * D + j] + A[mb + (long long)j * D + i]);
-    if (i == j) v += 1.0f;
-    Lm[i * P + j] = v;
-  }
-  if (tid == 0) bad = 0;
-  __syncthreads();
-  // Right-looking Cholesky, lower triangle in place.
+  const int ti = threadIdx.x / 16, tj = threadIdx.x % 16;
+  const int r0 = ti * TB, c0 = tj * TB;
+  float m[TB][TB];
+#pragma unroll
+  for (int i = 0; i < TB; ++i)
+#pragma unroll
+    for (int j = 0; j < TB; ++j) {
+      const int r = r0 + i, c = c0 + j;
+      m[i][j] = 0.5f * (A[mb + (long long)r * D + c] + A[mb + (long long)c * D + r]) + (r == c ? 1.f : 0.f);
+    }
+  int bad = 0;
   for (int k = 0; k < D; ++k) {
-    const float dkk = Lm[k * P + k];
-    if (dkk <= 0.f || !(dkk == dkk)) {
-      if (tid == 0 && bad == 0) bad = k + 1;
-      break;  // uniform: every thread reads the same value
-    }
-    const float d = sqrtf(dkk);
-    __syncthreads();
-    if (tid == 0) Lm[k * P + k] = d;
-    for (int i = k + 1 + tid; i < D; i += 256) Lm[i * P + k] /= d;
-    __syncthreads();
-    // trailing update of the lower triangle: rows i > k, columns k < j <= i
-    const int n = D - k - 1;
-    for (int e = tid; e < n * n; e += 256) {
-      const int i = k + 1 + e / n, j = k + 1 + e % n;
-      if (j <= i) Lm[i * P + j] -= Lm[i * P + k] * Lm[j * P + k];
-    }
-    __syncthreads();
-  }
-  __syncthreads();
-  if (tid == 0) info[(long long)f * H + h] = bad;
-  if (bad) {
-    for (int e = tid; e < D * D; e += 256) inv_out[mb + e] = __int_as_float(0x7fc00000);
-    return;
-  }
-  // X = L^-1, one column j per thread (threads >= D idle).
-  if (tid < D) {
-    const int j = tid;
-    for (int i = 0; i < D; ++i) {
-      if (i < j) {
-        X[i * P + j] = 0.f;
-        continue;
+    const int kb = k / TB, kr = k % TB;
+    if (tj == kb) {
+#pragma unroll
+      for (int i = 0; i < TB; ++i) {
+#pragma unroll
+        for (int j = 0; j < TB; ++j)
+          if (j == kr) colk[r0 + i] = m[i][j];
       }
-      float acc = (i == j) ? 1.f : 0.f;
-      for (int k = j; k < i; ++k) acc -= Lm[i * P + k] * X[k * P + j];
-      X[i * P + j] = acc / Lm[i * P + i];
     }
-  }
-  __syncthreads();
-  // inv[i][j] = sum_k X[k][i] X[k][j], k >= max(i, j)
-  for (int e = tid; e < D * D; e += 256) {
-    const int i = e / D, j = e % D;
-    float acc = 0.f;
-    for (int k = max(i, j); k < D; ++k) acc += X[k * P + i] * X[k * P + j];
-    inv_out[mb + e] = acc;
-  }
-  if (f == text_frame && s0_out) {
-    __syncthreads();
-    // reuse Lm for inv (full, symmetric)
-    for (int e = tid; e < D * D; e += 256) Lm[(e / D) * P + (e % D)] = inv_out[mb + e];
-    __syncthreads();
-    for (int e = tid; e < D * D; e += 256) {
-      const int r = e / D, c = e % D;
-      float acc = 0.f;
-      for (int k = 0; k < D; ++k) acc += Bm[mb + (long long)r * D + k] * Lm[k * P + c];
-      s0_out[(long long)h * D * D + e] = text_scale * acc;
+    if (ti == kb) {
+#pragma unroll
+      for (int i = 0; i < TB; ++i)
+        if (i == kr) {
+#pragma unroll
+          for (int j = 0; j < TB; ++j) rowk[c0 + j] = m[i][j];
+        }
     }
+    __syncthreads();
+    const float p = rowk[k];
+    if (!(p > 0.f)) {  // uniform: every thread read the same pivot
+      bad = k + 1;
+      break;
+    }
+    const float ip = 1.0f / p;
+    float a_i[TB], b_j[TB];
+#pragma unroll
+    for (int i = 0; i < TB; ++i) a_i[i] = colk[r0 + i] * ip;
+#pragma unroll
+    for (int j = 0; j < TB; ++j) b_j[j] = rowk[c0 + j];
+#pragma unroll
+    for (int i = 0; i < TB; ++i)
+#pragma unroll
+      for (int j = 0; j < TB; ++j) m[i][j] -= a_i[i] * b_j[j];
+    // row k: a_kj / p ; column k: -a_ik / p ; pivot: 1 / p
+    if (ti == kb) {
+#pragma unroll
+      for (int i = 0; i < TB; ++i)
+        if (i == kr) {
+#pragma unroll
+          for (int j = 0; j < TB; ++j) m[i][j] = b_j[j] * ip;
+        }
+    }
+    if (tj == kb) {
+#pragma unroll
+      for (int i = 0; i < TB; ++i)
+#pragma unroll
+        for (int j = 0; j < TB; ++j)
+          if (j == kr) m[i][j] = (r0 + i == k) ? ip : -a_i[i];
+    }
+    __syncthreads();
   }
+  if (threadIdx.x == 0) info[(long long)f * H + h] = bad;
+  const float nan = __int_as_float(0x7fc00000);
+#pragma unroll
+  for (int i = 0; i < TB; ++i)
+#pragma unroll
+    for (int j = 0; j < TB; ++j) inv_out[mb + (long long)(r0 + i) * D + c0 + j] = bad ? nan : m[i][j];
+}
+
+// s0[h] = scale * B[f_text, h] inv[f_text, h] (the text state, branch.py:649-670).
+// grid H, 256 threads; each thread computes TB x TB entries.
+template <int D>
+__global__ void __launch_bounds__(256) text_state_kernel(const float* __restrict__ Bm, const float* __restrict__ inv,
+                                                         int H, int text_frame, float scale, float* __restrict__ s0) {
+  constexpr int TB = D / 16;
+  const int h = blockIdx.x;
+  const long long mb = ((long long)text_frame * H + h) * D * D;
+  const int r0 = (threadIdx.x / 16) * TB, c0 = (threadIdx.x % 16) * TB;
+  float acc[TB][TB] = {};
+  for (int k = 0; k < D; ++k) {
+    float a[TB], b[TB];
+#pragma unroll
+    for (int i = 0; i < TB; ++i) a[i] = Bm[mb + (long long)(r0 + i) * D + k];
+#pragma unroll
+    for (int j = 0; j < TB; ++j) b[j] = inv[mb + (long long)k * D + c0 + j];
+#pragma unroll
+    for (int i = 0; i < TB; ++i)
+#pragma unroll
+      for (int j = 0; j < TB; ++j) acc[i][j] += a[i] * b[j];
+  }
+#pragma unroll
+  for (int i = 0; i < TB; ++i)
+#pragma unroll
+    for (int j = 0; j < TB; ++j) s0[((long long)h * D + r0 + i) * D + c0 + j] = scale * acc[i][j];
 }
 
 // ---------------------------------------------------------------------------------
@@ -349,7 +439,7 @@ __global__ void __launch_bounds__(256) bidir_scan_kernel(const float* __restrict
 // ---------------------------------------------------------------------------------
 // 7. Readout: state (gather + alpha bridge, cast to bf16) -> R = Q S^T -> bf16 ->
 // RMSNorm(D) x norm_w -> bf16 -> x output gate -> out rows.
-// grid (ceil(T/64), H, F), 256 threads: thread = (token s = tid/4, v = g + 4*vi).
+// grid (ceil(T/64), H, F), 256 threads: thread = (4 tokens, D/16 values v = g + 16*vi).
 // ---------------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(256) readout_kernel(
@@ -359,16 +449,16 @@ __global__ void __launch_bounds__(256) readout_kernel(
     const float* __restrict__ norm_w, const __nv_bfloat16* __restrict__ gate, long long ld_gate,
     __nv_bfloat16* __restrict__ out, long long ld_out, long long out_row0) {
   constexpr int P = D + 1;
+  constexpr int NV = D / 16;
   extern __shared__ float sm[];
   float* st = sm;            // [D][P] state (v, k)
-  float* sq = sm + D * P;    // [64][P] q tile
+  float* qT = sm + D * P;    // [D][64] q tile, transposed (k, s)
   __shared__ float dec_b[D], dec_a[D];
   const int tile = blockIdx.x, h = blockIdx.y, f = blockIdx.z;
   const int tid = threadIdx.x;
   const int raw_lo = lo_arr[f], raw_hi = hi_arr[f];
   const int lo = max(raw_lo, 0), hi = min(raw_hi, F - 1);
   const bool has_before = raw_lo - 1 >= 0, has_after = raw_hi + 1 < F;
-  // decays
   for (int k = tid; k < D; k += 256) {
     float lb = 0.f, la = 0.f;
     if (use_alpha) {
@@ -391,37 +481,50 @@ __global__ void __launch_bounds__(256) readout_kernel(
   const int s_base = tile * 64;
   for (int e = tid; e < 64 * D; e += 256) {
     const int s = e / D, k = e % D;
-    sq[s * P + k] = (s_base + s < T) ? __bfloat162float(Q[(((long long)f * H + h) * T + s_base + s) * D + k]) : 0.f;
+    qT[k * 64 + s] = (s_base + s < T) ? __bfloat162float(Q[(((long long)f * H + h) * T + s_base + s) * D + k]) : 0.f;
   }
   __syncthreads();
-  const int s = tid / 4, g = tid % 4;
-  constexpr int NV = D / 4;
-  float acc[NV];
+  const int sg = (tid / 16) * 4, g = tid % 16;
+  float acc[4][NV];
 #pragma unroll
-  for (int vi = 0; vi < NV; ++vi) acc[vi] = 0.f;
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int vi = 0; vi < NV; ++vi) acc[a][vi] = 0.f;
   for (int k = 0; k < D; ++k) {
-    const float qk = sq[s * P + k];
+    const float4 q4 = *reinterpret_cast<const float4*>(qT + k * 64 + sg);
+    float sv[NV];
 #pragma unroll
-    for (int vi = 0; vi < NV; ++vi) acc[vi] += qk * st[(g + 4 * vi) * P + k];
-  }
-  float ss = 0.f;
-#pragma unroll
-  for (int vi = 0; vi < NV; ++vi) {
-    acc[vi] = bf16_round(acc[vi]);
-    ss += acc[vi] * acc[vi];
-  }
-  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-  const float inv = rsqrtf(ss / (float)D + 1e-6f);
-  const int tok = s_base + s;
-  if (tok < T) {
-    const long long row = out_row0 + (long long)f * T + tok;
+    for (int vi = 0; vi < NV; ++vi) sv[vi] = st[(g + 16 * vi) * P + k];
 #pragma unroll
     for (int vi = 0; vi < NV; ++vi) {
-      const int v = g + 4 * vi;
-      const float nv = bf16_round(acc[vi] * inv * norm_w[v]);
-      const float gv = __bfloat162float(gate[row * ld_gate + h * D + v]);
-      out[row * ld_out + h * D + v] = __float2bfloat16_rn(nv * gv);
+      acc[0][vi] += q4.x * sv[vi];
+      acc[1][vi] += q4.y * sv[vi];
+      acc[2][vi] += q4.z * sv[vi];
+      acc[3][vi] += q4.w * sv[vi];
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    float ss = 0.f;
+#pragma unroll
+    for (int vi = 0; vi < NV; ++vi) {
+      acc[a][vi] = bf16_round(acc[a][vi]);
+      ss += acc[a][vi] * acc[a][vi];
+    }
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = rsqrtf(ss / (float)D + 1e-6f);
+    const int tok = s_base + sg + a;
+    if (tok < T) {
+      const long long local = (long long)f * T + tok;  // row within the branch frames
+      const long long row = out_row0 + local;
+#pragma unroll
+      for (int vi = 0; vi < NV; ++vi) {
+        const int v = g + 16 * vi;
+        const float nv = bf16_round(acc[a][vi] * inv * norm_w[v]);
+        const float gv = __bfloat162float(gate[local * ld_gate + h * D + v]);
+        out[row * ld_out + h * D + v] = __float2bfloat16_rn(nv * gv);
+      }
     }
   }
 }
@@ -449,10 +552,18 @@ int vdn_spatial_conv(const void* in, long long ld_in, const float* w, int kh, in
   if (!in || !w || !out || kh <= 0 || kw <= 0 || kh * kw > 49 || (kh % 2) == 0 || (kw % 2) == 0)
     return vdn::kBadArgument;
   if (F <= 0 || gh <= 0 || gw <= 0 || C <= 0) return vdn::kBadArgument;
-  dim3 grid(gh, F, (C + 255) / 256);
-  spatial_conv_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, kh, kw, gh, gw, C,
-      reinterpret_cast<__nv_bfloat16*>(out), ld_out);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  const bool paired = kh == 5 && kw == 5 && (C % 2) == 0 && (ld_in % 2) == 0 && (ld_out % 2) == 0 &&
+                      (reinterpret_cast<uintptr_t>(in) % 4) == 0 && (reinterpret_cast<uintptr_t>(out) % 4) == 0;
+  if (paired) {
+    dim3 grid((C / 2 + 127) / 128, gh, F);
+    spatial_conv5_kernel<<<grid, 128, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, gh, gw, C,
+                                              reinterpret_cast<__nv_bfloat16*>(out), ld_out);
+  } else {
+    dim3 grid(gh, F, (C + 255) / 256);
+    spatial_conv_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, kh, kw, gh, gw,
+                                             C, reinterpret_cast<__nv_bfloat16*>(out), ld_out);
+  }
   return vdn::launch_status();
 }
 
@@ -479,7 +590,9 @@ int vdn_temporal_act(const void* in, long long ld_in, const float* w, int taps, 
 int vdn_alpha_gate(const float* down, long long ld_down, int F, int T, int R, const float* w_up,
                    const float* dt_bias, const float* a_log, int H, int D, float* alpha, void* stream) {
   if (!down || !w_up || !dt_bias || !a_log || !alpha || F <= 0 || T <= 0 || R <= 0) return vdn::kBadArgument;
-  alpha_gate_kernel<<<F, 256, R * sizeof(float), reinterpret_cast<cudaStream_t>(stream)>>>(
+  if (R > 4096) return vdn::kUnsupported;
+  dim3 grid(F, (H * D + 255) / 256);
+  alpha_gate_kernel<<<grid, 256, (R + 256) * sizeof(float), reinterpret_cast<cudaStream_t>(stream)>>>(
       down, ld_down, T, R, w_up, dt_bias, a_log, H, D, alpha);
   return vdn::launch_status();
 }
@@ -509,14 +622,15 @@ int vdn_frame_stats(const void* K, const void* V, int F, int H, int T, int D, co
 int vdn_delta_factor(const float* A, const float* B, int F, int H, int D, float* inv, int* info, int text_frame,
                      float text_scale, float* s0, void* stream) {
   if (!A || !inv || !info || (text_frame >= 0 && (!B || !s0))) return vdn::kBadArgument;
+  if (text_frame >= F) return vdn::kBadArgument;
   dim3 grid(H, F);
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  const size_t smem = 2 * (size_t)D * (D + 1) * sizeof(float);
   if (D == 128) {
-    cudaFuncSetAttribute(delta_factor_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    delta_factor_kernel<128><<<grid, 256, smem, s>>>(A, B, H, inv, info, text_frame, text_scale, s0);
+    spd_inverse_kernel<128><<<grid, 256, 0, s>>>(A, H, inv, info);
+    if (text_frame >= 0) text_state_kernel<128><<<H, 256, 0, s>>>(B, inv, H, text_frame, text_scale, s0);
   } else if (D == 64) {
-    delta_factor_kernel<64><<<grid, 256, smem, s>>>(A, B, H, inv, info, text_frame, text_scale, s0);
+    spd_inverse_kernel<64><<<grid, 256, 0, s>>>(A, H, inv, info);
+    if (text_frame >= 0) text_state_kernel<64><<<H, 256, 0, s>>>(B, inv, H, text_frame, text_scale, s0);
   } else {
     return vdn::kUnsupported;
   }
@@ -545,8 +659,8 @@ int vdn_bidir_scan(const float* inv, const float* B, const float* alpha, const f
 }
 
 // 7. Readout + epilogue (branch.py:372-396, :494-530, :780).  Q FHSD [F, H, T, D] bf16;
-// lo/hi [F] int32 raw window bounds of the branch frames; gate [rows, ld_gate] bf16 holding
-// sigmoid(up(down x) + b); out rows out_row0 + f*T + s, columns h*D + v.
+// lo/hi [F] int32 raw window bounds of the branch frames; gate [F*T, ld_gate] bf16 holding
+// sigmoid(up(down x) + b) per branch row; out rows out_row0 + f*T + s, columns h*D + v.
 int vdn_readout(const void* Q, int F, int H, int T, int D, const float* prefix, const float* suffix,
                 const float* alpha, const float* s0, const int* lo, const int* hi, int use_alpha,
                 const float* norm_w, const void* gate, long long ld_gate, void* out, long long ld_out,
@@ -554,7 +668,7 @@ int vdn_readout(const void* Q, int F, int H, int T, int D, const float* prefix, 
   if (!Q || !prefix || !suffix || !alpha || !lo || !hi || !norm_w || !gate || !out) return vdn::kBadArgument;
   dim3 grid((T + 63) / 64, H, F);
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  const size_t smem = (size_t)(D + 64) * (D + 1) * sizeof(float);
+  const size_t smem = (size_t)(D * (D + 1) + D * 64) * sizeof(float);
   if (D == 128) {
     cudaFuncSetAttribute(readout_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     readout_kernel<128><<<grid, 256, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(Q), T, F, H, prefix, suffix,

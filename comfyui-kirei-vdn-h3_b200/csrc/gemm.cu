@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_m = (M + BM - 1) / BM;
   const int num_n = (N + BN - 1) / BN;
   const int total = num_m * num_n;
-  const int nk = K / T::BK;
+  const int nk = (K + T::BK - 1) / T::BK;  // the TMA zero-fills the K tail
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -400,13 +400,13 @@ int launch(const void* A, long long lda, const void* A2, long long lda2, long lo
            const void* B, long long ldb, int M, int N, int K, const Epilogue& ep, int* err,
            cudaStream_t stream) {
   using T = Traits<KIND>;
-  if (M <= 0 || N <= 0 || K <= 0 || (K % T::BK) != 0) return kUnsupported;
+  if (M <= 0 || N <= 0 || K <= 0 || (K % 16) != 0) return kUnsupported;
   if (A2 == nullptr) {
     A2 = A;
     lda2 = lda;
     k_split = K;
   }
-  if (k_split <= 0 || k_split > K || (k_split % T::BK) != 0) return kUnsupported;
+  if (k_split <= 0 || k_split > K || (k_split != K && (k_split % T::BK) != 0)) return kUnsupported;
   const CUtensorMapDataType dt = KIND == 0 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const int eb = KIND == 0 ? 2 : 1;
   CUtensorMap ta, ta2, tb;

@@ -65,10 +65,11 @@ class WindowPlan:
         return len(self.tiles_per_q)
 
     def items(self, heads: int) -> np.ndarray:
-        """(head << 20) | q_tile, most expensive first, heads interleaved."""
+        """(head << 20) | q_tile, head-major so the CTAs in flight share one head's K/V in
+        L2; within a head the most expensive query tiles come first."""
         qt = np.arange(self.n_qtiles, dtype=np.int64)
         order = np.argsort(-self.tiles_per_q, kind="stable")
-        codes = (np.arange(heads, dtype=np.int64)[None, :] << 20) | qt[order][:, None]
+        codes = (np.arange(heads, dtype=np.int64)[:, None] << 20) | qt[order][None, :]
         return codes.reshape(-1).astype(np.int32)
 
     def key_tiles_total(self, heads: int) -> int:

@@ -83,8 +83,11 @@ def test_block_quantised_projections_match_oracle(precision):
     got = _run_block(bw, _layout(c), c["heads"], c["dim"], x, precision=precision)
     want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(), precision=precision)
     exact = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig())
-    # quantised block vs its own CPU restatement; and both near the unquantised block
-    assert rel_l2(got, want) < 2e-2
+    # Quantised block vs its own CPU restatement.  The two pipelines quantise activations
+    # that already differ by bf16 rounding, so a few per cent of e4m3 codes land one ulp
+    # (12.5 %) apart; that sets the fp8 floor near 2-3 %.  The GEMM itself is checked
+    # exactly (to 1e-5) in test_gpu_kernels.py.
+    assert rel_l2(got, want) < (2e-2 if precision == "int8" else 3e-2)
     assert rel_l2(got, exact) < (3e-2 if precision == "int8" else 8e-2)
 
 

@@ -110,9 +110,9 @@ def test_qkv_gemm_epilogue():
     qkn = torch.empty(S, 2 * inner, device=DEV, dtype=torch.bfloat16)
     aux = torch.empty(S, n_aux, device=DEV, dtype=torch.float32)
     st = pkg._lib.DeviceStatus(DEV)
-    xd, wd = x.to(DEV), w.to(DEV)
+    xd, wd, nwd = x.to(DEV), w.to(DEV), nw.to(DEV)
     pkg._lib.call("vdn_qkv_gemm", 0, xd.data_ptr(), hidden, wd.data_ptr(), hidden, S, hidden, inner, n_aux, D,
-                  nw.to(DEV).data_ptr(), 1e-6, 1.0, None, None, None, None, qkv.data_ptr(), 3 * inner,
+                  nwd.data_ptr(), 1e-6, 1.0, None, None, None, None, qkv.data_ptr(), 3 * inner,
                   qkn.data_ptr(), 2 * inner, aux.data_ptr(), n_aux, st.err_ptr, pkg._lib.stream_handle(DEV))
     torch.cuda.synchronize()
     st.raise_if_failed()
@@ -221,8 +221,8 @@ def test_statistics_factor_scan_match_oracle_and_report_non_spd():
     A = torch.empty(Fb, H, D, D, device=DEV)
     B = torch.empty_like(A)
     s = pkg._lib.stream_handle(DEV)
-    ld = logits.to(DEV)
-    pkg._lib.call("vdn_frame_stats", kf.to(DEV).data_ptr(), vf.to(DEV).data_ptr(), Fb, H, T, D, ld.data_ptr(), 8, 2,
+    ld, kd, vd = logits.to(DEV), kf.to(DEV), vf.to(DEV)  # device copies must outlive the async launch
+    pkg._lib.call("vdn_frame_stats", kd.data_ptr(), vd.data_ptr(), Fb, H, T, D, ld.data_ptr(), 8, 2,
                   A.data_ptr(), B.data_ptr(), s)
     beta = torch.sigmoid(logits[:, 2:2 + H]).reshape(Fb, T, H).permute(0, 2, 1)
     wa, wb = vo.frame_statistics(kf.float(), vf.float(), beta)
@@ -240,8 +240,8 @@ def test_statistics_factor_scan_match_oracle_and_report_non_spd():
     prefix = torch.empty_like(A)
     suffix = torch.empty_like(A)
     s0 = (torch.randn(H, D, D, generator=g) * 0.1)
-    ad = alpha.to(DEV)
-    pkg._lib.call("vdn_bidir_scan", inv.data_ptr(), B.data_ptr(), ad.data_ptr(), s0.to(DEV).data_ptr(), Fb, H, D,
+    ad, s0d = alpha.to(DEV), s0.to(DEV)
+    pkg._lib.call("vdn_bidir_scan", inv.data_ptr(), B.data_ptr(), ad.data_ptr(), s0d.data_ptr(), Fb, H, D,
                   prefix.data_ptr(), suffix.data_ptr(), s)
     trans, inj = vo.factor_apply(alpha, wa, wb)
     wp, wsf = vo.run_scans(trans, inj, s0.double())
@@ -276,8 +276,17 @@ def test_branch_readout_matches_oracle_with_and_without_text():
         got = br.readout(w, xv.to(DEV), q.to(DEV), k.to(DEV), v.to(DEV), F, tpf, bounds, frame_size=grid,
                          text_x=tx.to(DEV) if text else None, text_k_raw=tk.to(DEV), text_v_raw=tv.to(DEV),
                          skip_ends=True)
-        want = vo.branch_readout(w, xv.float(), q.float(), k.float(), v.float(), F, tpf, bounds, grid, H, D,
-                                 vo.BranchConfig(), text_x=tx.float() if text else None, text_k=tk.float(),
-                                 text_v=tv.float(), skip_ends=True)
-        assert rel_l2(got, want) < 2e-2, (text, rel_l2(got, want))
+        want, parts = vo.branch_readout(w, xv.float(), q.float(), k.float(), v.float(), F, tpf, bounds, grid, H, D,
+                                        vo.BranchConfig(), text_x=tx.float() if text else None, text_k=tk.float(),
+                                        text_v=tv.float(), skip_ends=True, return_parts=True)
+        ws = br.workspace(DEV, F - 2, tpf, 11 if text else 0)
+        stages = {name: rel_l2(getattr(ws, attr), parts[name]) for name, attr in
+                  (("q", "qf"), ("k", "kf"), ("v", "vf"), ("alpha", "alpha"), ("prefix", "prefix"),
+                   ("suffix", "suffix"))}
+        stages["A"] = rel_l2(ws.A[:F - 2], parts["A"])
+        stages["B"] = rel_l2(ws.B[:F - 2], parts["B"])
+        if text:
+            stages["text_state"] = rel_l2(ws.s0, parts["text_state"])
+        msg = "; ".join(f"{k}={v:.3e}" for k, v in stages.items())
+        assert rel_l2(got, want) < 2e-2, f"text={text} out={rel_l2(got, want):.3e} stages: {msg}"
         assert float(got[:tpf].abs().max()) == 0.0 and float(got[-tpf:].abs().max()) == 0.0
