@@ -28,7 +28,7 @@ SIGNATURES: dict[str, list] = {
     "vdn_qkv_gemm": [_I, _P, _L, _P, _L, _I, _I, _I, _I, _I, _P, _F, _F, _P, _P, _P, _P, _P, _L, _P, _L, _P, _L,
                      _P, _P],
     "vdn_window_attention": [_P, _L, _P, _L, _P, _L, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _I, _P,
-                             _P, _P, _L, _P, _L, _I, _P, _P, _P],
+                             _P, _P, _L, _P, _L, _I, _P, _P, _P, _P],
     "vdn_spatial_conv": [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _L, _P],
     "vdn_temporal_act": [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _P],
     "vdn_alpha_gate": [_P, _L, _I, _I, _I, _P, _P, _P, _I, _I, _P, _P],
@@ -112,6 +112,7 @@ class DeviceStatus:
     reference's deferred Cholesky validation, branch.py:27-59).
 
     word 0: first kernel wait-timeout code (0 = none).
+    word 1: work-queue counter of the persistent attention kernel (zeroed per launch).
     """
 
     def __init__(self, device):
@@ -120,6 +121,10 @@ class DeviceStatus:
     @property
     def err_ptr(self) -> int:
         return self.words.data_ptr()
+
+    @property
+    def counter_ptr(self) -> int:
+        return self.words.data_ptr() + 4
 
     def reset(self):
         self.words.zero_()

@@ -46,6 +46,7 @@ struct Params {
   long long ld_gate;
   int gate_col0;
   const float* gate_bias;           // [H] or null
+  int* work_counter;                // zeroed before the launch; items are claimed with atomicAdd
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -84,8 +85,10 @@ struct Layout {
 // Barrier slots.
 enum {
   B_QFULL = 0, B_QEMPTY, B_KFULL0, B_KFULL1, B_VFULL0, B_VFULL1, B_KEMPTY0, B_KEMPTY1,
-  B_VEMPTY0, B_VEMPTY1, B_SFULL0, B_SFULL1, B_SEMPTY0, B_SEMPTY1, B_PFULL, B_ODONE, B_OFREE, B_COUNT
+  B_VEMPTY0, B_VEMPTY1, B_SFULL0, B_SFULL1, B_SEMPTY0, B_SEMPTY1, B_PFULL, B_ODONE, B_OFREE,
+  B_IFULL0, B_IFULL1, B_IFULL2, B_IFULL3, B_IEMPTY0, B_IEMPTY1, B_IEMPTY2, B_IEMPTY3, B_COUNT
 };
+constexpr int kItemRing = 4;  // work items fetched ahead by the producer
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -97,6 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + B_COUNT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* item_ring = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [kItemRing]
   auto B = [&](int i) { return smem_u32(&bar[i]); };
 
   const int warp = threadIdx.x >> 5;
@@ -116,6 +120,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(B(B_PFULL), 4);
     mbar_init(B(B_ODONE), 1);
     mbar_init(B(B_OFREE), 4);
+    for (int s = 0; s < kItemRing; ++s) {
+      mbar_init(B(B_IFULL0 + s), 1);
+      mbar_init(B(B_IEMPTY0 + s), 5);  // the MMA thread and the four softmax warps
+    }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch(&tq);
@@ -140,9 +148,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       int g = 0;  // global kv tile counter
-      int it = 0;
-      for (int item = blockIdx.x; item < p.n_items; item += gridDim.x, ++it) {
-        const int code = p.items[item];
+      for (int it = 0;; ++it) {
+        // Dynamic schedule: fetch the next item from the global queue and hand it to the
+        // MMA and softmax warps through a small shared-memory ring (-1 ends the loop).
+        const int slot = it % kItemRing;
+        if (!mbar_wait(B(B_IEMPTY0 + slot), ((it / kItemRing) & 1) ^ 1, abort_flag, err, kErrWaitProducer)) break;
+        const int item = atomicAdd(p.work_counter, 1);
+        const int code = item < p.n_items ? p.items[item] : -1;
+        item_ring[slot] = code;
+        mbar_arrive(B(B_IFULL0 + slot));
+        if (code < 0) break;
         const int h = code >> 20, qt = code & 0xFFFFF;
         if (!mbar_wait(B(B_QEMPTY), (it & 1) ^ 1, abort_flag, err, kErrWaitProducer)) break;
         mbar_arrive_expect_tx(B(B_QFULL), L::kQBytes);
@@ -182,8 +197,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int g = 0;
       int it = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++it) {
-        const int qt = p.items[item] & 0xFFFFF;
+      for (; ok; ++it) {
+        const int slot = it % kItemRing;
+        if (!mbar_wait(B(B_IFULL0 + slot), (it / kItemRing) & 1, abort_flag, err, kErrWaitMma)) break;
+        const int code = item_ring[slot];
+        mbar_arrive(B(B_IEMPTY0 + slot));
+        if (code < 0) break;
+        const int qt = code & 0xFFFFF;
         const int n = p.tile_off[qt + 1] - p.tile_off[qt];
         if (!mbar_wait(B(B_QFULL), it & 1, abort_flag, err, kErrWaitMma)) break;
         tc_fence_after();
@@ -245,8 +265,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     int g = 0;
     int it = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++it) {
-      const int code = p.items[item];
+    for (; ok; ++it) {
+      const int slot = it % kItemRing;
+      if (!mbar_wait(B(B_IFULL0 + slot), (it / kItemRing) & 1, abort_flag, err, kErrWaitEpilogue)) break;
+      const int code = item_ring[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(B(B_IEMPTY0 + slot));
+      if (code < 0) break;
       const int h = code >> 20, qt = code & 0xFFFFF;
       const int t0 = p.tile_off[qt], n = p.tile_off[qt + 1] - t0;
       const int qrow = qt * BQ + row_in_tile;
@@ -439,14 +464,16 @@ extern "C" {
 //   frame_lo / frame_hi [F] int32 device arrays: clamped visible key-frame range per frame
 //   items / tile_off / ktile: the block-sparse plan built by the host package
 //   gate_logits [S, ld_gate] fp32 (column gate_col0 + h) and gate_bias [H]: optional
+//   work_counter: one device int, zeroed here on the stream; launches that share it must not overlap
 // Replaces window.py:277-313 (window_softmax_grouped) + hybrid.py:518-528.
 int vdn_window_attention(const void* q, long long ld_q, const void* k, long long ld_k, const void* v, long long ld_v,
                          int S, int H, int D, int video_start, int video_end, int num_frames, int tokens_per_frame,
                          int anchor_rows, int anchor_cols, float scale, const int* frame_lo, const int* frame_hi,
                          const int* items, int n_items, const int* tile_off, const int* ktile, void* out,
                          long long ld_out, const float* gate_logits, long long ld_gate, int gate_col0,
-                         const float* gate_bias, int* dev_err, void* stream) {
-  if (!q || !k || !v || !out || !items || !tile_off || !ktile || !frame_lo || !frame_hi) return vdn::kBadArgument;
+                         const float* gate_bias, int* work_counter, int* dev_err, void* stream) {
+  if (!q || !k || !v || !out || !items || !tile_off || !ktile || !frame_lo || !frame_hi || !work_counter)
+    return vdn::kBadArgument;
   if (D != 64 && D != 128) return vdn::kUnsupported;
   if (S <= 0 || H <= 0 || H >= 2048 || num_frames <= 0 || tokens_per_frame <= 0) return vdn::kBadArgument;
   if (S >= (1 << 22)) return vdn::kUnsupported;
@@ -474,7 +501,9 @@ int vdn_window_attention(const void* q, long long ld_q, const void* k, long long
   p.ld_gate = ld_gate;
   p.gate_col0 = gate_col0;
   p.gate_bias = gate_bias;
+  p.work_counter = work_counter;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaMemsetAsync(work_counter, 0, sizeof(int), s);
   return D == 128 ? vdn::attn::launch<128>(q, ld_q, k, ld_k, v, ld_v, p, dev_err, s)
                   : vdn::attn::launch<64>(q, ld_q, k, ld_k, v, ld_v, p, dev_err, s);
 }

@@ -225,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- TMA producer ----------------
     int stage = 0;
     uint32_t phase = 0;
-    const int ks_blocks = k_split / T::BK;
+    const int ks_blocks = (k_split + T::BK - 1) / T::BK;  // k-blocks read from the first A source
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int m, n;
       tile_coords(t, num_m, num_n, m, n);

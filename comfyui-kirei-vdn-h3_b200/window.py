@@ -196,7 +196,7 @@ def launch_window_attention(q, k, v, out, plan: WindowPlan, heads, dim, scale, s
         d["frame_lo"].data_ptr(), d["frame_hi"].data_ptr(), d["items"].data_ptr(), n_items,
         d["tile_off"].data_ptr(), d["ktile"].data_ptr(), out.data_ptr(), out.stride(0),
         _lib.ptr(gate_logits), gate_logits.stride(0) if gate_logits is not None else 0, int(gate_col0),
-        _lib.ptr(gate_bias), status.err_ptr, _lib.stream_handle(q.device),
+        _lib.ptr(gate_bias), status.counter_ptr, status.err_ptr, _lib.stream_handle(q.device),
     )
 
 

@@ -69,6 +69,8 @@ int vdn_quant_fp8_tensor(int src_kind, const void* x, long long ldx, int rows, i
  * frame_lo/frame_hi [F]: clamped visible key-frame range; items/tile_off/ktile: host plan
  * (window.py in the package).  out [S, ld_out] bf16 at columns h*D.
  * gate_logits [S, ld_gate] fp32 (column gate_col0 + h) + gate_bias [H]: optional.
+ * work_counter: one device int (zeroed on the stream by the call) through which the
+ * persistent CTAs claim work items; calls sharing it must not overlap on the GPU.
  * Replaces: window.py:277-313 (window_softmax_grouped), window.py:327-344 (mask),
  *           window.py:694-861 (flex / FA2 / FA4 backends), hybrid.py:518-528 and
  *           softmax_kernels.py:8-37 (gate and flatten). */
@@ -78,7 +80,7 @@ int vdn_window_attention(const void* q, long long ld_q, const void* k, long long
                          const int* frame_lo, const int* frame_hi, const int* items, int n_items,
                          const int* tile_off, const int* ktile, void* out, long long ld_out,
                          const float* gate_logits, long long ld_gate, int gate_col0, const float* gate_bias,
-                         int* dev_err, void* stream);
+                         int* work_counter, int* dev_err, void* stream);
 
 /* ---------------------------------------------------------------- VDA branch ------ */
 

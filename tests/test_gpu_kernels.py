@@ -32,7 +32,8 @@ def _randn(*shape, seed=0, scale=1.0):
 
 
 # --------------------------------------------------------------------------- GEMM
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (257, 520, 192), (1000, 768, 1024), (3000, 1024, 5120)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (257, 520, 192), (1000, 768, 1024), (3000, 1024, 5120),
+                                   (200, 130, 96), (77, 40, 48)])
 def test_gemm_bf16_matches_fp32(M, N, K):
     a = _randn(M, K, seed=1).to(torch.bfloat16)
     b = _randn(N, K, seed=2, scale=0.05).to(torch.bfloat16)
