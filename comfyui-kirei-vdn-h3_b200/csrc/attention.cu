@@ -477,7 +477,7 @@ int vdn_window_attention(const void* q, long long ld_q, const void* k, long long
   if (D != 64 && D != 128) return vdn::kUnsupported;
   if (S <= 0 || H <= 0 || H >= 2048 || num_frames <= 0 || tokens_per_frame <= 0) return vdn::kBadArgument;
   if (S >= (1 << 22)) return vdn::kUnsupported;
-  if ((ld_out * 2) % 16) return vdn::kMisaligned;
+  if ((ld_out * 2) % 16 || !vdn::aligned16(out)) return vdn::kMisaligned;  // 16-byte output vectors
   vdn::attn::Params p{};
   p.S = S;
   p.H = H;

@@ -573,6 +573,7 @@ int vdn_temporal_act(const void* in, long long ld_in, const float* w, int taps, 
                      int l2norm, void* out, void* stream) {
   if (!in || !out || (taps != 0 && taps != 1 && taps != 3 && taps != 5) || (taps && !w)) return vdn::kBadArgument;
   if (D != 64 && D != 128) return vdn::kUnsupported;
+  if (reinterpret_cast<uintptr_t>(out) & 3) return vdn::kMisaligned;  // paired bf16 stores
   const long long warps = (long long)T * H;
   const int blocks = (int)((warps * 32 + 255) / 256);
   auto s = reinterpret_cast<cudaStream_t>(stream);
@@ -642,6 +643,7 @@ int vdn_delta_factor(const float* A, const float* B, int F, int H, int D, float*
 int vdn_bidir_scan(const float* inv, const float* B, const float* alpha, const float* s0, int F, int H, int D,
                    float* prefix, float* suffix, void* stream) {
   if (!inv || !B || !alpha || !prefix || !suffix) return vdn::kBadArgument;
+  if (!vdn::aligned16(inv)) return vdn::kMisaligned;  // float4 loads of the inverse
   auto s = reinterpret_cast<cudaStream_t>(stream);
   constexpr int RB = 16;
   if (D == 128) {

@@ -40,6 +40,7 @@ struct Epilogue {
   void* out;
   long long ldo;
   int out_kind;
+  int vec_ok;  // 1 when `out` and its row pitch are 16-byte aligned (vector stores allowed)
   int act;  // 0 none, 1 sigmoid
   float alpha;
   const float* row_scale;  // [M]
@@ -122,7 +123,7 @@ __device__ __forceinline__ void store_plain_chunk(const Epilogue& ep, const uint
   if (row >= M) return;
   if (ep.out_kind == kOutS32) {
     int* dst = reinterpret_cast<int*>(ep.out) + (long long)row * ep.ldo + col0;
-    if (col0 + 32 <= N) {
+    if (ep.vec_ok && col0 + 32 <= N) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4)
         *reinterpret_cast<int4*>(dst + j) = make_int4(r[j], r[j + 1], r[j + 2], r[j + 3]);
@@ -149,7 +150,7 @@ __device__ __forceinline__ void store_plain_chunk(const Epilogue& ep, const uint
   }
   if (ep.out_kind == kOutF32) {
     float* dst = reinterpret_cast<float*>(ep.out) + (long long)row * ep.ldo + col0;
-    if (col0 + 32 <= N) {
+    if (ep.vec_ok && col0 + 32 <= N) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4)
         *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -158,7 +159,7 @@ __device__ __forceinline__ void store_plain_chunk(const Epilogue& ep, const uint
     }
   } else {
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ep.out) + (long long)row * ep.ldo + col0;
-    if (col0 + 32 <= N) {
+    if (ep.vec_ok && col0 + 32 <= N) {
 #pragma unroll
       for (int j = 0; j < 32; j += 8) {
         uint4 p;
@@ -446,6 +447,8 @@ static Epilogue plain_epilogue(void* C, long long ldc, int out_kind, float alpha
   ep.col_scale = col_scale;
   ep.col_bias = col_bias;
   ep.addend = reinterpret_cast<const __nv_bfloat16*>(addend);
+  const long long ebytes = out_kind == vdn::gemm::kOutBF16 ? 2 : 4;
+  ep.vec_ok = vdn::aligned16(C) && (ldc * ebytes) % 16 == 0;
   ep.ld_add = ld_add;
   ep.norm_cols = 0;
   ep.aux_col0 = 1 << 30;
@@ -488,6 +491,10 @@ int vdn_qkv_gemm(int kind, const void* x, long long ldx, const void* w, long lon
                  const float* col_scale, void* qkv_out, long long ld_qkv, void* qk_norm, long long ld_norm,
                  float* aux_out, long long ld_aux, int* dev_err, void* stream) {
   if (!x || !w || !qkv_out || !qk_norm || !norm_w) return vdn::kBadArgument;
+  // the QKV epilogue stores 16-byte vectors into all three outputs
+  if (!vdn::aligned16(qkv_out) || !vdn::aligned16(qk_norm) || (ld_qkv * 2) % 16 || (ld_norm * 2) % 16 ||
+      (aux_out && (!vdn::aligned16(aux_out) || (ld_aux * 4) % 16)))
+    return vdn::kMisaligned;
   if (head_dim != 64 && head_dim != 128) return vdn::kUnsupported;
   if ((2 * inner) % vdn::gemm::BN != 0 || (3 * inner) % vdn::gemm::BN != 0) return vdn::kUnsupported;
   if (n_aux > 0 && !aux_out) return vdn::kBadArgument;

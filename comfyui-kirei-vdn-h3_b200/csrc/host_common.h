@@ -52,6 +52,8 @@ inline int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType 
   return r == CUDA_SUCCESS ? kOk : kTensorMapFailed;
 }
 
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 inline int sm_count() {
   static int n[64] = {0};
   int dev = 0;
