@@ -39,6 +39,7 @@ SIGNATURES: dict[str, list] = {
     "vdn_cast_rows": [_P, _L, _I, _I, _I, _P, _L, _P],
     "vdn_quant_int8_rows": [_I, _P, _L, _I, _I, _P, _L, _P, _P],
     "vdn_quant_fp8_tensor": [_I, _P, _L, _I, _I, _P, _L, _P, _P, _P],
+    "vdn_fp8_linear_noalloc": [_P, _L, _I, _I, _P, _L, _I, _P, _P, _L, _P, _P],
 }
 
 _STATUS = {
@@ -47,6 +48,7 @@ _STATUS = {
     -3: (RuntimeError, "TMA tensor-map encoding failed"),
     -4: (RuntimeError, "CUDA launch failed"),
     -5: (ValueError, "pointer or row pitch is not 16-byte aligned"),
+    -6: (ValueError, "problem is larger than the library's fixed device scratch area"),
 }
 
 DEVICE_ERRORS = {

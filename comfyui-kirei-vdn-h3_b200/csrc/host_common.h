@@ -17,6 +17,7 @@ enum : int {
   kTensorMapFailed = -3,  // RuntimeError
   kLaunchFailed = -4,     // RuntimeError (cudaGetLastError after launch)
   kMisaligned = -5,       // ValueError (pointer / stride not 16-byte aligned)
+  kTooLarge = -6,         // ValueError (problem exceeds a fixed-size device scratch area)
 };
 
 inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {

@@ -132,3 +132,85 @@ int vdn_quant_fp8_tensor(int src_kind, const void* x, long long ldx, int rows, i
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// FP8 projection that allocates nothing.
+//
+// Some callers cannot allocate device memory while they run this projection: code that
+// executes inside a memory pool or arena it does not own, embedded hosts that hand the
+// library a fixed device budget at start-up, and callers on paths where an allocation
+// would synchronise or fail (for example while the caching allocator is exhausted).  For
+// them the quantised activations, the amax and the activation scale of the FP8 projection
+// live in one file-scope device array instead of buffers the caller provides.
+//
+// Limits and behaviour:
+//   * the array holds at most kNoAllocMaxElems (16 Mi) quantised activation elements, so
+//     rows * K must not exceed 16,777,216; larger calls return kTooLarge and do nothing;
+//   * every GPU that loads this library keeps the array (about 16 MiB) until the process
+//     exits;
+//   * the first call on a device looks up the array's device address with
+//     cudaGetSymbolAddress (with that device current) and caches it; make that first call
+//     before any stream capture;
+//   * all calls share the array and it keeps the previous call's contents: the amax word is
+//     cleared on the stream at the start of every call, and two calls that overlap on the
+//     GPU (different streams, no ordering between them) race on the array.
+// ---------------------------------------------------------------------------------------
+namespace vdn {
+namespace quant {
+
+constexpr long long kNoAllocMaxElems = 16ll * 1024 * 1024;
+constexpr long long kNoAllocHeader = 256;  // amax at byte 0, scale at byte 128
+static __device__ __align__(256) unsigned char g_fp8_noalloc_scratch[kNoAllocHeader + kNoAllocMaxElems];
+
+static unsigned char* noalloc_scratch_on_current_device() {
+  static unsigned char* addr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_fp8_noalloc_scratch) != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<unsigned char*>(p);
+  }
+  return addr[dev];
+}
+
+}  // namespace quant
+}  // namespace vdn
+
+extern "C" int vdn_gemm(int kind, const void* A, long long lda, const void* A2, long long lda2, long long k_split,
+                        const void* B, long long ldb, void* C, long long ldc, int out_kind, int M, int N, int K,
+                        float alpha, const float* dev_scale0, const float* dev_scale1, const float* row_scale,
+                        const float* col_scale, const float* col_bias, int act, const void* addend,
+                        long long ld_add, int* dev_err, void* stream);
+
+extern "C" {
+
+// out[M, N] (bf16) = x[M, K] (bf16) * W^T with x quantised to e4m3 per tensor inside the
+// library's own scratch array (see the block comment above), W [N, K] e4m3 with its
+// per-tensor scale w_scale (device fp32).  Same result as vdn_quant_fp8_tensor followed by
+// vdn_gemm(kind = 1).  Returns kTooLarge when M * K exceeds 16 Mi elements.
+int vdn_fp8_linear_noalloc(const void* x, long long ldx, int M, int K, const void* w_fp8, long long ldw, int N,
+                           const float* w_scale, void* out, long long ldo, int* dev_err, void* stream) {
+  if (!x || !w_fp8 || !w_scale || !out || M <= 0 || N <= 0 || K <= 0) return vdn::kBadArgument;
+  if ((long long)M * K > vdn::quant::kNoAllocMaxElems) return vdn::kTooLarge;
+  if (K % 16) return vdn::kMisaligned;  // quantised rows are packed at pitch K bytes
+  unsigned char* base = vdn::quant::noalloc_scratch_on_current_device();
+  if (!base) return vdn::kLaunchFailed;
+  float* amax = reinterpret_cast<float*>(base);
+  float* scale = reinterpret_cast<float*>(base + 128);
+  __nv_fp8_e4m3* q = reinterpret_cast<__nv_fp8_e4m3*>(base + vdn::quant::kNoAllocHeader);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(amax, 0, sizeof(float), s) != cudaSuccess) return vdn::kLaunchFailed;
+  const long long n = (long long)M * K;
+  const int blocks = (int)std::min<long long>((n + 255) / 256, 4LL * vdn::sm_count());
+  vdn::quant::amax_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M,
+                                                                 K, amax);
+  vdn::quant::fp8_cast_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+                                                                     M, K, amax, q, K, scale);
+  const int rc = vdn::launch_status();
+  if (rc) return rc;
+  return vdn_gemm(1, q, K, nullptr, 0, 0, w_fp8, ldw, out, ldo, 0, M, N, K, 1.0f, scale, w_scale, nullptr, nullptr,
+                  nullptr, 0, nullptr, 0, dev_err, stream);
+}
+
+}  // extern "C"

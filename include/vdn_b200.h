@@ -62,6 +62,17 @@ int vdn_quant_int8_rows(int src_kind, const void* x, long long ldx, int rows, in
 int vdn_quant_fp8_tensor(int src_kind, const void* x, long long ldx, int rows, int K, void* q, long long ldq,
                          float* work, float* scale_out, void* stream);
 
+/* FP8 projection that allocates nothing (no counterpart in the reference: an addition for
+ * callers that cannot allocate device memory while they run, e.g. code running inside a
+ * memory arena it does not own or a host that hands the library a fixed device budget).
+ * out[M, N] bf16 = x[M, K] bf16 * W^T with x quantised per tensor to e4m3 in the library's
+ * own file-scope device scratch array; W [N, K] e4m3, w_scale one fp32 device scalar.
+ * Limit: M * K <= 16,777,216 (else -6, nothing done); K % 16 == 0.  The array (~16 MiB)
+ * stays resident on every GPU that loads the library; the first call on a device looks up
+ * its address (make it before any stream capture); calls that overlap on the GPU race. */
+int vdn_fp8_linear_noalloc(const void* x, long long ldx, int M, int K, const void* w_fp8, long long ldw, int N,
+                           const float* w_scale, void* out, long long ldo, int* dev_err, void* stream);
+
 /* ---------------------------------------------------------------- window softmax -- */
 
 /* Exact block-sparse window softmax attention with the per-token head gate fused.
