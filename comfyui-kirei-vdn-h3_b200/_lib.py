@@ -33,6 +33,8 @@ SIGNATURES: dict[str, list] = {
     "vdn_temporal_act": [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _P],
     "vdn_alpha_gate": [_P, _L, _I, _I, _I, _P, _P, _P, _I, _I, _P, _P],
     "vdn_frame_stats": [_P, _P, _I, _I, _I, _I, _P, _L, _I, _P, _P, _P],
+    "vdn_frame_stats_tc": [_P, _P, _I, _I, _I, _P, _L, _I, _P, _P, _P, _P],
+    "vdn_readout_tc": [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _L, _L, _P, _P],
     "vdn_delta_factor": [_P, _P, _I, _I, _I, _P, _P, _I, _F, _P, _P],
     "vdn_bidir_scan": [_P, _P, _P, _P, _I, _I, _I, _P, _P, _P],
     "vdn_readout": [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _L, _P, _L, _L, _P],

@@ -161,7 +161,8 @@ class BranchWorkspace:
         self.prefix = torch.empty(Fb, heads, dim, dim, **f32)
         self.suffix = torch.empty(Fb, heads, dim, dim, **f32)
         self.ogd = torch.empty(rows, dim, **bf)
-        self.og = torch.empty(rows, inner, **bf)
+        # the output gate is materialised only on the head_dim-64 path (128 fuses it into the readout)
+        self.og = torch.empty(rows if dim != 128 else 0, inner, **bf)
         self.lohi: dict = {}
 
     def bounds_arrays(self, bounds):
@@ -209,16 +210,24 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
     aux_ld = aux.stride(0)
     call("vdn_alpha_gate", aux.data_ptr() + 4 * ad_col0, aux_ld, Fb, tpf, D, bw.alpha_up.data_ptr(),
          bw.dt_bias.data_ptr(), bw.a_log.data_ptr(), H, D, ws.alpha.data_ptr(), stream)
-    call("vdn_frame_stats", ws.kf.data_ptr(), ws.vf.data_ptr(), Fb, H, tpf, D, aux.data_ptr(), aux_ld, beta_col0,
-         ws.A.data_ptr(), ws.B.data_ptr(), stream)
+    tensor_cores = D == 128  # the tcgen05 statistics/readout kernels are written for head_dim 128
+
+    def stats(kf, vf, F_, T_, beta, A_ptr, B_ptr):
+        if tensor_cores:
+            call("vdn_frame_stats_tc", kf.data_ptr(), vf.data_ptr(), F_, H, T_, beta.data_ptr(), beta.stride(0),
+                 beta_col0, A_ptr, B_ptr, status.err_ptr, stream)
+        else:
+            call("vdn_frame_stats", kf.data_ptr(), vf.data_ptr(), F_, H, T_, D, beta.data_ptr(), beta.stride(0),
+                 beta_col0, A_ptr, B_ptr, stream)
+
+    stats(ws.kf, ws.vf, Fb, tpf, aux, ws.A.data_ptr(), ws.B.data_ptr())
     has_text = text_k is not None
     if has_text:
         L = text_k.shape[0]
         call("vdn_temporal_act", text_k.data_ptr(), text_k.stride(0), None, 0, 1, L, H, D, 1, ws.tk.data_ptr(), stream)
         call("vdn_temporal_act", text_v.data_ptr(), text_v.stride(0), None, 0, 1, L, H, D, 0, ws.tv.data_ptr(), stream)
         mat = D * D * H
-        call("vdn_frame_stats", ws.tk.data_ptr(), ws.tv.data_ptr(), 1, H, L, D, text_aux.data_ptr(),
-             text_aux.stride(0), beta_col0, ws.A.data_ptr() + 4 * Fb * mat, ws.B.data_ptr() + 4 * Fb * mat, stream)
+        stats(ws.tk, ws.tv, 1, L, text_aux, ws.A.data_ptr() + 4 * Fb * mat, ws.B.data_ptr() + 4 * Fb * mat)
         call("vdn_delta_factor", ws.A.data_ptr(), ws.B.data_ptr(), Fb + 1, H, D, ws.inv.data_ptr(),
              ws.info.data_ptr(), Fb, TEXT_STATE_SCALE, ws.s0.data_ptr(), stream)
         s0 = ws.s0
@@ -231,9 +240,16 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
          ws.prefix.data_ptr(), ws.suffix.data_ptr(), stream)
     # output gate: sigmoid(bf16(x W_down^T) W_up^T + b)  (branch.py:754-758)
     call("vdn_cast_rows", aux.data_ptr(), aux_ld, ogd_col0, rows, D, ws.ogd.data_ptr(), ws.ogd.stride(0), stream)
+    lo, hi = ws.bounds_arrays(bounds)
+    if tensor_cores:
+        # gather, Q S^T, the output-gate up-projection and the epilogue in one kernel
+        call("vdn_readout_tc", ws.qf.data_ptr(), Fb, H, tpf, ws.prefix.data_ptr(), ws.suffix.data_ptr(),
+             ws.alpha.data_ptr(), _lib.ptr(s0), lo.data_ptr(), hi.data_ptr(), int(bridge == "alpha"),
+             bw.norm_w.data_ptr(), ws.ogd.data_ptr(), bw.og_up.data_ptr(), bw.og_bias.data_ptr(), out.data_ptr(),
+             out.stride(0), int(out_row0), status.err_ptr, stream)
+        return
     call("vdn_gemm", 0, ws.ogd.data_ptr(), D, None, 0, 0, bw.og_up.data_ptr(), D, ws.og.data_ptr(), inner, 0,
          rows, inner, D, 1.0, None, None, None, None, bw.og_bias.data_ptr(), 1, None, 0, status.err_ptr, stream)
-    lo, hi = ws.bounds_arrays(bounds)
     call("vdn_readout", ws.qf.data_ptr(), Fb, H, tpf, D, ws.prefix.data_ptr(), ws.suffix.data_ptr(),
          ws.alpha.data_ptr(), _lib.ptr(s0), lo.data_ptr(), hi.data_ptr(), int(bridge == "alpha"),
          bw.norm_w.data_ptr(), ws.og.data_ptr(), inner, out.data_ptr(), out.stride(0), int(out_row0), stream)

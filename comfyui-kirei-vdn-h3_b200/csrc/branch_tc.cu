@@ -1,0 +1,408 @@
+// Tensor-core (tcgen05) kernels of the VDA branch for head_dim 128.
+//
+//   vdn_frame_stats_tc   A = (beta K)^T K and B = (beta V)^T K per frame and head
+//                        (branch.py:197-243): both operands MN-major straight from the FHSD
+//                        feature tiles, accumulated over 128-token chunks in TMEM.
+//   vdn_readout_tc       gather + alpha bridge into a bf16 state tile (branch.py:372-396), then
+//                        R = Q S^T and G = bf16(x W_og_down^T) W_og_up^T on the tensor cores
+//                        (branch.py:780, :754-758) and the RMSNorm(D) x sigmoid(G + b) epilogue
+//                        (branch.py:494-530) from TMEM: the output-gate up-projection never
+//                        touches HBM.
+// One warpgroup per CTA (thread = TMEM lane = tile row); thread 0 issues TMA and MMA.
+#include "host_common.h"
+#include "sm100.cuh"
+
+namespace vdn {
+namespace branch_tc {
+
+constexpr int D = 128;
+constexpr int kRows = 128;                 // tokens per chunk / tile
+constexpr int kTile = kRows * D * 2;       // 32 KB bf16 tile (two 64-column swizzle blocks)
+constexpr int kBlk = kRows * 128;          // 16 KB: one 64-column block
+
+__device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + __expf(-x)); }
+
+// ------------------------------------------------------------------------------- statistics
+// smem: K stage x2, V stage x2, beta*K, beta*V (each 32 KB) = 192 KB.
+struct StatsSmem {
+  static constexpr int kK = 0, kV = 2 * kTile, kBK = 4 * kTile, kBV = 5 * kTile, kBar = 6 * kTile;
+  static constexpr int kBytes = kBar + 256 + 1024;
+};
+
+__global__ void __launch_bounds__(128, 1)
+    frame_stats_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, int F, int H,
+                          int T, const float* __restrict__ beta_logits, long long ld_beta, int beta_col0,
+                          float* __restrict__ A, float* __restrict__ Bm, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + StatsSmem::kBar);  // [0,1] kv_full, [2] mma_done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (tid == 0) {
+    mbar_init(smem_u32(&bar[0]), 1);
+    mbar_init(smem_u32(&bar[1]), 1);
+    mbar_init(smem_u32(&bar[2]), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch(&tk);
+    tma_prefetch(&tv);
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sK = smem_u32(smem + StatsSmem::kK), sV = smem_u32(smem + StatsSmem::kV);
+  const uint32_t sBK = smem_u32(smem + StatsSmem::kBK), sBV = smem_u32(smem + StatsSmem::kBV);
+  const int units = F * H;
+  const int nch = (T + kRows - 1) / kRows;
+  constexpr uint32_t idesc = make_idesc(1, 1, 1, 1, 1, 128, 128);  // both operands MN-major
+  auto issue_load = [&](int unit, int c, int gc) {
+    const int st = gc & 1;
+    const int row0 = unit * T + c * kRows;  // FHSD rows: (f * H + h) * T + s
+    const uint32_t fb = smem_u32(&bar[st]);
+    mbar_arrive_expect_tx(fb, 2 * kTile);
+    for (int b = 0; b < 2; ++b) {
+      tma_load_2d(sK + st * kTile + b * kBlk, &tk, fb, b * 64, row0);
+      tma_load_2d(sV + st * kTile + b * kBlk, &tv, fb, b * 64, row0);
+    }
+  };
+  int gc = 0;
+  bool ok = true;
+  if (tid == 0 && blockIdx.x < units) issue_load(blockIdx.x, 0, 0);
+  for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
+    const int f = unit / H, h = unit % H;
+    for (int c = 0; c < nch; ++c, ++gc) {
+      const int st = gc & 1;
+      if (!mbar_wait(smem_u32(&bar[st]), (gc >> 1) & 1, abort_flag, err, kErrWaitOther) ||
+          (gc > 0 && !mbar_wait(smem_u32(&bar[2]), (gc - 1) & 1, abort_flag, err, kErrWaitOther))) {
+        ok = false;
+        break;
+      }
+      if (tid == 0) {  // prefetch the next chunk into the stage the finished MMA released
+        const bool more = c + 1 < nch;
+        const int nu = more ? unit : unit + gridDim.x;
+        if (nu < units) issue_load(nu, more ? c + 1 : 0, gc + 1);
+      }
+      // beta-weighted copies: row s of both tiles scaled by beta_s (0 past the frame end)
+      const int s = c * kRows + tid;
+      const float beta = s < T ? sigm(beta_logits[((long long)f * T + s) * ld_beta + beta_col0 + h]) : 0.f;
+      const __nv_bfloat162 b2 = __floats2bfloat162_rn(beta, beta);
+      for (int b = 0; b < 2; ++b) {
+        const uint32_t off = b * kBlk + tid * 128;
+        const uint4* srck = reinterpret_cast<const uint4*>(smem + StatsSmem::kK + st * kTile + off);
+        const uint4* srcv = reinterpret_cast<const uint4*>(smem + StatsSmem::kV + st * kTile + off);
+        uint4* dk = reinterpret_cast<uint4*>(smem + StatsSmem::kBK + off);
+        uint4* dv = reinterpret_cast<uint4*>(smem + StatsSmem::kBV + off);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint4 k4 = srck[i], v4 = srcv[i];
+          __nv_bfloat162* kp = reinterpret_cast<__nv_bfloat162*>(&k4);
+          __nv_bfloat162* vp = reinterpret_cast<__nv_bfloat162*>(&v4);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            kp[e] = __hmul2(kp[e], b2);
+            vp[e] = __hmul2(vp[e], b2);
+          }
+          dk[i] = k4;
+          dv[i] = v4;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kRows / 16; ++k) {
+          const uint32_t off = k * 2048;  // 16 tokens = two 8-row swizzle groups
+          const uint64_t bdesc = make_sdesc(sK + st * kTile + off, kBlk, 1024);
+          mma_f16(tmem, make_sdesc(sBK + off, kBlk, 1024), bdesc, idesc, (c > 0 || k > 0) ? 1u : 0u);
+          mma_f16(tmem + 128, make_sdesc(sBV + off, kBlk, 1024), bdesc, idesc, (c > 0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&bar[2]));
+      }
+    }
+    if (!ok) break;
+    // epilogue: row i of A and of B from TMEM lane i
+    if (!mbar_wait(smem_u32(&bar[2]), (gc - 1) & 1, abort_flag, err, kErrWaitOther)) break;
+    tc_fence_after();
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const long long ob = ((long long)unit * D + tid) * D;
+    for (int m = 0; m < 2; ++m) {
+      uint32_t r[D];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c)
+        tmem_ld32(tmem + lane_base + m * 128 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
+      tmem_ld_wait();
+      float* dst = (m == 0 ? A : Bm) + ob;
+#pragma unroll
+      for (int c = 0; c < D; c += 4)
+        *reinterpret_cast<float4*>(dst + c) = make_float4(__uint_as_float(r[c]), __uint_as_float(r[c + 1]),
+                                                          __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
+    }
+    tc_fence_before();
+    __syncthreads();  // TMEM is overwritten by the next unit's first MMA
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) abort_drain();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ------------------------------------------------------------------------------- readout
+// smem: state (32 KB, K-major), W_og_up rows of this head (32 KB), Q tile, og-down tile.
+struct ReadoutSmem {
+  static constexpr int kS = 0, kW = kTile, kQ = 2 * kTile, kG = 3 * kTile, kBar = 4 * kTile;
+  static constexpr int kDec = kBar + 256;           // 2 x D floats
+  static constexpr int kBytes = kDec + 2 * D * 4 + 1024;
+};
+
+__global__ void __launch_bounds__(128, 1)
+    readout_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tg,
+                      const __grid_constant__ CUtensorMap tw, int F, int H, int T, const float* __restrict__ prefix,
+                      const float* __restrict__ suffix, const float* __restrict__ alpha, const float* __restrict__ s0,
+                      const int* __restrict__ lo_arr, const int* __restrict__ hi_arr, int use_alpha,
+                      const float* __restrict__ norm_w, const float* __restrict__ og_bias,
+                      __nv_bfloat16* __restrict__ out, long long ld_out, long long out_row0, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + ReadoutSmem::kBar);  // [0] w, [1] tile, [2] mma
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* dec_b = reinterpret_cast<float*>(smem + ReadoutSmem::kDec);
+  float* dec_a = dec_b + D;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (tid == 0) {
+    for (int i = 0; i < 3; ++i) mbar_init(smem_u32(&bar[i]), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch(&tq);
+    tma_prefetch(&tg);
+    tma_prefetch(&tw);
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sS = smem_u32(smem + ReadoutSmem::kS), sW = smem_u32(smem + ReadoutSmem::kW);
+  const uint32_t sQ = smem_u32(smem + ReadoutSmem::kQ), sG = smem_u32(smem + ReadoutSmem::kG);
+  constexpr uint32_t idesc = make_idesc(1, 1, 1, 0, 0, 128, 128);
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const int units = F * H;
+  const int ntile = (T + kRows - 1) / kRows;
+  int nw = 0, nt = 0;  // completed phases of bar[0] and bar[1]/bar[2]
+  bool ok = true;
+  for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
+    const int f = unit / H, h = unit % H;
+    if (tid == 0) {  // output-gate up rows of this head: W_up[h*D + v][j], K-major
+      mbar_arrive_expect_tx(smem_u32(&bar[0]), kTile);
+      for (int b = 0; b < 2; ++b) tma_load_2d(sW + b * kBlk, &tw, smem_u32(&bar[0]), b * 64, h * D);
+    }
+    // alpha-bridge decays (branch.py:385-390)
+    const int raw_lo = lo_arr[f], raw_hi = hi_arr[f];
+    const int lo = max(raw_lo, 0), hi = min(raw_hi, F - 1);
+    const bool has_before = raw_lo - 1 >= 0, has_after = raw_hi + 1 < F;
+    {
+      float lb = 0.f, la = 0.f;
+      if (use_alpha) {
+        for (int j = lo; j <= f; ++j) lb += __logf(fmaxf(alpha[((long long)j * H + h) * D + tid], 1e-12f));
+        for (int j = f; j <= hi; ++j) la += __logf(fmaxf(alpha[((long long)j * H + h) * D + tid], 1e-12f));
+      }
+      dec_b[tid] = __expf(lb);
+      dec_a[tid] = __expf(la);
+    }
+    __syncthreads();
+    const float* pb = has_before ? prefix + ((long long)(lo - 1) * H + h) * D * D : (s0 ? s0 + (long long)h * D * D : nullptr);
+    const float* pa = has_after ? suffix + ((long long)(hi + 1) * H + h) * D * D : (s0 ? s0 + (long long)h * D * D : nullptr);
+    // state[v][k] in bf16 (branch.py:396 casts to the activation dtype), K-major swizzled
+    for (int i = 0; i < 16; ++i) {
+      const int e = tid + 128 * i;
+      const int v = e >> 4, c = e & 15;  // 16 chunks of 8 k per row
+      float val[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) val[u] = 0.f;
+      if (pb) {
+        const float4 a0 = *reinterpret_cast<const float4*>(pb + v * D + c * 8);
+        const float4 a1 = *reinterpret_cast<const float4*>(pb + v * D + c * 8 + 4);
+        const float t[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+        for (int u = 0; u < 8; ++u) val[u] += t[u] * dec_b[c * 8 + u];
+      }
+      if (pa) {
+        const float4 a0 = *reinterpret_cast<const float4*>(pa + v * D + c * 8);
+        const float4 a1 = *reinterpret_cast<const float4*>(pa + v * D + c * 8 + 4);
+        const float t[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+        for (int u = 0; u < 8; ++u) val[u] += t[u] * dec_a[c * 8 + u];
+      }
+      const uint32_t addr = sS + (c >> 3) * kBlk + v * 128 + (((c & 7) ^ (v & 7)) << 4);
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pack_bf16(val[0], val[1])),
+                   "r"(pack_bf16(val[2], val[3])), "r"(pack_bf16(val[4], val[5])), "r"(pack_bf16(val[6], val[7]))
+                   : "memory");
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (!mbar_wait(smem_u32(&bar[0]), nw & 1, abort_flag, err, kErrWaitOther)) break;
+    ++nw;
+    for (int t = 0; t < ntile; ++t, ++nt) {
+      if (tid == 0) {
+        mbar_arrive_expect_tx(smem_u32(&bar[1]), 2 * kTile);
+        for (int b = 0; b < 2; ++b) {
+          tma_load_2d(sQ + b * kBlk, &tq, smem_u32(&bar[1]), b * 64, unit * T + t * kRows);  // FHSD rows
+          tma_load_2d(sG + b * kBlk, &tg, smem_u32(&bar[1]), b * 64, f * T + t * kRows);     // branch rows
+        }
+      }
+      if (!mbar_wait(smem_u32(&bar[1]), nt & 1, abort_flag, err, kErrWaitOther)) {
+        ok = false;
+        break;
+      }
+      if (tid == 0) {
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k >> 2) * kBlk + (k & 3) * 32;
+          mma_f16(tmem, make_sdesc(sQ + off, 16, 1024), make_sdesc(sS + off, 16, 1024), idesc, k > 0 ? 1u : 0u);
+          mma_f16(tmem + 128, make_sdesc(sG + off, 16, 1024), make_sdesc(sW + off, 16, 1024), idesc,
+                  k > 0 ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&bar[2]));
+      }
+      if (!mbar_wait(smem_u32(&bar[2]), nt & 1, abort_flag, err, kErrWaitOther)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // epilogue: R -> bf16 -> RMSNorm x norm_w -> bf16 -> x sigmoid(G + b)
+      uint32_t r[D];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c)
+        tmem_ld32(tmem + lane_base + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
+      tmem_ld_wait();
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < D; ++i) {
+        const float x = bf16_round(__uint_as_float(r[i]));
+        r[i] = __float_as_uint(x);
+        ss += x * x;
+      }
+      const float inv = rsqrtf(ss / (float)D + 1e-6f);
+      const int tok = t * kRows + tid;
+      __nv_bfloat16* dst = out + (out_row0 + (long long)f * T + tok) * ld_out + h * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t gr[32];
+        tmem_ld32(tmem + lane_base + 128 + c * 32, gr);
+        tmem_ld_wait();
+        if (tok < T) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            float o[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int v = c * 32 + i + u;
+              const float nv = bf16_round(__uint_as_float(r[v]) * inv * norm_w[v]);
+              o[u] = nv * sigm(__uint_as_float(gr[i + u]) + og_bias[h * D + v]);
+            }
+            uint4 pk;
+            pk.x = pack_bf16(o[0], o[1]);
+            pk.y = pack_bf16(o[2], o[3]);
+            pk.z = pack_bf16(o[4], o[5]);
+            pk.w = pack_bf16(o[6], o[7]);
+            *reinterpret_cast<uint4*>(dst + c * 32 + i) = pk;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncthreads();  // smem tiles and TMEM are reused by the next tile
+    }
+    __syncthreads();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) abort_drain();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+}  // namespace branch_tc
+}  // namespace vdn
+
+extern "C" {
+
+// Frame statistics on tensor cores (head_dim 128).  K, V: FHSD [F, H, T, 128] bf16;
+// beta logits [F*T, ld_beta] fp32 (column beta_col0 + h); A, B out [F, H, 128, 128] fp32.
+// Replaces branch.py:197-282 (frame_statistics).
+int vdn_frame_stats_tc(const void* K, const void* V, int F, int H, int T, const float* beta_logits, long long ld_beta,
+                       int beta_col0, float* A, float* B, int* dev_err, void* stream) {
+  using namespace vdn::branch_tc;
+  if (!K || !V || !beta_logits || !A || !B || F <= 0 || H <= 0 || T <= 0) return vdn::kBadArgument;
+  if (!vdn::aligned16(A) || !vdn::aligned16(B)) return vdn::kMisaligned;  // float4 row stores
+  CUtensorMap tk, tv;
+  const uint64_t rows = (uint64_t)F * H * T;
+  int rc = vdn::make_tmap_2d(&tk, K, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, rows, D, 64, 128);
+  if (rc) return rc;
+  rc = vdn::make_tmap_2d(&tv, V, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, rows, D, 64, 128);
+  if (rc) return rc;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(frame_stats_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, StatsSmem::kBytes);
+    attr = true;
+  }
+  const int units = F * H;
+  const int grid = units < vdn::sm_count() ? units : vdn::sm_count();
+  frame_stats_tc_kernel<<<grid, 128, StatsSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
+      tk, tv, F, H, T, beta_logits, ld_beta, beta_col0, A, B, dev_err);
+  return vdn::launch_status();
+}
+
+// Readout on tensor cores (head_dim 128): Q FHSD [F, H, T, 128] bf16; og_down [F*T, 128] bf16
+// (bf16-rounded x W_og_down^T of the branch rows); og_up [H*128, 128] bf16 with bias og_bias
+// [H*128] fp32; prefix/suffix [F, H, 128, 128] fp32; alpha [F, H, 128]; s0 [H, 128, 128] or NULL;
+// lo/hi [F] raw window bounds.  Writes out[out_row0 + f*T + s, h*128 + v] (bf16).
+// Replaces branch.py:345-396 (gather), :780 (readout), :494-530 (epilogue), :754-758 (gate).
+int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, const float* suffix, const float* alpha,
+                   const float* s0, const int* lo, const int* hi, int use_alpha, const float* norm_w,
+                   const void* og_down, const void* og_up, const float* og_bias, void* out, long long ld_out,
+                   long long out_row0, int* dev_err, void* stream) {
+  using namespace vdn::branch_tc;
+  if (!Q || !prefix || !suffix || !alpha || !lo || !hi || !norm_w || !og_down || !og_up || !og_bias || !out)
+    return vdn::kBadArgument;
+  if ((ld_out * 2) % 16 || !vdn::aligned16(out) || !vdn::aligned16(prefix) || !vdn::aligned16(suffix) ||
+      (s0 && !vdn::aligned16(s0)))
+    return vdn::kMisaligned;  // 16-byte output vectors, float4 state loads
+  CUtensorMap tq, tg, tw;
+  int rc = vdn::make_tmap_2d(&tq, Q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, (uint64_t)F * H * T, D, 64, 128);
+  if (rc) return rc;
+  rc = vdn::make_tmap_2d(&tg, og_down, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, (uint64_t)F * T, D, 64, 128);
+  if (rc) return rc;
+  rc = vdn::make_tmap_2d(&tw, og_up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, (uint64_t)H * D, D, 64, 128);
+  if (rc) return rc;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(readout_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ReadoutSmem::kBytes);
+    attr = true;
+  }
+  const int units = F * H;
+  const int grid = units < vdn::sm_count() ? units : vdn::sm_count();
+  readout_tc_kernel<<<grid, 128, ReadoutSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
+      tq, tg, tw, F, H, T, prefix, suffix, alpha, s0, lo, hi, use_alpha, norm_w, og_bias,
+      reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0, dev_err);
+  return vdn::launch_status();
+}
+
+}  // extern "C"

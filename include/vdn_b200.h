@@ -116,6 +116,12 @@ int vdn_alpha_gate(const float* down, long long ld_down, int F, int T, int R, co
 int vdn_frame_stats(const void* K, const void* V, int F, int H, int T, int D, const float* beta_logits,
                     long long ld_beta, int beta_col0, float* A, float* B, void* stream);
 
+/* Tensor-core frame statistics for head_dim 128 (same contract as vdn_frame_stats):
+ * A = (beta K)^T K, B = (beta V)^T K as tcgen05 MMAs over 128-token chunks.
+ * Replaces: branch.py:197-282 (frame_statistics). */
+int vdn_frame_stats_tc(const void* K, const void* V, int F, int H, int T, const float* beta_logits,
+                       long long ld_beta, int beta_col0, float* A, float* B, int* dev_err, void* stream);
+
 /* inv = (I + A)^-1 via Cholesky + triangular inverse; info[f, h] = order of the first
  * non-positive leading minor (0 = SPD).  text_frame >= 0: s0 = text_scale * B inv of it.
  * Replaces: branch.py:148-160 (VdnDelta.factor_apply), :62-71 (cholesky_ex info),
@@ -136,6 +142,15 @@ int vdn_readout(const void* Q, int F, int H, int T, int D, const float* prefix, 
                 const float* alpha, const float* s0, const int* lo, const int* hi, int use_alpha,
                 const float* norm_w, const void* gate, long long ld_gate, void* out, long long ld_out,
                 long long out_row0, void* stream);
+
+/* Tensor-core readout for head_dim 128: gather + alpha bridge into a bf16 state, R = Q S^T and
+ * the output-gate up-projection G = og_down og_up^T as tcgen05 MMAs, then RMSNorm(D) x norm_w x
+ * sigmoid(G + og_bias) into out[out_row0 + f*T + s, h*128 + v].  og_down [F*T, 128] bf16,
+ * og_up [H*128, 128] bf16.  Replaces: branch.py:345-396, :494-530, :754-758, :780. */
+int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, const float* suffix,
+                   const float* alpha, const float* s0, const int* lo, const int* hi, int use_alpha,
+                   const float* norm_w, const void* og_down, const void* og_up, const float* og_bias,
+                   void* out, long long ld_out, long long out_row0, int* dev_err, void* stream);
 
 /* fp32 column block -> bf16 (output-gate bottleneck rounding, branch.py:755). */
 int vdn_cast_rows(const float* in, long long ld_in, int col0, int rows, int cols, void* out, long long ld_out,

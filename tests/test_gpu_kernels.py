@@ -229,6 +229,14 @@ def test_statistics_factor_scan_match_oracle_and_report_non_spd():
     wa, wb = vo.frame_statistics(kf.float(), vf.float(), beta)
     torch.cuda.synchronize()
     assert rel_l2(A, wa) < 1e-5 and rel_l2(B, wb) < 1e-5
+    # the tensor-core statistics (bf16 products of beta-weighted features) agree too
+    A_tc, B_tc = torch.empty_like(A), torch.empty_like(A)
+    st = pkg._lib.DeviceStatus(DEV)
+    pkg._lib.call("vdn_frame_stats_tc", kd.data_ptr(), vd.data_ptr(), Fb, H, T, ld.data_ptr(), 8, 2,
+                  A_tc.data_ptr(), B_tc.data_ptr(), st.err_ptr, s)
+    torch.cuda.synchronize()
+    st.raise_if_failed()
+    assert rel_l2(A_tc, wa) < 5e-3 and rel_l2(B_tc, wb) < 5e-3
     inv = torch.empty_like(A)
     info = torch.zeros(Fb, H, device=DEV, dtype=torch.int32)
     pkg._lib.call("vdn_delta_factor", A.data_ptr(), B.data_ptr(), Fb, H, D, inv.data_ptr(), info.data_ptr(), -1, 0.0,
@@ -260,9 +268,10 @@ def test_statistics_factor_scan_match_oracle_and_report_non_spd():
     assert int(info[2, 1]) == 1
 
 
-def test_branch_readout_matches_oracle_with_and_without_text():
-    H, D, hidden = 2, 64, 96
-    F, grid = 8, (4, 5)
+@pytest.mark.parametrize("D,grid", [(64, (4, 5)), (128, (10, 15))])
+def test_branch_readout_matches_oracle_with_and_without_text(D, grid):
+    H, hidden = 2, 96
+    F = 8
     tpf = grid[0] * grid[1]
     rows = F * tpf
     g = torch.Generator().manual_seed(60)
