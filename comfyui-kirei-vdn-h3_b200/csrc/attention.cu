@@ -8,45 +8,53 @@
 // flattened [S, H*D] layout the out-projection reads (softmax_kernels.py:8-9).
 //
 // B200 design:
-//   * persistent CTAs walk a cost-sorted list of (head, 128-row query tile) items;
-//   * the host plan gives each query tile the merged key intervals its rows can see, cut
-//     into 128-key tiles at arbitrary row offsets (TMA rows have no alignment rule); only
-//     tiles where some row of the query tile is excluded carry a mask flag, and for those
-//     the mask is rebuilt per element from the frame index (never materialised);
-//   * warp 4 streams K and V tiles with TMA into a 2-stage ring; warp 5 issues
-//     S = Q K^T (M=128, N=128) into one of two TMEM buffers and O += P V (V MN-major);
-//   * warps 0..3 own one query row per thread: they read S from TMEM, run the online
-//     softmax in registers (exp2 in log2 units), rescale O in TMEM, write P as bf16 into
-//     a 128-byte-swizzled shared-memory tile and finally apply 1/l and the gate.
+//   * persistent CTAs claim (head, 256-row query tile) items from a global queue; the host
+//     plan gives each query tile the merged key intervals its rows can see, cut into 128-key
+//     tiles at arbitrary row offsets (TMA rows have no alignment rule); only tiles where some
+//     row cannot see every key carry a mask flag, and the mask is then rebuilt per element
+//     from the frame index (never materialised);
+//   * the 256 query rows are two 128-row tiles (a = 0, 1) that share every K/V tile: warp 8
+//     streams Q and a 2-stage K/V ring with TMA, warp 9 issues all tcgen05 MMAs, and two
+//     softmax warpgroups (warps 0-3 for a = 0, 4-7 for a = 1) ping-pong against it;
+//   * TMEM (512 columns): S_a in columns [128a, 128a+128), O_a in [256+128a, 384+128a).  The
+//     softmax writes P_a as packed bf16 over the first 64 columns of S_a and the PV MMA reads
+//     it straight from TMEM (A operand in tensor memory), so shared memory holds only Q and
+//     the K/V ring.  The next S_a is issued after PV_a, so the in-order tensor pipe never
+//     overwrites P before it is consumed, and S_a's completion implies PV_a's;
+//   * online softmax in registers with exp2 in log2 units; the reference maximum moves only
+//     when a tile exceeds it by more than 2^8, so O is rescaled rarely (the result is exact);
+//     a quarter of the exponentials run as a polynomial on the FMA pipe;
+//   * the epilogue applies 1/l and the gate and writes bf16 rows.
 #include "host_common.h"
 #include "sm100.cuh"
 
 namespace vdn {
 namespace attn {
 
-constexpr int kThreads = 192;
-constexpr int BQ = 128;
+constexpr int kThreads = 320;  // 8 softmax warps, 1 TMA warp, 1 MMA warp
+constexpr int BQ = 128;        // rows per query tile (two per work item)
 constexpr int BKV = 128;
 constexpr int kStages = 2;
+constexpr int kItemRing = 4;
 
 struct Params {
   int S, H, D;
   int vs, ve, F, tpf;
   int anchor_rows, anchor_cols;
   float scale_log2;
-  const int* frame_lo;              // [F] first visible key frame (clamped)
-  const int* frame_hi;              // [F] last visible key frame (clamped)
-  const int* items;                 // [n_items] (head << 20) | q_tile
+  const int* frame_lo;   // [F] first visible key frame (clamped)
+  const int* frame_hi;   // [F] last visible key frame (clamped)
+  const int* items;      // [n_items] (head << 20) | query tile (256 rows)
   int n_items;
-  const int* tile_off;              // [n_qtiles + 1]
-  const int* ktile;                 // [n_ktiles] (k0 << 9) | (masked << 8) | (valid - 1)
+  const int* tile_off;   // [n_qtiles + 1]
+  const int* ktile;      // [n_ktiles] (k0 << 9) | (masked << 8) | (valid - 1)
   __nv_bfloat16* out;
   long long ld_out;
-  const float* gate_logits;         // [S, ld_gate] fp32 or null
+  const float* gate_logits;  // [S, ld_gate] fp32 or null
   long long ld_gate;
   int gate_col0;
-  const float* gate_bias;           // [H] or null
-  int* work_counter;                // zeroed before the launch; items are claimed with atomicAdd
+  const float* gate_bias;    // [H] or null
+  int* work_counter;         // zeroed before the launch; items are claimed with atomicAdd
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -68,27 +76,34 @@ __device__ __forceinline__ float exp2_poly(float x) {
   return x < -125.0f ? 0.0f : y;
 }
 
+// O += P V with P (A operand) in tensor memory.
+__device__ __forceinline__ void mma_f16_tmem_a(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 template <int D>
 struct Layout {
-  static constexpr int kQBytes = BQ * D * 2;
+  static constexpr int kQTile = BQ * D * 2;
   static constexpr int kKBytes = BKV * D * 2;
   static constexpr int kVBytes = BKV * D * 2;
-  static constexpr int kPBytes = BQ * BKV * 2;
   static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + kQBytes;
+  static constexpr int kOffK = kOffQ + 2 * kQTile;
   static constexpr int kOffV = kOffK + kStages * kKBytes;
-  static constexpr int kOffP = kOffV + kStages * kVBytes;
-  static constexpr int kOffBar = kOffP + kPBytes;
-  static constexpr int kSmem = kOffBar + 256 + 1024;
+  static constexpr int kOffBar = kOffV + kStages * kVBytes;
+  static constexpr int kSmem = kOffBar + 512 + 1024;
 };
 
-// Barrier slots.
 enum {
-  B_QFULL = 0, B_QEMPTY, B_KFULL0, B_KFULL1, B_VFULL0, B_VFULL1, B_KEMPTY0, B_KEMPTY1,
-  B_VEMPTY0, B_VEMPTY1, B_SFULL0, B_SFULL1, B_SEMPTY0, B_SEMPTY1, B_PFULL, B_ODONE, B_OFREE,
+  B_QFULL = 0, B_QEMPTY, B_KFULL0, B_KFULL1, B_VFULL0, B_VFULL1, B_KEMPTY0, B_KEMPTY1, B_VEMPTY0, B_VEMPTY1,
+  B_SFULL0, B_SFULL1, B_PFULL0, B_PFULL1, B_ODONE0, B_ODONE1, B_OFREE0, B_OFREE1,
   B_IFULL0, B_IFULL1, B_IFULL2, B_IFULL3, B_IEMPTY0, B_IEMPTY1, B_IEMPTY2, B_IEMPTY3, B_COUNT
 };
-constexpr int kItemRing = 4;  // work items fetched ahead by the producer
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -115,14 +130,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(B(B_KEMPTY0 + s), 1);
       mbar_init(B(B_VEMPTY0 + s), 1);
       mbar_init(B(B_SFULL0 + s), 1);
-      mbar_init(B(B_SEMPTY0 + s), 4);
+      mbar_init(B(B_PFULL0 + s), 4);
+      mbar_init(B(B_ODONE0 + s), 1);
+      mbar_init(B(B_OFREE0 + s), 4);
     }
-    mbar_init(B(B_PFULL), 4);
-    mbar_init(B(B_ODONE), 1);
-    mbar_init(B(B_OFREE), 4);
     for (int s = 0; s < kItemRing; ++s) {
       mbar_init(B(B_IFULL0 + s), 1);
-      mbar_init(B(B_IEMPTY0 + s), 5);  // the MMA thread and the four softmax warps
+      mbar_init(B(B_IEMPTY0 + s), 9);  // the MMA thread and the eight softmax warps
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -130,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch(&tk);
     tma_prefetch(&tv);
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -141,10 +155,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sQ = smem_u32(smem + L::kOffQ);
   const uint32_t sK = smem_u32(smem + L::kOffK);
   const uint32_t sV = smem_u32(smem + L::kOffV);
-  const uint32_t sP = smem_u32(smem + L::kOffP);
   constexpr int kDBlocks = D / 64;  // 64-element (128 B) column blocks per row
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       int g = 0;  // global kv tile counter
@@ -160,9 +173,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (code < 0) break;
         const int h = code >> 20, qt = code & 0xFFFFF;
         if (!mbar_wait(B(B_QEMPTY), (it & 1) ^ 1, abort_flag, err, kErrWaitProducer)) break;
-        mbar_arrive_expect_tx(B(B_QFULL), L::kQBytes);
-        for (int b = 0; b < kDBlocks; ++b)
-          tma_load_2d(sQ + b * (BQ * 128), &tq, B(B_QFULL), h * D + b * 64, qt * BQ);
+        mbar_arrive_expect_tx(B(B_QFULL), 2 * L::kQTile);
+        for (int a = 0; a < 2; ++a)
+          for (int b = 0; b < kDBlocks; ++b)
+            tma_load_2d(sQ + a * L::kQTile + b * (BQ * 128), &tq, B(B_QFULL), h * D + b * 64, qt * 2 * BQ + a * BQ);
         const int t0 = p.tile_off[qt], t1 = p.tile_off[qt + 1];
         bool ok = true;
         for (int t = t0; t < t1; ++t, ++g) {
@@ -188,12 +202,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc_s = make_idesc(1, 1, 1, 0, 0, BQ, BKV);
       constexpr uint32_t idesc_o = make_idesc(1, 1, 1, 0, 1, BQ, D);
-      const uint32_t o_tmem = tmem_base + 256;
+      auto issue_s = [&](int a, uint32_t kb) {
+#pragma unroll
+        for (int s = 0; s < D / 16; ++s) {
+          const uint32_t off = (s >> 2) * (BQ * 128) + (s & 3) * 32;
+          mma_f16(tmem_base + a * 128, make_sdesc(sQ + a * L::kQTile + off, 16, 1024), make_sdesc(kb + off, 16, 1024),
+                  idesc_s, s > 0 ? 1u : 0u);
+        }
+        tc_commit(B(B_SFULL0 + a));
+      };
       int g = 0;
       int it = 0;
       bool ok = true;
@@ -205,63 +227,59 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (code < 0) break;
         const int qt = code & 0xFFFFF;
         const int n = p.tile_off[qt + 1] - p.tile_off[qt];
-        if (!mbar_wait(B(B_QFULL), it & 1, abort_flag, err, kErrWaitMma)) break;
+        if (!mbar_wait(B(B_QFULL), it & 1, abort_flag, err, kErrWaitMma) ||
+            !mbar_wait(B(B_KFULL0 + (g & 1)), (g >> 1) & 1, abort_flag, err, kErrWaitMma)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const int g0 = g;
-        for (int j = 0; j <= n && ok; ++j) {
-          if (j < n) {
-            // S_j = Q K_j^T into S buffer (g0 + j) & 1
-            const int gj = g0 + j, st = gj & 1;
-            const uint32_t ph = (gj >> 1) & 1;
-            if (!mbar_wait(B(B_KFULL0 + st), ph, abort_flag, err, kErrWaitMma) ||
-                !mbar_wait(B(B_SEMPTY0 + st), ph ^ 1, abort_flag, err, kErrWaitMma)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t kb = sK + st * L::kKBytes;
-#pragma unroll
-            for (int s = 0; s < D / 16; ++s) {
-              const uint32_t off = (s >> 2) * (BQ * 128) + (s & 3) * 32;
-              mma_f16(tmem_base + st * 128, make_sdesc(sQ + off, 16, 1024), make_sdesc(kb + off, 16, 1024),
-                      idesc_s, s > 0 ? 1u : 0u);
-            }
-            tc_commit(B(B_SFULL0 + st));
-            tc_commit(B(B_KEMPTY0 + st));
-            if (j == n - 1) tc_commit(B(B_QEMPTY));
-          }
-          if (j > 0) {
-            // O += P_{j-1} V_{j-1}
-            const int gj = g0 + j - 1, st = gj & 1;
-            const uint32_t ph = (gj >> 1) & 1;
-            if (!mbar_wait(B(B_PFULL), gj & 1, abort_flag, err, kErrWaitMma) ||
-                !mbar_wait(B(B_VFULL0 + st), ph, abort_flag, err, kErrWaitMma)) {
-              ok = false;
-              break;
-            }
-            if (j == 1 && !mbar_wait(B(B_OFREE), (it & 1) ^ 1, abort_flag, err, kErrWaitMma)) {
+        issue_s(0, sK + (g & 1) * L::kKBytes);
+        issue_s(1, sK + (g & 1) * L::kKBytes);
+        tc_commit(B(B_KEMPTY0 + (g & 1)));
+        if (n == 1) tc_commit(B(B_QEMPTY));
+        for (int j = 0; j < n && ok; ++j) {
+          const int gj = g + j, st = gj & 1;
+          const uint32_t ph = (gj >> 1) & 1;
+          for (int a = 0; a < 2; ++a) {
+            if (!mbar_wait(B(B_PFULL0 + a), gj & 1, abort_flag, err, kErrWaitMma) ||
+                (j == 0 && !mbar_wait(B(B_OFREE0 + a), (it & 1) ^ 1, abort_flag, err, kErrWaitMma)) ||
+                (a == 0 && !mbar_wait(B(B_VFULL0 + st), ph, abort_flag, err, kErrWaitMma))) {
               ok = false;
               break;
             }
             tc_fence_after();
             const uint32_t vb = sV + st * L::kVBytes;
 #pragma unroll
-            for (int s = 0; s < BKV / 16; ++s) {
-              const uint32_t aoff = (s >> 2) * (BQ * 128) + (s & 3) * 32;
-              mma_f16(o_tmem, make_sdesc(sP + aoff, 16, 1024), make_sdesc(vb + s * 2048, BKV * 128, 1024),
-                      idesc_o, (j > 1 || s > 0) ? 1u : 0u);
+            for (int s = 0; s < BKV / 16; ++s)
+              mma_f16_tmem_a(tmem_base + 256 + a * 128, tmem_base + a * 128 + s * 8,
+                             make_sdesc(vb + s * 2048, BKV * 128, 1024), idesc_o, (j > 0 || s > 0) ? 1u : 0u);
+            if (a == 1) tc_commit(B(B_VEMPTY0 + st));
+            if (j == n - 1) tc_commit(B(B_ODONE0 + a));
+            if (j + 1 < n) {
+              const int g1 = gj + 1, st1 = g1 & 1;
+              if (a == 0 && !mbar_wait(B(B_KFULL0 + st1), (g1 >> 1) & 1, abort_flag, err, kErrWaitMma)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_s(a, sK + st1 * L::kKBytes);
+              if (a == 1) {
+                tc_commit(B(B_KEMPTY0 + st1));
+                if (j + 1 == n - 1) tc_commit(B(B_QEMPTY));
+              }
             }
-            tc_commit(B(B_ODONE));
-            tc_commit(B(B_VEMPTY0 + st));
           }
         }
-        g = g0 + n;
+        g += n;
       }
     }
   } else {
-    // ---------------- softmax / correction / epilogue (warps 0..3) ----------------
-    const int row_in_tile = warp * 32 + lane;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    // ---------------- softmax / correction / epilogue: warpgroup a = warp / 4 ----------------
+    const int a = warp >> 2;
+    const int row_in_tile = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t s_tmem = tmem_base + lane_base + a * 128;
+    const uint32_t o_tmem = tmem_base + lane_base + 256 + a * 128;
     int g = 0;
     int it = 0;
     bool ok = true;
@@ -274,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (code < 0) break;
       const int h = code >> 20, qt = code & 0xFFFFF;
       const int t0 = p.tile_off[qt], n = p.tile_off[qt + 1] - t0;
-      const int qrow = qt * BQ + row_in_tile;
+      const int qrow = qt * 2 * BQ + a * BQ + row_in_tile;
       // Per-row visibility (window.py:327-344).
       bool dense = (qrow < p.vs) || (qrow >= p.ve);
       int wlo = 0, whi = 0;
@@ -284,14 +302,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         wlo = p.vs + p.frame_lo[f] * p.tpf;
         whi = p.vs + (p.frame_hi[f] + 1) * p.tpf;
       }
-      const int acol_lo = p.anchor_cols ? p.vs + p.tpf : p.vs;   // keys < acol_lo are anchor frame 0
-      const int acol_hi = p.anchor_cols ? p.ve - p.tpf : p.ve;   // keys >= acol_hi are anchor frame F-1
+      const int acol_lo = p.anchor_cols ? p.vs + p.tpf : p.vs;  // keys < acol_lo are anchor frame 0
+      const int acol_hi = p.anchor_cols ? p.ve - p.tpf : p.ve;  // keys >= acol_hi are anchor frame F-1
       float m_run = -INFINITY, l_run = 0.f;
-      const int g0 = g;
       for (int j = 0; j < n; ++j) {
-        const int gj = g0 + j, st = gj & 1;
-        const uint32_t ph = (gj >> 1) & 1;
-        if (!mbar_wait(B(B_SFULL0 + st), ph, abort_flag, err, kErrWaitEpilogue)) {
+        const int gj = g + j;
+        if (!mbar_wait(B(B_SFULL0 + a), gj & 1, abort_flag, err, kErrWaitEpilogue)) {
           ok = false;
           break;
         }
@@ -299,11 +315,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t sr[BKV];  // raw scores of this row (fp32 bits)
 #pragma unroll
         for (int c = 0; c < BKV / 32; ++c)
-          tmem_ld32(tmem_base + lane_base + st * 128 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
+          tmem_ld32(s_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
         tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(B(B_SEMPTY0 + st));
         const int info = p.ktile[t0 + j];
         const int k0 = info >> 9;
         const int valid = (info & 0xFF) + 1;
@@ -325,69 +338,54 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < BKV; ++c) mt = fmaxf(mt, __uint_as_float(sr[c]));
         }
-        // The reference max only moves when the tile max exceeds it by more than 2^8 (in
-        // log2 units), so exponents stay <= 8 and O is rescaled rarely; the result is exact.
+        // The reference max only moves when the tile max exceeds it by more than 2^8 (in log2
+        // units), so exponents stay <= 8 and O is rescaled rarely; the result is exact.
         const float mts = mt * p.scale_log2;
         const bool grow = mts > m_run + 8.0f;
         const float m_new = grow ? mts : m_run;
         const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
         const float corr = grow ? ex2(m_run - m_use) : 1.0f;  // m_run = -inf gives 0
         float rs = 0.f;
-        uint32_t pk[BKV / 2];
 #pragma unroll
-        for (int c = 0; c < BKV; c += 2) {
-          const float xa = fmaf(__uint_as_float(sr[c]), p.scale_log2, -m_use);
-          const float xb = fmaf(__uint_as_float(sr[c + 1]), p.scale_log2, -m_use);
-          // a quarter of the exponentials run on the FMA pipe to relieve the MUFU unit
-          const float a = ex2(xa);
-          const float b = ((c & 3) == 2) ? exp2_poly(xb) : ex2(xb);
-          rs += a + b;
-          pk[c / 2] = pack_bf16(a, b);
-        }
-        l_run = l_run * corr + rs;
-        m_run = m_new;
-        if (j > 0) {
-          // The previous PV must be done before O is rescaled and P is overwritten.
-          if (!mbar_wait(B(B_ODONE), (gj - 1) & 1, abort_flag, err, kErrWaitEpilogue)) {
-            ok = false;
-            break;
+        for (int c0 = 0; c0 < BKV; c0 += 64) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int c = 0; c < 64; c += 2) {
+            const float xa = fmaf(__uint_as_float(sr[c0 + c]), p.scale_log2, -m_use);
+            const float xb = fmaf(__uint_as_float(sr[c0 + c + 1]), p.scale_log2, -m_use);
+            // a quarter of the exponentials run on the FMA pipe to relieve the MUFU unit
+            const float ea = ex2(xa);
+            const float eb = ((c & 3) == 2) ? exp2_poly(xb) : ex2(xb);
+            rs += ea + eb;
+            pk[c / 2] = pack_bf16(ea, eb);
           }
-          tc_fence_after();
-          if (__any_sync(0xffffffffu, grow)) {
-            uint32_t o[D];
+          // P over the first 64 columns of S_a: key 2c in the low half of column c
+          tmem_st32(s_tmem + c0 / 2, pk);
+        }
+        // O_a is stable here: S_j(a) completed, so PV_{j-1}(a) (issued before it) did too; and
+        // PV_j(a) is not issued before this warpgroup signals P_j(a) below.
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c)
-              tmem_ld32(tmem_base + lane_base + 256 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(o + c * 32));
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(o_tmem + c * 32, o);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < D; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
-#pragma unroll
-            for (int c = 0; c < D / 32; ++c)
-              tmem_st32(tmem_base + lane_base + 256 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(o + c * 32));
-            tmem_st_wait();
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+            tmem_st32(o_tmem + c * 32, o);
           }
         }
-        // P (bf16) -> shared memory, K-major 128-byte swizzle: 2 blocks of 64 keys.
-        {
-          const uint32_t rbase = sP + row_in_tile * 128;
-          const uint32_t sw = row_in_tile & 7;
-#pragma unroll
-          for (int c = 0; c < BKV / 8; ++c) {
-            const uint32_t addr = rbase + (c >> 3) * (BQ * 128) + (((c & 7) ^ sw) << 4);
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[c * 4]),
-                         "r"(pk[c * 4 + 1]), "r"(pk[c * 4 + 2]), "r"(pk[c * 4 + 3])
-                         : "memory");
-          }
-        }
-        fence_proxy_async_smem();
+        tmem_st_wait();
+        l_run = l_run * corr + rs;
+        m_run = m_new;
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(B(B_PFULL));
+        if (lane == 0) mbar_arrive(B(B_PFULL0 + a));
       }
       if (!ok) break;
-      g = g0 + n;
-      // Epilogue: wait for the last PV, normalise, gate, store.
-      if (!mbar_wait(B(B_ODONE), (g - 1) & 1, abort_flag, err, kErrWaitEpilogue)) break;
+      g += n;
+      // Epilogue: wait for the last PV of this tile, normalise, gate, store.
+      if (!mbar_wait(B(B_ODONE0 + a), it & 1, abort_flag, err, kErrWaitEpilogue)) break;
       tc_fence_after();
       float gate = 1.f;
       if (p.gate_logits && qrow < p.S) {
@@ -397,33 +395,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float inv_l = (l_run > 0.f) ? gate / l_run : 0.f;
       __nv_bfloat16* dst = p.out + (long long)qrow * p.ld_out + h * D;
-      uint32_t r[32];
+      uint32_t r[D];
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        tmem_ld32(tmem_base + lane_base + 256 + c * 32, r);
-        tmem_ld_wait();
-        if (qrow < p.S) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 v;
-            v.x = pack_bf16(__uint_as_float(r[i]) * inv_l, __uint_as_float(r[i + 1]) * inv_l);
-            v.y = pack_bf16(__uint_as_float(r[i + 2]) * inv_l, __uint_as_float(r[i + 3]) * inv_l);
-            v.z = pack_bf16(__uint_as_float(r[i + 4]) * inv_l, __uint_as_float(r[i + 5]) * inv_l);
-            v.w = pack_bf16(__uint_as_float(r[i + 6]) * inv_l, __uint_as_float(r[i + 7]) * inv_l);
-            *reinterpret_cast<uint4*>(dst + c * 32 + i) = v;
-          }
-        }
-      }
+      for (int c = 0; c < D / 32; ++c) tmem_ld32(o_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(B(B_OFREE));
+      if (lane == 0) mbar_arrive(B(B_OFREE0 + a));
+      if (qrow < p.S) {
+#pragma unroll
+        for (int i = 0; i < D; i += 8) {
+          uint4 v;
+          v.x = pack_bf16(__uint_as_float(r[i]) * inv_l, __uint_as_float(r[i + 1]) * inv_l);
+          v.y = pack_bf16(__uint_as_float(r[i + 2]) * inv_l, __uint_as_float(r[i + 3]) * inv_l);
+          v.z = pack_bf16(__uint_as_float(r[i + 4]) * inv_l, __uint_as_float(r[i + 5]) * inv_l);
+          v.w = pack_bf16(__uint_as_float(r[i + 6]) * inv_l, __uint_as_float(r[i + 7]) * inv_l);
+          *reinterpret_cast<uint4*>(dst + i) = v;
+        }
+      }
     }
   }
 
   tc_fence_before();
   __syncthreads();
   if (*abort_flag) abort_drain();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }
@@ -462,7 +458,8 @@ extern "C" {
 //            q and k already RMS-normalised (hybrid.py:271-273)
 //   out      [S, ld_out] bf16: gated output at columns h*D
 //   frame_lo / frame_hi [F] int32 device arrays: clamped visible key-frame range per frame
-//   items / tile_off / ktile: the block-sparse plan built by the host package
+//   items / tile_off / ktile: the block-sparse plan built by the host package (256-row
+//            query tiles)
 //   gate_logits [S, ld_gate] fp32 (column gate_col0 + h) and gate_bias [H]: optional
 //   work_counter: one device int, zeroed here on the stream; launches that share it must not overlap
 // Replaces window.py:277-313 (window_softmax_grouped) + hybrid.py:518-528.

@@ -5,7 +5,7 @@
 tcgen05 kernel over a host-built plan instead of per-group K/V gathers and SDPA calls.
 
 Plan (built once per geometry, cached like the reference's ``_DecomposedPlan``,
-window.py:726-797): query rows are cut into 128-row tiles; for each tile the key rows
+window.py:726-797): query rows are cut into 256-row tiles; for each tile the key rows
 visible to any of its rows are merged into intervals and cut into 128-key tiles that
 may start at any row.  A key tile carries a mask flag only when some row of the query
 tile cannot see all of its keys; the kernel then rebuilds that row's visibility from
@@ -24,7 +24,7 @@ import torch
 from . import _lib
 from .layout import ANCHOR_FRAME_MODES, validate_layout
 
-BQ = 128
+BQ = 256  # query rows per work item: two 128-row tiles that share every key tile
 BKV = 128
 ATTENTION_BACKENDS = ("auto", "grouped", "flex", "flash2", "decomposed", "reference", "compat", "b200")
 

@@ -24,7 +24,7 @@ def _expand_plan(plan, S):
     vs, ve, F, tpf = plan.video_start, plan.video_end, plan.num_frames, plan.tokens_per_frame
     allowed = np.zeros((S, S), dtype=bool)
     for qt in range(plan.n_qtiles):
-        rows = np.arange(qt * 128, min(S, qt * 128 + 128))
+        rows = np.arange(qt * bw.BQ, min(S, qt * bw.BQ + bw.BQ))
         dense = (rows < vs) | (rows >= ve)
         f = np.clip((rows - vs) // tpf, 0, F - 1)
         if plan.anchor_rows:
@@ -107,7 +107,7 @@ def test_plan_at_config1_is_block_sparse():
     visited = int(plan.tiles_per_q.sum())
     pairs = vo.attention_pairs(lay)
     # visited key tiles carry at most ~12 % more work than the allowed pairs, and far less than dense
-    assert visited * 128 * 128 < 1.12 * pairs
+    assert visited * bw.BQ * bw.BKV < 1.08 * pairs
     assert visited < 0.6 * dense_tiles
     assert plan.masked_tiles < 0.25 * visited
 
