@@ -76,6 +76,31 @@ __device__ __forceinline__ float exp2_poly(float x) {
   return x < -125.0f ? 0.0f : y;
 }
 
+// Paired fp32 arithmetic (one instruction for two lanes of work on sm_100).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // O += P V with P (A operand) in tensor memory.
 __device__ __forceinline__ void mma_f16_tmem_a(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
                                                uint32_t accumulate) {
@@ -105,8 +130,9 @@ enum {
   B_IFULL0, B_IFULL1, B_IFULL2, B_IFULL3, B_IEMPTY0, B_IEMPTY1, B_IEMPTY2, B_IEMPTY3, B_COUNT
 };
 
+// 320 threads, one CTA per SM: up to 200 registers per thread keep the softmax spill-free.
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __maxnreg__(200)
     window_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                             const __grid_constant__ CUtensorMap tv, Params p, int* err) {
   using L = Layout<D>;
@@ -305,8 +331,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int acol_lo = p.anchor_cols ? p.vs + p.tpf : p.vs;  // keys < acol_lo are anchor frame 0
       const int acol_hi = p.anchor_cols ? p.ve - p.tpf : p.ve;  // keys >= acol_hi are anchor frame F-1
       float m_run = -INFINITY, l_run = 0.f;
+      int info_next = p.ktile[t0];
       for (int j = 0; j < n; ++j) {
         const int gj = g + j;
+        const int info = info_next;
+        if (j + 1 < n) info_next = p.ktile[t0 + j + 1];  // prefetch the next tile descriptor
         if (!mbar_wait(B(B_SFULL0 + a), gj & 1, abort_flag, err, kErrWaitEpilogue)) {
           ok = false;
           break;
@@ -317,11 +346,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < BKV / 32; ++c)
           tmem_ld32(s_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
         tmem_ld_wait();
-        const int info = p.ktile[t0 + j];
         const int k0 = info >> 9;
         const int valid = (info & 0xFF) + 1;
         const bool masked = (info >> 8) & 1;
-        float mt = -INFINITY;  // tile max of the raw scores
         if (masked || valid < BKV) {
 #pragma unroll
           for (int c = 0; c < BKV; ++c) {
@@ -332,12 +359,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                       key >= acol_hi;
             }
             if (!allow) sr[c] = __float_as_uint(-INFINITY);
-            mt = fmaxf(mt, __uint_as_float(sr[c]));
           }
-        } else {
-#pragma unroll
-          for (int c = 0; c < BKV; ++c) mt = fmaxf(mt, __uint_as_float(sr[c]));
         }
+        // tile max of the raw scores: four independent 3-input max chains
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < BKV; c += 8) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            mq[u] = max3(mq[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
+        }
+        const float mt = max3(mq[0], mq[1], fmaxf(mq[2], mq[3]));
         // The reference max only moves when the tile max exceeds it by more than 2^8 (in log2
         // units), so exponents stay <= 8 and O is rescaled rarely; the result is exact.
         const float mts = mt * p.scale_log2;
@@ -345,23 +377,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float m_new = grow ? mts : m_run;
         const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
         const float corr = grow ? ex2(m_run - m_use) : 1.0f;  // m_run = -inf gives 0
-        float rs = 0.f;
+        const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
+        const float2 negm2 = make_float2(-m_use, -m_use);
+        float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
         for (int c0 = 0; c0 < BKV; c0 += 64) {
           uint32_t pk[32];
 #pragma unroll
           for (int c = 0; c < 64; c += 2) {
-            const float xa = fmaf(__uint_as_float(sr[c0 + c]), p.scale_log2, -m_use);
-            const float xb = fmaf(__uint_as_float(sr[c0 + c + 1]), p.scale_log2, -m_use);
-            // a quarter of the exponentials run on the FMA pipe to relieve the MUFU unit
-            const float ea = ex2(xa);
-            const float eb = ((c & 3) == 2) ? exp2_poly(xb) : ex2(xb);
-            rs += ea + eb;
-            pk[c / 2] = pack_bf16(ea, eb);
+            const float2 x = fma2(make_float2(__uint_as_float(sr[c0 + c]), __uint_as_float(sr[c0 + c + 1])), scale2,
+                                  negm2);
+            // 3/8 of the exponentials run on the FMA pipe to relieve the MUFU unit
+            float2 e;
+            e.x = ex2(x.x);
+            e.y = ((c & 6) != 0) ? exp2_poly(x.y) : ex2(x.y);
+            rs2[(c >> 1) & 3] = add2(rs2[(c >> 1) & 3], e);
+            pk[c / 2] = pack_bf16(e.x, e.y);
           }
           // P over the first 64 columns of S_a: key 2c in the low half of column c
           tmem_st32(s_tmem + c0 / 2, pk);
         }
+        const float2 rsum = add2(add2(rs2[0], rs2[1]), add2(rs2[2], rs2[3]));
+        const float rs = rsum.x + rsum.y;
         // O_a is stable here: S_j(a) completed, so PV_{j-1}(a) (issued before it) did too; and
         // PV_j(a) is not issued before this warpgroup signals P_j(a) below.
         if (j > 0 && __any_sync(0xffffffffu, grow)) {
