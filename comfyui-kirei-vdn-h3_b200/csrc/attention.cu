@@ -101,6 +101,16 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
+// 32 lanes x 32 bit x 16 columns TMEM store.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 // O += P V with P (A operand) in tensor memory.
 __device__ __forceinline__ void mma_f16_tmem_a(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
                                                uint32_t accumulate) {
@@ -130,9 +140,10 @@ enum {
   B_IFULL0, B_IFULL1, B_IFULL2, B_IFULL3, B_IEMPTY0, B_IEMPTY1, B_IEMPTY2, B_IEMPTY3, B_COUNT
 };
 
-// 320 threads, one CTA per SM: up to 200 registers per thread keep the softmax spill-free.
+// 320 threads, one CTA per SM.  Registers are allocated per SM sub-partition (16K each) and one
+// sub-partition hosts three of the ten warps, which caps the uniform allocation at 168/thread.
 template <int D>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kThreads, 1)
     window_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                             const __grid_constant__ CUtensorMap tv, Params p, int* err) {
   using L = Layout<D>;
@@ -381,10 +392,10 @@ __global__ void __maxnreg__(200)
         const float2 negm2 = make_float2(-m_use, -m_use);
         float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int c0 = 0; c0 < BKV; c0 += 64) {
-          uint32_t pk[32];
+        for (int c0 = 0; c0 < BKV; c0 += 32) {
+          uint32_t pk[16];
 #pragma unroll
-          for (int c = 0; c < 64; c += 2) {
+          for (int c = 0; c < 32; c += 2) {
             const float2 x = fma2(make_float2(__uint_as_float(sr[c0 + c]), __uint_as_float(sr[c0 + c + 1])), scale2,
                                   negm2);
             // 3/8 of the exponentials run on the FMA pipe to relieve the MUFU unit
@@ -395,7 +406,7 @@ __global__ void __maxnreg__(200)
             pk[c / 2] = pack_bf16(e.x, e.y);
           }
           // P over the first 64 columns of S_a: key 2c in the low half of column c
-          tmem_st32(s_tmem + c0 / 2, pk);
+          tmem_st16(s_tmem + c0 / 2, pk);
         }
         const float2 rsum = add2(add2(rs2[0], rs2[1]), add2(rs2[2], rs2[3]));
         const float rs = rsum.x + rsum.y;
