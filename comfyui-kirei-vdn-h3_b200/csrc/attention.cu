@@ -330,6 +330,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int h = code >> 20, qt = code & 0xFFFFF;
       const int t0 = p.tile_off[qt], n = p.tile_off[qt + 1] - t0;
       const int qrow = qt * 2 * BQ + a * BQ + row_in_tile;
+      // Per-row visibility (window.py:327-344).
+      bool dense = (qrow < p.vs) || (qrow >= p.ve);
+      int wlo = 0, whi = 0;
+      if (!dense && qrow < p.S) {
+        const int f = (qrow - p.vs) / p.tpf;
+        if (p.anchor_rows && (f == 0 || f == p.F - 1)) dense = true;
+        wlo = p.vs + p.frame_lo[f] * p.tpf;
+        whi = p.vs + (p.frame_hi[f] + 1) * p.tpf;
+      }
+      const int acol_lo = p.anchor_cols ? p.vs + p.tpf : p.vs;  // keys < acol_lo are anchor frame 0
+      const int acol_hi = p.anchor_cols ? p.ve - p.tpf : p.ve;  // keys >= acol_hi are anchor frame F-1
       float m_run = -INFINITY, l_run = 0.f;
       int info_next = p.ktile[t0];
       for (int j = 0; j < n; ++j) {
@@ -341,50 +352,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
+        uint32_t sr[BKV];  // raw scores of this row (fp32 bits)
+#pragma unroll
+        for (int c = 0; c < BKV / 32; ++c)
+          tmem_ld32(s_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
+        tmem_ld_wait();
         const int k0 = info >> 9;
         const int valid = (info & 0xFF) + 1;
         const bool masked = (info >> 8) & 1;
-        const bool any_mask = masked || valid < BKV;
-        // Per-row visibility (window.py:327-344), rebuilt on masked tiles only so that none of it
-        // stays live across the unmasked ones: a row sees key k iff k lies in its frame window
-        // [lo1, hi1), below hi2 (leading globals + anchor frame 0) or at/after lo3 (trailing
-        // anchor frame + globals); dense rows and unmasked tiles see [0, S).
-        int lo1 = 0, hi1 = p.S, hi2 = 0, lo3 = p.S;
-        if (masked && qrow >= p.vs && qrow < p.ve) {
-          const int f = (qrow - p.vs) / p.tpf;
-          if (!(p.anchor_rows && (f == 0 || f == p.F - 1))) {
-            lo1 = p.vs + p.frame_lo[f] * p.tpf;
-            hi1 = p.vs + (p.frame_hi[f] + 1) * p.tpf;
-            hi2 = p.anchor_cols ? p.vs + p.tpf : p.vs;
-            lo3 = p.anchor_cols ? p.ve - p.tpf : p.ve;
+        if (masked || valid < BKV) {
+#pragma unroll
+          for (int c = 0; c < BKV; ++c) {
+            const int key = k0 + c;
+            bool allow = c < valid;
+            if (masked && allow) {
+              allow = dense || key < p.vs || key >= p.ve || (key >= wlo && key < whi) || key < acol_lo ||
+                      key >= acol_hi;
+            }
+            if (!allow) sr[c] = __float_as_uint(-INFINITY);
           }
         }
-        auto apply_mask = [&](uint32_t* v, int cbase, int count) {
+        // tile max of the raw scores: four independent 3-input max chains
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-          for (int c = 0; c < count; ++c) {
-            const int key = k0 + cbase + c;
-            const bool allow = cbase + c < valid && ((key >= lo1 && key < hi1) || key < hi2 || key >= lo3);
-            if (!allow) v[c] = __float_as_uint(-INFINITY);
-          }
-        };
-        // Pass 1: tile max over the 128 raw scores (four independent 3-input max chains).
-        float mt;
-        {
-          uint32_t sr[BKV];
+        for (int c = 0; c < BKV; c += 8) {
 #pragma unroll
-          for (int c = 0; c < BKV / 32; ++c)
-            tmem_ld32(s_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
-          tmem_ld_wait();
-          if (any_mask) apply_mask(sr, 0, BKV);
-          float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-          for (int c = 0; c < BKV; c += 8) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-              mq[u] = max3(mq[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
-          }
-          mt = max3(mq[0], mq[1], fmaxf(mq[2], mq[3]));
+          for (int u = 0; u < 4; ++u)
+            mq[u] = max3(mq[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
         }
+        const float mt = max3(mq[0], mq[1], fmaxf(mq[2], mq[3]));
         // The reference max only moves when the tile max exceeds it by more than 2^8 (in log2
         // units), so exponents stay <= 8 and O is rescaled rarely; the result is exact.
         const float mts = mt * p.scale_log2;
@@ -394,35 +390,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float corr = grow ? ex2(m_run - m_use) : 1.0f;  // m_run = -inf gives 0
         const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
         const float2 negm2 = make_float2(-m_use, -m_use);
-        float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-        // Pass 2: reload the scores in two 64-key halves, exponentiate and pack P (bf16) over the
-        // first 64 columns of S_a (key 2c in the low half of column c).  Half h writes columns
-        // [32h, 32h + 32), whose scores were already read, before it reloads keys 64..127.
+        float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int h0 = 0; h0 < BKV; h0 += 64) {
-          uint32_t sr[64];
-          tmem_ld32(s_tmem + h0, *reinterpret_cast<uint32_t(*)[32]>(sr));
-          tmem_ld32(s_tmem + h0 + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-          tmem_ld_wait();
-          if (any_mask) apply_mask(sr, h0, 64);
+        for (int c0 = 0; c0 < BKV; c0 += 32) {
+          uint32_t pk[16];
 #pragma unroll
-          for (int c0 = 0; c0 < 64; c0 += 32) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int c = 0; c < 32; c += 2) {
-              const float2 x =
-                  fma2(make_float2(__uint_as_float(sr[c0 + c]), __uint_as_float(sr[c0 + c + 1])), scale2, negm2);
-              // 3/8 of the exponentials run on the FMA pipe to relieve the MUFU unit
-              float2 e;
-              e.x = ex2(x.x);
-              e.y = ((c & 6) != 0) ? exp2_poly(x.y) : ex2(x.y);
-              rs2[(c >> 1) & 1] = add2(rs2[(c >> 1) & 1], e);
-              pk[c / 2] = pack_bf16(e.x, e.y);
-            }
-            tmem_st16(s_tmem + (h0 + c0) / 2, pk);
+          for (int c = 0; c < 32; c += 2) {
+            const float2 x = fma2(make_float2(__uint_as_float(sr[c0 + c]), __uint_as_float(sr[c0 + c + 1])), scale2,
+                                  negm2);
+            // 3/8 of the exponentials run on the FMA pipe to relieve the MUFU unit
+            float2 e;
+            e.x = ex2(x.x);
+            e.y = ((c & 6) != 0) ? exp2_poly(x.y) : ex2(x.y);
+            rs2[(c >> 1) & 3] = add2(rs2[(c >> 1) & 3], e);
+            pk[c / 2] = pack_bf16(e.x, e.y);
           }
+          // P over the first 64 columns of S_a: key 2c in the low half of column c
+          tmem_st16(s_tmem + c0 / 2, pk);
         }
-        const float2 rsum = add2(rs2[0], rs2[1]);
+        const float2 rsum = add2(add2(rs2[0], rs2[1]), add2(rs2[2], rs2[3]));
         const float rs = rsum.x + rsum.y;
         // O_a is stable here: S_j(a) completed, so PV_{j-1}(a) (issued before it) did too; and
         // PV_j(a) is not issued before this warpgroup signals P_j(a) below.
