@@ -285,7 +285,9 @@ def main():
                                  out_proj=types.SimpleNamespace(weight=out_w),
                                  q_norm=types.SimpleNamespace(weight=qn, eps=1e-6),
                                  k_norm=types.SimpleNamespace(weight=kn, eps=1e-6), forward=None)
-    state = pkg.B200State("bench", {"enable_softmax_gate": True}, [branch], H, D)
+    # N > 1: the heads are sharded over the ranks (H/N each, recurrence kept per head), the
+    # per-head outputs exchanged by row block over NCCL and the projected rows all-gathered
+    state = pkg.B200State("bench", {"enable_softmax_gate": True}, [branch], H, D, shard_heads=world > 1)
     block = state.fused_block(attn, 0, dev)
     status = state.device_status(dev)
     g = torch.Generator().manual_seed(1)
@@ -306,7 +308,7 @@ def main():
     pkg.hybrid.launch_window_attention = timed_launch
     with pkg.cholesky_runtime_scope():
         for _ in range(args.warmup):
-            block.forward(x_dev, lay, state.window_plans, status, out=out_dev)
+            block.forward(x_dev, lay, state.window_plans, status, out=out_dev if world == 1 else None)
     torch.cuda.synchronize()
     status.raise_if_failed()
     attn_ms.clear()
@@ -317,7 +319,7 @@ def main():
         e_start.record()
         with pkg.cholesky_runtime_scope():
             for _ in range(args.steps):
-                block.forward(x_dev, lay, state.window_plans, status, out=out_dev)
+                block.forward(x_dev, lay, state.window_plans, status, out=out_dev if world == 1 else None)
             e_end.record()
             torch.cuda.synchronize()
     barrier(world)
@@ -325,20 +327,42 @@ def main():
     pkg.hybrid.launch_window_attention = orig_launch
     ms = e_start.elapsed_time(e_end) / max(args.steps, 1)
     ms = max_over_ranks(ms, world)
-    value = flops["total"] * world / (ms * 1e-3) / 1e12
+    value = flops["total"] / (ms * 1e-3) / 1e12  # one block forward of the whole problem per step
     attn_avg = sum(a.elapsed_time(b) for a, b in attn_ms) / max(len(attn_ms), 1)
     pk, pk_src = peaks()
-    achieved = flops["attention"] / (attn_avg * 1e-3) / 1e12
+    achieved = flops["attention"] / world / (attn_avg * 1e-3) / 1e12  # this rank's heads
+    
     peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
     # ---- end to end through the public operator with host buffers
     fwd = pkg.make_vdn_forward(attn, state, 0)
-    out_host = torch.empty(lay.seq_len, hidden, dtype=torch.bfloat16).pin_memory()
+    S = lay.seq_len
+    if world == 1:
+        out_host = torch.empty(S, hidden, dtype=torch.bfloat16).pin_memory()
 
-    def e2e_step():
-        xd = x_host.to(dev, non_blocking=True)
-        with pkg.publish_layout(lay):
-            y = fwd(xd)
-        out_host.copy_(y, non_blocking=True)
+        def e2e_step():
+            xd = x_host.to(dev, non_blocking=True)
+            with pkg.publish_layout(lay):
+                y = fwd(xd)
+            out_host.copy_(y, non_blocking=True)
+    else:
+        # each rank holds its own row block of x and of the output in pinned host memory:
+        # H2D of the block, NCCL all-gather of x, sharded forward, D2H of the rank's rows
+        import torch.distributed as dist
+
+        sb = -(-S // world)
+        r0, n_rows = rank * sb, max(0, min(sb, S - rank * sb))
+        x_rows_host = torch.zeros(sb, hidden, dtype=torch.bfloat16).pin_memory()
+        x_rows_host[:n_rows] = x_host[r0:r0 + n_rows]
+        x_all = torch.empty(world * sb, hidden, device=dev, dtype=torch.bfloat16)
+        mine = x_all[rank * sb:(rank + 1) * sb]
+        out_host = torch.empty(sb, hidden, dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            mine.copy_(x_rows_host, non_blocking=True)
+            dist.all_gather_into_tensor(x_all, mine)
+            with pkg.publish_layout(lay):
+                y = fwd(x_all[:S])
+            out_host[:n_rows].copy_(y[r0:r0 + n_rows], non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
@@ -354,21 +378,22 @@ def main():
         torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / max(args.steps, 1), world)
     status.raise_if_failed()
-    e2e_value = flops["total"] * world / (e2e_ms * 1e-3) / 1e12
+    e2e_value = flops["total"] / (e2e_ms * 1e-3) / 1e12
     launches_per_step = 18
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) x)",
         "config": {"workload": f"config{args.config}: 31x{c['grid'][0] * c['grid'][1]}+512 tokens, H={H}, D={D}, "
-                               f"hidden={hidden}", "tokens": lay.seq_len, "parallelism": "heads" if world > 1 else "none",
+                               f"hidden={hidden}", "tokens": lay.seq_len, "parallelism": f"heads/{world}" if world > 1 else "none",
                    "l2": "inputs larger than L2 (x 270 MB, weights 0.36 GB)"},
         "tflop_per_step": flops["total"] / 1e12,
         "roofline": {"kernel": "window_attention_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None, "peak_source": f"{pk_src} sustained",
                      "kernel_ms": attn_avg, "block_frac": value / world / peak},
+        # bytes summed over the ranks (at N > 1 each rank moves its own row block)
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2},
+                "h2d_bytes_per_step": S * hidden * 2, "d2h_bytes_per_step": S * hidden * 2},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
     }

@@ -8,16 +8,20 @@ CUDA for sm_100a loaded from the in-tree C-ABI library ``libvdn_b200.so``; there
 CPU or library fallback.
 """
 
-from . import _lib
+from . import _lib, projection, shard
+from ._lib import DeviceStatus
 from .branch import B200LinearBranch, cholesky_runtime_scope
 from .hybrid import B200State, FusedBlock, make_vdn_forward, run_forward_checked
 from .layout import (ANCHOR_FRAME_MODES, VDNLayout, current_layout, full_coverage, make_layout, publish_layout,
                      window_bounds, with_window)
-from .projection import gemm, prepare_projection_maps, project, quantize_rows_int8, quantize_tensor_fp8
+from .projection import (gemm, gemm_grouped_k, prepare_projection_maps, project, quantize_rows_int8,
+                         quantize_tensor_fp8)
+from .shard import HeadShard
 from .window import WindowPlanCache, build_window_plan, window_softmax_b200
 
 __all__ = [
-    "ANCHOR_FRAME_MODES", "B200LinearBranch", "B200State", "FusedBlock", "VDNLayout", "WindowPlanCache",
+    "ANCHOR_FRAME_MODES", "B200LinearBranch", "B200State", "DeviceStatus", "FusedBlock", "HeadShard", "VDNLayout",
+    "WindowPlanCache", "gemm_grouped_k",
     "build_window_plan", "cholesky_runtime_scope", "current_layout", "full_coverage", "gemm", "make_layout",
     "make_vdn_forward", "prepare_projection_maps", "project", "publish_layout", "quantize_rows_int8",
     "quantize_tensor_fp8", "run_forward_checked", "window_bounds", "window_softmax_b200", "with_window", "_lib",

@@ -25,6 +25,8 @@ _F = ctypes.c_float
 # name -> argument types (all return int status)
 SIGNATURES: dict[str, list] = {
     "vdn_gemm": [_I, _P, _L, _P, _L, _L, _P, _L, _P, _L, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _I, _P, _L, _P, _P],
+    "vdn_gemm_grouped_k": [_I, _P, _L, _L, _I, _I, _P, _L, _P, _L, _I, _I, _I, _F, _P, _P, _P, _P, _P, _I, _P, _L,
+                           _P, _P],
     "vdn_qkv_gemm": [_I, _P, _L, _P, _L, _I, _I, _I, _I, _I, _P, _F, _F, _P, _P, _P, _P, _P, _L, _P, _L, _P, _L,
                      _P, _P],
     "vdn_window_attention": [_P, _L, _P, _L, _P, _L, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _I, _P,
@@ -40,6 +42,8 @@ SIGNATURES: dict[str, list] = {
     "vdn_readout": [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _L, _P, _L, _L, _P],
     "vdn_cast_rows": [_P, _L, _I, _I, _I, _P, _L, _P],
     "vdn_quant_int8_rows": [_I, _P, _L, _I, _I, _P, _L, _P, _P],
+    "vdn_fp8_amax": [_I, _P, _L, _I, _I, _P, _P],
+    "vdn_fp8_cast": [_I, _P, _L, _I, _I, _P, _P, _L, _P, _P],
     "vdn_quant_fp8_tensor": [_I, _P, _L, _I, _I, _P, _L, _P, _P, _P],
     "vdn_fp8_linear_noalloc": [_P, _L, _I, _I, _P, _L, _I, _P, _P, _L, _P, _P],
 }

@@ -128,7 +128,9 @@ __device__ __forceinline__ void store_plain_chunk(const Epilogue& ep, const uint
       for (int j = 0; j < 32; j += 4)
         *reinterpret_cast<int4*>(dst + j) = make_int4(r[j], r[j + 1], r[j + 2], r[j + 3]);
     } else {
-      for (int j = 0; j < 32 && col0 + j < N; ++j) dst[j] = static_cast<int>(r[j]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) dst[j] = static_cast<int>(r[j]);
     }
     return;
   }
@@ -155,7 +157,9 @@ __device__ __forceinline__ void store_plain_chunk(const Epilogue& ep, const uint
       for (int j = 0; j < 32; j += 4)
         *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
     } else {
-      for (int j = 0; j < 32 && col0 + j < N; ++j) dst[j] = v[j];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) dst[j] = v[j];
     }
   } else {
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ep.out) + (long long)row * ep.ldo + col0;
@@ -170,7 +174,9 @@ __device__ __forceinline__ void store_plain_chunk(const Epilogue& ep, const uint
         *reinterpret_cast<uint4*>(dst + j) = p;
       }
     } else {
-      for (int j = 0; j < 32 && col0 + j < N; ++j) dst[j] = __float2bfloat16_rn(v[j]);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) dst[j] = __float2bfloat16_rn(v[j]);
     }
   }
 }
@@ -178,7 +184,7 @@ __device__ __forceinline__ void store_plain_chunk(const Epilogue& ep, const uint
 template <int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap ta2,
-                const __grid_constant__ CUtensorMap tb, int M, int N, int K, int k_split,
+                const __grid_constant__ CUtensorMap tb, int M, int N, int K, int k_split, int kg,
                 Epilogue ep, int* err) {
   using T = Traits<KIND>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -240,7 +246,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sb = sa + kStageA;
         const uint32_t fb = smem_u32(&full[stage]);
         mbar_arrive_expect_tx(fb, kStageBytes);
-        if (kb < ks_blocks)
+        if (kg > 0)  // grouped K: A is [K / kg][M][kg], k-block kb lies inside one group
+          tma_load_3d(sa, &ta, fb, (kb * T::BK) % kg, m * BM, (kb * T::BK) / kg);
+        else if (kb < ks_blocks)
           tma_load_2d(sa, &ta, fb, kb * T::BK, m * BM);
         else
           tma_load_2d(sa, &ta2, fb, (kb - ks_blocks) * T::BK, m * BM);
@@ -351,32 +359,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-      } else if (ep.aux_out && n0 >= ep.aux_col0) {
-        for (int c = 0; c < BN; c += 32) {
-          tmem_ld32(tbase + c, r);
-          tmem_ld_wait();
-          const int col = n0 + c;
-          if (row < M && col < N) {
-            float* dst = ep.aux_out + (long long)row * ep.ld_aux + (col - ep.aux_col0);
-            const int lim = min(32, N - col);
-            if (lim == 32) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(dst + j) =
-                    make_float4(scaled<KIND>(ep, r[j], ars, col + j, N), scaled<KIND>(ep, r[j + 1], ars, col + j + 1, N),
-                                scaled<KIND>(ep, r[j + 2], ars, col + j + 2, N),
-                                scaled<KIND>(ep, r[j + 3], ars, col + j + 3, N));
-            } else {
-              for (int j = 0; j < lim; ++j) dst[j] = scaled<KIND>(ep, r[j], ars, col + j, N);
-            }
-          }
-        }
       } else {
+        // 32-column chunks: a tile may straddle the v columns and the fp32 side columns
         for (int c = 0; c < BN; c += 32) {
-          if (n0 + c >= N) break;
+          const int col = n0 + c;
+          if (col >= N) break;
           tmem_ld32(tbase + c, r);
           tmem_ld_wait();
-          store_plain_chunk<KIND>(ep, r, row, n0 + c, M, N, alpha);
+          if (ep.aux_out && col >= ep.aux_col0) {
+            if (row < M) {
+              float* dst = ep.aux_out + (long long)row * ep.ld_aux + (col - ep.aux_col0);
+              const int lim = min(32, N - col);
+              if (lim == 32) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                  *reinterpret_cast<float4*>(dst + j) =
+                      make_float4(scaled<KIND>(ep, r[j], ars, col + j, N), scaled<KIND>(ep, r[j + 1], ars, col + j + 1, N),
+                                  scaled<KIND>(ep, r[j + 2], ars, col + j + 2, N),
+                                  scaled<KIND>(ep, r[j + 3], ars, col + j + 3, N));
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < lim) dst[j] = scaled<KIND>(ep, r[j], ars, col + j, N);
+              }
+            }
+          } else {
+            store_plain_chunk<KIND>(ep, r, row, col, M, N, alpha);
+          }
         }
       }
       tc_fence_before();
@@ -399,9 +408,10 @@ constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
 template <int KIND>
 int launch(const void* A, long long lda, const void* A2, long long lda2, long long k_split,
            const void* B, long long ldb, int M, int N, int K, const Epilogue& ep, int* err,
-           cudaStream_t stream) {
+           cudaStream_t stream, long long group_stride = 0, int kg = 0) {
   using T = Traits<KIND>;
   if (M <= 0 || N <= 0 || K <= 0 || (K % 16) != 0) return kUnsupported;
+  if (kg > 0 && (A2 != nullptr || (kg % T::BK) != 0 || (K % kg) != 0)) return kUnsupported;
   if (A2 == nullptr) {
     A2 = A;
     lda2 = lda;
@@ -411,7 +421,9 @@ int launch(const void* A, long long lda, const void* A2, long long lda2, long lo
   const CUtensorMapDataType dt = KIND == 0 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const int eb = KIND == 0 ? 2 : 1;
   CUtensorMap ta, ta2, tb;
-  int rc = make_tmap_2d(&ta, A, dt, eb, (uint64_t)k_split, (uint64_t)M, (uint64_t)lda, T::BK, BM);
+  int rc = kg > 0 ? make_tmap_3d(&ta, A, dt, eb, (uint64_t)kg, (uint64_t)M, (uint64_t)(K / kg), (uint64_t)lda,
+                                 (uint64_t)group_stride, T::BK, BM)
+                  : make_tmap_2d(&ta, A, dt, eb, (uint64_t)k_split, (uint64_t)M, (uint64_t)lda, T::BK, BM);
   if (rc) return rc;
   rc = make_tmap_2d(&ta2, A2, dt, eb, (uint64_t)(K - k_split > 0 ? K - k_split : T::BK), (uint64_t)M,
                     (uint64_t)lda2, T::BK, BM);
@@ -425,7 +437,7 @@ int launch(const void* A, long long lda, const void* A2, long long lda2, long lo
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  gemm_kernel<KIND><<<grid, kThreads, kSmemBytes, stream>>>(ta, ta2, tb, M, N, K, (int)k_split, ep, err);
+  gemm_kernel<KIND><<<grid, kThreads, kSmemBytes, stream>>>(ta, ta2, tb, M, N, K, (int)k_split, kg, ep, err);
   return launch_status();
 }
 
@@ -478,6 +490,32 @@ int vdn_gemm(int kind, const void* A, long long lda, const void* A2, long long l
   }
 }
 
+// C = epilogue(A * B^T) with a grouped-K A operand: A holds `groups` slabs of [M, kg]
+// (rows `lda` apart, slabs `group_stride` apart) and K = groups * kg runs through the
+// slabs in order.  This reads an all-to-all receive buffer [ranks][rows][kg] directly
+// as the K-concatenated operand of the row-split output projection.
+int vdn_gemm_grouped_k(int kind, const void* A, long long lda, long long group_stride, int groups, int kg,
+                       const void* B, long long ldb, void* C, long long ldc, int out_kind, int M, int N,
+                       float alpha, const float* dev_scale0, const float* dev_scale1, const float* row_scale,
+                       const float* col_scale, const float* col_bias, int act, const void* addend,
+                       long long ld_add, int* dev_err, void* stream) {
+  if (!A || !B || !C) return vdn::kBadArgument;
+  if (groups <= 0 || kg <= 0) return vdn::kBadArgument;
+  if (out_kind == vdn::gemm::kOutS32 && kind != 2) return vdn::kBadArgument;
+  if (group_stride < (long long)M * lda) return vdn::kBadArgument;  // slabs must not overlap
+  Epilogue ep = plain_epilogue(C, ldc, out_kind, alpha, row_scale, col_scale, col_bias, act, addend, ld_add);
+  ep.dev_scale0 = dev_scale0;
+  ep.dev_scale1 = dev_scale1;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int K = groups * kg;
+  switch (kind) {
+    case 0: return vdn::gemm::launch<0>(A, lda, nullptr, 0, 0, B, ldb, M, N, K, ep, dev_err, s, group_stride, kg);
+    case 1: return vdn::gemm::launch<1>(A, lda, nullptr, 0, 0, B, ldb, M, N, K, ep, dev_err, s, group_stride, kg);
+    case 2: return vdn::gemm::launch<2>(A, lda, nullptr, 0, 0, B, ldb, M, N, K, ep, dev_err, s, group_stride, kg);
+    default: return vdn::kBadArgument;
+  }
+}
+
 // Fused QKV projection: one GEMM of x [S, hidden] against the concatenated weight
 // [3*inner + n_aux, hidden] (q, k, v rows, then the fp32 side projections).
 //   qkv_out  [S, 3*inner] bf16   raw q/k/v (hybrid.py:260-268)
@@ -496,7 +534,8 @@ int vdn_qkv_gemm(int kind, const void* x, long long ldx, const void* w, long lon
       (aux_out && (!vdn::aligned16(aux_out) || (ld_aux * 4) % 16)))
     return vdn::kMisaligned;
   if (head_dim != 64 && head_dim != 128) return vdn::kUnsupported;
-  if ((2 * inner) % vdn::gemm::BN != 0 || (3 * inner) % vdn::gemm::BN != 0) return vdn::kUnsupported;
+  // a 256-column tile never mixes normalised q/k columns with v or side columns
+  if ((2 * inner) % vdn::gemm::BN != 0) return vdn::kUnsupported;
   if (n_aux > 0 && !aux_out) return vdn::kBadArgument;
   Epilogue ep = plain_epilogue(qkv_out, ld_qkv, vdn::gemm::kOutBF16, alpha, row_scale, col_scale, nullptr, 0,
                                nullptr, 0);

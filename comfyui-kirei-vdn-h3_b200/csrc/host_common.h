@@ -53,6 +53,25 @@ inline int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType 
   return r == CUDA_SUCCESS ? kOk : kTensorMapFailed;
 }
 
+// 3-D row-major tensor [groups][outer][inner]: rows `row_stride_elems` apart, groups
+// `group_stride_elems` apart; box {box_inner, box_outer, 1}.
+inline int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                        uint64_t inner, uint64_t outer, uint64_t groups, uint64_t row_stride_elems,
+                        uint64_t group_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return kTensorMapFailed;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((row_stride_elems * elem_bytes) & 15) ||
+      ((group_stride_elems * elem_bytes) & 15))
+    return kMisaligned;
+  cuuint64_t dims[3] = {inner, outer, groups};
+  cuuint64_t strides[2] = {row_stride_elems * (uint64_t)elem_bytes, group_stride_elems * (uint64_t)elem_bytes};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = enc(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kTensorMapFailed;
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 inline int sm_count() {

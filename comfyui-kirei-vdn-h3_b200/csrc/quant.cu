@@ -131,6 +131,43 @@ int vdn_quant_fp8_tensor(int src_kind, const void* x, long long ldx, int rows, i
   return vdn::launch_status();
 }
 
+// The two halves of vdn_quant_fp8_tensor, for callers that combine the amax of several
+// devices in between (an all-reduce MAX of `amax` across the ranks of a row-split
+// projection): vdn_fp8_amax clears and fills `amax`; vdn_fp8_cast quantises with it.
+int vdn_fp8_amax(int src_kind, const void* x, long long ldx, int rows, int K, float* amax, void* stream) {
+  if (!x || !amax || rows < 0 || K <= 0) return vdn::kBadArgument;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  cudaMemsetAsync(amax, 0, sizeof(float), s);
+  const long long n = (long long)rows * K;
+  const int blocks = (int)std::min<long long>((n + 255) / 256, 4LL * vdn::sm_count());
+  if (blocks > 0) {
+    if (src_kind == 0)
+      vdn::quant::amax_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+                                                                     rows, K, amax);
+    else
+      vdn::quant::amax_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, rows, K, amax);
+  }
+  return vdn::launch_status();
+}
+
+int vdn_fp8_cast(int src_kind, const void* x, long long ldx, int rows, int K, const float* amax, void* q,
+                 long long ldq, float* scale_out, void* stream) {
+  if (!x || !q || !amax || rows < 0 || K <= 0) return vdn::kBadArgument;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  const long long n = (long long)rows * K;
+  const int blocks = (int)std::min<long long>((n + 255) / 256, 4LL * vdn::sm_count());
+  if (blocks > 0) {
+    if (src_kind == 0)
+      vdn::quant::fp8_cast_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
+          reinterpret_cast<const __nv_bfloat16*>(x), ldx, rows, K, amax, reinterpret_cast<__nv_fp8_e4m3*>(q), ldq,
+          scale_out);
+    else
+      vdn::quant::fp8_cast_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, rows, K, amax,
+                                                                 reinterpret_cast<__nv_fp8_e4m3*>(q), ldq, scale_out);
+  }
+  return vdn::launch_status();
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------------------

@@ -17,6 +17,10 @@ On the device one block forward is four phases, all on the caller's stream:
 4. one tcgen05 GEMM over K = 2*H*D of [gated softmax | branch] against
    [W_out | W_to_out]: out_proj, to_out_linear and the delta add in one pass (bf16);
    the quantised precisions run out_proj then to_out_linear with an addend epilogue.
+
+With a ``HeadShard`` (one process per GPU, torch.distributed) phases 1-3 run on this
+rank's heads only and phase 4 becomes all-to-all by row block, the output projection on
+the rank's rows and an all-gather of the rows (shard.py).
 """
 
 from __future__ import annotations
@@ -30,6 +34,8 @@ from . import _lib
 from .branch import BranchDeviceWeights, BranchWorkspace, cholesky_runtime_scope, run_branch
 from .layout import VDNLayout, current_layout
 from .projection import KIND, QuantizedMatrix, quantize_rows_int8, quantize_tensor_fp8, quantize_weight
+from .shard import (HeadShard, RowExchange, concat_rows, default_shard, qkv_row_index, rank_major_out_weight,
+                    slice_branch_weights, split_heads_outputs)
 from .window import ATTENTION_BACKENDS, WindowPlanCache, launch_window_attention
 
 AUX_ALIGN = 256
@@ -55,19 +61,29 @@ class FusedBlock:
     """Device weights of one H3 attention block + its VDN branch, laid out for the kernels."""
 
     def __init__(self, qkv_w, q_norm_w, k_norm_w, out_w, branch_w: Mapping, heads, dim, device, *,
-                 precision="bf16", eps=1e-6, enable_gate=True, short_conv=("k", "v")):
+                 precision="bf16", eps=1e-6, enable_gate=True, short_conv=("k", "v"), shard: HeadShard | None = None):
         dev = torch.device(device)
-        H, D = int(heads), int(dim)
-        inner = H * D
+        H_all, D = int(heads), int(dim)
+        inner_all = H_all * D
         hidden = int(qkv_w.shape[1])
-        if qkv_w.shape[0] != 3 * inner or out_w.shape != (hidden, inner):
+        if qkv_w.shape[0] != 3 * inner_all or out_w.shape != (hidden, inner_all):
             raise ValueError("attention weights do not match the head geometry")
-        self.geo = BlockGeometry(H, D, hidden)
+        if shard is not None and shard.world == 1:
+            shard = None
+        if shard is not None and shard.heads != H_all:
+            raise ValueError("head shard does not match the block's head count")
+        self.shard = shard
+        hs = shard.head_slice if shard is not None else slice(0, H_all)
+        H = hs.stop - hs.start
+        inner = H * D
+        self.geo = BlockGeometry(H, D, hidden)  # this rank's heads
+        self.heads_total = H_all
         self.device = dev
         self.precision = precision
         self.eps = float(eps)
         self.enable_gate = bool(enable_gate)
         self.short_conv = tuple(short_conv)
+        qkv_rows = qkv_row_index(H_all, D, hs)
 
         def f32(t):
             return t.detach().to(dev, torch.float32).contiguous()
@@ -75,11 +91,13 @@ class FusedBlock:
         def b16(t):
             return t.detach().to(dev, torch.bfloat16).contiguous()
 
+        # this rank's view of the branch weights (the full map on one GPU)
+        wl = slice_branch_weights(branch_w, H_all, D, hs) if shard is not None else branch_w
         zeros_h = torch.zeros(H, hidden)
-        gate_w = branch_w.get("softmax_gate.up.weight", zeros_h) if enable_gate else zeros_h
-        self.gate_bias = f32(branch_w.get("softmax_gate.up.bias", torch.zeros(H))) if enable_gate else None
-        side = [gate_w, branch_w.get("beta_proj.weight", zeros_h), branch_w.get("output_gate.down.weight",
-                torch.zeros(D, hidden)), branch_w.get("alpha.down.weight", torch.zeros(D, hidden))]
+        gate_w = wl.get("softmax_gate.up.weight", zeros_h) if enable_gate else zeros_h
+        self.gate_bias = f32(wl.get("softmax_gate.up.bias", torch.zeros(H))) if enable_gate else None
+        side = [gate_w, wl.get("beta_proj.weight", zeros_h), wl.get("output_gate.down.weight",
+                torch.zeros(D, hidden)), wl.get("alpha.down.weight", torch.zeros(D, hidden))]
         n_side = 2 * H + 2 * D
         self.n_aux = (n_side + AUX_ALIGN - 1) // AUX_ALIGN * AUX_ALIGN
         pad = torch.zeros(self.n_aux - n_side, hidden)
@@ -89,19 +107,32 @@ class FusedBlock:
         self.norm_w = torch.cat([f32(q_norm_w), f32(k_norm_w)]).contiguous()
         self.has_branch = "to_out_linear.weight" in branch_w or "to_out_linear.weight_fp8" in branch_w
         to_out = branch_w.get("to_out_linear.weight")
+        if to_out is not None and not self.has_branch:
+            to_out = None
         if precision == "bf16":
-            self.w_big = torch.cat([b16(qkv_w), side_w.to(dev, torch.bfloat16)], 0).contiguous()
-            if self.has_branch and to_out is not None:
+            self.w_big = torch.cat([b16(qkv_w[qkv_rows]), side_w.to(dev, torch.bfloat16)], 0).contiguous()
+            if shard is not None:
+                # every rank projects all hidden columns of its row block: K in rank-major order
+                self.w_out_cat = b16(rank_major_out_weight(out_w.detach().cpu(), None if to_out is None else
+                                                           to_out.detach().cpu(), H_all, D, shard.world))
+            elif to_out is not None:
                 self.w_out_cat = torch.cat([b16(out_w), b16(to_out)], 1).contiguous()
             else:
                 self.w_out_cat = torch.cat([b16(out_w), torch.zeros(hidden, inner, device=dev,
                                                                     dtype=torch.bfloat16)], 1).contiguous()
         else:
-            self.w_qkv_q = quantize_weight(qkv_w, precision, dev)
+            # quantise the whole matrix, then keep this rank's rows: the fp8 per-tensor scale
+            # stays the one of the full weight
+            wq = quantize_weight(qkv_w, precision, dev)
+            if shard is not None:
+                idx = qkv_rows.to(dev)
+                wq = QuantizedMatrix(wq.data[idx].contiguous(),
+                                     wq.scale[idx].contiguous() if precision == "int8" else wq.scale, precision)
+            self.w_qkv_q = wq
             self.w_side = side_w.to(dev, torch.bfloat16).contiguous()
             self.w_out_q = quantize_weight(out_w, precision, dev)
             self.w_to_q = quantize_weight(to_out, precision, dev) if to_out is not None else None
-        self.bw = BranchDeviceWeights.from_dict(branch_w, H, D, dev, short_conv=self.short_conv) if self.has_branch \
+        self.bw = BranchDeviceWeights.from_dict(wl, H, D, dev, short_conv=self.short_conv) if self.has_branch \
             else None
         self._ws: dict = {}
 
@@ -118,14 +149,25 @@ class FusedBlock:
                 "qkv": torch.empty(S, 3 * g.inner, **bf),
                 "qkn": torch.empty(S, 2 * g.inner, **bf),
                 "aux": torch.empty(S, self.n_aux, device=dev, dtype=torch.float32),
-                "flat": torch.empty(S, g.inner, **bf),
-                "branch": torch.zeros(S, g.inner, **bf),
             }
+            if self.shard is not None:
+                # per-head outputs [gated softmax | branch] side by side: one all-to-all chunk per rank
+                xchg = RowExchange(self.shard, S, 2 * g.inner, g.hidden, dev)
+                ws["xchg"] = xchg
+                ws["flat"] = xchg.send[:S, :g.inner]
+                ws["branch"] = xchg.send[:S, g.inner:]
+                ws["branch_written"] = False
+            else:
+                ws["flat"] = torch.empty(S, g.inner, **bf)
+                ws["branch"] = torch.zeros(S, g.inner, **bf)
             if self.precision != "bf16":
                 qdt = torch.int8 if self.precision == "int8" else torch.float8_e4m3fn
-                sdim = S if self.precision == "int8" else 1
-                for name, k in (("xq", g.hidden), ("fq", g.inner), ("bq", g.inner)):
-                    ws[name] = QuantizedMatrix(torch.empty(S, k, device=dev, dtype=qdt),
+                # the row-split projection quantises only this rank's rows of all heads
+                rows_out = S if self.shard is None else self.shard.row_block(S)
+                k_out = self.heads_total * g.dim
+                for name, rows, k in (("xq", S, g.hidden), ("fq", rows_out, k_out), ("bq", rows_out, k_out)):
+                    sdim = rows if self.precision == "int8" else 1
+                    ws[name] = QuantizedMatrix(torch.empty(rows, k, device=dev, dtype=qdt),
                                                torch.empty(sdim, device=dev, dtype=torch.float32), self.precision)
                 ws["work"] = torch.empty(1, device=dev, dtype=torch.float32)
             if layout is not None and self.bw is not None and not layout.full_cover:
@@ -173,26 +215,91 @@ class FusedBlock:
                       self.w_out_cat.data_ptr(), self.w_out_cat.stride(0), out.data_ptr(), out.stride(0), 0, S,
                       g.hidden, K, 1.0, None, None, None, None, None, 0, None, 0, status.err_ptr, stream)
             return
-        kind = KIND[self.precision]
+        self._quantized_out(ws["flat"], ws["branch"] if with_branch else None, ws, out, status, stream)
 
-        def quantized_gemm(src, buf, w: QuantizedMatrix, addend):
+    def _quantized_out(self, flat, branch, ws, out, status, stream, amax_reduce=None):
+        """out = Q(flat) W_out^T (+ Q(branch) W_to^T as an addend pass), quantised
+        activations: int8 per row, fp8 per tensor (``amax_reduce`` combines the amax of
+        the ranks' row blocks)."""
+        kind = KIND[self.precision]
+        rows = flat.shape[0]
+        K = flat.shape[1]
+
+        def quantized_gemm(src, buf: QuantizedMatrix, w: QuantizedMatrix, addend):
+            if rows == 0 and self.precision == "int8":
+                return  # per-row scales: nothing to combine across ranks
+            buf = QuantizedMatrix(buf.data[:rows], buf.scale[:rows] if self.precision == "int8" else buf.scale,
+                                  self.precision)
             if self.precision == "int8":
                 qa = quantize_rows_int8(src, buf)
                 rs, cs, d0, d1 = qa.scale, w.scale, None, None
             else:
-                qa = quantize_tensor_fp8(src, buf, ws["work"])
+                qa = quantize_tensor_fp8(src, buf, ws["work"], amax_reduce=amax_reduce)
                 rs, cs, d0, d1 = None, None, qa.scale, w.scale
+            if rows == 0:
+                return
             _lib.call("vdn_gemm", kind, qa.data.data_ptr(), qa.data.stride(0), None, 0, 0, w.data.data_ptr(),
-                      w.data.stride(0), out.data_ptr(), out.stride(0), 0, S, g.hidden, g.inner, 1.0, _lib.ptr(d0),
+                      w.data.stride(0), out.data_ptr(), out.stride(0), 0, rows, out.shape[1], K, 1.0, _lib.ptr(d0),
                       _lib.ptr(d1), _lib.ptr(rs), _lib.ptr(cs), None, 0, _lib.ptr(addend),
                       addend.stride(0) if addend is not None else 0, status.err_ptr, stream)
 
-        quantized_gemm(ws["flat"], ws["fq"], self.w_out_q, None)
-        if with_branch and self.w_to_q is not None:
-            quantized_gemm(ws["branch"], ws["bq"], self.w_to_q, out)
+        quantized_gemm(flat, ws["fq"], self.w_out_q, None)
+        if branch is not None and self.w_to_q is not None:
+            quantized_gemm(branch, ws["bq"], self.w_to_q, out)
+
+    def project_rows(self, ws, with_branch, recv, rows, out_rows, status, stream, amax_reduce=None):
+        """Head-sharded phase 4 on this rank: the output projection of ``rows`` rows from
+        the all-to-all receive buffer ``recv`` [ranks, Sb, 2*H/g*D] into ``out_rows``."""
+        g = self.geo
+        world = recv.shape[0]
+        if self.precision == "bf16":
+            if rows > 0:
+                _lib.call("vdn_gemm_grouped_k", 0, recv.data_ptr(), recv.stride(1), recv.stride(0), world,
+                          2 * g.inner, self.w_out_cat.data_ptr(), self.w_out_cat.stride(0), out_rows.data_ptr(),
+                          out_rows.stride(0), 0, rows, g.hidden, 1.0, None, None, None, None, None, 0, None, 0,
+                          status.err_ptr, stream)
+            return
+        flat, branch = split_heads_outputs(concat_rows(recv, rows), world, g.inner)
+        self._quantized_out(flat, branch if with_branch else None, ws, out_rows, status, stream,
+                            amax_reduce=amax_reduce)
+
+    def _out_sharded(self, ws, with_branch, status, stream) -> torch.Tensor:
+        """All-to-all of the per-head outputs by row block, the output projection on this
+        rank's rows (grouped-K over the receive buffer), all-gather of the rows."""
+        sh = self.shard
+        xchg: RowExchange = ws["xchg"]
+        xchg.exchange()
+        amax_reduce = None
+        if self.precision == "fp8":
+            import torch.distributed as dist
+
+            def amax_reduce(t):
+                dist.all_reduce(t, op=dist.ReduceOp.MAX, group=sh.group)
+
+        return xchg.project_and_gather(
+            lambda recv, rows, out_rows: self.project_rows(ws, with_branch, recv, rows, out_rows, status, stream,
+                                                           amax_reduce))
 
     def forward(self, x: torch.Tensor, layout: VDNLayout, plans: WindowPlanCache, status: _lib.DeviceStatus,
                 *, linear_enabled=True, bridge="alpha", enable_text_state=True, out=None) -> torch.Tensor:
+        ws, linear_active = self.forward_heads(x, layout, plans, status, linear_enabled=linear_enabled,
+                                               bridge=bridge, enable_text_state=enable_text_state)
+        stream = _lib.stream_handle(x.device)
+        if self.shard is not None:
+            full = self._out_sharded(ws, linear_active, status, stream)
+            if out is None:
+                return full
+            out.copy_(full)
+            return out
+        if out is None:
+            out = torch.empty(x.shape[0], self.geo.hidden, device=x.device, dtype=torch.bfloat16)
+        self._out(ws, out, linear_active, status, stream)
+        return out
+
+    def forward_heads(self, x: torch.Tensor, layout: VDNLayout, plans: WindowPlanCache, status: _lib.DeviceStatus,
+                      *, linear_enabled=True, bridge="alpha", enable_text_state=True):
+        """Phases 1-3 (QKV, branch, window attention) for this rank's heads; returns the
+        workspace holding the per-head outputs and whether the branch ran."""
         g = self.geo
         S = x.shape[0]
         if x.dtype != torch.bfloat16 or x.stride(-1) != 1:
@@ -228,19 +335,27 @@ class FusedBlock:
                                 g.dim, g.dim ** -0.5, status,
                                 gate_logits=ws["aux"] if self.enable_gate else None, gate_col0=self.col_gate,
                                 gate_bias=self.gate_bias)
-        if out is None:
-            out = torch.empty(S, g.hidden, device=x.device, dtype=torch.bfloat16)
-        self._out(ws, out, linear_active, status, stream)
-        return out
+        if self.shard is not None:
+            # the grouped operand of the row-split projection always spans the branch columns
+            if linear_active:
+                ws["branch_written"] = True
+            elif ws["branch_written"]:
+                ws["branch"].zero_()
+                ws["branch_written"] = False
+        return ws, linear_active
 
 
 class B200State:
     """Runtime state of one patched model on the B200 path (counterpart of VDNState,
     hybrid.py:33-150).  ``branches`` holds one weight mapping (or an object exposing it
-    as ``.w``) per block."""
+    as ``.w``) per block.
+
+    ``shard_heads``: False (one GPU per block), True (shard the heads over the default
+    torch.distributed group, one process per GPU) or a process group to shard over.
+    Every rank then runs the patched forward on the same x and gets the full output."""
 
     def __init__(self, name, config: Mapping, branches, num_heads, head_dim, *, attention_backend="b200",
-                 projection_precision="bf16", inference=True, weight_maps=None, **_ignored):
+                 projection_precision="bf16", inference=True, weight_maps=None, shard_heads=False, **_ignored):
         if attention_backend not in ATTENTION_BACKENDS:
             raise ValueError(f"unsupported attention backend {attention_backend!r}")
         if projection_precision not in ("bf16", "fp8", "int8"):
@@ -261,6 +376,9 @@ class B200State:
         self.status: dict[str, _lib.DeviceStatus] = {}
         self.forwards = 0
         self.last_attention_backend = None
+        self.shard = None
+        if shard_heads is not False and shard_heads is not None:
+            self.shard = default_shard(self.num_heads, None if shard_heads is True else shard_heads)
 
     def device_status(self, device) -> _lib.DeviceStatus:
         key = str(device)
@@ -276,7 +394,7 @@ class B200State:
                             _weight_of(attn.out_proj), self.weight_maps[index], self.num_heads, self.head_dim,
                             device, precision=self.projection_precision, eps=float(getattr(attn.q_norm, "eps", 1e-6)),
                             enable_gate=bool(cfg.get("enable_softmax_gate", True)),
-                            short_conv=tuple(cfg.get("short_conv", ("k", "v"))))
+                            short_conv=tuple(cfg.get("short_conv", ("k", "v"))), shard=self.shard)
             self.blocks[index] = fb
         return fb
 

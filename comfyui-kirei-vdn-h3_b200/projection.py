@@ -57,8 +57,10 @@ def quantize_rows_int8(x: torch.Tensor, out: QuantizedMatrix | None = None) -> Q
 
 
 def quantize_tensor_fp8(x: torch.Tensor, out: QuantizedMatrix | None = None,
-                        work: torch.Tensor | None = None) -> QuantizedMatrix:
-    """Per-tensor e4m3 of a bf16/fp32 [rows, K] tensor (fp8.py:99-133, per_tensor=True)."""
+                        work: torch.Tensor | None = None, amax_reduce=None) -> QuantizedMatrix:
+    """Per-tensor e4m3 of a bf16/fp32 [rows, K] tensor (fp8.py:99-133, per_tensor=True).
+    ``amax_reduce(amax)``, when given, combines the device amax [1] fp32 in place (an
+    all-reduce MAX over the ranks that each hold some rows of the tensor) before the cast."""
     _lib.require_cuda(x)
     if x.stride(-1) != 1:
         x = x.contiguous()
@@ -71,8 +73,14 @@ def quantize_tensor_fp8(x: torch.Tensor, out: QuantizedMatrix | None = None,
     src = 0 if x.dtype == torch.bfloat16 else 1
     if src == 1 and x.dtype != torch.float32:
         x = x.float()
-    _lib.call("vdn_quant_fp8_tensor", src, x.data_ptr(), x.stride(0), rows, K, out.data.data_ptr(),
-              out.data.stride(0), work.data_ptr(), out.scale.data_ptr(), _stream(x))
+    if amax_reduce is None:
+        _lib.call("vdn_quant_fp8_tensor", src, x.data_ptr(), x.stride(0), rows, K, out.data.data_ptr(),
+                  out.data.stride(0), work.data_ptr(), out.scale.data_ptr(), _stream(x))
+        return out
+    _lib.call("vdn_fp8_amax", src, x.data_ptr(), x.stride(0), rows, K, work.data_ptr(), _stream(x))
+    amax_reduce(work)
+    _lib.call("vdn_fp8_cast", src, x.data_ptr(), x.stride(0), rows, K, work.data_ptr(), out.data.data_ptr(),
+              out.data.stride(0), out.scale.data_ptr(), _stream(x))
     return out
 
 
@@ -101,6 +109,30 @@ def gemm(a, b, *, out=None, out_dtype=torch.bfloat16, alpha=1.0, a2=None, k_spli
               float(alpha), _lib.ptr(dev_scale0), _lib.ptr(dev_scale1), _lib.ptr(row_scale), _lib.ptr(col_scale),
               _lib.ptr(col_bias), int(sigmoid), _lib.ptr(addend), addend.stride(0) if addend is not None else 0,
               st.err_ptr, _stream(a))
+    if status is None:
+        st.raise_if_failed()
+    return out
+
+
+def gemm_grouped_k(a3, b, *, rows=None, out=None, out_dtype=torch.bfloat16, alpha=1.0,
+                   status: _lib.DeviceStatus | None = None, kind=0):
+    """out = a @ b^T where ``a3`` [G, M', Kg] is read as the K-concatenation of its G slabs
+    (first ``rows`` rows of each).  b: [N, G * Kg]."""
+    _lib.require_cuda(a3, b)
+    if a3.ndim != 3 or a3.stride(-1) != 1:
+        raise ValueError("grouped operand must be [groups, rows, kg] with unit inner stride")
+    G, Mp, Kg = a3.shape
+    M = Mp if rows is None else int(rows)
+    N, K = b.shape
+    if K != G * Kg or not 0 < M <= Mp:
+        raise ValueError("grouped operand does not match the weight's K")
+    if out is None:
+        out = torch.empty(M, N, device=a3.device, dtype=out_dtype)
+    okind = {torch.bfloat16: 0, torch.float32: 1, torch.int32: 2}[out.dtype]
+    st = status or _lib.DeviceStatus(a3.device)
+    _lib.call("vdn_gemm_grouped_k", kind, a3.data_ptr(), a3.stride(1), a3.stride(0), G, Kg, b.data_ptr(),
+              b.stride(0), out.data_ptr(), out.stride(0), okind, M, N, float(alpha), None, None, None, None, None,
+              0, None, 0, st.err_ptr, _stream(a3))
     if status is None:
         st.raise_if_failed()
     return out

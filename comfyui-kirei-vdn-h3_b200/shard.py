@@ -1,0 +1,189 @@
+"""Head sharding of the VDN-H3 block over the GPUs of one node.
+
+Every per-head computation of the block is independent: the q/k/v columns, the gate and
+beta columns, the short-conv channels, the alpha / output-gate ``up`` rows, the frame
+statistics, the factor, the scan and the readout.  Rank r of a group of g GPUs owns heads
+[r*H/g, (r+1)*H/g) and computes them over the whole sequence (a head's frame recurrence
+never crosses GPUs).  The ``down`` projections of alpha and the output gate (hidden ->
+head_dim) are replicated.
+
+The per-head outputs [S, 2*H/g*D] (gated softmax | branch readout) are then exchanged:
+
+1. all-to-all by row block: rank r receives rows [r*Sb, (r+1)*Sb) of every rank's heads,
+   as [g][Sb][2*H/g*D] (Sb = ceil(S/g));
+2. the output projection (out_proj + to_out_linear over K = 2*H*D) runs on those Sb rows,
+   reading the receive buffer in place as a grouped-K operand against the output weight
+   whose columns were permuted once into the same rank-major order;
+3. all-gather of the projected rows returns the full [S, hidden] output on every rank,
+   which is what the patched ``attn.forward`` returns (hybrid.py:409-579 semantics).
+
+The reference runs each block on one GPU; this module has no reference counterpart.
+Collectives use ``torch.distributed`` (NCCL over NVLink on the GPU box, gloo in the CPU
+tests); remote data always lands in local HBM before a kernel reads it.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass(frozen=True)
+class HeadShard:
+    """This rank's slice of the heads of one block."""
+
+    rank: int
+    world: int
+    heads: int
+    group: object = None  # torch.distributed process group (None = default group)
+
+    def __post_init__(self):
+        if self.world < 1 or not 0 <= self.rank < self.world:
+            raise ValueError(f"rank {self.rank} outside a group of {self.world}")
+        if self.heads % self.world:
+            raise ValueError(f"{self.heads} heads do not split evenly over {self.world} GPUs")
+
+    @property
+    def heads_local(self) -> int:
+        return self.heads // self.world
+
+    @property
+    def head0(self) -> int:
+        return self.rank * self.heads_local
+
+    @property
+    def head_slice(self) -> slice:
+        return slice(self.head0, self.head0 + self.heads_local)
+
+    def row_block(self, seq_len: int) -> int:
+        return -(-int(seq_len) // self.world)
+
+    def rows_of(self, seq_len: int, rank: int | None = None) -> tuple[int, int]:
+        """(first row, row count) of ``rank``'s block of the output projection."""
+        r = self.rank if rank is None else int(rank)
+        sb = self.row_block(seq_len)
+        r0 = r * sb
+        return r0, max(0, min(sb, int(seq_len) - r0))
+
+
+def qkv_row_index(heads: int, dim: int, head_slice: slice) -> torch.Tensor:
+    """Rows of W_qkv [3*H*D, hidden] that produce the q, k and v columns of the local heads."""
+    inner = heads * dim
+    cols = torch.arange(head_slice.start * dim, head_slice.stop * dim)
+    return torch.cat([cols, cols + inner, cols + 2 * inner])
+
+
+# Branch weights indexed by head (first axis H) or by channel h*D + d (first axis H*D,
+# or the second axis of to_out_linear); everything else (norm, the down projections) is
+# shared by all heads.  Names follow the reference's weight map (weights.py).
+_HEAD_ROWS = ("beta_proj.weight", "alpha.A_log", "softmax_gate.up.weight", "softmax_gate.up.bias")
+_CHANNEL_ROWS = ("alpha.dt_bias", "alpha.up.weight", "output_gate.up.weight", "output_gate.up.bias")
+_CHANNEL_COLS = ("to_out_linear.weight",)
+
+
+def slice_branch_weights(w, heads: int, dim: int, head_slice: slice) -> dict:
+    """The branch weight map restricted to ``head_slice`` (a map for H/g heads).  Quantised
+    ``to_out_linear`` masters are dropped: the row-split projection uses the full matrix."""
+    hs = head_slice
+    cs = slice(hs.start * dim, hs.stop * dim)
+    out = {}
+    for name, t in w.items():
+        if name in _HEAD_ROWS:
+            out[name] = t[hs]
+        elif name in _CHANNEL_ROWS or name.startswith("short_conv."):
+            out[name] = t[cs]
+        elif name in _CHANNEL_COLS:
+            out[name] = t[:, cs]
+        elif name.startswith("to_out_linear."):
+            continue
+        else:
+            out[name] = t
+    return out
+
+
+def rank_major_out_weight(out_w: torch.Tensor, to_out: torch.Tensor | None, heads: int, dim: int,
+                          world: int) -> torch.Tensor:
+    """[W_out | W_to_out] ([hidden, 2*H*D]) with its K columns reordered rank-major:
+    for each rank r, r's heads of W_out, then r's heads of W_to_out -- the order in
+    which the all-to-all receive buffer [g][rows][2*H/g*D] lays K out."""
+    hidden = out_w.shape[0]
+    if to_out is None:
+        to_out = torch.zeros_like(out_w)
+    hl = heads // world
+    parts = []
+    for r in range(world):
+        cs = slice(r * hl * dim, (r + 1) * hl * dim)
+        parts += [out_w[:, cs], to_out[:, cs]]
+    w = torch.cat(parts, 1)
+    assert w.shape == (hidden, 2 * heads * dim)
+    return w
+
+
+class RowExchange:
+    """Buffers and collectives of one sequence length: ``send`` is the rank's per-head
+    output [g*Sb, width] (rows past S stay zero), ``recv`` the all-to-all result
+    [g, Sb, width], ``out`` the gathered projection [g*Sb, hidden]."""
+
+    def __init__(self, shard: HeadShard, seq_len: int, width: int, hidden: int, device, dtype=torch.bfloat16):
+        self.shard = shard
+        self.seq_len = int(seq_len)
+        self.sb = shard.row_block(seq_len)
+        g = shard.world
+        self.send = torch.zeros(g * self.sb, width, device=device, dtype=dtype)
+        self.recv = torch.empty(g, self.sb, width, device=device, dtype=dtype)
+        self.hidden = int(hidden)
+
+    def exchange(self):
+        import torch.distributed as dist
+
+        g = self.shard.world
+        dist.all_to_all_single(self.recv.view(g * self.sb, -1), self.send, group=self.shard.group)
+
+    def project_and_gather(self, project, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Run ``project(recv, rows, out_rows)`` on this rank's rows, then all-gather;
+        returns the [S, hidden] output.  ``project`` is called on every rank, with
+        rows == 0 on a rank past the end of a short sequence, so that collectives it
+        issues (the fp8 amax reduction) stay matched across ranks."""
+        import torch.distributed as dist
+
+        g = self.shard.world
+        if out is None or out.shape != (g * self.sb, self.hidden):
+            out = torch.empty(g * self.sb, self.hidden, device=self.send.device, dtype=self.send.dtype)
+        _, n = self.shard.rows_of(self.seq_len)
+        mine = out[self.shard.rank * self.sb:(self.shard.rank + 1) * self.sb]
+        project(self.recv, n, mine)
+        dist.all_gather_into_tensor(out, mine, group=self.shard.group)
+        return out[:self.seq_len]
+
+
+def concat_rows(recv: torch.Tensor, rows: int) -> torch.Tensor:
+    """[g, Sb, width] -> [rows, g*width]: the grouped-K operand as one matrix (the layout
+    the quantised projections need, and the CPU tests' reading of the operand)."""
+    g, _, w = recv.shape
+    return recv[:, :rows].permute(1, 0, 2).reshape(rows, g * w)
+
+
+def split_heads_outputs(a: torch.Tensor, world: int, inner_local: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Undo the rank-major K order of ``concat_rows``: [rows, g*2*inner_l] ->
+    (flat [rows, H*D], branch [rows, H*D]) in head order."""
+    rows = a.shape[0]
+    v = a.view(rows, world, 2, inner_local)
+    return v[:, :, 0].reshape(rows, world * inner_local), v[:, :, 1].reshape(rows, world * inner_local)
+
+
+def default_shard(heads: int, group=None) -> HeadShard | None:
+    """HeadShard over ``group`` (the default group when None) if torch.distributed is
+    initialised with more than one rank, else None."""
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()):
+        return None
+    world = dist.get_world_size(group)
+    if world <= 1:
+        return None
+    return HeadShard(dist.get_rank(group), world, int(heads), group)
+
+
+__all__ = ["HeadShard", "RowExchange", "concat_rows", "default_shard", "qkv_row_index", "rank_major_out_weight",
+           "slice_branch_weights", "split_heads_outputs"]

@@ -38,6 +38,19 @@ int vdn_gemm(int kind, const void* A, long long lda, const void* A2, long long l
              const float* col_scale, const float* col_bias, int act, const void* addend, long long ld_add,
              int* dev_err, void* stream);
 
+/* vdn_gemm with a grouped-K A operand: A is `groups` slabs of [M, kg] (rows lda elements
+ * apart, slabs group_stride elements apart) read in order as one [M, groups*kg] operand;
+ * kg must be a multiple of the k-block (64 bf16, 128 fp8/int8).  Used for the row-split
+ * output projection of the head-sharded block, reading the all-to-all receive buffer
+ * [ranks][rows][2*heads_per_rank*head_dim] in place.
+ * No reference counterpart: the reference runs one GPU per block (hybrid.py:534-540 is the
+ * projection this feeds). */
+int vdn_gemm_grouped_k(int kind, const void* A, long long lda, long long group_stride, int groups, int kg,
+                       const void* B, long long ldb, void* C, long long ldc, int out_kind, int M, int N,
+                       float alpha, const float* dev_scale0, const float* dev_scale1, const float* row_scale,
+                       const float* col_scale, const float* col_bias, int act, const void* addend,
+                       long long ld_add, int* dev_err, void* stream);
+
 /* Fused QKV projection of x [S, hidden] against [W_qkv; W_side] ([3*inner + n_aux, hidden]):
  * raw q/k/v -> qkv_out [S, 3*inner] bf16; RMSNorm(q), RMSNorm(k) per head with weights
  * norm_w [2, head_dim] fp32 -> qk_norm [S, 2*inner] bf16; side columns -> aux_out [S, n_aux] fp32.
@@ -61,6 +74,15 @@ int vdn_quant_int8_rows(int src_kind, const void* x, long long ldx, int rows, in
  * Replaces: fp8.py:108-133 (quantize_activation, per_tensor=True). */
 int vdn_quant_fp8_tensor(int src_kind, const void* x, long long ldx, int rows, int K, void* q, long long ldq,
                          float* work, float* scale_out, void* stream);
+
+/* The two halves of vdn_quant_fp8_tensor: vdn_fp8_amax zeroes and fills amax (device fp32);
+ * vdn_fp8_cast quantises with a given amax and writes the scale.  Between them the
+ * head-sharded block all-reduces amax (MAX) so a row-split projection uses the scale of
+ * the whole tensor.  Replaces: fp8.py:99-133 (per_tensor=True), split in two steps; the
+ * split itself has no reference counterpart. */
+int vdn_fp8_amax(int src_kind, const void* x, long long ldx, int rows, int K, float* amax, void* stream);
+int vdn_fp8_cast(int src_kind, const void* x, long long ldx, int rows, int K, const float* amax, void* q,
+                 long long ldq, float* scale_out, void* stream);
 
 /* FP8 projection that allocates nothing (no counterpart in the reference: an addition for
  * callers that cannot allocate device memory while they run, e.g. code running inside a

@@ -1,0 +1,163 @@
+"""GPU tests of the head-sharded block.
+
+* On one GPU the ranks are emulated in one process: each rank's FusedBlock runs its heads
+  (phases 1-3), the all-to-all is replayed by copies between the ranks' buffers, and each
+  rank runs its row-split projection.  INT8 must reproduce the unsharded block bit for bit
+  (every per-head value and every projected row is the same arithmetic); bf16 sums the
+  output projection's K in rank-major order, so it is compared within 2e-3.
+* With two or more GPUs, two NCCL ranks run the patched forward (B200State with
+  shard_heads=True) and are compared with the unsharded block and the oracle.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+
+from __graft_entry__ import _Attn, load_package
+from oracle import vdn_oracle as vo
+
+pytestmark = pytest.mark.gpu
+
+pkg = load_package()
+from vdn_b200 import shard as sh  # noqa: E402
+
+DEV = torch.device("cuda:0") if torch.cuda.is_available() else None
+
+
+def rel_l2(got, want):
+    got = got.double().cpu()
+    want = want.double().cpu()
+    return float((got - want).norm() / want.norm())
+
+
+def _block(bw, heads, dim, precision, shard=None):
+    return pkg.FusedBlock(bw.qkv, bw.q_norm, bw.k_norm, bw.out, bw.branch, heads, dim, DEV, precision=precision,
+                          shard=shard)
+
+
+def _emulated_sharded_forward(bw, lay, heads, dim, x, precision, world):
+    plans = pkg.WindowPlanCache()
+    status = pkg.DeviceStatus(DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    blocks = [_block(bw, heads, dim, precision, sh.HeadShard(r, world, heads)) for r in range(world)]
+    parts = [b.forward_heads(x, lay, plans, status) for b in blocks]
+    S = x.shape[0]
+    sb = blocks[0].shard.row_block(S)
+    out = torch.zeros(world * sb, bw.out.shape[0], device=DEV, dtype=torch.bfloat16)
+    for r, b in enumerate(blocks):
+        ws, linear_active = parts[r]
+        recv = ws["xchg"].recv
+        for src in range(world):
+            recv[src].copy_(parts[src][0]["xchg"].send[r * sb:(r + 1) * sb])
+        _, rows = b.shard.rows_of(S)
+        b.project_rows(ws, linear_active, recv, rows, out[r * sb:(r + 1) * sb], status, stream)
+    torch.cuda.synchronize()
+    status.raise_if_failed()
+    return out[:S]
+
+
+GEOMETRIES = {
+    "config0": (vo.CONFIG0, (2,)),
+    "d128_ragged": (dict(text=64, frames=7, grid=(9, 14), heads=4, dim=128, hidden=512), (2, 4)),
+}
+
+
+@pytest.mark.parametrize("precision", ["bf16", "int8"])
+@pytest.mark.parametrize("geom", sorted(GEOMETRIES))
+def test_sharded_block_emulated_on_one_gpu(geom, precision):
+    c, worlds = GEOMETRIES[geom]
+    H, D, hidden = c["heads"], c["dim"], c["hidden"]
+    bw = vo.make_block(5, hidden, H, D)
+    lay = pkg.make_layout(c["text"], c["frames"], c["grid"])
+    x = vo.make_x(5, lay.seq_len, hidden).to(DEV, torch.bfloat16)
+    full = _block(bw, H, D, precision)
+    ref = full.forward(x, lay, pkg.WindowPlanCache(), pkg.DeviceStatus(DEV)).clone()
+    torch.cuda.synchronize()
+    for world in worlds:
+        got = _emulated_sharded_forward(bw, lay, H, D, x, precision, world)
+        if precision == "int8":
+            assert torch.equal(got, ref), f"world {world}: int8 sharded output differs from the unsharded block"
+        else:
+            assert rel_l2(got, ref) < 2e-3, world
+    if precision == "bf16":
+        want = vo.block_forward(x.float().cpu(), bw, vo.config_layout(c), H, D, vo.BranchConfig())
+        assert rel_l2(got, want) < 2e-2
+
+
+def test_grouped_k_gemm_matches_torch():
+    gen = torch.Generator().manual_seed(11)
+    G, Mp, Kg, N, M = 4, 300, 192, 520, 257
+    a3 = (torch.randn(G, Mp, Kg, generator=gen) * 0.5).to(DEV, torch.bfloat16)
+    b = (torch.randn(N, G * Kg, generator=gen) * 0.5).to(DEV, torch.bfloat16)
+    got = pkg.projection.gemm_grouped_k(a3, b, rows=M, out_dtype=torch.float32)
+    want = sh.concat_rows(a3.float(), M) @ b.float().T
+    torch.testing.assert_close(got, want, rtol=1e-4, atol=1e-3)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        pkg_r = load_package()
+        c = dict(text=64, frames=7, grid=(9, 14), heads=4, dim=128, hidden=512)
+        H, D, hidden = c["heads"], c["dim"], c["hidden"]
+        bw = vo.make_block(6, hidden, H, D)
+        lay = pkg_r.make_layout(c["text"], c["frames"], c["grid"])
+        x = vo.make_x(6, lay.seq_len, hidden).to(f"cuda:{rank}", torch.bfloat16)
+        res = {}
+        for precision in ("bf16", "int8", "fp8"):
+            state = pkg_r.B200State("t", {"enable_softmax_gate": True}, [bw.branch], H, D,
+                                    projection_precision=precision, shard_heads=True)
+            fwd = pkg_r.make_vdn_forward(_Attn(bw, H, D), state, 0)
+            with pkg_r.publish_layout(lay):
+                got = pkg_r.run_forward_checked(state, fwd, x)
+            single = pkg_r.B200State("t", {"enable_softmax_gate": True}, [bw.branch], H, D,
+                                     projection_precision=precision)
+            fwd1 = pkg_r.make_vdn_forward(_Attn(bw, H, D), single, 0)
+            with pkg_r.publish_layout(lay):
+                ref = pkg_r.run_forward_checked(single, fwd1, x)
+            torch.cuda.synchronize()
+            res[precision] = (bool(torch.equal(got, ref)), rel_l2(got, ref))
+            if precision == "bf16":
+                want = vo.block_forward(x.float().cpu(), bw, vo.config_layout(c), H, D, vo.BranchConfig())
+                res["oracle"] = rel_l2(got, want)
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sharded_block_on_two_gpus_over_nccl():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, res in results.items():
+        assert res["int8"][0], (rank, res)
+        assert res["fp8"][0], (rank, res)  # the amax all-reduce restores the whole tensor's scale
+        assert res["bf16"][1] < 2e-3, (rank, res)
+        assert res["oracle"] < 2e-2, (rank, res)
