@@ -45,6 +45,21 @@ def peaks():
     return dict(PEAK_FALLBACK), "fallback"
 
 
+def attention_traffic(heads_per_rank: int, heads_total: int):
+    """DRAM bytes (read + write) of one window-attention launch, from the committed ncu
+    summary of the config-1 geometry (scaled by the head count: every head is a separate
+    q/k/v/out slab), or None when the summary is absent."""
+    path = os.path.join(ROOT, "profiles", "window_attention_config1_8heads.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch_40_heads:"):
+                    return float(line.split(":")[1]) * heads_per_rank / 40.0
+    except OSError:
+        pass
+    return None
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled during the timed region."""
 
@@ -389,7 +404,9 @@ def main():
                    "l2": "inputs larger than L2 (x 270 MB, weights 0.36 GB)"},
         "tflop_per_step": flops["total"] / 1e12,
         "roofline": {"kernel": "window_attention_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
-                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None, "peak_source": f"{pk_src} sustained",
+                     "unit": "TFLOP/s", "frac": achieved / peak,
+                     "traffic": attention_traffic(H // world, H) if args.config == 1 else None,
+                     "algorithmic_bytes": lay.seq_len * (H // world) * D * 2 * 4, "peak_source": f"{pk_src} sustained",
                      "kernel_ms": attn_avg, "block_frac": value / world / peak},
         # bytes summed over the ranks (at N > 1 each rank moves its own row block)
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
