@@ -80,6 +80,117 @@ __global__ void __launch_bounds__(128) spatial_conv5_kernel(const __nv_bfloat16*
   }
 }
 
+// Tiled 5x5 depthwise conv.  A persistent CTA walks a contiguous range of tiles (64
+// channels x 8 output rows of one frame, channel-slab-major so the weights change
+// rarely).  Each tile's input rows y0-2 .. y0+9 are staged in shared memory by 16-byte
+// cp.async copies, with the zero padding written in place (two zero columns left and
+// right, zero rows outside the frame), so the inner loop has no bounds checks; the next
+// tile's copies are in flight while this one is computed (two buffers when they fit).
+// Warp w computes output row y0 + w, lane l channels c0 + 2l, 2l + 1: it slides along x
+// keeping the 5x5 window of both channels in registers (5 shared loads per output) and
+// accumulates five independent paired-fp32 chains, one per kernel row.
+constexpr int kConvRows = 8;
+constexpr int kConvCh = 64;
+constexpr int kConvThreads = kConvRows * 32;
+
+__device__ __forceinline__ float2 lds_bf162(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+
+__global__ void __launch_bounds__(kConvThreads, 1)
+    spatial_conv5_tiled_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in, const float* __restrict__ w,
+                               int F, int gh, int gw, int C, __nv_bfloat16* __restrict__ out, long long ld_out,
+                               int stages) {
+  extern __shared__ __align__(16) __nv_bfloat16 conv_smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bands = (gh + kConvRows - 1) / kConvRows;
+  const int per_slab = F * bands;
+  const int n_tiles = (C / kConvCh) * per_slab;
+  const int pitch = gw + 4;  // shared-memory columns per row: image column x sits at x + 2
+  const int buf_elems = (kConvRows + 4) * pitch * kConvCh;
+  const int t0 = (int)((long long)blockIdx.x * n_tiles / gridDim.x);
+  const int t1 = (int)((long long)(blockIdx.x + 1) * n_tiles / gridDim.x);
+  if (t0 >= t1) return;
+
+  auto issue = [&](int t, int buf) {
+    const int slab = t / per_slab, r = t - slab * per_slab;
+    const int f = r / bands, y0 = (r - f * bands) * kConvRows;
+    const int c0 = slab * kConvCh;
+    __nv_bfloat16* dst0 = conv_smem + buf * buf_elems;
+    const int chunks = (kConvRows + 4) * pitch * (kConvCh / 8);
+    for (int i = tid; i < chunks; i += kConvThreads) {
+      const int q = i & 7, px = i >> 3;
+      const int row = px / pitch, col = px - row * pitch;
+      const int yy = y0 - 2 + row, xx = col - 2;
+      __nv_bfloat16* dst = dst0 + px * kConvCh + q * 8;
+      if (yy >= 0 && yy < gh && xx >= 0 && xx < gw)
+        cp_async16(smem_u32(dst), in + ((long long)(f * gh + yy) * gw + xx) * ld_in + c0 + q * 8);
+      else
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    cp_async_commit();
+  };
+
+  float2 wr[5][5];
+  int cur_slab = -1;
+  issue(t0, 0);
+  for (int t = t0; t < t1; ++t) {
+    const int buf = stages == 2 ? ((t - t0) & 1) : 0;
+    if (stages == 1 && t > t0) issue(t, 0);
+    if (stages == 2 && t + 1 < t1) {
+      issue(t + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int slab = t / per_slab, r = t - slab * per_slab;
+    const int f = r / bands, y0 = (r - f * bands) * kConvRows;
+    const int c = slab * kConvCh + 2 * lane;
+    if (slab != cur_slab) {
+#pragma unroll
+      for (int dy = 0; dy < 5; ++dy)
+#pragma unroll
+        for (int dx = 0; dx < 5; ++dx)
+          wr[dy][dx] = make_float2(w[(long long)c * 25 + dy * 5 + dx], w[(long long)(c + 1) * 25 + dy * 5 + dx]);
+      cur_slab = slab;
+    }
+    const int y = y0 + warp;
+    if (y < gh) {
+      // shared row `warp + dy` holds image row y - 2 + dy
+      const __nv_bfloat16* base = conv_smem + buf * buf_elems + warp * pitch * kConvCh + 2 * lane;
+      __nv_bfloat16* orow = out + (long long)(f * gh + y) * gw * ld_out + c;
+      float2 win[5][5];  // win[slot][dy]; slot (x + k) % 5 holds shared column x + k
+#pragma unroll
+      for (int s = 0; s < 5; ++s)
+#pragma unroll
+        for (int dy = 0; dy < 5; ++dy) win[s][dy] = lds_bf162(base + (dy * pitch + s) * kConvCh);
+      for (int x0 = 0; x0 < gw; x0 += 5) {
+#pragma unroll
+        for (int u = 0; u < 5; ++u) {
+          const int x = x0 + u;
+          if (x < gw) {
+            float2 a[5];
+#pragma unroll
+            for (int dy = 0; dy < 5; ++dy) a[dy] = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < 5; ++k)
+#pragma unroll
+              for (int dy = 0; dy < 5; ++dy) a[dy] = fma2(wr[dy][k], win[(u + k) % 5][dy], a[dy]);
+            const float2 s = add2(add2(add2(a[0], a[1]), add2(a[2], a[3])), a[4]);
+            *reinterpret_cast<__nv_bfloat162*>(orow + (long long)x * ld_out) = __floats2bfloat162_rn(s.x, s.y);
+            if (x + 5 < pitch) {
+#pragma unroll
+              for (int dy = 0; dy < 5; ++dy) win[u][dy] = lds_bf162(base + (dy * pitch + x + 5) * kConvCh);
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();  // every warp is done with `buf` before it is refilled
+  }
+}
+
 // Generic odd kernel sizes (kh*kw <= 49): one thread per channel, direct sum.
 __global__ void spatial_conv_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in,
                                     const float* __restrict__ w, int kh, int kw, int gh, int gw, int C,
@@ -107,71 +218,95 @@ __global__ void spatial_conv_kernel(const __nv_bfloat16* __restrict__ in, long l
 
 // ---------------------------------------------------------------------------------
 // 2. Temporal conv + SiLU + optional L2, output FHSD [F, H, T, D] bf16.
-// One warp per (token s, head h), looping over frames with a 5-frame register ring.
-// taps == 0 means no temporal conv (plain activation).
+// One warp per (token s, head h); lane l holds channels h*D + l*D/32 .. +D/32.  Frames
+// are processed in chunks of 16 outputs: the 20 input frames a chunk needs are loaded
+// first (one 8-byte load per lane and frame for D = 128, all independent, so a warp
+// keeps 20 loads in flight instead of one), then the 5-tap conv, SiLU and the L2 norm
+// (a warp reduction) run from registers.  taps == 0 means no temporal conv.
 // ---------------------------------------------------------------------------------
-template <int D>
-__global__ void temporal_act_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in, const float* __restrict__ w,
-                                    int taps, int F, int T, int H, int l2, __nv_bfloat16* __restrict__ out) {
-  constexpr int V = D / 32;  // channels per lane
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (gw >= T * H) return;
-  const int s = gw / H, h = gw % H;
-  const int c0 = h * D + lane * V;
-  float wt[5][V];
-  const int pad = taps / 2;
-  for (int dt = 0; dt < 5; ++dt)
-    for (int i = 0; i < V; ++i) wt[dt][i] = (dt < taps) ? w[(long long)(c0 + i) * taps + dt] : 0.f;
-  auto load = [&](int t, float (&v)[V]) {
-    if (t < 0 || t >= F) {
-#pragma unroll
-      for (int i = 0; i < V; ++i) v[i] = 0.f;
-      return;
-    }
-    const __nv_bfloat16* src = in + ((long long)t * T + s) * ld_in + c0;
-#pragma unroll
-    for (int i = 0; i < V; ++i) v[i] = __bfloat162float(src[i]);
-  };
-  float ring[5][V];
-  if (taps > 0) {
-    for (int k = 0; k < 5; ++k) load(k - pad, ring[k]);
+template <int V>
+struct PackedBf16;
+template <>
+struct PackedBf16<4> {
+  using T = uint2;
+  __device__ static void unpack(T p, float (&v)[4]) {
+    v[0] = __uint_as_float(p.x << 16);
+    v[1] = __uint_as_float(p.x & 0xffff0000u);
+    v[2] = __uint_as_float(p.y << 16);
+    v[3] = __uint_as_float(p.y & 0xffff0000u);
   }
-  for (int t = 0; t < F; ++t) {
-    float y[V];
-    if (taps > 0) {
+  __device__ static T pack(const float (&v)[4]) { return make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3])); }
+};
+template <>
+struct PackedBf16<2> {
+  using T = uint32_t;
+  __device__ static void unpack(T p, float (&v)[2]) {
+    v[0] = __uint_as_float(p << 16);
+    v[1] = __uint_as_float(p & 0xffff0000u);
+  }
+  __device__ static T pack(const float (&v)[2]) { return pack_bf16(v[0], v[1]); }
+};
+
+template <int D>
+__global__ void __launch_bounds__(256) temporal_act_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in,
+                                                           const float* __restrict__ w, int taps, int F, int T,
+                                                           int H, int l2, __nv_bfloat16* __restrict__ out) {
+  constexpr int V = D / 32;  // channels per lane
+  constexpr int kChunk = 16;
+  constexpr int kLoad = kChunk + 4;
+  using P = PackedBf16<V>;
+  const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gwarp >= T * H) return;
+  const int s = gwarp / H, h = gwarp % H;
+  const int c0 = h * D + lane * V;
+  // y_t = sum_dt wt[dt] x_{t - pad + dt}; no conv = one tap of weight 1
+  const int pad = taps / 2;
+  float wt[5][V];
 #pragma unroll
-      for (int i = 0; i < V; ++i) {
-        float a = 0.f;
+  for (int dt = 0; dt < 5; ++dt)
 #pragma unroll
-        for (int dt = 0; dt < 5; ++dt) a += wt[dt][i] * ring[dt][i];
-        y[i] = a;
+    for (int i = 0; i < V; ++i)
+      wt[dt][i] = taps == 0 ? (dt == 0 ? 1.f : 0.f) : (dt < taps ? w[(long long)(c0 + i) * taps + dt] : 0.f);
+  const int span = taps == 0 ? 1 : taps;
+  for (int t0 = 0; t0 < F; t0 += kChunk) {
+    typename P::T raw[kLoad];
+#pragma unroll
+    for (int j = 0; j < kLoad; ++j) {
+      const int tt = t0 - pad + j;
+      if (j < kChunk + span - 1 && tt >= 0 && tt < F)
+        raw[j] = *reinterpret_cast<const typename P::T*>(in + ((long long)tt * T + s) * ld_in + c0);
+      else
+        raw[j] = typename P::T{};
+    }
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i) {
+      const int t = t0 + i;
+      if (t >= F) break;
+      float y[V];
+#pragma unroll
+      for (int v = 0; v < V; ++v) y[v] = 0.f;
+#pragma unroll
+      for (int dt = 0; dt < 5; ++dt) {
+        float x[V];
+        P::unpack(raw[i + dt < kLoad ? i + dt : kLoad - 1], x);
+#pragma unroll
+        for (int v = 0; v < V; ++v) y[v] = fmaf(wt[dt][v], x[v], y[v]);
       }
-    } else {
-      load(t, y);
-    }
-    float ss = 0.f;
+      float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < V; ++i) {
-      y[i] = silu(y[i]);
-      ss += y[i] * y[i];
-    }
-    if (l2) {
+      for (int v = 0; v < V; ++v) {
+        y[v] = silu(y[v]);
+        ss += y[v] * y[v];
+      }
+      if (l2) {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-6f);
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-6f);
 #pragma unroll
-      for (int i = 0; i < V; ++i) y[i] *= inv;
-    }
-    __nv_bfloat16* dst = out + (((long long)t * H + h) * T + s) * D + lane * V;
-#pragma unroll
-    for (int i = 0; i < V; i += 2) *reinterpret_cast<uint32_t*>(dst + i) = pack_bf16(y[i], y[i + 1]);
-    if (taps > 0) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-#pragma unroll
-        for (int i = 0; i < V; ++i) ring[k][i] = ring[k + 1][i];
-      load(t + 1 - pad + 4, ring[4]);
+        for (int v = 0; v < V; ++v) y[v] *= inv;
+      }
+      *reinterpret_cast<typename P::T*>(out + (((long long)t * H + h) * T + s) * D + lane * V) = P::pack(y);
     }
   }
 }
@@ -181,24 +316,37 @@ __global__ void temporal_act_kernel(const __nv_bfloat16* __restrict__ in, long l
 // projection GEMM), mean over the T rows of each frame, then up + dt_bias, softplus.
 // grid F, block 256.  alpha out [F, H, D] fp32.
 // ---------------------------------------------------------------------------------
-__global__ void alpha_gate_kernel(const float* __restrict__ down, long long ld_down, int T, int R,
-                                  const float* __restrict__ w_up, const float* __restrict__ dt_bias,
-                                  const float* __restrict__ a_log, int H, int D, float* __restrict__ alpha) {
-  extern __shared__ float mean[];  // [R] then [256] partials
+constexpr int kAlphaThreads = 512;
+
+__global__ void __launch_bounds__(kAlphaThreads) alpha_gate_kernel(const float* __restrict__ down, long long ld_down,
+                                                                   int T, int R, const float* __restrict__ w_up,
+                                                                   const float* __restrict__ dt_bias,
+                                                                   const float* __restrict__ a_log, int H, int D,
+                                                                   float* __restrict__ alpha) {
+  extern __shared__ float mean[];  // [R] then [kAlphaThreads] partials
   float* part = mean + R;
   const int f = blockIdx.x;
-  // frame mean: thread t sums column t % R over rows t / R, t / R + G, ... (G = 256 / R)
-  const int G = max(1, 256 / R);
-  for (int j0 = 0; j0 < R; j0 += 256 / G) {
-    const int j = j0 + (int)threadIdx.x % (256 / G), r0 = (int)threadIdx.x / (256 / G);
-    float acc = 0.f;
-    if (j < R && r0 < G)
-      for (int s = r0; s < T; s += G) acc += down[((long long)f * T + s) * ld_down + j];
-    part[threadIdx.x] = acc;
+  // frame mean: G = kAlphaThreads / Rc row phases per column chunk of Rc columns; each
+  // thread keeps 8 independent partial sums so 8 loads are in flight
+  const int Rc = R < kAlphaThreads ? R : kAlphaThreads;
+  const int G = kAlphaThreads / Rc;
+  for (int j0 = 0; j0 < R; j0 += Rc) {
+    const int j = j0 + (int)threadIdx.x % Rc, r0 = (int)threadIdx.x / Rc;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (j < R && r0 < G) {
+      const float* col = down + (long long)f * T * ld_down + j;
+      int s = r0;
+      for (; s + 7 * G < T; s += 8 * G) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[u] += col[(long long)(s + u * G) * ld_down];
+      }
+      for (; s < T; s += G) acc[0] += col[(long long)s * ld_down];
+    }
+    part[threadIdx.x] = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
     __syncthreads();
-    if ((int)threadIdx.x < 256 / G && j0 + (int)threadIdx.x < R) {
+    if ((int)threadIdx.x < Rc && j0 + (int)threadIdx.x < R) {
       float tot = 0.f;
-      for (int r = 0; r < G; ++r) tot += part[r * (256 / G) + threadIdx.x];
+      for (int r = 0; r < G; ++r) tot += part[r * Rc + threadIdx.x];
       mean[j0 + threadIdx.x] = tot / (float)T;
     }
     __syncthreads();
@@ -291,8 +439,10 @@ template <int D>
 __global__ void __launch_bounds__(256) spd_inverse_kernel(const float* __restrict__ A, int H, float* __restrict__ inv_out,
                                                           int* __restrict__ info) {
   constexpr int TB = D / 16;
-  __shared__ float colk[D];
-  __shared__ float rowk[D];
+  // pivot column / row of step k in buffer k & 1: one barrier per step suffices, since a
+  // buffer is rewritten two steps later, after every thread has passed the barrier between
+  __shared__ __align__(16) float colk[2][D];
+  __shared__ __align__(16) float rowk[2][D];
   const int h = blockIdx.x, f = blockIdx.y;
   const long long mb = ((long long)f * H + h) * D * D;
   const int ti = threadIdx.x / 16, tj = threadIdx.x % 16;
@@ -306,57 +456,53 @@ __global__ void __launch_bounds__(256) spd_inverse_kernel(const float* __restric
       m[i][j] = 0.5f * (A[mb + (long long)r * D + c] + A[mb + (long long)c * D + r]) + (r == c ? 1.f : 0.f);
     }
   int bad = 0;
-  for (int k = 0; k < D; ++k) {
-    const int kb = k / TB, kr = k % TB;
-    if (tj == kb) {
+  // k = kb * TB + kr: the block kb is a loop variable, the offset kr is unrolled so every
+  // register of m is addressed statically
+  for (int kb = 0; kb < 16 && !bad; ++kb) {
+#pragma unroll
+    for (int kr = 0; kr < TB; ++kr) {
+      const int k = kb * TB + kr;
+      const int pb = kr & 1;
+      if (tj == kb) {
+#pragma unroll
+        for (int i = 0; i < TB; ++i) colk[pb][r0 + i] = m[i][kr];
+      }
+      if (ti == kb) {
+#pragma unroll
+        for (int j = 0; j < TB; ++j) rowk[pb][c0 + j] = m[kr][j];
+      }
+      __syncthreads();
+      const float p = rowk[pb][k];
+      if (!(p > 0.f)) {  // uniform: every thread read the same pivot
+        bad = k + 1;
+        break;
+      }
+      const float ip = 1.0f / p;
+      float a_i[TB], b_j[TB];
+#pragma unroll
+      for (int i = 0; i < TB; ++i) a_i[i] = colk[pb][r0 + i] * ip;
+#pragma unroll
+      for (int j = 0; j < TB; ++j) b_j[j] = rowk[pb][c0 + j];
 #pragma unroll
       for (int i = 0; i < TB; ++i) {
+        const float2 na = make_float2(-a_i[i], -a_i[i]);
 #pragma unroll
-        for (int j = 0; j < TB; ++j)
-          if (j == kr) colk[r0 + i] = m[i][j];
+        for (int j = 0; j < TB; j += 2) {
+          const float2 v = fma2(na, make_float2(b_j[j], b_j[j + 1]), make_float2(m[i][j], m[i][j + 1]));
+          m[i][j] = v.x;
+          m[i][j + 1] = v.y;
+        }
+      }
+      // row k: a_kj / p ; column k: -a_ik / p ; pivot: 1 / p
+      if (ti == kb) {
+#pragma unroll
+        for (int j = 0; j < TB; ++j) m[kr][j] = b_j[j] * ip;
+      }
+      if (tj == kb) {
+#pragma unroll
+        for (int i = 0; i < TB; ++i) m[i][kr] = (r0 + i == k) ? ip : -a_i[i];
       }
     }
-    if (ti == kb) {
-#pragma unroll
-      for (int i = 0; i < TB; ++i)
-        if (i == kr) {
-#pragma unroll
-          for (int j = 0; j < TB; ++j) rowk[c0 + j] = m[i][j];
-        }
-    }
-    __syncthreads();
-    const float p = rowk[k];
-    if (!(p > 0.f)) {  // uniform: every thread read the same pivot
-      bad = k + 1;
-      break;
-    }
-    const float ip = 1.0f / p;
-    float a_i[TB], b_j[TB];
-#pragma unroll
-    for (int i = 0; i < TB; ++i) a_i[i] = colk[r0 + i] * ip;
-#pragma unroll
-    for (int j = 0; j < TB; ++j) b_j[j] = rowk[c0 + j];
-#pragma unroll
-    for (int i = 0; i < TB; ++i)
-#pragma unroll
-      for (int j = 0; j < TB; ++j) m[i][j] -= a_i[i] * b_j[j];
-    // row k: a_kj / p ; column k: -a_ik / p ; pivot: 1 / p
-    if (ti == kb) {
-#pragma unroll
-      for (int i = 0; i < TB; ++i)
-        if (i == kr) {
-#pragma unroll
-          for (int j = 0; j < TB; ++j) m[i][j] = b_j[j] * ip;
-        }
-    }
-    if (tj == kb) {
-#pragma unroll
-      for (int i = 0; i < TB; ++i)
-#pragma unroll
-        for (int j = 0; j < TB; ++j)
-          if (j == kr) m[i][j] = (r0 + i == k) ? ip : -a_i[i];
-    }
-    __syncthreads();
   }
   if (threadIdx.x == 0) info[(long long)f * H + h] = bad;
   const float nan = __int_as_float(0x7fc00000);
@@ -433,6 +579,124 @@ __global__ void __launch_bounds__(256) bidir_scan_kernel(const float* __restrict
     }
 #pragma unroll
     for (int o = 0; o < OUT; ++o) dst_all[mb + (long long)(r0 + r) * D + c0 + o] = s[o];
+  }
+}
+
+// Head-dim-128 scan: one CTA of 512 threads owns the whole 128 x 128 state of one
+// (head, direction), so each frame's inverse crosses L2 once per direction.  Per step:
+//   u = B_t + s o alpha_t   (registers -> shared, stored transposed u_t[k][row])
+//   s = u (I+A_t)^-1        (register-tiled fp32 GEMM from shared memory: every thread
+//                            owns 4 rows x 8 columns, one 16-byte u load and two 16-byte
+//                            inverse loads feed 16 paired FMAs per k)
+// The next frame's inverse is copied into the second shared buffer by cp.async while
+// this frame's product runs, and B_{t+1} is loaded into registers during it.
+constexpr int kScanThreads = 512;
+constexpr int kScanUPitch = 132;  // u_t row pitch (floats): 16-byte aligned, fewer bank conflicts
+
+__global__ void __launch_bounds__(kScanThreads, 1)
+    bidir_scan128_kernel(const float* __restrict__ inv, const float* __restrict__ Bm, const float* __restrict__ alpha,
+                         const float* __restrict__ s0, int F, int H, float* __restrict__ prefix,
+                         float* __restrict__ suffix) {
+  constexpr int D = 128;
+  extern __shared__ __align__(16) float scan_smem[];
+  float* sinv = scan_smem;              // [2][D][D]
+  float* ut = scan_smem + 2 * D * D;    // [D][kScanUPitch]
+  const int h = blockIdx.x, dir = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // warp w: rows 32*(w/4) .. +31, columns 32*(w%4) .. +31; lane: 4 rows x 8 columns
+  const int r = 32 * (warp >> 2) + 4 * (lane >> 2);
+  const int c = 32 * (warp & 3) + 8 * (lane & 3);
+  float* dst_all = dir == 0 ? prefix : suffix;
+  auto frame = [&](int step) { return dir == 0 ? step : F - 1 - step; };
+  auto issue_inv = [&](int step, int buf) {
+    const float* src = inv + ((long long)frame(step) * H + h) * D * D;
+    float* dst = sinv + buf * D * D;
+#pragma unroll
+    for (int i = 0; i < D * D / 4 / kScanThreads; ++i) {
+      const int e = (i * kScanThreads + tid) * 4;
+      cp_async16(smem_u32(dst + e), src + e);
+    }
+    cp_async_commit();
+  };
+  auto load_b = [&](int step, float (&b)[4][8]) {
+    const float* src = Bm + ((long long)frame(step) * H + h) * D * D;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 lo = *reinterpret_cast<const float4*>(src + (r + i) * D + c);
+      const float4 hi = *reinterpret_cast<const float4*>(src + (r + i) * D + c + 4);
+      b[i][0] = lo.x; b[i][1] = lo.y; b[i][2] = lo.z; b[i][3] = lo.w;
+      b[i][4] = hi.x; b[i][5] = hi.y; b[i][6] = hi.z; b[i][7] = hi.w;
+    }
+  };
+  float s[4][8], b[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[i][j] = s0 ? s0[((long long)h * D + r + i) * D + c + j] : 0.f;
+  issue_inv(0, 0);
+  load_b(0, b);
+  for (int step = 0; step < F; ++step) {
+    const int t = frame(step);
+    const int buf = step & 1;
+    const bool more = step + 1 < F;
+    if (more) issue_inv(step + 1, buf ^ 1);
+    // u = B_t + s o alpha_t, stored transposed
+    const float* al = alpha + ((long long)t * H + h) * D + c;
+    const float4 a_lo = *reinterpret_cast<const float4*>(al);
+    const float4 a_hi = *reinterpret_cast<const float4*>(al + 4);
+    const float av[8] = {a_lo.x, a_lo.y, a_lo.z, a_lo.w, a_hi.x, a_hi.y, a_hi.z, a_hi.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 col;
+      col.x = fmaf(s[0][j], av[j], b[0][j]);
+      col.y = fmaf(s[1][j], av[j], b[1][j]);
+      col.z = fmaf(s[2][j], av[j], b[2][j]);
+      col.w = fmaf(s[3][j], av[j], b[3][j]);
+      *reinterpret_cast<float4*>(ut + (c + j) * kScanUPitch + r) = col;
+    }
+    if (more) {
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (more) load_b(step + 1, b);  // in flight during the product
+    float2 acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
+    const float* iv = sinv + buf * D * D + c;
+    const float* uk = ut + r;
+#pragma unroll 4
+    for (int k = 0; k < D; ++k) {
+      const float4 u4 = *reinterpret_cast<const float4*>(uk + k * kScanUPitch);
+      const float4 v0 = *reinterpret_cast<const float4*>(iv + k * D);
+      const float4 v1 = *reinterpret_cast<const float4*>(iv + k * D + 4);
+      const float2 w01 = make_float2(v0.x, v0.y), w23 = make_float2(v0.z, v0.w);
+      const float2 w45 = make_float2(v1.x, v1.y), w67 = make_float2(v1.z, v1.w);
+      const float uu[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 ui = make_float2(uu[i], uu[i]);
+        acc[i][0] = fma2(ui, w01, acc[i][0]);
+        acc[i][1] = fma2(ui, w23, acc[i][1]);
+        acc[i][2] = fma2(ui, w45, acc[i][2]);
+        acc[i][3] = fma2(ui, w67, acc[i][3]);
+      }
+    }
+    float* dst = dst_all + ((long long)t * H + h) * D * D;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s[i][2 * j] = acc[i][j].x;
+        s[i][2 * j + 1] = acc[i][j].y;
+      }
+      *reinterpret_cast<float4*>(dst + (r + i) * D + c) = make_float4(s[i][0], s[i][1], s[i][2], s[i][3]);
+      *reinterpret_cast<float4*>(dst + (r + i) * D + c + 4) = make_float4(s[i][4], s[i][5], s[i][6], s[i][7]);
+    }
+    __syncthreads();  // u_t and this inverse buffer are rewritten next step
   }
 }
 
@@ -555,7 +819,24 @@ int vdn_spatial_conv(const void* in, long long ld_in, const float* w, int kh, in
   auto s = reinterpret_cast<cudaStream_t>(stream);
   const bool paired = kh == 5 && kw == 5 && (C % 2) == 0 && (ld_in % 2) == 0 && (ld_out % 2) == 0 &&
                       (reinterpret_cast<uintptr_t>(in) % 4) == 0 && (reinterpret_cast<uintptr_t>(out) % 4) == 0;
-  if (paired) {
+  // tiled path: 16-byte copies of 64-channel slabs
+  const long long buf_bytes = (long long)(kConvRows + 4) * (gw + 4) * kConvCh * 2;
+  constexpr long long kSmemLimit = 227 * 1024;
+  const bool tiled = paired && (C % kConvCh) == 0 && (ld_in % 8) == 0 && vdn::aligned16(in) &&
+                     buf_bytes <= kSmemLimit;
+  if (tiled) {
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(spatial_conv5_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
+      attr_set = true;
+    }
+    const int stages = 2 * buf_bytes <= kSmemLimit ? 2 : 1;
+    const long long n_tiles = (long long)(C / kConvCh) * F * ((gh + kConvRows - 1) / kConvRows);
+    const int grid = (int)std::min<long long>(n_tiles, vdn::sm_count());
+    spatial_conv5_tiled_kernel<<<grid, kConvThreads, stages * buf_bytes, s>>>(
+        reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, F, gh, gw, C, reinterpret_cast<__nv_bfloat16*>(out),
+        ld_out, stages);
+  } else if (paired) {
     dim3 grid((C / 2 + 127) / 128, gh, F);
     spatial_conv5_kernel<<<grid, 128, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, gh, gw, C,
                                               reinterpret_cast<__nv_bfloat16*>(out), ld_out);
@@ -573,7 +854,11 @@ int vdn_temporal_act(const void* in, long long ld_in, const float* w, int taps, 
                      int l2norm, void* out, void* stream) {
   if (!in || !out || (taps != 0 && taps != 1 && taps != 3 && taps != 5) || (taps && !w)) return vdn::kBadArgument;
   if (D != 64 && D != 128) return vdn::kUnsupported;
-  if (reinterpret_cast<uintptr_t>(out) & 3) return vdn::kMisaligned;  // paired bf16 stores
+  // one D/32-channel vector per lane: 8-byte (D = 128) or 4-byte (D = 64) loads and stores
+  const int vec_bytes = D / 16;
+  if ((reinterpret_cast<uintptr_t>(out) % vec_bytes) || (reinterpret_cast<uintptr_t>(in) % vec_bytes) ||
+      ((ld_in * 2) % vec_bytes))
+    return vdn::kMisaligned;
   const long long warps = (long long)T * H;
   const int blocks = (int)((warps * 32 + 255) / 256);
   auto s = reinterpret_cast<cudaStream_t>(stream);
@@ -592,8 +877,9 @@ int vdn_alpha_gate(const float* down, long long ld_down, int F, int T, int R, co
                    const float* dt_bias, const float* a_log, int H, int D, float* alpha, void* stream) {
   if (!down || !w_up || !dt_bias || !a_log || !alpha || F <= 0 || T <= 0 || R <= 0) return vdn::kBadArgument;
   if (R > 4096) return vdn::kUnsupported;
-  dim3 grid(F, (H * D + 255) / 256);
-  alpha_gate_kernel<<<grid, 256, (R + 256) * sizeof(float), reinterpret_cast<cudaStream_t>(stream)>>>(
+  dim3 grid(F, (H * D + kAlphaThreads - 1) / kAlphaThreads);
+  alpha_gate_kernel<<<grid, kAlphaThreads, (R + kAlphaThreads) * sizeof(float),
+                      reinterpret_cast<cudaStream_t>(stream)>>>(
       down, ld_down, T, R, w_up, dt_bias, a_log, H, D, alpha);
   return vdn::launch_status();
 }
@@ -647,9 +933,16 @@ int vdn_bidir_scan(const float* inv, const float* B, const float* alpha, const f
   auto s = reinterpret_cast<cudaStream_t>(stream);
   constexpr int RB = 16;
   if (D == 128) {
-    const size_t smem = (size_t)(128 * 128 + RB * 128) * sizeof(float);
-    cudaFuncSetAttribute(bidir_scan_kernel<128, RB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    bidir_scan_kernel<128, RB><<<dim3(H, 2, 128 / RB), 256, smem, s>>>(inv, B, alpha, s0, F, H, prefix, suffix);
+    // 16-byte vector access to B, alpha, the states and the inverse
+    if (!vdn::aligned16(B) || !vdn::aligned16(alpha) || !vdn::aligned16(prefix) || !vdn::aligned16(suffix))
+      return vdn::kMisaligned;
+    const size_t smem = (size_t)(2 * 128 * 128 + 128 * kScanUPitch) * sizeof(float);
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(bidir_scan128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      attr_set = true;
+    }
+    bidir_scan128_kernel<<<dim3(H, 2), kScanThreads, smem, s>>>(inv, B, alpha, s0, F, H, prefix, suffix);
   } else if (D == 64) {
     const size_t smem = (size_t)(64 * 64 + 2 * RB * 64) * sizeof(float);
     bidir_scan_kernel<64, 2 * RB><<<dim3(H, 2, 64 / (2 * RB)), 256, smem, s>>>(inv, B, alpha, s0, F, H, prefix,

@@ -212,6 +212,30 @@ def test_conv_features_match_oracle():
     assert rel_l2(ws.qf, want_q) < 5e-3
 
 
+@pytest.mark.parametrize("F,gh,gw,C,pitch_mult", [
+    (3, 22, 38, 192, 3),   # config-1 frame grid, three 64-channel slabs, strided rows (double-buffered tiles)
+    (2, 9, 97, 128, 1),    # wide rows: one shared-memory buffer
+    (2, 7, 11, 96, 2),     # C not a multiple of 64: the untiled paired kernel
+    (1, 3, 4, 64, 1),      # frame smaller than the 5x5 window
+])
+def test_spatial_conv_matches_torch_conv2d(F, gh, gw, C, pitch_mult):
+    g = torch.Generator().manual_seed(F * 1000 + gw)
+    rows = F * gh * gw
+    base = torch.randn(rows, C * pitch_mult, generator=g).to(torch.bfloat16)
+    x = base[:, :C]
+    w = torch.randn(C, 1, 5, 5, generator=g) * 0.2
+    xd, wd = base.to(DEV), w.reshape(C, 25).contiguous().to(DEV)
+    out = torch.empty(rows, C, device=DEV, dtype=torch.bfloat16)
+    pkg._lib.call("vdn_spatial_conv", xd.data_ptr(), xd.stride(0), wd.data_ptr(), 5, 5, F, gh, gw, C, out.data_ptr(),
+                  out.stride(0), pkg._lib.stream_handle(DEV))
+    torch.cuda.synchronize()
+    img = x.double().reshape(F, gh, gw, C).permute(0, 3, 1, 2)
+    want = torch.nn.functional.conv2d(img, w.double(), padding=2, groups=C).permute(0, 2, 3, 1).reshape(rows, C)
+    # one bf16 rounding of the output: ~2^-9 relative per element
+    assert rel_l2(out, want) < 3e-3
+    assert float((out.double().cpu() - want).abs().max()) < 2e-2 * float(want.abs().max())
+
+
 def test_statistics_factor_scan_match_oracle_and_report_non_spd():
     Fb, H, T, D = 5, 3, 70, 128
     g = torch.Generator().manual_seed(50)
