@@ -8,7 +8,8 @@
 //                        (branch.py:780, :754-758) and the RMSNorm(D) x sigmoid(G + b) epilogue
 //                        (branch.py:494-530) from TMEM: the output-gate up-projection never
 //                        touches HBM.
-// One warpgroup per CTA (thread = TMEM lane = tile row); thread 0 issues TMA and MMA.
+// Statistics: one warpgroup per CTA (thread = TMEM lane = tile row), thread 0 issues TMA
+// and MMA.  Readout: warp-specialised, see below.
 #include "host_common.h"
 #include "sm100.cuh"
 
@@ -158,14 +159,27 @@ __global__ void __launch_bounds__(128, 1)
 }
 
 // ------------------------------------------------------------------------------- readout
-// smem: state (32 KB, K-major), W_og_up rows of this head (32 KB), Q tile, og-down tile.
+// Warp-specialised and pipelined (256 threads):
+//   warp 0      TMA producer: the output-gate up rows of the current head (once per head,
+//               the CTA walks its units head-major), and per 128-token tile the Q tile and
+//               the og-down tile into one of two stages;
+//   warp 1      MMA issuer: R = Q S^T and G = og_down W_up^T into one of two TMEM
+//               accumulator pairs (2 x 256 columns), so tile i+1 is multiplied while the
+//               epilogue drains tile i;
+//   warps 2-3   state builders: gather + alpha bridge of the NEXT unit's bf16 state into
+//               the second state buffer while the current unit's tiles run;
+//   warps 4-11  epilogue (TMEM lane = token row, two warps per lane quadrant, one per
+//               64-column half): bf16(R) -> RMSNorm x norm_w -> bf16 -> x sigmoid(G + b)
+//               -> 16-byte stores.
+// smem: 2 state buffers, W_up, 2 stages x (Q, og-down) = 7 x 32 KB.
 struct ReadoutSmem {
-  static constexpr int kS = 0, kW = kTile, kQ = 2 * kTile, kG = 3 * kTile, kBar = 4 * kTile;
-  static constexpr int kDec = kBar + 256;           // 2 x D floats
-  static constexpr int kBytes = kDec + 2 * D * 4 + 1024;
+  static constexpr int kS = 0, kW = 2 * kTile, kQG = 3 * kTile, kBar = 7 * kTile;
+  static constexpr int kSsq = kBar + 256;               // epilogue partial sums [2 acc][2 halves][128 rows]
+  static constexpr int kBytes = kSsq + 2 * 2 * 128 * 4;  // 231,680 B: no room for alignment slack
 };
+constexpr int kReadoutThreads = 384;  // 12 warps: producer, MMA, 2 state builders, 8 epilogue
 
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kReadoutThreads, 1)
     readout_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tg,
                       const __grid_constant__ CUtensorMap tw, int F, int H, int T, const float* __restrict__ prefix,
                       const float* __restrict__ suffix, const float* __restrict__ alpha, const float* __restrict__ s0,
@@ -173,23 +187,36 @@ __global__ void __launch_bounds__(128, 1)
                       const float* __restrict__ norm_w, const float* __restrict__ og_bias,
                       __nv_bfloat16* __restrict__ out, long long ld_out, long long out_row0, int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + ReadoutSmem::kBar);  // [0] w, [1] tile, [2] mma
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 4);
+  // The layout uses the whole 227 KB, so the dynamic window must start 1024-aligned (it
+  // does when the kernel has no static shared memory); otherwise report and leave.
+  if (smem_u32(smem_raw) & 1023) {
+    if (threadIdx.x == 0) atomicExch(err, kErrWaitOther);
+    return;
+  }
+  uint8_t* smem = smem_raw;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + ReadoutSmem::kBar);
+  uint64_t* qg_full = bar;        // [2]
+  uint64_t* qg_empty = bar + 2;   // [2]
+  uint64_t* s_full = bar + 4;     // [2]
+  uint64_t* s_empty = bar + 6;    // [2]
+  uint64_t* acc_full = bar + 8;   // [2]
+  uint64_t* acc_empty = bar + 10; // [2], 8 epilogue warps
+  uint64_t* w_full = bar + 12;
+  uint64_t* w_empty = bar + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* dec_b = reinterpret_cast<float*>(smem + ReadoutSmem::kDec);
-  float* dec_a = dec_b + D;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int i = 0; i < 3; ++i) mbar_init(smem_u32(&bar[i]), 1);
+    for (int i = 0; i < 14; ++i) mbar_init(smem_u32(&bar[i]), (i == 10 || i == 11) ? 8 : 1);
     *abort_flag = 0;
+    abort_flag[2] = 1;  // epilogue "go" flag
     fence_mbar_init();
     tma_prefetch(&tq);
     tma_prefetch(&tg);
     tma_prefetch(&tw);
   }
-  if (warp == 0) {
-    tmem_alloc(smem_u32(tmem_slot), 256);
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -197,145 +224,252 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t sS = smem_u32(smem + ReadoutSmem::kS), sW = smem_u32(smem + ReadoutSmem::kW);
-  const uint32_t sQ = smem_u32(smem + ReadoutSmem::kQ), sG = smem_u32(smem + ReadoutSmem::kG);
-  constexpr uint32_t idesc = make_idesc(1, 1, 1, 0, 0, 128, 128);
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t sQG = smem_u32(smem + ReadoutSmem::kQG);
+  // units (f, h) head-major, a contiguous range per CTA so W_up changes rarely
   const int units = F * H;
+  const int u0 = (int)((long long)blockIdx.x * units / gridDim.x);
+  const int u1 = (int)((long long)(blockIdx.x + 1) * units / gridDim.x);
   const int ntile = (T + kRows - 1) / kRows;
-  int nw = 0, nt = 0;  // completed phases of bar[0] and bar[1]/bar[2]
-  bool ok = true;
-  for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
-    const int f = unit / H, h = unit % H;
-    if (tid == 0) {  // output-gate up rows of this head: W_up[h*D + v][j], K-major
-      mbar_arrive_expect_tx(smem_u32(&bar[0]), kTile);
-      for (int b = 0; b < 2; ++b) tma_load_2d(sW + b * kBlk, &tw, smem_u32(&bar[0]), b * 64, h * D);
-    }
-    // alpha-bridge decays (branch.py:385-390)
-    const int raw_lo = lo_arr[f], raw_hi = hi_arr[f];
-    const int lo = max(raw_lo, 0), hi = min(raw_hi, F - 1);
-    const bool has_before = raw_lo - 1 >= 0, has_after = raw_hi + 1 < F;
-    {
-      float lb = 0.f, la = 0.f;
-      if (use_alpha) {
-        for (int j = lo; j <= f; ++j) lb += __logf(fmaxf(alpha[((long long)j * H + h) * D + tid], 1e-12f));
-        for (int j = f; j <= hi; ++j) la += __logf(fmaxf(alpha[((long long)j * H + h) * D + tid], 1e-12f));
-      }
-      dec_b[tid] = __expf(lb);
-      dec_a[tid] = __expf(la);
-    }
-    __syncthreads();
-    const float* pb = has_before ? prefix + ((long long)(lo - 1) * H + h) * D * D : (s0 ? s0 + (long long)h * D * D : nullptr);
-    const float* pa = has_after ? suffix + ((long long)(hi + 1) * H + h) * D * D : (s0 ? s0 + (long long)h * D * D : nullptr);
-    // state[v][k] in bf16 (branch.py:396 casts to the activation dtype), K-major swizzled
-    for (int i = 0; i < 16; ++i) {
-      const int e = tid + 128 * i;
-      const int v = e >> 4, c = e & 15;  // 16 chunks of 8 k per row
-      float val[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) val[u] = 0.f;
-      if (pb) {
-        const float4 a0 = *reinterpret_cast<const float4*>(pb + v * D + c * 8);
-        const float4 a1 = *reinterpret_cast<const float4*>(pb + v * D + c * 8 + 4);
-        const float t[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-        for (int u = 0; u < 8; ++u) val[u] += t[u] * dec_b[c * 8 + u];
-      }
-      if (pa) {
-        const float4 a0 = *reinterpret_cast<const float4*>(pa + v * D + c * 8);
-        const float4 a1 = *reinterpret_cast<const float4*>(pa + v * D + c * 8 + 4);
-        const float t[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-        for (int u = 0; u < 8; ++u) val[u] += t[u] * dec_a[c * 8 + u];
-      }
-      const uint32_t addr = sS + (c >> 3) * kBlk + v * 128 + (((c & 7) ^ (v & 7)) << 4);
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pack_bf16(val[0], val[1])),
-                   "r"(pack_bf16(val[2], val[3])), "r"(pack_bf16(val[4], val[5])), "r"(pack_bf16(val[6], val[7]))
-                   : "memory");
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (!mbar_wait(smem_u32(&bar[0]), nw & 1, abort_flag, err, kErrWaitOther)) break;
-    ++nw;
-    for (int t = 0; t < ntile; ++t, ++nt) {
-      if (tid == 0) {
-        mbar_arrive_expect_tx(smem_u32(&bar[1]), 2 * kTile);
-        for (int b = 0; b < 2; ++b) {
-          tma_load_2d(sQ + b * kBlk, &tq, smem_u32(&bar[1]), b * 64, unit * T + t * kRows);  // FHSD rows
-          tma_load_2d(sG + b * kBlk, &tg, smem_u32(&bar[1]), b * 64, f * T + t * kRows);     // branch rows
+  auto head_of = [&](int u) { return u / F; };
+  auto frame_of = [&](int u) { return u - (u / F) * F; };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0, w_waits = 0;
+      for (int u = u0; u < u1; ++u) {
+        const int h = head_of(u), f = frame_of(u);
+        if (u == u0 || h != head_of(u - 1)) {
+          if (u != u0 && !mbar_wait(smem_u32(w_empty), (w_waits++) & 1, abort_flag, err, kErrWaitProducer)) break;
+          mbar_arrive_expect_tx(smem_u32(w_full), kTile);
+          for (int b = 0; b < 2; ++b) tma_load_2d(sW + b * kBlk, &tw, smem_u32(w_full), b * 64, h * D);
         }
-      }
-      if (!mbar_wait(smem_u32(&bar[1]), nt & 1, abort_flag, err, kErrWaitOther)) {
-        ok = false;
-        break;
-      }
-      if (tid == 0) {
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k >> 2) * kBlk + (k & 3) * 32;
-          mma_f16(tmem, make_sdesc(sQ + off, 16, 1024), make_sdesc(sS + off, 16, 1024), idesc, k > 0 ? 1u : 0u);
-          mma_f16(tmem + 128, make_sdesc(sG + off, 16, 1024), make_sdesc(sW + off, 16, 1024), idesc,
-                  k > 0 ? 1u : 0u);
-        }
-        tc_commit(smem_u32(&bar[2]));
-      }
-      if (!mbar_wait(smem_u32(&bar[2]), nt & 1, abort_flag, err, kErrWaitOther)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // epilogue: R -> bf16 -> RMSNorm x norm_w -> bf16 -> x sigmoid(G + b)
-      uint32_t r[D];
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c)
-        tmem_ld32(tmem + lane_base + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
-      tmem_ld_wait();
-      float ss = 0.f;
-#pragma unroll
-      for (int i = 0; i < D; ++i) {
-        const float x = bf16_round(__uint_as_float(r[i]));
-        r[i] = __float_as_uint(x);
-        ss += x * x;
-      }
-      const float inv = rsqrtf(ss / (float)D + 1e-6f);
-      const int tok = t * kRows + tid;
-      __nv_bfloat16* dst = out + (out_row0 + (long long)f * T + tok) * ld_out + h * D;
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t gr[32];
-        tmem_ld32(tmem + lane_base + 128 + c * 32, gr);
-        tmem_ld_wait();
-        if (tok < T) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            float o[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int v = c * 32 + i + u;
-              const float nv = bf16_round(__uint_as_float(r[v]) * inv * norm_w[v]);
-              o[u] = nv * sigm(__uint_as_float(gr[i + u]) + og_bias[h * D + v]);
-            }
-            uint4 pk;
-            pk.x = pack_bf16(o[0], o[1]);
-            pk.y = pack_bf16(o[2], o[3]);
-            pk.z = pack_bf16(o[4], o[5]);
-            pk.w = pack_bf16(o[6], o[7]);
-            *reinterpret_cast<uint4*>(dst + c * 32 + i) = pk;
+        bool ok = true;
+        for (int t = 0; t < ntile; ++t) {
+          if (!mbar_wait(smem_u32(&qg_empty[stage]), ph ^ 1, abort_flag, err, kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sq = sQG + stage * 2 * kTile, sg = sq + kTile;
+          mbar_arrive_expect_tx(smem_u32(&qg_full[stage]), 2 * kTile);
+          for (int b = 0; b < 2; ++b) {
+            tma_load_2d(sq + b * kBlk, &tq, smem_u32(&qg_full[stage]), b * 64, ((f * H + h) * T) + t * kRows);
+            tma_load_2d(sg + b * kBlk, &tg, smem_u32(&qg_full[stage]), b * 64, f * T + t * kRows);
+          }
+          if (++stage == 2) {
+            stage = 0;
+            ph ^= 1;
           }
         }
+        if (!ok) break;
       }
-      tc_fence_before();
-      __syncthreads();  // smem tiles and TMEM are reused by the next tile
     }
-    __syncthreads();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(1, 1, 1, 0, 0, 128, 128);
+      int stage = 0, acc = 0, sb = 0;
+      uint32_t ph = 0, acc_ph = 0, w_waits = 0;
+      bool ok = true;
+      for (int u = u0; u < u1 && ok; ++u) {
+        const int h = head_of(u);
+        const bool last_of_head = (u + 1 == u1) || head_of(u + 1) != h;
+        if (u == u0 || h != head_of(u - 1)) {
+          if (!mbar_wait(smem_u32(w_full), (w_waits++) & 1, abort_flag, err, kErrWaitMma)) break;
+        }
+        // state buffer sb serves units u0 + sb, u0 + sb + 2, ...
+        if (!mbar_wait(smem_u32(&s_full[sb]), ((u - u0) >> 1) & 1, abort_flag, err, kErrWaitMma)) break;
+        const uint32_t ss = sS + sb * kTile;
+        for (int t = 0; t < ntile; ++t) {
+          if (!mbar_wait(smem_u32(&acc_empty[acc]), acc_ph ^ 1, abort_flag, err, kErrWaitMma) ||
+              !mbar_wait(smem_u32(&qg_full[stage]), ph, abort_flag, err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sq = sQG + stage * 2 * kTile, sg = sq + kTile;
+          const uint32_t d = tmem + acc * 256;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t off = (k >> 2) * kBlk + (k & 3) * 32;
+            mma_f16(d, make_sdesc(sq + off, 16, 1024), make_sdesc(ss + off, 16, 1024), idesc, k > 0 ? 1u : 0u);
+            mma_f16(d + 128, make_sdesc(sg + off, 16, 1024), make_sdesc(sW + off, 16, 1024), idesc,
+                    k > 0 ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&qg_empty[stage]));
+          tc_commit(smem_u32(&acc_full[acc]));
+          if (t == ntile - 1) {
+            tc_commit(smem_u32(&s_empty[sb]));
+            if (last_of_head) tc_commit(smem_u32(w_empty));
+          }
+          if (++stage == 2) {
+            stage = 0;
+            ph ^= 1;
+          }
+          if (++acc == 2) {
+            acc = 0;
+            acc_ph ^= 1;
+          }
+        }
+        sb ^= 1;
+      }
+    }
+  } else if (warp < 4) {
+    // state builders (64 threads): state[v][k] = bf16(prefix[v][k] dec_b[k] + suffix[v][k] dec_a[k])
+    // The 64 builders synchronise on named barrier 1; builder 0 alone waits on the
+    // mbarrier and publishes the outcome in shared memory, so a timed-out wait makes all
+    // 64 leave together instead of stranding some at the named barrier.
+    const int bt = tid - 64;
+    volatile int* go = reinterpret_cast<volatile int*>(abort_flag + 1);
+    int sb = 0;
+    for (int u = u0; u < u1; ++u) {
+      const int h = head_of(u), f = frame_of(u);
+      if (bt == 0)
+        *go = mbar_wait(smem_u32(&s_empty[sb]), (((u - u0) >> 1) & 1) ^ 1, abort_flag, err, kErrWaitOther) ? 1 : 0;
+      asm volatile("bar.sync 1, 64;" ::: "memory");
+      if (!*go) break;
+      // alpha-bridge decays (branch.py:385-390) of this thread's fixed chunk of 8 k
+      // (every element it writes has k = (bt & 15) * 8 + q)
+      const int raw_lo = lo_arr[f], raw_hi = hi_arr[f];
+      const int lo = max(raw_lo, 0), hi = min(raw_hi, F - 1);
+      const bool has_before = raw_lo - 1 >= 0, has_after = raw_hi + 1 < F;
+      const int kc = (bt & 15) * 8;
+      float dec_b[8], dec_a[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float lb = 0.f, la = 0.f;
+        if (use_alpha) {
+          for (int j = lo; j <= f; ++j) lb += __logf(fmaxf(alpha[((long long)j * H + h) * D + kc + q], 1e-12f));
+          for (int j = f; j <= hi; ++j) la += __logf(fmaxf(alpha[((long long)j * H + h) * D + kc + q], 1e-12f));
+        }
+        dec_b[q] = __expf(lb);
+        dec_a[q] = __expf(la);
+      }
+      const float* pb = has_before ? prefix + ((long long)(lo - 1) * H + h) * D * D
+                                   : (s0 ? s0 + (long long)h * D * D : nullptr);
+      const float* pa = has_after ? suffix + ((long long)(hi + 1) * H + h) * D * D
+                                  : (s0 ? s0 + (long long)h * D * D : nullptr);
+      const uint32_t ss = sS + sb * kTile;
+#pragma unroll 4
+      for (int i = 0; i < 32; ++i) {
+        const int e = bt + 64 * i;
+        const int v = e >> 4, c = e & 15;  // 16 chunks of 8 k per row
+        float val[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) val[q] = 0.f;
+        if (pb) {
+          const float4 a0 = *reinterpret_cast<const float4*>(pb + v * D + c * 8);
+          const float4 a1 = *reinterpret_cast<const float4*>(pb + v * D + c * 8 + 4);
+          const float tv[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+          for (int q = 0; q < 8; ++q) val[q] += tv[q] * dec_b[q];
+        }
+        if (pa) {
+          const float4 a0 = *reinterpret_cast<const float4*>(pa + v * D + c * 8);
+          const float4 a1 = *reinterpret_cast<const float4*>(pa + v * D + c * 8 + 4);
+          const float tv[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+          for (int q = 0; q < 8; ++q) val[q] += tv[q] * dec_a[q];
+        }
+        const uint32_t addr = ss + (c >> 3) * kBlk + v * 128 + (((c & 7) ^ (v & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pack_bf16(val[0], val[1])),
+                     "r"(pack_bf16(val[2], val[3])), "r"(pack_bf16(val[4], val[5])), "r"(pack_bf16(val[6], val[7]))
+                     : "memory");
+      }
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 1, 64;" ::: "memory");
+      if (bt == 0) mbar_arrive(smem_u32(&s_full[sb]));
+      sb ^= 1;
+    }
+  } else {
+    // epilogue: 8 warps; warp w reads TMEM lane quadrant w % 4 (32 token rows) and column
+    // half ch = (w - 4) / 4 (64 of the 128 values).  The RMSNorm sum of squares of a row is
+    // combined across the two halves through shared memory (named barrier 2, 256 threads).
+    const int quad = warp & 3, ch = (warp - 4) >> 2;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    float* ssp = reinterpret_cast<float*>(smem + ReadoutSmem::kSsq);  // [2 acc][2 halves][128 rows]
+    volatile int* epi_go = reinterpret_cast<volatile int*>(abort_flag + 2);
+    const float* nw = norm_w + ch * 64;
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    bool ok = true;
+    for (int u = u0; u < u1 && ok; ++u) {
+      const int h = head_of(u), f = frame_of(u);
+      const float* bias = og_bias + h * D + ch * 64;
+      for (int t = 0; t < ntile; ++t) {
+        // warp-uniform wait; a failed wait still joins the named barrier, then all leave
+        const bool okw = __all_sync(0xffffffffu,
+                                    mbar_wait(smem_u32(&acc_full[acc]), acc_ph, abort_flag, err, kErrWaitEpilogue));
+        uint32_t r[64];
+        float ssq = 0.f;
+        const uint32_t tb = tmem + lane_base + acc * 256 + ch * 64;
+        if (okw) {
+          tc_fence_after();
+          tmem_ld32(tb, *reinterpret_cast<uint32_t(*)[32]>(r));
+          tmem_ld32(tb + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const float x = bf16_round(__uint_as_float(r[i]));
+            r[i] = __float_as_uint(x);
+            ssq = fmaf(x, x, ssq);
+          }
+          ssp[(acc * 2 + ch) * 128 + row] = ssq;
+        } else {
+          *epi_go = 0;
+        }
+        asm volatile("bar.sync 2, 256;" ::: "memory");
+        if (!*epi_go) {
+          ok = false;
+          break;
+        }
+        const float* sp = ssp + acc * 2 * 128 + row;
+        const float inv = rsqrtf((sp[0] + sp[128]) / (float)D + 1e-6f);
+        const int tok = t * kRows + row;
+        __nv_bfloat16* dst = out + (out_row0 + (long long)f * T + tok) * ld_out + h * D + ch * 64;
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t gr[32];
+          tmem_ld32(tb + 128 + c2 * 32, gr);
+          tmem_ld_wait();
+          if (c2 == 1) {  // every TMEM read of this accumulator is done
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc]));
+          }
+          if (tok < T) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              float o[8];
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const int v = c2 * 32 + i + q;
+                const float nv = bf16_round(__uint_as_float(r[v]) * inv * nw[v]);
+                const float e = __expf(-(__uint_as_float(gr[i + q]) + bias[v]));
+                o[q] = __fdividef(nv, 1.0f + e);  // nv * sigmoid(g + b)
+              }
+              uint4 pk;
+              pk.x = pack_bf16(o[0], o[1]);
+              pk.y = pack_bf16(o[2], o[3]);
+              pk.z = pack_bf16(o[4], o[5]);
+              pk.w = pack_bf16(o[6], o[7]);
+              *reinterpret_cast<uint4*>(dst + c2 * 32 + i) = pk;
+            }
+          }
+        }
+        if (++acc == 2) {
+          acc = 0;
+          acc_ph ^= 1;
+        }
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
   if (*abort_flag) abort_drain();
-  if (warp == 0) {
+  if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -399,7 +533,7 @@ int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, cons
   }
   const int units = F * H;
   const int grid = units < vdn::sm_count() ? units : vdn::sm_count();
-  readout_tc_kernel<<<grid, 128, ReadoutSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
+  readout_tc_kernel<<<grid, kReadoutThreads, ReadoutSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
       tq, tg, tw, F, H, T, prefix, suffix, alpha, s0, lo, hi, use_alpha, norm_w, og_bias,
       reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0, dev_err);
   return vdn::launch_status();
