@@ -11,6 +11,7 @@ CPU or library fallback.
 from . import _lib, projection, shard
 from ._lib import DeviceStatus
 from .branch import B200LinearBranch, cholesky_runtime_scope
+from .host_io import HostStreamer
 from .hybrid import B200State, FusedBlock, make_vdn_forward, run_forward_checked
 from .layout import (ANCHOR_FRAME_MODES, VDNLayout, current_layout, full_coverage, make_layout, publish_layout,
                      window_bounds, with_window)
@@ -20,7 +21,7 @@ from .shard import HeadShard
 from .window import WindowPlanCache, build_window_plan, window_softmax_b200
 
 __all__ = [
-    "ANCHOR_FRAME_MODES", "B200LinearBranch", "B200State", "DeviceStatus", "FusedBlock", "HeadShard", "VDNLayout",
+    "ANCHOR_FRAME_MODES", "B200LinearBranch", "B200State", "DeviceStatus", "FusedBlock", "HeadShard", "HostStreamer", "VDNLayout",
     "WindowPlanCache", "gemm_grouped_k",
     "build_window_plan", "cholesky_runtime_scope", "current_layout", "full_coverage", "gemm", "make_layout",
     "make_vdn_forward", "prepare_projection_maps", "project", "publish_layout", "quantize_rows_int8",

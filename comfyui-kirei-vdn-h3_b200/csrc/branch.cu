@@ -19,7 +19,9 @@
 namespace vdn {
 namespace branch {
 
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+// x * sigmoid(x) with the fast reciprocal (2 ulp; the result is rounded to bf16); for
+// x -> -inf the denominator overflows to inf and the quotient is -0
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 
@@ -160,14 +162,18 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       // shared row `warp + dy` holds image row y - 2 + dy
       const __nv_bfloat16* base = conv_smem + buf * buf_elems + warp * pitch * kConvCh + 2 * lane;
       __nv_bfloat16* orow = out + (long long)(f * gh + y) * gw * ld_out + c;
-      float2 win[5][5];  // win[slot][dy]; slot (x + k) % 5 holds shared column x + k
+      // six-slot ring: while output x is computed, slot (x + k) % 6 holds shared column
+      // x + k for k < 5 and column x + 5 is already in flight, so each shared load has a
+      // whole output's arithmetic to land
+      float2 win[6][5];
 #pragma unroll
-      for (int s = 0; s < 5; ++s)
+      for (int s = 0; s < 6; ++s)
 #pragma unroll
-        for (int dy = 0; dy < 5; ++dy) win[s][dy] = lds_bf162(base + (dy * pitch + s) * kConvCh);
-      for (int x0 = 0; x0 < gw; x0 += 5) {
+        for (int dy = 0; dy < 5; ++dy)
+          win[s][dy] = s < pitch ? lds_bf162(base + (dy * pitch + s) * kConvCh) : make_float2(0.f, 0.f);
+      for (int x0 = 0; x0 < gw; x0 += 6) {
 #pragma unroll
-        for (int u = 0; u < 5; ++u) {
+        for (int u = 0; u < 6; ++u) {
           const int x = x0 + u;
           if (x < gw) {
             float2 a[5];
@@ -176,12 +182,12 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 #pragma unroll
             for (int k = 0; k < 5; ++k)
 #pragma unroll
-              for (int dy = 0; dy < 5; ++dy) a[dy] = fma2(wr[dy][k], win[(u + k) % 5][dy], a[dy]);
+              for (int dy = 0; dy < 5; ++dy) a[dy] = fma2(wr[dy][k], win[(u + k) % 6][dy], a[dy]);
             const float2 s = add2(add2(add2(a[0], a[1]), add2(a[2], a[3])), a[4]);
             *reinterpret_cast<__nv_bfloat162*>(orow + (long long)x * ld_out) = __floats2bfloat162_rn(s.x, s.y);
-            if (x + 5 < pitch) {
+            if (x + 6 < pitch) {  // column x + 6 replaces column x
 #pragma unroll
-              for (int dy = 0; dy < 5; ++dy) win[u][dy] = lds_bf162(base + (dy * pitch + x + 5) * kConvCh);
+              for (int dy = 0; dy < 5; ++dy) win[u][dy] = lds_bf162(base + (dy * pitch + x + 6) * kConvCh);
             }
           }
         }
@@ -219,9 +225,9 @@ __global__ void spatial_conv_kernel(const __nv_bfloat16* __restrict__ in, long l
 // ---------------------------------------------------------------------------------
 // 2. Temporal conv + SiLU + optional L2, output FHSD [F, H, T, D] bf16.
 // One warp per (token s, head h); lane l holds channels h*D + l*D/32 .. +D/32.  Frames
-// are processed in chunks of 16 outputs: the 20 input frames a chunk needs are loaded
+// are processed in chunks of 12 outputs: the 16 input frames a chunk needs are loaded
 // first (one 8-byte load per lane and frame for D = 128, all independent, so a warp
-// keeps 20 loads in flight instead of one), then the 5-tap conv, SiLU and the L2 norm
+// keeps 16 loads in flight instead of one), then the 5-tap conv, SiLU and the L2 norm
 // (a warp reduction) run from registers.  taps == 0 means no temporal conv.
 // ---------------------------------------------------------------------------------
 template <int V>
@@ -248,11 +254,11 @@ struct PackedBf16<2> {
 };
 
 template <int D>
-__global__ void __launch_bounds__(256) temporal_act_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in,
+__global__ void __launch_bounds__(256, 3) temporal_act_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in,
                                                            const float* __restrict__ w, int taps, int F, int T,
                                                            int H, int l2, __nv_bfloat16* __restrict__ out) {
   constexpr int V = D / 32;  // channels per lane
-  constexpr int kChunk = 16;
+  constexpr int kChunk = 12;
   constexpr int kLoad = kChunk + 4;
   using P = PackedBf16<V>;
   const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;

@@ -109,3 +109,26 @@ def test_repeated_forward_is_deterministic():
     a = _run_block(bw, lay, c["heads"], c["dim"], x)
     b = _run_block(bw, lay, c["heads"], c["dim"], x)
     assert torch.equal(a, b)
+
+
+def test_host_streamer_matches_direct_forward():
+    """Overlapped host->device->host streaming returns exactly the direct outputs."""
+    c = vo.CONFIG0
+    bw = vo.make_block(7, c["hidden"], c["heads"], c["dim"])
+    lay = _layout(c)
+    state = pkg.B200State("t", {"enable_softmax_gate": True}, [bw.branch], c["heads"], c["dim"])
+    fwd = pkg.make_vdn_forward(_Attn(bw, c["heads"], c["dim"]), state, 0)
+
+    def run(xd):
+        with pkg.publish_layout(lay):
+            return fwd(xd)
+
+    xs = [vo.make_x(10 + i, lay.seq_len, c["hidden"]).to(torch.bfloat16).pin_memory() for i in range(4)]
+    outs = [torch.empty(lay.seq_len, c["hidden"], dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+    streamer = pkg.HostStreamer(run, DEV, (lay.seq_len, c["hidden"]))
+    with pkg.cholesky_runtime_scope():
+        streamer.run(xs, outs)
+        torch.cuda.synchronize()
+        direct = [run(x.to(DEV)).cpu() for x in xs]
+    for got, want in zip(outs, direct):
+        assert torch.equal(got, want)
