@@ -86,8 +86,8 @@ __global__ void __launch_bounds__(128) spatial_conv5_kernel(const __nv_bfloat16*
 // channels x 8 output rows of one frame, channel-slab-major so the weights change
 // rarely).  Each tile's input rows y0-2 .. y0+9 are staged in shared memory by 16-byte
 // cp.async copies, with the zero padding written in place (two zero columns left and
-// right, zero rows outside the frame), so the inner loop has no bounds checks; the next
-// tile's copies are in flight while this one is computed (two buffers when they fit).
+// right, zero rows outside the frame), so the inner loop has no bounds checks.  Two CTAs
+// share an SM, so one's copies are in flight while the other computes.
 // Warp w computes output row y0 + w, lane l channels c0 + 2l, 2l + 1: it slides along x
 // keeping the 5x5 window of both channels in registers (5 shared loads per output) and
 // accumulates five independent paired-fp32 chains, one per kernel row.
@@ -99,7 +99,7 @@ __device__ __forceinline__ float2 lds_bf162(const __nv_bfloat16* p) {
   return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
 }
 
-__global__ void __launch_bounds__(kConvThreads, 1)
+__global__ void __launch_bounds__(kConvThreads, 2)
     spatial_conv5_tiled_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in, const float* __restrict__ w,
                                int F, int gh, int gw, int C, __nv_bfloat16* __restrict__ out, long long ld_out,
                                int stages) {
@@ -162,18 +162,14 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       // shared row `warp + dy` holds image row y - 2 + dy
       const __nv_bfloat16* base = conv_smem + buf * buf_elems + warp * pitch * kConvCh + 2 * lane;
       __nv_bfloat16* orow = out + (long long)(f * gh + y) * gw * ld_out + c;
-      // six-slot ring: while output x is computed, slot (x + k) % 6 holds shared column
-      // x + k for k < 5 and column x + 5 is already in flight, so each shared load has a
-      // whole output's arithmetic to land
-      float2 win[6][5];
+      float2 win[5][5];  // win[slot][dy]; slot (x + k) % 5 holds shared column x + k
 #pragma unroll
-      for (int s = 0; s < 6; ++s)
+      for (int s = 0; s < 5; ++s)
 #pragma unroll
-        for (int dy = 0; dy < 5; ++dy)
-          win[s][dy] = s < pitch ? lds_bf162(base + (dy * pitch + s) * kConvCh) : make_float2(0.f, 0.f);
-      for (int x0 = 0; x0 < gw; x0 += 6) {
+        for (int dy = 0; dy < 5; ++dy) win[s][dy] = lds_bf162(base + (dy * pitch + s) * kConvCh);
+      for (int x0 = 0; x0 < gw; x0 += 5) {
 #pragma unroll
-        for (int u = 0; u < 6; ++u) {
+        for (int u = 0; u < 5; ++u) {
           const int x = x0 + u;
           if (x < gw) {
             float2 a[5];
@@ -182,12 +178,16 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 #pragma unroll
             for (int k = 0; k < 5; ++k)
 #pragma unroll
-              for (int dy = 0; dy < 5; ++dy) a[dy] = fma2(wr[dy][k], win[(u + k) % 6][dy], a[dy]);
-            const float2 s = add2(add2(add2(a[0], a[1]), add2(a[2], a[3])), a[4]);
+              for (int dy = 0; dy < 5; ++dy) {
+                a[dy].x = fmaf(wr[dy][k].x, win[(u + k) % 5][dy].x, a[dy].x);
+                a[dy].y = fmaf(wr[dy][k].y, win[(u + k) % 5][dy].y, a[dy].y);
+              }
+            const float2 s = make_float2(((a[0].x + a[1].x) + (a[2].x + a[3].x)) + a[4].x,
+                                         ((a[0].y + a[1].y) + (a[2].y + a[3].y)) + a[4].y);
             *reinterpret_cast<__nv_bfloat162*>(orow + (long long)x * ld_out) = __floats2bfloat162_rn(s.x, s.y);
-            if (x + 6 < pitch) {  // column x + 6 replaces column x
+            if (x + 5 < pitch) {
 #pragma unroll
-              for (int dy = 0; dy < 5; ++dy) win[u][dy] = lds_bf162(base + (dy * pitch + x + 6) * kConvCh);
+              for (int dy = 0; dy < 5; ++dy) win[u][dy] = lds_bf162(base + (dy * pitch + x + 5) * kConvCh);
             }
           }
         }
@@ -836,9 +836,13 @@ int vdn_spatial_conv(const void* in, long long ld_in, const float* w, int kh, in
       cudaFuncSetAttribute(spatial_conv5_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
       attr_set = true;
     }
-    const int stages = 2 * buf_bytes <= kSmemLimit ? 2 : 1;
+    // two CTAs per SM with one buffer each when they fit (one CTA computes while the other
+    // loads); the kernel can also double-buffer inside one CTA (stages = 2), which measured
+    // slower at 8 warps per SM
+    const bool two_ctas = 2 * buf_bytes <= kSmemLimit;
+    const int stages = 1;
     const long long n_tiles = (long long)(C / kConvCh) * F * ((gh + kConvRows - 1) / kConvRows);
-    const int grid = (int)std::min<long long>(n_tiles, vdn::sm_count());
+    const int grid = (int)std::min<long long>(n_tiles, (two_ctas ? 2 : 1) * vdn::sm_count());
     spatial_conv5_tiled_kernel<<<grid, kConvThreads, stages * buf_bytes, s>>>(
         reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, F, gh, gw, C, reinterpret_cast<__nv_bfloat16*>(out),
         ld_out, stages);

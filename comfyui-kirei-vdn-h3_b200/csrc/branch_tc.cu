@@ -8,8 +8,8 @@
 //                        (branch.py:780, :754-758) and the RMSNorm(D) x sigmoid(G + b) epilogue
 //                        (branch.py:494-530) from TMEM: the output-gate up-projection never
 //                        touches HBM.
-// Statistics: one warpgroup per CTA (thread = TMEM lane = tile row), thread 0 issues TMA
-// and MMA.  Readout: warp-specialised, see below.
+// Both kernels are warp-specialised pipelines (TMA producer, MMA issuer, worker warps,
+// double-buffered TMEM accumulators), described above each kernel.
 #include "host_common.h"
 #include "sm100.cuh"
 
@@ -24,137 +24,209 @@ constexpr int kBlk = kRows * 128;          // 16 KB: one 64-column block
 __device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + __expf(-x)); }
 
 // ------------------------------------------------------------------------------- statistics
-// smem: K stage x2, V stage x2, beta*K, beta*V (each 32 KB) = 192 KB.
+// Warp-specialised pipeline (320 threads):
+//   warp 0      TMA producer: K and V chunks (128 tokens x 128 features each) of the CTA's
+//               (frame, head) units into a 2-stage ring;
+//   warps 2-5   scalers (thread = token row): beta = sigmoid(logit) (0 past the frame end),
+//               write beta*K into one of two beta-K buffers and scale V in place;
+//   warp 1      MMA issuer: A += (beta K)^T K and B += (beta V)^T K (both operands MN-major,
+//               straight from the feature tiles) into one of two TMEM accumulator pairs;
+//   warps 6-9   epilogue (TMEM lane = feature row): A and B rows of the finished unit to HBM
+//               while the next unit accumulates in the other pair.
+// smem: 2 x (K, V) + 2 x beta-K = 6 x 32 KB.
 struct StatsSmem {
-  static constexpr int kK = 0, kV = 2 * kTile, kBK = 4 * kTile, kBV = 5 * kTile, kBar = 6 * kTile;
+  static constexpr int kKV = 0, kBK = 4 * kTile, kBar = 6 * kTile;
   static constexpr int kBytes = kBar + 256 + 1024;
 };
+constexpr int kStatsThreads = 320;
 
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kStatsThreads, 1)
     frame_stats_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, int F, int H,
                           int T, const float* __restrict__ beta_logits, long long ld_beta, int beta_col0,
                           float* __restrict__ A, float* __restrict__ Bm, int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + StatsSmem::kBar);  // [0,1] kv_full, [2] mma_done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 4);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + StatsSmem::kBar);
+  uint64_t* kv_full = bar;       // [2] TMA bytes
+  uint64_t* kv_empty = bar + 2;  // [2] MMA commit
+  uint64_t* bk_full = bar + 4;   // [2] 4 scaler warps
+  uint64_t* bk_empty = bar + 6;  // [2] MMA commit
+  uint64_t* acc_full = bar + 8;  // [2] MMA commit
+  uint64_t* acc_empty = bar + 10;  // [2] 4 epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    mbar_init(smem_u32(&bar[0]), 1);
-    mbar_init(smem_u32(&bar[1]), 1);
-    mbar_init(smem_u32(&bar[2]), 1);
+    for (int i = 0; i < 12; ++i) mbar_init(smem_u32(&bar[i]), (i == 4 || i == 5 || i == 10 || i == 11) ? 4 : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch(&tk);
     tma_prefetch(&tv);
   }
-  if (warp == 0) {
-    tmem_alloc(smem_u32(tmem_slot), 256);
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t sK = smem_u32(smem + StatsSmem::kK), sV = smem_u32(smem + StatsSmem::kV);
-  const uint32_t sBK = smem_u32(smem + StatsSmem::kBK), sBV = smem_u32(smem + StatsSmem::kBV);
+  const uint32_t sKV = smem_u32(smem + StatsSmem::kKV), sBK = smem_u32(smem + StatsSmem::kBK);
   const int units = F * H;
+  const int u0 = (int)((long long)blockIdx.x * units / gridDim.x);
+  const int u1 = (int)((long long)(blockIdx.x + 1) * units / gridDim.x);
   const int nch = (T + kRows - 1) / kRows;
-  constexpr uint32_t idesc = make_idesc(1, 1, 1, 1, 1, 128, 128);  // both operands MN-major
-  auto issue_load = [&](int unit, int c, int gc) {
-    const int st = gc & 1;
-    const int row0 = unit * T + c * kRows;  // FHSD rows: (f * H + h) * T + s
-    const uint32_t fb = smem_u32(&bar[st]);
-    mbar_arrive_expect_tx(fb, 2 * kTile);
-    for (int b = 0; b < 2; ++b) {
-      tma_load_2d(sK + st * kTile + b * kBlk, &tk, fb, b * 64, row0);
-      tma_load_2d(sV + st * kTile + b * kBlk, &tv, fb, b * 64, row0);
-    }
-  };
-  int gc = 0;
-  bool ok = true;
-  if (tid == 0 && blockIdx.x < units) issue_load(blockIdx.x, 0, 0);
-  for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
-    const int f = unit / H, h = unit % H;
-    for (int c = 0; c < nch; ++c, ++gc) {
-      const int st = gc & 1;
-      if (!mbar_wait(smem_u32(&bar[st]), (gc >> 1) & 1, abort_flag, err, kErrWaitOther) ||
-          (gc > 0 && !mbar_wait(smem_u32(&bar[2]), (gc - 1) & 1, abort_flag, err, kErrWaitOther))) {
-        ok = false;
-        break;
-      }
-      if (tid == 0) {  // prefetch the next chunk into the stage the finished MMA released
-        const bool more = c + 1 < nch;
-        const int nu = more ? unit : unit + gridDim.x;
-        if (nu < units) issue_load(nu, more ? c + 1 : 0, gc + 1);
-      }
-      // beta-weighted copies: row s of both tiles scaled by beta_s (0 past the frame end)
-      const int s = c * kRows + tid;
-      const float beta = s < T ? sigm(beta_logits[((long long)f * T + s) * ld_beta + beta_col0 + h]) : 0.f;
-      const __nv_bfloat162 b2 = __floats2bfloat162_rn(beta, beta);
-      for (int b = 0; b < 2; ++b) {
-        const uint32_t off = b * kBlk + tid * 128;
-        const uint4* srck = reinterpret_cast<const uint4*>(smem + StatsSmem::kK + st * kTile + off);
-        const uint4* srcv = reinterpret_cast<const uint4*>(smem + StatsSmem::kV + st * kTile + off);
-        uint4* dk = reinterpret_cast<uint4*>(smem + StatsSmem::kBK + off);
-        uint4* dv = reinterpret_cast<uint4*>(smem + StatsSmem::kBV + off);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          uint4 k4 = srck[i], v4 = srcv[i];
-          __nv_bfloat162* kp = reinterpret_cast<__nv_bfloat162*>(&k4);
-          __nv_bfloat162* vp = reinterpret_cast<__nv_bfloat162*>(&v4);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            kp[e] = __hmul2(kp[e], b2);
-            vp[e] = __hmul2(vp[e], b2);
+  // stage st: K at sKV + st * 2 * kTile, V right after it
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int unit = u0; unit < u1 && ok; ++unit) {
+        for (int c = 0; c < nch; ++c, ++g) {
+          const int st = g & 1;
+          if (!mbar_wait(smem_u32(&kv_empty[st]), ((g >> 1) & 1) ^ 1, abort_flag, err, kErrWaitProducer)) {
+            ok = false;
+            break;
           }
-          dk[i] = k4;
-          dv[i] = v4;
+          const int row0 = unit * T + c * kRows;  // FHSD rows: (f * H + h) * T + s
+          const uint32_t fb = smem_u32(&kv_full[st]);
+          const uint32_t kb = sKV + st * 2 * kTile, vb = kb + kTile;
+          mbar_arrive_expect_tx(fb, 2 * kTile);
+          for (int b = 0; b < 2; ++b) {
+            tma_load_2d(kb + b * kBlk, &tk, fb, b * 64, row0);
+            tma_load_2d(vb + b * kBlk, &tv, fb, b * 64, row0);
+          }
         }
       }
-      fence_proxy_async_smem();
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(1, 1, 1, 1, 1, 128, 128);  // both operands MN-major
+      int g = 0, acc = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      for (int unit = u0; unit < u1 && ok; ++unit) {
+        if (!mbar_wait(smem_u32(&acc_empty[acc]), acc_ph ^ 1, abort_flag, err, kErrWaitMma)) break;
+        const uint32_t d = tmem + acc * 256;
+        for (int c = 0; c < nch; ++c, ++g) {
+          const int st = g & 1;
+          if (!mbar_wait(smem_u32(&bk_full[st]), (g >> 1) & 1, abort_flag, err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t kb = sKV + st * 2 * kTile, vb = kb + kTile, bkb = sBK + st * kTile;
+#pragma unroll
+          for (int k = 0; k < kRows / 16; ++k) {
+            const uint32_t off = k * 2048;  // 16 tokens = two 8-row swizzle groups
+            const uint64_t bdesc = make_sdesc(kb + off, kBlk, 1024);
+            mma_f16(d, make_sdesc(bkb + off, kBlk, 1024), bdesc, idesc, (c > 0 || k > 0) ? 1u : 0u);
+            mma_f16(d + 128, make_sdesc(vb + off, kBlk, 1024), bdesc, idesc, (c > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&kv_empty[st]));
+          tc_commit(smem_u32(&bk_empty[st]));
+          if (c == nch - 1) tc_commit(smem_u32(&acc_full[acc]));
+        }
+        if (++acc == 2) {
+          acc = 0;
+          acc_ph ^= 1;
+        }
+      }
+    }
+  } else if (warp < 6) {
+    // scalers: thread = token row of the chunk
+    const int r = tid - 64;
+    int g = 0;
+    bool ok = true;
+    for (int unit = u0; unit < u1 && ok; ++unit) {
+      const int f = unit / H, h = unit % H;
+      for (int c = 0; c < nch; ++c, ++g) {
+        const int st = g & 1;
+        // K/V of this chunk landed, and the MMA that read this beta-K buffer two chunks ago is done
+        const bool okw = __all_sync(0xffffffffu,
+                                    mbar_wait(smem_u32(&kv_full[st]), (g >> 1) & 1, abort_flag, err, kErrWaitOther) &&
+                                        mbar_wait(smem_u32(&bk_empty[st]), ((g >> 1) & 1) ^ 1, abort_flag, err,
+                                                  kErrWaitOther));
+        if (!okw) {
+          ok = false;
+          break;
+        }
+        const int s = c * kRows + r;
+        const float beta = s < T ? sigm(beta_logits[((long long)f * T + s) * ld_beta + beta_col0 + h]) : 0.f;
+        const __nv_bfloat162 b2 = __floats2bfloat162_rn(beta, beta);
+        uint8_t* kt = smem + StatsSmem::kKV + st * 2 * kTile;
+        uint8_t* vt = kt + kTile;
+        uint8_t* bk = smem + StatsSmem::kBK + st * kTile;
+        for (int b = 0; b < 2; ++b) {
+          const uint32_t off = b * kBlk + r * 128;
+          const uint4* srck = reinterpret_cast<const uint4*>(kt + off);
+          uint4* vv = reinterpret_cast<uint4*>(vt + off);
+          uint4* dk = reinterpret_cast<uint4*>(bk + off);
+          // the scale is the same for the whole row, so any chunk order works: start each
+          // row at a different 16-byte chunk so the eight rows of a quarter-warp hit
+          // different banks
+#pragma unroll
+          for (int i0 = 0; i0 < 8; ++i0) {
+            const int i = i0 ^ (r & 7);
+            uint4 k4 = srck[i], v4 = vv[i];
+            __nv_bfloat162* kp = reinterpret_cast<__nv_bfloat162*>(&k4);
+            __nv_bfloat162* vp = reinterpret_cast<__nv_bfloat162*>(&v4);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              kp[e] = __hmul2(kp[e], b2);
+              vp[e] = __hmul2(vp[e], b2);
+            }
+            dk[i] = k4;
+            vv[i] = v4;
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bk_full[st]));
+      }
+    }
+  } else {
+    // epilogue: row i of A and of B from TMEM lane i (quadrant = warp % 4)
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int unit = u0; unit < u1; ++unit) {
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&acc_full[acc]), acc_ph, abort_flag, err, kErrWaitEpilogue)))
+        break;
+      tc_fence_after();
+      const long long ob = ((long long)unit * D + row) * D;
+      for (int m = 0; m < 2; ++m) {
+        float* dst = (m == 0 ? A : Bm) + ob;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tmem + lane_base + acc * 256 + m * 128 + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(dst + c * 32 + i) =
+                make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]),
+                            __uint_as_float(v[i + 3]));
+        }
+      }
       tc_fence_before();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < kRows / 16; ++k) {
-          const uint32_t off = k * 2048;  // 16 tokens = two 8-row swizzle groups
-          const uint64_t bdesc = make_sdesc(sK + st * kTile + off, kBlk, 1024);
-          mma_f16(tmem, make_sdesc(sBK + off, kBlk, 1024), bdesc, idesc, (c > 0 || k > 0) ? 1u : 0u);
-          mma_f16(tmem + 128, make_sdesc(sBV + off, kBlk, 1024), bdesc, idesc, (c > 0 || k > 0) ? 1u : 0u);
-        }
-        tc_commit(smem_u32(&bar[2]));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc]));
+      if (++acc == 2) {
+        acc = 0;
+        acc_ph ^= 1;
       }
     }
-    if (!ok) break;
-    // epilogue: row i of A and of B from TMEM lane i
-    if (!mbar_wait(smem_u32(&bar[2]), (gc - 1) & 1, abort_flag, err, kErrWaitOther)) break;
-    tc_fence_after();
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const long long ob = ((long long)unit * D + tid) * D;
-    for (int m = 0; m < 2; ++m) {
-      uint32_t r[D];
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c)
-        tmem_ld32(tmem + lane_base + m * 128 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
-      tmem_ld_wait();
-      float* dst = (m == 0 ? A : Bm) + ob;
-#pragma unroll
-      for (int c = 0; c < D; c += 4)
-        *reinterpret_cast<float4*>(dst + c) = make_float4(__uint_as_float(r[c]), __uint_as_float(r[c + 1]),
-                                                          __uint_as_float(r[c + 2]), __uint_as_float(r[c + 3]));
-    }
-    tc_fence_before();
-    __syncthreads();  // TMEM is overwritten by the next unit's first MMA
   }
   tc_fence_before();
   __syncthreads();
   if (*abort_flag) abort_drain();
-  if (warp == 0) {
+  if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -499,7 +571,7 @@ int vdn_frame_stats_tc(const void* K, const void* V, int F, int H, int T, const 
   }
   const int units = F * H;
   const int grid = units < vdn::sm_count() ? units : vdn::sm_count();
-  frame_stats_tc_kernel<<<grid, 128, StatsSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
+  frame_stats_tc_kernel<<<grid, kStatsThreads, StatsSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
       tk, tv, F, H, T, beta_logits, ld_beta, beta_col0, A, B, dev_err);
   return vdn::launch_status();
 }
