@@ -61,7 +61,11 @@ def attention_traffic(heads_per_rank: int, heads_total: int):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons, sampled every 50 ms from before the warm-up to
+    after the timed region.  ``mark_start()`` / ``mark_end()`` bracket the timed region on
+    the same monotonic clock the samples are stamped with; ``summary()`` keeps the samples
+    inside it (or, for a region shorter than the sampling period, the nearest one on each
+    side)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -70,13 +74,14 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []
+        self.t0 = self.t1 = None
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
         except Exception:
@@ -85,10 +90,17 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
 
-    def __exit__(self, *exc):
+    def mark_start(self):
+        self.t0 = time.monotonic()
+
+    def mark_end(self):
+        self.t1 = time.monotonic()
+
+    def stop(self):
         if self.proc is not None:
+            time.sleep(0.2)  # let the sample after the timed region arrive
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -96,23 +108,27 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        rows = []
+        for t, line in self.lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
+                rows.append((t, float(parts[1]), float(parts[2]), parts[5:9]))
             except ValueError:
                 continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        window = "timed region"
+        picked = [r for r in rows if self.t0 is not None and self.t0 <= r[0] <= self.t1]
+        if not picked and rows and self.t0 is not None:
+            before = [r for r in rows if r[0] < self.t0]
+            after = [r for r in rows if r[0] > self.t1]
+            picked = ([before[-1]] if before else []) + ([after[0]] if after else [])
+            window = "nearest samples around a timed region shorter than the 50 ms period"
+        sm = sorted(r[1] for r in picked)
+        reasons = sorted({n for r in picked for n, v in zip(names, r[3]) if v.lower().startswith("active")})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": picked[-1][2] if picked else None,
+                "reasons": reasons, "samples": len(sm), "window": window}
 
 
 def dist_setup():
@@ -321,6 +337,7 @@ def main():
         attn_ms.append((e0, e1))
 
     pkg.hybrid.launch_window_attention = timed_launch
+    clocks = ClockSampler(local).start()  # running through the warm-up, so it samples the timed region
     with pkg.cholesky_runtime_scope():
         for _ in range(args.warmup):
             block.forward(x_dev, lay, state.window_plans, status, out=out_dev if world == 1 else None)
@@ -330,13 +347,14 @@ def main():
     barrier(world)
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        e_start.record()
-        with pkg.cholesky_runtime_scope():
-            for _ in range(args.steps):
-                block.forward(x_dev, lay, state.window_plans, status, out=out_dev if world == 1 else None)
-            e_end.record()
-            torch.cuda.synchronize()
+    clocks.mark_start()
+    e_start.record()
+    with pkg.cholesky_runtime_scope():
+        for _ in range(args.steps):
+            block.forward(x_dev, lay, state.window_plans, status, out=out_dev if world == 1 else None)
+        e_end.record()
+        torch.cuda.synchronize()
+    clocks.mark_end()
     barrier(world)
     status.raise_if_failed()
     pkg.hybrid.launch_window_attention = orig_launch
@@ -397,6 +415,18 @@ def main():
         torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / max(args.steps, 1), world)
     status.raise_if_failed()
+    # diagnostics outside the timed region: one bare host->device and device->host copy
+    c0, c1, c2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    x_probe = torch.empty_like(streamer.x_dev[0])
+    c0.record()
+    x_probe.copy_(inputs_host[0], non_blocking=True)
+    c1.record()
+    outs_host[0].copy_(x_probe[:outs_host[0].shape[0], :outs_host[0].shape[1]], non_blocking=True)
+    c2.record()
+    torch.cuda.synchronize()
+    copy_ms = {"h2d_ms": c0.elapsed_time(c1), "d2h_ms": c1.elapsed_time(c2)}
+    clocks.stop()
+    clock_summary = clocks.summary()
     e2e_value = flops["total"] / (e2e_ms * 1e-3) / 1e12
     launches_per_step = 18
     line = {
@@ -415,9 +445,10 @@ def main():
         # bytes summed over the ranks (at N > 1 each rank moves its own row block)
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": S * hidden * 2, "d2h_bytes_per_step": S * hidden * 2,
-                "copies": "pinned host buffers; H2D of step i+1 and D2H of step i-1 overlap step i (HostStreamer)"},
+                "copies": "pinned host buffers; H2D of step i+1 and D2H of step i-1 overlap step i (HostStreamer)",
+                **copy_ms},
         "gpu_launches": launches_per_step * args.steps,
-        "clocks": clocks.summary(),
+        "clocks": clock_summary,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(c)

@@ -379,10 +379,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < 32; c += 2) {
             const float2 x = fma2(make_float2(__uint_as_float(sr[c0 + c]), __uint_as_float(sr[c0 + c + 1])), scale2,
                                   negm2);
-            // 3/8 of the exponentials run on the FMA pipe to relieve the MUFU unit
+            // a quarter of the exponentials run on the FMA pipe to relieve the MUFU unit
             float2 e;
             e.x = ex2(x.x);
-            e.y = ((c & 6) != 0) ? exp2_poly(x.y) : ex2(x.y);
+            e.y = ((c & 2) != 0) ? exp2_poly(x.y) : ex2(x.y);
             rs2[(c >> 1) & 3] = add2(rs2[(c >> 1) & 3], e);
             pk[c / 2] = pack_bf16(e.x, e.y);
           }
@@ -424,22 +424,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float inv_l = (l_run > 0.f) ? gate / l_run : 0.f;
       __nv_bfloat16* dst = p.out + (long long)qrow * p.ld_out + h * D;
-      uint32_t r[D];
+      // O in 32-column chunks (keeps 32 values live); the accumulator is released after the last
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) tmem_ld32(o_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(B(B_OFREE0 + a));
-      if (qrow < p.S) {
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(o_tmem + c * 32, r);
+        tmem_ld_wait();
+        if (c == D / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(B(B_OFREE0 + a));
+        }
+        if (qrow < p.S) {
 #pragma unroll
-        for (int i = 0; i < D; i += 8) {
-          uint4 v;
-          v.x = pack_bf16(__uint_as_float(r[i]) * inv_l, __uint_as_float(r[i + 1]) * inv_l);
-          v.y = pack_bf16(__uint_as_float(r[i + 2]) * inv_l, __uint_as_float(r[i + 3]) * inv_l);
-          v.z = pack_bf16(__uint_as_float(r[i + 4]) * inv_l, __uint_as_float(r[i + 5]) * inv_l);
-          v.w = pack_bf16(__uint_as_float(r[i + 6]) * inv_l, __uint_as_float(r[i + 7]) * inv_l);
-          *reinterpret_cast<uint4*>(dst + i) = v;
+          for (int i = 0; i < 32; i += 8) {
+            uint4 v;
+            v.x = pack_bf16(__uint_as_float(r[i]) * inv_l, __uint_as_float(r[i + 1]) * inv_l);
+            v.y = pack_bf16(__uint_as_float(r[i + 2]) * inv_l, __uint_as_float(r[i + 3]) * inv_l);
+            v.z = pack_bf16(__uint_as_float(r[i + 4]) * inv_l, __uint_as_float(r[i + 5]) * inv_l);
+            v.w = pack_bf16(__uint_as_float(r[i + 6]) * inv_l, __uint_as_float(r[i + 7]) * inv_l);
+            *reinterpret_cast<uint4*>(dst + c * 32 + i) = v;
+          }
         }
       }
     }
