@@ -156,6 +156,8 @@ class BranchWorkspace:
         self.A = torch.empty(Fb + nt, heads, dim, dim, **f32)
         self.B = torch.empty(Fb + nt, heads, dim, dim, **f32)
         self.inv = torch.empty(Fb + nt, heads, dim, dim, **f32)
+        # bf16 hi / lo halves of the inverses for the tensor-core scan (head_dim 128)
+        self.inv_split = torch.empty(2 if dim == 128 else 0, Fb + nt, heads, dim, dim, **bf)
         self.info = torch.zeros(Fb + nt, heads, device=dev, dtype=torch.int32)
         self.s0 = torch.empty(heads, dim, dim, **f32)
         self.prefix = torch.empty(Fb, heads, dim, dim, **f32)
@@ -222,6 +224,7 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
 
     stats(ws.kf, ws.vf, Fb, tpf, aux, ws.A.data_ptr(), ws.B.data_ptr())
     has_text = text_k is not None
+    split = ws.inv_split.data_ptr() if tensor_cores else None
     if has_text:
         L = text_k.shape[0]
         call("vdn_temporal_act", text_k.data_ptr(), text_k.stride(0), None, 0, 1, L, H, D, 1, ws.tk.data_ptr(), stream)
@@ -229,15 +232,19 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
         mat = D * D * H
         stats(ws.tk, ws.tv, 1, L, text_aux, ws.A.data_ptr() + 4 * Fb * mat, ws.B.data_ptr() + 4 * Fb * mat)
         call("vdn_delta_factor", ws.A.data_ptr(), ws.B.data_ptr(), Fb + 1, H, D, ws.inv.data_ptr(),
-             ws.info.data_ptr(), Fb, TEXT_STATE_SCALE, ws.s0.data_ptr(), stream)
+             ws.info.data_ptr(), Fb, TEXT_STATE_SCALE, ws.s0.data_ptr(), split, stream)
         s0 = ws.s0
     else:
         call("vdn_delta_factor", ws.A.data_ptr(), ws.B.data_ptr(), Fb, H, D, ws.inv.data_ptr(), ws.info.data_ptr(),
-             -1, 0.0, None, stream)
+             -1, 0.0, None, split, stream)
         s0 = None
     record_factor_status(ws.info)
-    call("vdn_bidir_scan", ws.inv.data_ptr(), ws.B.data_ptr(), ws.alpha.data_ptr(), _lib.ptr(s0), Fb, H, D,
-         ws.prefix.data_ptr(), ws.suffix.data_ptr(), stream)
+    if tensor_cores:
+        call("vdn_bidir_scan_tc", split, ws.B.data_ptr(), ws.alpha.data_ptr(), _lib.ptr(s0), Fb, Fb + int(has_text), H,
+             ws.prefix.data_ptr(), ws.suffix.data_ptr(), status.err_ptr, stream)
+    else:
+        call("vdn_bidir_scan", ws.inv.data_ptr(), ws.B.data_ptr(), ws.alpha.data_ptr(), _lib.ptr(s0), Fb, H, D,
+             ws.prefix.data_ptr(), ws.suffix.data_ptr(), stream)
     # output gate: sigmoid(bf16(x W_down^T) W_up^T + b)  (branch.py:754-758)
     call("vdn_cast_rows", aux.data_ptr(), aux_ld, ogd_col0, rows, D, ws.ogd.data_ptr(), ws.ogd.stride(0), stream)
     lo, hi = ws.bounds_arrays(bounds)

@@ -63,17 +63,19 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x for x <= 0 on the FMA/ALU pipes: x = n + f with n = round(x) (added-magic-number
+// 2^x for x <= 8 on the FMA/ALU pipes: x = n + f with n = round(x) (added-magic-number
 // rounding) and f in [-0.5, 0.5]; 2^f by a cubic fitted here for minimum relative error
 // (max 1.0e-4, far below the bf16 rounding P receives); 2^n added to the exponent bits.
+// Inputs below -126 (masked keys are -inf) are clamped to 2^-126 instead of 0: the row sum
+// is at least 1 (the key that set the reference maximum has weight 1), so such weights stay
+// below fp32 resolution in every sum, and no select is spent on exact zeros.
 __device__ __forceinline__ float exp2_poly(float x) {
   const float xc = fmaxf(x, -126.0f);
   const float t = xc + 12582912.0f;  // 1.5 * 2^23: rounds xc to an integer in the low bits
   const int n = __float_as_int(t) - 0x4B400000;
   const float f = xc - (t - 12582912.0f);
   const float p = fmaf(fmaf(fmaf(0.05500844f, f, 0.24220988f), f, 0.69328284f), f, 1.0f);
-  const float y = __int_as_float(__float_as_int(p) + (n << 23));
-  return x < -125.0f ? 0.0f : y;
+  return __int_as_float(__float_as_int(p) + (n << 23));
 }
 
 __device__ __forceinline__ float max3(float a, float b, float c) {

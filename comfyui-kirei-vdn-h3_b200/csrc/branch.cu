@@ -443,7 +443,8 @@ __global__ void __launch_bounds__(256) frame_stats_kernel(const __nv_bfloat16* _
 // ---------------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(256) spd_inverse_kernel(const float* __restrict__ A, int H, float* __restrict__ inv_out,
-                                                          int* __restrict__ info) {
+                                                          int* __restrict__ info,
+                                                          __nv_bfloat16* __restrict__ inv_split) {
   constexpr int TB = D / 16;
   // pivot column / row of step k in buffer k & 1: one barrier per step suffices, since a
   // buffer is rewritten two steps later, after every thread has passed the barrier between
@@ -516,6 +517,23 @@ __global__ void __launch_bounds__(256) spd_inverse_kernel(const float* __restric
   for (int i = 0; i < TB; ++i)
 #pragma unroll
     for (int j = 0; j < TB; ++j) inv_out[mb + (long long)(r0 + i) * D + c0 + j] = bad ? nan : m[i][j];
+  if (inv_split) {
+    // the same inverse as two bf16 matrices hi + lo (hi = bf16(x), lo = bf16(x - hi)) for the
+    // tensor-core scan: hi at inv_split, lo F*H*D*D elements further
+    __nv_bfloat16* hi = inv_split + mb;
+    __nv_bfloat16* lo = inv_split + (long long)gridDim.y * H * D * D + mb;
+#pragma unroll
+    for (int i = 0; i < TB; ++i)
+#pragma unroll
+      for (int j = 0; j < TB; j += 2) {
+        const float x0 = bad ? nan : m[i][j], x1 = bad ? nan : m[i][j + 1];
+        const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+        const float2 hf = __bfloat1622float2(h2);
+        *reinterpret_cast<__nv_bfloat162*>(hi + (long long)(r0 + i) * D + c0 + j) = h2;
+        *reinterpret_cast<__nv_bfloat162*>(lo + (long long)(r0 + i) * D + c0 + j) =
+            __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+      }
+  }
 }
 
 // s0[h] = scale * B[f_text, h] inv[f_text, h] (the text state, branch.py:649-670).
@@ -917,16 +935,18 @@ int vdn_frame_stats(const void* K, const void* V, int F, int H, int T, int D, co
 // A, B: [F, H, D, D] fp32.  inv out [F, H, D, D]; info [F, H] int32.  If text_frame >= 0,
 // s0 [H, D, D] = text_scale * B[text_frame] inv[text_frame] (branch.py:649-670).
 int vdn_delta_factor(const float* A, const float* B, int F, int H, int D, float* inv, int* info, int text_frame,
-                     float text_scale, float* s0, void* stream) {
+                     float text_scale, float* s0, void* inv_split, void* stream) {
   if (!A || !inv || !info || (text_frame >= 0 && (!B || !s0))) return vdn::kBadArgument;
   if (text_frame >= F) return vdn::kBadArgument;
+  if (inv_split && (D != 128 || (reinterpret_cast<uintptr_t>(inv_split) & 3))) return vdn::kBadArgument;
   dim3 grid(H, F);
   auto s = reinterpret_cast<cudaStream_t>(stream);
+  auto* split = reinterpret_cast<__nv_bfloat16*>(inv_split);
   if (D == 128) {
-    spd_inverse_kernel<128><<<grid, 256, 0, s>>>(A, H, inv, info);
+    spd_inverse_kernel<128><<<grid, 256, 0, s>>>(A, H, inv, info, split);
     if (text_frame >= 0) text_state_kernel<128><<<H, 256, 0, s>>>(B, inv, H, text_frame, text_scale, s0);
   } else if (D == 64) {
-    spd_inverse_kernel<64><<<grid, 256, 0, s>>>(A, H, inv, info);
+    spd_inverse_kernel<64><<<grid, 256, 0, s>>>(A, H, inv, info, nullptr);
     if (text_frame >= 0) text_state_kernel<64><<<H, 256, 0, s>>>(B, inv, H, text_frame, text_scale, s0);
   } else {
     return vdn::kUnsupported;

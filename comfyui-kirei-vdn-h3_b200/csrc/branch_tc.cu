@@ -545,6 +545,190 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------------------- scan
+// Bidirectional scan on the tensor cores: one CTA per (head, direction) keeps the 128 x 128
+// state in TMEM and runs, per frame,
+//     u = B_t + s o alpha_t          (warps 0-3, thread = state row, from TMEM + HBM)
+//     s = u (I + A_t)^-1             (warp 4: 24 tcgen05 MMAs)
+// The product is done in three bf16 passes, u_hi inv_hi + u_hi inv_lo + u_lo inv_hi with
+// x = hi + lo (hi = bf16(x), lo = bf16(x - hi)), accumulated in fp32: 16 significant bits per
+// operand, so the state carries ~1e-5 relative error per frame (it is rounded to bf16 for the
+// readout).  The inverse halves come from vdn_delta_factor; the next frame's are loaded by
+// TMA while the current frame is multiplied.
+// smem: 2 stages x (inv hi, inv lo) + (u hi, u lo) = 6 x 32 KB.
+struct ScanSmem {
+  static constexpr int kInv = 0, kU = 4 * kTile, kBar = 6 * kTile;
+  static constexpr int kBytes = kBar + 256 + 1024;
+};
+constexpr int kScanThreads = 160;
+
+__global__ void __launch_bounds__(kScanThreads, 1)
+    scan_tc_kernel(const __grid_constant__ CUtensorMap tinv, const float* __restrict__ Bm,
+                   const float* __restrict__ alpha, const float* __restrict__ s0, int F, int F_inv, int H,
+                   float* __restrict__ prefix, float* __restrict__ suffix, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + ScanSmem::kBar);
+  uint64_t* inv_full = bar;       // [2]
+  uint64_t* inv_empty = bar + 2;  // [2]
+  uint64_t* a_full = bar + 4;     // 4 row warps
+  uint64_t* mma_done = bar + 5;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 6);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = blockIdx.x, dir = blockIdx.y;
+  if (tid == 0) {
+    for (int i = 0; i < 6; ++i) mbar_init(smem_u32(&bar[i]), i == 4 ? 4 : 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch(&tinv);
+  }
+  if (warp == 4) {
+    tmem_alloc(smem_u32(tmem_slot), 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sInv = smem_u32(smem + ScanSmem::kInv), sU = smem_u32(smem + ScanSmem::kU);
+  auto frame = [&](int step) { return dir == 0 ? step : F - 1 - step; };
+  float* dst_all = dir == 0 ? prefix : suffix;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(1, 1, 1, 0, 0, 128, 128);
+      const int lo_rows = F_inv * H * D;  // the lo halves follow the hi halves
+      auto issue = [&](int step) {
+        const int st = step & 1;
+        if (!mbar_wait(smem_u32(&inv_empty[st]), ((step >> 1) & 1) ^ 1, abort_flag, err, kErrWaitProducer))
+          return false;
+        const int row = (frame(step) * H + h) * D;
+        const uint32_t hi = sInv + st * 2 * kTile, lo = hi + kTile;
+        mbar_arrive_expect_tx(smem_u32(&inv_full[st]), 2 * kTile);
+        for (int b = 0; b < 2; ++b) {
+          tma_load_2d(hi + b * kBlk, &tinv, smem_u32(&inv_full[st]), b * 64, row);
+          tma_load_2d(lo + b * kBlk, &tinv, smem_u32(&inv_full[st]), b * 64, lo_rows + row);
+        }
+        return true;
+      };
+      bool ok = issue(0);
+      for (int step = 0; step < F && ok; ++step) {
+        const int st = step & 1;
+        if (step + 1 < F && !issue(step + 1)) break;
+        if (!mbar_wait(smem_u32(&inv_full[st]), (step >> 1) & 1, abort_flag, err, kErrWaitMma) ||
+            !mbar_wait(smem_u32(a_full), step & 1, abort_flag, err, kErrWaitMma))
+          break;
+        tc_fence_after();
+        const uint32_t ihi = sInv + st * 2 * kTile, ilo = ihi + kTile, uhi = sU, ulo = sU + kTile;
+        const uint32_t ops[3][2] = {{uhi, ihi}, {uhi, ilo}, {ulo, ihi}};
+#pragma unroll
+        for (int pass = 0; pass < 3; ++pass)
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t off = (k >> 2) * kBlk + (k & 3) * 32;
+            mma_f16(tmem, make_sdesc(ops[pass][0] + off, 16, 1024), make_sdesc(ops[pass][1] + off, 16, 1024), idesc,
+                    (pass > 0 || k > 0) ? 1u : 0u);
+          }
+        tc_commit(smem_u32(&inv_empty[st]));
+        tc_commit(smem_u32(mma_done));
+      }
+    }
+  } else {
+    // state rows: thread i = row i = TMEM lane i
+    const int i = tid;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    bool ok = true;
+    for (int step = 0; step < F && ok; ++step) {
+      const int t = frame(step);
+      if (step > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(mma_done), (step - 1) & 1, abort_flag, err, kErrWaitOther));
+        if (!ok) break;
+        tc_fence_after();
+      }
+      if (step + 1 < F) {  // the next frame's B row into L2 while this one is built
+        const float* nb = Bm + (((long long)frame(step + 1) * H + h) * D + i) * D;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) asm volatile("prefetch.global.L2 [%0];" ::"l"(nb + q * 32));
+      }
+      const float* brow = Bm + (((long long)t * H + h) * D + i) * D;
+      const float* al = alpha + ((long long)t * H + h) * D;
+      float* prev = step > 0 ? dst_all + (((long long)frame(step - 1) * H + h) * D + i) * D : nullptr;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float sv[32];
+        if (step == 0) {
+#pragma unroll
+          for (int q = 0; q < 32; ++q) sv[q] = s0 ? s0[((long long)h * D + i) * D + c * 32 + q] : 0.f;
+        } else {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_base + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < 32; ++q) sv[q] = __uint_as_float(r[q]);
+#pragma unroll
+          for (int q = 0; q < 32; q += 4)
+            *reinterpret_cast<float4*>(prev + c * 32 + q) = make_float4(sv[q], sv[q + 1], sv[q + 2], sv[q + 3]);
+        }
+        // u = B + s o alpha, split into bf16 hi + lo, written K-major swizzled (8 values per 16 B)
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int k0 = c * 32 + q8 * 8;
+          const float4 b0 = *reinterpret_cast<const float4*>(brow + k0);
+          const float4 b1 = *reinterpret_cast<const float4*>(brow + k0 + 4);
+          const float4 a0 = *reinterpret_cast<const float4*>(al + k0);
+          const float4 a1 = *reinterpret_cast<const float4*>(al + k0 + 4);
+          const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+          const float aa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+          uint32_t hp[4], lp[4];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            const float u0 = fmaf(sv[q8 * 8 + e], aa[e], bb[e]);
+            const float u1 = fmaf(sv[q8 * 8 + e + 1], aa[e + 1], bb[e + 1]);
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(u0, u1);
+            const float2 hf = __bfloat1622float2(h2);
+            hp[e / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+            lp[e / 2] = pack_bf16(u0 - hf.x, u1 - hf.y);
+          }
+          const int ch = k0 >> 3;  // 16-byte chunk of the row, 0..15
+          const uint32_t off = (ch >> 3) * kBlk + i * 128 + (((ch & 7) ^ (i & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sU + off), "r"(hp[0]), "r"(hp[1]), "r"(hp[2]),
+                       "r"(hp[3])
+                       : "memory");
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sU + kTile + off), "r"(lp[0]), "r"(lp[1]),
+                       "r"(lp[2]), "r"(lp[3])
+                       : "memory");
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(a_full));
+    }
+    if (ok && __all_sync(0xffffffffu, mbar_wait(smem_u32(mma_done), (F - 1) & 1, abort_flag, err, kErrWaitOther))) {
+      tc_fence_after();
+      float* last = dst_all + (((long long)frame(F - 1) * H + h) * D + i) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + c * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int q = 0; q < 32; q += 4)
+          *reinterpret_cast<float4*>(last + c * 32 + q) = make_float4(
+              __uint_as_float(r[q]), __uint_as_float(r[q + 1]), __uint_as_float(r[q + 2]), __uint_as_float(r[q + 3]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) abort_drain();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
 }  // namespace branch_tc
 }  // namespace vdn
 
@@ -608,6 +792,31 @@ int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, cons
   readout_tc_kernel<<<grid, kReadoutThreads, ReadoutSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
       tq, tg, tw, F, H, T, prefix, suffix, alpha, s0, lo, hi, use_alpha, norm_w, og_bias,
       reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0, dev_err);
+  return vdn::launch_status();
+}
+
+// Bidirectional scan on tensor cores (head_dim 128): inv_split = the bf16 hi halves of the
+// F_inv inverses [F_inv, H, 128, 128] followed by the lo halves (vdn_delta_factor's
+// inv_split output); B [F_inv, H, 128, 128] fp32 (frames 0..F-1 used); alpha [F, H, 128];
+// s0 [H, 128, 128] or NULL; prefix/suffix [F, H, 128, 128] fp32.
+// Replaces branch.py:297-312 (run_scans_*), with T and Inj folded as in vdn_bidir_scan.
+int vdn_bidir_scan_tc(const void* inv_split, const float* B, const float* alpha, const float* s0, int F, int F_inv,
+                      int H, float* prefix, float* suffix, int* dev_err, void* stream) {
+  using namespace vdn::branch_tc;
+  if (!inv_split || !B || !alpha || !prefix || !suffix || F <= 0 || F > F_inv || H <= 0) return vdn::kBadArgument;
+  if (!vdn::aligned16(B) || !vdn::aligned16(alpha) || !vdn::aligned16(prefix) || !vdn::aligned16(suffix))
+    return vdn::kMisaligned;  // float4 rows
+  CUtensorMap tinv;
+  int rc = vdn::make_tmap_2d(&tinv, inv_split, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, (uint64_t)2 * F_inv * H * D, D,
+                             64, 128);
+  if (rc) return rc;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ScanSmem::kBytes);
+    attr = true;
+  }
+  scan_tc_kernel<<<dim3(H, 2), kScanThreads, ScanSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
+      tinv, B, alpha, s0, F, F_inv, H, prefix, suffix, dev_err);
   return vdn::launch_status();
 }
 

@@ -144,18 +144,28 @@ int vdn_frame_stats(const void* K, const void* V, int F, int H, int T, int D, co
 int vdn_frame_stats_tc(const void* K, const void* V, int F, int H, int T, const float* beta_logits,
                        long long ld_beta, int beta_col0, float* A, float* B, int* dev_err, void* stream);
 
-/* inv = (I + A)^-1 via Cholesky + triangular inverse; info[f, h] = order of the first
- * non-positive leading minor (0 = SPD).  text_frame >= 0: s0 = text_scale * B inv of it.
+/* inv = (I + sym(A))^-1 by Gauss-Jordan without pivoting (the pivots are ratios of leading
+ * minors); info[f, h] = order of the first non-positive leading minor (0 = SPD).
+ * text_frame >= 0: s0 = text_scale * B inv of it.  inv_split (head_dim 128, optional): the
+ * inverses again as bf16 hi halves [F, H, 128, 128] followed by the lo halves
+ * (hi = bf16(x), lo = bf16(x - hi)), the operands of vdn_bidir_scan_tc.
  * Replaces: branch.py:148-160 (VdnDelta.factor_apply), :62-71 (cholesky_ex info),
  *           :649-670 (_text_state). */
 int vdn_delta_factor(const float* A, const float* B, int F, int H, int D, float* inv, int* info,
-                     int text_frame, float text_scale, float* s0, void* stream);
+                     int text_frame, float text_scale, float* s0, void* inv_split, void* stream);
 
 /* prefix_t = (B_t + prefix_{t-1} diag(alpha_t)) inv_t (t up), suffix likewise (t down),
  * both from s0 (NULL = zero).  Replaces: branch.py:297-333 (run_scans_*),
  * runtime.py:118-150 (_run_scans_shared). */
 int vdn_bidir_scan(const float* inv, const float* B, const float* alpha, const float* s0, int F, int H, int D,
                    float* prefix, float* suffix, void* stream);
+
+/* The same scan on tensor cores (head_dim 128): one CTA per (head, direction) keeps the state
+ * in TMEM and multiplies by the inverse in three bf16 passes (hi*hi + hi*lo + lo*hi, fp32
+ * accumulation).  inv_split from vdn_delta_factor over F_inv >= F frames; B [F_inv, H, 128, 128].
+ * Replaces: branch.py:297-333 (run_scans_*). */
+int vdn_bidir_scan_tc(const void* inv_split, const float* B, const float* alpha, const float* s0, int F,
+                      int F_inv, int H, float* prefix, float* suffix, int* dev_err, void* stream);
 
 /* Gather with alpha bridge, readout Q S^T, RMSNorm over D, x output gate, into
  * out[out_row0 + f*T + s, h*D + v].  Replaces: branch.py:345-396 (gather_linear_state),

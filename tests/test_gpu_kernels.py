@@ -263,8 +263,9 @@ def test_statistics_factor_scan_match_oracle_and_report_non_spd():
     assert rel_l2(A_tc, wa) < 5e-3 and rel_l2(B_tc, wb) < 5e-3
     inv = torch.empty_like(A)
     info = torch.zeros(Fb, H, device=DEV, dtype=torch.int32)
+    split = torch.empty(2, Fb, H, D, D, device=DEV, dtype=torch.bfloat16)
     pkg._lib.call("vdn_delta_factor", A.data_ptr(), B.data_ptr(), Fb, H, D, inv.data_ptr(), info.data_ptr(), -1, 0.0,
-                  None, s)
+                  None, split.data_ptr(), s)
     eye = torch.eye(D, dtype=torch.float64)
     want_inv = torch.linalg.inv(eye + wa)
     torch.cuda.synchronize()
@@ -280,12 +281,20 @@ def test_statistics_factor_scan_match_oracle_and_report_non_spd():
     wp, wsf = vo.run_scans(trans, inj, s0.double())
     torch.cuda.synchronize()
     assert rel_l2(prefix, wp) < 1e-4 and rel_l2(suffix, wsf) < 1e-4
+    # hi + lo halves reproduce the inverse to ~2^-16, and the tensor-core scan matches
+    assert rel_l2(split[0].float() + split[1].float(), want_inv) < 2e-5
+    p_tc, s_tc = torch.empty_like(A), torch.empty_like(A)
+    pkg._lib.call("vdn_bidir_scan_tc", split.data_ptr(), B.data_ptr(), ad.data_ptr(), s0d.data_ptr(), Fb, Fb, H,
+                  p_tc.data_ptr(), s_tc.data_ptr(), st.err_ptr, s)
+    torch.cuda.synchronize()
+    st.raise_if_failed()
+    assert rel_l2(p_tc, wp) < 1e-4 and rel_l2(s_tc, wsf) < 1e-4
     # a matrix that is not SPD reports the order of its first bad leading minor
     bad = wa.clone().float()
     bad[2, 1] = -3.0 * torch.eye(D)
     bd = bad.to(DEV)
     pkg._lib.call("vdn_delta_factor", bd.data_ptr(), B.data_ptr(), Fb, H, D, inv.data_ptr(), info.data_ptr(), -1, 0.0,
-                  None, s)
+                  None, None, s)
     torch.cuda.synchronize()
     want_info = vo.cholesky_info(bad.double())
     assert torch.equal(info.cpu(), want_info)
