@@ -179,14 +179,15 @@ class BranchWorkspace:
 
 def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_raw, aux, beta_col0, ogd_col0,
                ad_col0, Fb, tpf, frame_size, bounds, bridge, text_k=None, text_v=None, text_aux=None,
-               out, out_row0, status: _lib.DeviceStatus, short_conv=("k", "v")):
+               out, out_row0, status: _lib.DeviceStatus, short_conv=("k", "v"), q_ready=False):
     """Run the branch kernels on the current stream.
 
     q_raw / k_raw / v_raw: [Fb*tpf, H*D] bf16 row views (pitch = stride(0)) of the raw
     projections of the branch frames; aux: [Fb*tpf, *] fp32 rows holding the beta logits
     (column beta_col0 + h), the output-gate bottleneck (ogd_col0 + j) and the alpha
     bottleneck (ad_col0 + j); text_k / text_v / text_aux: the same for the text rows.
-    Writes out[out_row0 + f*tpf + s, h*D + v] (bf16).
+    Writes out[out_row0 + f*tpf + s, h*D + v] (bf16).  q_ready: ws.qf already holds the q
+    features (written by the QKV GEMM epilogue).
     """
     H, D = bw.heads, bw.dim
     inner = H * D
@@ -208,7 +209,8 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
 
     feature(k_raw, "k", ws.kf, True)
     feature(v_raw, "v", ws.vf, False)
-    feature(q_raw, "q", ws.qf, True)
+    if not q_ready:
+        feature(q_raw, "q", ws.qf, True)
     aux_ld = aux.stride(0)
     call("vdn_alpha_gate", aux.data_ptr() + 4 * ad_col0, aux_ld, Fb, tpf, D, bw.alpha_up.data_ptr(),
          bw.dt_bias.data_ptr(), bw.a_log.data_ptr(), H, D, ws.alpha.data_ptr(), stream)

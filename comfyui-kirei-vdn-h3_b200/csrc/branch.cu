@@ -167,31 +167,32 @@ __global__ void __launch_bounds__(kConvThreads, 2)
       for (int s = 0; s < 5; ++s)
 #pragma unroll
         for (int dy = 0; dy < 5; ++dy) win[s][dy] = lds_bf162(base + (dy * pitch + s) * kConvCh);
-      for (int x0 = 0; x0 < gw; x0 += 5) {
+      // one output: five paired-fp32 chains (one per kernel row), then column x + 5 replaces x
+      auto step = [&](int u, int x, bool tail) {
+        float2 a[5];
 #pragma unroll
-        for (int u = 0; u < 5; ++u) {
-          const int x = x0 + u;
-          if (x < gw) {
-            float2 a[5];
+        for (int dy = 0; dy < 5; ++dy) a[dy] = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int dy = 0; dy < 5; ++dy) a[dy] = make_float2(0.f, 0.f);
+        for (int k = 0; k < 5; ++k)
 #pragma unroll
-            for (int k = 0; k < 5; ++k)
+          for (int dy = 0; dy < 5; ++dy) a[dy] = fma2(wr[dy][k], win[(u + k) % 5][dy], a[dy]);
+        const float2 sum = add2(add2(add2(a[0], a[1]), add2(a[2], a[3])), a[4]);
+        *reinterpret_cast<__nv_bfloat162*>(orow + (long long)x * ld_out) = __floats2bfloat162_rn(sum.x, sum.y);
+        if (!tail || x + 5 < pitch) {
 #pragma unroll
-              for (int dy = 0; dy < 5; ++dy) {
-                a[dy].x = fmaf(wr[dy][k].x, win[(u + k) % 5][dy].x, a[dy].x);
-                a[dy].y = fmaf(wr[dy][k].y, win[(u + k) % 5][dy].y, a[dy].y);
-              }
-            const float2 s = make_float2(((a[0].x + a[1].x) + (a[2].x + a[3].x)) + a[4].x,
-                                         ((a[0].y + a[1].y) + (a[2].y + a[3].y)) + a[4].y);
-            *reinterpret_cast<__nv_bfloat162*>(orow + (long long)x * ld_out) = __floats2bfloat162_rn(s.x, s.y);
-            if (x + 5 < pitch) {
-#pragma unroll
-              for (int dy = 0; dy < 5; ++dy) win[u][dy] = lds_bf162(base + (dy * pitch + x + 5) * kConvCh);
-            }
-          }
+          for (int dy = 0; dy < 5; ++dy) win[u][dy] = lds_bf162(base + (dy * pitch + x + 5) * kConvCh);
         }
+      };
+      int x0 = 0;
+      // main groups: outputs x0 .. x0 + 4 < gw and their column loads x + 5 <= x0 + 9 < pitch
+      for (; x0 + 5 < gw; x0 += 5) {
+#pragma unroll
+        for (int u = 0; u < 5; ++u) step(u, x0 + u, false);
       }
+      // the last 1..5 outputs, with both checks
+#pragma unroll
+      for (int u = 0; u < 5; ++u)
+        if (x0 + u < gw) step(u, x0 + u, true);
     }
     __syncthreads();  // every warp is done with `buf` before it is refilled
   }

@@ -61,7 +61,14 @@ struct Epilogue {
   int aux_col0;  // columns >= aux_col0 are written as fp32 to aux_out
   float* aux_out;
   long long ld_aux;
+  // branch q features (QKV epilogue): rows [act_row0, act_row0 + act_rows) of the q columns,
+  // activated and stored [frame][head][token][head_dim]
+  __nv_bfloat16* act_out;
+  int act_row0, act_rows, act_tpf, act_heads;
 };
+
+// x * sigmoid(x) with the fast reciprocal (the result is rounded to bf16)
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 template <int KIND>
 struct Traits;
@@ -358,6 +365,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<uint4*>(dst + 2 * j) = make_uint4(pk[j], pk[j + 1], pk[j + 2], pk[j + 3]);
             }
           }
+          if (ep.act_out && c_head < ep.norm_split) {
+            // branch q features of the video rows: silu(bf16 q) L2-normalised over the head,
+            // stored frame-head-token-dim (kernels.py:47-51 with the FHSD permute)
+            const int br = row - ep.act_row0;
+            const bool mine = row < M && br >= 0 && br < ep.act_rows;
+            float ss2 = 0.f;
+            for (int c = 0; c < hd; c += 32) {
+              tmem_ld32(tbase + h0 + c, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float y = silu_fast(bf16_round(scaled<KIND>(ep, r[j], ars, c_head + c + j, N)));
+                ss2 = fmaf(y, y, ss2);
+              }
+            }
+            const float inv2 = 1.0f / fmaxf(sqrtf(ss2), 1e-6f);
+            const int f = mine ? br / ep.act_tpf : 0, s = mine ? br - f * ep.act_tpf : 0;
+            const int head = c_head / hd;
+            __nv_bfloat16* dst = ep.act_out + (((long long)f * ep.act_heads + head) * ep.act_tpf + s) * hd;
+            for (int c = 0; c < hd; c += 32) {
+              tmem_ld32(tbase + h0 + c, r);
+              tmem_ld_wait();
+              uint32_t pk[16];
+#pragma unroll
+              for (int j = 0; j < 32; j += 2) {
+                const float a = silu_fast(bf16_round(scaled<KIND>(ep, r[j], ars, c_head + c + j, N))) * inv2;
+                const float b = silu_fast(bf16_round(scaled<KIND>(ep, r[j + 1], ars, c_head + c + j + 1, N))) * inv2;
+                pk[j / 2] = pack_bf16(a, b);
+              }
+              if (mine) {
+#pragma unroll
+                for (int j = 0; j < 16; j += 4)
+                  *reinterpret_cast<uint4*>(dst + c + 2 * j) = make_uint4(pk[j], pk[j + 1], pk[j + 2], pk[j + 3]);
+              }
+            }
+          }
         }
       } else {
         // 32-column chunks: a tile may straddle the v columns and the fp32 side columns
@@ -527,7 +570,8 @@ int vdn_qkv_gemm(int kind, const void* x, long long ldx, const void* w, long lon
                  int inner, int n_aux, int head_dim, const float* norm_w, float eps, float alpha,
                  const float* dev_scale0, const float* dev_scale1, const float* row_scale,
                  const float* col_scale, void* qkv_out, long long ld_qkv, void* qk_norm, long long ld_norm,
-                 float* aux_out, long long ld_aux, int* dev_err, void* stream) {
+                 float* aux_out, long long ld_aux, void* q_act, int act_row0, int act_rows, int act_tpf,
+                 int* dev_err, void* stream) {
   if (!x || !w || !qkv_out || !qk_norm || !norm_w) return vdn::kBadArgument;
   // the QKV epilogue stores 16-byte vectors into all three outputs
   if (!vdn::aligned16(qkv_out) || !vdn::aligned16(qk_norm) || (ld_qkv * 2) % 16 || (ld_norm * 2) % 16 ||
@@ -551,6 +595,16 @@ int vdn_qkv_gemm(int kind, const void* x, long long ldx, const void* w, long lon
   ep.aux_col0 = 3 * inner;
   ep.aux_out = aux_out;
   ep.ld_aux = ld_aux;
+  if (q_act) {
+    if (!vdn::aligned16(q_act) || act_row0 < 0 || act_rows <= 0 || act_tpf <= 0 || act_rows % act_tpf ||
+        act_row0 + act_rows > S)
+      return vdn::kBadArgument;
+    ep.act_out = reinterpret_cast<__nv_bfloat16*>(q_act);
+    ep.act_row0 = act_row0;
+    ep.act_rows = act_rows;
+    ep.act_tpf = act_tpf;
+    ep.act_heads = inner / head_dim;
+  }
   const int N = 3 * inner + n_aux;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (kind) {

@@ -9,8 +9,9 @@ the branch delta added on the video rows.
 On the device one block forward is four phases, all on the caller's stream:
 
 1. one tcgen05 GEMM of x against [W_qkv; W_gate; W_beta; W_og_down; W_alpha_down]
-   writing raw q/k/v (bf16), per-head RMS-normalised q/k (bf16) and the side
-   projections (fp32) from a single pass over x;
+   writing raw q/k/v (bf16), per-head RMS-normalised q/k (bf16), the side projections
+   (fp32) and the branch's q features (silu + L2, frame-head-token layout) from a single
+   pass over x;
 2. the branch kernels (features, alpha, statistics, Cholesky inverse, fused scan,
    gather/readout/RMSNorm/output gate) writing the branch rows of a [S, H*D] buffer;
 3. the block-sparse window attention kernel with the gate fused in its epilogue;
@@ -179,14 +180,17 @@ class FusedBlock:
         return ws
 
     # ------------------------------------------------------------------ phases
-    def _qkv(self, x, ws, status, stream):
+    def _qkv(self, x, ws, status, stream, q_act=None):
+        """q_act: (buffer, first row, rows, tokens per frame) of the branch q features the
+        epilogue writes, or None."""
         g = self.geo
         S = x.shape[0]
+        qa = (None, 0, 0, 0) if q_act is None else (q_act[0].data_ptr(),) + tuple(q_act[1:])
         if self.precision == "bf16":
             _lib.call("vdn_qkv_gemm", 0, x.data_ptr(), x.stride(0), self.w_big.data_ptr(), self.w_big.stride(0), S,
                       g.hidden, g.inner, self.n_aux, g.dim, self.norm_w.data_ptr(), self.eps, 1.0, None, None, None,
                       None, ws["qkv"].data_ptr(), ws["qkv"].stride(0), ws["qkn"].data_ptr(), ws["qkn"].stride(0),
-                      ws["aux"].data_ptr(), ws["aux"].stride(0), status.err_ptr, stream)
+                      ws["aux"].data_ptr(), ws["aux"].stride(0), *qa, status.err_ptr, stream)
             return
         kind = KIND[self.precision]
         if self.precision == "int8":
@@ -198,7 +202,7 @@ class FusedBlock:
         _lib.call("vdn_qkv_gemm", kind, xq.data.data_ptr(), xq.data.stride(0), self.w_qkv_q.data.data_ptr(),
                   self.w_qkv_q.data.stride(0), S, g.hidden, g.inner, 0, g.dim, self.norm_w.data_ptr(), self.eps, 1.0,
                   _lib.ptr(d0), _lib.ptr(d1), _lib.ptr(rs), _lib.ptr(cs), ws["qkv"].data_ptr(), ws["qkv"].stride(0),
-                  ws["qkn"].data_ptr(), ws["qkn"].stride(0), None, 0, status.err_ptr, stream)
+                  ws["qkn"].data_ptr(), ws["qkn"].stride(0), None, 0, *qa, status.err_ptr, stream)
         # side projections stay bf16 -> fp32 (gates, beta, alpha are never quantised: fp8.py:1-12)
         _lib.call("vdn_gemm", 0, x.data_ptr(), x.stride(0), None, 0, 0, self.w_side.data_ptr(),
                   self.w_side.stride(0), ws["aux"].data_ptr(), ws["aux"].stride(0), 1, S, self.n_aux, g.hidden, 1.0,
@@ -306,20 +310,25 @@ class FusedBlock:
             x = x.to(torch.bfloat16).contiguous()
         stream = _lib.stream_handle(x.device)
         ws = self.workspace(S, layout)
-        self._qkv(x, ws, status, stream)
         linear_active = linear_enabled and not layout.full_cover and self.bw is not None and "bws" in ws
+        q_act = None
         if linear_active:
             skip = layout.anchor_frames == "both"
             tpf = layout.tokens_per_frame
             Fb = layout.num_frames - 2 if skip else layout.num_frames
             r0 = layout.video_start + (tpf if skip else 0)
+            if "q" not in self.short_conv:  # q's features need no conv: the QKV epilogue writes them
+                q_act = (ws["bws"].qf, r0, Fb * tpf, tpf)
+        self._qkv(x, ws, status, stream, q_act)
+        if linear_active:
             rows = slice(r0, r0 + Fb * tpf)
             bounds_b = [(lo - 1, hi - 1) for lo, hi in layout.bounds[1:-1]] if skip else list(layout.bounds)
             qkv, aux = ws["qkv"], ws["aux"]
             kw = dict(q_raw=qkv[rows, :g.inner], k_raw=qkv[rows, g.inner:2 * g.inner],
                       v_raw=qkv[rows, 2 * g.inner:], aux=aux[rows], beta_col0=self.col_beta, ogd_col0=self.col_ogd,
                       ad_col0=self.col_ad, Fb=Fb, tpf=tpf, frame_size=layout.frame_size, bounds=bounds_b,
-                      bridge=bridge, out=ws["branch"], out_row0=r0, status=status, short_conv=self.short_conv)
+                      bridge=bridge, out=ws["branch"], out_row0=r0, status=status, short_conv=self.short_conv,
+                      q_ready=q_act is not None)
             if enable_text_state and layout.text_len > 0:
                 ts = slice(layout.text_start, layout.text_start + layout.text_len)
                 kw.update(text_k=qkv[ts, g.inner:2 * g.inner], text_v=qkv[ts, 2 * g.inner:], text_aux=aux[ts])

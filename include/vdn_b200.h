@@ -57,12 +57,16 @@ int vdn_gemm_grouped_k(int kind, const void* A, long long lda, long long group_s
  * kind / scales as in vdn_gemm (int8: row_scale per token, col_scale per channel).
  * Replaces: hybrid.py:260-268 (_qkv), hybrid.py:271-273 (q_norm / k_norm, rope_freqs=None),
  *           hybrid.py:520-522 (gate logits), branch.py:736 (beta), :743-751 (alpha down),
- *           :755 (output-gate down). */
+ *           :755 (output-gate down).  q_act (optional): the branch's q features of rows
+ * [act_row0, act_row0 + act_rows) -- silu(bf16 q) L2-normalised per head, stored
+ * [frame][head][token][head_dim] with act_tpf tokens per frame (kernels.py:47-51 and the FHSD
+ * permute of branch.py:672-689). */
 int vdn_qkv_gemm(int kind, const void* x, long long ldx, const void* w, long long ldw, int S, int hidden,
                  int inner, int n_aux, int head_dim, const float* norm_w, float eps, float alpha,
                  const float* dev_scale0, const float* dev_scale1, const float* row_scale,
                  const float* col_scale, void* qkv_out, long long ld_qkv, void* qk_norm, long long ld_norm,
-                 float* aux_out, long long ld_aux, int* dev_err, void* stream);
+                 float* aux_out, long long ld_aux, void* q_act, int act_row0, int act_rows, int act_tpf,
+                 int* dev_err, void* stream);
 
 /* Per-row symmetric int8 (scale = max(amax/127, 1e-12), round half to even).
  * src_kind: 0 bf16, 1 fp32.  Replaces: projection.py:74-97 (TensorWiseINT8 quantisation,

@@ -110,11 +110,15 @@ def test_qkv_gemm_epilogue():
     qkv = torch.empty(S, 3 * inner, device=DEV, dtype=torch.bfloat16)
     qkn = torch.empty(S, 2 * inner, device=DEV, dtype=torch.bfloat16)
     aux = torch.empty(S, n_aux, device=DEV, dtype=torch.float32)
+    # branch q features of rows [r0, r0 + Fq * tq), frame-head-token-dim
+    r0, Fq, tq = 17, 5, 40
+    qf = torch.empty(Fq, H, tq, D, device=DEV, dtype=torch.bfloat16)
     st = pkg._lib.DeviceStatus(DEV)
     xd, wd, nwd = x.to(DEV), w.to(DEV), nw.to(DEV)
     pkg._lib.call("vdn_qkv_gemm", 0, xd.data_ptr(), hidden, wd.data_ptr(), hidden, S, hidden, inner, n_aux, D,
                   nwd.data_ptr(), 1e-6, 1.0, None, None, None, None, qkv.data_ptr(), 3 * inner,
-                  qkn.data_ptr(), 2 * inner, aux.data_ptr(), n_aux, st.err_ptr, pkg._lib.stream_handle(DEV))
+                  qkn.data_ptr(), 2 * inner, aux.data_ptr(), n_aux, qf.data_ptr(), r0, Fq * tq, tq, st.err_ptr,
+                  pkg._lib.stream_handle(DEV))
     torch.cuda.synchronize()
     st.raise_if_failed()
     full = x.float() @ w.float().T
@@ -123,6 +127,9 @@ def test_qkv_gemm_epilogue():
     raw = full[:, :2 * inner].to(torch.bfloat16).float().reshape(S, 2, H, D)
     normed = raw * torch.rsqrt(raw.square().mean(-1, keepdim=True) + 1e-6) * nw.reshape(2, 1, D)
     assert rel_l2(qkn, normed.reshape(S, 2 * inner)) < 5e-3
+    qraw = full[r0:r0 + Fq * tq, :inner].to(torch.bfloat16).double().reshape(Fq * tq, H, D)
+    want_qf = vo.to_fhsd(vo.activate(qraw, True), Fq)
+    assert rel_l2(qf, want_qf) < 5e-3
 
 
 # --------------------------------------------------------------------------- window attention
