@@ -39,7 +39,9 @@ from .shard import (HeadShard, RowExchange, concat_rows, default_shard, qkv_row_
                     slice_branch_weights, split_heads_outputs)
 from .window import ATTENTION_BACKENDS, WindowPlanCache, launch_window_attention
 
-AUX_ALIGN = 256
+AUX_ALIGN = 32  # side columns padded to 32: 128-byte fp32 rows, and no extra 256-column GEMM tile
+EXCHANGE_CHUNKS = 4  # pipelined exchange / projection / gather steps of the head-sharded block
+EXCHANGE_MIN_ROWS = 4096  # per rank and chunk; shorter sequences exchange in one step
 
 
 def _weight_of(module_or_tensor):
@@ -153,7 +155,11 @@ class FusedBlock:
             }
             if self.shard is not None:
                 # per-head outputs [gated softmax | branch] side by side: one all-to-all chunk per rank
-                xchg = RowExchange(self.shard, S, 2 * g.inner, g.hidden, dev)
+                # bf16: four chunks, so the exchange and the gather of one overlap the projection
+                # of another; the quantised projections need whole-tensor activation scales (fp8)
+                chunks = (EXCHANGE_CHUNKS if self.precision == "bf16" and S >= EXCHANGE_MIN_ROWS * EXCHANGE_CHUNKS *
+                          self.shard.world else 1)
+                xchg = RowExchange(self.shard, S, 2 * g.inner, g.hidden, dev, chunks=chunks)
                 ws["xchg"] = xchg
                 ws["flat"] = xchg.send[:S, :g.inner]
                 ws["branch"] = xchg.send[:S, g.inner:]
@@ -164,7 +170,7 @@ class FusedBlock:
             if self.precision != "bf16":
                 qdt = torch.int8 if self.precision == "int8" else torch.float8_e4m3fn
                 # the row-split projection quantises only this rank's rows of all heads
-                rows_out = S if self.shard is None else self.shard.row_block(S)
+                rows_out = S if self.shard is None else ws["xchg"].cs
                 k_out = self.heads_total * g.dim
                 for name, rows, k in (("xq", S, g.hidden), ("fq", rows_out, k_out), ("bq", rows_out, k_out)):
                     sdim = rows if self.precision == "int8" else 1

@@ -7,15 +7,17 @@ statistics, the factor, the scan and the readout.  Rank r of a group of g GPUs o
 never crosses GPUs).  The ``down`` projections of alpha and the output gate (hidden ->
 head_dim) are replicated.
 
-The per-head outputs [S, 2*H/g*D] (gated softmax | branch readout) are then exchanged:
+The per-head outputs [S, 2*H/g*D] (gated softmax | branch readout) are then exchanged,
+in ``chunks`` pipelined steps (RowExchange):
 
-1. all-to-all by row block: rank r receives rows [r*Sb, (r+1)*Sb) of every rank's heads,
-   as [g][Sb][2*H/g*D] (Sb = ceil(S/g));
-2. the output projection (out_proj + to_out_linear over K = 2*H*D) runs on those Sb rows,
+1. all-to-all by row block: in chunk c rank r receives its block of rows from every rank's
+   heads, as [g][rows][2*H/g*D];
+2. the output projection (out_proj + to_out_linear over K = 2*H*D) runs on those rows,
    reading the receive buffer in place as a grouped-K operand against the output weight
    whose columns were permuted once into the same rank-major order;
-3. all-gather of the projected rows returns the full [S, hidden] output on every rank,
-   which is what the patched ``attn.forward`` returns (hybrid.py:409-579 semantics).
+3. all-gather of the projected rows (asynchronous, overlapping the next chunk's projection)
+   returns the full [S, hidden] output on every rank, which is what the patched
+   ``attn.forward`` returns (hybrid.py:409-579 semantics).
 
 The reference runs each block on one GPU; this module has no reference counterpart.
 Collectives use ``torch.distributed`` (NCCL over NVLink on the GPU box, gloo in the CPU
@@ -121,39 +123,70 @@ def rank_major_out_weight(out_w: torch.Tensor, to_out: torch.Tensor | None, head
 
 
 class RowExchange:
-    """Buffers and collectives of one sequence length: ``send`` is the rank's per-head
-    output [g*Sb, width] (rows past S stay zero), ``recv`` the all-to-all result
-    [g, Sb, width], ``out`` the gathered projection [g*Sb, hidden]."""
+    """Buffers and collectives of one sequence length, pipelined over ``chunks``.
 
-    def __init__(self, shard: HeadShard, seq_len: int, width: int, hidden: int, device, dtype=torch.bfloat16):
+    Rows are cut into g * chunks blocks of ``cs`` rows, chunk-major: chunk c holds blocks
+    c*g .. c*g + g - 1 and rank r owns block c*g + r of every chunk.  ``send`` is the rank's
+    per-head output [g*chunks*cs, width] in natural row order (rows past S stay zero), so
+    chunk c is one contiguous all-to-all send buffer; ``recv[c]`` is its result [g, cs,
+    width].  The output projection of chunk c runs while chunk c+1 is exchanged, and the
+    projected rows of chunk c are all-gathered (into a contiguous slab of the output, thanks
+    to the chunk-major order) while chunk c+1 is projected."""
+
+    def __init__(self, shard: HeadShard, seq_len: int, width: int, hidden: int, device, dtype=torch.bfloat16,
+                 chunks: int = 1):
         self.shard = shard
         self.seq_len = int(seq_len)
-        self.sb = shard.row_block(seq_len)
         g = shard.world
-        self.send = torch.zeros(g * self.sb, width, device=device, dtype=dtype)
-        self.recv = torch.empty(g, self.sb, width, device=device, dtype=dtype)
+        self.chunks = max(1, int(chunks))
+        self.cs = -(-self.seq_len // (g * self.chunks))
+        self.send = torch.zeros(g * self.chunks * self.cs, width, device=device, dtype=dtype)
+        self.recv = torch.empty(self.chunks, g, self.cs, width, device=device, dtype=dtype)
         self.hidden = int(hidden)
+        self._works = []
+
+    @property
+    def sb(self) -> int:  # rows of one block
+        return self.cs
+
+    def rows_of(self, chunk: int, rank: int | None = None) -> tuple[int, int]:
+        """(first row, row count) of ``rank``'s block of ``chunk``."""
+        r = self.shard.rank if rank is None else int(rank)
+        r0 = (chunk * self.shard.world + r) * self.cs
+        return r0, max(0, min(self.cs, self.seq_len - r0))
 
     def exchange(self):
+        """Queue the all-to-all of every chunk (asynchronous; each is waited on before use)."""
         import torch.distributed as dist
 
-        g = self.shard.world
-        dist.all_to_all_single(self.recv.view(g * self.sb, -1), self.send, group=self.shard.group)
+        g, cs = self.shard.world, self.cs
+        self._works = [dist.all_to_all_single(self.recv[c].view(g * cs, -1), self.send[c * g * cs:(c + 1) * g * cs],
+                                              group=self.shard.group, async_op=True) for c in range(self.chunks)]
 
     def project_and_gather(self, project, out: torch.Tensor | None = None) -> torch.Tensor:
-        """Run ``project(recv, rows, out_rows)`` on this rank's rows, then all-gather;
-        returns the [S, hidden] output.  ``project`` is called on every rank, with
-        rows == 0 on a rank past the end of a short sequence, so that collectives it
-        issues (the fp8 amax reduction) stay matched across ranks."""
+        """Run ``project(recv[c], rows, out_rows)`` on this rank's block of every chunk and
+        all-gather the chunk; returns the [S, hidden] output.  ``project`` is called on
+        every rank, with rows == 0 on a rank past the end of a short sequence, so that
+        collectives it issues (the fp8 amax reduction) stay matched across ranks."""
         import torch.distributed as dist
 
-        g = self.shard.world
-        if out is None or out.shape != (g * self.sb, self.hidden):
-            out = torch.empty(g * self.sb, self.hidden, device=self.send.device, dtype=self.send.dtype)
-        _, n = self.shard.rows_of(self.seq_len)
-        mine = out[self.shard.rank * self.sb:(self.shard.rank + 1) * self.sb]
-        project(self.recv, n, mine)
-        dist.all_gather_into_tensor(out, mine, group=self.shard.group)
+        g, cs = self.shard.world, self.cs
+        total = g * self.chunks * cs
+        if out is None or out.shape != (total, self.hidden):
+            out = torch.empty(total, self.hidden, device=self.send.device, dtype=self.send.dtype)
+        if not self._works:
+            self.exchange()
+        gathers = []
+        for c in range(self.chunks):
+            self._works[c].wait()  # the compute stream waits for this chunk's exchange
+            r0, n = self.rows_of(c)
+            mine = out[r0:r0 + cs]
+            project(self.recv[c], n, mine)
+            gathers.append(dist.all_gather_into_tensor(out[c * g * cs:(c + 1) * g * cs], mine,
+                                                       group=self.shard.group, async_op=True))
+        for w in gathers:
+            w.wait()
+        self._works = []
         return out[:self.seq_len]
 
 

@@ -46,15 +46,18 @@ def _emulated_sharded_forward(bw, lay, heads, dim, x, precision, world):
     blocks = [_block(bw, heads, dim, precision, sh.HeadShard(r, world, heads)) for r in range(world)]
     parts = [b.forward_heads(x, lay, plans, status) for b in blocks]
     S = x.shape[0]
-    sb = blocks[0].shard.row_block(S)
-    out = torch.zeros(world * sb, bw.out.shape[0], device=DEV, dtype=torch.bfloat16)
+    x0 = parts[0][0]["xchg"]
+    cs = x0.cs
+    out = torch.zeros(world * x0.chunks * cs, bw.out.shape[0], device=DEV, dtype=torch.bfloat16)
+    # replay the chunked all-to-all: rank r's block of chunk c is rows (c * world + r) * cs
     for r, b in enumerate(blocks):
         ws, linear_active = parts[r]
-        recv = ws["xchg"].recv
-        for src in range(world):
-            recv[src].copy_(parts[src][0]["xchg"].send[r * sb:(r + 1) * sb])
-        _, rows = b.shard.rows_of(S)
-        b.project_rows(ws, linear_active, recv, rows, out[r * sb:(r + 1) * sb], status, stream)
+        xr = ws["xchg"]
+        for c in range(xr.chunks):
+            r0, rows = xr.rows_of(c)
+            for src in range(world):
+                xr.recv[c][src].copy_(parts[src][0]["xchg"].send[r0:r0 + cs])
+            b.project_rows(ws, linear_active, xr.recv[c], rows, out[r0:r0 + cs], status, stream)
     torch.cuda.synchronize()
     status.raise_if_failed()
     return out[:S]
@@ -68,7 +71,8 @@ GEOMETRIES = {
 
 @pytest.mark.parametrize("precision", ["bf16", "int8"])
 @pytest.mark.parametrize("geom", sorted(GEOMETRIES))
-def test_sharded_block_emulated_on_one_gpu(geom, precision):
+def test_sharded_block_emulated_on_one_gpu(geom, precision, monkeypatch):
+    monkeypatch.setattr(pkg.hybrid, "EXCHANGE_MIN_ROWS", 1)  # chunked exchange even at test sizes
     c, worlds = GEOMETRIES[geom]
     H, D, hidden = c["heads"], c["dim"], c["hidden"]
     bw = vo.make_block(5, hidden, H, D)

@@ -32,6 +32,21 @@ def test_row_blocks_tile_the_sequence(S, world):
     assert covered == list(range(S))
 
 
+@pytest.mark.parametrize("S", [1, 7, 64, 26428])
+@pytest.mark.parametrize("world,chunks", [(1, 1), (2, 1), (2, 4), (8, 4), (3, 2)])
+def test_exchange_blocks_tile_the_sequence(S, world, chunks):
+    sh_ = sh.HeadShard(0, world, 24)
+    x = sh.RowExchange(sh_, S, 8, 4, "cpu", dtype=torch.float32, chunks=chunks)
+    covered = []
+    for c in range(chunks):
+        for r in range(world):
+            r0, n = x.rows_of(c, r)
+            assert r0 == (c * world + r) * x.cs and 0 <= n <= x.cs
+            covered += list(range(r0, r0 + n))
+    assert covered == list(range(S))
+    assert x.send.shape[0] == world * chunks * x.cs >= S
+
+
 def test_head_shard_rejects_uneven_split():
     with pytest.raises(ValueError):
         sh.HeadShard(0, 3, 40)
@@ -105,7 +120,7 @@ def _heads_outputs(x, bw: vo.BlockWeights, lay, heads, dim, shard: sh.HeadShard,
     return torch.cat([flat, branch], 1)
 
 
-def _worker(rank, world, port, anchors, q):
+def _worker(rank, world, port, anchors, chunks, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -118,7 +133,8 @@ def _worker(rank, world, port, anchors, q):
         bcfg = vo.BranchConfig()
         shard = sh.default_shard(H)
         assert shard.rank == rank and shard.world == world
-        xchg = sh.RowExchange(shard, lay.seq_len, 2 * shard.heads_local * D, hidden, "cpu", dtype=torch.float64)
+        xchg = sh.RowExchange(shard, lay.seq_len, 2 * shard.heads_local * D, hidden, "cpu", dtype=torch.float64,
+                              chunks=chunks)
         xchg.send[:lay.seq_len] = _heads_outputs(x, bw, lay, H, D, shard, bcfg)
         xchg.exchange()
         w_rm = sh.rank_major_out_weight(bw.out.double(), bw.branch["to_out_linear.weight"].double(), H, D, world)
@@ -135,12 +151,12 @@ def _worker(rank, world, port, anchors, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,anchors", [(2, "both"), (4, "none")])
-def test_sharded_block_matches_unsharded_oracle_on_gloo_ranks(world, anchors):
+@pytest.mark.parametrize("world,anchors,chunks", [(2, "both", 3), (4, "none", 1)])
+def test_sharded_block_matches_unsharded_oracle_on_gloo_ranks(world, anchors, chunks):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, anchors, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, anchors, chunks, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in procs]
