@@ -41,7 +41,7 @@ from .window import ATTENTION_BACKENDS, WindowPlanCache, launch_window_attention
 
 AUX_ALIGN = 32  # side columns padded to 32: 128-byte fp32 rows, and no extra 256-column GEMM tile
 EXCHANGE_CHUNKS = 4  # pipelined exchange / projection / gather steps of the head-sharded block
-EXCHANGE_MIN_ROWS = 4096  # per rank and chunk; shorter sequences exchange in one step
+EXCHANGE_MIN_ROWS = 512  # rows per rank and chunk (one wave of projection tiles); fewer: one step
 
 
 def _weight_of(module_or_tensor):
