@@ -84,6 +84,13 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
+// 32 lanes x 32 bit x 8 columns TMEM store.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
 // 32 lanes x 32 bit x 16 columns TMEM store.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
@@ -322,8 +329,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         wlo = p.vs + p.frame_lo[f] * p.tpf;
         whi = p.vs + (p.frame_hi[f] + 1) * p.tpf;
       }
-      const int acol_lo = p.anchor_cols ? p.vs + p.tpf : p.vs;  // keys < acol_lo are anchor frame 0
-      const int acol_hi = p.anchor_cols ? p.ve - p.tpf : p.ve;  // keys >= acol_hi are anchor frame F-1
       float m_run = -INFINITY, l_run = 0.f;
       int info_next = p.ktile[t0];
       for (int j = 0; j < n; ++j) {
@@ -344,6 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int valid = (info & 0xFF) + 1;
         const bool masked = (info >> 8) & 1;
         if (masked || valid < BKV) {
+          const int acol_lo = p.anchor_cols ? p.vs + p.tpf : p.vs;  // keys < acol_lo are anchor frame 0
+          const int acol_hi = p.anchor_cols ? p.ve - p.tpf : p.ve;  // keys >= acol_hi are anchor frame F-1
 #pragma unroll
           for (int c = 0; c < BKV; ++c) {
             const int key = k0 + c;
@@ -373,25 +380,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float corr = grow ? ex2(m_run - m_use) : 1.0f;  // m_run = -inf gives 0
         const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
         const float2 negm2 = make_float2(-m_use, -m_use);
-        float2 rs2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        // two row-sum chains and 16-key P chunks keep this loop within the register budget
+        float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int c0 = 0; c0 < BKV; c0 += 32) {
-          uint32_t pk[16];
+        for (int c0 = 0; c0 < BKV; c0 += 16) {
+          uint32_t pk[8];
 #pragma unroll
-          for (int c = 0; c < 32; c += 2) {
+          for (int c = 0; c < 16; c += 2) {
             const float2 x = fma2(make_float2(__uint_as_float(sr[c0 + c]), __uint_as_float(sr[c0 + c + 1])), scale2,
                                   negm2);
             // a quarter of the exponentials run on the FMA pipe to relieve the MUFU unit
             float2 e;
             e.x = ex2(x.x);
             e.y = ((c & 2) != 0) ? exp2_poly(x.y) : ex2(x.y);
-            rs2[(c >> 1) & 3] = add2(rs2[(c >> 1) & 3], e);
+            rs2[(c >> 1) & 1] = add2(rs2[(c >> 1) & 1], e);
             pk[c / 2] = pack_bf16(e.x, e.y);
           }
           // P over the first 64 columns of S_a: key 2c in the low half of column c
-          tmem_st16(s_tmem + c0 / 2, pk);
+          tmem_st8(s_tmem + c0 / 2, pk);
         }
-        const float2 rsum = add2(add2(rs2[0], rs2[1]), add2(rs2[2], rs2[3]));
+        const float2 rsum = add2(rs2[0], rs2[1]);
         const float rs = rsum.x + rsum.y;
         // O_a is stable here: S_j(a) completed, so PV_{j-1}(a) (issued before it) did too; and
         // PV_j(a) is not issued before this warpgroup signals P_j(a) below.

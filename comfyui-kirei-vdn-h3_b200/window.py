@@ -65,12 +65,19 @@ class WindowPlan:
         return len(self.tiles_per_q)
 
     def items(self, heads: int) -> np.ndarray:
-        """(head << 20) | q_tile, head-major so the CTAs in flight share one head's K/V in
-        L2; within a head the most expensive query tiles come first."""
+        """(head << 20) | q_tile in claim order.  The long items (query tiles whose rows see
+        at least twice the median number of key tiles: global rows and anchor frames) of
+        every head come first, longest first, so none of them starts near the end of the
+        queue and sets the makespan; the rest follow head-major (the CTAs in flight share one
+        head's K/V in L2), the most expensive first within a head."""
         qt = np.arange(self.n_qtiles, dtype=np.int64)
-        order = np.argsort(-self.tiles_per_q, kind="stable")
-        codes = (np.arange(heads, dtype=np.int64)[:, None] << 20) | qt[order][None, :]
-        return codes.reshape(-1).astype(np.int32)
+        cost = self.tiles_per_q.astype(np.int64)
+        order = np.argsort(-cost, kind="stable")
+        long_q = cost >= 2 * max(int(np.median(cost)), 1)
+        hs = np.arange(heads, dtype=np.int64)
+        first = [(h << 20) | q for q in order if long_q[q] for h in hs]
+        rest = [(h << 20) | q for h in hs for q in order if not long_q[q]]
+        return np.asarray(first + rest, dtype=np.int64).astype(np.int32)
 
     def key_tiles_total(self, heads: int) -> int:
         return int(self.tiles_per_q.sum()) * heads

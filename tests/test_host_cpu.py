@@ -95,8 +95,26 @@ def test_plan_items_sorted_by_cost_and_cover_all_heads():
     heads = items >> 20
     qts = items & 0xFFFFF
     costs = plan.tiles_per_q[qts]
-    assert np.all(np.diff(costs) <= 0)
     assert sorted(zip(heads.tolist(), qts.tolist())) == [(h, q) for h in range(4) for q in range(plan.n_qtiles)]
+    # the long items of every head first, longest first; then head-major, longest first per head
+    long_q = plan.tiles_per_q >= 2 * max(int(np.median(plan.tiles_per_q)), 1)
+    n_long = 4 * int(long_q.sum())
+    assert np.all(long_q[qts[:n_long]]) and not np.any(long_q[qts[n_long:]])
+    assert np.all(np.diff(costs[:n_long]) <= 0)
+    rest_heads = heads[n_long:]
+    assert np.all(np.diff(rest_heads) >= 0)
+    for h in range(4):
+        assert np.all(np.diff(costs[n_long:][rest_heads == h]) <= 0)
+
+
+def test_plan_at_config1_puts_long_items_first():
+    lay = vo.config_layout(vo.CONFIG1)
+    plan = bw.build_window_plan(lay.seq_len, lay.video_start, lay.video_end, lay.num_frames,
+                                lay.tokens_per_frame, list(lay.bounds), lay.anchor_frames)
+    items = plan.items(5)
+    costs = plan.tiles_per_q[items & 0xFFFFF]
+    # the global rows and the anchor frames see every key: those tiles lead the queue
+    assert costs[0] == costs.max() and costs.max() > 4 * np.median(costs)
 
 
 def test_plan_at_config1_is_block_sparse():
