@@ -30,7 +30,7 @@ SIGNATURES: dict[str, list] = {
     "vdn_qkv_gemm": [_I, _P, _L, _P, _L, _I, _I, _I, _I, _I, _P, _F, _F, _P, _P, _P, _P, _P, _L, _P, _L, _P, _L,
                      _P, _I, _I, _I, _P, _P],
     "vdn_window_attention": [_P, _L, _P, _L, _P, _L, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _I, _P,
-                             _P, _P, _L, _P, _L, _I, _P, _P, _P, _P],
+                             _P, _P, _P, _L, _P, _L, _I, _P, _P, _P, _P],
     "vdn_spatial_conv": [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _L, _P],
     "vdn_temporal_act": [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _P],
     "vdn_alpha_gate": [_P, _L, _I, _I, _I, _P, _P, _P, _I, _I, _P, _P],

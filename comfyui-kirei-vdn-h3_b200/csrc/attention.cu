@@ -44,9 +44,10 @@ struct Params {
   float scale_log2;
   const int* frame_lo;   // [F] first visible key frame (clamped)
   const int* frame_hi;   // [F] last visible key frame (clamped)
-  const int* items;      // [n_items] (head << 20) | query tile (256 rows)
+  const int* items;      // [n_items] (head << 20) | query tile
   int n_items;
   const int* tile_off;   // [n_qtiles + 1]
+  const int* qtile;      // [n_qtiles] (row0 << 8) | (rows - 1), rows <= 256; null: row0 = 256 * tile
   const int* ktile;      // [n_ktiles] (k0 << 9) | (masked << 8) | (valid - 1)
   __nv_bfloat16* out;
   long long ld_out;
@@ -56,6 +57,10 @@ struct Params {
   const float* gate_bias;    // [H] or null
   int* work_counter;         // zeroed before the launch; items are claimed with atomicAdd
 };
+
+__device__ __forceinline__ int q_row0(const Params& p, int qt) {
+  return p.qtile ? (p.qtile[qt] >> 8) : qt * 256;
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -203,7 +208,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(B(B_QFULL), 2 * L::kQTile);
         for (int a = 0; a < 2; ++a)
           for (int b = 0; b < kDBlocks; ++b)
-            tma_load_2d(sQ + a * L::kQTile + b * (BQ * 128), &tq, B(B_QFULL), h * D + b * 64, qt * 2 * BQ + a * BQ);
+            tma_load_2d(sQ + a * L::kQTile + b * (BQ * 128), &tq, B(B_QFULL), h * D + b * 64,
+                        q_row0(p, qt) + a * BQ);
         const int t0 = p.tile_off[qt], t1 = p.tile_off[qt + 1];
         bool ok = true;
         for (int t = t0; t < t1; ++t, ++g) {
@@ -319,7 +325,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (code < 0) break;
       const int h = code >> 20, qt = code & 0xFFFFF;
       const int t0 = p.tile_off[qt], n = p.tile_off[qt + 1] - t0;
-      const int qrow = qt * 2 * BQ + a * BQ + row_in_tile;
+      const int qinfo = p.qtile ? p.qtile[qt] : (((qt * 2 * BQ) << 8) | (2 * BQ - 1));
+      const int qrow = (qinfo >> 8) + a * BQ + row_in_tile;
+      // rows past the tile's count belong to the next tile (or lie past S): computed, not stored
+      const bool row_valid = a * BQ + row_in_tile <= (qinfo & 0xFF) && qrow < p.S;
       // Per-row visibility (window.py:327-344).
       bool dense = (qrow < p.vs) || (qrow >= p.ve);
       int wlo = 0, whi = 0;
@@ -427,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(B(B_ODONE0 + a), it & 1, abort_flag, err, kErrWaitEpilogue)) break;
       tc_fence_after();
       float gate = 1.f;
-      if (p.gate_logits && qrow < p.S) {
+      if (p.gate_logits && row_valid) {
         float z = p.gate_logits[(long long)qrow * p.ld_gate + p.gate_col0 + h];
         if (p.gate_bias) z += p.gate_bias[h];
         gate = 1.f / (1.f + __expf(-z));
@@ -445,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(B(B_OFREE0 + a));
         }
-        if (qrow < p.S) {
+        if (row_valid) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             uint4 v;
@@ -502,15 +511,17 @@ extern "C" {
 //            q and k already RMS-normalised (hybrid.py:271-273)
 //   out      [S, ld_out] bf16: gated output at columns h*D
 //   frame_lo / frame_hi [F] int32 device arrays: clamped visible key-frame range per frame
-//   items / tile_off / ktile: the block-sparse plan built by the host package (256-row
-//            query tiles)
+//   items / tile_off / qtile / ktile: the block-sparse plan built by the host package;
+//            qtile [n_qtiles] = (first row << 8) | (rows - 1) with rows <= 256, or null for
+//            query tile t = rows [256 t, 256 t + 256)
 //   gate_logits [S, ld_gate] fp32 (column gate_col0 + h) and gate_bias [H]: optional
 //   work_counter: one device int, zeroed here on the stream; launches that share it must not overlap
 // Replaces window.py:277-313 (window_softmax_grouped) + hybrid.py:518-528.
 int vdn_window_attention(const void* q, long long ld_q, const void* k, long long ld_k, const void* v, long long ld_v,
                          int S, int H, int D, int video_start, int video_end, int num_frames, int tokens_per_frame,
                          int anchor_rows, int anchor_cols, float scale, const int* frame_lo, const int* frame_hi,
-                         const int* items, int n_items, const int* tile_off, const int* ktile, void* out,
+                         const int* items, int n_items, const int* tile_off, const int* qtile, const int* ktile,
+                         void* out,
                          long long ld_out, const float* gate_logits, long long ld_gate, int gate_col0,
                          const float* gate_bias, int* work_counter, int* dev_err, void* stream) {
   if (!q || !k || !v || !out || !items || !tile_off || !ktile || !frame_lo || !frame_hi || !work_counter)
@@ -535,6 +546,7 @@ int vdn_window_attention(const void* q, long long ld_q, const void* k, long long
   p.items = items;
   p.n_items = n_items;
   p.tile_off = tile_off;
+  p.qtile = qtile;
   p.ktile = ktile;
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.ld_out = ld_out;

@@ -5,9 +5,10 @@
 tcgen05 kernel over a host-built plan instead of per-group K/V gathers and SDPA calls.
 
 Plan (built once per geometry, cached like the reference's ``_DecomposedPlan``,
-window.py:726-797): query rows are cut into 256-row tiles; for each tile the key rows
-visible to any of its rows are merged into intervals and cut into 128-key tiles that
-may start at any row.  A key tile carries a mask flag only when some row of the query
+window.py:726-797): query rows are cut into segments where they switch between seeing
+every key (text rows, anchor-frame rows) and seeing a frame window, and each segment into
+tiles of at most 256 rows; for each tile the key rows visible to any of its rows are merged
+into intervals and cut into 128-key tiles that may start at any row.  A key tile carries a mask flag only when some row of the query
 tile cannot see all of its keys; the kernel then rebuilds that row's visibility from
 the frame index.  Work items (head, query tile) are sorted by key-tile count so the
 persistent CTAs stay balanced.
@@ -26,6 +27,9 @@ from .layout import ANCHOR_FRAME_MODES, validate_layout
 
 BQ = 256  # query rows per work item: two 128-row tiles that share every key tile
 BKV = 128
+# Items at least this many times the median cost can be claimed first (None: plain head-major
+# order, which measured slightly faster at config 1 once no query tile mixes dense and windowed rows).
+LONG_ITEM_FACTOR = None
 ATTENTION_BACKENDS = ("auto", "grouped", "flex", "flash2", "decomposed", "reference", "compat", "b200")
 
 
@@ -55,6 +59,7 @@ class WindowPlan:
     frame_lo: np.ndarray  # [F] int32, clamped
     frame_hi: np.ndarray  # [F] int32, clamped
     tile_off: np.ndarray  # [nq + 1] int32
+    qtile: np.ndarray  # [nq] int32 packed (row0 << 8) | (rows - 1)
     ktile: np.ndarray  # [n_ktiles] int32 packed (k0 << 9) | (masked << 8) | (valid - 1)
     tiles_per_q: np.ndarray  # [nq]
     masked_tiles: int
@@ -64,18 +69,26 @@ class WindowPlan:
     def n_qtiles(self) -> int:
         return len(self.tiles_per_q)
 
-    def items(self, heads: int) -> np.ndarray:
-        """(head << 20) | q_tile in claim order.  The long items (query tiles whose rows see
-        at least twice the median number of key tiles: global rows and anchor frames) of
-        every head come first, longest first, so none of them starts near the end of the
-        queue and sets the makespan; the rest follow head-major (the CTAs in flight share one
-        head's K/V in L2), the most expensive first within a head."""
-        qt = np.arange(self.n_qtiles, dtype=np.int64)
+    def q_rows(self, qt: int) -> tuple[int, int]:
+        """(first row, row count) of query tile ``qt``."""
+        code = int(self.qtile[qt])
+        return code >> 8, (code & 0xFF) + 1
+
+    def items(self, heads: int, long_factor: float | None = None) -> np.ndarray:
+        """(head << 20) | q_tile in claim order: head-major (the CTAs in flight share one
+        head's K/V in L2), the most expensive first within a head.  With a ``long_factor``
+        (default ``LONG_ITEM_FACTOR``), the long items (query tiles whose rows see at least
+        that many times the median number of key tiles: text rows and anchor frames) of all
+        heads come first, head by head, so none of them starts near the end of the queue."""
+        long_factor = LONG_ITEM_FACTOR if long_factor is None else long_factor
         cost = self.tiles_per_q.astype(np.int64)
         order = np.argsort(-cost, kind="stable")
-        long_q = cost >= 2 * max(int(np.median(cost)), 1)
+        if long_factor is None:
+            long_q = np.zeros(len(cost), dtype=bool)
+        else:
+            long_q = cost >= long_factor * max(float(np.median(cost)), 1.0)
         hs = np.arange(heads, dtype=np.int64)
-        first = [(h << 20) | q for q in order if long_q[q] for h in hs]
+        first = [(h << 20) | q for h in hs for q in order if long_q[q]]
         rest = [(h << 20) | q for h in hs for q in order if not long_q[q]]
         return np.asarray(first + rest, dtype=np.int64).astype(np.int32)
 
@@ -92,6 +105,7 @@ class WindowPlan:
                 "frame_lo": torch.from_numpy(self.frame_lo).to(dev),
                 "frame_hi": torch.from_numpy(self.frame_hi).to(dev),
                 "tile_off": torch.from_numpy(self.tile_off).to(dev),
+                "qtile": torch.from_numpy(self.qtile).to(dev),
                 "ktile": torch.from_numpy(self.ktile).to(dev),
                 "items": torch.from_numpy(self.items(heads)).to(dev),
             }
@@ -120,13 +134,18 @@ def build_window_plan(seq_len, video_start, video_end, num_frames, tokens_per_fr
                 cls_cache[c] = _merge(iv)
         return cls_cache[c]
 
-    nq = (S + BQ - 1) // BQ
+    # rows that see every key: text rows and (anchor rows) the first and last frame
+    w0, w1 = (vs + tpf, ve - tpf) if a_rows else (vs, ve)
+    cuts = sorted({0, S} | ({w0, w1} if w0 < w1 else set()))
+    q_tiles = [(r0, min(b, r0 + BQ)) for a, b in zip(cuts, cuts[1:]) for r0 in range(a, b, BQ)]
+    nq = len(q_tiles)
     tile_off = np.zeros(nq + 1, dtype=np.int64)
+    qtile = np.zeros(nq, dtype=np.int64)
     ktiles = []
     tiles_per_q = np.zeros(nq, dtype=np.int64)
     masked = 0
-    for qt in range(nq):
-        r0, r1 = qt * BQ, min(S, qt * BQ + BQ)
+    for qt, (r0, r1) in enumerate(q_tiles):
+        qtile[qt] = (r0 << 8) | (r1 - r0 - 1)
         classes = set()
         if r0 < vs or r1 > ve:
             classes.add(-1)
@@ -148,7 +167,7 @@ def build_window_plan(seq_len, video_start, video_end, num_frames, tokens_per_fr
             raise ValueError(f"query tile {qt} sees no keys")
         tiles_per_q[qt] = n
         tile_off[qt + 1] = tile_off[qt] + n
-    return WindowPlan(S, vs, ve, F, tpf, a_rows, a_cols, lo, hi, tile_off.astype(np.int32),
+    return WindowPlan(S, vs, ve, F, tpf, a_rows, a_cols, lo, hi, tile_off.astype(np.int32), qtile.astype(np.int32),
                       np.asarray(ktiles, dtype=np.int64).astype(np.int32), tiles_per_q, masked)
 
 
@@ -201,7 +220,7 @@ def launch_window_attention(q, k, v, out, plan: WindowPlan, heads, dim, scale, s
         plan.seq_len, heads, dim, plan.video_start, plan.video_end, plan.num_frames, plan.tokens_per_frame,
         int(plan.anchor_rows), int(plan.anchor_cols), float(scale),
         d["frame_lo"].data_ptr(), d["frame_hi"].data_ptr(), d["items"].data_ptr(), n_items,
-        d["tile_off"].data_ptr(), d["ktile"].data_ptr(), out.data_ptr(), out.stride(0),
+        d["tile_off"].data_ptr(), d["qtile"].data_ptr(), d["ktile"].data_ptr(), out.data_ptr(), out.stride(0),
         _lib.ptr(gate_logits), gate_logits.stride(0) if gate_logits is not None else 0, int(gate_col0),
         _lib.ptr(gate_bias), status.counter_ptr, status.err_ptr, _lib.stream_handle(q.device),
     )

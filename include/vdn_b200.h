@@ -103,8 +103,9 @@ int vdn_fp8_linear_noalloc(const void* x, long long ldx, int M, int K, const voi
 
 /* Exact block-sparse window softmax attention with the per-token head gate fused.
  * q, k, v: [S, H*D] bf16 views (pitches ld_q/ld_k/ld_v); q, k already RMS-normalised.
- * frame_lo/frame_hi [F]: clamped visible key-frame range; items/tile_off/ktile: host plan
- * (window.py in the package).  out [S, ld_out] bf16 at columns h*D.
+ * frame_lo/frame_hi [F]: clamped visible key-frame range; items/tile_off/qtile/ktile: host
+ * plan (window.py in the package); qtile [n_qtiles] = (first row << 8) | (rows - 1), rows <= 256
+ * (null: tile t covers rows [256 t, 256 t + 256)).  out [S, ld_out] bf16 at columns h*D.
  * gate_logits [S, ld_gate] fp32 (column gate_col0 + h) + gate_bias [H]: optional.
  * work_counter: one device int (zeroed on the stream by the call) through which the
  * persistent CTAs claim work items; calls sharing it must not overlap on the GPU.
@@ -115,7 +116,7 @@ int vdn_window_attention(const void* q, long long ld_q, const void* k, long long
                          long long ld_v, int S, int H, int D, int video_start, int video_end, int num_frames,
                          int tokens_per_frame, int anchor_rows, int anchor_cols, float scale,
                          const int* frame_lo, const int* frame_hi, const int* items, int n_items,
-                         const int* tile_off, const int* ktile, void* out, long long ld_out,
+                         const int* tile_off, const int* qtile, const int* ktile, void* out, long long ld_out,
                          const float* gate_logits, long long ld_gate, int gate_col0, const float* gate_bias,
                          int* work_counter, int* dev_err, void* stream);
 

@@ -23,8 +23,12 @@ def _expand_plan(plan, S):
     and asserts that no (row, key) pair is visited twice."""
     vs, ve, F, tpf = plan.video_start, plan.video_end, plan.num_frames, plan.tokens_per_frame
     allowed = np.zeros((S, S), dtype=bool)
+    rows_seen = np.zeros(S, dtype=np.int32)
     for qt in range(plan.n_qtiles):
-        rows = np.arange(qt * bw.BQ, min(S, qt * bw.BQ + bw.BQ))
+        r0, n = plan.q_rows(qt)
+        assert 1 <= n <= bw.BQ and r0 + n <= S
+        rows = np.arange(r0, r0 + n)
+        rows_seen[rows] += 1
         dense = (rows < vs) | (rows >= ve)
         f = np.clip((rows - vs) // tpf, 0, F - 1)
         if plan.anchor_rows:
@@ -48,6 +52,7 @@ def _expand_plan(plan, S):
             seen[:, keys] += 1
             allowed[rows[:, None], keys[None, :]] |= ok
         assert seen.max() <= 1, "a key tile overlaps another one"
+    assert np.all(rows_seen == 1), "query tiles must tile the sequence"
     return allowed
 
 
@@ -86,35 +91,49 @@ def test_window_plan_covers_exactly_the_reference_mask(geom, anchors):
     np.testing.assert_array_equal(got, want)
 
 
-def test_plan_items_sorted_by_cost_and_cover_all_heads():
+@pytest.mark.parametrize("long_factor", [None, 1.5, 1.0])
+def test_plan_items_sorted_by_cost_and_cover_all_heads(long_factor):
     lay = vo.config_layout(vo.CONFIG0)
     plan = bw.build_window_plan(lay.seq_len, lay.video_start, lay.video_end, lay.num_frames,
                                 lay.tokens_per_frame, list(lay.bounds), lay.anchor_frames)
-    items = plan.items(4)
+    items = plan.items(4, long_factor)
     assert len(items) == 4 * plan.n_qtiles
     heads = items >> 20
     qts = items & 0xFFFFF
     costs = plan.tiles_per_q[qts]
     assert sorted(zip(heads.tolist(), qts.tolist())) == [(h, q) for h in range(4) for q in range(plan.n_qtiles)]
-    # the long items of every head first, longest first; then head-major, longest first per head
-    long_q = plan.tiles_per_q >= 2 * max(int(np.median(plan.tiles_per_q)), 1)
+    # the long items first, head by head; then head-major, longest first per head
+    if long_factor is None:
+        long_q = np.zeros(plan.n_qtiles, dtype=bool)
+    else:
+        long_q = plan.tiles_per_q >= long_factor * max(float(np.median(plan.tiles_per_q)), 1.0)
     n_long = 4 * int(long_q.sum())
     assert np.all(long_q[qts[:n_long]]) and not np.any(long_q[qts[n_long:]])
-    assert np.all(np.diff(costs[:n_long]) <= 0)
-    rest_heads = heads[n_long:]
-    assert np.all(np.diff(rest_heads) >= 0)
-    for h in range(4):
-        assert np.all(np.diff(costs[n_long:][rest_heads == h]) <= 0)
+    for lo, hi in ((0, n_long), (n_long, len(items))):
+        hh = heads[lo:hi]
+        assert np.all(np.diff(hh) >= 0)
+        for h in range(4):
+            assert np.all(np.diff(costs[lo:hi][hh == h]) <= 0)
 
 
-def test_plan_at_config1_puts_long_items_first():
+def test_plan_at_config1_cuts_query_tiles_at_dense_rows():
     lay = vo.config_layout(vo.CONFIG1)
     plan = bw.build_window_plan(lay.seq_len, lay.video_start, lay.video_end, lay.num_frames,
                                 lay.tokens_per_frame, list(lay.bounds), lay.anchor_frames)
-    items = plan.items(5)
+    w0, w1 = lay.video_start + lay.tokens_per_frame, lay.video_end - lay.tokens_per_frame
+    full = (lay.seq_len + bw.BKV - 1) // bw.BKV
+    for qt in range(plan.n_qtiles):
+        r0, n = plan.q_rows(qt)
+        # no tile mixes rows that see every key with windowed rows
+        assert (r0 + n <= w0) or (r0 >= w1) or (w0 <= r0 and r0 + n <= w1), (r0, n)
+        if r0 + n <= w0 or r0 >= w1:
+            assert plan.tiles_per_q[qt] == full
+            assert not any((int(c) >> 8) & 1 for c in plan.ktile[plan.tile_off[qt]:plan.tile_off[qt + 1]])
+    items = plan.items(5, 1.5)
     costs = plan.tiles_per_q[items & 0xFFFFF]
-    # the global rows and the anchor frames see every key: those tiles lead the queue
-    assert costs[0] == costs.max() and costs.max() > 4 * np.median(costs)
+    n_dense = 5 * int((plan.tiles_per_q == full).sum())
+    # with a long factor, the text rows and anchor frames (every key visible) lead the queue
+    assert np.all(costs[:n_dense] == full) and np.all(costs[n_dense:] < full)
 
 
 def test_plan_at_config1_is_block_sparse():
