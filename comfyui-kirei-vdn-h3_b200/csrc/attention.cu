@@ -62,6 +62,15 @@ __device__ __forceinline__ int q_row0(const Params& p, int qt) {
   return p.qtile ? (p.qtile[qt] >> 8) : qt * 256;
 }
 
+// Low min(max(n, 0), 32) bits set.
+__device__ __forceinline__ uint32_t bits_below(int n) {
+  n = min(max(n, 0), 32);
+  return n == 32 ? 0xFFFFFFFFu : ((1u << n) - 1u);
+}
+
+// Bits [a, b) of a 32-bit word (clamped to the word; empty when b <= a).
+__device__ __forceinline__ uint32_t bit_span(int a, int b) { return bits_below(b) & ~bits_below(a); }
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -106,14 +115,41 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
-// O += P V with P (A operand) in tensor memory.
-__device__ __forceinline__ void mma_f16_tmem_a(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
-                                               uint32_t accumulate) {
+// The MMAs below take shared-memory descriptors as two 32-bit words.  The low word holds the
+// start-address field (bits 0-13, address >> 4) and the leading byte offset, so a constant
+// byte offset inside one buffer is a single add of (offset >> 4) to it (smem addresses stay
+// below 256 KB: no carry leaves the field); the high word is a per-layout constant.  This keeps
+// the issuing thread at a few instructions per MMA while it shares its scheduler with two
+// busy softmax warps.
+__device__ __forceinline__ uint32_t sdesc_lo(uint32_t saddr, uint32_t lbo) {
+  return ((saddr >> 4) & 0x3FFFu) | (((lbo >> 4) & 0x3FFFu) << 16);
+}
+__host__ __device__ constexpr uint32_t sdesc_hi_sw128(uint32_t sbo) {
+  return ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);  // version 1 (bit 46), 128-byte swizzle (bits 61-63)
+}
+
+// S = Q K^T, both operands from shared memory.
+__device__ __forceinline__ void mma_ss(uint32_t d, uint32_t a_lo, uint32_t b_lo, uint32_t hi, uint32_t idesc,
+                                       uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 da, {%1, %3};\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, p;\n\t}" ::"r"(d),
+      "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// O += P V with P (A operand) in tensor memory.
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -240,12 +276,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc_s = make_idesc(1, 1, 1, 0, 0, BQ, BKV);
       constexpr uint32_t idesc_o = make_idesc(1, 1, 1, 0, 1, BQ, D);
-      auto issue_s = [&](int a, uint32_t kb) {
+      constexpr uint32_t hi_k = sdesc_hi_sw128(1024);  // K-major Q / K, and MN-major V: SBO 1024
+      const uint32_t q_lo = sdesc_lo(sQ, 16), k_lo = sdesc_lo(sK, 16), v_lo = sdesc_lo(sV, BKV * 128);
+      auto issue_s = [&](int a, int st) {
+        const uint32_t qa = q_lo + a * (L::kQTile >> 4), kb = k_lo + st * (L::kKBytes >> 4);
 #pragma unroll
         for (int s = 0; s < D / 16; ++s) {
-          const uint32_t off = (s >> 2) * (BQ * 128) + (s & 3) * 32;
-          mma_f16(tmem_base + a * 128, make_sdesc(sQ + a * L::kQTile + off, 16, 1024), make_sdesc(kb + off, 16, 1024),
-                  idesc_s, s > 0 ? 1u : 0u);
+          const uint32_t off = ((s >> 2) * (BQ * 128) + (s & 3) * 32) >> 4;
+          mma_ss(tmem_base + a * 128, qa + off, kb + off, hi_k, idesc_s, s > 0 ? 1u : 0u);
         }
         tc_commit(B(B_SFULL0 + a));
       };
@@ -266,8 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        issue_s(0, sK + (g & 1) * L::kKBytes);
-        issue_s(1, sK + (g & 1) * L::kKBytes);
+        issue_s(0, g & 1);
+        issue_s(1, g & 1);
         tc_commit(B(B_KEMPTY0 + (g & 1)));
         if (n == 1) tc_commit(B(B_QEMPTY));
         for (int j = 0; j < n && ok; ++j) {
@@ -281,11 +319,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t vb = sV + st * L::kVBytes;
+            const uint32_t vb = v_lo + st * (L::kVBytes >> 4);
 #pragma unroll
             for (int s = 0; s < BKV / 16; ++s)
-              mma_f16_tmem_a(tmem_base + 256 + a * 128, tmem_base + a * 128 + s * 8,
-                             make_sdesc(vb + s * 2048, BKV * 128, 1024), idesc_o, (j > 0 || s > 0) ? 1u : 0u);
+              mma_ts(tmem_base + 256 + a * 128, tmem_base + a * 128 + s * 8, vb + s * (2048 >> 4), hi_k, idesc_o,
+                     (j > 0 || s > 0) ? 1u : 0u);
             if (a == 1) tc_commit(B(B_VEMPTY0 + st));
             if (j == n - 1) tc_commit(B(B_ODONE0 + a));
             if (j + 1 < n) {
@@ -295,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
               }
               tc_fence_after();
-              issue_s(a, sK + st1 * L::kKBytes);
+              issue_s(a, st1);
               if (a == 1) {
                 tc_commit(B(B_KEMPTY0 + st1));
                 if (j + 1 == n - 1) tc_commit(B(B_QEMPTY));
@@ -329,14 +367,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int qrow = (qinfo >> 8) + a * BQ + row_in_tile;
       // rows past the tile's count belong to the next tile (or lie past S): computed, not stored
       const bool row_valid = a * BQ + row_in_tile <= (qinfo & 0xFF) && qrow < p.S;
-      // Per-row visibility (window.py:327-344).
-      bool dense = (qrow < p.vs) || (qrow >= p.ve);
-      int wlo = 0, whi = 0;
-      if (!dense && qrow < p.S) {
+      // Per-row visibility (window.py:327-344): a windowed row cannot see the video keys in
+      // [x0, x1) and [x2, x3) = [first non-anchor key, window start) and [window end, first
+      // key of the last anchor frame); rows that see every key get two empty spans.
+      int x0 = 0, x1 = 0, x2 = 0, x3 = 0;
+      if (qrow >= p.vs && qrow < p.ve) {
         const int f = (qrow - p.vs) / p.tpf;
-        if (p.anchor_rows && (f == 0 || f == p.F - 1)) dense = true;
-        wlo = p.vs + p.frame_lo[f] * p.tpf;
-        whi = p.vs + (p.frame_hi[f] + 1) * p.tpf;
+        if (!(p.anchor_rows && (f == 0 || f == p.F - 1))) {
+          x0 = p.anchor_cols ? p.vs + p.tpf : p.vs;
+          x1 = p.vs + p.frame_lo[f] * p.tpf;
+          x2 = p.vs + (p.frame_hi[f] + 1) * p.tpf;
+          x3 = p.anchor_cols ? p.ve - p.tpf : p.ve;
+        }
       }
       float m_run = -INFINITY, l_run = 0.f;
       int info_next = p.ktile[t0];
@@ -358,18 +400,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int valid = (info & 0xFF) + 1;
         const bool masked = (info >> 8) & 1;
         if (masked || valid < BKV) {
-          const int acol_lo = p.anchor_cols ? p.vs + p.tpf : p.vs;  // keys < acol_lo are anchor frame 0
-          const int acol_hi = p.anchor_cols ? p.ve - p.tpf : p.ve;  // keys >= acol_hi are anchor frame F-1
+          // visible keys of this row as four 32-key bit words, then one test + select per key
+          uint32_t vis[BKV / 32];
 #pragma unroll
-          for (int c = 0; c < BKV; ++c) {
-            const int key = k0 + c;
-            bool allow = c < valid;
-            if (masked && allow) {
-              allow = dense || key < p.vs || key >= p.ve || (key >= wlo && key < whi) || key < acol_lo ||
-                      key >= acol_hi;
-            }
-            if (!allow) sr[c] = __float_as_uint(-INFINITY);
+          for (int w = 0; w < BKV / 32; ++w) {
+            const int base = k0 + 32 * w;
+            uint32_t m = bits_below(valid - 32 * w);
+            if (masked) m &= ~(bit_span(x0 - base, x1 - base) | bit_span(x2 - base, x3 - base));
+            vis[w] = m;
           }
+#pragma unroll
+          for (int c = 0; c < BKV; ++c)
+            if (!((vis[c >> 5] >> (c & 31)) & 1u)) sr[c] = __float_as_uint(-INFINITY);
         }
         // tile max of the raw scores: four independent 3-input max chains
         float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};

@@ -27,6 +27,10 @@ from .layout import ANCHOR_FRAME_MODES, validate_layout
 
 BQ = 256  # query rows per work item: two 128-row tiles that share every key tile
 BKV = 128
+# Planner cost model, in unmasked key-tile steps: a masked key tile (per-row visibility
+# rebuilt in the softmax) and the fixed cost of one work item (Q load, epilogue, handoffs).
+MASKED_TILE_COST = 1.1
+ITEM_COST = 0.5
 # Items at least this many times the median cost can be claimed first (None: plain head-major
 # order, which measured slightly faster at config 1 once no query tile mixes dense and windowed rows).
 LONG_ITEM_FACTOR = None
@@ -113,7 +117,12 @@ class WindowPlan:
 
 
 def build_window_plan(seq_len, video_start, video_end, num_frames, tokens_per_frame, bounds,
-                      anchor_frames) -> WindowPlan:
+                      anchor_frames, cutting: str = "auto") -> WindowPlan:
+    """``cutting``: "class" cuts query tiles at every change of the rows' visible keys,
+    "dense" only where rows switch between seeing every key and a window, "auto" keeps the
+    cheaper of the two under the planner's cost model."""
+    if cutting not in ("auto", "class", "dense"):
+        raise ValueError(f"unknown cutting {cutting!r}")
     validate_layout(seq_len, video_start, video_end, num_frames, tokens_per_frame, bounds, anchor_frames)
     S, vs, ve, F, tpf = int(seq_len), int(video_start), int(video_end), int(num_frames), int(tokens_per_frame)
     a_rows = anchor_frames in ("rows", "both")
@@ -134,41 +143,72 @@ def build_window_plan(seq_len, video_start, video_end, num_frames, tokens_per_fr
                 cls_cache[c] = _merge(iv)
         return cls_cache[c]
 
-    # rows that see every key: text rows and (anchor rows) the first and last frame
-    w0, w1 = (vs + tpf, ve - tpf) if a_rows else (vs, ve)
-    cuts = sorted({0, S} | ({w0, w1} if w0 < w1 else set()))
-    q_tiles = [(r0, min(b, r0 + BQ)) for a, b in zip(cuts, cuts[1:]) for r0 in range(a, b, BQ)]
-    nq = len(q_tiles)
-    tile_off = np.zeros(nq + 1, dtype=np.int64)
-    qtile = np.zeros(nq, dtype=np.int64)
-    ktiles = []
-    tiles_per_q = np.zeros(nq, dtype=np.int64)
-    masked = 0
-    for qt, (r0, r1) in enumerate(q_tiles):
-        qtile[qt] = (r0 << 8) | (r1 - r0 - 1)
+    def row_class(f):
+        """Visible-key class of the rows of frame ``f``: -1 (every key) or its frame window."""
+        return -1 if (a_rows and f in (0, last)) else (int(lo[f]), int(hi[f]))
+
+    def tile_keys(r0, r1):
+        """Key tiles of query rows [r0, r1): (packed codes, number of masked tiles)."""
         classes = set()
         if r0 < vs or r1 > ve:
             classes.add(-1)
         a, b = max(r0, vs), min(r1, ve)
         if a < b:
             for f in range((a - vs) // tpf, (b - 1 - vs) // tpf + 1):
-                classes.add(-1 if (a_rows and f in (0, last)) else f)
+                classes.add(-1 if row_class(f) == -1 else f)
         ivs = {c: class_iv(c) for c in classes}
         union = _merge([iv for c in classes for iv in ivs[c]])
-        n = 0
+        codes, n_masked = [], 0
         for x, y in union:
             for k0 in range(x, y, BKV):
                 kend = min(k0 + BKV, y)
                 m = any(not _contained(k0, kend, ivs[c]) for c in classes)
-                masked += int(m)
-                ktiles.append((k0 << 9) | (int(m) << 8) | (kend - k0 - 1))
-                n += 1
-        if n == 0:
-            raise ValueError(f"query tile {qt} sees no keys")
-        tiles_per_q[qt] = n
-        tile_off[qt + 1] = tile_off[qt] + n
+                n_masked += int(m)
+                codes.append((k0 << 9) | (int(m) << 8) | (kend - k0 - 1))
+        if not codes:
+            raise ValueError(f"query rows [{r0}, {r1}) see no keys")
+        return codes, n_masked
+
+    # Row runs of one visible-key class: text rows and anchor-frame rows see every key;
+    # consecutive frames with the same window (chunked windows) share a class.
+    runs = [0]
+    prev = -1 if vs > 0 else None
+    for f in range(F):
+        c = row_class(f)
+        if c != prev:
+            runs.append(vs + f * tpf)
+            prev = c
+    if ve < S and prev != -1:
+        runs.append(ve)
+    runs = sorted(set(runs) | {S})
+    # Two cuttings of the rows into query tiles: at every class change (no masked key tiles,
+    # but a partial tile per run), or only where rows switch between seeing every key and a
+    # window (tiles may straddle frames and mask some keys).  The cheaper one is kept.
+    dense_cuts = {0, S}
+    for r0, r1 in zip(runs, runs[1:]):
+        f = (r0 - vs) // tpf if vs <= r0 < ve else None
+        dense = f is None or row_class(f) == -1
+        prev_dense = r0 == 0 or (r0 - 1 < vs or r0 - 1 >= ve or row_class((r0 - 1 - vs) // tpf) == -1)
+        if dense != prev_dense:
+            dense_cuts.add(r0)
+    candidates = {"class": [runs], "dense": [sorted(dense_cuts)], "auto": [runs, sorted(dense_cuts)]}[cutting]
+    best = None
+    for cuts in candidates:
+        q_tiles = [(r0, min(b, r0 + BQ)) for a, b in zip(cuts, cuts[1:]) for r0 in range(a, b, BQ)]
+        keys = [tile_keys(r0, r1) for r0, r1 in q_tiles]
+        cost = sum(len(c) + (MASKED_TILE_COST - 1.0) * m + ITEM_COST for c, m in keys)
+        if best is None or cost < best[0]:
+            best = (cost, q_tiles, keys)
+    _, q_tiles, keys = best
+    nq = len(q_tiles)
+    tile_off = np.zeros(nq + 1, dtype=np.int64)
+    tile_off[1:] = np.cumsum([len(c) for c, _ in keys])
+    qtile = np.array([(r0 << 8) | (r1 - r0 - 1) for r0, r1 in q_tiles], dtype=np.int64)
+    ktiles = np.asarray([code for c, _ in keys for code in c], dtype=np.int64)
+    tiles_per_q = np.array([len(c) for c, _ in keys], dtype=np.int64)
+    masked = int(sum(m for _, m in keys))
     return WindowPlan(S, vs, ve, F, tpf, a_rows, a_cols, lo, hi, tile_off.astype(np.int32), qtile.astype(np.int32),
-                      np.asarray(ktiles, dtype=np.int64).astype(np.int32), tiles_per_q, masked)
+                      ktiles.astype(np.int32), tiles_per_q, masked)
 
 
 class WindowPlanCache:

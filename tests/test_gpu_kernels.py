@@ -168,7 +168,8 @@ def test_window_attention_golden_vector():
 @pytest.mark.parametrize("geom", [(24, 9, (4, 4), 8, 2, 0, "columns", 2, 64),
                                   (512, 7, (38, 22), 0, 1, 5, "both", 2, 128),
                                   (100, 5, (20, 13), 37, 1, 2, "rows", 3, 128)])
-def test_window_attention_ragged_tiles(geom):
+@pytest.mark.parametrize("cutting", ["class", "dense"])
+def test_window_attention_ragged_tiles(geom, cutting):
     before, F, grid, after, radius, chunk, mode, H, D = geom
     tpf = grid[0] * grid[1]
     vs, ve = before, before + F * tpf
@@ -177,7 +178,12 @@ def test_window_attention_ragged_tiles(geom):
                     text_start=0, text_len=before, bounds=tuple(vo.window_bounds(F, radius, chunk)),
                     anchor_frames=mode)
     q, k, v, logits, bias = _attention_case(lay, H, D, 30)
-    got = pkg.window_softmax_b200(q.to(DEV), k.to(DEV), v.to(DEV), vs, ve, F, tpf, list(lay.bounds), D ** -0.5, mode)
+    plan = pkg.window.build_window_plan(S, vs, ve, F, tpf, list(lay.bounds), mode, cutting=cutting)
+    got = torch.empty(S, H, D, device=DEV, dtype=torch.bfloat16)
+    st = pkg.DeviceStatus(DEV)
+    pkg.window.launch_window_attention(q.to(DEV), k.to(DEV), v.to(DEV), got, plan, H, D, D ** -0.5, st)
+    torch.cuda.synchronize()
+    st.raise_if_failed()
     rows = torch.unique(torch.cat([torch.arange(0, S, 37), torch.arange(max(0, vs - 3), min(S, vs + 130)),
                                    torch.tensor([S - 1])]))
     want = vo.window_attention(q.float(), k.float(), v.float(), vs, ve, F, tpf, list(lay.bounds), D ** -0.5, mode,

@@ -71,14 +71,17 @@ GEOMS = [
 
 @pytest.mark.parametrize("geom", GEOMS)
 @pytest.mark.parametrize("anchors", vo.ANCHOR_MODES)
-def test_window_plan_covers_exactly_the_reference_mask(geom, anchors):
+@pytest.mark.parametrize("cutting", ["class", "dense"])
+def test_window_plan_covers_exactly_the_reference_mask(geom, anchors, cutting):
     before, F, tpf, after, radius, chunk = geom
     vs, ve = before, before + F * tpf
     S = ve + after
     if S > 8192 and anchors != "both":
         pytest.skip("large geometry checked in the released anchor mode only")
     bounds = vo.window_bounds(F, radius, chunk)
-    plan = bw.build_window_plan(S, vs, ve, F, tpf, bounds, anchors)
+    plan = bw.build_window_plan(S, vs, ve, F, tpf, bounds, anchors, cutting=cutting)
+    if cutting == "class":
+        assert plan.masked_tiles == 0  # every tile's rows share one visible-key set
     if S > 8192:
         # spot-check rows instead of the full [S, S] mask
         got = _expand_plan(plan, S)
