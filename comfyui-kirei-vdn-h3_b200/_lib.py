@@ -82,6 +82,8 @@ def library() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = ctypes.c_int
+        lib.vdn_launch_count.argtypes = []
+        lib.vdn_launch_count.restype = ctypes.c_longlong
         _lib = lib
     return _lib
 
@@ -98,6 +100,11 @@ def check(status: int, what: str) -> None:
 
 def call(name: str, *args) -> None:
     check(getattr(library(), name)(*args), name)
+
+
+def launch_count() -> int:
+    """Kernels launched by the library so far (host-side count; diff it around a region)."""
+    return int(library().vdn_launch_count())
 
 
 def ptr(t) -> int | None:

@@ -540,6 +540,7 @@ int launch(const void* q, long long ld_q, const void* k, long long ld_k, const v
   const int grid = p.n_items < sm_count() ? p.n_items : sm_count();
   if (grid <= 0) return kOk;
   window_attention_kernel<D><<<grid, kThreads, Layout<D>::kSmem, stream>>>(tq, tk, tv, p, err);
+  vdn::count_launch();
   return launch_status();
 }
 

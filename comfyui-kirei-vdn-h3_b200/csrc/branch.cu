@@ -865,14 +865,17 @@ int vdn_spatial_conv(const void* in, long long ld_in, const float* w, int kh, in
     spatial_conv5_tiled_kernel<<<grid, kConvThreads, stages * buf_bytes, s>>>(
         reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, F, gh, gw, C, reinterpret_cast<__nv_bfloat16*>(out),
         ld_out, stages);
+    vdn::count_launch();
   } else if (paired) {
     dim3 grid((C / 2 + 127) / 128, gh, F);
     spatial_conv5_kernel<<<grid, 128, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, gh, gw, C,
                                               reinterpret_cast<__nv_bfloat16*>(out), ld_out);
+    vdn::count_launch();
   } else {
     dim3 grid(gh, F, (C + 255) / 256);
     spatial_conv_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, kh, kw, gh, gw,
                                              C, reinterpret_cast<__nv_bfloat16*>(out), ld_out);
+    vdn::count_launch();
   }
   return vdn::launch_status();
 }
@@ -897,6 +900,7 @@ int vdn_temporal_act(const void* in, long long ld_in, const float* w, int taps, 
   else
     temporal_act_kernel<64><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, taps, F, T,
                                                     H, l2norm, reinterpret_cast<__nv_bfloat16*>(out));
+  vdn::count_launch();
   return vdn::launch_status();
 }
 
@@ -910,6 +914,7 @@ int vdn_alpha_gate(const float* down, long long ld_down, int F, int T, int R, co
   alpha_gate_kernel<<<grid, kAlphaThreads, (R + kAlphaThreads) * sizeof(float),
                       reinterpret_cast<cudaStream_t>(stream)>>>(
       down, ld_down, T, R, w_up, dt_bias, a_log, H, D, alpha);
+  vdn::count_launch();
   return vdn::launch_status();
 }
 
@@ -929,6 +934,7 @@ int vdn_frame_stats(const void* K, const void* V, int F, int H, int T, int D, co
                                                 ld_beta, beta_col0, A, B);
   else
     return vdn::kUnsupported;
+  vdn::count_launch();
   return vdn::launch_status();
 }
 
@@ -945,10 +951,18 @@ int vdn_delta_factor(const float* A, const float* B, int F, int H, int D, float*
   auto* split = reinterpret_cast<__nv_bfloat16*>(inv_split);
   if (D == 128) {
     spd_inverse_kernel<128><<<grid, 256, 0, s>>>(A, H, inv, info, split);
-    if (text_frame >= 0) text_state_kernel<128><<<H, 256, 0, s>>>(B, inv, H, text_frame, text_scale, s0);
+    vdn::count_launch();
+    if (text_frame >= 0) {
+      text_state_kernel<128><<<H, 256, 0, s>>>(B, inv, H, text_frame, text_scale, s0);
+      vdn::count_launch();
+    }
   } else if (D == 64) {
     spd_inverse_kernel<64><<<grid, 256, 0, s>>>(A, H, inv, info, nullptr);
-    if (text_frame >= 0) text_state_kernel<64><<<H, 256, 0, s>>>(B, inv, H, text_frame, text_scale, s0);
+    vdn::count_launch();
+    if (text_frame >= 0) {
+      text_state_kernel<64><<<H, 256, 0, s>>>(B, inv, H, text_frame, text_scale, s0);
+      vdn::count_launch();
+    }
   } else {
     return vdn::kUnsupported;
   }
@@ -974,10 +988,12 @@ int vdn_bidir_scan(const float* inv, const float* B, const float* alpha, const f
       attr_set = true;
     }
     bidir_scan128_kernel<<<dim3(H, 2), kScanThreads, smem, s>>>(inv, B, alpha, s0, F, H, prefix, suffix);
+    vdn::count_launch();
   } else if (D == 64) {
     const size_t smem = (size_t)(64 * 64 + 2 * RB * 64) * sizeof(float);
     bidir_scan_kernel<64, 2 * RB><<<dim3(H, 2, 64 / (2 * RB)), 256, smem, s>>>(inv, B, alpha, s0, F, H, prefix,
                                                                                suffix);
+    vdn::count_launch();
   } else {
     return vdn::kUnsupported;
   }
@@ -1001,11 +1017,13 @@ int vdn_readout(const void* Q, int F, int H, int T, int D, const float* prefix, 
                                                 alpha, s0, lo, hi, use_alpha, norm_w,
                                                 reinterpret_cast<const __nv_bfloat16*>(gate), ld_gate,
                                                 reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0);
+    vdn::count_launch();
   } else if (D == 64) {
     readout_kernel<64><<<grid, 256, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(Q), T, F, H, prefix, suffix,
                                                alpha, s0, lo, hi, use_alpha, norm_w,
                                                reinterpret_cast<const __nv_bfloat16*>(gate), ld_gate,
                                                reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0);
+    vdn::count_launch();
   } else {
     return vdn::kUnsupported;
   }
@@ -1021,6 +1039,7 @@ int vdn_cast_rows(const float* in, long long ld_in, int col0, int rows, int cols
   if (n == 0) return vdn::kOk;
   cast_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       in, ld_in, col0, rows, cols, reinterpret_cast<__nv_bfloat16*>(out), ld_out);
+  vdn::count_launch();
   return vdn::launch_status();
 }
 

@@ -757,6 +757,7 @@ int vdn_frame_stats_tc(const void* K, const void* V, int F, int H, int T, const 
   const int grid = units < vdn::sm_count() ? units : vdn::sm_count();
   frame_stats_tc_kernel<<<grid, kStatsThreads, StatsSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
       tk, tv, F, H, T, beta_logits, ld_beta, beta_col0, A, B, dev_err);
+  vdn::count_launch();
   return vdn::launch_status();
 }
 
@@ -792,6 +793,7 @@ int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, cons
   readout_tc_kernel<<<grid, kReadoutThreads, ReadoutSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
       tq, tg, tw, F, H, T, prefix, suffix, alpha, s0, lo, hi, use_alpha, norm_w, og_bias,
       reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0, dev_err);
+  vdn::count_launch();
   return vdn::launch_status();
 }
 
@@ -817,6 +819,7 @@ int vdn_bidir_scan_tc(const void* inv_split, const float* B, const float* alpha,
   }
   scan_tc_kernel<<<dim3(H, 2), kScanThreads, ScanSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
       tinv, B, alpha, s0, F, F_inv, H, prefix, suffix, dev_err);
+  vdn::count_launch();
   return vdn::launch_status();
 }
 

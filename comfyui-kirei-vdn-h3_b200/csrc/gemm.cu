@@ -481,6 +481,7 @@ int launch(const void* A, long long lda, const void* A2, long long lda2, long lo
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
   gemm_kernel<KIND><<<grid, kThreads, kSmemBytes, stream>>>(ta, ta2, tb, M, N, K, (int)k_split, kg, ep, err);
+  vdn::count_launch();
   return launch_status();
 }
 
@@ -614,5 +615,7 @@ int vdn_qkv_gemm(int kind, const void* x, long long ldx, const void* w, long lon
     default: return vdn::kBadArgument;
   }
 }
+
+long long vdn_launch_count(void) { return vdn::launch_counter().load(std::memory_order_relaxed); }
 
 }  // extern "C"

@@ -2,6 +2,7 @@
 // the driver entry point (no -lcuda link), status codes and SM-count caching.
 #pragma once
 
+#include <atomic>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -82,6 +83,14 @@ inline int sm_count() {
   if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
   return n[dev] > 0 ? n[dev] : 148;
 }
+
+// Kernel launches made by this library since it was loaded: every <<<>>> site is followed
+// by count_launch() (host side, so the count is exact without touching the device).
+inline std::atomic<long long>& launch_counter() {
+  static std::atomic<long long> n{0};
+  return n;
+}
+inline void count_launch() { launch_counter().fetch_add(1, std::memory_order_relaxed); }
 
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();

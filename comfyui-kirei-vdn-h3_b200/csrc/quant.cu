@@ -103,6 +103,7 @@ int vdn_quant_int8_rows(int src_kind, const void* x, long long ldx, int rows, in
   else
     vdn::quant::int8_rows_kernel<float><<<rows, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, K,
                                                               reinterpret_cast<int8_t*>(q), ldq, scale);
+  vdn::count_launch();
   return vdn::launch_status();
 }
 
@@ -119,13 +120,17 @@ int vdn_quant_fp8_tensor(int src_kind, const void* x, long long ldx, int rows, i
     if (src_kind == 0) {
       vdn::quant::amax_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
                                                                      rows, K, work);
+      vdn::count_launch();
       vdn::quant::fp8_cast_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
           reinterpret_cast<const __nv_bfloat16*>(x), ldx, rows, K, work, reinterpret_cast<__nv_fp8_e4m3*>(q), ldq,
           scale_out);
+      vdn::count_launch();
     } else {
       vdn::quant::amax_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, rows, K, work);
+      vdn::count_launch();
       vdn::quant::fp8_cast_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, rows, K, work,
                                                                  reinterpret_cast<__nv_fp8_e4m3*>(q), ldq, scale_out);
+      vdn::count_launch();
     }
   }
   return vdn::launch_status();
@@ -146,6 +151,7 @@ int vdn_fp8_amax(int src_kind, const void* x, long long ldx, int rows, int K, fl
                                                                      rows, K, amax);
     else
       vdn::quant::amax_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, rows, K, amax);
+    vdn::count_launch();
   }
   return vdn::launch_status();
 }
@@ -164,6 +170,7 @@ int vdn_fp8_cast(int src_kind, const void* x, long long ldx, int rows, int K, co
     else
       vdn::quant::fp8_cast_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, rows, K, amax,
                                                                  reinterpret_cast<__nv_fp8_e4m3*>(q), ldq, scale_out);
+    vdn::count_launch();
   }
   return vdn::launch_status();
 }
@@ -242,8 +249,10 @@ int vdn_fp8_linear_noalloc(const void* x, long long ldx, int M, int K, const voi
   const int blocks = (int)std::min<long long>((n + 255) / 256, 4LL * vdn::sm_count());
   vdn::quant::amax_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M,
                                                                  K, amax);
+  vdn::count_launch();
   vdn::quant::fp8_cast_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
                                                                      M, K, amax, q, K, scale);
+  vdn::count_launch();
   const int rc = vdn::launch_status();
   if (rc) return rc;
   return vdn_gemm(1, q, K, nullptr, 0, 0, w_fp8, ldw, out, ldo, 0, M, N, K, 1.0f, scale, w_scale, nullptr, nullptr,

@@ -193,6 +193,12 @@ int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, cons
 int vdn_cast_rows(const float* in, long long ld_in, int col0, int rows, int cols, void* out, long long ld_out,
                   void* stream);
 
+/* ---------------------------------------------------------------- diagnostics ----- */
+
+/* Number of kernels this library has launched since it was loaded (host-side count, one per
+ * launch; a caller takes the difference around a region to count its launches). */
+long long vdn_launch_count(void);
+
 #ifdef __cplusplus
 }
 #endif

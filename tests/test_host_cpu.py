@@ -180,6 +180,8 @@ def test_library_exports_every_declared_symbol():
     for name in sorted(declared):
         assert hasattr(lib, name), name
     assert declared == set(pkg._lib.SIGNATURES), "ctypes table and header disagree"
+    assert re.search(r"^long long vdn_launch_count\(void\);", header, flags=re.M)
+    assert pkg._lib.launch_count() == 0  # nothing launched without a GPU
 
 
 def test_missing_library_fails_loudly(monkeypatch):
