@@ -220,7 +220,7 @@ def run_reference_arm(args, c, world, rank):
     val = sorted(steps[args.warmup:])[len(steps[args.warmup:]) // 2] if args.steps else base["value"]
     fl = vo.block_flops(lay, c["heads"], c["dim"], c["hidden"])["total"]
     line = {
-        "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": metric_name(c), "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": fl / (val * 1e12) * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"config{args.config}", "tokens": lay.seq_len, "heads": c["heads"],
@@ -231,7 +231,10 @@ def run_reference_arm(args, c, world, rank):
     print(json.dumps(line), flush=True)
 
 
-METRIC = "VDN hybrid block fwd TFLOP/s at 31x836+512 tokens (ms in ms_per_step)"
+def metric_name(c) -> str:
+    """BASELINE's metric on the config's geometry (config 1: 31x836+512 tokens)."""
+    return (f"VDN hybrid block fwd TFLOP/s at {c['frames']}x{c['grid'][0] * c['grid'][1]}+{c['text']} tokens "
+            "(ms in ms_per_step)")
 
 
 def run_attention_only(args, c):
@@ -431,12 +434,13 @@ def main():
     clock_summary = clocks.summary()
     e2e_value = flops["total"] / (e2e_ms * 1e-3) / 1e12
     line = {
-        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "metric": metric_name(c), "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) x)",
         "config": {"workload": f"config{args.config}: 31x{c['grid'][0] * c['grid'][1]}+512 tokens, H={H}, D={D}, "
                                f"hidden={hidden}", "tokens": lay.seq_len, "parallelism": f"heads/{world}" if world > 1 else "none",
-                   "l2": "inputs larger than L2 (x 270 MB, weights 0.36 GB)"},
+                   "l2": f"inputs larger than L2 (x {lay.seq_len * hidden * 2 / 1e6:.0f} MB, weights "
+                         f"{(5 * H * D + 2 * H + 2 * D) * hidden * 2 / 1e9:.2f} GB)"},
         "tflop_per_step": flops["total"] / 1e12,
         "roofline": {"kernel": "window_attention_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak,
