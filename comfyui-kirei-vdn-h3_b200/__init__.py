@@ -8,11 +8,12 @@ CUDA for sm_100a loaded from the in-tree C-ABI library ``libvdn_b200.so``; there
 CPU or library fallback.
 """
 
-from . import _lib, projection, shard
+from . import _lib, dit, projection, shard
 from ._lib import DeviceStatus
 from .branch import B200LinearBranch, cholesky_runtime_scope
 from .host_io import HostStreamer
-from .hybrid import B200State, FusedBlock, make_vdn_forward, run_forward_checked
+from .dit import B200DiTBlock, make_fast_block_forward
+from .hybrid import B200State, FusedBlock, GatedResidual, make_vdn_forward, run_forward_checked
 from .layout import (ANCHOR_FRAME_MODES, VDNLayout, current_layout, full_coverage, make_layout, publish_layout,
                      window_bounds, with_window)
 from .projection import (gemm, gemm_grouped_k, prepare_projection_maps, project, quantize_rows_int8,
@@ -21,7 +22,8 @@ from .shard import HeadShard
 from .window import WindowPlanCache, build_window_plan, window_softmax_b200
 
 __all__ = [
-    "ANCHOR_FRAME_MODES", "B200LinearBranch", "B200State", "DeviceStatus", "FusedBlock", "HeadShard", "HostStreamer", "VDNLayout",
+    "ANCHOR_FRAME_MODES", "B200DiTBlock", "B200LinearBranch", "B200State", "GatedResidual",
+    "make_fast_block_forward", "DeviceStatus", "FusedBlock", "HeadShard", "HostStreamer", "VDNLayout",
     "WindowPlanCache", "gemm_grouped_k",
     "build_window_plan", "cholesky_runtime_scope", "current_layout", "full_coverage", "gemm", "make_layout",
     "make_vdn_forward", "prepare_projection_maps", "project", "publish_layout", "quantize_rows_int8",

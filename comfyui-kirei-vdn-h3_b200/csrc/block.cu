@@ -1,0 +1,141 @@
+// Pointwise stretches of the DiT block around the hybrid attention (block_kernels.py:85-93).
+//
+// The pre-norm of both residual branches, RMSNorm(x) * (1 + scale[g]) + shift[g] with g the
+// modulation row of each token, reads x from HBM once: a warp owns a row, reduces its sum of
+// squares with shuffles and writes the modulated row as bf16 and/or as per-token int8 codes
+// with their scale (the quantiser of the INT8 projections, applied to the row it just
+// produced; the later passes over the row hit L1/L2).  Roundings follow the reference's bf16
+// tensors: the RMSNorm output, 1 + scale, the product and the sum are each rounded to bf16.
+// The gated residual x + gate[g] * y is fused into the epilogue of the GEMM that makes y
+// (gemm.cu), so no other pass over the residual stream exists.
+#include "host_common.h"
+#include "sm100.cuh"
+
+namespace vdn {
+namespace block {
+
+constexpr int kRowsPerBlock = 8;  // one warp per row
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// Modulated RMSNorm of 8 consecutive columns (one 16-byte vector `vi`) of a row.
+__device__ __forceinline__ void modulate8(uint4 xv, uint4 s4, uint4 h4, const float* __restrict__ w, int vi,
+                                          float rstd, float (&y)[8]) {
+  const float4 w0 = __ldg(reinterpret_cast<const float4*>(w) + 2 * vi);
+  const float4 w1 = __ldg(reinterpret_cast<const float4*>(w) + 2 * vi + 1);
+  const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  const uint32_t xp[4] = {xv.x, xv.y, xv.z, xv.w};
+  const uint32_t sp[4] = {s4.x, s4.y, s4.z, s4.w};
+  const uint32_t hp[4] = {h4.x, h4.y, h4.z, h4.w};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const bool hi = e & 1;
+    const float xe = hi ? bf_hi(xp[e >> 1]) : bf_lo(xp[e >> 1]);
+    const float se = hi ? bf_hi(sp[e >> 1]) : bf_lo(sp[e >> 1]);
+    const float he = hi ? bf_hi(hp[e >> 1]) : bf_lo(hp[e >> 1]);
+    const float n = bf16_round(xe * rstd * wv[e]);
+    y[e] = bf16_round(bf16_round(n * bf16_round(1.0f + se)) + he);
+  }
+}
+
+// One warp per row, streaming passes over the row's 16-byte vectors: sum of squares; the
+// modulated row (bf16 out, amax); the int8 codes.
+__global__ void __launch_bounds__(256) adaln_rmsnorm_kernel(
+    const __nv_bfloat16* __restrict__ x, long long ldx, int rows, int hidden, const float* __restrict__ w, float eps,
+    const __nv_bfloat16* __restrict__ scale_tab, const __nv_bfloat16* __restrict__ shift_tab, long long ld_tab,
+    const int* __restrict__ row_group, __nv_bfloat16* __restrict__ out, long long ldo, int8_t* __restrict__ q,
+    long long ldq, float* __restrict__ q_scale) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * kRowsPerBlock + warp;
+  if (row >= rows) return;
+  const int nvec = hidden >> 3;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
+  float ss = 0.f;
+#pragma unroll 4
+  for (int vi = lane; vi < nvec; vi += 32) {
+    const uint4 v = __ldg(xr + vi);
+    const uint32_t p[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ss += bf_lo(p[e]) * bf_lo(p[e]) + bf_hi(p[e]) * bf_hi(p[e]);
+  }
+  const float rstd = rsqrtf(warp_sum(ss) / (float)hidden + eps);
+  const long long g = row_group ? row_group[row] : 0;
+  const uint4* sc = scale_tab ? reinterpret_cast<const uint4*>(scale_tab + g * ld_tab) : nullptr;
+  const uint4* sh = shift_tab ? reinterpret_cast<const uint4*>(shift_tab + g * ld_tab) : nullptr;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  float amax = 0.f;
+#pragma unroll 2
+  for (int vi = lane; vi < nvec; vi += 32) {
+    float y[8];
+    modulate8(__ldg(xr + vi), sc ? __ldg(sc + vi) : zero, sh ? __ldg(sh + vi) : zero, w, vi, rstd, y);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(y[e]));
+    if (out)
+      reinterpret_cast<uint4*>(out + row * ldo)[vi] =
+          make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
+  }
+  if (!q) return;
+  // per-token int8 (quant.cu's rule): scale = max(amax / 127, 1e-12), q = rne(y / scale)
+  const float s = fmaxf(__fdiv_rn(warp_max(amax), 127.0f), 1e-12f);
+  if (lane == 0) q_scale[row] = s;
+#pragma unroll 2
+  for (int vi = lane; vi < nvec; vi += 32) {
+    float y[8];
+    modulate8(__ldg(xr + vi), sc ? __ldg(sc + vi) : zero, sh ? __ldg(sh + vi) : zero, w, vi, rstd, y);
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float c = fminf(fmaxf(rintf(__fdiv_rn(y[e], s)), -127.f), 127.f);
+      packed[e >> 2] |= (uint32_t)(static_cast<int>(c) & 0xFF) << (8 * (e & 3));
+    }
+    reinterpret_cast<uint2*>(q + row * ldq)[vi] = make_uint2(packed[0], packed[1]);
+  }
+}
+
+}  // namespace block
+}  // namespace vdn
+
+extern "C" {
+
+// out / q[r] = RMSNorm(x[r]) * norm_w * (1 + scale_tab[g]) + shift_tab[g], g = row_group[r]
+// (block_kernels.py:85-89).  x [rows, ldx] bf16; norm_w [hidden] fp32; scale_tab / shift_tab
+// [groups, ld_tab] bf16 (either may be NULL: scale 0 / shift 0); row_group [rows] int32 (NULL:
+// every row uses group 0).  Writes out [rows, ldo] bf16 and/or q [rows, ldq] int8 with
+// q_scale [rows] fp32 (per-token int8 of the modulated row).  hidden % 8 == 0; 16-byte aligned
+// rows (8-byte for q).
+int vdn_adaln_rmsnorm(const void* x, long long ldx, int rows, int hidden, const float* norm_w, float eps,
+                      const void* scale_tab, const void* shift_tab, long long ld_tab, const int* row_group,
+                      void* out, long long ldo, void* q, long long ldq, float* q_scale, void* stream) {
+  if (!x || !norm_w || (!out && !q) || (q && !q_scale) || rows < 0 || hidden <= 0) return vdn::kBadArgument;
+  if (hidden % 8) return vdn::kUnsupported;
+  if (!vdn::aligned16(x) || (ldx * 2) % 16 || !vdn::aligned16(norm_w)) return vdn::kMisaligned;
+  if (out && (!vdn::aligned16(out) || (ldo * 2) % 16)) return vdn::kMisaligned;
+  if (q && ((reinterpret_cast<uintptr_t>(q) & 7) || ldq % 8)) return vdn::kMisaligned;
+  if ((scale_tab && !vdn::aligned16(scale_tab)) || (shift_tab && !vdn::aligned16(shift_tab)) ||
+      ((scale_tab || shift_tab) && (ld_tab * 2) % 16))
+    return vdn::kMisaligned;
+  if (rows == 0) return vdn::kOk;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned blocks = (unsigned)((rows + vdn::block::kRowsPerBlock - 1) / vdn::block::kRowsPerBlock);
+  vdn::block::adaln_rmsnorm_kernel<<<blocks, 32 * vdn::block::kRowsPerBlock, 0, s>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), ldx, rows, hidden, norm_w, eps,
+      reinterpret_cast<const __nv_bfloat16*>(scale_tab), reinterpret_cast<const __nv_bfloat16*>(shift_tab), ld_tab,
+      row_group, reinterpret_cast<__nv_bfloat16*>(out), ldo, reinterpret_cast<int8_t*>(q), ldq, q_scale);
+  vdn::count_launch();
+  return vdn::launch_status();
+}
+
+}  // extern "C"

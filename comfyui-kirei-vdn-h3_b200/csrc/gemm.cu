@@ -41,7 +41,7 @@ struct Epilogue {
   long long ldo;
   int out_kind;
   int vec_ok;  // 1 when `out` and its row pitch are 16-byte aligned (vector stores allowed)
-  int act;  // 0 none, 1 sigmoid
+  int act;  // 0 none, 1 sigmoid, 2 GELU (erf), 3 SwiGLU over paired 128-column blocks
   float alpha;
   const float* row_scale;  // [M]
   const float* col_scale;  // [N]
@@ -50,6 +50,11 @@ struct Epilogue {
   const float* col_bias;   // [N]
   const __nv_bfloat16* addend;
   long long ld_add;
+  // gated residual (block_kernels.py:92-93): out = addend + gate[row_group[row], col] * y, with
+  // y and the product rounded to bf16 like the reference's bf16 tensors
+  const int* row_group;
+  const __nv_bfloat16* group_gate;
+  long long ld_group_gate;
   // QKV extension
   int norm_cols;  // columns [0, norm_cols) are RMS-normalised per head into norm_out
   int norm_split; // columns < norm_split use norm_w[0:hd], others norm_w[hd:2hd]
@@ -69,6 +74,11 @@ struct Epilogue {
 
 // x * sigmoid(x) with the fast reciprocal (the result is rounded to bf16)
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// GELU with the error function (torch.nn.functional.gelu, approximate="none")
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
+enum Act : int { kActNone = 0, kActSigmoid = 1, kActGelu = 2, kActSwiGLU = 3 };
 
 template <int KIND>
 struct Traits;
@@ -148,8 +158,15 @@ __device__ __forceinline__ void store_plain_chunk(const Epilogue& ep, const uint
     const int c = col0 + j;
     float x = scaled<KIND>(ep, r[j], ars, c, N);
     if (ep.col_bias && c < N) x += ep.col_bias[c];
-    if (ep.act == 1) x = 1.0f / (1.0f + __expf(-x));
+    if (ep.act == kActSigmoid) x = 1.0f / (1.0f + __expf(-x));
+    if (ep.act == kActGelu) x = gelu_erf(bf16_round(x));
     v[j] = x;
+  }
+  if (ep.group_gate) {
+    const __nv_bfloat16* gate = ep.group_gate + (long long)ep.row_group[row] * ep.ld_group_gate + col0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < N) v[j] = bf16_round(bf16_round(v[j]) * __bfloat162float(gate[j]));
   }
   if (ep.addend) {
     const __nv_bfloat16* src = ep.addend + (long long)row * ep.ld_add + col0;
@@ -402,6 +419,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+      } else if (ep.act == kActSwiGLU) {
+        // columns [n0, n0 + 128) hold the gate rows and [n0 + 128, n0 + 256) the matching up
+        // rows of output columns [n0 / 2, n0 / 2 + 128) (the host interleaves W_fc1 that way):
+        // out = silu(gate) * up with the reference's bf16 roundings (block_kernels.py:113-115)
+        for (int c = 0; c < BN / 2; c += 32) {
+          if (n0 + c >= N) break;
+          uint32_t u[32];
+          tmem_ld32(tbase + c, r);
+          tmem_ld32(tbase + BN / 2 + c, u);
+          tmem_ld_wait();
+          if (row < M) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              float o[2];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int cg = n0 + c + j + e, cu = cg + BN / 2;
+                float g = scaled<KIND>(ep, r[j + e], ars, cg, N), up = scaled<KIND>(ep, u[j + e], ars, cu, N);
+                if (ep.col_bias) {
+                  g += ep.col_bias[cg];
+                  up += ep.col_bias[cu];
+                }
+                g = bf16_round(g);
+                o[e] = bf16_round(g / (1.0f + __expf(-g))) * bf16_round(up);
+              }
+              pk[j / 2] = pack_bf16(o[0], o[1]);
+            }
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ep.out) + (long long)row * ep.ldo + n0 / 2 + c;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              *reinterpret_cast<uint4*>(dst + 2 * j) = make_uint4(pk[j], pk[j + 1], pk[j + 2], pk[j + 3]);
+          }
+        }
       } else {
         // 32-column chunks: a tile may straddle the v columns and the fp32 side columns
         for (int c = 0; c < BN; c += 32) {
@@ -522,6 +573,7 @@ int vdn_gemm(int kind, const void* A, long long lda, const void* A2, long long l
              int* dev_err, void* stream) {
   if (!A || !B || !C) return vdn::kBadArgument;
   if (out_kind == vdn::gemm::kOutS32 && kind != 2) return vdn::kBadArgument;
+  if (act < vdn::gemm::kActNone || act > vdn::gemm::kActGelu) return vdn::kBadArgument;
   Epilogue ep = plain_epilogue(C, ldc, out_kind, alpha, row_scale, col_scale, col_bias, act, addend, ld_add);
   ep.dev_scale0 = dev_scale0;
   ep.dev_scale1 = dev_scale1;
@@ -547,6 +599,7 @@ int vdn_gemm_grouped_k(int kind, const void* A, long long lda, long long group_s
   if (groups <= 0 || kg <= 0) return vdn::kBadArgument;
   if (out_kind == vdn::gemm::kOutS32 && kind != 2) return vdn::kBadArgument;
   if (group_stride < (long long)M * lda) return vdn::kBadArgument;  // slabs must not overlap
+  if (act < vdn::gemm::kActNone || act > vdn::gemm::kActGelu) return vdn::kBadArgument;
   Epilogue ep = plain_epilogue(C, ldc, out_kind, alpha, row_scale, col_scale, col_bias, act, addend, ld_add);
   ep.dev_scale0 = dev_scale0;
   ep.dev_scale1 = dev_scale1;
@@ -612,6 +665,45 @@ int vdn_qkv_gemm(int kind, const void* x, long long ldx, const void* w, long lon
     case 0: return vdn::gemm::launch<0>(x, ldx, nullptr, 0, 0, w, ldw, S, N, hidden, ep, dev_err, s);
     case 1: return vdn::gemm::launch<1>(x, ldx, nullptr, 0, 0, w, ldw, S, N, hidden, ep, dev_err, s);
     case 2: return vdn::gemm::launch<2>(x, ldx, nullptr, 0, 0, w, ldw, S, N, hidden, ep, dev_err, s);
+    default: return vdn::kBadArgument;
+  }
+}
+
+// Block projections with the DiT pointwise work fused into the epilogue (block_kernels.py):
+//   C[M, N'] bf16 = residual + gate[row_group[row]] * act(alpha * dev scales * row_scale * col_scale * (A B^T)
+//                   + bias)
+// act: 0 none, 2 GELU (erf), 3 SwiGLU over paired 128-row blocks of B (N' = N / 2, N % 256 == 0).
+// A: one source (A2 = NULL, kg = 0), K-concatenated (A2 for k >= k_split) or grouped-K (kg > 0:
+// `groups` = K / kg slabs `group_stride` apart).  residual [M, ld_res] bf16 and the gate table
+// [groups of rows, ld_gate] bf16 with row_group [M] int32 are optional (both or neither gate).
+int vdn_gemm_block(int kind, const void* A, long long lda, const void* A2, long long lda2, long long k_split,
+                   long long group_stride, int kg, const void* B, long long ldb, void* C, long long ldc, int M,
+                   int N, int K, float alpha, const float* dev_scale0, const float* dev_scale1,
+                   const float* row_scale, const float* col_scale, const float* col_bias, int act,
+                   const void* residual, long long ld_res,
+                   const int* row_group, const void* group_gate, long long ld_gate, int* dev_err, void* stream) {
+  if (!A || !B || !C) return vdn::kBadArgument;
+  if (act != vdn::gemm::kActNone && act != vdn::gemm::kActGelu && act != vdn::gemm::kActSwiGLU)
+    return vdn::kBadArgument;
+  if ((row_group == nullptr) != (group_gate == nullptr)) return vdn::kBadArgument;
+  if (act == vdn::gemm::kActSwiGLU) {
+    // one tile = one gate block + its up block; the vector stores need 16-byte rows
+    if (N % vdn::gemm::BN || group_gate || residual) return vdn::kUnsupported;
+    if (!vdn::aligned16(C) || (ldc * 2) % 16) return vdn::kMisaligned;
+  }
+  if (kg > 0 && (A2 || group_stride < (long long)M * lda)) return vdn::kBadArgument;
+  Epilogue ep = plain_epilogue(C, ldc, vdn::gemm::kOutBF16, alpha, row_scale, col_scale, col_bias, act, residual,
+                               ld_res);
+  ep.dev_scale0 = dev_scale0;
+  ep.dev_scale1 = dev_scale1;
+  ep.row_group = row_group;
+  ep.group_gate = reinterpret_cast<const __nv_bfloat16*>(group_gate);
+  ep.ld_group_gate = ld_gate;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (kind) {
+    case 0: return vdn::gemm::launch<0>(A, lda, A2, lda2, k_split, B, ldb, M, N, K, ep, dev_err, s, group_stride, kg);
+    case 1: return vdn::gemm::launch<1>(A, lda, A2, lda2, k_split, B, ldb, M, N, K, ep, dev_err, s, group_stride, kg);
+    case 2: return vdn::gemm::launch<2>(A, lda, A2, lda2, k_split, B, ldb, M, N, K, ep, dev_err, s, group_stride, kg);
     default: return vdn::kBadArgument;
   }
 }

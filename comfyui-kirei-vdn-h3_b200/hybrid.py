@@ -50,6 +50,41 @@ def _weight_of(module_or_tensor):
 
 
 @dataclass
+class GatedResidual:
+    """``x + gate[group[row]] * y`` fused into the projection that makes y (the DiT block's
+    post-branch residual, block_kernels.py:92-93): x [S, hidden] bf16, gate [groups, hidden]
+    bf16, group [S] int32."""
+
+    x: torch.Tensor
+    gate: torch.Tensor
+    group: torch.Tensor
+
+    def rows(self, r0: int, n: int) -> "GatedResidual":
+        return GatedResidual(self.x[r0:r0 + n], self.gate, self.group[r0:r0 + n])
+
+
+def gemm_block(kind, a, w, out, *, a2=None, k_split=0, grouped=None, alpha=1.0, dev_scales=(None, None),
+               row_scale=None, col_scale=None, col_bias=None, act=0, residual: GatedResidual | None = None,
+               addend=None, status, stream, rows=None, k=None):
+    """One ``vdn_gemm_block`` call: out[:rows] = (residual or addend) + gate * act(scales * a w^T + bias).
+    ``grouped`` = (groups, kg, group_stride) reads ``a`` as a grouped-K operand."""
+    M = a.shape[-2] if rows is None else int(rows)
+    K = (k if k is not None else (grouped[0] * grouped[1] if grouped else a.shape[-1] + (0 if a2 is None else
+                                                                                          a2.shape[-1])))
+    N = w.shape[0]
+    groups, kg, gstride = grouped if grouped else (0, 0, 0)
+    lda = a.stride(-2)
+    res = residual.x if residual is not None else addend
+    _lib.call("vdn_gemm_block", kind, a.data_ptr(), lda, _lib.ptr(a2), a2.stride(0) if a2 is not None else 0,
+              int(k_split), int(gstride), int(kg), w.data_ptr(), w.stride(0), out.data_ptr(), out.stride(0), M, N, K,
+              float(alpha), _lib.ptr(dev_scales[0]), _lib.ptr(dev_scales[1]), _lib.ptr(row_scale), _lib.ptr(col_scale),
+              _lib.ptr(col_bias), int(act), _lib.ptr(res), res.stride(0) if res is not None else 0,
+              _lib.ptr(residual.group if residual is not None else None),
+              _lib.ptr(residual.gate if residual is not None else None),
+              residual.gate.stride(0) if residual is not None else 0, status.err_ptr, stream)
+
+
+@dataclass
 class BlockGeometry:
     heads: int
     dim: int
@@ -214,28 +249,29 @@ class FusedBlock:
                   self.w_side.stride(0), ws["aux"].data_ptr(), ws["aux"].stride(0), 1, S, self.n_aux, g.hidden, 1.0,
                   None, None, None, None, None, 0, None, 0, status.err_ptr, stream)
 
-    def _out(self, ws, out, with_branch, status, stream):
+    def _out(self, ws, out, with_branch, status, stream, residual: GatedResidual | None = None):
         g = self.geo
         S = out.shape[0]
         if self.precision == "bf16":
-            K = 2 * g.inner if with_branch else g.inner
             a2 = ws["branch"] if with_branch else None
-            _lib.call("vdn_gemm", 0, ws["flat"].data_ptr(), ws["flat"].stride(0), _lib.ptr(a2),
-                      ws["branch"].stride(0) if with_branch else 0, g.inner if with_branch else 0,
-                      self.w_out_cat.data_ptr(), self.w_out_cat.stride(0), out.data_ptr(), out.stride(0), 0, S,
-                      g.hidden, K, 1.0, None, None, None, None, None, 0, None, 0, status.err_ptr, stream)
+            gemm_block(0, ws["flat"], self.w_out_cat, out, a2=a2, k_split=g.inner if with_branch else 0,
+                       k=2 * g.inner if with_branch else g.inner, residual=residual, status=status, stream=stream,
+                       rows=S)
             return
-        self._quantized_out(ws["flat"], ws["branch"] if with_branch else None, ws, out, status, stream)
+        self._quantized_out(ws["flat"], ws["branch"] if with_branch else None, ws, out, status, stream,
+                            residual=residual)
 
-    def _quantized_out(self, flat, branch, ws, out, status, stream, amax_reduce=None):
+    def _quantized_out(self, flat, branch, ws, out, status, stream, amax_reduce=None,
+                       residual: GatedResidual | None = None):
         """out = Q(flat) W_out^T (+ Q(branch) W_to^T as an addend pass), quantised
         activations: int8 per row, fp8 per tensor (``amax_reduce`` combines the amax of
-        the ranks' row blocks)."""
+        the ranks' row blocks).  With a ``residual`` both passes are gated and the first
+        adds the residual stream."""
         kind = KIND[self.precision]
         rows = flat.shape[0]
         K = flat.shape[1]
 
-        def quantized_gemm(src, buf: QuantizedMatrix, w: QuantizedMatrix, addend):
+        def quantized_gemm(src, buf: QuantizedMatrix, w: QuantizedMatrix, addend, first):
             if rows == 0 and self.precision == "int8":
                 return  # per-row scales: nothing to combine across ranks
             buf = QuantizedMatrix(buf.data[:rows], buf.scale[:rows] if self.precision == "int8" else buf.scale,
@@ -248,34 +284,37 @@ class FusedBlock:
                 rs, cs, d0, d1 = None, None, qa.scale, w.scale
             if rows == 0:
                 return
-            _lib.call("vdn_gemm", kind, qa.data.data_ptr(), qa.data.stride(0), None, 0, 0, w.data.data_ptr(),
-                      w.data.stride(0), out.data_ptr(), out.stride(0), 0, rows, out.shape[1], K, 1.0, _lib.ptr(d0),
-                      _lib.ptr(d1), _lib.ptr(rs), _lib.ptr(cs), None, 0, _lib.ptr(addend),
-                      addend.stride(0) if addend is not None else 0, status.err_ptr, stream)
+            res = None
+            if residual is not None:
+                res = residual if first else GatedResidual(out, residual.gate, residual.group)
+            gemm_block(kind, qa.data, w.data, out, dev_scales=(d0, d1), row_scale=rs, col_scale=cs, residual=res,
+                       addend=None if res is not None else addend, status=status, stream=stream, rows=rows, k=K)
 
-        quantized_gemm(flat, ws["fq"], self.w_out_q, None)
+        quantized_gemm(flat, ws["fq"], self.w_out_q, None, True)
         if branch is not None and self.w_to_q is not None:
-            quantized_gemm(branch, ws["bq"], self.w_to_q, out)
+            quantized_gemm(branch, ws["bq"], self.w_to_q, out, False)
 
-    def project_rows(self, ws, with_branch, recv, rows, out_rows, status, stream, amax_reduce=None):
+    def project_rows(self, ws, with_branch, recv, rows, out_rows, status, stream, amax_reduce=None,
+                     residual: GatedResidual | None = None):
         """Head-sharded phase 4 on this rank: the output projection of ``rows`` rows from
-        the all-to-all receive buffer ``recv`` [ranks, Sb, 2*H/g*D] into ``out_rows``."""
+        the all-to-all receive buffer ``recv`` [ranks, Sb, 2*H/g*D] into ``out_rows``
+        (``residual``: already restricted to those rows)."""
         g = self.geo
         world = recv.shape[0]
         if self.precision == "bf16":
             if rows > 0:
-                _lib.call("vdn_gemm_grouped_k", 0, recv.data_ptr(), recv.stride(1), recv.stride(0), world,
-                          2 * g.inner, self.w_out_cat.data_ptr(), self.w_out_cat.stride(0), out_rows.data_ptr(),
-                          out_rows.stride(0), 0, rows, g.hidden, 1.0, None, None, None, None, None, 0, None, 0,
-                          status.err_ptr, stream)
+                gemm_block(0, recv, self.w_out_cat, out_rows, grouped=(world, 2 * g.inner, recv.stride(0)),
+                           residual=residual, status=status, stream=stream, rows=rows)
             return
         flat, branch = split_heads_outputs(concat_rows(recv, rows), world, g.inner)
         self._quantized_out(flat, branch if with_branch else None, ws, out_rows, status, stream,
-                            amax_reduce=amax_reduce)
+                            amax_reduce=amax_reduce, residual=residual)
 
-    def _out_sharded(self, ws, with_branch, status, stream) -> torch.Tensor:
+    def _out_sharded(self, ws, with_branch, status, stream, residual: GatedResidual | None = None,
+                     row_epilogue=None) -> torch.Tensor:
         """All-to-all of the per-head outputs by row block, the output projection on this
-        rank's rows (grouped-K over the receive buffer), all-gather of the rows."""
+        rank's rows (grouped-K over the receive buffer), ``row_epilogue(rows_view, row0,
+        n)`` on them (the DiT block's token-parallel MLP), all-gather of the rows."""
         sh = self.shard
         xchg: RowExchange = ws["xchg"]
         xchg.exchange()
@@ -286,24 +325,34 @@ class FusedBlock:
             def amax_reduce(t):
                 dist.all_reduce(t, op=dist.ReduceOp.MAX, group=sh.group)
 
-        return xchg.project_and_gather(
-            lambda recv, rows, out_rows: self.project_rows(ws, with_branch, recv, rows, out_rows, status, stream,
-                                                           amax_reduce))
+        def project(recv, rows, out_rows, row0):
+            self.project_rows(ws, with_branch, recv, rows, out_rows, status, stream, amax_reduce,
+                              residual.rows(row0, rows) if residual is not None else None)
+            if row_epilogue is not None:
+                row_epilogue(out_rows[:rows], row0, rows)
+
+        return xchg.project_and_gather(project)
 
     def forward(self, x: torch.Tensor, layout: VDNLayout, plans: WindowPlanCache, status: _lib.DeviceStatus,
-                *, linear_enabled=True, bridge="alpha", enable_text_state=True, out=None) -> torch.Tensor:
+                *, linear_enabled=True, bridge="alpha", enable_text_state=True, out=None,
+                residual: GatedResidual | None = None, row_epilogue=None) -> torch.Tensor:
+        """The block output [S, hidden]; with ``residual`` the gated residual stream
+        ``residual.x + gate * block(x)`` instead, and ``row_epilogue(rows_view, row0, n)``
+        run on the projected rows (in place) before they leave this GPU."""
         ws, linear_active = self.forward_heads(x, layout, plans, status, linear_enabled=linear_enabled,
                                                bridge=bridge, enable_text_state=enable_text_state)
         stream = _lib.stream_handle(x.device)
         if self.shard is not None:
-            full = self._out_sharded(ws, linear_active, status, stream)
+            full = self._out_sharded(ws, linear_active, status, stream, residual, row_epilogue)
             if out is None:
                 return full
             out.copy_(full)
             return out
         if out is None:
             out = torch.empty(x.shape[0], self.geo.hidden, device=x.device, dtype=torch.bfloat16)
-        self._out(ws, out, linear_active, status, stream)
+        self._out(ws, out, linear_active, status, stream, residual)
+        if row_epilogue is not None:
+            row_epilogue(out, 0, out.shape[0])
         return out
 
     def forward_heads(self, x: torch.Tensor, layout: VDNLayout, plans: WindowPlanCache, status: _lib.DeviceStatus,

@@ -164,7 +164,7 @@ class RowExchange:
                                               group=self.shard.group, async_op=True) for c in range(self.chunks)]
 
     def project_and_gather(self, project, out: torch.Tensor | None = None) -> torch.Tensor:
-        """Run ``project(recv[c], rows, out_rows)`` on this rank's block of every chunk and
+        """Run ``project(recv[c], rows, out_rows, row0)`` on this rank's block of every chunk and
         all-gather the chunk; returns the [S, hidden] output.  ``project`` is called on
         every rank, with rows == 0 on a rank past the end of a short sequence, so that
         collectives it issues (the fp8 amax reduction) stay matched across ranks."""
@@ -181,7 +181,7 @@ class RowExchange:
             self._works[c].wait()  # the compute stream waits for this chunk's exchange
             r0, n = self.rows_of(c)
             mine = out[r0:r0 + cs]
-            project(self.recv[c], n, mine)
+            project(self.recv[c], n, mine, r0)
             gathers.append(dist.all_gather_into_tensor(out[c * g * cs:(c + 1) * g * cs], mine,
                                                        group=self.shard.group, async_op=True))
         for w in gathers:

@@ -193,6 +193,31 @@ int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, cons
 int vdn_cast_rows(const float* in, long long ld_in, int col0, int rows, int cols, void* out, long long ld_out,
                   void* stream);
 
+/* ---------------------------------------------------------------- DiT block -------- */
+
+/* out / q[r] = RMSNorm(x[r]) * norm_w * (1 + scale_tab[g]) + shift_tab[g], g = row_group[r].
+ * x [rows, ldx] bf16, norm_w [hidden] fp32, tables [groups, ld_tab] bf16 (NULL: 0),
+ * row_group [rows] int32 (NULL: group 0).  Writes out [rows, ldo] bf16 and/or per-token int8
+ * q [rows, ldq] with q_scale [rows] fp32.  hidden % 8 == 0.
+ * Replaces: block_kernels.py:85-89 (_pre_body) and the activation quantiser of the INT8 MLP. */
+int vdn_adaln_rmsnorm(const void* x, long long ldx, int rows, int hidden, const float* norm_w, float eps,
+                      const void* scale_tab, const void* shift_tab, long long ld_tab, const int* row_group,
+                      void* out, long long ldo, void* q, long long ldq, float* q_scale, void* stream);
+
+/* C [M, N'] bf16 = residual + gate[row_group[row]] * act(alpha * dev_scale0 * dev_scale1 * row_scale * col_scale
+ * * (A B^T) + col_bias).  act: 0 none, 2 GELU (erf), 3 SwiGLU (B's rows interleaved in 128-row
+ * gate / up blocks, N % 256 == 0, N' = N / 2).  A: one source, K-concatenated (A2 for
+ * k >= k_split) or grouped-K (kg > 0, K / kg slabs group_stride apart).  residual [M, ld_res]
+ * bf16 and (row_group [M] int32, group_gate [groups, ld_gate] bf16) are optional.
+ * Replaces: block_kernels.py:92-93 (_post_body) fused into the projection that feeds it,
+ * :113-146 (fc1, SwiGLU, fc2). */
+int vdn_gemm_block(int kind, const void* A, long long lda, const void* A2, long long lda2, long long k_split,
+                   long long group_stride, int kg, const void* B, long long ldb, void* C, long long ldc, int M,
+                   int N, int K, float alpha, const float* dev_scale0, const float* dev_scale1,
+                   const float* row_scale, const float* col_scale, const float* col_bias, int act,
+                   const void* residual, long long ld_res,
+                   const int* row_group, const void* group_gate, long long ld_gate, int* dev_err, void* stream);
+
 /* ---------------------------------------------------------------- diagnostics ----- */
 
 /* Number of kernels this library has launched since it was loaded (host-side count, one per

@@ -630,3 +630,117 @@ def block_flops(lay: Layout, heads, dim, hidden, *, branch=True) -> dict:
         fl["readout"] = 2.0 * rows * heads * dim * dim
     fl["total"] = sum(fl.values())
     return fl
+
+
+# ---------------------------------------------------------------------------------------
+# DiT block around the hybrid attention (block_kernels.py:85-240)
+# ---------------------------------------------------------------------------------------
+
+MOD_NAMES = ("shift_msa", "scale_msa", "gate_msa", "shift_mlp", "scale_mlp", "gate_mlp")
+
+
+@dataclass
+class DiTWeights:
+    """One MiniMax-H3 DiT block: its attention block plus norm1/norm2 and the MLP."""
+
+    attn: BlockWeights
+    norm1: torch.Tensor  # [hidden]
+    norm2: torch.Tensor  # [hidden]
+    fc1: torch.Tensor  # [2F, hidden] (SwiGLU: gate rows then up rows) or [F, hidden] (GELU)
+    fc1_b: torch.Tensor | None
+    fc2: torch.Tensor  # [hidden, F]
+    fc2_b: torch.Tensor | None
+    eps: float = 1e-6
+
+
+def segment_rows(segments, rows) -> torch.Tensor:
+    """Modulation row index of every token (block_kernels.py:34-60, int segments)."""
+    ids = torch.empty(rows, dtype=torch.long)
+    covered = 0
+    for start, stop, row in segments:
+        if start != covered or stop < start or stop > rows:
+            raise ValueError("MiniMax-H3 modulation segments must cover the sequence contiguously")
+        ids[start:stop] = int(row)
+        covered = stop
+    if covered != rows:
+        raise ValueError(f"MiniMax-H3 modulation segments cover {covered}/{rows} rows")
+    return ids
+
+
+def dit_pre(x, weight, eps, scale, shift, idx):
+    """RMSNorm(x) * weight * (1 + scale[idx]) + shift[idx] (block_kernels.py:85-89)."""
+    return rms_norm(_t(x), weight, eps) * (1.0 + _t(scale)[idx]) + _t(shift)[idx]
+
+
+def dit_post(residual, gate, idx, branch_out):
+    """residual + gate[idx] * branch_out (block_kernels.py:92-93)."""
+    return _t(residual) + _t(gate)[idx] * _t(branch_out)
+
+
+def dit_mlp(h, dw: DiTWeights, activation="swiglu", precision="bf16"):
+    """fc2(act(fc1(h))): SwiGLU silu(gate) * up over fc1's two row halves
+    (block_kernels.py:113-146), or GELU (erf) over one fc1."""
+    a = project(h, dw.fc1, precision)
+    if dw.fc1_b is not None:
+        a = a + _t(dw.fc1_b)
+    if activation == "swiglu":
+        gate, up = a.chunk(2, dim=-1)
+        a = F.silu(gate) * up
+    elif activation == "gelu":
+        a = F.gelu(a)
+    else:
+        raise ValueError(f"unknown MLP activation {activation!r}")
+    out = project(a, dw.fc2, precision)
+    if dw.fc2_b is not None:
+        out = out + _t(dw.fc2_b)
+    return out
+
+
+def dit_block_forward(x, dw: DiTWeights, mods, idx, lay: Layout, heads, dim, cfg: BranchConfig, *,
+                      activation="swiglu", precision="bf16", mlp_precision=None):
+    """The fused DiT block forward of block_kernels.py:149-240: pre-norm + AdaLN, hybrid
+    attention, gated residual, pre-norm + AdaLN, MLP, gated residual.  ``mods`` are the six
+    adaln_proj outputs [rows of modulation, hidden] in MOD_NAMES order."""
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = mods
+    x = _t(x)
+    h = dit_pre(x, dw.norm1, dw.eps, scale_msa, shift_msa, idx)
+    attn_out = block_forward(h, dw.attn, lay, heads, dim, cfg, precision=precision)
+    x = dit_post(x, gate_msa, idx, attn_out)
+    h = dit_pre(x, dw.norm2, dw.eps, scale_mlp, shift_mlp, idx)
+    return dit_post(x, gate_mlp, idx, dit_mlp(h, dw, activation, mlp_precision or precision))
+
+
+def make_dit(seed, hidden, heads, dim, ffn, *, activation="swiglu", std=0.02, bias=True) -> DiTWeights:
+    gen = torch.Generator().manual_seed(seed + 104729)
+    rows1 = 2 * ffn if activation == "swiglu" else ffn
+    return DiTWeights(
+        attn=make_block(seed, hidden, heads, dim, std=std),
+        norm1=1.0 + 0.1 * torch.randn(hidden, generator=gen),
+        norm2=1.0 + 0.1 * torch.randn(hidden, generator=gen),
+        fc1=torch.randn(rows1, hidden, generator=gen) * std,
+        fc1_b=torch.randn(rows1, generator=gen) * 0.02 if bias else None,
+        fc2=torch.randn(hidden, ffn, generator=gen) * std,
+        fc2_b=torch.randn(hidden, generator=gen) * 0.02 if bias else None,
+    )
+
+
+def make_mods(seed, groups, hidden) -> list[torch.Tensor]:
+    """Six adaln tables [groups, hidden]: shifts and scales ~ N(0, 0.1), gates ~ N(1, 0.1)."""
+    gen = torch.Generator().manual_seed(seed + 15485863)
+    out = []
+    for name in MOD_NAMES:
+        t = torch.randn(groups, hidden, generator=gen) * 0.1
+        if name.startswith("gate"):
+            t = t + 1.0
+        out.append(t)
+    return out
+
+
+def dit_flops(lay: Layout, heads, dim, hidden, ffn, activation="swiglu") -> dict:
+    """Algorithmic FLOPs of one DiT block forward: the hybrid attention block plus the MLP."""
+    fl = dict(block_flops(lay, heads, dim, hidden))
+    s = lay.seq_len
+    rows1 = 2 * ffn if activation == "swiglu" else ffn
+    fl["mlp"] = 2.0 * s * hidden * rows1 + 2.0 * s * ffn * hidden
+    fl["total"] = fl["total"] + fl["mlp"]
+    return fl

@@ -139,7 +139,7 @@ def _worker(rank, world, port, anchors, chunks, q):
         xchg.exchange()
         w_rm = sh.rank_major_out_weight(bw.out.double(), bw.branch["to_out_linear.weight"].double(), H, D, world)
 
-        def project(recv, rows, out_rows):
+        def project(recv, rows, out_rows, row0):
             if rows:
                 out_rows[:rows] = sh.concat_rows(recv, rows) @ w_rm.T
 
