@@ -34,6 +34,9 @@ PEAK_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustaine
 CONFIGS = {
     1: dict(text=512, frames=31, grid=(38, 22), heads=40, dim=128, hidden=5120),
     3: dict(text=512, frames=31, grid=(80, 48), heads=40, dim=128, hidden=5120),
+    # the 50-block denoiser stack: DiT blocks (GELU 4x MLP, INT8 projections), CFG batch 2
+    4: dict(text=512, frames=31, grid=(38, 22), heads=40, dim=128, hidden=5120, blocks=50, ffn_mult=4,
+            activation="gelu", precision="int8", cfg_batch=2, sampler_steps=8),
 }
 
 
@@ -274,6 +277,127 @@ def run_attention_only(args, c):
                       pk["bf16_tflops"], "peak_source": src}), flush=True)
 
 
+def run_dit_stack(args, c, world, rank, local):
+    """Config 4: the denoiser forward stack of ``blocks`` DiT blocks (hybrid attention + GELU MLP,
+    INT8 projections) over a CFG batch of 2 latent sequences; one step = one sampler step
+    (cfg_batch x blocks block forwards).  Weights are random-init on the device, seeded."""
+    from __graft_entry__ import load_package
+    from oracle import vdn_oracle as vo  # FLOP model only
+
+    pkg = load_package()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    H, D, hidden = c["heads"], c["dim"], c["hidden"]
+    F = c["ffn_mult"] * hidden
+    n_blocks = args.blocks or c["blocks"]
+    lay = pkg.make_layout(c["text"], c["frames"], c["grid"])
+    lay_o = vo.config_layout(c)
+    S = lay.seq_len
+    fl_block = vo.dit_flops(lay_o, H, D, hidden, F, c["activation"])["total"]
+    fl_step = fl_block * n_blocks * c["cfg_batch"]
+    shard = pkg.shard.default_shard(H) if world > 1 else None
+    gen = torch.Generator(device=dev).manual_seed(0)
+
+    def rn(*shape, s=0.02, mean=0.0):
+        return torch.randn(*shape, device=dev, dtype=torch.bfloat16, generator=gen) * s + mean
+
+    base_branch = vo.make_branch_weights(torch.Generator().manual_seed(0), hidden, H, D)
+    ws_attn, ws_mlp, blocks, mods = {}, {}, [], []
+    for _ in range(n_blocks):
+        branch = dict(base_branch)
+        branch["to_out_linear.weight"] = rn(hidden, H * D)
+        fb = pkg.FusedBlock(rn(3 * H * D, hidden), rn(D, s=0.1, mean=1.0), rn(D, s=0.1, mean=1.0), rn(hidden, H * D),
+                            branch, H, D, dev, precision=c["precision"], shard=shard, workspaces=ws_attn)
+        blocks.append(pkg.B200DiTBlock(fb, rn(hidden, s=0.1, mean=1.0), 1e-6, rn(hidden, s=0.1, mean=1.0), 1e-6,
+                                       rn(F, hidden), rn(F), rn(hidden, F), rn(hidden), dev,
+                                       activation=c["activation"], precision=c["precision"], workspaces=ws_mlp))
+        mods.append([rn(2, hidden, s=0.1, mean=1.0 if name.startswith("gate") else 0.0)
+                     for name in pkg.dit.MOD_NAMES])
+    group = pkg.dit.segment_indices([(0, lay.video_start, 0), (lay.video_start, S, 1)], S, dev)
+    plans = pkg.WindowPlanCache()
+    status = pkg.DeviceStatus(dev)
+    g = torch.Generator().manual_seed(1)
+    x_host = [torch.randn(S, hidden, generator=g).to(torch.bfloat16).pin_memory() for _ in range(c["cfg_batch"])]
+    out_host = [torch.empty(S, hidden, dtype=torch.bfloat16).pin_memory() for _ in range(c["cfg_batch"])]
+    x_dev = [t.to(dev) for t in x_host]
+
+    def sampler_step(copies=False):
+        for i in range(c["cfg_batch"]):
+            if copies:
+                x_dev[i].copy_(x_host[i], non_blocking=True)
+            x = x_dev[i]
+            for b, blk in enumerate(blocks):
+                x = blk.forward(x, mods[b], group, lay, plans, status)
+            if copies:
+                out_host[i].copy_(x, non_blocking=True)
+
+    clocks = ClockSampler(local).start()
+    with pkg.cholesky_runtime_scope():
+        for _ in range(args.warmup):
+            sampler_step()
+    torch.cuda.synchronize()
+    status.raise_if_failed()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.mark_start()
+    launches0 = pkg._lib.launch_count()
+    e0.record()
+    with pkg.cholesky_runtime_scope():
+        for _ in range(args.steps):
+            sampler_step()
+        e1.record()
+        torch.cuda.synchronize()
+    launches = pkg._lib.launch_count() - launches0
+    clocks.mark_end()
+    barrier(world)
+    status.raise_if_failed()
+    ms = max_over_ranks(e0.elapsed_time(e1) / max(args.steps, 1), world)
+    # end to end: every sampler step copies the CFG batch's latents in from pinned host memory
+    # and the denoised outputs back
+    barrier(world)
+    torch.cuda.synchronize()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record()
+    with pkg.cholesky_runtime_scope():
+        for _ in range(args.steps):
+            sampler_step(copies=True)
+        c1.record()
+        torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(c0.elapsed_time(c1) / max(args.steps, 1), world)
+    clocks.stop()
+    status.raise_if_failed()
+    pk, pk_src = peaks()
+    if rank == 0:
+        io_bytes = c["cfg_batch"] * S * hidden * 2
+        line = {
+            "metric": f"VDN-H3 DiT denoiser TFLOP/s: {n_blocks} blocks x CFG {c['cfg_batch']} per sampler step "
+                      f"(ms per sampler step in ms_per_step)",
+            "value": fl_step / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8" if c["precision"] == "int8" else "bf16",
+            "data": "synthetic (seeded random-init weights on the device, N(0,1) latents)",
+            "config": {"workload": f"config4: {n_blocks} DiT blocks (hybrid attention + {c['activation'].upper()} "
+                                   f"{c['ffn_mult']}x MLP, {c['precision']} projections), CFG batch "
+                                   f"{c['cfg_batch']}, {c['frames']}x{c['grid'][0] * c['grid'][1]}+{c['text']} tokens",
+                       "tokens": S, "blocks": n_blocks, "sampler_steps_timed": args.steps,
+                       "parallelism": f"heads sharded over {world} GPUs, MLP token-parallel" if world > 1 else "none",
+                       "l2": "every block's weights and activations exceed L2"},
+            "tflop_per_step": fl_step / 1e12, "tflop_per_block": fl_block / 1e12,
+            "ms_per_block_forward": ms / (n_blocks * c["cfg_batch"]),
+            "roofline": {"kernel": "whole denoiser step", "bound": "tensor",
+                         "achieved": fl_step / (ms * 1e-3) / 1e12 / world, "peak": pk.get("bf16_tflops_sustained"),
+                         "unit": "TFLOP/s per GPU", "frac": fl_step / (ms * 1e-3) / 1e12 / world /
+                         pk.get("bf16_tflops_sustained", 1.0), "traffic": None,
+                         "peak_source": f"{pk_src} sustained bf16 (int8 tensor peak is 2x)"},
+            "e2e": {"value": fl_step / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -285,6 +409,7 @@ def main():
     ap.add_argument("--only", choices=["attention"], default=None,
                     help="run one kernel alone on the config geometry (profiling small cases)")
     ap.add_argument("--heads", type=int, default=None, help="override the head count (profiling small cases)")
+    ap.add_argument("--blocks", type=int, default=None, help="config 4: number of DiT blocks (default 50)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
@@ -293,6 +418,13 @@ def main():
         c["heads"] = args.heads
     if args.only == "attention":
         run_attention_only(args, c)
+        return
+    if args.config == 4 and args.impl != "reference":
+        run_dit_stack(args, c, world, rank, local)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
         return
     if args.impl == "reference":
         run_reference_arm(args, c, world, rank)

@@ -8,7 +8,9 @@
 //   * warp 0 issues TMA loads (128-byte swizzle) into a 4-stage shared-memory ring;
 //   * warp 1 issues tcgen05.mma (M=128, N=256) into one of two TMEM accumulators
 //     (2 x 256 fp32 columns), so the epilogue of tile i overlaps the main loop of i+1;
-//   * warps 2..5 drain TMEM (tcgen05.ld 32x32b) and apply the fused epilogue.
+//   * warps 2..9 drain TMEM (tcgen05.ld 32x32b) and apply the fused epilogue: two warps per
+//     TMEM lane quarter, each taking half of the tile's columns, so the epilogue (which
+//     otherwise sets a per-tile floor of ~38 us) keeps up with the main loop.
 // Kinds: 0 = bf16 (kind::f16), 1 = fp8 e4m3 (kind::f8f6f4), 2 = int8 (kind::i8, s32).
 //
 // Epilogue modes cover every projection of the block:
@@ -28,7 +30,8 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int kStages = 4;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, each draining half of the tile's columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kStageA = BM * 128;  // bytes: 128 rows x 128 B
 constexpr int kStageB = BN * 128;
 constexpr int kStageBytes = kStageA + kStageB;
@@ -55,6 +58,10 @@ struct Epilogue {
   const int* row_group;
   const __nv_bfloat16* group_gate;
   long long ld_group_gate;
+  int cs_vec_ok;    // col_scale / col_bias 16-byte aligned: float4 loads
+  int cb_vec_ok;
+  int add_vec_ok;   // addend rows 16-byte aligned: 8-element vector loads
+  int gate_vec_ok;  // gate table rows 16-byte aligned
   // QKV extension
   int norm_cols;  // columns [0, norm_cols) are RMS-normalised per head into norm_out
   int norm_split; // columns < norm_split use norm_w[0:hd], others norm_w[hd:2hd]
@@ -151,28 +158,82 @@ __device__ __forceinline__ void store_plain_chunk(const Epilogue& ep, const uint
     }
     return;
   }
+  // One branch per optional feature per 32-column chunk (never per element), 16-byte loads
+  // of the per-column vectors when the chunk is whole: the epilogue must keep up with a
+  // main loop of a few microseconds per tile.
   float v[32];
   const float ars = alpha * (ep.row_scale ? ep.row_scale[row] : 1.0f);
+  const bool full = col0 + 32 <= N;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const int c = col0 + j;
-    float x = scaled<KIND>(ep, r[j], ars, c, N);
-    if (ep.col_bias && c < N) x += ep.col_bias[c];
-    if (ep.act == kActSigmoid) x = 1.0f / (1.0f + __expf(-x));
-    if (ep.act == kActGelu) x = gelu_erf(bf16_round(x));
-    v[j] = x;
+  for (int j = 0; j < 32; ++j) v[j] = acc_value<KIND>(r[j]) * ars;
+  if (ep.col_scale) {
+    if (full && ep.cs_vec_ok) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 c = __ldg(reinterpret_cast<const float4*>(ep.col_scale + col0 + j));
+        v[j] *= c.x, v[j + 1] *= c.y, v[j + 2] *= c.z, v[j + 3] *= c.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) v[j] *= ep.col_scale[col0 + j];
+    }
+  }
+  if (ep.col_bias) {
+    if (full && ep.cb_vec_ok) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 c = __ldg(reinterpret_cast<const float4*>(ep.col_bias + col0 + j));
+        v[j] += c.x, v[j + 1] += c.y, v[j + 2] += c.z, v[j + 3] += c.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) v[j] += ep.col_bias[col0 + j];
+    }
+  }
+  if (ep.act == kActSigmoid) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 1.0f / (1.0f + __expf(-v[j]));
+  } else if (ep.act == kActGelu) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gelu_erf(bf16_round(v[j]));
   }
   if (ep.group_gate) {
     const __nv_bfloat16* gate = ep.group_gate + (long long)ep.row_group[row] * ep.ld_group_gate + col0;
+    if (ep.gate_vec_ok && full) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (col0 + j < N) v[j] = bf16_round(bf16_round(v[j]) * __bfloat162float(gate[j]));
+      for (int j = 0; j < 32; j += 8) {
+        const uint4 p = __ldg(reinterpret_cast<const uint4*>(gate + j));
+        const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float gv = __uint_as_float((e & 1) ? (w[e >> 1] & 0xFFFF0000u) : (w[e >> 1] << 16));
+          v[j + e] = bf16_round(bf16_round(v[j + e]) * gv);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) v[j] = bf16_round(bf16_round(v[j]) * __bfloat162float(gate[j]));
+    }
   }
   if (ep.addend) {
     const __nv_bfloat16* src = ep.addend + (long long)row * ep.ld_add + col0;
+    if (ep.add_vec_ok && full) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (col0 + j < N) v[j] += __bfloat162float(src[j]);
+      for (int j = 0; j < 32; j += 8) {
+        const uint4 p = *reinterpret_cast<const uint4*>(src + j);  // may alias the output row: no __ldg
+        const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          v[j + e] += __uint_as_float((e & 1) ? (w[e >> 1] & 0xFFFF0000u) : (w[e >> 1] << 16));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) v[j] += __bfloat162float(src[j]);
+    }
   }
   if (ep.out_kind == kOutF32) {
     float* dst = reinterpret_cast<float*>(ep.out) + (long long)row * ep.ldo + col0;
@@ -235,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&tfull[a]), 1);
-      mbar_init(smem_u32(&tempty[a]), 4);
+      mbar_init(smem_u32(&tempty[a]), kEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -321,7 +382,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 2) {
     // ---------------- epilogue ----------------
-    const int quad = warp & 3;
+    const int quad = warp & 3;  // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;  // which half of the tile's columns it drains
     const int row_in_tile = quad * 32 + lane;
     float alpha = ep.alpha;
     if (ep.dev_scale0) alpha *= *ep.dev_scale0;
@@ -341,8 +403,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t r[32];
       if (n0 < ep.norm_cols) {
         // q / k columns: raw bf16 + per-head RMSNorm into norm_out.
-        const int hd = ep.head_dim;
-        for (int h0 = 0; h0 < BN; h0 += hd) {
+        const int hd = ep.head_dim;  // 64 or 128: each half of the tile holds whole heads
+        for (int h0 = half * (BN / 2); h0 < (half + 1) * (BN / 2); h0 += hd) {
           const int c_head = n0 + h0;
           const float* w = ep.norm_w + (c_head < ep.norm_split ? 0 : hd);
           float ss = 0.f;
@@ -423,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // columns [n0, n0 + 128) hold the gate rows and [n0 + 128, n0 + 256) the matching up
         // rows of output columns [n0 / 2, n0 / 2 + 128) (the host interleaves W_fc1 that way):
         // out = silu(gate) * up with the reference's bf16 roundings (block_kernels.py:113-115)
-        for (int c = 0; c < BN / 2; c += 32) {
+        for (int c = half * (BN / 4); c < (half + 1) * (BN / 4); c += 32) {
           if (n0 + c >= N) break;
           uint32_t u[32];
           tmem_ld32(tbase + c, r);
@@ -455,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
         // 32-column chunks: a tile may straddle the v columns and the fp32 side columns
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
           const int col = n0 + c;
           if (col >= N) break;
           tmem_ld32(tbase + c, r);
@@ -557,6 +619,9 @@ static Epilogue plain_epilogue(void* C, long long ldc, int out_kind, float alpha
   const long long ebytes = out_kind == vdn::gemm::kOutBF16 ? 2 : 4;
   ep.vec_ok = vdn::aligned16(C) && (ldc * ebytes) % 16 == 0;
   ep.ld_add = ld_add;
+  ep.add_vec_ok = addend && vdn::aligned16(addend) && (ld_add * 2) % 16 == 0;
+  ep.cs_vec_ok = col_scale && vdn::aligned16(col_scale);
+  ep.cb_vec_ok = col_bias && vdn::aligned16(col_bias);
   ep.norm_cols = 0;
   ep.aux_col0 = 1 << 30;
   return ep;
@@ -699,6 +764,7 @@ int vdn_gemm_block(int kind, const void* A, long long lda, const void* A2, long 
   ep.row_group = row_group;
   ep.group_gate = reinterpret_cast<const __nv_bfloat16*>(group_gate);
   ep.ld_group_gate = ld_gate;
+  ep.gate_vec_ok = group_gate && vdn::aligned16(group_gate) && (ld_gate * 2) % 16 == 0;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (kind) {
     case 0: return vdn::gemm::launch<0>(A, lda, A2, lda2, k_split, B, ldb, M, N, K, ep, dev_err, s, group_stride, kg);

@@ -58,6 +58,47 @@ __global__ void int8_rows_kernel(const T* __restrict__ x, long long ldx, int K, 
   }
 }
 
+// bf16 rows read once into registers with 16-byte loads (NV vectors of 8 per thread of
+// THREADS, K <= 8 * THREADS * NV), same rule as int8_rows_kernel; codes stored 8 per 8-byte
+// store.  Wide rows use more threads, not more registers, so several CTAs share an SM.
+template <int NV, int THREADS>
+__global__ void __launch_bounds__(THREADS) int8_rows_vec_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                             int K, int8_t* __restrict__ q, long long ldq,
+                                                             float* __restrict__ scale) {
+  const long long r = blockIdx.x;
+  const uint4* row = reinterpret_cast<const uint4*>(x + r * ldx);
+  const int nvec = K >> 3;
+  uint4 v[NV];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int vi = threadIdx.x + THREADS * i;
+    v[i] = vi < nvec ? __ldg(row + vi) : make_uint4(0, 0, 0, 0);
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(w[e] << 16)), fabsf(__uint_as_float(w[e] & 0xFFFF0000u))));
+  }
+  amax = block_max(amax);
+  const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+  if (threadIdx.x == 0) scale[r] = s;
+  uint2* qr = reinterpret_cast<uint2*>(q + r * ldq);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int vi = threadIdx.x + THREADS * i;
+    if (vi >= nvec) continue;
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float f = __uint_as_float((e & 1) ? (w[e >> 1] & 0xFFFF0000u) : (w[e >> 1] << 16));
+      const float c = fminf(fmaxf(rintf(__fdiv_rn(f, s)), -127.f), 127.f);
+      packed[e >> 2] |= (uint32_t)(static_cast<int>(c) & 0xFF) << (8 * (e & 3));
+    }
+    qr[vi] = make_uint2(packed[0], packed[1]);
+  }
+}
+
 template <typename T>
 __global__ void amax_kernel(const T* __restrict__ x, long long ldx, int rows, int K, float* __restrict__ amax) {
   float m = 0.f;
@@ -97,7 +138,19 @@ int vdn_quant_int8_rows(int src_kind, const void* x, long long ldx, int rows, in
   if (!x || !q || !scale || rows < 0 || K <= 0) return vdn::kBadArgument;
   if (rows == 0) return vdn::kOk;
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  if (src_kind == 0)
+  const bool vec = src_kind == 0 && K % 8 == 0 && K <= 8 * 1024 * 4 && vdn::aligned16(x) && (ldx * 2) % 16 == 0 &&
+                   (reinterpret_cast<uintptr_t>(q) & 7) == 0 && ldq % 8 == 0;
+  if (vec) {
+    const int nvec = K / 8;
+    const auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
+    const auto qb = reinterpret_cast<int8_t*>(q);
+    if (nvec <= 256 * 2)
+      vdn::quant::int8_rows_vec_kernel<2, 256><<<rows, 256, 0, s>>>(xb, ldx, K, qb, ldq, scale);
+    else if (nvec <= 256 * 4)
+      vdn::quant::int8_rows_vec_kernel<4, 256><<<rows, 256, 0, s>>>(xb, ldx, K, qb, ldq, scale);
+    else
+      vdn::quant::int8_rows_vec_kernel<4, 1024><<<rows, 1024, 0, s>>>(xb, ldx, K, qb, ldq, scale);
+  } else if (src_kind == 0)
     vdn::quant::int8_rows_kernel<__nv_bfloat16><<<rows, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, K,
                                                                       reinterpret_cast<int8_t*>(q), ldq, scale);
   else

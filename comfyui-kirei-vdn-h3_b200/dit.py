@@ -123,7 +123,7 @@ class B200DiTBlock:
     """Device weights of one DiT block (its attention is a :class:`FusedBlock`)."""
 
     def __init__(self, attn: FusedBlock, norm1_w, norm1_eps, norm2_w, norm2_eps, fc1_w, fc1_b, fc2_w, fc2_b,
-                 device, *, activation="swiglu", precision="bf16"):
+                 device, *, activation="swiglu", precision="bf16", workspaces: dict | None = None):
         if activation not in MLP_ACTIVATIONS:
             raise ValueError(f"unsupported MLP activation {activation!r}")
         if precision not in ("bf16", "int8"):
@@ -157,12 +157,13 @@ class B200DiTBlock:
         else:
             self.w1 = quantize_weight(w1, "int8", dev)
             self.w2 = quantize_weight(fc2_w, "int8", dev)
-        self._ws: dict = {}
+        self._ws: dict = workspaces if workspaces is not None else {}  # shareable by like blocks
+        self._ws_key = ("dit", hidden, ffn, precision)
 
     def workspace(self, rows: int) -> dict:
         """Buffers for ``rows`` rows (the pre-norm output, reused by both pre-norms, and the
         MLP activation); a larger workspace already held serves fewer rows."""
-        ws = self._ws.get("cur")
+        ws = self._ws.get(self._ws_key)
         if ws is None or ws["h"].shape[0] < rows:
             dev, H, F = self.device, self.hidden, self.ffn
             ws = {"h": torch.empty(rows, H, device=dev, dtype=torch.bfloat16),
@@ -172,7 +173,7 @@ class B200DiTBlock:
                                            torch.empty(rows, device=dev, dtype=torch.float32), "int8")
                 ws["aq"] = QuantizedMatrix(torch.empty(rows, F, device=dev, dtype=torch.int8),
                                            torch.empty(rows, device=dev, dtype=torch.float32), "int8")
-            self._ws = {"cur": ws}  # one geometry at a time
+            self._ws[self._ws_key] = ws  # one row count at a time
         return ws
 
     # ------------------------------------------------------------------ kernels
@@ -250,7 +251,7 @@ def dit_block(state: B200State, block, index: int, device) -> B200DiTBlock:
                           _weight_of(mlp.fc2), getattr(mlp.fc2, "bias", None), device,
                           activation=str(cfg.get("mlp_activation", "swiglu")),
                           precision=str(cfg.get("mlp_precision", "int8" if state.projection_precision == "int8"
-                                                else "bf16")))
+                                                else "bf16")), workspaces=state.workspaces)
         cache[index] = db
     return db
 

@@ -99,7 +99,8 @@ class FusedBlock:
     """Device weights of one H3 attention block + its VDN branch, laid out for the kernels."""
 
     def __init__(self, qkv_w, q_norm_w, k_norm_w, out_w, branch_w: Mapping, heads, dim, device, *,
-                 precision="bf16", eps=1e-6, enable_gate=True, short_conv=("k", "v"), shard: HeadShard | None = None):
+                 precision="bf16", eps=1e-6, enable_gate=True, short_conv=("k", "v"), shard: HeadShard | None = None,
+                 workspaces: dict | None = None):
         dev = torch.device(device)
         H_all, D = int(heads), int(dim)
         inner_all = H_all * D
@@ -172,12 +173,16 @@ class FusedBlock:
             self.w_to_q = quantize_weight(to_out, precision, dev) if to_out is not None else None
         self.bw = BranchDeviceWeights.from_dict(wl, H, D, dev, short_conv=self.short_conv) if self.has_branch \
             else None
-        self._ws: dict = {}
+        # blocks of one model run one after another on one stream: they may share workspaces
+        # (pass the same dict), keyed by geometry, precision and shard so only like blocks meet
+        self._ws: dict = workspaces if workspaces is not None else {}
 
     # ------------------------------------------------------------------ workspaces
     def workspace(self, S: int, layout: VDNLayout | None):
         key = (S, None if layout is None else (layout.num_frames, layout.tokens_per_frame, layout.text_len,
-                                               layout.anchor_frames))
+                                               layout.anchor_frames),
+               self.geo.heads, self.geo.dim, self.geo.hidden, self.precision, self.n_aux,
+               None if self.shard is None else (self.shard.rank, self.shard.world), self.bw is not None)
         ws = self._ws.get(key)
         if ws is None:
             g = self.geo
@@ -437,6 +442,7 @@ class B200State:
         self.weight_maps = maps
         self.window_plans = WindowPlanCache(limit=24)
         self.blocks: dict[int, FusedBlock] = {}
+        self.workspaces: dict = {}  # shared by every block of the model
         self.status: dict[str, _lib.DeviceStatus] = {}
         self.forwards = 0
         self.last_attention_backend = None
@@ -458,12 +464,14 @@ class B200State:
                             _weight_of(attn.out_proj), self.weight_maps[index], self.num_heads, self.head_dim,
                             device, precision=self.projection_precision, eps=float(getattr(attn.q_norm, "eps", 1e-6)),
                             enable_gate=bool(cfg.get("enable_softmax_gate", True)),
-                            short_conv=tuple(cfg.get("short_conv", ("k", "v"))), shard=self.shard)
+                            short_conv=tuple(cfg.get("short_conv", ("k", "v"))), shard=self.shard,
+                            workspaces=self.workspaces)
             self.blocks[index] = fb
         return fb
 
     def release(self):
         self.blocks.clear()
+        self.workspaces.clear()
         self.window_plans.clear()
         return self
 

@@ -83,6 +83,18 @@ def test_int8_quantisation_and_accumulator_bit_exact():
     assert rel_l2(deq, want) < 1e-6
 
 
+@pytest.mark.parametrize("K", [8, 1000, 1004, 5120, 20480, 20488])
+def test_int8_row_quantiser_is_bit_exact_at_every_width(K):
+    """Both quantiser kernels (16-byte register-resident rows for bf16 with K % 8 == 0, the
+    scalar one otherwise) give the oracle's codes and scales bit for bit."""
+    x = (_randn(37, K, seed=K) * 3).to(torch.bfloat16)
+    x[5] = 0  # an all-zero row: scale 1e-12, codes 0
+    q = pkg.quantize_rows_int8(x.to(DEV))
+    oa, sa = vo.int8_quantize_rows(x.float())
+    assert torch.equal(q.scale.cpu(), sa)
+    assert torch.equal(q.data.cpu(), oa)
+
+
 def test_fp8_gemm_matches_oracle():
     M, N, K = 500, 768, 2048
     x = _randn(M, K, seed=12).to(torch.bfloat16)
