@@ -141,6 +141,24 @@ def _nccl_worker(rank, world, port, q):
             if precision == "bf16":
                 want = vo.block_forward(x.float().cpu(), bw, vo.config_layout(c), H, D, vo.BranchConfig())
                 res["oracle"] = rel_l2(got, want)
+        # the DiT block around it: MLP token-parallel on each rank's rows before the gather
+        dw = vo.make_dit(8, hidden, H, D, 512, activation="swiglu")
+        mods = [m.to(f"cuda:{rank}", torch.bfloat16) for m in vo.make_mods(8, 2, hidden)]
+        group = torch.tensor([0] * lay.video_start + [1] * (lay.seq_len - lay.video_start), dtype=torch.int32,
+                             device=f"cuda:{rank}")
+        for precision in ("bf16", "int8"):
+            outs = []
+            for shard in (sh.default_shard(H), None):
+                fb = pkg_r.FusedBlock(dw.attn.qkv, dw.attn.q_norm, dw.attn.k_norm, dw.attn.out, dw.attn.branch, H, D,
+                                      f"cuda:{rank}", precision=precision, shard=shard)
+                blk = pkg_r.B200DiTBlock(fb, dw.norm1, dw.eps, dw.norm2, dw.eps, dw.fc1, dw.fc1_b, dw.fc2, dw.fc2_b,
+                                         f"cuda:{rank}", precision=precision)
+                st = pkg_r.DeviceStatus(f"cuda:{rank}")
+                with pkg_r.cholesky_runtime_scope():
+                    outs.append(blk.forward(x, mods, group, lay, pkg_r.WindowPlanCache(), st).clone())
+                torch.cuda.synchronize()
+                st.raise_if_failed()
+            res["dit_" + precision] = (bool(torch.equal(outs[0], outs[1])), rel_l2(outs[0], outs[1]))
         q.put((rank, res))
     finally:
         dist.destroy_process_group()
@@ -165,3 +183,5 @@ def test_sharded_block_on_two_gpus_over_nccl():
         assert res["fp8"][0], (rank, res)  # the amax all-reduce restores the whole tensor's scale
         assert res["bf16"][1] < 2e-3, (rank, res)
         assert res["oracle"] < 2e-2, (rank, res)
+        assert res["dit_int8"][0], (rank, res)
+        assert res["dit_bf16"][1] < 2e-3, (rank, res)
