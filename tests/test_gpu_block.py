@@ -132,3 +132,26 @@ def test_host_streamer_matches_direct_forward():
         direct = [run(x.to(DEV)).cpu() for x in xs]
     for got, want in zip(outs, direct):
         assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("order", [("text", "audio", "video", "ref"), ("video", "audio", "text")])
+def test_block_on_packed_layout_with_global_segments(order):
+    """A ComfyUI PackedLayout with audio / reference-frame rows around the video (global rows
+    that see and are seen by every row) through the adapter, against the oracle."""
+    import dataclasses
+    import types
+
+    H, D, hidden = 4, 64, 256
+    sizes = {"text": 32, "audio": 12, "video": 7 * 20, "ref": 20}
+    segs, pos = [], 0
+    for kind in order:
+        segs.append((pos, pos + sizes[kind], kind))
+        pos += sizes[kind]
+    packed = types.SimpleNamespace(signature=(32, 7, 8, 9, 12), segments=segs, seq_len=pos)
+    lay = pkg.from_comfy_packed_layout(packed, radius=1, chunk=0, anchor_frames="both")
+    lay_o = vo.Layout(**{f.name: getattr(lay, f.name) for f in dataclasses.fields(vo.Layout)})
+    bw = vo.make_block(21, hidden, H, D)
+    x = vo.make_x(21, lay.seq_len, hidden)
+    got = _run_block(bw, lay, H, D, x)
+    want = vo.block_forward(x, bw, lay_o, H, D, vo.BranchConfig())
+    assert rel_l2(got, want) < 2e-2
