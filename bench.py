@@ -64,36 +64,83 @@ def attention_traffic(heads_per_rank: int, heads_total: int):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled every 50 ms from before the warm-up to
-    after the timed region.  ``mark_start()`` / ``mark_end()`` bracket the timed region on
-    the same monotonic clock the samples are stamped with; ``summary()`` keeps the samples
-    inside it (or, for a region shorter than the sampling period, the nearest one on each
-    side)."""
+    """SM clock and throttle reasons sampled from before the warm-up to after the timed
+    region: NVML polled every 5 ms from a thread (nvidia-smi every 50 ms when NVML is not
+    importable).  ``mark_start()`` / ``mark_end()`` bracket the timed region on the clock the
+    samples are stamped with; ``summary()`` keeps the samples inside it (or, for a region
+    shorter than the sampling period, the nearest one on each side).  Read-only: nothing
+    here changes a GPU setting."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    NVML_BITS = (0x8, 0x40, 0x20, 0x4)  # the NAMES' bits in NVML's clocks-event-reason mask
+    PERIOD_S = 0.005
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.lines: list[tuple[float, str]] = []
+        self.rows: list[tuple[float, float, float, tuple]] = []  # (t, sm_mhz, max_mhz, active names)
         self.t0 = self.t1 = None
+        self._stop = False
+        self._t = None
+        self.source = None
 
     def start(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            handle = self._nvml_handle(pynvml)
+            self.source = "nvml"
+            self._t = threading.Thread(target=self._poll_nvml, args=(pynvml, handle), daemon=True)
+            self._t.start()
+            return self
+        except Exception:
+            pass
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self._t = threading.Thread(target=self._read, daemon=True)
+            self.source = "nvidia-smi"
+            self._t = threading.Thread(target=self._read_smi, daemon=True)
             self._t.start()
         except Exception:
             self.proc = None
         return self
 
-    def _read(self):
+    def _nvml_handle(self, pynvml):
+        # the CUDA device's own PCI address, so a remapped CUDA_VISIBLE_DEVICES cannot mislead
+        try:
+            props = torch.cuda.get_device_properties(self.index)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _poll_nvml(self, pynvml, handle):
+        max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+        while not self._stop:
+            try:
+                sm = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
+                mask = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
+                active = tuple(n for n, b in zip(self.NAMES, self.NVML_BITS) if mask & b)
+                self.rows.append((time.monotonic(), sm, max_mhz, active))
+            except Exception:
+                pass
+            time.sleep(self.PERIOD_S)
+
+    def _read_smi(self):
         for line in self.proc.stdout:
-            self.lines.append((time.monotonic(), line.strip()))
+            parts = [p.strip() for p in line.strip().split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                active = tuple(n for n, v in zip(self.NAMES, parts[5:9]) if v.lower().startswith("active"))
+                self.rows.append((time.monotonic(), float(parts[1]), float(parts[2]), active))
+            except ValueError:
+                continue
 
     def mark_start(self):
         self.t0 = time.monotonic()
@@ -102,36 +149,30 @@ class ClockSampler:
         self.t1 = time.monotonic()
 
     def stop(self):
+        time.sleep(0.06)  # let the sample after the timed region arrive
+        self._stop = True
         if self.proc is not None:
-            time.sleep(0.2)  # let the sample after the timed region arrive
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+        if self._t is not None:
+            self._t.join(timeout=2)
 
     def summary(self):
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        rows = []
-        for t, line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((t, float(parts[1]), float(parts[2]), parts[5:9]))
-            except ValueError:
-                continue
+        rows = list(self.rows)
         window = "timed region"
         picked = [r for r in rows if self.t0 is not None and self.t0 <= r[0] <= self.t1]
         if not picked and rows and self.t0 is not None:
             before = [r for r in rows if r[0] < self.t0]
             after = [r for r in rows if r[0] > self.t1]
             picked = ([before[-1]] if before else []) + ([after[0]] if after else [])
-            window = "nearest samples around a timed region shorter than the 50 ms period"
+            window = "nearest samples around a timed region shorter than the sampling period"
         sm = sorted(r[1] for r in picked)
-        reasons = sorted({n for r in picked for n, v in zip(names, r[3]) if v.lower().startswith("active")})
+        reasons = sorted({n for r in picked for n in r[3]})
         return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": picked[-1][2] if picked else None,
-                "reasons": reasons, "samples": len(sm), "window": window}
+                "reasons": reasons, "samples": len(sm), "window": window, "source": self.source}
 
 
 def dist_setup():
