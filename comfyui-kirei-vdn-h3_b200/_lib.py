@@ -31,7 +31,8 @@ SIGNATURES: dict[str, list] = {
                      _P, _I, _I, _I, _P, _P],
     "vdn_adaln_rmsnorm": [_P, _L, _I, _I, _P, _F, _P, _P, _L, _P, _P, _L, _P, _L, _P, _P],
     "vdn_gemm_block": [_I, _P, _L, _P, _L, _L, _L, _I, _P, _L, _P, _L, _I, _I, _I, _F, _P, _P, _P, _P, _P, _I, _P,
-                       _L, _P, _P, _L, _P, _P],
+                       _L, _P, _P, _L, _P, _P, _P],
+    "vdn_quant_int8_rows_amax": [_P, _L, _I, _I, _P, _P, _L, _P, _P],
     "vdn_window_attention": [_P, _L, _P, _L, _P, _L, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _I, _P,
                              _P, _P, _P, _L, _P, _L, _I, _P, _P, _P, _P],
     "vdn_spatial_conv": [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _L, _P],

@@ -1,11 +1,12 @@
 // Pointwise stretches of the DiT block around the hybrid attention (block_kernels.py:85-93).
 //
 // The pre-norm of both residual branches, RMSNorm(x) * (1 + scale[g]) + shift[g] with g the
-// modulation row of each token, reads x from HBM once: a warp owns a row, reduces its sum of
-// squares with shuffles and writes the modulated row as bf16 and/or as per-token int8 codes
-// with their scale (the quantiser of the INT8 projections, applied to the row it just
-// produced; the later passes over the row hit L1/L2).  Roundings follow the reference's bf16
-// tensors: the RMSNorm output, 1 + scale, the product and the sum are each rounded to bf16.
+// modulation row of each token, reads x from HBM once: a CTA owns a row held in registers,
+// reduces its sum of squares and writes the modulated row as bf16 and/or as per-token int8
+// codes with their scale (the quantiser of the INT8 projections, applied to the row it just
+// produced).  Rows wider than 32,768 fall back to a warp per row with streaming passes.
+// Roundings follow the reference's bf16 tensors: the RMSNorm output, 1 + scale, the product
+// and the sum are each rounded to bf16.
 // The gated residual x + gate[g] * y is fused into the epilogue of the GEMM that makes y
 // (gemm.cu), so no other pass over the residual stream exists.
 #include "host_common.h"
@@ -105,6 +106,82 @@ __global__ void __launch_bounds__(256) adaln_rmsnorm_kernel(
   }
 }
 
+// Block-wide sum / max through shared memory (every thread gets the result).
+template <bool kMax>
+__device__ __forceinline__ float block_reduce(float v, float* red) {
+  v = kMax ? warp_max(v) : warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = l < (int)(blockDim.x >> 5) ? red[l] : 0.f;
+    v = kMax ? warp_max(v) : warp_sum(v);
+    if (l == 0) red[32] = v;
+  }
+  __syncthreads();
+  const float r = red[32];
+  __syncthreads();
+  return r;
+}
+
+// One CTA per row with the row in registers (NV 16-byte vectors per thread, hidden <= 8 *
+// THREADS * NV): x is read once, the modulated row is kept packed for the int8 codes.
+template <int NV, int THREADS>
+__global__ void __launch_bounds__(THREADS) adaln_rmsnorm_row_kernel(
+    const __nv_bfloat16* __restrict__ x, long long ldx, int hidden, const float* __restrict__ w, float eps,
+    const __nv_bfloat16* __restrict__ scale_tab, const __nv_bfloat16* __restrict__ shift_tab, long long ld_tab,
+    const int* __restrict__ row_group, __nv_bfloat16* __restrict__ out, long long ldo, int8_t* __restrict__ q,
+    long long ldq, float* __restrict__ q_scale) {
+  __shared__ float red[33];
+  const long long row = blockIdx.x;
+  const int nvec = hidden >> 3;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
+  uint4 v[NV];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int vi = threadIdx.x + THREADS * i;
+    v[i] = vi < nvec ? __ldg(xr + vi) : make_uint4(0, 0, 0, 0);
+    const uint32_t p[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ss += bf_lo(p[e]) * bf_lo(p[e]) + bf_hi(p[e]) * bf_hi(p[e]);
+  }
+  const float rstd = rsqrtf(block_reduce<false>(ss, red) / (float)hidden + eps);
+  const long long g = row_group ? row_group[row] : 0;
+  const uint4* sc = scale_tab ? reinterpret_cast<const uint4*>(scale_tab + g * ld_tab) : nullptr;
+  const uint4* sh = shift_tab ? reinterpret_cast<const uint4*>(shift_tab + g * ld_tab) : nullptr;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int vi = threadIdx.x + THREADS * i;
+    if (vi >= nvec) continue;
+    float y[8];
+    modulate8(v[i], sc ? __ldg(sc + vi) : zero, sh ? __ldg(sh + vi) : zero, w, vi, rstd, y);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(y[e]));
+    v[i] = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
+    if (out) reinterpret_cast<uint4*>(out + row * ldo)[vi] = v[i];
+  }
+  if (!q) return;
+  const float s = fmaxf(__fdiv_rn(block_reduce<true>(amax, red), 127.0f), 1e-12f);
+  if (threadIdx.x == 0) q_scale[row] = s;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int vi = threadIdx.x + THREADS * i;
+    if (vi >= nvec) continue;
+    const uint32_t yp[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float yv = (e & 1) ? bf_hi(yp[e >> 1]) : bf_lo(yp[e >> 1]);
+      const float c = fminf(fmaxf(rintf(__fdiv_rn(yv, s)), -127.f), 127.f);
+      packed[e >> 2] |= (uint32_t)(static_cast<int>(c) & 0xFF) << (8 * (e & 3));
+    }
+    reinterpret_cast<uint2*>(q + row * ldq)[vi] = make_uint2(packed[0], packed[1]);
+  }
+}
+
 }  // namespace block
 }  // namespace vdn
 
@@ -129,6 +206,31 @@ int vdn_adaln_rmsnorm(const void* x, long long ldx, int rows, int hidden, const 
     return vdn::kMisaligned;
   if (rows == 0) return vdn::kOk;
   auto s = reinterpret_cast<cudaStream_t>(stream);
+  const int nvec = hidden / 8;
+  const auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  const auto st = reinterpret_cast<const __nv_bfloat16*>(scale_tab);
+  const auto ht = reinterpret_cast<const __nv_bfloat16*>(shift_tab);
+  const auto ob = reinterpret_cast<__nv_bfloat16*>(out);
+  const auto qb = reinterpret_cast<int8_t*>(q);
+  if (nvec <= 256 * 2) {
+    vdn::block::adaln_rmsnorm_row_kernel<2, 256><<<(unsigned)rows, 256, 0, s>>>(
+        xb, ldx, hidden, norm_w, eps, st, ht, ld_tab, row_group, ob, ldo, qb, ldq, q_scale);
+    vdn::count_launch();
+    return vdn::launch_status();
+  }
+  if (nvec <= 256 * 4) {
+    vdn::block::adaln_rmsnorm_row_kernel<4, 256><<<(unsigned)rows, 256, 0, s>>>(
+        xb, ldx, hidden, norm_w, eps, st, ht, ld_tab, row_group, ob, ldo, qb, ldq, q_scale);
+    vdn::count_launch();
+    return vdn::launch_status();
+  }
+  if (nvec <= 1024 * 4) {
+    vdn::block::adaln_rmsnorm_row_kernel<4, 1024><<<(unsigned)rows, 1024, 0, s>>>(
+        xb, ldx, hidden, norm_w, eps, st, ht, ld_tab, row_group, ob, ldo, qb, ldq, q_scale);
+    vdn::count_launch();
+    return vdn::launch_status();
+  }
+  // wider rows: one warp per row, streaming passes
   const unsigned blocks = (unsigned)((rows + vdn::block::kRowsPerBlock - 1) / vdn::block::kRowsPerBlock);
   vdn::block::adaln_rmsnorm_kernel<<<blocks, 32 * vdn::block::kRowsPerBlock, 0, s>>>(
       reinterpret_cast<const __nv_bfloat16*>(x), ldx, rows, hidden, norm_w, eps,

@@ -58,6 +58,9 @@ struct Epilogue {
   const int* row_group;
   const __nv_bfloat16* group_gate;
   long long ld_group_gate;
+  // per-row max |output| (of the bf16-rounded values), accumulated with atomicMax over the
+  // row's tiles: the next projection's per-token int8 scale without another pass
+  float* row_amax;
   int cs_vec_ok;    // col_scale / col_bias 16-byte aligned: float4 loads
   int cb_vec_ok;
   int add_vec_ok;   // addend rows 16-byte aligned: 8-element vector loads
@@ -247,6 +250,13 @@ __device__ __forceinline__ void store_plain_chunk(const Epilogue& ep, const uint
         if (col0 + j < N) dst[j] = v[j];
     }
   } else {
+    if (ep.row_amax) {
+      float m = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) m = fmaxf(m, fabsf(bf16_round(v[j])));
+      atomicMax(reinterpret_cast<int*>(ep.row_amax + row), __float_as_int(m));  // m >= 0: int order = float order
+    }
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ep.out) + (long long)row * ep.ldo + col0;
     if (ep.vec_ok && col0 + 32 <= N) {
 #pragma unroll
@@ -493,6 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           if (row < M) {
             uint32_t pk[16];
+            float m = 0.f;
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
               float o[2];
@@ -506,9 +517,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 g = bf16_round(g);
                 o[e] = bf16_round(g / (1.0f + __expf(-g))) * bf16_round(up);
+                m = fmaxf(m, fabsf(bf16_round(o[e])));
               }
               pk[j / 2] = pack_bf16(o[0], o[1]);
             }
+            if (ep.row_amax) atomicMax(reinterpret_cast<int*>(ep.row_amax + row), __float_as_int(m));
             __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ep.out) + (long long)row * ep.ldo + n0 / 2 + c;
 #pragma unroll
             for (int j = 0; j < 16; j += 4)
@@ -741,12 +754,13 @@ int vdn_qkv_gemm(int kind, const void* x, long long ldx, const void* w, long lon
 // A: one source (A2 = NULL, kg = 0), K-concatenated (A2 for k >= k_split) or grouped-K (kg > 0:
 // `groups` = K / kg slabs `group_stride` apart).  residual [M, ld_res] bf16 and the gate table
 // [groups of rows, ld_gate] bf16 with row_group [M] int32 are optional (both or neither gate).
+// row_amax [M] fp32 (optional, zeroed by the caller) receives max |C[row, :]| of the stored values.
 int vdn_gemm_block(int kind, const void* A, long long lda, const void* A2, long long lda2, long long k_split,
                    long long group_stride, int kg, const void* B, long long ldb, void* C, long long ldc, int M,
                    int N, int K, float alpha, const float* dev_scale0, const float* dev_scale1,
                    const float* row_scale, const float* col_scale, const float* col_bias, int act,
-                   const void* residual, long long ld_res,
-                   const int* row_group, const void* group_gate, long long ld_gate, int* dev_err, void* stream) {
+                   const void* residual, long long ld_res, const int* row_group, const void* group_gate,
+                   long long ld_gate, float* row_amax, int* dev_err, void* stream) {
   if (!A || !B || !C) return vdn::kBadArgument;
   if (act != vdn::gemm::kActNone && act != vdn::gemm::kActGelu && act != vdn::gemm::kActSwiGLU)
     return vdn::kBadArgument;
@@ -764,6 +778,7 @@ int vdn_gemm_block(int kind, const void* A, long long lda, const void* A2, long 
   ep.row_group = row_group;
   ep.group_gate = reinterpret_cast<const __nv_bfloat16*>(group_gate);
   ep.ld_group_gate = ld_gate;
+  ep.row_amax = row_amax;
   ep.gate_vec_ok = group_gate && vdn::aligned16(group_gate) && (ld_gate * 2) % 16 == 0;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (kind) {

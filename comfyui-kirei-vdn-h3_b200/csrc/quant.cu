@@ -99,6 +99,29 @@ __global__ void __launch_bounds__(THREADS) int8_rows_vec_kernel(const __nv_bfloa
   }
 }
 
+// Per-row int8 with the row amax already known (accumulated by the producing GEMM's
+// epilogue): one streaming pass, block (row, 256-vector chunk), 8 codes per thread.
+__global__ void __launch_bounds__(256) int8_rows_amax_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                              int K, const float* __restrict__ amax,
+                                                              int8_t* __restrict__ q, long long ldq,
+                                                              float* __restrict__ scale) {
+  const long long r = blockIdx.x;
+  const int vi = blockIdx.y * 256 + threadIdx.x;
+  const float s = fmaxf(__fdiv_rn(amax[r], 127.0f), 1e-12f);
+  if (vi == 0) scale[r] = s;
+  if (vi >= (K >> 3)) return;
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + r * ldx) + vi);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float f = __uint_as_float((e & 1) ? (w[e >> 1] & 0xFFFF0000u) : (w[e >> 1] << 16));
+    const float c = fminf(fmaxf(rintf(__fdiv_rn(f, s)), -127.f), 127.f);
+    packed[e >> 2] |= (uint32_t)(static_cast<int>(c) & 0xFF) << (8 * (e & 3));
+  }
+  reinterpret_cast<uint2*>(q + r * ldq)[vi] = make_uint2(packed[0], packed[1]);
+}
+
 template <typename T>
 __global__ void amax_kernel(const T* __restrict__ x, long long ldx, int rows, int K, float* __restrict__ amax) {
   float m = 0.f;
@@ -156,6 +179,23 @@ int vdn_quant_int8_rows(int src_kind, const void* x, long long ldx, int rows, in
   else
     vdn::quant::int8_rows_kernel<float><<<rows, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, K,
                                                               reinterpret_cast<int8_t*>(q), ldq, scale);
+  vdn::count_launch();
+  return vdn::launch_status();
+}
+
+// Per-row symmetric int8 of bf16 rows whose max |x| per row is already in amax [rows] (the
+// same codes and scales as vdn_quant_int8_rows).  K % 8 == 0, 16-byte aligned x rows, 8-byte
+// aligned q rows.
+int vdn_quant_int8_rows_amax(const void* x, long long ldx, int rows, int K, const float* amax, void* q,
+                             long long ldq, float* scale, void* stream) {
+  if (!x || !q || !scale || !amax || rows < 0 || K <= 0) return vdn::kBadArgument;
+  if (K % 8) return vdn::kUnsupported;
+  if (!vdn::aligned16(x) || (ldx * 2) % 16 || (reinterpret_cast<uintptr_t>(q) & 7) || ldq % 8)
+    return vdn::kMisaligned;
+  if (rows == 0) return vdn::kOk;
+  const dim3 grid((unsigned)rows, (unsigned)((K / 8 + 255) / 256));
+  vdn::quant::int8_rows_amax_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), ldx, K, amax, reinterpret_cast<int8_t*>(q), ldq, scale);
   vdn::count_launch();
   return vdn::launch_status();
 }

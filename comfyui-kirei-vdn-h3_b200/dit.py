@@ -31,7 +31,7 @@ import torch
 from . import _lib
 from .hybrid import B200State, FusedBlock, GatedResidual, _weight_of, gemm_block
 from .layout import current_layout
-from .projection import QuantizedMatrix, quantize_rows_int8, quantize_weight
+from .projection import QuantizedMatrix, quantize_weight
 
 MLP_ACTIVATIONS = ("swiglu", "gelu")
 _ACT_CODE = {"gelu": 2, "swiglu": 3}
@@ -173,6 +173,7 @@ class B200DiTBlock:
                                            torch.empty(rows, device=dev, dtype=torch.float32), "int8")
                 ws["aq"] = QuantizedMatrix(torch.empty(rows, F, device=dev, dtype=torch.int8),
                                            torch.empty(rows, device=dev, dtype=torch.float32), "int8")
+                ws["amax"] = torch.empty(rows, device=dev, dtype=torch.float32)
             self._ws[self._ws_key] = ws  # one row count at a time
         return ws
 
@@ -202,9 +203,15 @@ class B200DiTBlock:
             return
         hq = QuantizedMatrix(ws["hq"].data[:n], ws["hq"].scale[:n], "int8")
         self._adaln(x1, self.norm2, self.eps2, scale, shift, group, q=hq, stream=stream)
+        # fc1's epilogue records each row's max |activation|, so the per-token int8 of the
+        # activation for fc2 is one streaming pass
+        amax = ws["amax"][:n]
+        amax.zero_()
         gemm_block(2, hq.data, self.w1.data, a, row_scale=hq.scale, col_scale=self.w1.scale, col_bias=self.b1,
-                   act=act, status=status, stream=stream, rows=n)
-        aq = quantize_rows_int8(a, QuantizedMatrix(ws["aq"].data[:n], ws["aq"].scale[:n], "int8"))
+                   act=act, row_amax=amax, status=status, stream=stream, rows=n)
+        aq = QuantizedMatrix(ws["aq"].data[:n], ws["aq"].scale[:n], "int8")
+        _lib.call("vdn_quant_int8_rows_amax", a.data_ptr(), a.stride(0), n, self.ffn, amax.data_ptr(),
+                  aq.data.data_ptr(), aq.data.stride(0), aq.scale.data_ptr(), stream)
         gemm_block(2, aq.data, self.w2.data, x1, row_scale=aq.scale, col_scale=self.w2.scale, col_bias=self.b2,
                    residual=res, status=status, stream=stream, rows=n)
 

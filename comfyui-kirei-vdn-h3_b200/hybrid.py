@@ -65,9 +65,10 @@ class GatedResidual:
 
 def gemm_block(kind, a, w, out, *, a2=None, k_split=0, grouped=None, alpha=1.0, dev_scales=(None, None),
                row_scale=None, col_scale=None, col_bias=None, act=0, residual: GatedResidual | None = None,
-               addend=None, status, stream, rows=None, k=None):
+               addend=None, row_amax=None, status, stream, rows=None, k=None):
     """One ``vdn_gemm_block`` call: out[:rows] = (residual or addend) + gate * act(scales * a w^T + bias).
-    ``grouped`` = (groups, kg, group_stride) reads ``a`` as a grouped-K operand."""
+    ``grouped`` = (groups, kg, group_stride) reads ``a`` as a grouped-K operand; ``row_amax``
+    (zeroed fp32 [rows]) receives each output row's max |value|."""
     M = a.shape[-2] if rows is None else int(rows)
     K = (k if k is not None else (grouped[0] * grouped[1] if grouped else a.shape[-1] + (0 if a2 is None else
                                                                                           a2.shape[-1])))
@@ -81,7 +82,7 @@ def gemm_block(kind, a, w, out, *, a2=None, k_split=0, grouped=None, alpha=1.0, 
               _lib.ptr(col_bias), int(act), _lib.ptr(res), res.stride(0) if res is not None else 0,
               _lib.ptr(residual.group if residual is not None else None),
               _lib.ptr(residual.gate if residual is not None else None),
-              residual.gate.stride(0) if residual is not None else 0, status.err_ptr, stream)
+              residual.gate.stride(0) if residual is not None else 0, _lib.ptr(row_amax), status.err_ptr, stream)
 
 
 @dataclass

@@ -195,6 +195,12 @@ int vdn_cast_rows(const float* in, long long ld_in, int col0, int rows, int cols
 
 /* ---------------------------------------------------------------- DiT block -------- */
 
+/* Per-row int8 of bf16 rows whose max |x| per row is already in amax [rows] (e.g. from
+ * vdn_gemm_block's row_amax): same codes and scales as vdn_quant_int8_rows, one streaming pass.
+ * K % 8 == 0; 16-byte aligned x rows, 8-byte aligned q rows. */
+int vdn_quant_int8_rows_amax(const void* x, long long ldx, int rows, int K, const float* amax, void* q,
+                             long long ldq, float* scale, void* stream);
+
 /* out / q[r] = RMSNorm(x[r]) * norm_w * (1 + scale_tab[g]) + shift_tab[g], g = row_group[r].
  * x [rows, ldx] bf16, norm_w [hidden] fp32, tables [groups, ld_tab] bf16 (NULL: 0),
  * row_group [rows] int32 (NULL: group 0).  Writes out [rows, ldo] bf16 and/or per-token int8
@@ -208,15 +214,16 @@ int vdn_adaln_rmsnorm(const void* x, long long ldx, int rows, int hidden, const 
  * * (A B^T) + col_bias).  act: 0 none, 2 GELU (erf), 3 SwiGLU (B's rows interleaved in 128-row
  * gate / up blocks, N % 256 == 0, N' = N / 2).  A: one source, K-concatenated (A2 for
  * k >= k_split) or grouped-K (kg > 0, K / kg slabs group_stride apart).  residual [M, ld_res]
- * bf16 and (row_group [M] int32, group_gate [groups, ld_gate] bf16) are optional.
+ * bf16 and (row_group [M] int32, group_gate [groups, ld_gate] bf16) are optional; row_amax [M] fp32
+ * (optional, zeroed by the caller) receives each row's max |C| for vdn_quant_int8_rows_amax.
  * Replaces: block_kernels.py:92-93 (_post_body) fused into the projection that feeds it,
  * :113-146 (fc1, SwiGLU, fc2). */
 int vdn_gemm_block(int kind, const void* A, long long lda, const void* A2, long long lda2, long long k_split,
                    long long group_stride, int kg, const void* B, long long ldb, void* C, long long ldc, int M,
                    int N, int K, float alpha, const float* dev_scale0, const float* dev_scale1,
                    const float* row_scale, const float* col_scale, const float* col_bias, int act,
-                   const void* residual, long long ld_res,
-                   const int* row_group, const void* group_gate, long long ld_gate, int* dev_err, void* stream);
+                   const void* residual, long long ld_res, const int* row_group, const void* group_gate,
+                   long long ld_gate, float* row_amax, int* dev_err, void* stream);
 
 /* ---------------------------------------------------------------- diagnostics ----- */
 

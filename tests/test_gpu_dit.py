@@ -42,9 +42,12 @@ def _segments(lay):
     return [(0, lay.video_start, 0), (lay.video_start, lay.seq_len, 1)]
 
 
-def test_adaln_rmsnorm_matches_oracle_and_int8_codes_are_exact():
+@pytest.mark.parametrize("H", [256, 5120, 12288, 40960])
+def test_adaln_rmsnorm_matches_oracle_and_int8_codes_are_exact(H):
+    """Every kernel width class: CTA-per-row with 2 or 4 vectors per thread of 256 / 1024
+    threads, and the warp-per-row streaming kernel for the widest rows."""
     gen = torch.Generator().manual_seed(1)
-    S, H = 777, 5120
+    S = 777 if H <= 12288 else 97
     x = torch.randn(S, H, generator=gen).to(torch.bfloat16)
     w = 1 + 0.1 * torch.randn(H, generator=gen)
     scale = (torch.randn(3, H, generator=gen) * 0.1).to(torch.bfloat16)
@@ -120,6 +123,32 @@ def test_gemm_block_epilogues_match_torch(kind):
     torch.cuda.synchronize()
     st.raise_if_failed()
     assert rel_l2(out, want) < 1e-2
+
+
+@pytest.mark.parametrize("act", [0, 2, 3])
+def test_row_amax_epilogue_gives_the_quantiser_its_exact_scales(act):
+    """fc1 with row_amax + the streaming quantiser == the two-pass row quantiser, bit for bit."""
+    gen = torch.Generator().manual_seed(5)
+    M, K, F = 333, 512, 1024
+    a = torch.randn(M, K, generator=gen)
+    w = torch.randn(2 * F if act == 3 else F, K, generator=gen) * 0.05
+    qa, sa = vo.int8_quantize_rows(a)
+    qw, sw = vo.int8_quantize_weight(w)
+    A, W, rs, cs = qa.to(DEV), qw.to(DEV), sa.to(DEV), sw.to(DEV)
+    out = torch.empty(M, F, device=DEV, dtype=torch.bfloat16)
+    amax = torch.zeros(M, device=DEV)
+    st = pkg.DeviceStatus(DEV)
+    stream = pkg._lib.stream_handle(DEV)
+    gemm_block(2, A, W, out, row_scale=rs, col_scale=cs, act=act, row_amax=amax, status=st, stream=stream, rows=M)
+    q = torch.empty(M, F, device=DEV, dtype=torch.int8)
+    qs = torch.empty(M, device=DEV)
+    pkg._lib.call("vdn_quant_int8_rows_amax", out.data_ptr(), out.stride(0), M, F, amax.data_ptr(), q.data_ptr(),
+                  q.stride(0), qs.data_ptr(), stream)
+    torch.cuda.synchronize()
+    st.raise_if_failed()
+    assert torch.equal(amax.cpu(), out.float().abs().amax(1).cpu())
+    ref = pkg.quantize_rows_int8(out)
+    assert torch.equal(q, ref.data) and torch.equal(qs, ref.scale)
 
 
 def _dit(seed, activation):
