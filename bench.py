@@ -275,6 +275,9 @@ def run_reference_arm(args, c, world, rank):
     print(json.dumps(line), flush=True)
 
 
+E2E_ROW_BLOCKS = 4  # row blocks of the end-to-end copies at N = 1
+
+
 def metric_name(c) -> str:
     """BASELINE's metric on the config's geometry (config 1: 31x836+512 tokens)."""
     return (f"VDN hybrid block fwd TFLOP/s at {c['frames']}x{c['grid'][0] * c['grid'][1]}+{c['text']} tokens "
@@ -550,9 +553,9 @@ def main():
     fwd = pkg.make_vdn_forward(attn, state, 0)
     S = lay.seq_len
 
-    def run_fwd(xd):
+    def run_fwd(xd, io=None):
         with pkg.publish_layout(lay):
-            return fwd(xd)
+            return fwd(xd, transformer_options={pkg.hybrid.STREAM_IO_KEY: io} if io is not None else None)
 
     if world == 1:
         streamer = pkg.HostStreamer(run_fwd, dev, (S, hidden))
@@ -579,7 +582,10 @@ def main():
         outs_host = [torch.empty(n_rows, hidden, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
 
     def e2e_run(k):
-        streamer.run([inputs_host[0]] * k, [outs_host[i & 1] for i in range(k)], prepare=prepare)
+        # one GPU: inputs copied in and outputs copied back by row blocks, overlapping the
+        # first step's QKV and the last step's output projection too
+        streamer.run([inputs_host[0]] * k, [outs_host[i & 1] for i in range(k)], prepare=prepare,
+                     chunks=E2E_ROW_BLOCKS if world == 1 else 1)
 
     e2e_run(args.warmup)
     torch.cuda.synchronize()
@@ -623,7 +629,8 @@ def main():
         # bytes summed over the ranks (at N > 1 each rank moves its own row block)
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": S * hidden * 2, "d2h_bytes_per_step": S * hidden * 2,
-                "copies": "pinned host buffers; H2D of step i+1 and D2H of step i-1 overlap step i (HostStreamer)",
+                "copies": "pinned host buffers; H2D of step i+1 and D2H of step i-1 overlap step i (HostStreamer); "
+                  f"{E2E_ROW_BLOCKS if world == 1 else 1} row blocks per copy",
                 **copy_ms},
         "gpu_launches": launches,
         "clocks": clock_summary,

@@ -728,9 +728,9 @@ int vdn_qkv_gemm(int kind, const void* x, long long ldx, const void* w, long lon
   ep.aux_out = aux_out;
   ep.ld_aux = ld_aux;
   if (q_act) {
-    if (!vdn::aligned16(q_act) || act_row0 < 0 || act_rows <= 0 || act_tpf <= 0 || act_rows % act_tpf ||
-        act_row0 + act_rows > S)
-      return vdn::kBadArgument;
+    // act_row0 is relative to this call's first row: a call over a block of rows (negative
+    // act_row0 when the block starts inside the branch rows) writes the rows it holds
+    if (!vdn::aligned16(q_act) || act_rows <= 0 || act_tpf <= 0 || act_rows % act_tpf) return vdn::kBadArgument;
     ep.act_out = reinterpret_cast<__nv_bfloat16*>(q_act);
     ep.act_row0 = act_row0;
     ep.act_rows = act_rows;

@@ -29,7 +29,7 @@ from collections import OrderedDict
 import torch
 
 from . import _lib
-from .hybrid import B200State, FusedBlock, GatedResidual, _weight_of, gemm_block
+from .hybrid import STREAM_IO_KEY, B200State, FusedBlock, GatedResidual, StreamIO, _weight_of, gemm_block
 from .layout import current_layout
 from .projection import QuantizedMatrix, quantize_weight
 
@@ -215,10 +215,15 @@ class B200DiTBlock:
         gemm_block(2, aq.data, self.w2.data, x1, row_scale=aq.scale, col_scale=self.w2.scale, col_bias=self.b2,
                    residual=res, status=status, stream=stream, rows=n)
 
-    def forward(self, x, mods, group, layout, plans, status, *, out=None, **attn_kwargs) -> torch.Tensor:
+    def forward(self, x, mods, group, layout, plans, status, *, out=None, io: StreamIO | None = None,
+                **attn_kwargs) -> torch.Tensor:
         """x [S, hidden] bf16 (the residual stream), mods: the six adaln tables
-        [groups, hidden], group [S] int32 -> the block output [S, hidden] bf16."""
+        [groups, hidden], group [S] int32 -> the block output [S, hidden] bf16.  ``io``: x
+        arrives and the output leaves by row blocks (``StreamIO``)."""
         _lib.require_cuda(x)
+        compute = torch.cuda.current_stream(x.device)
+        if io is not None and (x.dtype != torch.bfloat16 or x.stride(-1) != 1):
+            io.wait_all(compute)
         if x.dtype != torch.bfloat16 or x.stride(-1) != 1:
             x = x.to(torch.bfloat16).contiguous()
         S = x.shape[0]
@@ -226,13 +231,24 @@ class B200DiTBlock:
         mods = _mods_device(mods, self.hidden, x.device)
         group = group.to(x.device, torch.int32).contiguous()
         h = self.workspace(S)["h"][:S]
-        self._adaln(x, self.norm1, self.eps1, mods[1], mods[0], group, out=h, stream=stream)
+        inner_io = None
+        if io is not None and len(io.in_blocks) > 1:
+            # pre-norm each row block as it lands; the attention then follows on this stream
+            for k, (r0, r1) in enumerate(io.bounds()):
+                io.wait(compute, k)
+                self._adaln(x[r0:r1], self.norm1, self.eps1, mods[1], mods[0], group[r0:r1], out=h[r0:r1],
+                            stream=stream)
+            inner_io = StreamIO([(r1, None) for r1, _ in io.in_blocks], io.out_ready)
+        else:
+            if io is not None:
+                io.wait_all(compute)
+            self._adaln(x, self.norm1, self.eps1, mods[1], mods[0], group, out=h, stream=stream)
         residual = GatedResidual(x, mods[2], group)
 
         def mlp(rows_view, row0, n):
             self.mlp_rows(rows_view, group[row0:row0 + n], mods, status, stream)
 
-        return self.attn.forward(h, layout, plans, status, out=out, residual=residual, row_epilogue=mlp,
+        return self.attn.forward(h, layout, plans, status, out=out, residual=residual, row_epilogue=mlp, io=inner_io,
                                  **attn_kwargs)
 
 
@@ -285,6 +301,7 @@ def make_fast_block_forward(block, state: B200State, block_index: int):
         mods = block.adaln_proj(t_emb)
         status = state.device_status(x.device)
         out = db.forward(x, mods, group, layout, state.window_plans, status,
+                         io=(transformer_options or {}).get(STREAM_IO_KEY),
                          linear_enabled=bool(config.get("linear_enabled", True)),
                          bridge=str(config.get("bridge", "alpha")),
                          enable_text_state=bool(config.get("enable_text_state", True)))

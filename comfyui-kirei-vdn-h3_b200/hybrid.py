@@ -39,6 +39,7 @@ from .shard import (HeadShard, RowExchange, concat_rows, default_shard, qkv_row_
                     slice_branch_weights, split_heads_outputs)
 from .window import ATTENTION_BACKENDS, WindowPlanCache, launch_window_attention
 
+STREAM_IO_KEY = "vdn_b200_io"  # transformer_options entry carrying a StreamIO (HostStreamer)
 AUX_ALIGN = 32  # side columns padded to 32: 128-byte fp32 rows, and no extra 256-column GEMM tile
 EXCHANGE_CHUNKS = 4  # pipelined exchange / projection / gather steps of the head-sharded block
 EXCHANGE_MIN_ROWS = 512  # rows per rank and chunk (one wave of projection tiles); fewer: one step
@@ -61,6 +62,40 @@ class GatedResidual:
 
     def rows(self, r0: int, n: int) -> "GatedResidual":
         return GatedResidual(self.x[r0:r0 + n], self.gate, self.group[r0:r0 + n])
+
+
+class StreamIO:
+    """Row-block hand-over between host copies and one block forward (``HostStreamer``):
+    ``in_blocks`` = [(row_end, event), ...] cover x in order, each event recorded when that
+    block's copy-in landed; the block projects each row block as soon as it may and calls
+    ``out_ready(out, row0, rows)`` once each block of its output is final.  A forward that
+    cannot work by blocks waits for every block first (``wait_all``)."""
+
+    def __init__(self, in_blocks, out_ready=None):
+        self.in_blocks = list(in_blocks)
+        self.out_ready = out_ready
+        self.waited = 0
+
+    def bounds(self):
+        r0 = 0
+        for r1, _ in self.in_blocks:
+            yield r0, r1
+            r0 = r1
+
+    def wait(self, stream, k: int):
+        ev = self.in_blocks[k][1]
+        if ev is not None:  # None: the block was produced on the compute stream itself
+            stream.wait_event(ev)
+        self.waited = max(self.waited, k + 1)
+
+    def wait_all(self, stream):
+        if self.in_blocks and self.waited < len(self.in_blocks):
+            self.wait(stream, len(self.in_blocks) - 1)  # one copy stream: the last block lands last
+            self.waited = len(self.in_blocks)
+
+    @property
+    def complete(self) -> bool:
+        return self.waited >= len(self.in_blocks)
 
 
 def gemm_block(kind, a, w, out, *, a2=None, k_split=0, grouped=None, alpha=1.0, dev_scales=(None, None),
@@ -227,45 +262,52 @@ class FusedBlock:
         return ws
 
     # ------------------------------------------------------------------ phases
-    def _qkv(self, x, ws, status, stream, q_act=None):
+    def _qkv(self, x, ws, status, stream, q_act=None, rows=None):
         """q_act: (buffer, first row, rows, tokens per frame) of the branch q features the
-        epilogue writes, or None."""
+        epilogue writes, or None.  rows = (r0, r1): project only those rows of x (a block of
+        the sequence whose copy has landed)."""
         g = self.geo
-        S = x.shape[0]
-        qa = (None, 0, 0, 0) if q_act is None else (q_act[0].data_ptr(),) + tuple(q_act[1:])
+        r0, r1 = rows if rows is not None else (0, x.shape[0])
+        S = r1 - r0
+        x = x[r0:r1]
+        qkv, qkn, aux = ws["qkv"][r0:r1], ws["qkn"][r0:r1], ws["aux"][r0:r1]
+        qa = (None, 0, 0, 0) if q_act is None else (q_act[0].data_ptr(), q_act[1] - r0) + tuple(q_act[2:])
         if self.precision == "bf16":
             _lib.call("vdn_qkv_gemm", 0, x.data_ptr(), x.stride(0), self.w_big.data_ptr(), self.w_big.stride(0), S,
                       g.hidden, g.inner, self.n_aux, g.dim, self.norm_w.data_ptr(), self.eps, 1.0, None, None, None,
-                      None, ws["qkv"].data_ptr(), ws["qkv"].stride(0), ws["qkn"].data_ptr(), ws["qkn"].stride(0),
-                      ws["aux"].data_ptr(), ws["aux"].stride(0), *qa, status.err_ptr, stream)
+                      None, qkv.data_ptr(), qkv.stride(0), qkn.data_ptr(), qkn.stride(0), aux.data_ptr(),
+                      aux.stride(0), *qa, status.err_ptr, stream)
             return
         kind = KIND[self.precision]
         if self.precision == "int8":
-            xq = quantize_rows_int8(x, ws["xq"])
+            xq = quantize_rows_int8(x, QuantizedMatrix(ws["xq"].data[r0:r1], ws["xq"].scale[r0:r1], "int8"))
             rs, cs, d0, d1 = xq.scale, self.w_qkv_q.scale, None, None
         else:
             xq = quantize_tensor_fp8(x, ws["xq"], ws["work"])
             rs, cs, d0, d1 = None, None, xq.scale, self.w_qkv_q.scale
         _lib.call("vdn_qkv_gemm", kind, xq.data.data_ptr(), xq.data.stride(0), self.w_qkv_q.data.data_ptr(),
                   self.w_qkv_q.data.stride(0), S, g.hidden, g.inner, 0, g.dim, self.norm_w.data_ptr(), self.eps, 1.0,
-                  _lib.ptr(d0), _lib.ptr(d1), _lib.ptr(rs), _lib.ptr(cs), ws["qkv"].data_ptr(), ws["qkv"].stride(0),
-                  ws["qkn"].data_ptr(), ws["qkn"].stride(0), None, 0, *qa, status.err_ptr, stream)
+                  _lib.ptr(d0), _lib.ptr(d1), _lib.ptr(rs), _lib.ptr(cs), qkv.data_ptr(), qkv.stride(0),
+                  qkn.data_ptr(), qkn.stride(0), None, 0, *qa, status.err_ptr, stream)
         # side projections stay bf16 -> fp32 (gates, beta, alpha are never quantised: fp8.py:1-12)
         _lib.call("vdn_gemm", 0, x.data_ptr(), x.stride(0), None, 0, 0, self.w_side.data_ptr(),
-                  self.w_side.stride(0), ws["aux"].data_ptr(), ws["aux"].stride(0), 1, S, self.n_aux, g.hidden, 1.0,
+                  self.w_side.stride(0), aux.data_ptr(), aux.stride(0), 1, S, self.n_aux, g.hidden, 1.0,
                   None, None, None, None, None, 0, None, 0, status.err_ptr, stream)
 
-    def _out(self, ws, out, with_branch, status, stream, residual: GatedResidual | None = None):
+    def _out(self, ws, out, with_branch, status, stream, residual: GatedResidual | None = None, rows=None):
+        """The output projection of rows [r0, r1) (all rows by default)."""
         g = self.geo
-        S = out.shape[0]
+        r0, r1 = rows if rows is not None else (0, out.shape[0])
+        flat, branch, out = ws["flat"][r0:r1], ws["branch"][r0:r1], out[r0:r1]
+        if residual is not None and rows is not None:
+            residual = residual.rows(r0, r1 - r0)
         if self.precision == "bf16":
-            a2 = ws["branch"] if with_branch else None
-            gemm_block(0, ws["flat"], self.w_out_cat, out, a2=a2, k_split=g.inner if with_branch else 0,
+            a2 = branch if with_branch else None
+            gemm_block(0, flat, self.w_out_cat, out, a2=a2, k_split=g.inner if with_branch else 0,
                        k=2 * g.inner if with_branch else g.inner, residual=residual, status=status, stream=stream,
-                       rows=S)
+                       rows=r1 - r0)
             return
-        self._quantized_out(ws["flat"], ws["branch"] if with_branch else None, ws, out, status, stream,
-                            residual=residual)
+        self._quantized_out(flat, branch if with_branch else None, ws, out, status, stream, residual=residual)
 
     def _quantized_out(self, flat, branch, ws, out, status, stream, amax_reduce=None,
                        residual: GatedResidual | None = None):
@@ -341,12 +383,13 @@ class FusedBlock:
 
     def forward(self, x: torch.Tensor, layout: VDNLayout, plans: WindowPlanCache, status: _lib.DeviceStatus,
                 *, linear_enabled=True, bridge="alpha", enable_text_state=True, out=None,
-                residual: GatedResidual | None = None, row_epilogue=None) -> torch.Tensor:
+                residual: GatedResidual | None = None, row_epilogue=None, io: StreamIO | None = None) -> torch.Tensor:
         """The block output [S, hidden]; with ``residual`` the gated residual stream
         ``residual.x + gate * block(x)`` instead, and ``row_epilogue(rows_view, row0, n)``
-        run on the projected rows (in place) before they leave this GPU."""
+        run on the projected rows (in place) before they leave this GPU.  ``io``: x arrives
+        and the output leaves by row blocks (see :class:`StreamIO`)."""
         ws, linear_active = self.forward_heads(x, layout, plans, status, linear_enabled=linear_enabled,
-                                               bridge=bridge, enable_text_state=enable_text_state)
+                                               bridge=bridge, enable_text_state=enable_text_state, io=io)
         stream = _lib.stream_handle(x.device)
         if self.shard is not None:
             full = self._out_sharded(ws, linear_active, status, stream, residual, row_epilogue)
@@ -356,17 +399,26 @@ class FusedBlock:
             return out
         if out is None:
             out = torch.empty(x.shape[0], self.geo.hidden, device=x.device, dtype=torch.bfloat16)
-        self._out(ws, out, linear_active, status, stream, residual)
-        if row_epilogue is not None:
-            row_epilogue(out, 0, out.shape[0])
+        blocks = list(io.bounds()) if io is not None and io.out_ready is not None and self.precision != "fp8" \
+            else [(0, out.shape[0])]
+        for r0, r1 in blocks:
+            self._out(ws, out, linear_active, status, stream, residual, rows=(r0, r1))
+            if row_epilogue is not None:
+                row_epilogue(out[r0:r1], r0, r1 - r0)
+            if io is not None and io.out_ready is not None and len(blocks) > 1:
+                io.out_ready(out, r0, r1 - r0)
         return out
 
     def forward_heads(self, x: torch.Tensor, layout: VDNLayout, plans: WindowPlanCache, status: _lib.DeviceStatus,
-                      *, linear_enabled=True, bridge="alpha", enable_text_state=True):
+                      *, linear_enabled=True, bridge="alpha", enable_text_state=True, io: StreamIO | None = None):
         """Phases 1-3 (QKV, branch, window attention) for this rank's heads; returns the
         workspace holding the per-head outputs and whether the branch ran."""
         g = self.geo
         S = x.shape[0]
+        by_blocks = (io is not None and x.dtype == torch.bfloat16 and x.stride(-1) == 1 and self.shard is None and
+                     self.precision != "fp8" and len(io.in_blocks) > 1)
+        if io is not None and not by_blocks:
+            io.wait_all(torch.cuda.current_stream(x.device))  # fp8 needs the whole tensor's scale
         if x.dtype != torch.bfloat16 or x.stride(-1) != 1:
             x = x.to(torch.bfloat16).contiguous()
         stream = _lib.stream_handle(x.device)
@@ -380,7 +432,14 @@ class FusedBlock:
             r0 = layout.video_start + (tpf if skip else 0)
             if "q" not in self.short_conv:  # q's features need no conv: the QKV epilogue writes them
                 q_act = (ws["bws"].qf, r0, Fb * tpf, tpf)
-        self._qkv(x, ws, status, stream, q_act)
+        if by_blocks:
+            # project each row block of x as soon as its copy has landed
+            compute = torch.cuda.current_stream(x.device)
+            for k, (r0b, r1b) in enumerate(io.bounds()):
+                io.wait(compute, k)
+                self._qkv(x, ws, status, stream, q_act, rows=(r0b, r1b))
+        else:
+            self._qkv(x, ws, status, stream, q_act)
         if linear_active:
             rows = slice(r0, r0 + Fb * tpf)
             bounds_b = [(lo - 1, hi - 1) for lo, hi in layout.bounds[1:-1]] if skip else list(layout.bounds)
@@ -499,7 +558,8 @@ def make_vdn_forward(attn, state: B200State, block_index: int):
         out = block.forward(x, layout, state.window_plans, status,
                             linear_enabled=bool(config.get("linear_enabled", True)),
                             bridge=str(config.get("bridge", "alpha")),
-                            enable_text_state=bool(config.get("enable_text_state", True)))
+                            enable_text_state=bool(config.get("enable_text_state", True)),
+                            io=(transformer_options or {}).get(STREAM_IO_KEY))
         state.last_attention_backend = "b200_dense" if layout.full_cover else "b200"
         return out.to(x.dtype)
 

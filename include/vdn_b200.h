@@ -60,7 +60,8 @@ int vdn_gemm_grouped_k(int kind, const void* A, long long lda, long long group_s
  *           :755 (output-gate down).  q_act (optional): the branch's q features of rows
  * [act_row0, act_row0 + act_rows) -- silu(bf16 q) L2-normalised per head, stored
  * [frame][head][token][head_dim] with act_tpf tokens per frame (kernels.py:47-51 and the FHSD
- * permute of branch.py:672-689). */
+ * permute of branch.py:672-689).  act_row0 counts from this call's first row (it may be
+ * negative when the call covers a block of rows starting inside the branch rows). */
 int vdn_qkv_gemm(int kind, const void* x, long long ldx, const void* w, long long ldw, int S, int hidden,
                  int inner, int n_aux, int head_dim, const float* norm_w, float eps, float alpha,
                  const float* dev_scale0, const float* dev_scale1, const float* row_scale,

@@ -134,6 +134,32 @@ def test_host_streamer_matches_direct_forward():
         assert torch.equal(got, want)
 
 
+@pytest.mark.parametrize("precision", ["bf16", "int8"])
+def test_host_streamer_by_row_blocks_matches_direct_forward(precision):
+    """Row-block copies in and out (the block's QKV starts on each landed block, each
+    projected block goes back at once): bit-identical to the direct forward."""
+    c = dict(vo.CONFIG0, frames=15, grid=(8, 8))  # 992 rows: several 128-row blocks
+    bw = vo.make_block(9, c["hidden"], c["heads"], c["dim"])
+    lay = _layout(c)
+    state = pkg.B200State("t", {"enable_softmax_gate": True}, [bw.branch], c["heads"], c["dim"],
+                          projection_precision=precision)
+    fwd = pkg.make_vdn_forward(_Attn(bw, c["heads"], c["dim"]), state, 0)
+
+    def run(xd, io=None):
+        with pkg.publish_layout(lay):
+            return fwd(xd, transformer_options={pkg.hybrid.STREAM_IO_KEY: io} if io is not None else None)
+
+    xs = [vo.make_x(30 + i, lay.seq_len, c["hidden"]).to(torch.bfloat16).pin_memory() for i in range(3)]
+    outs = [torch.full((lay.seq_len, c["hidden"]), 7.0, dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+    streamer = pkg.HostStreamer(run, DEV, (lay.seq_len, c["hidden"]))
+    with pkg.cholesky_runtime_scope():
+        streamer.run(xs, outs, chunks=4)
+        torch.cuda.synchronize()
+        direct = [run(x.to(DEV)).cpu() for x in xs]
+    for got, want in zip(outs, direct):
+        assert torch.equal(got, want)
+
+
 @pytest.mark.parametrize("order", [("text", "audio", "video", "ref"), ("video", "audio", "text")])
 def test_block_on_packed_layout_with_global_segments(order):
     """A ComfyUI PackedLayout with audio / reference-frame rows around the video (global rows

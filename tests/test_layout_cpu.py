@@ -84,3 +84,14 @@ def test_layout_from_payload_uses_the_matching_payload_layout():
         pkg.layout_from_payload({"layout": p}, (torch.zeros(1, 16, 6, 8, 10), audio), context, {})
     with pytest.raises(TypeError, match="expected x="):
         pkg.layout_from_payload({}, (video,), context, {})
+
+
+@pytest.mark.parametrize("rows", [1, 100, 127, 128, 129, 992, 26428, 119552])
+@pytest.mark.parametrize("chunks", [1, 2, 4, 7])
+def test_streamer_row_blocks_tile_rows_on_gemm_tiles(rows, chunks):
+    from vdn_b200.host_io import row_blocks
+
+    blocks = row_blocks(rows, chunks)
+    assert blocks[0][0] == 0 and blocks[-1][1] == rows and len(blocks) <= chunks
+    assert all(a1 == b0 for (_, a1), (b0, _) in zip(blocks, blocks[1:]))
+    assert all(r0 % 128 == 0 and r1 > r0 for r0, r1 in blocks)
