@@ -47,7 +47,8 @@ struct Params {
   const int* items;      // [n_items] (head << 20) | query tile
   int n_items;
   const int* tile_off;   // [n_qtiles + 1]
-  const int* qtile;      // [n_qtiles] (row0 << 8) | (rows - 1), rows <= 256; null: row0 = 256 * tile
+  const int* qtile;      // [n_qtiles][2] per 128-row half: (row0 << 8) | rows, rows <= 128 (0: empty
+                         // half, row0 still a valid row); null: half a = rows [256 t + 128 a, +128)
   const int* ktile;      // [n_ktiles] (k0 << 9) | (masked << 8) | (valid - 1)
   __nv_bfloat16* out;
   long long ld_out;
@@ -58,8 +59,10 @@ struct Params {
   int* work_counter;         // zeroed before the launch; items are claimed with atomicAdd
 };
 
-__device__ __forceinline__ int q_row0(const Params& p, int qt) {
-  return p.qtile ? (p.qtile[qt] >> 8) : qt * 256;
+// (first row << 8) | rows of half `a` of query tile `qt`: the two halves of a work item may
+// come from different places of the sequence (rows with the same visible keys).
+__device__ __forceinline__ int q_half(const Params& p, int qt, int a) {
+  return p.qtile ? p.qtile[2 * qt + a] : (((qt * 256 + a * 128) << 8) | 128);
 }
 
 // Low min(max(n, 0), 32) bits set.
@@ -245,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int a = 0; a < 2; ++a)
           for (int b = 0; b < kDBlocks; ++b)
             tma_load_2d(sQ + a * L::kQTile + b * (BQ * 128), &tq, B(B_QFULL), h * D + b * 64,
-                        q_row0(p, qt) + a * BQ);
+                        q_half(p, qt, a) >> 8);
         const int t0 = p.tile_off[qt], t1 = p.tile_off[qt + 1];
         bool ok = true;
         for (int t = t0; t < t1; ++t, ++g) {
@@ -363,10 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (code < 0) break;
       const int h = code >> 20, qt = code & 0xFFFFF;
       const int t0 = p.tile_off[qt], n = p.tile_off[qt + 1] - t0;
-      const int qinfo = p.qtile ? p.qtile[qt] : (((qt * 2 * BQ) << 8) | (2 * BQ - 1));
-      const int qrow = (qinfo >> 8) + a * BQ + row_in_tile;
-      // rows past the tile's count belong to the next tile (or lie past S): computed, not stored
-      const bool row_valid = a * BQ + row_in_tile <= (qinfo & 0xFF) && qrow < p.S;
+      const int qinfo = q_half(p, qt, a);
+      const int qrow = (qinfo >> 8) + row_in_tile;
+      // rows past the half's count belong to another tile (or lie past S): computed, not stored
+      const bool row_valid = row_in_tile < (qinfo & 0xFF) && qrow < p.S;
       // Per-row visibility (window.py:327-344): a windowed row cannot see the video keys in
       // [x0, x1) and [x2, x3) = [first non-anchor key, window start) and [window end, first
       // key of the last anchor frame); rows that see every key get two empty spans.
@@ -555,8 +558,9 @@ extern "C" {
 //   out      [S, ld_out] bf16: gated output at columns h*D
 //   frame_lo / frame_hi [F] int32 device arrays: clamped visible key-frame range per frame
 //   items / tile_off / qtile / ktile: the block-sparse plan built by the host package;
-//            qtile [n_qtiles] = (first row << 8) | (rows - 1) with rows <= 256, or null for
-//            query tile t = rows [256 t, 256 t + 256)
+//            qtile [n_qtiles][2] = per 128-row half (first row << 8) | rows, rows <= 128 (0: an
+//            empty half whose first row is still a valid row), or null for query tile t =
+//            rows [256 t, 256 t + 256)
 //   gate_logits [S, ld_gate] fp32 (column gate_col0 + h) and gate_bias [H]: optional
 //   work_counter: one device int, zeroed here on the stream; launches that share it must not overlap
 // Replaces window.py:277-313 (window_softmax_grouped) + hybrid.py:518-528.

@@ -63,7 +63,7 @@ class WindowPlan:
     frame_lo: np.ndarray  # [F] int32, clamped
     frame_hi: np.ndarray  # [F] int32, clamped
     tile_off: np.ndarray  # [nq + 1] int32
-    qtile: np.ndarray  # [nq] int32 packed (row0 << 8) | (rows - 1)
+    qtile: np.ndarray  # [nq, 2] int32 per 128-row half: (row0 << 8) | rows (0 rows: empty half)
     ktile: np.ndarray  # [n_ktiles] int32 packed (k0 << 9) | (masked << 8) | (valid - 1)
     tiles_per_q: np.ndarray  # [nq]
     masked_tiles: int
@@ -73,10 +73,14 @@ class WindowPlan:
     def n_qtiles(self) -> int:
         return len(self.tiles_per_q)
 
-    def q_rows(self, qt: int) -> tuple[int, int]:
-        """(first row, row count) of query tile ``qt``."""
-        code = int(self.qtile[qt])
-        return code >> 8, (code & 0xFF) + 1
+    def q_halves(self, qt: int) -> list[tuple[int, int]]:
+        """[(first row, row count)] of the non-empty 128-row halves of query tile ``qt``."""
+        out = []
+        for a in range(2):
+            code = int(self.qtile[qt, a])
+            if code & 0xFF:
+                out.append((code >> 8, code & 0xFF))
+        return out
 
     def items(self, heads: int, long_factor: float | None = None) -> np.ndarray:
         """(head << 20) | q_tile in claim order: head-major (the CTAs in flight share one
@@ -109,11 +113,36 @@ class WindowPlan:
                 "frame_lo": torch.from_numpy(self.frame_lo).to(dev),
                 "frame_hi": torch.from_numpy(self.frame_hi).to(dev),
                 "tile_off": torch.from_numpy(self.tile_off).to(dev),
-                "qtile": torch.from_numpy(self.qtile).to(dev),
+                "qtile": torch.from_numpy(np.ascontiguousarray(self.qtile.reshape(-1))).to(dev),
                 "ktile": torch.from_numpy(self.ktile).to(dev),
                 "items": torch.from_numpy(self.items(heads)).to(dev),
             }
         return self._device[key]
+
+
+HALF = BQ // 2  # rows per MMA half of a work item
+
+
+def _pair_short_tiles(q_tiles, keys):
+    """Query tiles as two 128-row halves [(first row, rows), (first row, rows)]; tiles of at
+    most 128 rows whose key tiles are identical (the partial tiles at the ends of the
+    every-key segments before and after the video) share one work item, one per half."""
+    halves, out_keys, waiting = [], [], {}
+    for (r0, r1), kc in zip(q_tiles, keys):
+        n = r1 - r0
+        if n > HALF:
+            halves.append([(r0, HALF), (r0 + HALF, n - HALF)])
+            out_keys.append(kc)
+            continue
+        sig = tuple(kc[0])
+        if sig in waiting:
+            i = waiting.pop(sig)
+            halves[i][1] = (r0, n)
+        else:
+            waiting[sig] = len(halves)
+            halves.append([(r0, n), (r0, 0)])  # an empty second half keeps a valid first row
+            out_keys.append(kc)
+    return halves, out_keys
 
 
 def build_window_plan(seq_len, video_start, video_end, num_frames, tokens_per_frame, bounds,
@@ -196,14 +225,15 @@ def build_window_plan(seq_len, video_start, video_end, num_frames, tokens_per_fr
     for cuts in candidates:
         q_tiles = [(r0, min(b, r0 + BQ)) for a, b in zip(cuts, cuts[1:]) for r0 in range(a, b, BQ)]
         keys = [tile_keys(r0, r1) for r0, r1 in q_tiles]
+        halves, keys = _pair_short_tiles(q_tiles, keys)
         cost = sum(len(c) + (MASKED_TILE_COST - 1.0) * m + ITEM_COST for c, m in keys)
         if best is None or cost < best[0]:
-            best = (cost, q_tiles, keys)
-    _, q_tiles, keys = best
-    nq = len(q_tiles)
+            best = (cost, halves, keys)
+    _, halves, keys = best
+    nq = len(halves)
     tile_off = np.zeros(nq + 1, dtype=np.int64)
     tile_off[1:] = np.cumsum([len(c) for c, _ in keys])
-    qtile = np.array([(r0 << 8) | (r1 - r0 - 1) for r0, r1 in q_tiles], dtype=np.int64)
+    qtile = np.array([[(r0 << 8) | n for r0, n in hv] for hv in halves], dtype=np.int64).reshape(nq, 2)
     ktiles = np.asarray([code for c, _ in keys for code in c], dtype=np.int64)
     tiles_per_q = np.array([len(c) for c, _ in keys], dtype=np.int64)
     masked = int(sum(m for _, m in keys))

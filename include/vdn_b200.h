@@ -105,8 +105,9 @@ int vdn_fp8_linear_noalloc(const void* x, long long ldx, int M, int K, const voi
 /* Exact block-sparse window softmax attention with the per-token head gate fused.
  * q, k, v: [S, H*D] bf16 views (pitches ld_q/ld_k/ld_v); q, k already RMS-normalised.
  * frame_lo/frame_hi [F]: clamped visible key-frame range; items/tile_off/qtile/ktile: host
- * plan (window.py in the package); qtile [n_qtiles] = (first row << 8) | (rows - 1), rows <= 256
- * (null: tile t covers rows [256 t, 256 t + 256)).  out [S, ld_out] bf16 at columns h*D.
+ * plan (window.py in the package); qtile [n_qtiles][2] = per 128-row half (first row << 8) | rows,
+ * rows <= 128, 0 for an empty half whose first row is still valid (null: tile t covers rows
+ * [256 t, 256 t + 256)).  out [S, ld_out] bf16 at columns h*D.
  * gate_logits [S, ld_gate] fp32 (column gate_col0 + h) + gate_bias [H]: optional.
  * work_counter: one device int (zeroed on the stream by the call) through which the
  * persistent CTAs claim work items; calls sharing it must not overlap on the GPU.

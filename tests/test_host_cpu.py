@@ -25,9 +25,9 @@ def _expand_plan(plan, S):
     allowed = np.zeros((S, S), dtype=bool)
     rows_seen = np.zeros(S, dtype=np.int32)
     for qt in range(plan.n_qtiles):
-        r0, n = plan.q_rows(qt)
-        assert 1 <= n <= bw.BQ and r0 + n <= S
-        rows = np.arange(r0, r0 + n)
+        halves = plan.q_halves(qt)
+        assert 1 <= len(halves) <= 2 and all(1 <= n <= bw.BQ // 2 and r0 + n <= S for r0, n in halves)
+        rows = np.concatenate([np.arange(r0, r0 + n) for r0, n in halves])
         rows_seen[rows] += 1
         dense = (rows < vs) | (rows >= ve)
         f = np.clip((rows - vs) // tpf, 0, F - 1)
@@ -125,13 +125,21 @@ def test_plan_at_config1_cuts_query_tiles_at_dense_rows():
                                 lay.tokens_per_frame, list(lay.bounds), lay.anchor_frames)
     w0, w1 = lay.video_start + lay.tokens_per_frame, lay.video_end - lay.tokens_per_frame
     full = (lay.seq_len + bw.BKV - 1) // bw.BKV
+    paired = 0
     for qt in range(plan.n_qtiles):
-        r0, n = plan.q_rows(qt)
+        halves = plan.q_halves(qt)
+        dense = [r0 + n <= w0 or r0 >= w1 for r0, n in halves]
         # no tile mixes rows that see every key with windowed rows
-        assert (r0 + n <= w0) or (r0 >= w1) or (w0 <= r0 and r0 + n <= w1), (r0, n)
-        if r0 + n <= w0 or r0 >= w1:
+        for (r0, n), d in zip(halves, dense):
+            assert d or (w0 <= r0 and r0 + n <= w1), (r0, n)
+        assert len(set(dense)) == 1
+        if dense[0]:
             assert plan.tiles_per_q[qt] == full
             assert not any((int(c) >> 8) & 1 for c in plan.ktile[plan.tile_off[qt]:plan.tile_off[qt + 1]])
+        if len(halves) == 2 and halves[1][0] != halves[0][0] + halves[0][1]:
+            paired += 1
+    # the 68-row remainders of the front and back every-key segments share one item
+    assert paired == 1
     items = plan.items(5, 1.5)
     costs = plan.tiles_per_q[items & 0xFFFFF]
     n_dense = 5 * int((plan.tiles_per_q == full).sum())
