@@ -641,17 +641,22 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     bool ok = true;
     for (int step = 0; step < F && ok; ++step) {
       const int t = frame(step);
+      // this frame's B row does not depend on the previous state: it is in registers before
+      // the wait for the previous step's MMA, off the dependent chain of the recurrence
+      const float* brow = Bm + (((long long)t * H + h) * D + i) * D;
+      float4 bv[D / 4];
+#pragma unroll
+      for (int q = 0; q < D / 4; ++q) bv[q] = __ldg(reinterpret_cast<const float4*>(brow) + q);
+      if (step + 1 < F) {  // the next frame's B row into L2 meanwhile
+        const float* nb = Bm + (((long long)frame(step + 1) * H + h) * D + i) * D;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) asm volatile("prefetch.global.L2 [%0];" ::"l"(nb + q * 32));
+      }
       if (step > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(mma_done), (step - 1) & 1, abort_flag, err, kErrWaitOther));
         if (!ok) break;
         tc_fence_after();
       }
-      if (step + 1 < F) {  // the next frame's B row into L2 while this one is built
-        const float* nb = Bm + (((long long)frame(step + 1) * H + h) * D + i) * D;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) asm volatile("prefetch.global.L2 [%0];" ::"l"(nb + q * 32));
-      }
-      const float* brow = Bm + (((long long)t * H + h) * D + i) * D;
       const float* al = alpha + ((long long)t * H + h) * D;
       float* prev = step > 0 ? dst_all + (((long long)frame(step - 1) * H + h) * D + i) * D : nullptr;
 #pragma unroll
@@ -674,8 +679,8 @@ __global__ void __launch_bounds__(kScanThreads, 1)
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {
           const int k0 = c * 32 + q8 * 8;
-          const float4 b0 = *reinterpret_cast<const float4*>(brow + k0);
-          const float4 b1 = *reinterpret_cast<const float4*>(brow + k0 + 4);
+          const float4 b0 = bv[k0 / 4];
+          const float4 b1 = bv[k0 / 4 + 1];
           const float4 a0 = *reinterpret_cast<const float4*>(al + k0);
           const float4 a1 = *reinterpret_cast<const float4*>(al + k0 + 4);
           const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
