@@ -13,6 +13,7 @@ Reference entry points exercised (file:line inside the reference project):
   * window.window_softmax_grouped            vdn_h3/window.py:277-313
   * branch.frame_statistics                  vdn_h3/branch.py:246-282
   * branch.VdnDelta.factor_apply             vdn_h3/branch.py:148-160
+  * branch.SanaDelta.factor_apply            vdn_h3/branch.py:163-177 (delta_rule="sana_scaled")
   * branch.run_scans_reference               vdn_h3/branch.py:297-312
   * branch.gather_linear_state               vdn_h3/branch.py:399-435
   * branch.conv_features                     vdn_h3/branch.py:443-480
@@ -133,6 +134,14 @@ def main():
     out["suffix_first"] = suffix[0].numpy().astype(np.float32)
     out["state_h0"] = state[::2, 0].numpy().astype(np.float32)
     out["state_notext_h1"] = state_nt[1::3, 1].numpy().astype(np.float32)
+    # the alternative delta rule on the same statistics
+    sana = branch.SanaDelta(tpf)
+    s_trans, s_inj = sana.factor_apply(alpha, a, b)
+    s_prefix, s_suffix = branch.run_scans_reference(sana, alpha, a, b, text_state=text)
+    out["sana_T_f0"] = s_trans[0].numpy().astype(np.float32)
+    out["sana_inj_f0"] = s_inj[0].numpy().astype(np.float32)
+    out["sana_prefix_last"] = s_prefix[-1].numpy().astype(np.float32)
+    out["sana_suffix_first"] = s_suffix[0].numpy().astype(np.float32)
 
     # ---- conv features ----------------------------------------------------------------
     bw = vo.make_block(0, hidden, heads, dim)
@@ -181,6 +190,20 @@ def main():
             skip_ends=True, inference=False,
         )
     out["branch_delta"] = delta.numpy().astype(np.float32)
+    # the whole block with the sana_scaled rule
+    br_s = runtime.OptimizedLinearBranch(
+        {k: v.clone() for k, v in w.items()}, heads, dim, delta_rule="sana_scaled", bridge="alpha",
+        a_fp32=True, short_conv=("k", "v"), enable_text_state=True,
+        kernel_backend="eager", compile_policy="off",
+    )
+    state_s = hybrid.VDNState(
+        "golden_sana", cfg, [br_s], heads, dim, weight_mode="resident", attention_backend="grouped",
+        inference=False, kernel_backend="eager", compile_policy="off",
+    )
+    fwd_s = hybrid.make_vdn_forward(attn, state_s, 0)
+    with torch.no_grad(), layout.publish_layout(ref_layout):
+        y_s = fwd_s(x)
+    out["sana_block_out"] = y_s.numpy().astype(np.float32)
     out["weights_digest"] = np.array(tensor_digest(x, bw.qkv, bw.out, *[w[k] for k in sorted(w)]))
     np.savez_compressed(args.out, **out)
     total = sum(v.nbytes for v in out.values())

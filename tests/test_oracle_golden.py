@@ -90,9 +90,33 @@ def test_statistics_factor_scan_gather_match_reference(golden, setup):
     _close(prefix[-1], golden["prefix_last"], 1e-4, 1e-5)
     _close(suffix[0], golden["suffix_first"], 1e-4, 1e-5)
     state = vo.gather_linear_state(prefix, suffix, vo._t(alpha), bounds_b, "alpha", vo._t(text))
-    _close(state[::2, 0], golden["state_h0"], 1e-4, 1e-5)
+    # the reference gathers in fp32; its output moves by ~1.5e-5 with the CPU thread count
+    _close(state[::2, 0], golden["state_h0"], 1e-4, 3e-5)
     state_nt = vo.gather_linear_state(prefix, suffix, vo._t(alpha), bounds_b, "alpha", None)
     _close(state_nt[1::3, 1], golden["state_notext_h1"], 1e-4, 1e-5)
+
+
+def test_sana_factor_and_scans_match_reference(golden, setup):
+    """delta_rule="sana_scaled": T = diag(alpha) (I - A/L), Inj = B/sqrt(L) (branch.py:163-177)."""
+    c, lay, _ = setup
+    kf, vf, beta, alpha, text, _ = _branch_inputs(setup)
+    a, b = vo.frame_statistics(kf, vf, beta)
+    trans, inj = vo.sana_factor_apply(alpha, a, b, lay.tokens_per_frame)
+    _close(trans[0], golden["sana_T_f0"], 1e-5, 1e-6)
+    _close(inj[0], golden["sana_inj_f0"], 1e-5, 1e-6)
+    prefix, suffix = vo.run_scans(trans, inj, vo._t(text))
+    _close(prefix[-1], golden["sana_prefix_last"], 1e-4, 1e-5)
+    _close(suffix[0], golden["sana_suffix_first"], 1e-4, 1e-5)
+
+
+def test_sana_block_forward_matches_reference(golden, setup):
+    c, lay, _ = setup
+    bw = vo.make_block(0, c["hidden"], c["heads"], c["dim"])
+    x = vo.make_x(0, lay.seq_len, c["hidden"])
+    out = vo.block_forward(x, bw, lay, c["heads"], c["dim"], vo.BranchConfig(delta_rule="sana_scaled"))
+    _close(out, golden["sana_block_out"], 1e-4, 2e-6)
+    # the two rules really differ on this input
+    assert np.abs(golden["sana_block_out"] - golden["block_out"]).max() > 1e-3
 
 
 def test_conv_features_match_reference(golden, setup):
