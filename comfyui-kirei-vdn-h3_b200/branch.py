@@ -9,10 +9,11 @@ a_fp32, short_conv, enable_text_state) and its two entry points:
 * ``projected_delta(..., projector=None)`` (runtime.py:545-607), returning it after.
 
 Both run the same kernel sequence as the fused block (``run_branch``): features, alpha,
-frame statistics (+ the text frame), Cholesky inverse, the fused bidirectional scan
-and the gather/readout/RMSNorm/gate kernel.  Only the ``vdn_solve`` rule with the
-``alpha`` or ``none`` bridge is implemented on the device (the released lineage,
-docs/ARCHITECTURE.md:70-82); ``sana_scaled`` raises.
+frame statistics (+ the text frame), the delta factor, the fused bidirectional scan and the
+gather/readout/RMSNorm/gate kernel.  Both delta rules of branch.py:180 run on the device:
+``vdn_solve`` (the released lineage, docs/ARCHITECTURE.md:70-82: Cholesky-checked inverse
+of I + A) and ``sana_scaled`` (M = I - A/L, injection B/sqrt(L)); the bridge is ``alpha``
+or ``none``.
 """
 
 from __future__ import annotations
@@ -26,7 +27,7 @@ import torch
 from . import _lib
 
 TEXT_STATE_SCALE = 0.5  # branch.py:23
-DELTA_RULES = ("vdn_solve",)
+DELTA_RULES = ("vdn_solve", "sana_scaled")  # branch.py:180
 _CHOLESKY_CHECKS: ContextVar = ContextVar("vdn_b200_cholesky_checks", default=None)
 
 
@@ -179,7 +180,8 @@ class BranchWorkspace:
 
 def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_raw, aux, beta_col0, ogd_col0,
                ad_col0, Fb, tpf, frame_size, bounds, bridge, text_k=None, text_v=None, text_aux=None,
-               out, out_row0, status: _lib.DeviceStatus, short_conv=("k", "v"), q_ready=False):
+               out, out_row0, status: _lib.DeviceStatus, short_conv=("k", "v"), q_ready=False,
+               delta_rule="vdn_solve"):
     """Run the branch kernels on the current stream.
 
     q_raw / k_raw / v_raw: [Fb*tpf, H*D] bf16 row views (pitch = stride(0)) of the raw
@@ -187,8 +189,12 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
     (column beta_col0 + h), the output-gate bottleneck (ogd_col0 + j) and the alpha
     bottleneck (ad_col0 + j); text_k / text_v / text_aux: the same for the text rows.
     Writes out[out_row0 + f*tpf + s, h*D + v] (bf16).  q_ready: ws.qf already holds the q
-    features (written by the QKV GEMM epilogue).
+    features (written by the QKV GEMM epilogue).  delta_rule: "vdn_solve" (inverse of I + A,
+    injection folded before the product) or "sana_scaled" (M = I - A/tpf, injection B/sqrt(tpf)
+    added after it; text state 0.5 B/sqrt(text_len), no factorisation).
     """
+    if delta_rule not in DELTA_RULES:
+        raise ValueError(f"unknown delta rule: {delta_rule!r}")
     H, D = bw.heads, bw.dim
     inner = H * D
     rows = Fb * tpf
@@ -233,20 +239,28 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
         call("vdn_temporal_act", text_v.data_ptr(), text_v.stride(0), None, 0, 1, L, H, D, 0, ws.tv.data_ptr(), stream)
         mat = D * D * H
         stats(ws.tk, ws.tv, 1, L, text_aux, ws.A.data_ptr() + 4 * Fb * mat, ws.B.data_ptr() + 4 * Fb * mat)
-        call("vdn_delta_factor", ws.A.data_ptr(), ws.B.data_ptr(), Fb + 1, H, D, ws.inv.data_ptr(),
-             ws.info.data_ptr(), Fb, TEXT_STATE_SCALE, ws.s0.data_ptr(), split, stream)
-        s0 = ws.s0
+    F_inv = Fb + int(has_text)
+    text_frame = Fb if has_text else -1
+    s0 = ws.s0 if has_text else None
+    if delta_rule == "sana_scaled":
+        # python-float scalars as branch.py:167-168 computes them; the C ABI rounds them to fp32
+        # as torch does when it multiplies them into an fp32 tensor
+        inj_scale = (1.0 / tpf) ** 0.5
+        text_inj = (1.0 / L) ** 0.5 if has_text else 0.0
+        call("vdn_sana_factor", ws.A.data_ptr(), ws.B.data_ptr(), F_inv, H, D, 1.0 / tpf,
+             None if tensor_cores else ws.inv.data_ptr(), split, text_frame, text_inj, TEXT_STATE_SCALE,
+             _lib.ptr(s0), stream)
     else:
-        call("vdn_delta_factor", ws.A.data_ptr(), ws.B.data_ptr(), Fb, H, D, ws.inv.data_ptr(), ws.info.data_ptr(),
-             -1, 0.0, None, split, stream)
-        s0 = None
-    record_factor_status(ws.info)
+        inj_scale = 0.0
+        call("vdn_delta_factor", ws.A.data_ptr(), ws.B.data_ptr(), F_inv, H, D, ws.inv.data_ptr(), ws.info.data_ptr(),
+             text_frame, TEXT_STATE_SCALE if has_text else 0.0, _lib.ptr(s0), split, stream)
+        record_factor_status(ws.info)
     if tensor_cores:
-        call("vdn_bidir_scan_tc", split, ws.B.data_ptr(), ws.alpha.data_ptr(), _lib.ptr(s0), Fb, Fb + int(has_text), H,
+        call("vdn_bidir_scan_tc", split, ws.B.data_ptr(), ws.alpha.data_ptr(), _lib.ptr(s0), Fb, F_inv, H, inj_scale,
              ws.prefix.data_ptr(), ws.suffix.data_ptr(), status.err_ptr, stream)
     else:
         call("vdn_bidir_scan", ws.inv.data_ptr(), ws.B.data_ptr(), ws.alpha.data_ptr(), _lib.ptr(s0), Fb, H, D,
-             ws.prefix.data_ptr(), ws.suffix.data_ptr(), stream)
+             inj_scale, ws.prefix.data_ptr(), ws.suffix.data_ptr(), stream)
     # output gate: sigmoid(bf16(x W_down^T) W_up^T + b)  (branch.py:754-758)
     call("vdn_cast_rows", aux.data_ptr(), aux_ld, ogd_col0, rows, D, ws.ogd.data_ptr(), ws.ogd.stride(0), stream)
     lo, hi = ws.bounds_arrays(bounds)
@@ -270,7 +284,7 @@ class B200LinearBranch:
 
     def __init__(self, weights, num_heads, head_dim, delta_rule="vdn_solve", bridge="alpha", a_fp32=True,
                  short_conv=("k", "v"), enable_text_state=True, **_runtime):
-        if delta_rule not in ("vdn_solve", "sana_scaled"):
+        if delta_rule not in DELTA_RULES:
             raise ValueError(f"unknown delta rule: {delta_rule!r}")
         if bridge not in ("alpha", "none"):
             raise ValueError("bridge must be 'alpha' or 'none'")
@@ -313,8 +327,6 @@ class B200LinearBranch:
 
     def readout(self, weights, xv, q_raw, k_raw, v_raw, num_frames, tokens_per_frame, bounds, frame_size=None,
                 text_x=None, text_k_raw=None, text_v_raw=None, skip_ends=False, *, inference=False):
-        if self.delta_rule != "vdn_solve":
-            raise NotImplementedError("the B200 branch implements the released vdn_solve rule only")
         expected_rows = num_frames * tokens_per_frame
         if xv.ndim != 2 or xv.shape[0] != expected_rows:
             raise ValueError("xv rows must equal num_frames * tokens_per_frame")
@@ -365,7 +377,8 @@ class B200LinearBranch:
 
         kw = dict(q_raw=flat(q_raw[rows]), k_raw=flat(k_raw[rows]), v_raw=flat(v_raw[rows]), aux=aux, beta_col0=0,
                   ogd_col0=H, ad_col0=H + D, Fb=F_b, tpf=tokens_per_frame, frame_size=frame_size, bounds=bounds_b,
-                  bridge=self.bridge, out=out, out_row0=r0, status=st, short_conv=self.short_conv)
+                  bridge=self.bridge, out=out, out_row0=r0, status=st, short_conv=self.short_conv,
+                  delta_rule=self.delta_rule)
         if text:
             kw.update(text_k=flat(text_k_raw), text_v=flat(text_v_raw), text_aux=side(text_x))
         run_branch(ws, bw, **kw)
@@ -386,5 +399,5 @@ class B200LinearBranch:
         return projector(readout.to(xv.dtype))
 
 
-__all__ = ["B200LinearBranch", "BranchDeviceWeights", "BranchWorkspace", "TEXT_STATE_SCALE",
+__all__ = ["B200LinearBranch", "BranchDeviceWeights", "BranchWorkspace", "DELTA_RULES", "TEXT_STATE_SCALE",
            "cholesky_runtime_scope", "run_branch"]

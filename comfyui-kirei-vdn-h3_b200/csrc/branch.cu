@@ -564,6 +564,46 @@ __global__ void __launch_bounds__(256) text_state_kernel(const float* __restrict
     for (int j = 0; j < TB; ++j) s0[((long long)h * D + r0 + i) * D + c0 + j] = scale * acc[i][j];
 }
 
+// The sana_scaled transition factor M = I - A / L (branch.py:163-177; the scan applies the
+// alpha scaling and the injection B / sqrt(L) on the fly).  One 32 x 32 tile per CTA
+// (32 x 8 threads): M row-major into m_out (optional) and, for the tensor-core scan, M^T as
+// bf16 hi / lo halves (its B operand is read K-major, so element [n][k] must hold M[k][n]).
+// grid (D/32, D/32, F*H).
+__global__ void __launch_bounds__(256) sana_factor_kernel(const float* __restrict__ A, int D, float inv_tokens,
+                                                          float* __restrict__ m_out, __nv_bfloat16* __restrict__ split,
+                                                          long long lo_offset) {
+  __shared__ float tile[32][33];
+  const long long mb = (long long)blockIdx.z * D * D;
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = r0 + ty + 8 * k, c = c0 + tx;
+    const float m = (r == c ? 1.0f : 0.0f) - inv_tokens * A[mb + (long long)r * D + c];
+    tile[ty + 8 * k][tx] = m;
+    if (m_out) m_out[mb + (long long)r * D + c] = m;
+  }
+  if (!split) return;
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    // transposed element (n = c0 + ty + 8k, kk = r0 + tx) = M[r0 + tx][c0 + ty + 8k]
+    const float x = tile[tx][ty + 8 * k];
+    const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+    const long long e = mb + (long long)(c0 + ty + 8 * k) * D + r0 + tx;
+    split[e] = hi;
+    split[lo_offset + e] = __float2bfloat16_rn(x - __bfloat162float(hi));
+  }
+}
+
+// s0[h] = outer * (inner * B[text_frame, h]): the sana_scaled text state, rounded like the
+// reference's two fp32 products (injection, then TEXT_STATE_SCALE; branch.py:649-670).
+__global__ void scale_matrix_kernel(const float* __restrict__ Bm, long long n, float inner, float outer,
+                                    float* __restrict__ out) {
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x)
+    out[e] = outer * (inner * Bm[e]);
+}
+
 // ---------------------------------------------------------------------------------
 // 6. Bidirectional scan, state rows split across CTAs (the rows of s evolve independently).
 // grid (H, 2 directions, D / RB), 256 threads.  states out [F, H, D, D] fp32 (prefix, suffix).
@@ -571,7 +611,7 @@ __global__ void __launch_bounds__(256) text_state_kernel(const float* __restrict
 template <int D, int RB>
 __global__ void __launch_bounds__(256) bidir_scan_kernel(const float* __restrict__ inv, const float* __restrict__ Bm,
                                                          const float* __restrict__ alpha, const float* __restrict__ s0,
-                                                         int F, int H, float* __restrict__ prefix,
+                                                         int F, int H, float inj_scale, float* __restrict__ prefix,
                                                          float* __restrict__ suffix) {
   extern __shared__ float sm[];
   float* sinv = sm;             // [D][D]
@@ -591,9 +631,10 @@ __global__ void __launch_bounds__(256) bidir_scan_kernel(const float* __restrict
     for (int e = tid * 4; e < D * D; e += 256 * 4)
       *reinterpret_cast<float4*>(sinv + e) = *reinterpret_cast<const float4*>(inv + mb + e);
     const float* al = alpha + ((long long)t * H + h) * D;
+    const float* brow = Bm + mb + (long long)(r0 + r) * D + c0;
+    // vdn_solve: u = B + s o alpha, s = u inv;  sana_scaled: u = s o alpha, s = u M + scale B
 #pragma unroll
-    for (int o = 0; o < OUT; ++o)
-      u[r * D + c0 + o] = Bm[mb + (long long)(r0 + r) * D + c0 + o] + s[o] * al[c0 + o];
+    for (int o = 0; o < OUT; ++o) u[r * D + c0 + o] = inj_scale == 0.f ? brow[o] + s[o] * al[c0 + o] : s[o] * al[c0 + o];
     __syncthreads();
 #pragma unroll
     for (int o = 0; o < OUT; ++o) s[o] = 0.f;
@@ -601,6 +642,10 @@ __global__ void __launch_bounds__(256) bidir_scan_kernel(const float* __restrict
       const float ui = u[r * D + i];
 #pragma unroll
       for (int o = 0; o < OUT; ++o) s[o] += ui * sinv[i * D + c0 + o];
+    }
+    if (inj_scale != 0.f) {
+#pragma unroll
+      for (int o = 0; o < OUT; ++o) s[o] = fmaf(inj_scale, brow[o], s[o]);
     }
 #pragma unroll
     for (int o = 0; o < OUT; ++o) dst_all[mb + (long long)(r0 + r) * D + c0 + o] = s[o];
@@ -620,9 +665,10 @@ constexpr int kScanUPitch = 132;  // u_t row pitch (floats): 16-byte aligned, fe
 
 __global__ void __launch_bounds__(kScanThreads, 1)
     bidir_scan128_kernel(const float* __restrict__ inv, const float* __restrict__ Bm, const float* __restrict__ alpha,
-                         const float* __restrict__ s0, int F, int H, float* __restrict__ prefix,
+                         const float* __restrict__ s0, int F, int H, float inj_scale, float* __restrict__ prefix,
                          float* __restrict__ suffix) {
   constexpr int D = 128;
+  const bool sana = inj_scale != 0.f;  // u = s o alpha and s = u M + inj_scale B_t
   extern __shared__ __align__(16) float scan_smem[];
   float* sinv = scan_smem;              // [2][D][D]
   float* ut = scan_smem + 2 * D * D;    // [D][kScanUPitch]
@@ -673,10 +719,10 @@ __global__ void __launch_bounds__(kScanThreads, 1)
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float4 col;
-      col.x = fmaf(s[0][j], av[j], b[0][j]);
-      col.y = fmaf(s[1][j], av[j], b[1][j]);
-      col.z = fmaf(s[2][j], av[j], b[2][j]);
-      col.w = fmaf(s[3][j], av[j], b[3][j]);
+      col.x = fmaf(s[0][j], av[j], sana ? 0.f : b[0][j]);
+      col.y = fmaf(s[1][j], av[j], sana ? 0.f : b[1][j]);
+      col.z = fmaf(s[2][j], av[j], sana ? 0.f : b[2][j]);
+      col.w = fmaf(s[3][j], av[j], sana ? 0.f : b[3][j]);
       *reinterpret_cast<float4*>(ut + (c + j) * kScanUPitch + r) = col;
     }
     if (more) {
@@ -685,7 +731,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
       cp_async_wait<0>();
     }
     __syncthreads();
-    if (more) load_b(step + 1, b);  // in flight during the product
+    if (more && !sana) load_b(step + 1, b);  // in flight during the product
     float2 acc[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
@@ -715,12 +761,13 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     for (int i = 0; i < 4; ++i) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        s[i][2 * j] = acc[i][j].x;
-        s[i][2 * j + 1] = acc[i][j].y;
+        s[i][2 * j] = sana ? fmaf(inj_scale, b[i][2 * j], acc[i][j].x) : acc[i][j].x;
+        s[i][2 * j + 1] = sana ? fmaf(inj_scale, b[i][2 * j + 1], acc[i][j].y) : acc[i][j].y;
       }
       *reinterpret_cast<float4*>(dst + (r + i) * D + c) = make_float4(s[i][0], s[i][1], s[i][2], s[i][3]);
       *reinterpret_cast<float4*>(dst + (r + i) * D + c + 4) = make_float4(s[i][4], s[i][5], s[i][6], s[i][7]);
     }
+    if (more && sana) load_b(step + 1, b);  // B_t was needed after the product
     __syncthreads();  // u_t and this inverse buffer are rewritten next step
   }
 }
@@ -969,11 +1016,39 @@ int vdn_delta_factor(const float* A, const float* B, int F, int H, int D, float*
   return vdn::launch_status();
 }
 
+// 5b. sana_scaled factor (branch.py:163-177): M = I - inv_tokens * A for F frames, row-major
+// into M (optional) and transposed as bf16 hi / lo halves into M_split (head_dim 128, optional;
+// lo halves F*H*D*D elements after the hi halves, the layout vdn_bidir_scan_tc reads).  If
+// text_frame >= 0: s0 = text_scale * (text_inj_scale * B[text_frame]) (branch.py:649-670).
+int vdn_sana_factor(const float* A, const float* B, int F, int H, int D, float inv_tokens, float* M, void* M_split,
+                    int text_frame, float text_inj_scale, float text_scale, float* s0, void* stream) {
+  if (!A || F <= 0 || H <= 0 || (text_frame >= 0 && (!B || !s0)) || text_frame >= F) return vdn::kBadArgument;
+  if (D != 64 && D != 128) return vdn::kUnsupported;
+  if (M_split && (D != 128 || (reinterpret_cast<uintptr_t>(M_split) & 3))) return vdn::kBadArgument;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (M || M_split) {
+    const long long mats = (long long)F * H;
+    if (mats > 65535) return vdn::kUnsupported;  // grid z
+    sana_factor_kernel<<<dim3(D / 32, D / 32, (unsigned)mats), 256, 0, s>>>(
+        A, D, inv_tokens, M, reinterpret_cast<__nv_bfloat16*>(M_split), mats * D * D);
+    vdn::count_launch();
+  }
+  if (text_frame >= 0) {
+    const long long n = (long long)H * D * D;
+    scale_matrix_kernel<<<(unsigned)((n + 1023) / 1024), 256, 0, s>>>(B + (long long)text_frame * n, n,
+                                                                       text_inj_scale, text_scale, s0);
+    vdn::count_launch();
+  }
+  return vdn::launch_status();
+}
+
 // 6. Bidirectional scan (branch.py:297-312 with the factor applied on the fly).
-// inv, B: [F, H, D, D]; alpha [F, H, D]; s0 [H, D, D] or NULL (zero start).
+// inv, B: [F, H, D, D]; alpha [F, H, D]; s0 [H, D, D] or NULL (zero start).  inj_scale = 0:
+// vdn_solve, s_t = (B_t + s_{t-1} o alpha_t) inv_t;  inj_scale > 0: sana_scaled with inv = M,
+// s_t = (s_{t-1} o alpha_t) M_t + inj_scale B_t.
 int vdn_bidir_scan(const float* inv, const float* B, const float* alpha, const float* s0, int F, int H, int D,
-                   float* prefix, float* suffix, void* stream) {
-  if (!inv || !B || !alpha || !prefix || !suffix) return vdn::kBadArgument;
+                   float inj_scale, float* prefix, float* suffix, void* stream) {
+  if (!inv || !B || !alpha || !prefix || !suffix || inj_scale < 0.f) return vdn::kBadArgument;
   if (!vdn::aligned16(inv)) return vdn::kMisaligned;  // float4 loads of the inverse
   auto s = reinterpret_cast<cudaStream_t>(stream);
   constexpr int RB = 16;
@@ -987,12 +1062,13 @@ int vdn_bidir_scan(const float* inv, const float* B, const float* alpha, const f
       cudaFuncSetAttribute(bidir_scan128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       attr_set = true;
     }
-    bidir_scan128_kernel<<<dim3(H, 2), kScanThreads, smem, s>>>(inv, B, alpha, s0, F, H, prefix, suffix);
+    bidir_scan128_kernel<<<dim3(H, 2), kScanThreads, smem, s>>>(inv, B, alpha, s0, F, H, inj_scale, prefix,
+                                                                 suffix);
     vdn::count_launch();
   } else if (D == 64) {
     const size_t smem = (size_t)(64 * 64 + 2 * RB * 64) * sizeof(float);
-    bidir_scan_kernel<64, 2 * RB><<<dim3(H, 2, 64 / (2 * RB)), 256, smem, s>>>(inv, B, alpha, s0, F, H, prefix,
-                                                                               suffix);
+    bidir_scan_kernel<64, 2 * RB><<<dim3(H, 2, 64 / (2 * RB)), 256, smem, s>>>(inv, B, alpha, s0, F, H, inj_scale,
+                                                                               prefix, suffix);
     vdn::count_launch();
   } else {
     return vdn::kUnsupported;

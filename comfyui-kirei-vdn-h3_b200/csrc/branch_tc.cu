@@ -555,6 +555,10 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
 // operand, so the state carries ~1e-5 relative error per frame (it is rounded to bf16 for the
 // readout).  The inverse halves come from vdn_delta_factor; the next frame's are loaded by
 // TMA while the current frame is multiplied.
+// kSana (delta_rule "sana_scaled", branch.py:163-177): the matrix is M = I - A/L (halves from
+// vdn_sana_factor) and the injection is added after the product,
+//     u = s o alpha_t,   s = u M_t + inj_scale B_t,
+// so the B row a thread needs at step t is that of the frame whose product it reads back.
 // smem: 2 stages x (inv hi, inv lo) + (u hi, u lo) = 6 x 32 KB.
 struct ScanSmem {
   static constexpr int kInv = 0, kU = 4 * kTile, kBar = 6 * kTile;
@@ -562,10 +566,11 @@ struct ScanSmem {
 };
 constexpr int kScanThreads = 160;
 
+template <bool kSana>
 __global__ void __launch_bounds__(kScanThreads, 1)
     scan_tc_kernel(const __grid_constant__ CUtensorMap tinv, const float* __restrict__ Bm,
                    const float* __restrict__ alpha, const float* __restrict__ s0, int F, int F_inv, int H,
-                   float* __restrict__ prefix, float* __restrict__ suffix, int* err) {
+                   float inj_scale, float* __restrict__ prefix, float* __restrict__ suffix, int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + ScanSmem::kBar);
@@ -641,12 +646,14 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     bool ok = true;
     for (int step = 0; step < F && ok; ++step) {
       const int t = frame(step);
-      // this frame's B row does not depend on the previous state: it is in registers before
-      // the wait for the previous step's MMA, off the dependent chain of the recurrence
-      const float* brow = Bm + (((long long)t * H + h) * D + i) * D;
+      // this frame's B row (kSana: the previous frame's) does not depend on the previous state:
+      // it is in registers before the wait for the previous step's MMA, off the dependent
+      // chain of the recurrence
+      const float* brow = Bm + (((long long)(kSana ? frame(step > 0 ? step - 1 : 0) : t) * H + h) * D + i) * D;
       float4 bv[D / 4];
 #pragma unroll
-      for (int q = 0; q < D / 4; ++q) bv[q] = __ldg(reinterpret_cast<const float4*>(brow) + q);
+      for (int q = 0; q < D / 4; ++q)
+        bv[q] = (kSana && step == 0) ? make_float4(0.f, 0.f, 0.f, 0.f) : __ldg(reinterpret_cast<const float4*>(brow) + q);
       if (step + 1 < F) {  // the next frame's B row into L2 meanwhile
         const float* nb = Bm + (((long long)frame(step + 1) * H + h) * D + i) * D;
 #pragma unroll
@@ -671,6 +678,16 @@ __global__ void __launch_bounds__(kScanThreads, 1)
           tmem_ld_wait();
 #pragma unroll
           for (int q = 0; q < 32; ++q) sv[q] = __uint_as_float(r[q]);
+          if (kSana) {
+#pragma unroll
+            for (int q = 0; q < 32; q += 4) {
+              const float4 b4 = bv[(c * 32 + q) / 4];
+              sv[q] = fmaf(inj_scale, b4.x, sv[q]);
+              sv[q + 1] = fmaf(inj_scale, b4.y, sv[q + 1]);
+              sv[q + 2] = fmaf(inj_scale, b4.z, sv[q + 2]);
+              sv[q + 3] = fmaf(inj_scale, b4.w, sv[q + 3]);
+            }
+          }
 #pragma unroll
           for (int q = 0; q < 32; q += 4)
             *reinterpret_cast<float4*>(prev + c * 32 + q) = make_float4(sv[q], sv[q + 1], sv[q + 2], sv[q + 3]);
@@ -688,8 +705,8 @@ __global__ void __launch_bounds__(kScanThreads, 1)
           uint32_t hp[4], lp[4];
 #pragma unroll
           for (int e = 0; e < 8; e += 2) {
-            const float u0 = fmaf(sv[q8 * 8 + e], aa[e], bb[e]);
-            const float u1 = fmaf(sv[q8 * 8 + e + 1], aa[e + 1], bb[e + 1]);
+            const float u0 = kSana ? sv[q8 * 8 + e] * aa[e] : fmaf(sv[q8 * 8 + e], aa[e], bb[e]);
+            const float u1 = kSana ? sv[q8 * 8 + e + 1] * aa[e + 1] : fmaf(sv[q8 * 8 + e + 1], aa[e + 1], bb[e + 1]);
             const __nv_bfloat162 h2 = __floats2bfloat162_rn(u0, u1);
             const float2 hf = __bfloat1622float2(h2);
             hp[e / 2] = *reinterpret_cast<const uint32_t*>(&h2);
@@ -713,15 +730,23 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     if (ok && __all_sync(0xffffffffu, mbar_wait(smem_u32(mma_done), (F - 1) & 1, abort_flag, err, kErrWaitOther))) {
       tc_fence_after();
       float* last = dst_all + (((long long)frame(F - 1) * H + h) * D + i) * D;
+      const float* blast = Bm + (((long long)frame(F - 1) * H + h) * D + i) * D;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem + lane_base + c * 32, r);
         tmem_ld_wait();
 #pragma unroll
-        for (int q = 0; q < 32; q += 4)
-          *reinterpret_cast<float4*>(last + c * 32 + q) = make_float4(
-              __uint_as_float(r[q]), __uint_as_float(r[q + 1]), __uint_as_float(r[q + 2]), __uint_as_float(r[q + 3]));
+        for (int q = 0; q < 32; q += 4) {
+          float4 v = make_float4(__uint_as_float(r[q]), __uint_as_float(r[q + 1]), __uint_as_float(r[q + 2]),
+                                 __uint_as_float(r[q + 3]));
+          if (kSana) {
+            const float4 b4 = __ldg(reinterpret_cast<const float4*>(blast + c * 32 + q));
+            v = make_float4(fmaf(inj_scale, b4.x, v.x), fmaf(inj_scale, b4.y, v.y), fmaf(inj_scale, b4.z, v.z),
+                            fmaf(inj_scale, b4.w, v.w));
+          }
+          *reinterpret_cast<float4*>(last + c * 32 + q) = v;
+        }
       }
     }
   }
@@ -804,13 +829,15 @@ int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, cons
 
 // Bidirectional scan on tensor cores (head_dim 128): inv_split = the bf16 hi halves of the
 // F_inv inverses [F_inv, H, 128, 128] followed by the lo halves (vdn_delta_factor's
-// inv_split output); B [F_inv, H, 128, 128] fp32 (frames 0..F-1 used); alpha [F, H, 128];
-// s0 [H, 128, 128] or NULL; prefix/suffix [F, H, 128, 128] fp32.
-// Replaces branch.py:297-312 (run_scans_*), with T and Inj folded as in vdn_bidir_scan.
+// inv_split output, or vdn_sana_factor's M_split with inj_scale > 0); B [F_inv, H, 128, 128]
+// fp32 (frames 0..F-1 used); alpha [F, H, 128]; s0 [H, 128, 128] or NULL; prefix/suffix
+// [F, H, 128, 128] fp32.  Replaces branch.py:297-312 (run_scans_*), with T and Inj folded as
+// in vdn_bidir_scan.
 int vdn_bidir_scan_tc(const void* inv_split, const float* B, const float* alpha, const float* s0, int F, int F_inv,
-                      int H, float* prefix, float* suffix, int* dev_err, void* stream) {
+                      int H, float inj_scale, float* prefix, float* suffix, int* dev_err, void* stream) {
   using namespace vdn::branch_tc;
-  if (!inv_split || !B || !alpha || !prefix || !suffix || F <= 0 || F > F_inv || H <= 0) return vdn::kBadArgument;
+  if (!inv_split || !B || !alpha || !prefix || !suffix || F <= 0 || F > F_inv || H <= 0 || inj_scale < 0.f)
+    return vdn::kBadArgument;
   if (!vdn::aligned16(B) || !vdn::aligned16(alpha) || !vdn::aligned16(prefix) || !vdn::aligned16(suffix))
     return vdn::kMisaligned;  // float4 rows
   CUtensorMap tinv;
@@ -819,11 +846,13 @@ int vdn_bidir_scan_tc(const void* inv_split, const float* B, const float* alpha,
   if (rc) return rc;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(scan_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ScanSmem::kBytes);
+    cudaFuncSetAttribute(scan_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScanSmem::kBytes);
+    cudaFuncSetAttribute(scan_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScanSmem::kBytes);
     attr = true;
   }
-  scan_tc_kernel<<<dim3(H, 2), kScanThreads, ScanSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
-      tinv, B, alpha, s0, F, F_inv, H, prefix, suffix, dev_err);
+  auto kernel = inj_scale > 0.f ? scan_tc_kernel<true> : scan_tc_kernel<false>;
+  kernel<<<dim3(H, 2), kScanThreads, ScanSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
+      tinv, B, alpha, s0, F, F_inv, H, inj_scale, prefix, suffix, dev_err);
   vdn::count_launch();
   return vdn::launch_status();
 }

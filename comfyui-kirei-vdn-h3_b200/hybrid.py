@@ -32,7 +32,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from .branch import BranchDeviceWeights, BranchWorkspace, cholesky_runtime_scope, run_branch
+from .branch import DELTA_RULES, BranchDeviceWeights, BranchWorkspace, cholesky_runtime_scope, run_branch
 from .layout import VDNLayout, current_layout
 from .projection import KIND, QuantizedMatrix, quantize_rows_int8, quantize_tensor_fp8, quantize_weight
 from .shard import (HeadShard, RowExchange, concat_rows, default_shard, qkv_row_index, rank_major_out_weight,
@@ -136,7 +136,7 @@ class FusedBlock:
 
     def __init__(self, qkv_w, q_norm_w, k_norm_w, out_w, branch_w: Mapping, heads, dim, device, *,
                  precision="bf16", eps=1e-6, enable_gate=True, short_conv=("k", "v"), shard: HeadShard | None = None,
-                 workspaces: dict | None = None):
+                 workspaces: dict | None = None, delta_rule="vdn_solve"):
         dev = torch.device(device)
         H_all, D = int(heads), int(dim)
         inner_all = H_all * D
@@ -158,6 +158,9 @@ class FusedBlock:
         self.eps = float(eps)
         self.enable_gate = bool(enable_gate)
         self.short_conv = tuple(short_conv)
+        if delta_rule not in DELTA_RULES:
+            raise ValueError(f"unsupported delta_rule {delta_rule!r}")
+        self.delta_rule = delta_rule
         qkv_rows = qkv_row_index(H_all, D, hs)
 
         def f32(t):
@@ -448,6 +451,7 @@ class FusedBlock:
                       v_raw=qkv[rows, 2 * g.inner:], aux=aux[rows], beta_col0=self.col_beta, ogd_col0=self.col_ogd,
                       ad_col0=self.col_ad, Fb=Fb, tpf=tpf, frame_size=layout.frame_size, bounds=bounds_b,
                       bridge=bridge, out=ws["branch"], out_row0=r0, status=status, short_conv=self.short_conv,
+                      delta_rule=self.delta_rule,
                       q_ready=q_act is not None)
             if enable_text_state and layout.text_len > 0:
                 ts = slice(layout.text_start, layout.text_start + layout.text_len)
@@ -520,12 +524,16 @@ class B200State:
         fb = self.blocks.get(index)
         if fb is None:
             cfg = self.config
+            # the branch object's own rule (LinearBranch.delta_rule), else the node config's
+            # (nodes.py:106)
+            owner = self.branches[index] if index < len(self.branches) else None
+            rule = getattr(owner, "delta_rule", None) or cfg.get("delta_rule", "vdn_solve")
             fb = FusedBlock(_weight_of(attn.qkv_proj), _weight_of(attn.q_norm), _weight_of(attn.k_norm),
                             _weight_of(attn.out_proj), self.weight_maps[index], self.num_heads, self.head_dim,
                             device, precision=self.projection_precision, eps=float(getattr(attn.q_norm, "eps", 1e-6)),
                             enable_gate=bool(cfg.get("enable_softmax_gate", True)),
                             short_conv=tuple(cfg.get("short_conv", ("k", "v"))), shard=self.shard,
-                            workspaces=self.workspaces)
+                            workspaces=self.workspaces, delta_rule=rule)
             self.blocks[index] = fb
         return fb
 

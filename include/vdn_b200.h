@@ -161,18 +161,26 @@ int vdn_frame_stats_tc(const void* K, const void* V, int F, int H, int T, const 
 int vdn_delta_factor(const float* A, const float* B, int F, int H, int D, float* inv, int* info,
                      int text_frame, float text_scale, float* s0, void* inv_split, void* stream);
 
-/* prefix_t = (B_t + prefix_{t-1} diag(alpha_t)) inv_t (t up), suffix likewise (t down),
- * both from s0 (NULL = zero).  Replaces: branch.py:297-333 (run_scans_*),
- * runtime.py:118-150 (_run_scans_shared). */
+/* The sana_scaled factor: M = I - inv_tokens * A per frame, row-major into M (optional) and,
+ * for head_dim 128, transposed as bf16 hi / lo halves into M_split (optional; the operand of
+ * vdn_bidir_scan_tc).  text_frame >= 0: s0 = text_scale * (text_inj_scale * B[text_frame]).
+ * Replaces: branch.py:163-177 (SanaDelta.factor_apply), :649-670 (_text_state). */
+int vdn_sana_factor(const float* A, const float* B, int F, int H, int D, float inv_tokens, float* M, void* M_split,
+                    int text_frame, float text_inj_scale, float text_scale, float* s0, void* stream);
+
+/* inj_scale = 0 (vdn_solve): prefix_t = (B_t + prefix_{t-1} diag(alpha_t)) inv_t (t up),
+ * suffix likewise (t down), both from s0 (NULL = zero).  inj_scale > 0 (sana_scaled, inv = M):
+ * prefix_t = prefix_{t-1} diag(alpha_t) M_t + inj_scale B_t.  Replaces: branch.py:297-333
+ * (run_scans_*), runtime.py:118-150 (_run_scans_shared). */
 int vdn_bidir_scan(const float* inv, const float* B, const float* alpha, const float* s0, int F, int H, int D,
-                   float* prefix, float* suffix, void* stream);
+                   float inj_scale, float* prefix, float* suffix, void* stream);
 
 /* The same scan on tensor cores (head_dim 128): one CTA per (head, direction) keeps the state
  * in TMEM and multiplies by the inverse in three bf16 passes (hi*hi + hi*lo + lo*hi, fp32
  * accumulation).  inv_split from vdn_delta_factor over F_inv >= F frames; B [F_inv, H, 128, 128].
  * Replaces: branch.py:297-333 (run_scans_*). */
 int vdn_bidir_scan_tc(const void* inv_split, const float* B, const float* alpha, const float* s0, int F,
-                      int F_inv, int H, float* prefix, float* suffix, int* dev_err, void* stream);
+                      int F_inv, int H, float inj_scale, float* prefix, float* suffix, int* dev_err, void* stream);
 
 /* Gather with alpha bridge, readout Q S^T, RMSNorm over D, x output gate, into
  * out[out_row0 + f*T + s, h*D + v].  Replaces: branch.py:345-396 (gather_linear_state),

@@ -91,14 +91,32 @@ def test_block_quantised_projections_match_oracle(precision):
     assert rel_l2(got, exact) < (3e-2 if precision == "int8" else 8e-2)
 
 
-def test_block_d128_ragged_frames_matches_oracle():
+@pytest.mark.parametrize("delta_rule", ["vdn_solve", "sana_scaled"])
+def test_block_d128_ragged_frames_matches_oracle(delta_rule):
     c = dict(text=64, frames=7, grid=(9, 14), heads=2, dim=128, hidden=512)
     bw = vo.make_block(4, c["hidden"], c["heads"], c["dim"])
     lay_o = vo.config_layout(c)
     x = vo.make_x(4, lay_o.seq_len, c["hidden"])
-    got = _run_block(bw, _layout(c), c["heads"], c["dim"], x)
-    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig())
+    got = _run_block(bw, _layout(c), c["heads"], c["dim"], x,
+                     config={"enable_softmax_gate": True, "delta_rule": delta_rule})
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(delta_rule=delta_rule))
     assert rel_l2(got, want) < 2e-2
+
+
+def test_block_sana_rule_matches_oracle_and_golden():
+    """delta_rule="sana_scaled" from the node config (nodes.py:106) on config 0."""
+    c = vo.CONFIG0
+    bw = vo.make_block(0, c["hidden"], c["heads"], c["dim"])
+    lay_o = vo.config_layout(c)
+    x = vo.make_x(0, lay_o.seq_len, c["hidden"])
+    got = _run_block(bw, _layout(c), c["heads"], c["dim"], x,
+                     config={"enable_softmax_gate": True, "delta_rule": "sana_scaled"})
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(delta_rule="sana_scaled"))
+    assert rel_l2(got, want) < 2e-2
+    golden = dict(np.load(GOLDEN))
+    assert rel_l2(got, torch.from_numpy(golden["sana_block_out"])) < 2e-2
+    # and it is not the vdn_solve output
+    assert rel_l2(got, torch.from_numpy(golden["block_out"])) > 5e-2
 
 
 def test_repeated_forward_is_deterministic():

@@ -300,7 +300,7 @@ def test_statistics_factor_scan_match_oracle_and_report_non_spd():
     suffix = torch.empty_like(A)
     s0 = (torch.randn(H, D, D, generator=g) * 0.1)
     ad, s0d = alpha.to(DEV), s0.to(DEV)
-    pkg._lib.call("vdn_bidir_scan", inv.data_ptr(), B.data_ptr(), ad.data_ptr(), s0d.data_ptr(), Fb, H, D,
+    pkg._lib.call("vdn_bidir_scan", inv.data_ptr(), B.data_ptr(), ad.data_ptr(), s0d.data_ptr(), Fb, H, D, 0.0,
                   prefix.data_ptr(), suffix.data_ptr(), s)
     trans, inj = vo.factor_apply(alpha, wa, wb)
     wp, wsf = vo.run_scans(trans, inj, s0.double())
@@ -309,7 +309,7 @@ def test_statistics_factor_scan_match_oracle_and_report_non_spd():
     # hi + lo halves reproduce the inverse to ~2^-16, and the tensor-core scan matches
     assert rel_l2(split[0].float() + split[1].float(), want_inv) < 2e-5
     p_tc, s_tc = torch.empty_like(A), torch.empty_like(A)
-    pkg._lib.call("vdn_bidir_scan_tc", split.data_ptr(), B.data_ptr(), ad.data_ptr(), s0d.data_ptr(), Fb, Fb, H,
+    pkg._lib.call("vdn_bidir_scan_tc", split.data_ptr(), B.data_ptr(), ad.data_ptr(), s0d.data_ptr(), Fb, Fb, H, 0.0,
                   p_tc.data_ptr(), s_tc.data_ptr(), st.err_ptr, s)
     torch.cuda.synchronize()
     st.raise_if_failed()
@@ -326,8 +326,56 @@ def test_statistics_factor_scan_match_oracle_and_report_non_spd():
     assert int(info[2, 1]) == 1
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_sana_factor_and_scans_match_oracle(D):
+    """delta_rule="sana_scaled" (branch.py:163-177): M = I - A/L, s_t = s_{t-1} diag(alpha) M + B/sqrt(L),
+    through the SIMT scan and, at head_dim 128, the tensor-core scan; text state 0.5 B/sqrt(L_text)."""
+    Fb, H, T, L_text = 6, 3, 70, 11
+    g = torch.Generator().manual_seed(51)
+    kf = torch.nn.functional.normalize(torch.randn(Fb + 1, H, T, D, generator=g), dim=-1)
+    vf = torch.randn(Fb + 1, H, T, D, generator=g)
+    beta = torch.sigmoid(torch.randn(Fb + 1, H, T, generator=g))
+    alpha = torch.sigmoid(torch.randn(Fb, H, D, generator=g) + 2)
+    wa, wb = vo.frame_statistics(kf, vf, beta)  # the last frame stands in for the text frame
+    A, B = wa.float().to(DEV).contiguous(), wb.float().to(DEV).contiguous()
+    s = pkg._lib.stream_handle(DEV)
+    M = torch.empty_like(A)
+    split = torch.empty(2, Fb + 1, H, D, D, device=DEV, dtype=torch.bfloat16) if D == 128 else None
+    s0 = torch.empty(H, D, D, device=DEV)
+    pkg._lib.call("vdn_sana_factor", A.data_ptr(), B.data_ptr(), Fb + 1, H, D, 1.0 / T, M.data_ptr(),
+                  None if split is None else split.data_ptr(), Fb, (1.0 / L_text) ** 0.5, 0.5, s0.data_ptr(), s)
+    trans, inj = vo.sana_factor_apply(alpha, wa[:Fb], wb[:Fb], T)
+    _, t_inj = vo.sana_factor_apply(torch.ones(1, H, D), wa[Fb:], wb[Fb:], L_text)
+    want_s0 = 0.5 * t_inj[0]
+    eye = torch.eye(D, dtype=torch.float64)
+    torch.cuda.synchronize()
+    assert rel_l2(M[:Fb], eye - wa[:Fb] / T) < 1e-6
+    assert rel_l2(s0, want_s0) < 1e-6
+    wp, wsf = vo.run_scans(trans, inj, want_s0)
+    ad = alpha.to(DEV)
+    prefix, suffix = torch.empty(Fb, H, D, D, device=DEV), torch.empty(Fb, H, D, D, device=DEV)
+    pkg._lib.call("vdn_bidir_scan", M.data_ptr(), B.data_ptr(), ad.data_ptr(), s0.data_ptr(), Fb, H, D,
+                  (1.0 / T) ** 0.5, prefix.data_ptr(), suffix.data_ptr(), s)
+    torch.cuda.synchronize()
+    assert rel_l2(prefix, wp) < 1e-5 and rel_l2(suffix, wsf) < 1e-5
+    # the vdn_solve folding gives a different answer on the same buffers
+    assert rel_l2(prefix, vo.run_scans(*vo.factor_apply(alpha, wa[:Fb], wb[:Fb]), want_s0)[0]) > 1e-2
+    if D == 128:
+        # the split holds M^T: element [n][k] = M[k][n], hi + lo to ~2^-16
+        mt = (eye - wa / T).transpose(-1, -2)
+        assert rel_l2(split[0].float() + split[1].float(), mt) < 2e-5
+        st = pkg._lib.DeviceStatus(DEV)
+        p_tc, s_tc = torch.empty_like(prefix), torch.empty_like(prefix)
+        pkg._lib.call("vdn_bidir_scan_tc", split.data_ptr(), B.data_ptr(), ad.data_ptr(), s0.data_ptr(), Fb, Fb + 1,
+                      H, (1.0 / T) ** 0.5, p_tc.data_ptr(), s_tc.data_ptr(), st.err_ptr, s)
+        torch.cuda.synchronize()
+        st.raise_if_failed()
+        assert rel_l2(p_tc, wp) < 1e-4 and rel_l2(s_tc, wsf) < 1e-4
+
+
+@pytest.mark.parametrize("delta_rule", ["vdn_solve", "sana_scaled"])
 @pytest.mark.parametrize("D,grid", [(64, (4, 5)), (128, (10, 15))])
-def test_branch_readout_matches_oracle_with_and_without_text(D, grid):
+def test_branch_readout_matches_oracle_with_and_without_text(D, grid, delta_rule):
     H, hidden = 2, 96
     F = 8
     tpf = grid[0] * grid[1]
@@ -339,13 +387,14 @@ def test_branch_readout_matches_oracle_with_and_without_text(D, grid):
     tx = torch.randn(11, hidden, generator=g).to(torch.bfloat16)
     tk, tv = (torch.randn(11, H, D, generator=g).to(torch.bfloat16) for _ in range(2))
     bounds = vo.window_bounds(F, 1, 2)
-    br = pkg.B200LinearBranch(w, H, D)
+    br = pkg.B200LinearBranch(w, H, D, delta_rule=delta_rule)
     for text in (True, False):
         got = br.readout(w, xv.to(DEV), q.to(DEV), k.to(DEV), v.to(DEV), F, tpf, bounds, frame_size=grid,
                          text_x=tx.to(DEV) if text else None, text_k_raw=tk.to(DEV), text_v_raw=tv.to(DEV),
                          skip_ends=True)
         want, parts = vo.branch_readout(w, xv.float(), q.float(), k.float(), v.float(), F, tpf, bounds, grid, H, D,
-                                        vo.BranchConfig(), text_x=tx.float() if text else None, text_k=tk.float(),
+                                        vo.BranchConfig(delta_rule=delta_rule), text_x=tx.float() if text else None,
+                                        text_k=tk.float(),
                                         text_v=tv.float(), skip_ends=True, return_parts=True)
         ws = br.workspace(DEV, F - 2, tpf, 11 if text else 0)
         stages = {name: rel_l2(getattr(ws, attr), parts[name]) for name, attr in

@@ -221,6 +221,18 @@ def test_deferred_cholesky_scope_reports_factor_and_batch():
         bbr.record_factor_status(bad)
 
 
+def test_delta_rules_mirror_the_reference_and_unknown_rules_raise():
+    assert bbr.DELTA_RULES == ("vdn_solve", "sana_scaled")  # branch.py:180
+    w = vo.make_branch_weights(torch.Generator().manual_seed(0), 32, 2, 64)
+    assert pkg.B200LinearBranch(w, 2, 64, delta_rule="sana_scaled").delta_rule == "sana_scaled"
+    with pytest.raises(ValueError, match="delta rule"):
+        pkg.B200LinearBranch(w, 2, 64, delta_rule="gated_delta")
+    with pytest.raises(ValueError, match="delta rule"):
+        bbr.run_branch(None, None, q_raw=None, k_raw=None, v_raw=None, aux=None, beta_col0=0, ogd_col0=0,
+                       ad_col0=0, Fb=1, tpf=1, frame_size=(1, 1), bounds=[(0, 0)], bridge="alpha", out=None,
+                       out_row0=0, status=None, delta_rule="gated_delta")
+
+
 def test_status_codes_map_to_reference_exceptions():
     with pytest.raises(ValueError):
         pkg._lib.check(-1, "x")
