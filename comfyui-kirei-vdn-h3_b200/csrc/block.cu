@@ -182,6 +182,75 @@ __global__ void __launch_bounds__(THREADS) adaln_rmsnorm_row_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------------
+// Rotary position embedding on the normalised q / k heads, split-half pairing: for each
+// head slot and j < rot/2 the pair (x[j], x[j + rot/2]) becomes f[j] (x[j], x[j + rot/2])^T
+// with f[j] the token's 2 x 2 matrix in ComfyUI's freqs layout ([..., rot/2, 2, 2] =
+// [[cos, -sin], [sin, cos]]); features >= rot pass through.  In place, fp32 arithmetic, one
+// bf16 rounding.  One CTA per token row, the row's matrices staged in shared memory (every
+// head slot of the row reuses them); V pairs per thread step (8: 16-byte accesses).
+template <int V>
+__global__ void __launch_bounds__(256) rope_split_half_kernel(__nv_bfloat16* __restrict__ qk, long long ld, int slots,
+                                                              int D, int half, const float* __restrict__ freqs,
+                                                              long long ld_freqs) {
+  extern __shared__ float fm[];  // [half][2][2]
+  const long long row = blockIdx.x;
+  const float* fr = freqs + row * ld_freqs;
+  for (int e = threadIdx.x; e < half * 4; e += blockDim.x) fm[e] = fr[e];
+  __syncthreads();
+  const int groups = half / V;
+  __nv_bfloat16* base = qk + row * ld;
+  for (int v = threadIdx.x; v < slots * groups; v += blockDim.x) {
+    const int slot = v / groups, j0 = (v - slot * groups) * V;
+    __nv_bfloat16* p1 = base + (long long)slot * D + j0;
+    __nv_bfloat16* p2 = p1 + half;
+    float x1[V], x2[V];
+    if constexpr (V == 8) {
+      const uint4 a = *reinterpret_cast<const uint4*>(p1);
+      const uint4 b = *reinterpret_cast<const uint4*>(p2);
+      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 af = __bfloat1622float2(a2[i]), bf = __bfloat1622float2(b2[i]);
+        x1[2 * i] = af.x; x1[2 * i + 1] = af.y;
+        x2[2 * i] = bf.x; x2[2 * i + 1] = bf.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        x1[i] = __bfloat162float(p1[i]);
+        x2[i] = __bfloat162float(p2[i]);
+      }
+    }
+    float o1[V], o2[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float4 f = *reinterpret_cast<const float4*>(fm + 4 * (j0 + i));
+      o1[i] = fmaf(f.y, x2[i], f.x * x1[i]);
+      o2[i] = fmaf(f.w, x2[i], f.z * x1[i]);
+    }
+    if constexpr (V == 8) {
+      uint4 a, b;
+      uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
+      uint32_t* bw = reinterpret_cast<uint32_t*>(&b);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        aw[i] = pack_bf16(o1[2 * i], o1[2 * i + 1]);
+        bw[i] = pack_bf16(o2[2 * i], o2[2 * i + 1]);
+      }
+      *reinterpret_cast<uint4*>(p1) = a;
+      *reinterpret_cast<uint4*>(p2) = b;
+    } else {
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        p1[i] = __float2bfloat16_rn(o1[i]);
+        p2[i] = __float2bfloat16_rn(o2[i]);
+      }
+    }
+  }
+}
+
 }  // namespace block
 }  // namespace vdn
 
@@ -236,6 +305,32 @@ int vdn_adaln_rmsnorm(const void* x, long long ldx, int rows, int hidden, const 
       reinterpret_cast<const __nv_bfloat16*>(x), ldx, rows, hidden, norm_w, eps,
       reinterpret_cast<const __nv_bfloat16*>(scale_tab), reinterpret_cast<const __nv_bfloat16*>(shift_tab), ld_tab,
       row_group, reinterpret_cast<__nv_bfloat16*>(out), ldo, reinterpret_cast<int8_t*>(q), ldq, q_scale);
+  vdn::count_launch();
+  return vdn::launch_status();
+}
+
+// RoPE, split-half pairing, in place on `slots` consecutive heads of D bf16 features per
+// row (q heads then k heads of the normalised projection): qk [rows, ld] bf16; freqs fp32
+// [rows, rot/2, 2, 2] with row stride ld_freqs (0: one set of matrices for every row).
+// rot even, 2 <= rot <= D.  Replaces the RoPE half of comfy-kitchen's
+// rms_rope_split_half_(q, k, freqs, ..., rot_dim = 2 * freqs.shape[-3]) (hybrid.py:271-292).
+int vdn_rope_split_half(void* qk, long long ld, int rows, int slots, int D, int rot, const float* freqs,
+                        long long ld_freqs, void* stream) {
+  using namespace vdn::block;
+  if (!qk || !freqs || rows < 0 || slots <= 0 || D <= 0 || rot < 2 || rot > D || (rot & 1) || ld < (long long)slots * D ||
+      ld_freqs < 0)
+    return vdn::kBadArgument;
+  if (rows == 0) return 0;
+  const int half = rot / 2;
+  const size_t smem = (size_t)half * 4 * sizeof(float);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  const bool vec = half % 8 == 0 && D % 8 == 0 && ld % 8 == 0 && vdn::aligned16(qk);
+  if (vec)
+    rope_split_half_kernel<8><<<rows, 256, smem, s>>>(reinterpret_cast<__nv_bfloat16*>(qk), ld, slots, D, half, freqs,
+                                                      ld_freqs);
+  else
+    rope_split_half_kernel<1><<<rows, 256, smem, s>>>(reinterpret_cast<__nv_bfloat16*>(qk), ld, slots, D, half, freqs,
+                                                      ld_freqs);
   vdn::count_launch();
   return vdn::launch_status();
 }

@@ -29,7 +29,7 @@ from collections import OrderedDict
 import torch
 
 from . import _lib
-from .hybrid import STREAM_IO_KEY, B200State, FusedBlock, GatedResidual, StreamIO, _weight_of, gemm_block
+from .hybrid import STREAM_IO_KEY, B200State, FusedBlock, GatedResidual, StreamIO, _weight_of, gemm_block, rope_table
 from .layout import current_layout
 from .projection import QuantizedMatrix, quantize_weight
 
@@ -291,8 +291,6 @@ def make_fast_block_forward(block, state: B200State, block_index: int):
         if attention is not None or layout is None:
             return original_forward(x, t_emb, mod_segments, rope_freqs,
                                     transformer_options=transformer_options or {}, attention=attention)
-        if rope_freqs is not None:
-            raise NotImplementedError("RoPE is not implemented on the B200 path (rope_freqs must be None)")
         if int(x.shape[0]) != layout.seq_len:
             raise RuntimeError(f"VDN layout has {layout.seq_len} rows but the block received {x.shape[0]}")
         _lib.require_cuda(x)
@@ -304,7 +302,8 @@ def make_fast_block_forward(block, state: B200State, block_index: int):
                          io=(transformer_options or {}).get(STREAM_IO_KEY),
                          linear_enabled=bool(config.get("linear_enabled", True)),
                          bridge=str(config.get("bridge", "alpha")),
-                         enable_text_state=bool(config.get("enable_text_state", True)))
+                         enable_text_state=bool(config.get("enable_text_state", True)),
+                         rope=rope_table(rope_freqs, layout.seq_len, state.head_dim, x.device))
         return out.to(x.dtype)
 
     forward._vdn_h3_fast_block = True

@@ -51,6 +51,44 @@ def _weight_of(module_or_tensor):
 
 
 @dataclass
+class RopeTable:
+    """``rope_freqs`` in the form the RoPE kernel reads: fp32 [rows or 1, rot/2 * 4] on the
+    device, ``ld`` floats between rows (0: one set of matrices for every row)."""
+
+    freqs: torch.Tensor
+    rot: int
+    ld: int
+
+
+def rope_table(rope_freqs, seq: int, head_dim: int, device) -> RopeTable | None:
+    """Canonical device form of the ``rope_freqs`` a block receives (hybrid.py:271-292 reads
+    rot_dim = 2 * rope_freqs.shape[-3]; the trailing [rot/2, 2, 2] are ComfyUI's per-pair
+    rotation matrices).  Leading dimensions must broadcast over the heads: after dropping
+    size-1 dimensions they are empty (one table for all rows) or [seq]."""
+    if rope_freqs is None:
+        return None
+    f = rope_freqs
+    if not isinstance(f, torch.Tensor):
+        raise TypeError(f"rope_freqs must be a tensor, got {type(f).__name__}")
+    if f.ndim < 3 or tuple(f.shape[-2:]) != (2, 2):
+        raise ValueError(f"rope_freqs must end in [rot/2, 2, 2], got {tuple(f.shape)}")
+    half = int(f.shape[-3])
+    rot = 2 * half
+    if half < 1 or rot > head_dim:
+        raise ValueError(f"rope rot_dim {rot} must be in [2, head_dim={head_dim}]")
+    lead = [int(d) for d in f.shape[:-3] if d != 1]
+    if not lead:
+        n = 1
+    elif lead == [seq]:
+        n = seq
+    else:
+        raise ValueError(f"rope_freqs leading dims {tuple(f.shape[:-3])} must be one table or one per row "
+                         f"({seq} rows), broadcast over heads")
+    f = f.detach().to(device=device, dtype=torch.float32).reshape(n, half * 4).contiguous()
+    return RopeTable(f, rot, 0 if n == 1 else half * 4)
+
+
+@dataclass
 class GatedResidual:
     """``x + gate[group[row]] * y`` fused into the projection that makes y (the DiT block's
     post-branch residual, block_kernels.py:92-93): x [S, hidden] bf16, gate [groups, hidden]
@@ -386,13 +424,15 @@ class FusedBlock:
 
     def forward(self, x: torch.Tensor, layout: VDNLayout, plans: WindowPlanCache, status: _lib.DeviceStatus,
                 *, linear_enabled=True, bridge="alpha", enable_text_state=True, out=None,
-                residual: GatedResidual | None = None, row_epilogue=None, io: StreamIO | None = None) -> torch.Tensor:
+                residual: GatedResidual | None = None, row_epilogue=None, io: StreamIO | None = None,
+                rope: RopeTable | None = None) -> torch.Tensor:
         """The block output [S, hidden]; with ``residual`` the gated residual stream
         ``residual.x + gate * block(x)`` instead, and ``row_epilogue(rows_view, row0, n)``
         run on the projected rows (in place) before they leave this GPU.  ``io``: x arrives
-        and the output leaves by row blocks (see :class:`StreamIO`)."""
+        and the output leaves by row blocks (see :class:`StreamIO`).  ``rope``: rotary
+        embedding of the normalised q / k (``rope_table``)."""
         ws, linear_active = self.forward_heads(x, layout, plans, status, linear_enabled=linear_enabled,
-                                               bridge=bridge, enable_text_state=enable_text_state, io=io)
+                                               bridge=bridge, enable_text_state=enable_text_state, io=io, rope=rope)
         stream = _lib.stream_handle(x.device)
         if self.shard is not None:
             full = self._out_sharded(ws, linear_active, status, stream, residual, row_epilogue)
@@ -413,7 +453,8 @@ class FusedBlock:
         return out
 
     def forward_heads(self, x: torch.Tensor, layout: VDNLayout, plans: WindowPlanCache, status: _lib.DeviceStatus,
-                      *, linear_enabled=True, bridge="alpha", enable_text_state=True, io: StreamIO | None = None):
+                      *, linear_enabled=True, bridge="alpha", enable_text_state=True, io: StreamIO | None = None,
+                      rope: RopeTable | None = None):
         """Phases 1-3 (QKV, branch, window attention) for this rank's heads; returns the
         workspace holding the per-head outputs and whether the branch ran."""
         g = self.geo
@@ -464,6 +505,10 @@ class FusedBlock:
             plan = plans.get(S, layout.video_start, layout.video_end, layout.num_frames, layout.tokens_per_frame,
                              layout.bounds, layout.anchor_frames)
         qkn, qkv = ws["qkn"], ws["qkv"]
+        if rope is not None:
+            # after the q / k RMSNorm of the QKV epilogue; the branch read the raw projections
+            _lib.call("vdn_rope_split_half", qkn.data_ptr(), qkn.stride(0), S, 2 * g.heads, g.dim, rope.rot,
+                      rope.freqs.data_ptr(), rope.ld, stream)
         launch_window_attention(qkn[:, :g.inner], qkn[:, g.inner:], qkv[:, 2 * g.inner:], ws["flat"], plan, g.heads,
                                 g.dim, g.dim ** -0.5, status,
                                 gate_logits=ws["aux"] if self.enable_gate else None, gate_col0=self.col_gate,
@@ -558,16 +603,15 @@ def make_vdn_forward(attn, state: B200State, block_index: int):
             return original_forward(x, rope_freqs=rope_freqs, transformer_options=transformer_options or {})
         if int(x.shape[0]) != layout.seq_len:
             raise RuntimeError(f"VDN layout has {layout.seq_len} rows but attention received {x.shape[0]}")
-        if rope_freqs is not None:
-            raise NotImplementedError("RoPE is not implemented on the B200 path (rope_freqs must be None)")
         _lib.require_cuda(x)
+        rope = rope_table(rope_freqs, layout.seq_len, head_dim, x.device)
         status = state.device_status(x.device)
         block = state.fused_block(attn, block_index, x.device)
         out = block.forward(x, layout, state.window_plans, status,
                             linear_enabled=bool(config.get("linear_enabled", True)),
                             bridge=str(config.get("bridge", "alpha")),
                             enable_text_state=bool(config.get("enable_text_state", True)),
-                            io=(transformer_options or {}).get(STREAM_IO_KEY))
+                            io=(transformer_options or {}).get(STREAM_IO_KEY), rope=rope)
         state.last_attention_backend = "b200_dense" if layout.full_cover else "b200"
         return out.to(x.dtype)
 
@@ -586,4 +630,4 @@ def run_forward_checked(state: B200State, fn, *args, **kwargs):
     return result
 
 
-__all__ = ["B200State", "FusedBlock", "make_vdn_forward", "run_forward_checked"]
+__all__ = ["B200State", "FusedBlock", "RopeTable", "make_vdn_forward", "rope_table", "run_forward_checked"]

@@ -203,6 +203,15 @@ int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, cons
 int vdn_cast_rows(const float* in, long long ld_in, int col0, int rows, int cols, void* out, long long ld_out,
                   void* stream);
 
+/* Rotary position embedding, split-half pairing, in place on `slots` consecutive heads of D
+ * bf16 features per row (the normalised q heads then k heads): for j < rot/2 the pair
+ * (x[j], x[j + rot/2]) becomes f[row, j] (x[j], x[j + rot/2])^T, f fp32 [rows, rot/2, 2, 2]
+ * (ComfyUI's freqs layout [[cos, -sin], [sin, cos]]) with row stride ld_freqs (0: shared by
+ * every row); features >= rot unchanged.  rot even, rot <= D.
+ * Replaces: the RoPE half of ck.rms_rope_split_half_ (hybrid.py:271-292). */
+int vdn_rope_split_half(void* qk, long long ld, int rows, int slots, int D, int rot, const float* freqs,
+                        long long ld_freqs, void* stream);
+
 /* ---------------------------------------------------------------- DiT block -------- */
 
 /* Per-row int8 of bf16 rows whose max |x| per row is already in amax [rows] (e.g. from

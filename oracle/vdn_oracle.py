@@ -14,6 +14,9 @@ reference's fp32 CPU path and bf16 GPU path alike.
 Pinning: ``tests/golden/make_golden.py`` runs the reference itself (its own torch code,
 imported read-only where it is mounted) on seeded config-0 inputs and stores the outputs
 under ``tests/golden/``; ``tests/test_oracle_golden.py`` checks this module against them.
+Parity unpinned for RoPE (``rope_split_half``): the reference hands it to comfy-kitchen's
+``rms_rope_split_half_``, which is absent from the reference tree and this image; the
+restatement follows ComfyUI's published freqs convention (see the function).
 """
 
 from __future__ import annotations
@@ -309,6 +312,36 @@ def gather_linear_state(prefix, suffix, alpha, bounds, bridge="alpha", text_stat
     return torch.stack(out)
 
 
+def rope_split_half(x, freqs) -> torch.Tensor:
+    """RoPE on [S, H, D] heads, split-half pairing (hybrid.py:271-292 calls comfy-kitchen's
+    ``rms_rope_split_half_`` with rot_dim = 2 * freqs.shape[-3]).  PARITY UNPINNED: that
+    library is absent, so this restates ComfyUI's freqs convention: freqs [S, rot/2, 2, 2]
+    holds per token and pair index j the matrix [[cos, -sin], [sin, cos]] applied as
+    out_a = sum_b f[j, a, b] pair_b (comfy/ldm/flux/math.py apply_rope1), with the pair
+    (x[j], x[j + rot/2]) instead of the interleaved (x[2j], x[2j + 1]); features >= rot pass
+    through."""
+    x, f = _t(x), _t(freqs)
+    half = f.shape[-3]
+    rot = 2 * half
+    f = f.reshape(-1, 1, half, 2, 2)  # [S or 1, heads broadcast, half, 2, 2]
+    a, b = x[..., :half], x[..., half:rot]
+    out = x.clone()
+    out[..., :half] = f[..., 0, 0] * a + f[..., 0, 1] * b
+    out[..., half:rot] = f[..., 1, 0] * a + f[..., 1, 1] * b
+    return out
+
+
+def make_rope_freqs(seq, rot, *, theta=10000.0, offset=0) -> torch.Tensor:
+    """Deterministic synthetic RoPE table [seq, rot/2, 2, 2] (fp32) of 1-D positions
+    offset..offset+seq-1 with the usual theta^(-2j/rot) frequencies (the layout ComfyUI's
+    ``rope()`` returns, comfy/ldm/flux/math.py)."""
+    pos = torch.arange(offset, offset + seq, dtype=torch.float64)
+    omega = 1.0 / theta ** (torch.arange(0, rot, 2, dtype=torch.float64) / rot)
+    ang = pos[:, None] * omega[None]
+    c, s = torch.cos(ang), torch.sin(ang)
+    return torch.stack([torch.stack([c, -s], -1), torch.stack([s, c], -1)], -2).float()
+
+
 def rms_norm(x, weight, eps=1e-6) -> torch.Tensor:
     """x * rsqrt(mean(x^2) + eps) * weight over the last dim (branch.py:494-498)."""
     x = _t(x)
@@ -478,7 +511,7 @@ class BlockWeights:
 
 def block_forward(x, bw: BlockWeights, lay: Layout, heads, dim, cfg: BranchConfig,
                   *, enable_softmax_gate=True, linear_enabled=True, precision="bf16",
-                  return_parts=False):
+                  return_parts=False, rope_freqs=None):
     """VDN hybrid block forward: QKV, branch on raw video q/k/v, q/k RMSNorm, window
     softmax, per-token head gate, out_proj, delta add on video rows (hybrid.py:409-579).
 
@@ -510,6 +543,8 @@ def block_forward(x, bw: BlockWeights, lay: Layout, heads, dim, cfg: BranchConfi
         parts["readout"] = readout
     qn = rms_norm(q_raw, bw.q_norm, 1e-6)
     kn = rms_norm(k_raw, bw.k_norm, 1e-6)
+    if rope_freqs is not None:  # after the norm, softmax path only (the branch read q_raw)
+        qn, kn = rope_split_half(qn, rope_freqs), rope_split_half(kn, rope_freqs)
     scale = dim ** -0.5
     if lay.full_cover:
         soft = window_attention(qn, kn, v, 0, seq, 1, seq, [(0, 0)], scale, "none")
@@ -697,14 +732,14 @@ def dit_mlp(h, dw: DiTWeights, activation="swiglu", precision="bf16"):
 
 
 def dit_block_forward(x, dw: DiTWeights, mods, idx, lay: Layout, heads, dim, cfg: BranchConfig, *,
-                      activation="swiglu", precision="bf16", mlp_precision=None):
+                      activation="swiglu", precision="bf16", mlp_precision=None, rope_freqs=None):
     """The fused DiT block forward of block_kernels.py:149-240: pre-norm + AdaLN, hybrid
     attention, gated residual, pre-norm + AdaLN, MLP, gated residual.  ``mods`` are the six
     adaln_proj outputs [rows of modulation, hidden] in MOD_NAMES order."""
     shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = mods
     x = _t(x)
     h = dit_pre(x, dw.norm1, dw.eps, scale_msa, shift_msa, idx)
-    attn_out = block_forward(h, dw.attn, lay, heads, dim, cfg, precision=precision)
+    attn_out = block_forward(h, dw.attn, lay, heads, dim, cfg, precision=precision, rope_freqs=rope_freqs)
     x = dit_post(x, gate_msa, idx, attn_out)
     h = dit_pre(x, dw.norm2, dw.eps, scale_mlp, shift_mlp, idx)
     return dit_post(x, gate_mlp, idx, dit_mlp(h, dw, activation, mlp_precision or precision))

@@ -103,6 +103,26 @@ def test_block_d128_ragged_frames_matches_oracle(delta_rule):
     assert rel_l2(got, want) < 2e-2
 
 
+def test_block_with_rope_matches_oracle():
+    """rope_freqs in ComfyUI's [1, S, 1, rot/2, 2, 2] form through the drop-in operator (RoPE
+    parity unpinned: restated, not checked against comfy-kitchen)."""
+    c = dict(text=64, frames=7, grid=(9, 14), heads=2, dim=128, hidden=512)
+    bw = vo.make_block(4, c["hidden"], c["heads"], c["dim"])
+    lay_o = vo.config_layout(c)
+    x = vo.make_x(4, lay_o.seq_len, c["hidden"])
+    freqs = vo.make_rope_freqs(lay_o.seq_len, 128)
+    state = pkg.B200State("t", {"enable_softmax_gate": True}, [bw.branch], c["heads"], c["dim"])
+    fwd = pkg.make_vdn_forward(_Attn(bw, c["heads"], c["dim"]), state, 0)
+    rope = freqs.reshape(1, lay_o.seq_len, 1, 64, 2, 2).to(DEV)
+    with pkg.publish_layout(_layout(c)):
+        got = pkg.run_forward_checked(state, fwd, x.to(DEV, torch.bfloat16), rope)
+    torch.cuda.synchronize()
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(), rope_freqs=freqs)
+    plain = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig())
+    assert rel_l2(got, want) < 2e-2
+    assert rel_l2(want, plain) > 5e-2  # the rotation matters on this input
+
+
 def test_block_sana_rule_matches_oracle_and_golden():
     """delta_rule="sana_scaled" from the node config (nodes.py:106) on config 0."""
     c = vo.CONFIG0

@@ -226,16 +226,18 @@ def test_fast_block_forward_is_a_drop_in():
     x = vo.make_x(11, lay_o.seq_len, hidden).to(torch.bfloat16)
     t_emb = torch.tensor(1.0, device=DEV, dtype=torch.bfloat16)
     segs = _segments(lay_o)
+    freqs = vo.make_rope_freqs(lay_o.seq_len, D)  # RoPE on the attention's q / k (parity unpinned)
     with pkg.publish_layout(lay):
-        got = pkg.run_forward_checked(state, fwd, x.to(DEV), t_emb, segs, None)
+        got = pkg.run_forward_checked(state, fwd, x.to(DEV), t_emb, segs, freqs.to(DEV))
         # an attention override runs the block's own forward, as in the reference
         fwd(x.to(DEV), t_emb, segs, None, attention="native")
     assert blk.calls == ["native"]
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(TypeError):
         with pkg.publish_layout(lay):
             fwd(x.to(DEV), t_emb, segs, object())
     idx = vo.segment_rows(segs, lay_o.seq_len)
-    want = vo.dit_block_forward(x.double(), dw, [m.double() for m in mods], idx, lay_o, H, D, vo.BranchConfig())
+    want = vo.dit_block_forward(x.double(), dw, [m.double() for m in mods], idx, lay_o, H, D, vo.BranchConfig(),
+                                rope_freqs=freqs)
     assert rel_l2(got, want) < 2e-2
 
 

@@ -326,6 +326,29 @@ def test_statistics_factor_scan_match_oracle_and_report_non_spd():
     assert int(info[2, 1]) == 1
 
 
+@pytest.mark.parametrize("D,rot,shared", [(128, 128, False), (128, 64, True), (64, 12, False)])
+def test_rope_split_half_matches_oracle(D, rot, shared):
+    """In-place RoPE on q and k heads (16-byte path for rot % 16 == 0, scalar path otherwise;
+    one table per row or one for all rows): within one bf16 rounding of the float64 oracle."""
+    S, H = 300, 3
+    g = torch.Generator().manual_seed(52)
+    qk = torch.randn(S, 2 * H * D + 16, generator=g).to(torch.bfloat16)  # padded pitch
+    freqs = vo.make_rope_freqs(1 if shared else S, rot, offset=7)
+    dev_qk = qk.to(DEV)
+    fd = freqs.to(DEV).reshape(freqs.shape[0], -1).contiguous()
+    pkg._lib.call("vdn_rope_split_half", dev_qk.data_ptr(), dev_qk.stride(0), S, 2 * H, D, rot, fd.data_ptr(),
+                  0 if shared else fd.stride(0), pkg._lib.stream_handle(DEV))
+    heads = qk[:, :2 * H * D].double().reshape(S, 2 * H, D)
+    want = vo.rope_split_half(heads, freqs.expand(S, -1, -1, -1) if shared else freqs)
+    torch.cuda.synchronize()
+    got = dev_qk.cpu()
+    assert torch.equal(got[:, 2 * H * D:], qk[:, 2 * H * D:])  # the pitch padding is untouched
+    got = got[:, :2 * H * D].double().reshape(S, 2 * H, D)
+    assert torch.equal(got[..., rot:], heads[..., rot:])  # features past rot_dim pass through
+    err = (got - want).abs()
+    assert float((err - 2 ** -8 * want.abs()).max()) <= 1e-6  # one bf16 rounding (half an ulp, with slack)
+
+
 @pytest.mark.parametrize("D", [64, 128])
 def test_sana_factor_and_scans_match_oracle(D):
     """delta_rule="sana_scaled" (branch.py:163-177): M = I - A/L, s_t = s_{t-1} diag(alpha) M + B/sqrt(L),

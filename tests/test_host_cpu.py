@@ -233,6 +233,39 @@ def test_delta_rules_mirror_the_reference_and_unknown_rules_raise():
                        out_row0=0, status=None, delta_rule="gated_delta")
 
 
+def test_rope_table_accepts_comfy_shapes_and_rejects_others():
+    S, D = 10, 64
+    f = vo.make_rope_freqs(S, 32)
+    t = pkg.rope_table(f.reshape(1, S, 1, 16, 2, 2), S, D, "cpu")
+    assert t.rot == 32 and t.ld == 64 and t.freqs.shape == (S, 64) and t.freqs.dtype == torch.float32
+    assert torch.equal(t.freqs.reshape(S, 16, 2, 2), f)
+    shared = pkg.rope_table(f[:1].reshape(1, 1, 16, 2, 2), S, D, "cpu")
+    assert shared.ld == 0 and shared.freqs.shape == (1, 64)
+    assert pkg.rope_table(None, S, D, "cpu") is None
+    with pytest.raises(ValueError, match="2, 2"):
+        pkg.rope_table(torch.zeros(S, 16, 4), S, D, "cpu")
+    with pytest.raises(ValueError, match="rot_dim"):
+        pkg.rope_table(vo.make_rope_freqs(S, 128), S, D, "cpu")
+    with pytest.raises(ValueError, match="one per row"):
+        pkg.rope_table(torch.zeros(1, S, 3, 16, 2, 2), S, D, "cpu")  # per-head tables
+
+
+def test_oracle_rope_is_comfy_rotation_on_split_halves():
+    """Split-half RoPE equals ComfyUI's interleaved rotation applied to the features
+    reordered (j, j + rot/2) -> (2j, 2j + 1), keeps pair norms and leaves features past rot."""
+    S, H, D, rot = 6, 2, 16, 12
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(S, H, D, generator=g, dtype=torch.float64)
+    f = vo.make_rope_freqs(S, rot, offset=3).double()
+    got = vo.rope_split_half(x, f)
+    half = rot // 2
+    inter = torch.stack([x[..., :half], x[..., half:rot]], -1)  # [S, H, half, 2]
+    rotated = (f[:, None] * inter[..., None, :]).sum(-1)  # out_a = sum_b f[a, b] pair_b
+    assert torch.allclose(got[..., :half], rotated[..., 0]) and torch.allclose(got[..., half:rot], rotated[..., 1])
+    assert torch.equal(got[..., rot:], x[..., rot:])
+    assert torch.allclose(got[..., :half] ** 2 + got[..., half:rot] ** 2, x[..., :half] ** 2 + x[..., half:rot] ** 2)
+
+
 def test_status_codes_map_to_reference_exceptions():
     with pytest.raises(ValueError):
         pkg._lib.check(-1, "x")
