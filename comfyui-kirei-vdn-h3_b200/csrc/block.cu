@@ -187,9 +187,59 @@ __global__ void __launch_bounds__(THREADS) adaln_rmsnorm_row_kernel(
 // head slot and j < rot/2 the pair (x[j], x[j + rot/2]) becomes f[j] (x[j], x[j + rot/2])^T
 // with f[j] the token's 2 x 2 matrix in ComfyUI's freqs layout ([..., rot/2, 2, 2] =
 // [[cos, -sin], [sin, cos]]); features >= rot pass through.  In place, fp32 arithmetic, one
-// bf16 rounding.  One CTA per token row, the row's matrices staged in shared memory (every
-// head slot of the row reuses them); V pairs per thread step (8: 16-byte accesses).
-template <int V>
+// bf16 rounding.
+//
+// Vector path (rot % 16 == 0): one warp per token row, 8 rows per CTA; lane l takes the
+// 16-byte groups v = l, l + 32, ... of the row's slots x G groups of 8 pairs (G = rot / 16).
+// When G divides 32 a lane's pair group is the same for every v, so its 8 matrices are
+// read once per row into registers (L1 serves the lanes sharing them).
+template <bool kFixedGroup>
+__global__ void __launch_bounds__(256) rope_split_half_vec_kernel(__nv_bfloat16* __restrict__ qk, long long ld,
+                                                                  int rows, int slots, int D, int half,
+                                                                  const float* __restrict__ freqs, long long ld_freqs) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * 8 + warp;
+  if (row >= rows) return;
+  const int G = half / 8;
+  const float4* fr = reinterpret_cast<const float4*>(freqs + row * ld_freqs);
+  __nv_bfloat16* base = qk + row * ld;
+  float4 f[8];
+  if (kFixedGroup) {
+    const int g = lane % G;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = __ldg(fr + g * 8 + i);
+  }
+  const int n = slots * G;
+#pragma unroll 2
+  for (int v = lane; v < n; v += 32) {
+    const int slot = v / G, g = v - slot * G;
+    if (!kFixedGroup) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = __ldg(fr + g * 8 + i);
+    }
+    __nv_bfloat16* p1 = base + (long long)slot * D + g * 8;
+    __nv_bfloat16* p2 = p1 + half;
+    const uint4 a = *reinterpret_cast<const uint4*>(p1);
+    const uint4 b = *reinterpret_cast<const uint4*>(p2);
+    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+    uint4 oa, ob;
+    uint32_t* aw = reinterpret_cast<uint32_t*>(&oa);
+    uint32_t* bw = reinterpret_cast<uint32_t*>(&ob);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 x1 = __bfloat1622float2(a2[i]), x2 = __bfloat1622float2(b2[i]);
+      const float4 f0 = f[2 * i], f1 = f[2 * i + 1];
+      aw[i] = pack_bf16(fmaf(f0.y, x2.x, f0.x * x1.x), fmaf(f1.y, x2.y, f1.x * x1.y));
+      bw[i] = pack_bf16(fmaf(f0.w, x2.x, f0.z * x1.x), fmaf(f1.w, x2.y, f1.z * x1.y));
+    }
+    *reinterpret_cast<uint4*>(p1) = oa;
+    *reinterpret_cast<uint4*>(p2) = ob;
+  }
+}
+
+// Scalar path (any even rot): one CTA per token row, the row's matrices staged in shared
+// memory, one pair per thread step.
 __global__ void __launch_bounds__(256) rope_split_half_kernel(__nv_bfloat16* __restrict__ qk, long long ld, int slots,
                                                               int D, int half, const float* __restrict__ freqs,
                                                               long long ld_freqs) {
@@ -198,56 +248,13 @@ __global__ void __launch_bounds__(256) rope_split_half_kernel(__nv_bfloat16* __r
   const float* fr = freqs + row * ld_freqs;
   for (int e = threadIdx.x; e < half * 4; e += blockDim.x) fm[e] = fr[e];
   __syncthreads();
-  const int groups = half / V;
   __nv_bfloat16* base = qk + row * ld;
-  for (int v = threadIdx.x; v < slots * groups; v += blockDim.x) {
-    const int slot = v / groups, j0 = (v - slot * groups) * V;
-    __nv_bfloat16* p1 = base + (long long)slot * D + j0;
-    __nv_bfloat16* p2 = p1 + half;
-    float x1[V], x2[V];
-    if constexpr (V == 8) {
-      const uint4 a = *reinterpret_cast<const uint4*>(p1);
-      const uint4 b = *reinterpret_cast<const uint4*>(p2);
-      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
-      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 af = __bfloat1622float2(a2[i]), bf = __bfloat1622float2(b2[i]);
-        x1[2 * i] = af.x; x1[2 * i + 1] = af.y;
-        x2[2 * i] = bf.x; x2[2 * i + 1] = bf.y;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < V; ++i) {
-        x1[i] = __bfloat162float(p1[i]);
-        x2[i] = __bfloat162float(p2[i]);
-      }
-    }
-    float o1[V], o2[V];
-#pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const float4 f = *reinterpret_cast<const float4*>(fm + 4 * (j0 + i));
-      o1[i] = fmaf(f.y, x2[i], f.x * x1[i]);
-      o2[i] = fmaf(f.w, x2[i], f.z * x1[i]);
-    }
-    if constexpr (V == 8) {
-      uint4 a, b;
-      uint32_t* aw = reinterpret_cast<uint32_t*>(&a);
-      uint32_t* bw = reinterpret_cast<uint32_t*>(&b);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        aw[i] = pack_bf16(o1[2 * i], o1[2 * i + 1]);
-        bw[i] = pack_bf16(o2[2 * i], o2[2 * i + 1]);
-      }
-      *reinterpret_cast<uint4*>(p1) = a;
-      *reinterpret_cast<uint4*>(p2) = b;
-    } else {
-#pragma unroll
-      for (int i = 0; i < V; ++i) {
-        p1[i] = __float2bfloat16_rn(o1[i]);
-        p2[i] = __float2bfloat16_rn(o2[i]);
-      }
-    }
+  for (int v = threadIdx.x; v < slots * half; v += blockDim.x) {
+    const int slot = v / half, j = v - slot * half;
+    __nv_bfloat16* p1 = base + (long long)slot * D + j;
+    const float x1 = __bfloat162float(p1[0]), x2 = __bfloat162float(p1[half]);
+    p1[0] = __float2bfloat16_rn(fmaf(fm[4 * j + 1], x2, fm[4 * j] * x1));
+    p1[half] = __float2bfloat16_rn(fmaf(fm[4 * j + 3], x2, fm[4 * j + 2] * x1));
   }
 }
 
@@ -322,15 +329,20 @@ int vdn_rope_split_half(void* qk, long long ld, int rows, int slots, int D, int 
     return vdn::kBadArgument;
   if (rows == 0) return 0;
   const int half = rot / 2;
-  const size_t smem = (size_t)half * 4 * sizeof(float);
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  const bool vec = half % 8 == 0 && D % 8 == 0 && ld % 8 == 0 && vdn::aligned16(qk);
-  if (vec)
-    rope_split_half_kernel<8><<<rows, 256, smem, s>>>(reinterpret_cast<__nv_bfloat16*>(qk), ld, slots, D, half, freqs,
-                                                      ld_freqs);
-  else
-    rope_split_half_kernel<1><<<rows, 256, smem, s>>>(reinterpret_cast<__nv_bfloat16*>(qk), ld, slots, D, half, freqs,
-                                                      ld_freqs);
+  auto* p = reinterpret_cast<__nv_bfloat16*>(qk);
+  const bool vec = half % 8 == 0 && D % 8 == 0 && ld % 8 == 0 && vdn::aligned16(qk) && vdn::aligned16(freqs) &&
+                   ld_freqs % 4 == 0;
+  if (vec) {
+    const unsigned grid = (unsigned)((rows + 7) / 8);
+    if (32 % (half / 8) == 0)
+      rope_split_half_vec_kernel<true><<<grid, 256, 0, s>>>(p, ld, rows, slots, D, half, freqs, ld_freqs);
+    else
+      rope_split_half_vec_kernel<false><<<grid, 256, 0, s>>>(p, ld, rows, slots, D, half, freqs, ld_freqs);
+  } else {
+    rope_split_half_kernel<<<rows, 256, (size_t)half * 4 * sizeof(float), s>>>(p, ld, slots, D, half, freqs,
+                                                                              ld_freqs);
+  }
   vdn::count_launch();
   return vdn::launch_status();
 }

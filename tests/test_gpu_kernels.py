@@ -326,10 +326,11 @@ def test_statistics_factor_scan_match_oracle_and_report_non_spd():
     assert int(info[2, 1]) == 1
 
 
-@pytest.mark.parametrize("D,rot,shared", [(128, 128, False), (128, 64, True), (64, 12, False)])
+@pytest.mark.parametrize("D,rot,shared", [(128, 128, False), (128, 64, True), (64, 48, False), (64, 12, False)])
 def test_rope_split_half_matches_oracle(D, rot, shared):
-    """In-place RoPE on q and k heads (16-byte path for rot % 16 == 0, scalar path otherwise;
-    one table per row or one for all rows): within one bf16 rounding of the float64 oracle."""
+    """In-place RoPE on q and k heads (16-byte path for rot % 16 == 0, with a lane's matrices
+    fixed per row when rot/16 divides 32; scalar path otherwise; one table per row or one for
+    all rows): within one bf16 rounding of the float64 oracle."""
     S, H = 300, 3
     g = torch.Generator().manual_seed(52)
     qk = torch.randn(S, 2 * H * D + 16, generator=g).to(torch.bfloat16)  # padded pitch
