@@ -40,13 +40,13 @@ SIGNATURES: dict[str, list] = {
     "vdn_alpha_gate": [_P, _L, _I, _I, _I, _P, _P, _P, _I, _I, _P, _P],
     "vdn_frame_stats": [_P, _P, _I, _I, _I, _I, _P, _L, _I, _P, _P, _P],
     "vdn_frame_stats_tc": [_P, _P, _I, _I, _I, _P, _L, _I, _P, _P, _P, _P],
-    "vdn_readout_tc": [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _L, _L, _P, _P],
+    "vdn_readout_tc": [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _L, _L, _I, _I, _P, _P],
     "vdn_delta_factor": [_P, _P, _I, _I, _I, _P, _P, _I, _F, _P, _P, _P],
     "vdn_rope_split_half": [_P, _L, _I, _I, _I, _I, _P, _L, _P],
     "vdn_sana_factor": [_P, _P, _I, _I, _I, _F, _P, _P, _I, _F, _F, _P, _P],
     "vdn_bidir_scan": [_P, _P, _P, _P, _I, _I, _I, _F, _P, _P, _P],
     "vdn_bidir_scan_tc": [_P, _P, _P, _P, _I, _I, _I, _F, _P, _P, _P, _P],
-    "vdn_readout": [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _L, _P, _L, _L, _P],
+    "vdn_readout": [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _L, _P, _L, _L, _I, _I, _P],
     "vdn_cast_rows": [_P, _L, _I, _I, _I, _P, _L, _P],
     "vdn_quant_int8_rows": [_I, _P, _L, _I, _I, _P, _L, _P, _P],
     "vdn_fp8_amax": [_I, _P, _L, _I, _I, _P, _P],

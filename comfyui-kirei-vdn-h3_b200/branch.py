@@ -137,19 +137,25 @@ class BranchDeviceWeights:
 
 
 class BranchWorkspace:
-    """Device buffers of one branch geometry, reused across calls."""
+    """Device buffers of one branch geometry, reused across calls.  ``tile_frames`` (the
+    frame-tiled low-memory mode of runtime.py:421-543): the per-row feature buffers hold one
+    tile plus its temporal halo (``TILE_HALO`` frames each side) instead of the whole clip;
+    the per-frame matrices always cover the clip."""
 
-    def __init__(self, device, Fb, tpf, heads, dim, text_len):
+    def __init__(self, device, Fb, tpf, heads, dim, text_len, tile_frames=None):
         dev = torch.device(device)
         inner = heads * dim
-        rows = Fb * tpf
+        tile = feature_frames(Fb, tile_frames)
+        rows = tile * tpf
         bf = dict(device=dev, dtype=torch.bfloat16)
         f32 = dict(device=dev, dtype=torch.float32)
-        self.key = (str(dev), Fb, tpf, heads, dim, text_len)
+        self.key = (str(dev), Fb, tpf, heads, dim, text_len, tile_frames)
+        self.tile_frames = tile_frames
+        self.feature_frames = tile
         self.conv_tmp = torch.empty(rows, inner, **bf)
-        self.qf = torch.empty(Fb, heads, tpf, dim, **bf)
-        self.kf = torch.empty(Fb, heads, tpf, dim, **bf)
-        self.vf = torch.empty(Fb, heads, tpf, dim, **bf)
+        self.qf = torch.empty(tile, heads, tpf, dim, **bf)
+        self.kf = torch.empty(tile, heads, tpf, dim, **bf)
+        self.vf = torch.empty(tile, heads, tpf, dim, **bf)
         nt = 1 if text_len > 0 else 0
         self.tk = torch.empty(1, heads, max(text_len, 1), dim, **bf)
         self.tv = torch.empty(1, heads, max(text_len, 1), dim, **bf)
@@ -178,6 +184,28 @@ class BranchWorkspace:
         return self.lohi[key]
 
 
+TILE_HALO = 2  # frames each side: the 5-tap temporal conv's reach (runtime.py:428-430)
+
+
+def frame_tiles(Fb: int, tile_frames) -> list[tuple[int, int]]:
+    """[start, stop) frame tiles of a clip of Fb frames (one tile when ``tile_frames`` is None
+    or covers the clip), as runtime.py:452-453 / :516-517 step them."""
+    if tile_frames is None or int(tile_frames) >= Fb:
+        return [(0, Fb)]
+    t = int(tile_frames)
+    if t <= 0:
+        raise ValueError("tile_frames must be positive")
+    return [(a, min(Fb, a + t)) for a in range(0, Fb, t)]
+
+
+def feature_frames(Fb: int, tile_frames) -> int:
+    """Frames a feature buffer holds: the clip, or the largest tile plus its halo."""
+    tiles = frame_tiles(Fb, tile_frames)
+    if len(tiles) == 1:
+        return Fb
+    return min(Fb, max(b - a for a, b in tiles) + 2 * TILE_HALO)
+
+
 def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_raw, aux, beta_col0, ogd_col0,
                ad_col0, Fb, tpf, frame_size, bounds, bridge, text_k=None, text_v=None, text_aux=None,
                out, out_row0, status: _lib.DeviceStatus, short_conv=("k", "v"), q_ready=False,
@@ -189,56 +217,72 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
     (column beta_col0 + h), the output-gate bottleneck (ogd_col0 + j) and the alpha
     bottleneck (ad_col0 + j); text_k / text_v / text_aux: the same for the text rows.
     Writes out[out_row0 + f*tpf + s, h*D + v] (bf16).  q_ready: ws.qf already holds the q
-    features (written by the QKV GEMM epilogue).  delta_rule: "vdn_solve" (inverse of I + A,
-    injection folded before the product) or "sana_scaled" (M = I - A/tpf, injection B/sqrt(tpf)
-    added after it; text state 0.5 B/sqrt(text_len), no factorisation).
+    features of every frame (written by the QKV epilogue).  delta_rule: "vdn_solve" (inverse
+    of I + A, injection folded before the product) or "sana_scaled" (M = I - A/tpf, injection
+    B/sqrt(tpf) added after it; text state 0.5 B/sqrt(text_len), no factorisation).
+    With ``ws.tile_frames`` the clip runs in frame tiles (runtime.py:421-543): features,
+    statistics and alpha per tile (the conv'd features with a 2-frame halo each side), the
+    factor and the scans over the clip, then features, gate and readout per tile; the result
+    is the same as one tile.
     """
     if delta_rule not in DELTA_RULES:
         raise ValueError(f"unknown delta rule: {delta_rule!r}")
     H, D = bw.heads, bw.dim
     inner = H * D
-    rows = Fb * tpf
     stream = _lib.stream_handle(out.device)
     gh, gw = frame_size
     call = _lib.call
+    tiles = frame_tiles(Fb, ws.tile_frames)
+    if q_ready and len(tiles) > 1:
+        raise ValueError("q features written by the QKV epilogue need the untiled branch")
+    fhsd = H * tpf * D  # elements of one frame of a feature buffer
 
-    def feature(raw, name, dst, l2):
-        if name in bw.conv and name in short_conv:
+    def feature(raw, name, dst, l2, a, b):
+        """Features of clip frames [a, b) into dst; returns the offset (in frames) of frame a
+        inside dst (the conv'd features are computed over a halo that the tile discards)."""
+        conv = name in bw.conv and name in short_conv
+        ha, hb = (max(0, a - TILE_HALO), min(Fb, b + TILE_HALO)) if conv and len(tiles) > 1 else (a, b)
+        src = raw[ha * tpf:hb * tpf]
+        nf = hb - ha
+        if conv:
             sp, kh, kw, tm, taps = bw.conv[name]
-            call("vdn_spatial_conv", raw.data_ptr(), raw.stride(0), sp.data_ptr(), kh, kw, Fb, gh, gw, inner,
+            call("vdn_spatial_conv", src.data_ptr(), src.stride(0), sp.data_ptr(), kh, kw, nf, gh, gw, inner,
                  ws.conv_tmp.data_ptr(), ws.conv_tmp.stride(0), stream)
-            call("vdn_temporal_act", ws.conv_tmp.data_ptr(), ws.conv_tmp.stride(0), tm.data_ptr(), taps, Fb, tpf,
+            call("vdn_temporal_act", ws.conv_tmp.data_ptr(), ws.conv_tmp.stride(0), tm.data_ptr(), taps, nf, tpf,
                  H, D, int(l2), dst.data_ptr(), stream)
         else:
-            call("vdn_temporal_act", raw.data_ptr(), raw.stride(0), None, 0, Fb, tpf, H, D, int(l2), dst.data_ptr(),
+            call("vdn_temporal_act", src.data_ptr(), src.stride(0), None, 0, nf, tpf, H, D, int(l2), dst.data_ptr(),
                  stream)
+        return a - ha
 
-    feature(k_raw, "k", ws.kf, True)
-    feature(v_raw, "v", ws.vf, False)
-    if not q_ready:
-        feature(q_raw, "q", ws.qf, True)
     aux_ld = aux.stride(0)
-    call("vdn_alpha_gate", aux.data_ptr() + 4 * ad_col0, aux_ld, Fb, tpf, D, bw.alpha_up.data_ptr(),
-         bw.dt_bias.data_ptr(), bw.a_log.data_ptr(), H, D, ws.alpha.data_ptr(), stream)
     tensor_cores = D == 128  # the tcgen05 statistics/readout kernels are written for head_dim 128
 
-    def stats(kf, vf, F_, T_, beta, A_ptr, B_ptr):
+    def stats(kf_ptr, vf_ptr, F_, T_, beta, beta_row0, A_ptr, B_ptr):
+        bp = beta.data_ptr() + 4 * beta_row0 * beta.stride(0)
         if tensor_cores:
-            call("vdn_frame_stats_tc", kf.data_ptr(), vf.data_ptr(), F_, H, T_, beta.data_ptr(), beta.stride(0),
-                 beta_col0, A_ptr, B_ptr, status.err_ptr, stream)
+            call("vdn_frame_stats_tc", kf_ptr, vf_ptr, F_, H, T_, bp, beta.stride(0), beta_col0, A_ptr, B_ptr,
+                 status.err_ptr, stream)
         else:
-            call("vdn_frame_stats", kf.data_ptr(), vf.data_ptr(), F_, H, T_, D, beta.data_ptr(), beta.stride(0),
-                 beta_col0, A_ptr, B_ptr, stream)
+            call("vdn_frame_stats", kf_ptr, vf_ptr, F_, H, T_, D, bp, beta.stride(0), beta_col0, A_ptr, B_ptr, stream)
 
-    stats(ws.kf, ws.vf, Fb, tpf, aux, ws.A.data_ptr(), ws.B.data_ptr())
+    mat = D * D * H
+    for a, b in tiles:
+        ok = feature(k_raw, "k", ws.kf, True, a, b)
+        ov = feature(v_raw, "v", ws.vf, False, a, b)
+        stats(ws.kf.data_ptr() + 2 * ok * fhsd, ws.vf.data_ptr() + 2 * ov * fhsd, b - a, tpf, aux, a * tpf,
+              ws.A.data_ptr() + 4 * a * mat, ws.B.data_ptr() + 4 * a * mat)
+        call("vdn_alpha_gate", aux.data_ptr() + 4 * (ad_col0 + a * tpf * aux_ld), aux_ld, b - a, tpf, D,
+             bw.alpha_up.data_ptr(), bw.dt_bias.data_ptr(), bw.a_log.data_ptr(), H, D,
+             ws.alpha.data_ptr() + 4 * a * H * D, stream)
     has_text = text_k is not None
     split = ws.inv_split.data_ptr() if tensor_cores else None
     if has_text:
         L = text_k.shape[0]
         call("vdn_temporal_act", text_k.data_ptr(), text_k.stride(0), None, 0, 1, L, H, D, 1, ws.tk.data_ptr(), stream)
         call("vdn_temporal_act", text_v.data_ptr(), text_v.stride(0), None, 0, 1, L, H, D, 0, ws.tv.data_ptr(), stream)
-        mat = D * D * H
-        stats(ws.tk, ws.tv, 1, L, text_aux, ws.A.data_ptr() + 4 * Fb * mat, ws.B.data_ptr() + 4 * Fb * mat)
+        stats(ws.tk.data_ptr(), ws.tv.data_ptr(), 1, L, text_aux, 0, ws.A.data_ptr() + 4 * Fb * mat,
+              ws.B.data_ptr() + 4 * Fb * mat)
     F_inv = Fb + int(has_text)
     text_frame = Fb if has_text else -1
     s0 = ws.s0 if has_text else None
@@ -261,21 +305,30 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
     else:
         call("vdn_bidir_scan", ws.inv.data_ptr(), ws.B.data_ptr(), ws.alpha.data_ptr(), _lib.ptr(s0), Fb, H, D,
              inj_scale, ws.prefix.data_ptr(), ws.suffix.data_ptr(), stream)
-    # output gate: sigmoid(bf16(x W_down^T) W_up^T + b)  (branch.py:754-758)
-    call("vdn_cast_rows", aux.data_ptr(), aux_ld, ogd_col0, rows, D, ws.ogd.data_ptr(), ws.ogd.stride(0), stream)
     lo, hi = ws.bounds_arrays(bounds)
-    if tensor_cores:
-        # gather, Q S^T, the output-gate up-projection and the epilogue in one kernel
-        call("vdn_readout_tc", ws.qf.data_ptr(), Fb, H, tpf, ws.prefix.data_ptr(), ws.suffix.data_ptr(),
+    for a, b in tiles:
+        n = (b - a) * tpf
+        if q_ready:
+            oq = a  # ws.qf holds every frame
+        else:
+            oq = feature(q_raw, "q", ws.qf, True, a, b)
+        q_ptr = ws.qf.data_ptr() + 2 * oq * fhsd
+        # output gate: sigmoid(bf16(x W_down^T) W_up^T + b)  (branch.py:754-758)
+        call("vdn_cast_rows", aux.data_ptr() + 4 * a * tpf * aux_ld, aux_ld, ogd_col0, n, D, ws.ogd.data_ptr(),
+             ws.ogd.stride(0), stream)
+        row0 = int(out_row0) + a * tpf
+        if tensor_cores:
+            # gather, Q S^T, the output-gate up-projection and the epilogue in one kernel
+            call("vdn_readout_tc", q_ptr, b - a, H, tpf, ws.prefix.data_ptr(), ws.suffix.data_ptr(),
+                 ws.alpha.data_ptr(), _lib.ptr(s0), lo.data_ptr(), hi.data_ptr(), int(bridge == "alpha"),
+                 bw.norm_w.data_ptr(), ws.ogd.data_ptr(), bw.og_up.data_ptr(), bw.og_bias.data_ptr(), out.data_ptr(),
+                 out.stride(0), row0, a, Fb, status.err_ptr, stream)
+            continue
+        call("vdn_gemm", 0, ws.ogd.data_ptr(), D, None, 0, 0, bw.og_up.data_ptr(), D, ws.og.data_ptr(), inner, 0,
+             n, inner, D, 1.0, None, None, None, None, bw.og_bias.data_ptr(), 1, None, 0, status.err_ptr, stream)
+        call("vdn_readout", q_ptr, b - a, H, tpf, D, ws.prefix.data_ptr(), ws.suffix.data_ptr(),
              ws.alpha.data_ptr(), _lib.ptr(s0), lo.data_ptr(), hi.data_ptr(), int(bridge == "alpha"),
-             bw.norm_w.data_ptr(), ws.ogd.data_ptr(), bw.og_up.data_ptr(), bw.og_bias.data_ptr(), out.data_ptr(),
-             out.stride(0), int(out_row0), status.err_ptr, stream)
-        return
-    call("vdn_gemm", 0, ws.ogd.data_ptr(), D, None, 0, 0, bw.og_up.data_ptr(), D, ws.og.data_ptr(), inner, 0,
-         rows, inner, D, 1.0, None, None, None, None, bw.og_bias.data_ptr(), 1, None, 0, status.err_ptr, stream)
-    call("vdn_readout", ws.qf.data_ptr(), Fb, H, tpf, D, ws.prefix.data_ptr(), ws.suffix.data_ptr(),
-         ws.alpha.data_ptr(), _lib.ptr(s0), lo.data_ptr(), hi.data_ptr(), int(bridge == "alpha"),
-         bw.norm_w.data_ptr(), ws.og.data_ptr(), inner, out.data_ptr(), out.stride(0), int(out_row0), stream)
+             bw.norm_w.data_ptr(), ws.og.data_ptr(), inner, out.data_ptr(), out.stride(0), row0, a, Fb, stream)
 
 
 class B200LinearBranch:
@@ -283,7 +336,7 @@ class B200LinearBranch:
     runtime.py:237-245) running the sm_100a kernels."""
 
     def __init__(self, weights, num_heads, head_dim, delta_rule="vdn_solve", bridge="alpha", a_fp32=True,
-                 short_conv=("k", "v"), enable_text_state=True, **_runtime):
+                 short_conv=("k", "v"), enable_text_state=True, tile_frames=0, **_runtime):
         if delta_rule not in DELTA_RULES:
             raise ValueError(f"unknown delta rule: {delta_rule!r}")
         if bridge not in ("alpha", "none"):
@@ -299,6 +352,9 @@ class B200LinearBranch:
         self.a_fp32 = bool(a_fp32)
         self.short_conv = targets
         self.enable_text_state = bool(enable_text_state)
+        if isinstance(tile_frames, bool) or not isinstance(tile_frames, int) or tile_frames < 0:
+            raise ValueError("tile_frames must be a non-negative integer")  # nodes.py:247-248
+        self.tile_frames = tile_frames
         self._dev_weights: dict = {}
         self._workspaces: dict = {}
         self.status = None
@@ -319,14 +375,20 @@ class B200LinearBranch:
                                                                    short_conv=self.short_conv)
         return self._dev_weights[key]
 
-    def workspace(self, device, Fb, tpf, text_len) -> BranchWorkspace:
-        key = (str(device), Fb, tpf, text_len)
+    def workspace(self, device, Fb, tpf, text_len, tile_frames=None) -> BranchWorkspace:
+        tile = None if tile_frames is None or int(tile_frames) >= Fb else int(tile_frames)
+        key = (str(device), Fb, tpf, text_len, tile)
         if key not in self._workspaces:
-            self._workspaces[key] = BranchWorkspace(device, Fb, tpf, self.num_heads, self.head_dim, text_len)
+            self._workspaces[key] = BranchWorkspace(device, Fb, tpf, self.num_heads, self.head_dim, text_len,
+                                                    tile_frames=tile)
         return self._workspaces[key]
 
     def readout(self, weights, xv, q_raw, k_raw, v_raw, num_frames, tokens_per_frame, bounds, frame_size=None,
-                text_x=None, text_k_raw=None, text_v_raw=None, skip_ends=False, *, inference=False):
+                text_x=None, text_k_raw=None, text_v_raw=None, skip_ends=False, *, inference=False,
+                tile_frames=None):
+        """The branch before ``to_out_linear`` (branch.py:672-722).  ``tile_frames``: run the
+        branch frames in tiles of that many frames (the low-memory spelling of
+        runtime.py:421-543; same result)."""
         expected_rows = num_frames * tokens_per_frame
         if xv.ndim != 2 or xv.shape[0] != expected_rows:
             raise ValueError("xv rows must equal num_frames * tokens_per_frame")
@@ -354,7 +416,7 @@ class B200LinearBranch:
         text = self.enable_text_state and text_x is not None
         if text and (text_k_raw is None or text_v_raw is None):
             raise ValueError("text state needs both raw text key and value")
-        ws = self.workspace(dev, F_b, tokens_per_frame, text_x.shape[0] if text else 0)
+        ws = self.workspace(dev, F_b, tokens_per_frame, text_x.shape[0] if text else 0, tile_frames)
         # side projections [beta | og_down | alpha_down] as fp32 (branch.py:736, :743-751, :755)
         w_side = torch.cat([bw.beta_w, bw.og_down, bw.alpha_down], 0).contiguous()
         n_side = w_side.shape[0]
@@ -389,10 +451,13 @@ class B200LinearBranch:
     def projected_delta(self, weights, xv, q_raw, k_raw, v_raw, num_frames, tokens_per_frame, bounds, *,
                         frame_size=None, text_x=None, text_k_raw=None, text_v_raw=None, skip_ends=False,
                         inference=False, projector=None, tile_frames=None):
-        """Branch output after ``to_out_linear`` (runtime.py:545-607)."""
+        """Branch output after ``to_out_linear`` (runtime.py:545-607).  As there, an inference
+        call with ``tile_frames`` (else the constructor's) > 0 runs in frame tiles."""
+        tile = self.tile_frames if tile_frames is None else int(tile_frames)
         readout = self.readout(weights, xv, q_raw, k_raw, v_raw, num_frames, tokens_per_frame, bounds,
                                frame_size=frame_size, text_x=text_x, text_k_raw=text_k_raw, text_v_raw=text_v_raw,
-                               skip_ends=skip_ends, inference=inference)
+                               skip_ends=skip_ends, inference=inference,
+                               tile_frames=tile if inference and tile > 0 else None)
         if projector is None:
             from .projection import project
             return project(readout.to(xv.dtype), weights)
@@ -400,4 +465,4 @@ class B200LinearBranch:
 
 
 __all__ = ["B200LinearBranch", "BranchDeviceWeights", "BranchWorkspace", "DELTA_RULES", "TEXT_STATE_SCALE",
-           "cholesky_runtime_scope", "run_branch"]
+           "TILE_HALO", "cholesky_runtime_scope", "feature_frames", "frame_tiles", "run_branch"]

@@ -783,7 +783,7 @@ __global__ void __launch_bounds__(256) readout_kernel(
     const float* __restrict__ suffix, const float* __restrict__ alpha, const float* __restrict__ s0,
     const int* __restrict__ lo_arr, const int* __restrict__ hi_arr, int use_alpha,
     const float* __restrict__ norm_w, const __nv_bfloat16* __restrict__ gate, long long ld_gate,
-    __nv_bfloat16* __restrict__ out, long long ld_out, long long out_row0) {
+    __nv_bfloat16* __restrict__ out, long long ld_out, long long out_row0, int f0, int F_all) {
   constexpr int P = D + 1;
   constexpr int NV = D / 16;
   extern __shared__ float sm[];
@@ -792,14 +792,15 @@ __global__ void __launch_bounds__(256) readout_kernel(
   __shared__ float dec_b[D], dec_a[D];
   const int tile = blockIdx.x, h = blockIdx.y, f = blockIdx.z;
   const int tid = threadIdx.x;
-  const int raw_lo = lo_arr[f], raw_hi = hi_arr[f];
-  const int lo = max(raw_lo, 0), hi = min(raw_hi, F - 1);
-  const bool has_before = raw_lo - 1 >= 0, has_after = raw_hi + 1 < F;
+  const int fg = f0 + f;  // clip frame of this call's frame f
+  const int raw_lo = lo_arr[fg], raw_hi = hi_arr[fg];
+  const int lo = max(raw_lo, 0), hi = min(raw_hi, F_all - 1);
+  const bool has_before = raw_lo - 1 >= 0, has_after = raw_hi + 1 < F_all;
   for (int k = tid; k < D; k += 256) {
     float lb = 0.f, la = 0.f;
     if (use_alpha) {
-      for (int j = lo; j <= f; ++j) lb += __logf(fmaxf(alpha[((long long)j * H + h) * D + k], 1e-12f));
-      for (int j = f; j <= hi; ++j) la += __logf(fmaxf(alpha[((long long)j * H + h) * D + k], 1e-12f));
+      for (int j = lo; j <= fg; ++j) lb += __logf(fmaxf(alpha[((long long)j * H + h) * D + k], 1e-12f));
+      for (int j = fg; j <= hi; ++j) la += __logf(fmaxf(alpha[((long long)j * H + h) * D + k], 1e-12f));
     }
     dec_b[k] = __expf(lb);
     dec_a[k] = __expf(la);
@@ -1082,8 +1083,9 @@ int vdn_bidir_scan(const float* inv, const float* B, const float* alpha, const f
 int vdn_readout(const void* Q, int F, int H, int T, int D, const float* prefix, const float* suffix,
                 const float* alpha, const float* s0, const int* lo, const int* hi, int use_alpha,
                 const float* norm_w, const void* gate, long long ld_gate, void* out, long long ld_out,
-                long long out_row0, void* stream) {
+                long long out_row0, int f0, int F_all, void* stream) {
   if (!Q || !prefix || !suffix || !alpha || !lo || !hi || !norm_w || !gate || !out) return vdn::kBadArgument;
+  if (F <= 0 || f0 < 0 || F_all < f0 + F) return vdn::kBadArgument;
   dim3 grid((T + 63) / 64, H, F);
   auto s = reinterpret_cast<cudaStream_t>(stream);
   const size_t smem = (size_t)(D * (D + 1) + D * 64) * sizeof(float);
@@ -1092,13 +1094,13 @@ int vdn_readout(const void* Q, int F, int H, int T, int D, const float* prefix, 
     readout_kernel<128><<<grid, 256, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(Q), T, F, H, prefix, suffix,
                                                 alpha, s0, lo, hi, use_alpha, norm_w,
                                                 reinterpret_cast<const __nv_bfloat16*>(gate), ld_gate,
-                                                reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0);
+                                                reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0, f0, F_all);
     vdn::count_launch();
   } else if (D == 64) {
     readout_kernel<64><<<grid, 256, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(Q), T, F, H, prefix, suffix,
                                                alpha, s0, lo, hi, use_alpha, norm_w,
                                                reinterpret_cast<const __nv_bfloat16*>(gate), ld_gate,
-                                               reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0);
+                                               reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0, f0, F_all);
     vdn::count_launch();
   } else {
     return vdn::kUnsupported;

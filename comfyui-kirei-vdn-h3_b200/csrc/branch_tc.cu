@@ -257,7 +257,8 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
                       const float* __restrict__ suffix, const float* __restrict__ alpha, const float* __restrict__ s0,
                       const int* __restrict__ lo_arr, const int* __restrict__ hi_arr, int use_alpha,
                       const float* __restrict__ norm_w, const float* __restrict__ og_bias,
-                      __nv_bfloat16* __restrict__ out, long long ld_out, long long out_row0, int* err) {
+                      __nv_bfloat16* __restrict__ out, long long ld_out, long long out_row0, int f0, int F_all,
+                      int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // The layout uses the whole 227 KB, so the dynamic window must start 1024-aligned (it
   // does when the kernel has no static shared memory); otherwise report and leave.
@@ -401,17 +402,19 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
       if (!*go) break;
       // alpha-bridge decays (branch.py:385-390) of this thread's fixed chunk of 8 k
       // (every element it writes has k = (bt & 15) * 8 + q)
-      const int raw_lo = lo_arr[f], raw_hi = hi_arr[f];
-      const int lo = max(raw_lo, 0), hi = min(raw_hi, F - 1);
-      const bool has_before = raw_lo - 1 >= 0, has_after = raw_hi + 1 < F;
+      // f is the frame within this call's frames; the gather works in clip frames fg
+      const int fg = f0 + f;
+      const int raw_lo = lo_arr[fg], raw_hi = hi_arr[fg];
+      const int lo = max(raw_lo, 0), hi = min(raw_hi, F_all - 1);
+      const bool has_before = raw_lo - 1 >= 0, has_after = raw_hi + 1 < F_all;
       const int kc = (bt & 15) * 8;
       float dec_b[8], dec_a[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         float lb = 0.f, la = 0.f;
         if (use_alpha) {
-          for (int j = lo; j <= f; ++j) lb += __logf(fmaxf(alpha[((long long)j * H + h) * D + kc + q], 1e-12f));
-          for (int j = f; j <= hi; ++j) la += __logf(fmaxf(alpha[((long long)j * H + h) * D + kc + q], 1e-12f));
+          for (int j = lo; j <= fg; ++j) lb += __logf(fmaxf(alpha[((long long)j * H + h) * D + kc + q], 1e-12f));
+          for (int j = fg; j <= hi; ++j) la += __logf(fmaxf(alpha[((long long)j * H + h) * D + kc + q], 1e-12f));
         }
         dec_b[q] = __expf(lb);
         dec_a[q] = __expf(la);
@@ -791,18 +794,20 @@ int vdn_frame_stats_tc(const void* K, const void* V, int F, int H, int T, const 
   return vdn::launch_status();
 }
 
-// Readout on tensor cores (head_dim 128): Q FHSD [F, H, T, 128] bf16; og_down [F*T, 128] bf16
-// (bf16-rounded x W_og_down^T of the branch rows); og_up [H*128, 128] bf16 with bias og_bias
-// [H*128] fp32; prefix/suffix [F, H, 128, 128] fp32; alpha [F, H, 128]; s0 [H, 128, 128] or NULL;
-// lo/hi [F] raw window bounds.  Writes out[out_row0 + f*T + s, h*128 + v] (bf16).
+// Readout on tensor cores (head_dim 128) of the F frames f0 .. f0+F-1 of a clip of F_all
+// frames: Q FHSD [F, H, T, 128] bf16 and og_down [F*T, 128] bf16 (bf16-rounded x W_og_down^T)
+// hold those frames' rows; og_up [H*128, 128] bf16 with bias og_bias [H*128] fp32;
+// prefix/suffix [F_all, H, 128, 128] fp32; alpha [F_all, H, 128]; s0 [H, 128, 128] or NULL;
+// lo/hi [F_all] raw window bounds.  Writes out[out_row0 + f*T + s, h*128 + v] (bf16).
 // Replaces branch.py:345-396 (gather), :780 (readout), :494-530 (epilogue), :754-758 (gate).
 int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, const float* suffix, const float* alpha,
                    const float* s0, const int* lo, const int* hi, int use_alpha, const float* norm_w,
                    const void* og_down, const void* og_up, const float* og_bias, void* out, long long ld_out,
-                   long long out_row0, int* dev_err, void* stream) {
+                   long long out_row0, int f0, int F_all, int* dev_err, void* stream) {
   using namespace vdn::branch_tc;
   if (!Q || !prefix || !suffix || !alpha || !lo || !hi || !norm_w || !og_down || !og_up || !og_bias || !out)
     return vdn::kBadArgument;
+  if (F <= 0 || f0 < 0 || F_all < f0 + F) return vdn::kBadArgument;
   if ((ld_out * 2) % 16 || !vdn::aligned16(out) || !vdn::aligned16(prefix) || !vdn::aligned16(suffix) ||
       (s0 && !vdn::aligned16(s0)))
     return vdn::kMisaligned;  // 16-byte output vectors, float4 state loads
@@ -822,7 +827,7 @@ int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, cons
   const int grid = units < vdn::sm_count() ? units : vdn::sm_count();
   readout_tc_kernel<<<grid, kReadoutThreads, ReadoutSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
       tq, tg, tw, F, H, T, prefix, suffix, alpha, s0, lo, hi, use_alpha, norm_w, og_bias,
-      reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0, dev_err);
+      reinterpret_cast<__nv_bfloat16*>(out), ld_out, out_row0, f0, F_all, dev_err);
   vdn::count_launch();
   return vdn::launch_status();
 }

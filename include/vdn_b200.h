@@ -183,21 +183,26 @@ int vdn_bidir_scan_tc(const void* inv_split, const float* B, const float* alpha,
                       int F_inv, int H, float inj_scale, float* prefix, float* suffix, int* dev_err, void* stream);
 
 /* Gather with alpha bridge, readout Q S^T, RMSNorm over D, x output gate, into
- * out[out_row0 + f*T + s, h*D + v].  Replaces: branch.py:345-396 (gather_linear_state),
- * branch.py:780, :494-530 (readout, linear_epilogue). */
+ * out[out_row0 + f*T + s, h*D + v] for the F frames f0 .. f0+F-1 of a clip of F_all frames
+ * (Q [F, H, T, D] and gate rows hold those frames; prefix, suffix, alpha, lo, hi cover the
+ * clip; f0 = 0, F_all = F for a whole clip).  Replaces: branch.py:345-396
+ * (gather_linear_state), branch.py:780, :494-530 (readout, linear_epilogue), and with f0 > 0
+ * the per-tile readout of runtime.py:516-543 (_projected_delta_tiled). */
 int vdn_readout(const void* Q, int F, int H, int T, int D, const float* prefix, const float* suffix,
                 const float* alpha, const float* s0, const int* lo, const int* hi, int use_alpha,
                 const float* norm_w, const void* gate, long long ld_gate, void* out, long long ld_out,
-                long long out_row0, void* stream);
+                long long out_row0, int f0, int F_all, void* stream);
 
 /* Tensor-core readout for head_dim 128: gather + alpha bridge into a bf16 state, R = Q S^T and
  * the output-gate up-projection G = og_down og_up^T as tcgen05 MMAs, then RMSNorm(D) x norm_w x
  * sigmoid(G + og_bias) into out[out_row0 + f*T + s, h*128 + v].  og_down [F*T, 128] bf16,
- * og_up [H*128, 128] bf16.  Replaces: branch.py:345-396, :494-530, :754-758, :780. */
+ * og_up [H*128, 128] bf16.  Frames f0 .. f0+F-1 of a clip of F_all, as in vdn_readout.
+ * Replaces: branch.py:345-396, :494-530, :754-758, :780. */
 int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, const float* suffix,
                    const float* alpha, const float* s0, const int* lo, const int* hi, int use_alpha,
                    const float* norm_w, const void* og_down, const void* og_up, const float* og_bias,
-                   void* out, long long ld_out, long long out_row0, int* dev_err, void* stream);
+                   void* out, long long ld_out, long long out_row0, int f0, int F_all, int* dev_err,
+                   void* stream);
 
 /* fp32 column block -> bf16 (output-gate bottleneck rounding, branch.py:755). */
 int vdn_cast_rows(const float* in, long long ld_in, int col0, int rows, int cols, void* out, long long ld_out,

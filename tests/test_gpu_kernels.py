@@ -397,6 +397,38 @@ def test_sana_factor_and_scans_match_oracle(D):
         assert rel_l2(p_tc, wp) < 1e-4 and rel_l2(s_tc, wsf) < 1e-4
 
 
+@pytest.mark.parametrize("D,grid,tile", [(64, (4, 5), 1), (64, (4, 5), 4), (128, (10, 15), 3), (128, (10, 15), 2)])
+def test_frame_tiled_branch_equals_untiled(D, grid, tile):
+    """The low-memory frame-tiled spelling (runtime.py:421-543; the reference's own test holds
+    it to 3e-5 of the untiled branch, tests/test_domestic_runtime.py:42-109) gives the same
+    bits here: every kernel computes a frame from the same inputs in the same order."""
+    H, hidden, F = 2, 96, 9
+    tpf = grid[0] * grid[1]
+    rows = F * tpf
+    g = torch.Generator().manual_seed(61)
+    w = vo.make_branch_weights(g, hidden, H, D)
+    w["to_out_linear.weight"] = torch.randn(hidden, H * D, generator=g) * 0.02
+    xv = torch.randn(rows, hidden, generator=g).to(torch.bfloat16).to(DEV)
+    q, k, v = (torch.randn(rows, H, D, generator=g).to(torch.bfloat16).to(DEV) for _ in range(3))
+    tx = torch.randn(11, hidden, generator=g).to(torch.bfloat16).to(DEV)
+    tk, tv = (torch.randn(11, H, D, generator=g).to(torch.bfloat16).to(DEV) for _ in range(2))
+    bounds = vo.window_bounds(F, 1, 2)
+    for rule in ("vdn_solve", "sana_scaled"):
+        br = pkg.B200LinearBranch(w, H, D, delta_rule=rule)
+        args = (w, xv, q, k, v, F, tpf, bounds)
+        kw = dict(frame_size=grid, text_x=tx, text_k_raw=tk, text_v_raw=tv, skip_ends=True)
+        whole = br.readout(*args, **kw).clone()
+        tiled = br.readout(*args, **kw, tile_frames=tile)
+        torch.cuda.synchronize()
+        assert torch.equal(tiled, whole), f"{rule}: tiled readout differs"
+        assert br.workspace(DEV, F - 2, tpf, 11, tile).feature_frames == min(F - 2, tile + 4)
+        # projected_delta tiles only in inference, as runtime.py:584-590 does
+        p_tiled = br.projected_delta(*args, **kw, inference=True, tile_frames=tile)
+        p_whole = br.projected_delta(*args, **kw, inference=False, tile_frames=tile)
+        torch.cuda.synchronize()
+        assert torch.equal(p_tiled, p_whole)
+
+
 @pytest.mark.parametrize("delta_rule", ["vdn_solve", "sana_scaled"])
 @pytest.mark.parametrize("D,grid", [(64, (4, 5)), (128, (10, 15))])
 def test_branch_readout_matches_oracle_with_and_without_text(D, grid, delta_rule):

@@ -266,6 +266,20 @@ def test_oracle_rope_is_comfy_rotation_on_split_halves():
     assert torch.allclose(got[..., :half] ** 2 + got[..., half:rot] ** 2, x[..., :half] ** 2 + x[..., half:rot] ** 2)
 
 
+def test_frame_tiles_cover_the_clip_with_halo_sized_buffers():
+    assert bbr.frame_tiles(7, None) == [(0, 7)] and bbr.frame_tiles(7, 7) == [(0, 7)]
+    assert bbr.frame_tiles(7, 3) == [(0, 3), (3, 6), (6, 7)]
+    assert bbr.frame_tiles(5, 1) == [(i, i + 1) for i in range(5)]
+    assert bbr.feature_frames(29, None) == 29 and bbr.feature_frames(29, 4) == 8 and bbr.feature_frames(5, 4) == 5
+    with pytest.raises(ValueError):
+        bbr.frame_tiles(7, 0)
+    w = vo.make_branch_weights(torch.Generator().manual_seed(0), 32, 2, 64)
+    assert pkg.B200LinearBranch(w, 2, 64, tile_frames=4).tile_frames == 4
+    for bad in (-1, 2.5, True):
+        with pytest.raises(ValueError, match="tile_frames"):
+            pkg.B200LinearBranch(w, 2, 64, tile_frames=bad)
+
+
 def test_status_codes_map_to_reference_exceptions():
     with pytest.raises(ValueError):
         pkg._lib.check(-1, "x")
