@@ -442,6 +442,16 @@ def run_dit_stack(args, c, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def rope_freqs_table(seq, rot, dev):
+    """A [1, seq, 1, rot/2, 2, 2] RoPE table of 1-D positions (ComfyUI's layout), built on the device."""
+    pos = torch.arange(seq, device=dev, dtype=torch.float64)
+    omega = 1.0 / 10000.0 ** (torch.arange(0, rot, 2, device=dev, dtype=torch.float64) / rot)
+    ang = pos[:, None] * omega[None]
+    c, s_ = torch.cos(ang), torch.sin(ang)
+    m = torch.stack([torch.stack([c, -s_], -1), torch.stack([s_, c], -1)], -2).float()
+    return m.reshape(1, seq, 1, rot // 2, 2, 2)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -454,6 +464,10 @@ def main():
                     help="run one kernel alone on the config geometry (profiling small cases)")
     ap.add_argument("--heads", type=int, default=None, help="override the head count (profiling small cases)")
     ap.add_argument("--blocks", type=int, default=None, help="config 4: number of DiT blocks (default 50)")
+    ap.add_argument("--delta-rule", choices=["vdn_solve", "sana_scaled"], default="vdn_solve",
+                    help="configs 1/3: the branch's delta rule (BASELINE's released lineage is vdn_solve)")
+    ap.add_argument("--rope", action="store_true",
+                    help="configs 1/3: apply a rot_dim = head_dim RoPE table to q/k (not in BASELINE's config)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
@@ -497,8 +511,11 @@ def main():
                                  k_norm=types.SimpleNamespace(weight=kn, eps=1e-6), forward=None)
     # N > 1: the heads are sharded over the ranks (H/N each, recurrence kept per head), the
     # per-head outputs exchanged by row block over NCCL and the projected rows all-gathered
-    state = pkg.B200State("bench", {"enable_softmax_gate": True}, [branch], H, D, shard_heads=world > 1)
+    state = pkg.B200State("bench", {"enable_softmax_gate": True, "delta_rule": args.delta_rule}, [branch], H, D,
+                          shard_heads=world > 1)
     block = state.fused_block(attn, 0, dev)
+    rope_freqs = rope_freqs_table(lay.seq_len, D, dev) if args.rope else None
+    rope = pkg.rope_table(rope_freqs, lay.seq_len, D, dev)
     status = state.device_status(dev)
     g = torch.Generator().manual_seed(1)
     x_host = torch.randn(lay.seq_len, hidden, generator=g).to(torch.bfloat16).pin_memory()
@@ -519,7 +536,7 @@ def main():
     clocks = ClockSampler(local).start()  # running through the warm-up, so it samples the timed region
     with pkg.cholesky_runtime_scope():
         for _ in range(args.warmup):
-            block.forward(x_dev, lay, state.window_plans, status, out=out_dev if world == 1 else None)
+            block.forward(x_dev, lay, state.window_plans, status, out=out_dev if world == 1 else None, rope=rope)
     torch.cuda.synchronize()
     status.raise_if_failed()
     attn_ms.clear()
@@ -531,7 +548,7 @@ def main():
     e_start.record()
     with pkg.cholesky_runtime_scope():
         for _ in range(args.steps):
-            block.forward(x_dev, lay, state.window_plans, status, out=out_dev if world == 1 else None)
+            block.forward(x_dev, lay, state.window_plans, status, out=out_dev if world == 1 else None, rope=rope)
         e_end.record()
         torch.cuda.synchronize()
     clocks.mark_end()
@@ -555,7 +572,8 @@ def main():
 
     def run_fwd(xd, io=None):
         with pkg.publish_layout(lay):
-            return fwd(xd, transformer_options={pkg.hybrid.STREAM_IO_KEY: io} if io is not None else None)
+            return fwd(xd, rope_freqs,
+                       transformer_options={pkg.hybrid.STREAM_IO_KEY: io} if io is not None else None)
 
     if world == 1:
         streamer = pkg.HostStreamer(run_fwd, dev, (S, hidden))
@@ -619,7 +637,8 @@ def main():
         "config": {"workload": f"config{args.config}: 31x{c['grid'][0] * c['grid'][1]}+512 tokens, H={H}, D={D}, "
                                f"hidden={hidden}", "tokens": lay.seq_len, "parallelism": f"heads/{world}" if world > 1 else "none",
                    "l2": f"inputs larger than L2 (x {lay.seq_len * hidden * 2 / 1e6:.0f} MB, weights "
-                         f"{(5 * H * D + 2 * H + 2 * D) * hidden * 2 / 1e9:.2f} GB)"},
+                         f"{(5 * H * D + 2 * H + 2 * D) * hidden * 2 / 1e9:.2f} GB)",
+                   "delta_rule": args.delta_rule, "rope": bool(args.rope)},
         "tflop_per_step": flops["total"] / 1e12,
         "roofline": {"kernel": "window_attention_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak,
