@@ -173,6 +173,13 @@ class BranchWorkspace:
         # the output gate is materialised only on the head_dim-64 path (128 fuses it into the readout)
         self.og = torch.empty(rows if dim != 128 else 0, inner, **bf)
         self.lohi: dict = {}
+        self._side = None
+
+    def side_stream(self) -> torch.cuda.Stream:
+        """The stream the text state runs on, beside the frames' kernels."""
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.alpha.device)
+        return self._side
 
     def bounds_arrays(self, bounds):
         key = tuple(bounds)
@@ -258,15 +265,41 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
     aux_ld = aux.stride(0)
     tensor_cores = D == 128  # the tcgen05 statistics/readout kernels are written for head_dim 128
 
-    def stats(kf_ptr, vf_ptr, F_, T_, beta, beta_row0, A_ptr, B_ptr):
+    def stats(kf_ptr, vf_ptr, F_, T_, beta, beta_row0, A_ptr, B_ptr, st=stream):
         bp = beta.data_ptr() + 4 * beta_row0 * beta.stride(0)
         if tensor_cores:
             call("vdn_frame_stats_tc", kf_ptr, vf_ptr, F_, H, T_, bp, beta.stride(0), beta_col0, A_ptr, B_ptr,
-                 status.err_ptr, stream)
+                 status.err_ptr, st)
         else:
-            call("vdn_frame_stats", kf_ptr, vf_ptr, F_, H, T_, D, bp, beta.stride(0), beta_col0, A_ptr, B_ptr, stream)
+            call("vdn_frame_stats", kf_ptr, vf_ptr, F_, H, T_, D, bp, beta.stride(0), beta_col0, A_ptr, B_ptr, st)
 
+    has_text = text_k is not None
+    s0 = ws.s0 if has_text else None
     mat = D * D * H
+    if has_text:
+        # The text "frame" (its features, statistics, factor and S0: small launches of 40-odd
+        # CTAs each, latency-bound) runs on a side stream beside the frames' kernels; the scan
+        # waits for it.  Its inputs were written before this call on the caller's stream.
+        L = text_k.shape[0]
+        main = torch.cuda.current_stream(out.device)
+        side = ws.side_stream()
+        side.wait_stream(main)
+        ts = side.cuda_stream
+        call("vdn_temporal_act", text_k.data_ptr(), text_k.stride(0), None, 0, 1, L, H, D, 1, ws.tk.data_ptr(), ts)
+        call("vdn_temporal_act", text_v.data_ptr(), text_v.stride(0), None, 0, 1, L, H, D, 0, ws.tv.data_ptr(), ts)
+        stats(ws.tk.data_ptr(), ws.tv.data_ptr(), 1, L, text_aux, 0, ws.A.data_ptr() + 4 * Fb * mat,
+              ws.B.data_ptr() + 4 * Fb * mat, st=ts)
+        if delta_rule == "sana_scaled":
+            # S0 = 0.5 * B / sqrt(L): no factor of the text matrix is needed
+            call("vdn_sana_factor", ws.A.data_ptr() + 4 * Fb * mat, ws.B.data_ptr() + 4 * Fb * mat, 1, H, D, 1.0 / L,
+                 None, None, 0, (1.0 / L) ** 0.5, TEXT_STATE_SCALE, ws.s0.data_ptr(), ts)
+        else:
+            call("vdn_delta_factor", ws.A.data_ptr() + 4 * Fb * mat, ws.B.data_ptr() + 4 * Fb * mat, 1, H, D,
+                 ws.inv.data_ptr() + 4 * Fb * mat, ws.info.data_ptr() + 4 * Fb * H, 0, TEXT_STATE_SCALE,
+                 ws.s0.data_ptr(), None, ts)
+        text_done = torch.cuda.Event()
+        text_done.record(side)
+
     for a, b in tiles:
         ok = feature(k_raw, "k", ws.kf, True, a, b)
         ov = feature(v_raw, "v", ws.vf, False, a, b)
@@ -275,32 +308,24 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
         call("vdn_alpha_gate", aux.data_ptr() + 4 * (ad_col0 + a * tpf * aux_ld), aux_ld, b - a, tpf, D,
              bw.alpha_up.data_ptr(), bw.dt_bias.data_ptr(), bw.a_log.data_ptr(), H, D,
              ws.alpha.data_ptr() + 4 * a * H * D, stream)
-    has_text = text_k is not None
+    # the frames' factor (the text matrix is factored on the side stream); the inverse halves
+    # of the Fb frames, hi then lo, are what the tensor-core scan reads
     split = ws.inv_split.data_ptr() if tensor_cores else None
-    if has_text:
-        L = text_k.shape[0]
-        call("vdn_temporal_act", text_k.data_ptr(), text_k.stride(0), None, 0, 1, L, H, D, 1, ws.tk.data_ptr(), stream)
-        call("vdn_temporal_act", text_v.data_ptr(), text_v.stride(0), None, 0, 1, L, H, D, 0, ws.tv.data_ptr(), stream)
-        stats(ws.tk.data_ptr(), ws.tv.data_ptr(), 1, L, text_aux, 0, ws.A.data_ptr() + 4 * Fb * mat,
-              ws.B.data_ptr() + 4 * Fb * mat)
-    F_inv = Fb + int(has_text)
-    text_frame = Fb if has_text else -1
-    s0 = ws.s0 if has_text else None
     if delta_rule == "sana_scaled":
         # python-float scalars as branch.py:167-168 computes them; the C ABI rounds them to fp32
         # as torch does when it multiplies them into an fp32 tensor
         inj_scale = (1.0 / tpf) ** 0.5
-        text_inj = (1.0 / L) ** 0.5 if has_text else 0.0
-        call("vdn_sana_factor", ws.A.data_ptr(), ws.B.data_ptr(), F_inv, H, D, 1.0 / tpf,
-             None if tensor_cores else ws.inv.data_ptr(), split, text_frame, text_inj, TEXT_STATE_SCALE,
-             _lib.ptr(s0), stream)
+        call("vdn_sana_factor", ws.A.data_ptr(), ws.B.data_ptr(), Fb, H, D, 1.0 / tpf,
+             None if tensor_cores else ws.inv.data_ptr(), split, -1, 0.0, 0.0, None, stream)
     else:
         inj_scale = 0.0
-        call("vdn_delta_factor", ws.A.data_ptr(), ws.B.data_ptr(), F_inv, H, D, ws.inv.data_ptr(), ws.info.data_ptr(),
-             text_frame, TEXT_STATE_SCALE if has_text else 0.0, _lib.ptr(s0), split, stream)
-        record_factor_status(ws.info)
+        call("vdn_delta_factor", ws.A.data_ptr(), ws.B.data_ptr(), Fb, H, D, ws.inv.data_ptr(), ws.info.data_ptr(),
+             -1, 0.0, None, split, stream)
+        record_factor_status(ws.info[:Fb + int(has_text)])
+    if has_text:
+        main.wait_event(text_done)
     if tensor_cores:
-        call("vdn_bidir_scan_tc", split, ws.B.data_ptr(), ws.alpha.data_ptr(), _lib.ptr(s0), Fb, F_inv, H, inj_scale,
+        call("vdn_bidir_scan_tc", split, ws.B.data_ptr(), ws.alpha.data_ptr(), _lib.ptr(s0), Fb, Fb, H, inj_scale,
              ws.prefix.data_ptr(), ws.suffix.data_ptr(), status.err_ptr, stream)
     else:
         call("vdn_bidir_scan", ws.inv.data_ptr(), ws.B.data_ptr(), ws.alpha.data_ptr(), _lib.ptr(s0), Fb, H, D,
