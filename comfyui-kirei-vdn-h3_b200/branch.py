@@ -276,15 +276,20 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
     has_text = text_k is not None
     s0 = ws.s0 if has_text else None
     mat = D * D * H
+    # The text "frame" (its features, statistics, factor and S0) and alpha (launches of 30 to
+    # 40-odd CTAs, latency-bound) run on a side stream beside the frames' conv, statistics and
+    # factor; the scan waits for them.  Their inputs were written before this call on the
+    # caller's stream.
+    main = torch.cuda.current_stream(out.device)
+    side = ws.side_stream()
+    side.wait_stream(main)
+    ts = side.cuda_stream
+    for a, b in tiles:
+        call("vdn_alpha_gate", aux.data_ptr() + 4 * (ad_col0 + a * tpf * aux_ld), aux_ld, b - a, tpf, D,
+             bw.alpha_up.data_ptr(), bw.dt_bias.data_ptr(), bw.a_log.data_ptr(), H, D,
+             ws.alpha.data_ptr() + 4 * a * H * D, ts)
     if has_text:
-        # The text "frame" (its features, statistics, factor and S0: small launches of 40-odd
-        # CTAs each, latency-bound) runs on a side stream beside the frames' kernels; the scan
-        # waits for it.  Its inputs were written before this call on the caller's stream.
         L = text_k.shape[0]
-        main = torch.cuda.current_stream(out.device)
-        side = ws.side_stream()
-        side.wait_stream(main)
-        ts = side.cuda_stream
         call("vdn_temporal_act", text_k.data_ptr(), text_k.stride(0), None, 0, 1, L, H, D, 1, ws.tk.data_ptr(), ts)
         call("vdn_temporal_act", text_v.data_ptr(), text_v.stride(0), None, 0, 1, L, H, D, 0, ws.tv.data_ptr(), ts)
         stats(ws.tk.data_ptr(), ws.tv.data_ptr(), 1, L, text_aux, 0, ws.A.data_ptr() + 4 * Fb * mat,
@@ -297,17 +302,14 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
             call("vdn_delta_factor", ws.A.data_ptr() + 4 * Fb * mat, ws.B.data_ptr() + 4 * Fb * mat, 1, H, D,
                  ws.inv.data_ptr() + 4 * Fb * mat, ws.info.data_ptr() + 4 * Fb * H, 0, TEXT_STATE_SCALE,
                  ws.s0.data_ptr(), None, ts)
-        text_done = torch.cuda.Event()
-        text_done.record(side)
+    side_done = torch.cuda.Event()
+    side_done.record(side)
 
     for a, b in tiles:
         ok = feature(k_raw, "k", ws.kf, True, a, b)
         ov = feature(v_raw, "v", ws.vf, False, a, b)
         stats(ws.kf.data_ptr() + 2 * ok * fhsd, ws.vf.data_ptr() + 2 * ov * fhsd, b - a, tpf, aux, a * tpf,
               ws.A.data_ptr() + 4 * a * mat, ws.B.data_ptr() + 4 * a * mat)
-        call("vdn_alpha_gate", aux.data_ptr() + 4 * (ad_col0 + a * tpf * aux_ld), aux_ld, b - a, tpf, D,
-             bw.alpha_up.data_ptr(), bw.dt_bias.data_ptr(), bw.a_log.data_ptr(), H, D,
-             ws.alpha.data_ptr() + 4 * a * H * D, stream)
     # the frames' factor (the text matrix is factored on the side stream); the inverse halves
     # of the Fb frames, hi then lo, are what the tensor-core scan reads
     split = ws.inv_split.data_ptr() if tensor_cores else None
@@ -321,9 +323,8 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
         inj_scale = 0.0
         call("vdn_delta_factor", ws.A.data_ptr(), ws.B.data_ptr(), Fb, H, D, ws.inv.data_ptr(), ws.info.data_ptr(),
              -1, 0.0, None, split, stream)
-        record_factor_status(ws.info[:Fb + int(has_text)])
-    if has_text:
-        main.wait_event(text_done)
+        record_factor_status(ws.info)
+    main.wait_event(side_done)
     if tensor_cores:
         call("vdn_bidir_scan_tc", split, ws.B.data_ptr(), ws.alpha.data_ptr(), _lib.ptr(s0), Fb, Fb, H, inj_scale,
              ws.prefix.data_ptr(), ws.suffix.data_ptr(), status.err_ptr, stream)
