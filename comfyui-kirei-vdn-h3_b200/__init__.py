@@ -17,7 +17,7 @@ from .hybrid import B200State, FusedBlock, GatedResidual, RopeTable, make_vdn_fo
 from .layout import (ANCHOR_FRAME_MODES, VDNLayout, current_layout, from_comfy_packed_layout, full_coverage,
                      layout_from_payload, make_layout, publish_layout, window_bounds, with_window)
 from .projection import (gemm, gemm_grouped_k, prepare_projection_maps, project, quantize_rows_int8,
-                         quantize_tensor_fp8)
+                         quantize_rows_int8_convrot, quantize_tensor_fp8)
 from .shard import HeadShard
 from .window import WindowPlanCache, build_window_plan, window_softmax_b200
 
@@ -27,5 +27,6 @@ __all__ = [
     "RopeTable", "WindowPlanCache", "gemm_grouped_k", "rope_table",
     "build_window_plan", "cholesky_runtime_scope", "current_layout", "full_coverage", "gemm", "make_layout",
     "make_vdn_forward", "prepare_projection_maps", "project", "publish_layout", "quantize_rows_int8",
+    "quantize_rows_int8_convrot",
     "quantize_tensor_fp8", "run_forward_checked", "window_bounds", "window_softmax_b200", "with_window", "_lib",
 ]

@@ -49,6 +49,7 @@ SIGNATURES: dict[str, list] = {
     "vdn_readout": [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P, _L, _P, _L, _L, _I, _I, _P],
     "vdn_cast_rows": [_P, _L, _I, _I, _I, _P, _L, _P],
     "vdn_quant_int8_rows": [_I, _P, _L, _I, _I, _P, _L, _P, _P],
+    "vdn_quant_int8_rows_convrot": [_P, _L, _I, _I, _I, _P, _L, _P, _P],
     "vdn_fp8_amax": [_I, _P, _L, _I, _I, _P, _P],
     "vdn_fp8_cast": [_I, _P, _L, _I, _I, _P, _P, _L, _P, _P],
     "vdn_quant_fp8_tensor": [_I, _P, _L, _I, _I, _P, _L, _P, _P, _P],

@@ -150,6 +150,88 @@ __global__ void fp8_cast_kernel(const T* __restrict__ x, long long ldx, int rows
   }
 }
 
+// ConvRot rows: each 256-wide group of a row is rotated by H = R/16, R the fourth Kronecker
+// power of the order-4 regular Hadamard matrix J - 2I (symmetric, H H = I), then the rotated
+// row is quantised per row like int8_rows_vec_kernel.  Rotating both the activation rows and
+// the weight rows leaves x W^T unchanged, and spreads a channel outlier over its group.
+//
+// A warp owns one group at a time, a lane 8 consecutive elements (index i = 8 lane + e).  The
+// group index has four base-4 digits, d0 = e & 3, d1 = (e >> 2) | (lane & 1) << 1,
+// d2 = (lane >> 1) & 3, d3 = lane >> 3; R applies J - 2I along each digit in the order
+// d0, d1, d2, d3: y = S - 2 x with S = (x[d=0] + x[d=1]) + (x[d=2] + x[d=3]).  Every lane of a
+// quadruple forms S from the same two pair sums (IEEE addition commutes exactly), so the
+// result is one fixed fp32 sequence that a CPU restatement reproduces bit for bit.
+// Block: WARPS warps, a row per CTA; warp w rotates groups w, w + WARPS, ... (G at most).
+template <int G, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) int8_rows_convrot_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                      long long ldx, int K, int8_t* __restrict__ q,
+                                                                      long long ldq, float* __restrict__ scale) {
+  const long long r = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int groups = K >> 8;
+  const __nv_bfloat16* row = x + r * ldx;
+  float v[G][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const int g = warp + WARPS * j;
+    if (g >= groups) {  // warp-uniform
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] = 0.f;
+      continue;
+    }
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(row + ((long long)g << 8)) + lane);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[j][e] = __uint_as_float((e & 1) ? (w[e >> 1] & 0xFFFF0000u) : (w[e >> 1] << 16));
+    // d0: four consecutive elements in registers
+#pragma unroll
+    for (int b = 0; b < 8; b += 4) {
+      const float s = (v[j][b] + v[j][b + 1]) + (v[j][b + 2] + v[j][b + 3]);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) v[j][b + t] = s - 2.f * v[j][b + t];
+    }
+    // d1: element bit 2 in registers, lane bit 0 across the pair of lanes
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float p = v[j][t] + v[j][t + 4];
+      const float s = p + __shfl_xor_sync(0xffffffffu, p, 1);
+      v[j][t] = s - 2.f * v[j][t];
+      v[j][t + 4] = s - 2.f * v[j][t + 4];
+    }
+    // d2: lane bits 1-2; d3: lane bits 3-4
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float p = v[j][e] + __shfl_xor_sync(0xffffffffu, v[j][e], 2);
+      const float s = p + __shfl_xor_sync(0xffffffffu, p, 4);
+      v[j][e] = s - 2.f * v[j][e];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float p = v[j][e] + __shfl_xor_sync(0xffffffffu, v[j][e], 8);
+      const float s = p + __shfl_xor_sync(0xffffffffu, p, 16);
+      v[j][e] = (s - 2.f * v[j][e]) * 0.0625f;
+      amax = fmaxf(amax, fabsf(v[j][e]));
+    }
+  }
+  amax = block_max(amax);
+  const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+  if (threadIdx.x == 0) scale[r] = s;
+  int8_t* qr = q + r * ldq;
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const int g = warp + WARPS * j;
+    if (g >= groups) continue;
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float c = fminf(fmaxf(rintf(__fdiv_rn(v[j][e], s)), -127.f), 127.f);
+      packed[e >> 2] |= (uint32_t)(static_cast<int>(c) & 0xFF) << (8 * (e & 3));
+    }
+    reinterpret_cast<uint2*>(qr + ((long long)g << 8))[lane] = make_uint2(packed[0], packed[1]);
+  }
+}
+
 }  // namespace quant
 }  // namespace vdn
 
@@ -196,6 +278,36 @@ int vdn_quant_int8_rows_amax(const void* x, long long ldx, int rows, int K, cons
   const dim3 grid((unsigned)rows, (unsigned)((K / 8 + 255) / 256));
   vdn::quant::int8_rows_amax_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(x), ldx, K, amax, reinterpret_cast<int8_t*>(q), ldq, scale);
+  vdn::count_launch();
+  return vdn::launch_status();
+}
+
+// ConvRot int8 rows (group 256): rotate each 256-wide group of a bf16 row, then per-row
+// symmetric int8 as vdn_quant_int8_rows.  K % 256 == 0, K <= 32768; x rows 16-byte aligned,
+// q rows 8-byte aligned.
+int vdn_quant_int8_rows_convrot(const void* x, long long ldx, int rows, int K, int group, void* q, long long ldq,
+                                float* scale, void* stream) {
+  if (!x || !q || !scale || rows < 0 || K <= 0) return vdn::kBadArgument;
+  if (group != 256 || K % 256 || K > 32768) return vdn::kUnsupported;
+  if (!vdn::aligned16(x) || (ldx * 2) % 16 || (reinterpret_cast<uintptr_t>(q) & 7) || ldq % 8)
+    return vdn::kMisaligned;
+  if (rows == 0) return vdn::kOk;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  const auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  const auto qb = reinterpret_cast<int8_t*>(q);
+  const int groups = K / 256;
+  if (groups <= 8)
+    vdn::quant::int8_rows_convrot_kernel<1, 8><<<rows, 256, 0, s>>>(xb, ldx, K, qb, ldq, scale);
+  else if (groups <= 16)
+    vdn::quant::int8_rows_convrot_kernel<2, 8><<<rows, 256, 0, s>>>(xb, ldx, K, qb, ldq, scale);
+  else if (groups <= 24)
+    vdn::quant::int8_rows_convrot_kernel<3, 8><<<rows, 256, 0, s>>>(xb, ldx, K, qb, ldq, scale);
+  else if (groups <= 32)
+    vdn::quant::int8_rows_convrot_kernel<4, 8><<<rows, 256, 0, s>>>(xb, ldx, K, qb, ldq, scale);
+  else if (groups <= 64)
+    vdn::quant::int8_rows_convrot_kernel<2, 32><<<rows, 1024, 0, s>>>(xb, ldx, K, qb, ldq, scale);
+  else
+    vdn::quant::int8_rows_convrot_kernel<4, 32><<<rows, 1024, 0, s>>>(xb, ldx, K, qb, ldq, scale);
   vdn::count_launch();
   return vdn::launch_status();
 }

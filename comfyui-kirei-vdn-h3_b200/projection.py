@@ -6,7 +6,10 @@ quantised ``to_out_linear.weight_fp8`` with ``to_out_linear.weight_scale`` runs 
 e4m3 (per-tensor) or int8 (per-output-channel weight, per-token activation) GEMM with
 the dequantisation fused into the epilogue.  ``prepare_projection_maps`` builds those
 quantised masters (fp8.py:168-222, projection.py:139-232); the int8 scheme is the
-config-2 one (symmetric, round-half-even, fp32 scales), not comfy-kitchen's ConvRot.
+config-2 one (symmetric, round-half-even, fp32 scales) unless ``convrot=True`` asks for
+ConvRot (projection.py:74-97, :243-256): both operands rotated per group of 256 channels
+by a regular Hadamard matrix before the same per-row quantisation; such a map carries
+``to_out_linear.convrot_groupsize`` and ``project`` rotates the activations to match.
 """
 
 from __future__ import annotations
@@ -24,6 +27,8 @@ PROJECTION_PRECISIONS = ("bf16", "fp8", "int8")
 DEFAULT_FP8_SKIP_END_BLOCKS = 4  # fp8.py:35
 
 KIND = {"bf16": 0, "fp8": 1, "int8": 2}
+CONVROT_GROUP = 256  # projection.py:44 (INT8_CONVROT_GROUP)
+CONVROT_KEY = "to_out_linear.convrot_groupsize"
 
 
 @dataclass
@@ -56,6 +61,26 @@ def quantize_rows_int8(x: torch.Tensor, out: QuantizedMatrix | None = None) -> Q
     return out
 
 
+def quantize_rows_int8_convrot(x: torch.Tensor, out: QuantizedMatrix | None = None,
+                               group: int = CONVROT_GROUP) -> QuantizedMatrix:
+    """ConvRot int8 of a [rows, K] tensor (its bf16 copy): every 256-channel group of a row
+    rotated by R/16 (R the fourth Kronecker power of the regular Hadamard J - 2I), then the
+    per-row rule of ``quantize_rows_int8``.  Rows are tokens for activations and output
+    channels for weights (projection.py:74-97: the weight is quantised from bf16)."""
+    _lib.require_cuda(x)
+    if x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    rows, K = x.shape
+    if out is None:
+        out = QuantizedMatrix(torch.empty(rows, K, device=x.device, dtype=torch.int8),
+                              torch.empty(rows, device=x.device, dtype=torch.float32), "int8")
+    _lib.call("vdn_quant_int8_rows_convrot", x.data_ptr(), x.stride(0), rows, K, int(group),
+              out.data.data_ptr(), out.data.stride(0), out.scale.data_ptr(), _stream(x))
+    return out
+
+
 def quantize_tensor_fp8(x: torch.Tensor, out: QuantizedMatrix | None = None,
                         work: torch.Tensor | None = None, amax_reduce=None) -> QuantizedMatrix:
     """Per-tensor e4m3 of a bf16/fp32 [rows, K] tensor (fp8.py:99-133, per_tensor=True).
@@ -84,7 +109,9 @@ def quantize_tensor_fp8(x: torch.Tensor, out: QuantizedMatrix | None = None,
     return out
 
 
-def quantize_weight(w: torch.Tensor, precision: str, device) -> QuantizedMatrix:
+def quantize_weight(w: torch.Tensor, precision: str, device, *, convrot: bool = False) -> QuantizedMatrix:
+    if precision == "int8" and convrot:
+        return quantize_rows_int8_convrot(w.detach().to(device=device, dtype=torch.bfloat16).contiguous())
     w = w.detach().to(device=device, dtype=torch.float32).contiguous()
     if precision == "int8":
         return quantize_rows_int8(w)
@@ -152,16 +179,24 @@ def project(rows: torch.Tensor, weights) -> torch.Tensor:
     q = weights[QUANT_WEIGHT_KEY].to(x.device)
     s = weights[QUANT_SCALE_KEY].to(device=x.device, dtype=torch.float32).reshape(-1).contiguous()
     if q.dtype == torch.int8:
-        xa = quantize_rows_int8(x)
+        group = weights.get(CONVROT_KEY)
+        if group is not None:
+            xa = quantize_rows_int8_convrot(x, group=int(group))
+        else:
+            xa = quantize_rows_int8(x)
         return gemm(xa.data, q.contiguous(), row_scale=xa.scale, col_scale=s, kind=2).to(rows.dtype)
     xa = quantize_tensor_fp8(x)
     return gemm(xa.data, q.contiguous(), dev_scale0=xa.scale, dev_scale1=s, kind=1).to(rows.dtype)
 
 
-def prepare_projection_maps(branch_maps, device, precision, *, skip_end_blocks=None):
-    """Quantised ``to_out_linear`` masters per block; edge blocks stay bf16 (fp8.py:168-222)."""
+def prepare_projection_maps(branch_maps, device, precision, *, skip_end_blocks=None, convrot=False):
+    """Quantised ``to_out_linear`` masters per block; edge blocks stay bf16 (fp8.py:168-222).
+    ``convrot=True`` (int8 only) quantises with ConvRot where K % 256 == 0, as
+    projection.py:74-86 does, and marks such a map with ``to_out_linear.convrot_groupsize``."""
     if precision not in PROJECTION_PRECISIONS:
         raise ValueError(f"unknown VDN projection precision {precision!r}")
+    if convrot and precision != "int8":
+        raise ValueError("ConvRot applies to int8 projections only")
     if precision == "bf16":
         return tuple(dict(b) for b in branch_maps), None
     skip = (DEFAULT_FP8_SKIP_END_BLOCKS if precision == "fp8" else 0) if skip_end_blocks is None else int(skip_end_blocks)
@@ -171,20 +206,30 @@ def prepare_projection_maps(branch_maps, device, precision, *, skip_end_blocks=N
     if skip and skip * 2 >= count:
         raise ValueError(f"skip_end_blocks={skip} leaves no quantised interior blocks for {count} branches")
     out = []
+    used_convrot = True
     for i, block in enumerate(branch_maps):
         if BF16_WEIGHT_KEY not in block:
             raise KeyError(f"VDN block {i} has no {BF16_WEIGHT_KEY!r}")
         if i < skip or i >= count - skip:
             out.append(dict(block))
             continue
-        qm = quantize_weight(block[BF16_WEIGHT_KEY], precision, device)
+        w = block[BF16_WEIGHT_KEY]
+        use_convrot = bool(convrot) and precision == "int8" and w.shape[1] % CONVROT_GROUP == 0
+        used_convrot = used_convrot and use_convrot
+        qm = quantize_weight(w, precision, device, convrot=use_convrot)
         copied = dict(block)
         copied.pop(BF16_WEIGHT_KEY)
         copied[QUANT_WEIGHT_KEY] = qm.data
         copied[QUANT_SCALE_KEY] = qm.scale.reshape(1, 1) if precision == "fp8" else qm.scale
+        if use_convrot:
+            copied[CONVROT_KEY] = torch.tensor(CONVROT_GROUP, dtype=torch.int32)
         out.append(copied)
-    return tuple(out), {"precision": precision, "skip_end_blocks": skip}
+    info = {"precision": precision, "skip_end_blocks": skip}
+    if precision == "int8":
+        info.update(convrot=bool(convrot) and used_convrot, convrot_groupsize=CONVROT_GROUP)
+    return tuple(out), info
 
 
-__all__ = ["PROJECTION_PRECISIONS", "QuantizedMatrix", "gemm", "prepare_projection_maps", "project",
-           "quantize_rows_int8", "quantize_tensor_fp8", "quantize_weight"]
+__all__ = ["CONVROT_GROUP", "CONVROT_KEY", "PROJECTION_PRECISIONS", "QuantizedMatrix", "gemm",
+           "prepare_projection_maps", "project", "quantize_rows_int8", "quantize_rows_int8_convrot",
+           "quantize_tensor_fp8", "quantize_weight"]

@@ -75,6 +75,18 @@ int vdn_qkv_gemm(int kind, const void* x, long long ldx, const void* w, long lon
 int vdn_quant_int8_rows(int src_kind, const void* x, long long ldx, int rows, int K, void* q, long long ldq,
                         float* scale, void* stream);
 
+/* ConvRot int8 rows: each 256-wide group of a bf16 row [rows, K] is rotated by R/16, R the
+ * fourth Kronecker power of the order-4 regular Hadamard matrix J - 2I (symmetric and
+ * orthogonal up to 1/16), then quantised per row as vdn_quant_int8_rows.  Applied to the
+ * activation rows and to the weight rows alike, it leaves x W^T unchanged.  group must be
+ * 256; K % 256 == 0, K <= 32768; 16-byte aligned x rows, 8-byte aligned q rows.
+ * Replaces: the ConvRot rotation + TensorWiseINT8 quantisation that comfy-kitchen's
+ * ck.int8_linear / QuantizedTensor.from_float(convrot=True, convrot_groupsize=256) perform
+ * for projection.py:74-97 and :243-256 (comfy-kitchen is outside the reference tree, so its
+ * exact Hadamard ordering and activation scaling are not pinned). */
+int vdn_quant_int8_rows_convrot(const void* x, long long ldx, int rows, int K, int group, void* q, long long ldq,
+                                float* scale, void* stream);
+
 /* Per-tensor e4m3 (scale = max(amax/448, 1e-12)); work: one fp32 device scalar.
  * Replaces: fp8.py:108-133 (quantize_activation, per_tensor=True). */
 int vdn_quant_fp8_tensor(int src_kind, const void* x, long long ldx, int rows, int K, void* q, long long ldq,

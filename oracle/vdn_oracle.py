@@ -16,7 +16,9 @@ imported read-only where it is mounted) on seeded config-0 inputs and stores the
 under ``tests/golden/``; ``tests/test_oracle_golden.py`` checks this module against them.
 Parity unpinned for RoPE (``rope_split_half``): the reference hands it to comfy-kitchen's
 ``rms_rope_split_half_``, which is absent from the reference tree and this image; the
-restatement follows ComfyUI's published freqs convention (see the function).
+restatement follows ComfyUI's published freqs convention (see the function).  Parity
+unpinned for ConvRot int8 (``convrot_rotate``): the reference hands it to comfy-kitchen too;
+the restatement follows the published ConvRot method with one fixed Hadamard construction.
 """
 
 from __future__ import annotations
@@ -461,6 +463,56 @@ def int8_quantize_rows(x) -> tuple[torch.Tensor, torch.Tensor]:
     return _int8_rows_np(_t(x).to(torch.float32).numpy())
 
 
+CONVROT_GROUP = 256  # projection.py:44 (INT8_CONVROT_GROUP)
+
+
+def convrot_rotate(x, group: int = CONVROT_GROUP) -> np.ndarray:
+    """ConvRot's group-wise rotation of the rows of ``x`` [rows, K], in IEEE fp32.
+
+    The reference hands the rotation to comfy-kitchen (``QuantizedTensor.from_float(...,
+    convrot=True, convrot_groupsize=256)`` and ``ck.int8_linear(..., convrot=True)``,
+    projection.py:74-97 and :243-256); comfy-kitchen is not in the reference tree, so this
+    restates the published ConvRot method (a block-diagonal regular Hadamard rotation over
+    groups of ``group`` channels) with one fixed construction: each group is multiplied by
+    R / sqrt(group), R the Kronecker power of the order-4 regular Hadamard matrix J - 2I.
+    Parity against comfy-kitchen is unpinned (its matrix ordering is not visible here).
+
+    Evaluation order (the CUDA quantiser follows it exactly): the group index is written in
+    base 4, digits d0 (least significant) to dn; for each digit in that order every quadruple
+    of elements that differ only in that digit becomes y = S - 2 x with
+    S = (x[d=0] + x[d=1]) + (x[d=2] + x[d=3]); the result is scaled by 1 / sqrt(group).
+    """
+    x32 = np.ascontiguousarray(_t(x).to(torch.float32).numpy())
+    rows, K = x32.shape
+    digits = int(round(math.log(group, 4)))
+    if 4 ** digits != group or K % group:
+        raise ValueError("ConvRot needs a group that is a power of 4 dividing K")
+    v = x32.reshape(rows, K // group, *([4] * digits))  # last axis = d0
+    for axis in range(v.ndim - 1, 1, -1):
+        a = [np.take(v, t, axis=axis) for t in range(4)]
+        s = np.expand_dims((a[0] + a[1]) + (a[2] + a[3]), axis)
+        v = s - np.float32(2.0) * v
+    v = v * np.float32(1.0 / math.sqrt(group))
+    return v.reshape(rows, K).astype(np.float32)
+
+
+def int8_quantize_rows_convrot(x, group: int = CONVROT_GROUP) -> tuple[torch.Tensor, torch.Tensor]:
+    """ConvRot int8 rows: the fp32 rotation above of the bf16 rows, then the per-row int8 rule
+    of ``_int8_rows_np`` (weights: per output channel, the reference quantises their bf16
+    copy, projection.py:84; activations: per token)."""
+    xb = _t(x).to(torch.bfloat16).to(torch.float32)
+    return _int8_rows_np(convrot_rotate(xb, group))
+
+
+def project_int8_convrot(rows, w, group: int = CONVROT_GROUP):
+    """``rows @ W^T`` through ConvRot int8 (projection.py:243-256): both operands rotated per
+    group, quantised per row, exact integer accumulate, dequantised by the two scales."""
+    qa, sa = int8_quantize_rows_convrot(rows, group)
+    qw, sw = int8_quantize_rows_convrot(w, group)
+    acc = int8_accumulate(qa, qw).to(_COMPUTE[0])
+    return acc * sa.to(_COMPUTE[0])[:, None] * sw.to(_COMPUTE[0])[None, :]
+
+
 def int8_accumulate(qa: torch.Tensor, qw: torch.Tensor) -> torch.Tensor:
     """Exact int32 accumulator of int8 operands, computed in int64 then checked to fit."""
     acc = qa.to(torch.int64) @ qw.to(torch.int64).T
@@ -566,7 +618,7 @@ def block_forward(x, bw: BlockWeights, lay: Layout, heads, dim, cfg: BranchConfi
 
 
 # ---------------------------------------------------------------------------------------
-# Seeded synthetic inputs (SURVEY-free restatement of the shapes)
+# Seeded synthetic inputs (the benchmark configs' shapes and value distributions)
 # ---------------------------------------------------------------------------------------
 
 def make_branch_weights(gen, hidden, heads, dim, *, std=0.02, kernel=5, gate=True,

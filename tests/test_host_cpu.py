@@ -288,3 +288,8 @@ def test_status_codes_map_to_reference_exceptions():
     with pytest.raises(RuntimeError):
         pkg._lib.check(-3, "x")
     pkg._lib.check(0, "x")
+
+
+def test_convrot_is_an_int8_option_only():
+    with pytest.raises(ValueError, match="int8"):
+        pkg.prepare_projection_maps([{"to_out_linear.weight": torch.zeros(8, 256)}], "cpu", "fp8", convrot=True)

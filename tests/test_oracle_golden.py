@@ -167,3 +167,43 @@ def test_int8_scheme_is_exact_integer_arithmetic():
     exact = x.double() @ w.double().T
     rel = (approx - exact).norm() / exact.norm()
     assert rel < 2e-2
+
+
+def test_convrot_rotation_is_the_regular_hadamard_group_rotation():
+    """ConvRot (projection.py:74-97, :243-256; comfy-kitchen, unpinned): the staged fp32
+    rotation equals the explicit block-diagonal R/16, R = (J - 2I)^(x4), which is symmetric
+    and orthogonal, so rotating both operands leaves x W^T unchanged."""
+    r4 = np.ones((4, 4)) - 2 * np.eye(4)
+    r = r4
+    for _ in range(3):
+        r = np.kron(r, r4)
+    h = r / 16
+    assert np.allclose(h, h.T) and np.allclose(h @ h, np.eye(256))
+    assert np.allclose(h.sum(axis=1), h[0].sum())  # regular: equal row sums
+    gen = torch.Generator().manual_seed(5)
+    x = torch.randn(9, 768, generator=gen)
+    w = torch.randn(11, 768, generator=gen)
+    xr = vo.convrot_rotate(x)
+    blocks = [x.double().numpy()[:, g * 256:(g + 1) * 256] @ h for g in range(3)]
+    np.testing.assert_allclose(xr, np.concatenate(blocks, 1), rtol=0, atol=2e-6)
+    wr = vo.convrot_rotate(w)
+    np.testing.assert_allclose(xr.astype(np.float64) @ wr.astype(np.float64).T,
+                               x.double().numpy() @ w.double().numpy().T, rtol=0, atol=2e-4)
+    with pytest.raises(ValueError):
+        vo.convrot_rotate(torch.zeros(2, 320))
+
+
+def test_convrot_int8_is_exact_integer_arithmetic_and_beats_plain_on_outliers():
+    gen = torch.Generator().manual_seed(6)
+    x = torch.randn(64, 1024, generator=gen)
+    x[:, 3] *= 200
+    x = x.to(torch.bfloat16).float()
+    w = torch.randn(48, 1024, generator=gen) * 0.02
+    qa, sa = vo.int8_quantize_rows_convrot(x)
+    qw, sw = vo.int8_quantize_rows_convrot(w)
+    assert qa.dtype == torch.int8 and int(qa.abs().max()) == 127
+    assert torch.equal(vo.int8_accumulate(qa, qw).double(), qa.double() @ qw.double().T)
+    exact = x.double() @ w.double().T
+    e_rot = float((vo.project_int8_convrot(x, w) - exact).norm() / exact.norm())
+    e_plain = float((vo.project(x, w, "int8") - exact).norm() / exact.norm())
+    assert e_rot < 0.5 * e_plain
