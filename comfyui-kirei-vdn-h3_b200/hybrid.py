@@ -34,7 +34,8 @@ import torch
 from . import _lib
 from .branch import DELTA_RULES, BranchDeviceWeights, BranchWorkspace, cholesky_runtime_scope, run_branch
 from .layout import VDNLayout, current_layout
-from .projection import KIND, QuantizedMatrix, quantize_rows_int8, quantize_tensor_fp8, quantize_weight
+from .projection import (CONVROT_KEY, KIND, QuantizedMatrix, dequantize_projection_weight, quantize_rows_int8,
+                         quantize_rows_int8_convrot, quantize_tensor_fp8, quantize_weight)
 from .shard import (HeadShard, RowExchange, concat_rows, default_shard, qkv_row_index, rank_major_out_weight,
                     slice_branch_weights, split_heads_outputs)
 from .window import ATTENTION_BACKENDS, WindowPlanCache, launch_window_attention
@@ -225,6 +226,23 @@ class FusedBlock:
         to_out = branch_w.get("to_out_linear.weight")
         if to_out is not None and not self.has_branch:
             to_out = None
+        # a stored quantised master (the reference's storage of fp8 / int8 projections,
+        # fp8.py:168-222, projection.py:139-232): used as is when it is this block's
+        # precision, else dequantised here once (a ConvRot master rotated back)
+        to_out_q = None
+        self.to_out_convrot = None
+        if to_out is None and "to_out_linear.weight_fp8" in branch_w:
+            stored = branch_w["to_out_linear.weight_fp8"]
+            stored_scale = branch_w["to_out_linear.weight_scale"]
+            group = branch_w.get(CONVROT_KEY)
+            group = None if group is None else int(group)
+            stored_prec = "int8" if stored.dtype == torch.int8 else "fp8"
+            if stored_prec == precision and (stored_prec == "int8" or (group is None and stored_scale.numel() == 1)):
+                to_out_q = QuantizedMatrix(stored.detach().to(dev).contiguous(),
+                                           f32(stored_scale).reshape(-1).contiguous(), precision)
+                self.to_out_convrot = group
+            else:
+                to_out = dequantize_projection_weight(stored, stored_scale, group)
         if precision == "bf16":
             self.w_big = torch.cat([b16(qkv_w[qkv_rows]), side_w.to(dev, torch.bfloat16)], 0).contiguous()
             if shard is not None:
@@ -247,7 +265,8 @@ class FusedBlock:
             self.w_qkv_q = wq
             self.w_side = side_w.to(dev, torch.bfloat16).contiguous()
             self.w_out_q = quantize_weight(out_w, precision, dev)
-            self.w_to_q = quantize_weight(to_out, precision, dev) if to_out is not None else None
+            self.w_to_q = to_out_q if to_out_q is not None else (
+                quantize_weight(to_out, precision, dev) if to_out is not None else None)
         self.bw = BranchDeviceWeights.from_dict(wl, H, D, dev, short_conv=self.short_conv) if self.has_branch \
             else None
         # blocks of one model run one after another on one stream: they may share workspaces
@@ -360,13 +379,14 @@ class FusedBlock:
         rows = flat.shape[0]
         K = flat.shape[1]
 
-        def quantized_gemm(src, buf: QuantizedMatrix, w: QuantizedMatrix, addend, first):
+        def quantized_gemm(src, buf: QuantizedMatrix, w: QuantizedMatrix, addend, first, convrot=None):
             if rows == 0 and self.precision == "int8":
                 return  # per-row scales: nothing to combine across ranks
             buf = QuantizedMatrix(buf.data[:rows], buf.scale[:rows] if self.precision == "int8" else buf.scale,
                                   self.precision)
             if self.precision == "int8":
-                qa = quantize_rows_int8(src, buf)
+                qa = quantize_rows_int8(src, buf) if convrot is None else \
+                    quantize_rows_int8_convrot(src, buf, group=convrot)
                 rs, cs, d0, d1 = qa.scale, w.scale, None, None
             else:
                 qa = quantize_tensor_fp8(src, buf, ws["work"], amax_reduce=amax_reduce)
@@ -381,7 +401,7 @@ class FusedBlock:
 
         quantized_gemm(flat, ws["fq"], self.w_out_q, None, True)
         if branch is not None and self.w_to_q is not None:
-            quantized_gemm(branch, ws["bq"], self.w_to_q, out, False)
+            quantized_gemm(branch, ws["bq"], self.w_to_q, out, False, self.to_out_convrot)
 
     def project_rows(self, ws, with_branch, recv, rows, out_rows, status, stream, amax_reduce=None,
                      residual: GatedResidual | None = None):

@@ -14,6 +14,7 @@ by a regular Hadamard matrix before the same per-row quantisation; such a map ca
 
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 import torch
@@ -118,6 +119,38 @@ def quantize_weight(w: torch.Tensor, precision: str, device, *, convrot: bool = 
     if precision == "fp8":
         return quantize_tensor_fp8(w)
     raise ValueError(f"unknown quantised precision {precision!r}")
+
+
+def convrot_matrix(group: int = CONVROT_GROUP) -> torch.Tensor:
+    """The ConvRot group rotation R / sqrt(group) (float64, symmetric, its own inverse), R the
+    Kronecker power of the order-4 regular Hadamard matrix J - 2I."""
+    r4 = torch.ones(4, 4, dtype=torch.float64) - 2 * torch.eye(4, dtype=torch.float64)
+    r = torch.ones(1, 1, dtype=torch.float64)
+    while r.shape[0] < group:
+        r = torch.kron(r, r4)
+    if r.shape[0] != group:
+        raise ValueError("ConvRot group must be a power of 4")
+    return r / math.sqrt(group)
+
+
+def dequantize_projection_weight(q: torch.Tensor, scale: torch.Tensor, convrot_group=None) -> torch.Tensor:
+    """float32 [N, K] weight of a stored quantised ``to_out_linear`` master: int8 codes times
+    their per-channel scale, or e4m3 codes times a per-tensor ([1, 1]) or per-channel ([1, N],
+    fp8.py:88-96) scale; a ConvRot master is rotated back (the rotation is its own inverse).
+    Setup-time only, on the host."""
+    w = q.detach().to("cpu").to(torch.float64)
+    s = scale.detach().to("cpu", torch.float64).reshape(-1)
+    if s.numel() == 1:
+        w = w * s[0]
+    elif s.numel() == w.shape[0]:
+        w = w * s[:, None]
+    else:
+        raise ValueError("quantised projection scale matches neither the tensor nor its rows")
+    if convrot_group is not None:
+        g = int(convrot_group)
+        n, k = w.shape
+        w = (w.reshape(n, k // g, g) @ convrot_matrix(g)).reshape(n, k)
+    return w.to(torch.float32)
 
 
 def gemm(a, b, *, out=None, out_dtype=torch.bfloat16, alpha=1.0, a2=None, k_split=None, row_scale=None,
@@ -230,6 +263,7 @@ def prepare_projection_maps(branch_maps, device, precision, *, skip_end_blocks=N
     return tuple(out), info
 
 
-__all__ = ["CONVROT_GROUP", "CONVROT_KEY", "PROJECTION_PRECISIONS", "QuantizedMatrix", "gemm",
+__all__ = ["CONVROT_GROUP", "CONVROT_KEY", "PROJECTION_PRECISIONS", "QuantizedMatrix", "convrot_matrix",
+           "dequantize_projection_weight", "gemm",
            "prepare_projection_maps", "project", "quantize_rows_int8", "quantize_rows_int8_convrot",
            "quantize_tensor_fp8", "quantize_weight"]

@@ -563,12 +563,14 @@ class BlockWeights:
 
 def block_forward(x, bw: BlockWeights, lay: Layout, heads, dim, cfg: BranchConfig,
                   *, enable_softmax_gate=True, linear_enabled=True, precision="bf16",
-                  return_parts=False, rope_freqs=None):
+                  return_parts=False, rope_freqs=None, to_out_convrot=False):
     """VDN hybrid block forward: QKV, branch on raw video q/k/v, q/k RMSNorm, window
     softmax, per-token head gate, out_proj, delta add on video rows (hybrid.py:409-579).
 
     ``precision`` selects the projection arithmetic of qkv/out_proj/to_out_linear
     (``bf16`` = exact float64 here; ``int8``/``fp8`` = the config-2 quantised schemes).
+    ``to_out_convrot`` (int8 only): ``to_out_linear`` through ConvRot int8 instead, the
+    reference's INT8 projection (projection.py:243-256).
     """
     x = _t(x)
     seq = x.shape[0]
@@ -591,7 +593,10 @@ def block_forward(x, bw: BlockWeights, lay: Layout, heads, dim, cfg: BranchConfi
             text_x=x[ta:tb] if text else None, text_k=k_raw[ta:tb] if text else None,
             text_v=v[ta:tb] if text else None, skip_ends=(lay.anchor_frames == "both"),
         )
-        delta = project(readout, w["to_out_linear.weight"], precision)
+        if to_out_convrot and precision == "int8":
+            delta = project_int8_convrot(readout, w["to_out_linear.weight"])
+        else:
+            delta = project(readout, w["to_out_linear.weight"], precision)
         parts["readout"] = readout
     qn = rms_norm(q_raw, bw.q_norm, 1e-6)
     kn = rms_norm(k_raw, bw.k_norm, 1e-6)

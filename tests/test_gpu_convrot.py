@@ -82,3 +82,66 @@ def test_convrot_rejects_unsupported_widths():
     x = torch.zeros(4, 320, device=DEV, dtype=torch.bfloat16)  # 320 % 256 != 0
     with pytest.raises(ValueError):
         pkg.quantize_rows_int8_convrot(x)
+
+
+# ------------------------------------------------------------------ the block with stored masters
+def _block_case():
+    c = dict(vo.CONFIG0, heads=2, dim=128)
+    bw = vo.make_block(3, c["hidden"], c["heads"], c["dim"])
+    lay_o = vo.config_layout(c)
+    x = vo.make_x(3, lay_o.seq_len, c["hidden"]).to(torch.bfloat16).float()
+    return c, bw, lay_o, x
+
+
+def _run_block_maps(bw, maps, c, x, precision):
+    from __graft_entry__ import _Attn
+
+    state = pkg.B200State("t", {"enable_softmax_gate": True}, [bw.branch], c["heads"], c["dim"],
+                          projection_precision=precision, weight_maps=maps)
+    fwd = pkg.make_vdn_forward(_Attn(bw, c["heads"], c["dim"]), state, 0)
+    with pkg.publish_layout(pkg.make_layout(c["text"], c["frames"], c["grid"])):
+        out = pkg.run_forward_checked(state, fwd, x.to(DEV, torch.bfloat16))
+    torch.cuda.synchronize()
+    return out
+
+
+def test_int8_block_runs_a_convrot_to_out_master_as_stored():
+    """The reference's INT8 storage of to_out_linear (int8 codes + per-channel scales, ConvRot,
+    projection.py:139-206) consumed by the int8 block: branch rows quantised with ConvRot."""
+    c, bw, lay_o, x = _block_case()
+    maps, _ = pkg.prepare_projection_maps([bw.branch], DEV, "int8", convrot=True)
+    assert "to_out_linear.weight" not in maps[0]
+    got = _run_block_maps(bw, maps, c, x, "int8")
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(), precision="int8",
+                            to_out_convrot=True)
+    exact = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig())
+    assert rel_l2(got, want) < 2e-2
+    assert rel_l2(got, exact) < 3e-2
+
+
+@pytest.mark.parametrize("stored", ["int8_convrot", "fp8"])
+def test_bf16_block_dequantises_a_stored_master(stored):
+    """A bf16 block given a quantised to_out_linear master runs its dequantised weight (the
+    branch delta is as large as the output at this size, so dropping it would show)."""
+    c, bw, lay_o, x = _block_case()
+    prec = "int8" if stored.startswith("int8") else "fp8"
+    maps, _ = pkg.prepare_projection_maps([bw.branch], DEV, prec, skip_end_blocks=0,
+                                          convrot=stored == "int8_convrot")
+    m = maps[0]
+    w_deq = pkg.projection.dequantize_projection_weight(m["to_out_linear.weight_fp8"], m["to_out_linear.weight_scale"],
+                                                        m.get(pkg.projection.CONVROT_KEY))
+    got = _run_block_maps(bw, maps, c, x, "bf16")
+    bw_deq = vo.BlockWeights(bw.qkv, bw.q_norm, bw.k_norm, bw.out, dict(bw.branch, **{"to_out_linear.weight": w_deq}))
+    want = vo.block_forward(x, bw_deq, lay_o, c["heads"], c["dim"], vo.BranchConfig())
+    assert rel_l2(got, want) < 2e-2
+    # the dequantised master is the original weight to within its quantisation step
+    w = bw.branch["to_out_linear.weight"].double()
+    assert rel_l2(w_deq, w) < 3e-2
+
+
+def test_fp8_block_runs_a_per_tensor_master_as_stored():
+    c, bw, lay_o, x = _block_case()
+    maps, _ = pkg.prepare_projection_maps([bw.branch], DEV, "fp8", skip_end_blocks=0)
+    got = _run_block_maps(bw, maps, c, x, "fp8")
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(), precision="fp8")
+    assert rel_l2(got, want) < 3e-2
