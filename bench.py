@@ -321,6 +321,40 @@ def run_attention_only(args, c):
                       pk["bf16_tflops"], "peak_source": src}), flush=True)
 
 
+def run_quantisers_only(args, c):
+    """The int8 row quantisers alone on the config's branch rows x hidden (bf16, larger than
+    L2): plain per-row int8 and ConvRot int8 (group-256 rotation in the same pass), each with
+    its algorithmic bytes (2 B read + 1 B written per element, 4 B of scale per row) over its
+    CUDA-event time, against the measured HBM copy bandwidth."""
+    from __graft_entry__ import load_package
+
+    pkg = load_package()
+    dev = torch.device("cuda", 0)
+    rows = (c["frames"] - 2) * c["grid"][0] * c["grid"][1]
+    K = c["heads"] * c["dim"]
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(rows, K, generator=g).to(dev, torch.bfloat16)
+    out = pkg.projection.QuantizedMatrix(torch.empty(rows, K, device=dev, dtype=torch.int8),
+                                         torch.empty(rows, device=dev, dtype=torch.float32), "int8")
+    pk, src = peaks()
+    algo = rows * K * 3 + rows * 4
+    for name, fn in (("int8_rows_vec_kernel", pkg.quantize_rows_int8),
+                     ("int8_rows_convrot_kernel", pkg.quantize_rows_int8_convrot)):
+        for _ in range(args.warmup):
+            fn(x, out)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn(x, out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / max(args.steps, 1)
+        gbs = algo / (ms * 1e-3) / 1e9
+        print(json.dumps({"kernel": name, "rows": rows, "K": K, "ms": ms, "algorithmic_bytes": algo,
+                          "gbs": gbs, "frac_of_hbm": gbs / pk["hbm_gbs"], "peak_source": src}), flush=True)
+
+
 def run_dit_stack(args, c, world, rank, local):
     """Config 4: the denoiser forward stack of ``blocks`` DiT blocks (hybrid attention + GELU MLP,
     INT8 projections) over a CFG batch of 2 latent sequences; one step = one sampler step
@@ -460,7 +494,7 @@ def main():
     ap.add_argument("--impl", default="b200")
     ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["attention"], default=None,
+    ap.add_argument("--only", choices=["attention", "quantisers"], default=None,
                     help="run one kernel alone on the config geometry (profiling small cases)")
     ap.add_argument("--heads", type=int, default=None, help="override the head count (profiling small cases)")
     ap.add_argument("--blocks", type=int, default=None, help="config 4: number of DiT blocks (default 50)")
@@ -476,6 +510,9 @@ def main():
         c["heads"] = args.heads
     if args.only == "attention":
         run_attention_only(args, c)
+        return
+    if args.only == "quantisers":
+        run_quantisers_only(args, c)
         return
     if args.config == 4 and args.impl != "reference":
         run_dit_stack(args, c, world, rank, local)
