@@ -293,3 +293,27 @@ def test_status_codes_map_to_reference_exceptions():
 def test_convrot_is_an_int8_option_only():
     with pytest.raises(ValueError, match="int8"):
         pkg.prepare_projection_maps([{"to_out_linear.weight": torch.zeros(8, 256)}], "cpu", "fp8", convrot=True)
+
+
+@pytest.mark.parametrize("convrot", [False, True])
+def test_stored_int8_master_dequantises_to_the_weight(convrot):
+    """A stored int8 to_out_linear master (plain or ConvRot codes, per-channel scales) turns back
+    into the weight within int8 resolution; the ConvRot rotation is its own inverse."""
+    gen = torch.Generator().manual_seed(9)
+    w = torch.randn(48, 512, generator=gen) * 0.02
+    q, s = vo.int8_quantize_rows_convrot(w) if convrot else vo.int8_quantize_weight(w)
+    deq = pkg.projection.dequantize_projection_weight(q, s, 256 if convrot else None)
+    assert deq.shape == w.shape and deq.dtype == torch.float32
+    assert float((deq - w).norm() / w.norm()) < 1.5e-2
+    h = pkg.projection.convrot_matrix(256)
+    assert torch.allclose(h, h.T) and torch.allclose(h @ h, torch.eye(256, dtype=torch.float64))
+    assert torch.allclose(h, torch.from_numpy(vo.convrot_rotate(torch.eye(256))).double(), atol=1e-7)
+
+
+def test_stored_fp8_master_scales_per_tensor_or_per_channel():
+    q = torch.ones(4, 16).to(torch.float8_e4m3fn)
+    assert torch.equal(pkg.projection.dequantize_projection_weight(q, torch.tensor([[0.5]])), torch.full((4, 16), 0.5))
+    per_ch = pkg.projection.dequantize_projection_weight(q, torch.tensor([[1.0, 2.0, 3.0, 4.0]]))
+    assert torch.equal(per_ch[:, 0], torch.tensor([1.0, 2.0, 3.0, 4.0]))
+    with pytest.raises(ValueError):
+        pkg.projection.dequantize_projection_weight(q, torch.ones(3))
