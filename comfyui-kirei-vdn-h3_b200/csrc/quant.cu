@@ -32,6 +32,18 @@ __device__ __forceinline__ float block_max(float v) {
   return r;
 }
 
+// rint(x / s) for |x / s| <= 128, bit-identical to rintf(__fdiv_rn(x, s)), the x / scale of
+// the CPU restatement.  r = 1/s correctly rounded, so q = x * r (both roundings included) lies
+// within 128 * 2^-23 = 2^-16 of x / s, and the correctly rounded quotient within 2^-17 of it:
+// the two round to the same integer unless q is within 2^-15 of a half-integer.  Elements with
+// q within 2^-12 of one (about 1 in 2,000) take the IEEE division instead.  q - rint(q) is
+// exact (Sterbenz), and __fmul_rn keeps the product from being fused into the subtraction.
+__device__ __forceinline__ float rint_quotient(float x, float s, float r) {
+  const float q = __fmul_rn(x, r);
+  const float c = rintf(q);
+  return fabsf(__fsub_rn(q, c)) <= 0.5f - 0x1p-12f ? c : rintf(__fdiv_rn(x, s));
+}
+
 template <typename T>
 __device__ __forceinline__ float to_f(T v);
 template <>
@@ -81,6 +93,7 @@ __global__ void __launch_bounds__(THREADS) int8_rows_vec_kernel(const __nv_bfloa
   }
   amax = block_max(amax);
   const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+  const float rs = __frcp_rn(s);
   if (threadIdx.x == 0) scale[r] = s;
   uint2* qr = reinterpret_cast<uint2*>(q + r * ldq);
 #pragma unroll
@@ -92,7 +105,7 @@ __global__ void __launch_bounds__(THREADS) int8_rows_vec_kernel(const __nv_bfloa
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const float f = __uint_as_float((e & 1) ? (w[e >> 1] & 0xFFFF0000u) : (w[e >> 1] << 16));
-      const float c = fminf(fmaxf(rintf(__fdiv_rn(f, s)), -127.f), 127.f);
+      const float c = fminf(fmaxf(rint_quotient(f, s, rs), -127.f), 127.f);
       packed[e >> 2] |= (uint32_t)(static_cast<int>(c) & 0xFF) << (8 * (e & 3));
     }
     qr[vi] = make_uint2(packed[0], packed[1]);
@@ -108,6 +121,7 @@ __global__ void __launch_bounds__(256) int8_rows_amax_kernel(const __nv_bfloat16
   const long long r = blockIdx.x;
   const int vi = blockIdx.y * 256 + threadIdx.x;
   const float s = fmaxf(__fdiv_rn(amax[r], 127.0f), 1e-12f);
+  const float rs = __frcp_rn(s);
   if (vi == 0) scale[r] = s;
   if (vi >= (K >> 3)) return;
   const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + r * ldx) + vi);
@@ -116,7 +130,7 @@ __global__ void __launch_bounds__(256) int8_rows_amax_kernel(const __nv_bfloat16
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const float f = __uint_as_float((e & 1) ? (w[e >> 1] & 0xFFFF0000u) : (w[e >> 1] << 16));
-    const float c = fminf(fmaxf(rintf(__fdiv_rn(f, s)), -127.f), 127.f);
+    const float c = fminf(fmaxf(rint_quotient(f, s, rs), -127.f), 127.f);
     packed[e >> 2] |= (uint32_t)(static_cast<int>(c) & 0xFF) << (8 * (e & 3));
   }
   reinterpret_cast<uint2*>(q + r * ldq)[vi] = make_uint2(packed[0], packed[1]);
@@ -216,6 +230,7 @@ __global__ void __launch_bounds__(WARPS * 32) int8_rows_convrot_kernel(const __n
   }
   amax = block_max(amax);
   const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+  const float rs = __frcp_rn(s);
   if (threadIdx.x == 0) scale[r] = s;
   int8_t* qr = q + r * ldq;
 #pragma unroll
@@ -225,7 +240,7 @@ __global__ void __launch_bounds__(WARPS * 32) int8_rows_convrot_kernel(const __n
     uint32_t packed[2] = {0u, 0u};
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float c = fminf(fmaxf(rintf(__fdiv_rn(v[j][e], s)), -127.f), 127.f);
+      const float c = fminf(fmaxf(rint_quotient(v[j][e], s, rs), -127.f), 127.f);
       packed[e >> 2] |= (uint32_t)(static_cast<int>(c) & 0xFF) << (8 * (e & 3));
     }
     reinterpret_cast<uint2*>(qr + ((long long)g << 8))[lane] = make_uint2(packed[0], packed[1]);
