@@ -322,10 +322,11 @@ def run_attention_only(args, c):
 
 
 def run_quantisers_only(args, c):
-    """The int8 row quantisers alone on the config's branch rows x hidden (bf16, larger than
-    L2): plain per-row int8 and ConvRot int8 (group-256 rotation in the same pass), each with
-    its algorithmic bytes (2 B read + 1 B written per element, 4 B of scale per row) over its
-    CUDA-event time, against the measured HBM copy bandwidth."""
+    """The activation quantisers alone on the config's branch rows x hidden (bf16, larger than
+    L2): plain per-row int8, ConvRot int8 (group-256 rotation in the same pass) and per-tensor
+    e4m3 (an amax pass, then the cast), each with the algorithmic bytes of one quantisation
+    (2 B read + 1 B written per element, 4 B of scale per row) over its CUDA-event time, against
+    the measured HBM copy bandwidth."""
     from __graft_entry__ import load_package
 
     pkg = load_package()
@@ -336,10 +337,15 @@ def run_quantisers_only(args, c):
     x = torch.randn(rows, K, generator=g).to(dev, torch.bfloat16)
     out = pkg.projection.QuantizedMatrix(torch.empty(rows, K, device=dev, dtype=torch.int8),
                                          torch.empty(rows, device=dev, dtype=torch.float32), "int8")
+    out8 = pkg.projection.QuantizedMatrix(torch.empty(rows, K, device=dev, dtype=torch.float8_e4m3fn),
+                                          torch.empty(1, device=dev, dtype=torch.float32), "fp8")
+    work = torch.empty(1, device=dev, dtype=torch.float32)
     pk, src = peaks()
     algo = rows * K * 3 + rows * 4
     for name, fn in (("int8_rows_vec_kernel", pkg.quantize_rows_int8),
-                     ("int8_rows_convrot_kernel", pkg.quantize_rows_int8_convrot)):
+                     ("int8_rows_convrot_kernel", pkg.quantize_rows_int8_convrot),
+                     ("amax_kernel + fp8_cast_kernel (reads the rows twice)",
+                      lambda t, _o: pkg.quantize_tensor_fp8(t, out8, work))):
         for _ in range(args.warmup):
             fn(x, out)
         torch.cuda.synchronize()

@@ -136,32 +136,99 @@ __global__ void __launch_bounds__(256) int8_rows_amax_kernel(const __nv_bfloat16
   reinterpret_cast<uint2*>(q + r * ldq)[vi] = make_uint2(packed[0], packed[1]);
 }
 
-template <typename T>
+// Per-tensor amax and e4m3 cast: CTAs stride over rows, threads over a row's columns (no
+// per-element index division); VEC: aligned bf16 rows read 8 at a time with 16-byte loads.
+// The per-element arithmetic is the same in every variant.
+template <typename T, bool VEC>
 __global__ void amax_kernel(const T* __restrict__ x, long long ldx, int rows, int K, float* __restrict__ amax) {
   float m = 0.f;
-  const long long n = (long long)rows * K;
-  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
-    const long long r = e / K;
-    const int c = (int)(e % K);
-    m = fmaxf(m, fabsf(to_f<T>(x[r * ldx + c])));
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const T* row = x + (long long)r * ldx;
+    if constexpr (VEC) {
+      const uint4* rv = reinterpret_cast<const uint4*>(row);
+      for (int vi = threadIdx.x; vi < (K >> 3); vi += blockDim.x) {
+        const uint4 v = __ldg(rv + vi);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[e] << 16)), fabsf(__uint_as_float(w[e] & 0xFFFF0000u))));
+      }
+    } else {
+      for (int c = threadIdx.x; c < K; c += blockDim.x) m = fmaxf(m, fabsf(to_f<T>(row[c])));
+    }
   }
   m = block_max(m);
   if (threadIdx.x == 0) atomicMax(reinterpret_cast<int*>(amax), __float_as_int(m));
 }
 
-template <typename T>
+__device__ __forceinline__ uint32_t e4m3_code(float f, float s) {
+  float v = __fdiv_rn(f, s);
+  v = fminf(fmaxf(v, -448.f), 448.f);
+  return (uint32_t)__nv_fp8_e4m3(v).__x;
+}
+
+template <typename T, bool VEC>
 __global__ void fp8_cast_kernel(const T* __restrict__ x, long long ldx, int rows, int K, const float* __restrict__ amax,
                                 __nv_fp8_e4m3* __restrict__ q, long long ldq, float* __restrict__ scale_out) {
   const float s = fmaxf(__fdiv_rn(*amax, 448.0f), 1e-12f);
   if (blockIdx.x == 0 && threadIdx.x == 0 && scale_out) *scale_out = s;
-  const long long n = (long long)rows * K;
-  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
-    const long long r = e / K;
-    const int c = (int)(e % K);
-    float v = __fdiv_rn(to_f<T>(x[r * ldx + c]), s);
-    v = fminf(fmaxf(v, -448.f), 448.f);
-    q[r * ldq + c] = __nv_fp8_e4m3(v);
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const T* row = x + (long long)r * ldx;
+    __nv_fp8_e4m3* qr = q + (long long)r * ldq;
+    if constexpr (VEC) {
+      const uint4* rv = reinterpret_cast<const uint4*>(row);
+      for (int vi = threadIdx.x; vi < (K >> 3); vi += blockDim.x) {
+        const uint4 v = __ldg(rv + vi);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float f = __uint_as_float((e & 1) ? (w[e >> 1] & 0xFFFF0000u) : (w[e >> 1] << 16));
+          packed[e >> 2] |= e4m3_code(f, s) << (8 * (e & 3));
+        }
+        reinterpret_cast<uint2*>(qr)[vi] = make_uint2(packed[0], packed[1]);
+      }
+    } else {
+      for (int c = threadIdx.x; c < K; c += blockDim.x) qr[c].__x = (__nv_fp8_storage_t)e4m3_code(to_f<T>(row[c]), s);
+    }
   }
+}
+
+// Grid of the two per-tensor passes: CTAs stride over rows, at most 4 per SM.
+inline int tensor_pass_blocks(int rows) { return std::max(1, std::min(rows, 4 * vdn::sm_count())); }
+
+inline bool bf16_rows_vec(int src_kind, const void* x, long long ldx, int K, const void* q, long long ldq) {
+  return src_kind == 0 && K % 8 == 0 && vdn::aligned16(x) && ldx % 8 == 0 &&
+         (q == nullptr || ((reinterpret_cast<uintptr_t>(q) & 7) == 0 && ldq % 8 == 0));
+}
+
+inline void launch_amax(int src_kind, const void* x, long long ldx, int rows, int K, float* amax, cudaStream_t s) {
+  const int blocks = tensor_pass_blocks(rows);
+  if (bf16_rows_vec(src_kind, x, ldx, K, nullptr, 0))
+    amax_kernel<__nv_bfloat16, true><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, rows, K,
+                                                            amax);
+  else if (src_kind == 0)
+    amax_kernel<__nv_bfloat16, false><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, rows, K,
+                                                             amax);
+  else
+    amax_kernel<float, false><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, rows, K, amax);
+  vdn::count_launch();
+}
+
+inline void launch_fp8_cast(int src_kind, const void* x, long long ldx, int rows, int K, const float* amax, void* q,
+                            long long ldq, float* scale_out, cudaStream_t s) {
+  const int blocks = tensor_pass_blocks(rows);
+  auto qb = reinterpret_cast<__nv_fp8_e4m3*>(q);
+  if (bf16_rows_vec(src_kind, x, ldx, K, q, ldq))
+    fp8_cast_kernel<__nv_bfloat16, true><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, rows,
+                                                                K, amax, qb, ldq, scale_out);
+  else if (src_kind == 0)
+    fp8_cast_kernel<__nv_bfloat16, false><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+                                                                 rows, K, amax, qb, ldq, scale_out);
+  else
+    fp8_cast_kernel<float, false><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, rows, K, amax, qb,
+                                                         ldq, scale_out);
+  vdn::count_launch();
 }
 
 // ConvRot rows: each 256-wide group of a row is rotated by H = R/16, R the fourth Kronecker
@@ -334,24 +401,9 @@ int vdn_quant_fp8_tensor(int src_kind, const void* x, long long ldx, int rows, i
   if (!x || !q || !work || !scale_out || rows < 0 || K <= 0) return vdn::kBadArgument;
   auto s = reinterpret_cast<cudaStream_t>(stream);
   cudaMemsetAsync(work, 0, sizeof(float), s);
-  const long long n = (long long)rows * K;
-  const int blocks = (int)std::min<long long>((n + 255) / 256, 4LL * vdn::sm_count());
-  if (blocks > 0) {
-    if (src_kind == 0) {
-      vdn::quant::amax_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
-                                                                     rows, K, work);
-      vdn::count_launch();
-      vdn::quant::fp8_cast_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
-          reinterpret_cast<const __nv_bfloat16*>(x), ldx, rows, K, work, reinterpret_cast<__nv_fp8_e4m3*>(q), ldq,
-          scale_out);
-      vdn::count_launch();
-    } else {
-      vdn::quant::amax_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, rows, K, work);
-      vdn::count_launch();
-      vdn::quant::fp8_cast_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, rows, K, work,
-                                                                 reinterpret_cast<__nv_fp8_e4m3*>(q), ldq, scale_out);
-      vdn::count_launch();
-    }
+  if ((long long)rows * K > 0) {
+    vdn::quant::launch_amax(src_kind, x, ldx, rows, K, work, s);
+    vdn::quant::launch_fp8_cast(src_kind, x, ldx, rows, K, work, q, ldq, scale_out, s);
   }
   return vdn::launch_status();
 }
@@ -363,16 +415,7 @@ int vdn_fp8_amax(int src_kind, const void* x, long long ldx, int rows, int K, fl
   if (!x || !amax || rows < 0 || K <= 0) return vdn::kBadArgument;
   auto s = reinterpret_cast<cudaStream_t>(stream);
   cudaMemsetAsync(amax, 0, sizeof(float), s);
-  const long long n = (long long)rows * K;
-  const int blocks = (int)std::min<long long>((n + 255) / 256, 4LL * vdn::sm_count());
-  if (blocks > 0) {
-    if (src_kind == 0)
-      vdn::quant::amax_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
-                                                                     rows, K, amax);
-    else
-      vdn::quant::amax_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, rows, K, amax);
-    vdn::count_launch();
-  }
+  if ((long long)rows * K > 0) vdn::quant::launch_amax(src_kind, x, ldx, rows, K, amax, s);
   return vdn::launch_status();
 }
 
@@ -380,18 +423,7 @@ int vdn_fp8_cast(int src_kind, const void* x, long long ldx, int rows, int K, co
                  long long ldq, float* scale_out, void* stream) {
   if (!x || !q || !amax || rows < 0 || K <= 0) return vdn::kBadArgument;
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  const long long n = (long long)rows * K;
-  const int blocks = (int)std::min<long long>((n + 255) / 256, 4LL * vdn::sm_count());
-  if (blocks > 0) {
-    if (src_kind == 0)
-      vdn::quant::fp8_cast_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
-          reinterpret_cast<const __nv_bfloat16*>(x), ldx, rows, K, amax, reinterpret_cast<__nv_fp8_e4m3*>(q), ldq,
-          scale_out);
-    else
-      vdn::quant::fp8_cast_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(x), ldx, rows, K, amax,
-                                                                 reinterpret_cast<__nv_fp8_e4m3*>(q), ldq, scale_out);
-    vdn::count_launch();
-  }
+  if ((long long)rows * K > 0) vdn::quant::launch_fp8_cast(src_kind, x, ldx, rows, K, amax, q, ldq, scale_out, s);
   return vdn::launch_status();
 }
 
@@ -465,14 +497,8 @@ int vdn_fp8_linear_noalloc(const void* x, long long ldx, int M, int K, const voi
   __nv_fp8_e4m3* q = reinterpret_cast<__nv_fp8_e4m3*>(base + vdn::quant::kNoAllocHeader);
   auto s = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(amax, 0, sizeof(float), s) != cudaSuccess) return vdn::kLaunchFailed;
-  const long long n = (long long)M * K;
-  const int blocks = (int)std::min<long long>((n + 255) / 256, 4LL * vdn::sm_count());
-  vdn::quant::amax_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M,
-                                                                 K, amax);
-  vdn::count_launch();
-  vdn::quant::fp8_cast_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
-                                                                     M, K, amax, q, K, scale);
-  vdn::count_launch();
+  vdn::quant::launch_amax(0, x, ldx, M, K, amax, s);
+  vdn::quant::launch_fp8_cast(0, x, ldx, M, K, amax, q, K, scale, s);
   const int rc = vdn::launch_status();
   if (rc) return rc;
   return vdn_gemm(1, q, K, nullptr, 0, 0, w_fp8, ldw, out, ldo, 0, M, N, K, 1.0f, scale, w_scale, nullptr, nullptr,
