@@ -167,3 +167,49 @@ def test_sharded_block_matches_unsharded_oracle_on_gloo_ranks(world, anchors, ch
     for rank, err, shape in results:
         assert shape == (seq, vo.CONFIG0["hidden"])
         assert err < 1e-12, (rank, err)
+
+
+
+def _leaving_worker(rank, world, port, q):
+    """Rank 1 stops on the host before the exchange (between steps, none of its collectives in
+    flight) and leaves; rank 0 goes on to the exchange, which must end with an error, bounded
+    by the process group's timeout, instead of waiting for good."""
+    import datetime
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    shard = sh.default_shard(4)
+    xchg = sh.RowExchange(shard, 64, 2 * shard.heads_local * 8, 32, "cpu", dtype=torch.float64)
+    if rank == 1:
+        result = "left"
+    else:
+        xchg.send.normal_()
+        try:
+            xchg.exchange()
+            xchg.project_and_gather(lambda recv, rows, out_rows, row0: None)
+            result = "completed"
+        except Exception as exc:  # noqa: BLE001 - the backend's error is the expected outcome
+            result = f"error: {type(exc).__name__}: {exc}"
+    q.put((rank, result))
+    q.close()
+    q.join_thread()  # flush the message before the hard exit
+    os._exit(0)  # no teardown: the group is broken, its destructor would wait on the peer
+
+
+def test_exchange_ends_with_an_error_when_a_rank_leaves():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        results = dict(q.get(timeout=120) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    assert results[1] == "left"
+    assert results[0].startswith("error"), results[0]
