@@ -317,3 +317,30 @@ def test_stored_fp8_master_scales_per_tensor_or_per_channel():
     assert torch.equal(per_ch[:, 0], torch.tensor([1.0, 2.0, 3.0, 4.0]))
     with pytest.raises(ValueError):
         pkg.projection.dequantize_projection_weight(q, torch.ones(3))
+
+
+
+def test_mask_known_answers_with_hand_written_bounds():
+    """The reference's mask cases (tests/test_window.py:378-389): video rows [4, 34), 3 frames of
+    10 tokens, frames 0-1 see frames 0-2 and frame 2 sees frame 0 only.  The mask function takes
+    such bounds; a layout does not (window.py:172-178): the plan builder rejects them with the
+    reference's message."""
+    S, vs, ve, F, tpf = 40, 4, 34, 3, 10
+    bounds = [(0, 2), (0, 2), (0, 0)]
+    none = vo.allowed_mask(S, vs, ve, F, tpf, bounds, "none").numpy()
+    assert not none[30, 18]  # frame 1 is outside frame 2's window
+    assert none[30, 8]  # frame 0 inside
+    assert none[30, 36]  # a global key
+    assert none[1, 18]  # a global query
+    both = vo.allowed_mask(S, vs, ve, F, tpf, bounds, "both").numpy()
+    assert both[30, 18]  # frame 2 is the last frame: an anchor row
+    with pytest.raises(ValueError, match=r"bounds\[2\]=\(0, 0\) does not contain its query frame"):
+        bw.build_window_plan(S, vs, ve, F, tpf, bounds, "none")
+    # the same answers from a valid layout whose last frame sees frames 1-2 only
+    ok = [(0, 2), (0, 2), (1, 2)]
+    for anchors in ("none", "both"):
+        want = vo.allowed_mask(S, vs, ve, F, tpf, ok, anchors).numpy()
+        assert want[30, 18]
+        assert want[30, 8] == (anchors == "both")  # frame 0 only through the anchor rows
+        plan = bw.build_window_plan(S, vs, ve, F, tpf, ok, anchors)
+        np.testing.assert_array_equal(_expand_plan(plan, S), want)
