@@ -207,3 +207,29 @@ def test_convrot_int8_is_exact_integer_arithmetic_and_beats_plain_on_outliers():
     e_rot = float((vo.project_int8_convrot(x, w) - exact).norm() / exact.norm())
     e_plain = float((vo.project(x, w, "int8") - exact).norm() / exact.norm())
     assert e_rot < 0.5 * e_plain
+
+
+def test_block_composition_mirrors_the_reference_hybrid_tests():
+    """tests/test_hybrid.py:107-189: with a zero softmax gate (sigmoid(0) = 1/2) the block is half
+    the ungated block, and the branch delta changes the video rows only."""
+    c = vo.CONFIG0
+    lay = vo.config_layout(c)
+    H, D, hidden = c["heads"], c["dim"], c["hidden"]
+    bw = vo.make_block(0, hidden, H, D)
+    x = vo.make_x(0, lay.seq_len, hidden)
+    cfg = vo.BranchConfig()
+    zero_gate = dict(bw.branch, **{"softmax_gate.up.weight": torch.zeros(H, hidden),
+                                   "softmax_gate.up.bias": torch.zeros(H)})
+    bw0 = vo.BlockWeights(bw.qkv, bw.q_norm, bw.k_norm, bw.out, zero_gate)
+    gated = vo.block_forward(x, bw0, lay, H, D, cfg, enable_softmax_gate=True, linear_enabled=False)
+    plain = vo.block_forward(x, bw0, lay, H, D, cfg, enable_softmax_gate=False, linear_enabled=False)
+    torch.testing.assert_close(gated, 0.5 * plain, rtol=1e-12, atol=1e-12)
+    on = vo.block_forward(x, bw, lay, H, D, cfg)
+    off = vo.block_forward(x, bw, lay, H, D, cfg, linear_enabled=False)
+    vs, ve = lay.video_start, lay.video_end
+    assert torch.equal(on[:vs], off[:vs]) and torch.equal(on[ve:], off[ve:])
+    changed = (on[vs:ve] - off[vs:ve]).abs().amax(dim=1) > 0
+    tpf = lay.tokens_per_frame
+    # skip_ends (anchors "both"): frames 0 and F-1 carry no delta (runtime.py:576-585)
+    assert not changed[:tpf].any() and not changed[-tpf:].any()
+    assert changed[tpf:-tpf].all()
