@@ -344,3 +344,19 @@ def test_mask_known_answers_with_hand_written_bounds():
         assert want[30, 8] == (anchors == "both")  # frame 0 only through the anchor rows
         plan = bw.build_window_plan(S, vs, ve, F, tpf, ok, anchors)
         np.testing.assert_array_equal(_expand_plan(plan, S), want)
+
+
+def test_alpha_parameters_keep_fp32_precision():
+    """The reference keeps alpha.A_log and alpha.dt_bias in fp32 when the other branch weights go
+    to bf16 (tests/test_optimized_runtime.py:97-105); the device weight map does too."""
+    from vdn_b200.branch import BranchDeviceWeights
+
+    c = vo.CONFIG0
+    H, D, hidden = c["heads"], c["dim"], c["hidden"]
+    w = vo.make_branch_weights(torch.Generator().manual_seed(0), hidden, H, D)
+    w["alpha.A_log"] = torch.full((H,), 1.0 + 2.0 ** -20)  # not representable in bf16
+    w["alpha.dt_bias"] = torch.full((H * D,), -3.0 + 2.0 ** -19)
+    bdw = BranchDeviceWeights.from_dict(w, H, D, "cpu")
+    assert bdw.a_log.dtype == torch.float32 and bdw.dt_bias.dtype == torch.float32
+    assert torch.equal(bdw.a_log, w["alpha.A_log"]) and torch.equal(bdw.dt_bias, w["alpha.dt_bias"])
+    assert bdw.beta_w.dtype == torch.bfloat16  # the projections themselves run in bf16
