@@ -233,3 +233,48 @@ def test_block_composition_mirrors_the_reference_hybrid_tests():
     # skip_ends (anchors "both"): frames 0 and F-1 carry no delta (runtime.py:576-585)
     assert not changed[:tpf].any() and not changed[-tpf:].any()
     assert changed[tpf:-tpf].all()
+
+
+def test_short_conv_k_features_have_unit_norm():
+    """tests/test_branch.py:130-146: after the spatial + temporal conv and SiLU, every k feature
+    vector is L2-normalised per head (v features are not)."""
+    c = vo.CONFIG0
+    lay = vo.config_layout(c)
+    H, D = c["heads"], c["dim"]
+    w = vo.make_branch_weights(torch.Generator().manual_seed(1), c["hidden"], H, D)
+    rows = lay.num_frames * lay.tokens_per_frame
+    tok = torch.randn(rows, H, D, generator=torch.Generator().manual_seed(2))
+    k = vo.conv_features(tok, w["short_conv.k_sp.weight"], w["short_conv.k_tm.weight"], lay.num_frames,
+                         lay.frame_size, True)
+    assert k.shape == (lay.num_frames, H, lay.tokens_per_frame, D)
+    torch.testing.assert_close(k.norm(dim=-1), torch.ones(k.shape[:-1], dtype=k.dtype), rtol=0, atol=1e-9)
+    v = vo.conv_features(tok, w["short_conv.v_sp.weight"], w["short_conv.v_tm.weight"], lay.num_frames,
+                         lay.frame_size, False)
+    assert not torch.allclose(v.norm(dim=-1), torch.ones(v.shape[:-1], dtype=v.dtype))
+
+
+def test_branch_with_skip_ends_zeroes_the_end_frames_and_stays_finite():
+    """tests/test_branch.py:163-194: with skip_ends the rows of frames 0 and F-1 are zero and the
+    rest finite."""
+    c = vo.CONFIG0
+    lay = vo.config_layout(c)
+    H, D, hidden = c["heads"], c["dim"], c["hidden"]
+    bw = vo.make_block(0, hidden, H, D)
+    x = vo.make_x(0, lay.seq_len, hidden)
+    ki = vo.make_kernel_inputs(0, lay, H, D)
+    vs, ve, tpf = lay.video_start, lay.video_end, lay.tokens_per_frame
+    out = vo.branch_readout(bw.branch, x[vs:ve], ki["q"][vs:ve], ki["k"][vs:ve], ki["v"][vs:ve], lay.num_frames, tpf,
+                            list(lay.bounds), lay.frame_size, H, D, vo.BranchConfig(), skip_ends=True)
+    assert out.shape == (ve - vs, H * D)
+    assert torch.count_nonzero(out[:tpf]) == 0 and torch.count_nonzero(out[-tpf:]) == 0
+    assert torch.isfinite(out).all()
+    # an interior frame reads the states before and after its window; a window that spans the
+    # whole clip (frames 1 .. F-2 after skip_ends) leaves none, so without text state it is zero
+    F = lay.num_frames
+    for f in range(1, F - 1):
+        lo, hi = lay.bounds[f]
+        rows = out[f * tpf:(f + 1) * tpf]
+        if lo <= 1 and hi >= F - 2:
+            assert torch.count_nonzero(rows) == 0, f
+        else:
+            assert (rows.abs().amax(dim=1) > 0).all(), f
