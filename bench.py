@@ -13,6 +13,10 @@ through the public operator (``make_vdn_forward``) with the input copied from pi
 memory and the output read back every step.  ``roofline`` covers the dominant kernel,
 timed with CUDA events on its launch stream inside the timed steps.  ``cpu_baseline`` is
 the float32 CPU restatement (oracle port) of the same block on a bounded head sample.
+
+Kernel-only modes for profiling: ``--only attention [--heads n]`` (the window attention kernel
+on the config geometry) and ``--only quantisers`` (the int8, ConvRot int8 and per-tensor e4m3
+activation quantisers on the config's branch rows, against the measured HBM bandwidth).
 """
 
 from __future__ import annotations
