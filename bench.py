@@ -282,6 +282,13 @@ def run_reference_arm(args, c, world, rank):
 E2E_ROW_BLOCKS = 4  # row blocks of the end-to-end copies at N = 1
 
 
+def node_config(delta_rule="vdn_solve") -> dict:
+    """BASELINE config 1's released-lineage block structure as a node config: short conv on
+    k and v, the text state, both gates, the alpha bridge (nodes.py:98-116 keys)."""
+    return {"enable_softmax_gate": True, "delta_rule": delta_rule, "bridge": "alpha", "short_conv": ("k", "v"),
+            "enable_text_state": True}
+
+
 def metric_name(c) -> str:
     """BASELINE's metric on the config's geometry (config 1: 31x836+512 tokens)."""
     return (f"VDN hybrid block fwd TFLOP/s at {c['frames']}x{c['grid'][0] * c['grid'][1]}+{c['text']} tokens "
@@ -558,8 +565,7 @@ def main():
                                  k_norm=types.SimpleNamespace(weight=kn, eps=1e-6), forward=None)
     # N > 1: the heads are sharded over the ranks (H/N each, recurrence kept per head), the
     # per-head outputs exchanged by row block over NCCL and the projected rows all-gathered
-    state = pkg.B200State("bench", {"enable_softmax_gate": True, "delta_rule": args.delta_rule}, [branch], H, D,
-                          shard_heads=world > 1)
+    state = pkg.B200State("bench", node_config(args.delta_rule), [branch], H, D, shard_heads=world > 1)
     block = state.fused_block(attn, 0, dev)
     rope_freqs = rope_freqs_table(lay.seq_len, D, dev) if args.rope else None
     rope = pkg.rope_table(rope_freqs, lay.seq_len, D, dev)

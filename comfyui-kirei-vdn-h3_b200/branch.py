@@ -31,12 +31,45 @@ DELTA_RULES = ("vdn_solve", "sana_scaled")  # branch.py:180
 _CHOLESKY_CHECKS: ContextVar = ContextVar("vdn_b200_cholesky_checks", default=None)
 
 
+class InfoRing:
+    """Status rows for the factor calls of one branch workspace: each call gets a [rows, H]
+    int32 slot of its own (the reference gets a fresh ``info`` from every ``cholesky_ex``,
+    branch.py:62-71), so blocks that share a workspace cannot overwrite a status before the
+    forward validates it.  Slots come from chunks allocated on first need and return to the
+    free list once their scope has validated them; after the first forward no call
+    allocates."""
+
+    CHUNK = 16
+
+    def __init__(self, rows: int, heads: int, device):
+        self.shape = (int(rows), int(heads))
+        self.device = torch.device(device)
+        self.chunks: list[torch.Tensor] = []
+        self.free: list[torch.Tensor] = []
+
+    def claim(self) -> torch.Tensor:
+        if not self.free:
+            chunk = torch.zeros(self.CHUNK, *self.shape, device=self.device, dtype=torch.int32)
+            self.chunks.append(chunk)
+            self.free = [chunk[i] for i in range(self.CHUNK - 1, -1, -1)]
+        return self.free.pop()
+
+    def release(self, slot: torch.Tensor):
+        self.free.append(slot)
+
+
 class _CholeskyChecks:
     """Deferred SPD validation of every factorisation of one forward (branch.py:27-45)."""
 
     def __init__(self):
         self.statuses: list[torch.Tensor] = []
         self.factor_calls = 0
+        self.claims: list[tuple[InfoRing, torch.Tensor]] = []
+
+    def release(self):
+        for ring, slot in self.claims:
+            ring.release(slot)
+        self.claims.clear()
 
     def validate(self):
         if not self.statuses:
@@ -64,19 +97,40 @@ def cholesky_runtime_scope():
         checks.validate()
     finally:
         checks.statuses.clear()
+        checks.release()
         _CHOLESKY_CHECKS.reset(token)
 
 
-def record_factor_status(info: torch.Tensor):
+def claim_factor_status(ring: InfoRing) -> torch.Tensor:
+    """A status slot for one branch call's factorisations (text frame and clip frames),
+    held until the enclosing scope has validated it (outside a scope: until the call's own
+    immediate validation)."""
+    slot = ring.claim()
+    checks = _CHOLESKY_CHECKS.get()
+    if checks is not None:
+        checks.claims.append((ring, slot))
+    return slot
+
+
+def record_factor_status(infos: list[torch.Tensor], ring: InfoRing | None = None,
+                         slot: torch.Tensor | None = None):
+    """Register the status rows of one call's factorisations, in the order the reference
+    factors them (the text frame's, then the clip's: branch.py:795-799), for validation:
+    deferred to the exit of ``cholesky_runtime_scope`` (branch.py:48-59), else validated now
+    (a host sync), ``slot`` going back to ``ring`` afterwards."""
     checks = _CHOLESKY_CHECKS.get()
     if checks is None:
         tmp = _CholeskyChecks()
-        tmp.statuses.append(info)
-        tmp.factor_calls = 1
-        tmp.validate()
+        tmp.statuses.extend(infos)
+        tmp.factor_calls = len(infos)
+        try:
+            tmp.validate()
+        finally:
+            if ring is not None and slot is not None:
+                ring.release(slot)
     else:
-        checks.statuses.append(info)
-        checks.factor_calls += 1
+        checks.statuses.extend(infos)
+        checks.factor_calls += len(infos)
 
 
 @dataclass
@@ -165,7 +219,7 @@ class BranchWorkspace:
         self.inv = torch.empty(Fb + nt, heads, dim, dim, **f32)
         # bf16 hi / lo halves of the inverses for the tensor-core scan (head_dim 128)
         self.inv_split = torch.empty(2 if dim == 128 else 0, Fb + nt, heads, dim, dim, **bf)
-        self.info = torch.zeros(Fb + nt, heads, device=dev, dtype=torch.int32)
+        self.info_ring = InfoRing(Fb + nt, heads, dev)  # one [Fb + nt, H] status slot per call
         self.s0 = torch.empty(heads, dim, dim, **f32)
         self.prefix = torch.empty(Fb, heads, dim, dim, **f32)
         self.suffix = torch.empty(Fb, heads, dim, dim, **f32)
@@ -276,6 +330,8 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
     has_text = text_k is not None
     s0 = ws.s0 if has_text else None
     mat = D * D * H
+    # this call's factor status rows: [Fb] clip frames then the text frame
+    info = claim_factor_status(ws.info_ring) if delta_rule == "vdn_solve" else None
     # The text "frame" (its features, statistics, factor and S0) and alpha (launches of 30 to
     # 40-odd CTAs, latency-bound) run on a side stream beside the frames' conv, statistics and
     # factor; the scan waits for them.  Their inputs were written before this call on the
@@ -300,7 +356,7 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
                  None, None, 0, (1.0 / L) ** 0.5, TEXT_STATE_SCALE, ws.s0.data_ptr(), ts)
         else:
             call("vdn_delta_factor", ws.A.data_ptr() + 4 * Fb * mat, ws.B.data_ptr() + 4 * Fb * mat, 1, H, D,
-                 ws.inv.data_ptr() + 4 * Fb * mat, ws.info.data_ptr() + 4 * Fb * H, 0, TEXT_STATE_SCALE,
+                 ws.inv.data_ptr() + 4 * Fb * mat, info.data_ptr() + 4 * Fb * H, 0, TEXT_STATE_SCALE,
                  ws.s0.data_ptr(), None, ts)
     side_done = torch.cuda.Event()
     side_done.record(side)
@@ -321,10 +377,12 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
              None if tensor_cores else ws.inv.data_ptr(), split, -1, 0.0, 0.0, None, stream)
     else:
         inj_scale = 0.0
-        call("vdn_delta_factor", ws.A.data_ptr(), ws.B.data_ptr(), Fb, H, D, ws.inv.data_ptr(), ws.info.data_ptr(),
+        call("vdn_delta_factor", ws.A.data_ptr(), ws.B.data_ptr(), Fb, H, D, ws.inv.data_ptr(), info.data_ptr(),
              -1, 0.0, None, split, stream)
-        record_factor_status(ws.info)
     main.wait_event(side_done)
+    if info is not None:
+        # after the join: an immediate validation (outside a scope) reads the text row too
+        record_factor_status(([info[Fb:Fb + 1]] if has_text else []) + [info[:Fb]], ws.info_ring, info)
     if tensor_cores:
         call("vdn_bidir_scan_tc", split, ws.B.data_ptr(), ws.alpha.data_ptr(), _lib.ptr(s0), Fb, Fb, H, inj_scale,
              ws.prefix.data_ptr(), ws.suffix.data_ptr(), status.err_ptr, stream)
@@ -490,5 +548,6 @@ class B200LinearBranch:
         return projector(readout.to(xv.dtype))
 
 
-__all__ = ["B200LinearBranch", "BranchDeviceWeights", "BranchWorkspace", "DELTA_RULES", "TEXT_STATE_SCALE",
-           "TILE_HALO", "cholesky_runtime_scope", "feature_frames", "frame_tiles", "run_branch"]
+__all__ = ["B200LinearBranch", "BranchDeviceWeights", "BranchWorkspace", "DELTA_RULES", "InfoRing", "TEXT_STATE_SCALE",
+           "TILE_HALO", "cholesky_runtime_scope", "claim_factor_status", "feature_frames", "frame_tiles",
+           "record_factor_status", "run_branch"]

@@ -534,12 +534,7 @@ int launch(const void* q, long long ld_q, const void* k, long long ld_k, const v
   if (rc) return rc;
   rc = make_tmap_2d(&tv, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, width, (uint64_t)p.S, (uint64_t)ld_v, 64, 128);
   if (rc) return rc;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(window_attention_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         Layout<D>::kSmem);
-    attr = true;
-  }
+  if (!smem_optin((const void*)window_attention_kernel<D>, Layout<D>::kSmem)) return kLaunchFailed;
   const int grid = p.n_items < sm_count() ? p.n_items : sm_count();
   if (grid <= 0) return kOk;
   window_attention_kernel<D><<<grid, kThreads, Layout<D>::kSmem, stream>>>(tq, tk, tv, p, err);

@@ -898,11 +898,7 @@ int vdn_spatial_conv(const void* in, long long ld_in, const float* w, int kh, in
   const bool tiled = paired && (C % kConvCh) == 0 && (ld_in % 8) == 0 && vdn::aligned16(in) &&
                      buf_bytes <= kSmemLimit;
   if (tiled) {
-    static bool attr_set = false;
-    if (!attr_set) {
-      cudaFuncSetAttribute(spatial_conv5_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemLimit);
-      attr_set = true;
-    }
+    if (!vdn::smem_optin((const void*)spatial_conv5_tiled_kernel, (int)kSmemLimit)) return vdn::kLaunchFailed;
     // two CTAs per SM with one buffer each when they fit (one CTA computes while the other
     // loads); the kernel can also double-buffer inside one CTA (stages = 2), which measured
     // slower at 8 warps per SM
@@ -1058,11 +1054,7 @@ int vdn_bidir_scan(const float* inv, const float* B, const float* alpha, const f
     if (!vdn::aligned16(B) || !vdn::aligned16(alpha) || !vdn::aligned16(prefix) || !vdn::aligned16(suffix))
       return vdn::kMisaligned;
     const size_t smem = (size_t)(2 * 128 * 128 + 128 * kScanUPitch) * sizeof(float);
-    static bool attr_set = false;
-    if (!attr_set) {
-      cudaFuncSetAttribute(bidir_scan128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      attr_set = true;
-    }
+    if (!vdn::smem_optin((const void*)bidir_scan128_kernel, (int)smem)) return vdn::kLaunchFailed;
     bidir_scan128_kernel<<<dim3(H, 2), kScanThreads, smem, s>>>(inv, B, alpha, s0, F, H, inj_scale, prefix,
                                                                  suffix);
     vdn::count_launch();
@@ -1090,7 +1082,7 @@ int vdn_readout(const void* Q, int F, int H, int T, int D, const float* prefix, 
   auto s = reinterpret_cast<cudaStream_t>(stream);
   const size_t smem = (size_t)(D * (D + 1) + D * 64) * sizeof(float);
   if (D == 128) {
-    cudaFuncSetAttribute(readout_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (!vdn::smem_optin((const void*)readout_kernel<128>, (int)smem)) return vdn::kLaunchFailed;
     readout_kernel<128><<<grid, 256, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(Q), T, F, H, prefix, suffix,
                                                 alpha, s0, lo, hi, use_alpha, norm_w,
                                                 reinterpret_cast<const __nv_bfloat16*>(gate), ld_gate,

@@ -781,11 +781,7 @@ int vdn_frame_stats_tc(const void* K, const void* V, int F, int H, int T, const 
   if (rc) return rc;
   rc = vdn::make_tmap_2d(&tv, V, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, rows, D, 64, 128);
   if (rc) return rc;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(frame_stats_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, StatsSmem::kBytes);
-    attr = true;
-  }
+  if (!vdn::smem_optin((const void*)frame_stats_tc_kernel, StatsSmem::kBytes)) return vdn::kLaunchFailed;
   const int units = F * H;
   const int grid = units < vdn::sm_count() ? units : vdn::sm_count();
   frame_stats_tc_kernel<<<grid, kStatsThreads, StatsSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
@@ -818,11 +814,7 @@ int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, cons
   if (rc) return rc;
   rc = vdn::make_tmap_2d(&tw, og_up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, (uint64_t)H * D, D, 64, 128);
   if (rc) return rc;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(readout_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ReadoutSmem::kBytes);
-    attr = true;
-  }
+  if (!vdn::smem_optin((const void*)readout_tc_kernel, ReadoutSmem::kBytes)) return vdn::kLaunchFailed;
   const int units = F * H;
   const int grid = units < vdn::sm_count() ? units : vdn::sm_count();
   readout_tc_kernel<<<grid, kReadoutThreads, ReadoutSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
@@ -849,12 +841,9 @@ int vdn_bidir_scan_tc(const void* inv_split, const float* B, const float* alpha,
   int rc = vdn::make_tmap_2d(&tinv, inv_split, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, (uint64_t)2 * F_inv * H * D, D,
                              64, 128);
   if (rc) return rc;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(scan_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScanSmem::kBytes);
-    cudaFuncSetAttribute(scan_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScanSmem::kBytes);
-    attr = true;
-  }
+  if (!vdn::smem_optin((const void*)scan_tc_kernel<false>, ScanSmem::kBytes) ||
+      !vdn::smem_optin((const void*)scan_tc_kernel<true>, ScanSmem::kBytes))
+    return vdn::kLaunchFailed;
   auto kernel = inj_scale > 0.f ? scan_tc_kernel<true> : scan_tc_kernel<false>;
   kernel<<<dim3(H, 2), kScanThreads, ScanSmem::kBytes, reinterpret_cast<cudaStream_t>(stream)>>>(
       tinv, B, alpha, s0, F, F_inv, H, inj_scale, prefix, suffix, dev_err);

@@ -599,11 +599,7 @@ int launch(const void* A, long long lda, const void* A2, long long lda2, long lo
   if (rc) return rc;
   rc = make_tmap_2d(&tb, B, dt, eb, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, T::BK, BN);
   if (rc) return rc;
-  static bool attr_set[3] = {false, false, false};
-  if (!attr_set[KIND]) {
-    cudaFuncSetAttribute(gemm_kernel<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    attr_set[KIND] = true;
-  }
+  if (!smem_optin((const void*)gemm_kernel<KIND>, kSmemBytes)) return kLaunchFailed;
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
   gemm_kernel<KIND><<<grid, kThreads, kSmemBytes, stream>>>(ta, ta2, tb, M, N, K, (int)k_split, kg, ep, err);

@@ -6,7 +6,10 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <mutex>
+#include <set>
 #include <stdint.h>
+#include <tuple>
 
 namespace vdn {
 
@@ -82,6 +85,26 @@ inline int sm_count() {
   if (dev < 0 || dev >= 64) dev = 0;
   if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
   return n[dev] > 0 ? n[dev] : 148;
+}
+
+// Opt `kernel` in to `bytes` of dynamic shared memory on the current device.  The attribute
+// belongs to the device that is current at the call, so each (kernel, device, size) is set
+// once per process -- a process driving several GPUs opts every one of them in -- under a
+// lock, since entry points may be called from several host threads.  False if CUDA refused.
+inline bool smem_optin(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::tuple<const void*, int, int>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const auto key = std::make_tuple(kernel, dev, bytes);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(key)) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+    cudaGetLastError();  // the caller reports the failure; later calls must not see it again
+    return false;
+  }
+  done.insert(key);
+  return true;
 }
 
 // Kernel launches made by this library since it was loaded: every <<<>>> site is followed

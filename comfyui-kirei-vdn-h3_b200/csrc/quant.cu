@@ -458,16 +458,21 @@ constexpr long long kNoAllocMaxElems = 16ll * 1024 * 1024;
 constexpr long long kNoAllocHeader = 256;  // amax at byte 0, scale at byte 128
 static __device__ __align__(256) unsigned char g_fp8_noalloc_scratch[kNoAllocHeader + kNoAllocMaxElems];
 
+// The array's device address on the current device, looked up once per device (atomic
+// slots: entry points may be called from several host threads; a lost race looks the same
+// address up twice).
 static unsigned char* noalloc_scratch_on_current_device() {
-  static unsigned char* addr[64] = {nullptr};
+  static std::atomic<unsigned char*> addr[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!addr[dev]) {
+  unsigned char* cached = addr[dev].load(std::memory_order_acquire);
+  if (!cached) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_fp8_noalloc_scratch) != cudaSuccess) return nullptr;
-    addr[dev] = static_cast<unsigned char*>(p);
+    cached = static_cast<unsigned char*>(p);
+    addr[dev].store(cached, std::memory_order_release);
   }
-  return addr[dev];
+  return cached;
 }
 
 }  // namespace quant
@@ -484,10 +489,12 @@ extern "C" {
 // out[M, N] (bf16) = x[M, K] (bf16) * W^T with x quantised to e4m3 per tensor inside the
 // library's own scratch array (see the block comment above), W [N, K] e4m3 with its
 // per-tensor scale w_scale (device fp32).  Same result as vdn_quant_fp8_tensor followed by
-// vdn_gemm(kind = 1).  Returns kTooLarge when M * K exceeds 16 Mi elements.
+// vdn_gemm(kind = 1).  Returns kTooLarge when M * K exceeds 16 Mi elements, kBadArgument
+// when a row pitch is shorter than its row (ldx or ldw < K, ldo < N).
 int vdn_fp8_linear_noalloc(const void* x, long long ldx, int M, int K, const void* w_fp8, long long ldw, int N,
                            const float* w_scale, void* out, long long ldo, int* dev_err, void* stream) {
   if (!x || !w_fp8 || !w_scale || !out || M <= 0 || N <= 0 || K <= 0) return vdn::kBadArgument;
+  if (ldx < K || ldw < K || ldo < N) return vdn::kBadArgument;  // rows must not overlap
   if ((long long)M * K > vdn::quant::kNoAllocMaxElems) return vdn::kTooLarge;
   if (K % 16) return vdn::kMisaligned;  // quantised rows are packed at pitch K bytes
   unsigned char* base = vdn::quant::noalloc_scratch_on_current_device();

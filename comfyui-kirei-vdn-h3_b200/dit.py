@@ -301,8 +301,6 @@ def make_fast_block_forward(block, state: B200State, block_index: int):
         out = db.forward(x, mods, group, layout, state.window_plans, status,
                          io=(transformer_options or {}).get(STREAM_IO_KEY),
                          linear_enabled=bool(config.get("linear_enabled", True)),
-                         bridge=str(config.get("bridge", "alpha")),
-                         enable_text_state=bool(config.get("enable_text_state", True)),
                          rope=rope_table(rope_freqs, layout.seq_len, state.head_dim, x.device))
         return out.to(x.dtype)
 

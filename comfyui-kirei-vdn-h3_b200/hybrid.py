@@ -16,8 +16,9 @@ On the device one block forward is four phases, all on the caller's stream:
    gather/readout/RMSNorm/output gate) writing the branch rows of a [S, H*D] buffer;
 3. the block-sparse window attention kernel with the gate fused in its epilogue;
 4. one tcgen05 GEMM over K = 2*H*D of [gated softmax | branch] against
-   [W_out | W_to_out]: out_proj, to_out_linear and the delta add in one pass (bf16);
-   the quantised precisions run out_proj then to_out_linear with an addend epilogue.
+   [W_out | W_to_out]: out_proj, to_out_linear and the delta add in one pass when both
+   projections are bf16; otherwise out_proj then to_out_linear (each in its own
+   arithmetic) with an addend epilogue.
 
 With a ``HeadShard`` (one process per GPU, torch.distributed) phases 1-3 run on this
 rank's heads only and phase 4 becomes all-to-all by row block, the output projection on
@@ -44,6 +45,29 @@ STREAM_IO_KEY = "vdn_b200_io"  # transformer_options entry carrying a StreamIO (
 AUX_ALIGN = 32  # side columns padded to 32: 128-byte fp32 rows, and no extra 256-column GEMM tile
 EXCHANGE_CHUNKS = 4  # pipelined exchange / projection / gather steps of the head-sharded block
 EXCHANGE_MIN_ROWS = 512  # rows per rank and chunk (one wave of projection tiles); fewer: one step
+
+# Branch settings a node config may leave out, with the values the reference falls back to:
+# the node builds each block's branch from the config with these defaults (nodes.py:98-116)
+# and the operator reads enable_text_state from the branch, then from the config with the
+# same default (hybrid.py:449-451).
+BRANCH_SETTING_DEFAULTS = {"delta_rule": "vdn_solve", "bridge": "alpha", "short_conv": (),
+                           "enable_text_state": False}
+
+
+def branch_setting(branch, config: Mapping, name: str):
+    """A branch setting as the reference resolves it: the branch object's own attribute when
+    the block's branch is an object (``LinearBranch`` / ``B200LinearBranch`` carry
+    delta_rule, bridge, short_conv, enable_text_state), else the node config's value, else
+    the reference default."""
+    if branch is not None and not isinstance(branch, Mapping) and hasattr(branch, name):
+        value = getattr(branch, name)
+    else:
+        value = config.get(name, BRANCH_SETTING_DEFAULTS[name])
+    if name == "short_conv":
+        return tuple(value)
+    if name == "enable_text_state":
+        return bool(value)
+    return str(value)
 
 
 def _weight_of(module_or_tensor):
@@ -171,11 +195,21 @@ class BlockGeometry:
 
 
 class FusedBlock:
-    """Device weights of one H3 attention block + its VDN branch, laid out for the kernels."""
+    """Device weights of one H3 attention block + its VDN branch, laid out for the kernels.
+
+    ``precision`` is the arithmetic of this block's own projections (qkv_proj, out_proj);
+    ``to_out_linear`` runs in the representation its map stores, as ``project`` dispatches
+    on it (projection.py:259-268): a bf16 ``to_out_linear.weight`` stays bf16 whatever the
+    block's precision (the edge blocks fp8.py:198 keeps in bf16), a quantised
+    ``to_out_linear.weight_fp8`` runs as int8 or e4m3.  The branch settings (short_conv,
+    delta_rule, bridge, enable_text_state) default to the released lineage, which is also
+    ``LinearBranch``'s constructor default (branch.py:533-546); ``tile_frames`` > 0 runs the
+    branch in frame tiles (runtime.py:421-543, same result)."""
 
     def __init__(self, qkv_w, q_norm_w, k_norm_w, out_w, branch_w: Mapping, heads, dim, device, *,
                  precision="bf16", eps=1e-6, enable_gate=True, short_conv=("k", "v"), shard: HeadShard | None = None,
-                 workspaces: dict | None = None, delta_rule="vdn_solve"):
+                 workspaces: dict | None = None, delta_rule="vdn_solve", bridge="alpha", enable_text_state=True,
+                 tile_frames=0):
         dev = torch.device(device)
         H_all, D = int(heads), int(dim)
         inner_all = H_all * D
@@ -199,7 +233,14 @@ class FusedBlock:
         self.short_conv = tuple(short_conv)
         if delta_rule not in DELTA_RULES:
             raise ValueError(f"unsupported delta_rule {delta_rule!r}")
+        if bridge not in ("alpha", "none"):
+            raise ValueError("bridge must be 'alpha' or 'none'")
+        if isinstance(tile_frames, bool) or not isinstance(tile_frames, int) or tile_frames < 0:
+            raise ValueError("tile_frames must be a non-negative integer")
         self.delta_rule = delta_rule
+        self.bridge = bridge
+        self.enable_text_state = bool(enable_text_state)
+        self.tile_frames = tile_frames
         qkv_rows = qkv_row_index(H_all, D, hs)
 
         def f32(t):
@@ -226,10 +267,12 @@ class FusedBlock:
         to_out = branch_w.get("to_out_linear.weight")
         if to_out is not None and not self.has_branch:
             to_out = None
-        # a stored quantised master (the reference's storage of fp8 / int8 projections,
-        # fp8.py:168-222, projection.py:139-232): used as is when it is this block's
-        # precision, else dequantised here once (a ConvRot master rotated back)
-        to_out_q = None
+        # A stored quantised master (the reference's storage of fp8 / int8 projections,
+        # fp8.py:168-222, projection.py:139-232) runs as stored: int8 codes with per-channel
+        # scales (ConvRot when the map says so), e4m3 codes with a per-tensor scale.  Only an
+        # e4m3 master with per-channel scales (fp8.py:88-96 on parts below sm_100) has no
+        # kernel here; it is dequantised once to bf16.
+        self.w_to_q = None
         self.to_out_convrot = None
         if to_out is None and "to_out_linear.weight_fp8" in branch_w:
             stored = branch_w["to_out_linear.weight_fp8"]
@@ -237,15 +280,23 @@ class FusedBlock:
             group = branch_w.get(CONVROT_KEY)
             group = None if group is None else int(group)
             stored_prec = "int8" if stored.dtype == torch.int8 else "fp8"
-            if stored_prec == precision and (stored_prec == "int8" or (group is None and stored_scale.numel() == 1)):
-                to_out_q = QuantizedMatrix(stored.detach().to(dev).contiguous(),
-                                           f32(stored_scale).reshape(-1).contiguous(), precision)
+            if stored_prec == "int8" or (group is None and stored_scale.numel() == 1):
+                self.w_to_q = QuantizedMatrix(stored.detach().to(dev).contiguous(),
+                                              f32(stored_scale).reshape(-1).contiguous(), stored_prec)
                 self.to_out_convrot = group
             else:
                 to_out = dequantize_projection_weight(stored, stored_scale, group)
+        # "bf16", "int8", "fp8" or None (no branch projection)
+        self.to_out_kind = self.w_to_q.precision if self.w_to_q is not None else (
+            "bf16" if to_out is not None else None)
+        # one K-concat GEMM [flat | branch] x [W_out | W_to_out] when both projections are bf16
+        self.concat_out = precision == "bf16" and self.to_out_kind in ("bf16", None)
+        self.w_to_b16 = b16(to_out) if to_out is not None and not self.concat_out else None
         if precision == "bf16":
             self.w_big = torch.cat([b16(qkv_w[qkv_rows]), side_w.to(dev, torch.bfloat16)], 0).contiguous()
-            if shard is not None:
+            if not self.concat_out:
+                self.w_out = b16(out_w)
+            elif shard is not None:
                 # every rank projects all hidden columns of its row block: K in rank-major order
                 self.w_out_cat = b16(rank_major_out_weight(out_w.detach().cpu(), None if to_out is None else
                                                            to_out.detach().cpu(), H_all, D, shard.world))
@@ -265,8 +316,6 @@ class FusedBlock:
             self.w_qkv_q = wq
             self.w_side = side_w.to(dev, torch.bfloat16).contiguous()
             self.w_out_q = quantize_weight(out_w, precision, dev)
-            self.w_to_q = to_out_q if to_out_q is not None else (
-                quantize_weight(to_out, precision, dev) if to_out is not None else None)
         self.bw = BranchDeviceWeights.from_dict(wl, H, D, dev, short_conv=self.short_conv) if self.has_branch \
             else None
         # blocks of one model run one after another on one stream: they may share workspaces
@@ -274,11 +323,16 @@ class FusedBlock:
         self._ws: dict = workspaces if workspaces is not None else {}
 
     # ------------------------------------------------------------------ workspaces
+    def _branch_tile(self, Fb: int):
+        """Frames per branch tile, or None for the untiled branch."""
+        return self.tile_frames if 0 < self.tile_frames < Fb else None
+
     def workspace(self, S: int, layout: VDNLayout | None):
         key = (S, None if layout is None else (layout.num_frames, layout.tokens_per_frame, layout.text_len,
                                                layout.anchor_frames),
                self.geo.heads, self.geo.dim, self.geo.hidden, self.precision, self.n_aux,
-               None if self.shard is None else (self.shard.rank, self.shard.world), self.bw is not None)
+               None if self.shard is None else (self.shard.rank, self.shard.world), self.bw is not None,
+               self.tile_frames)
         ws = self._ws.get(key)
         if ws is None:
             g = self.geo
@@ -303,23 +357,29 @@ class FusedBlock:
             else:
                 ws["flat"] = torch.empty(S, g.inner, **bf)
                 ws["branch"] = torch.zeros(S, g.inner, **bf)
-            if self.precision != "bf16":
-                qdt = torch.int8 if self.precision == "int8" else torch.float8_e4m3fn
-                # the row-split projection quantises only this rank's rows of all heads
-                rows_out = S if self.shard is None else ws["xchg"].cs
-                k_out = self.heads_total * g.dim
-                for name, rows, k in (("xq", S, g.hidden), ("fq", rows_out, k_out), ("bq", rows_out, k_out)):
-                    sdim = rows if self.precision == "int8" else 1
-                    ws[name] = QuantizedMatrix(torch.empty(rows, k, device=dev, dtype=qdt),
-                                               torch.empty(sdim, device=dev, dtype=torch.float32), self.precision)
-                ws["work"] = torch.empty(1, device=dev, dtype=torch.float32)
+            ws["work"] = torch.empty(1, device=dev, dtype=torch.float32)
             if layout is not None and self.bw is not None and not layout.full_cover:
                 skip = layout.anchor_frames == "both"
                 Fb = layout.num_frames - 2 if skip else layout.num_frames
                 if Fb > 0:
-                    ws["bws"] = BranchWorkspace(dev, Fb, layout.tokens_per_frame, g.heads, g.dim, layout.text_len)
+                    ws["bws"] = BranchWorkspace(dev, Fb, layout.tokens_per_frame, g.heads, g.dim, layout.text_len,
+                                                tile_frames=self._branch_tile(Fb))
             self._ws[key] = ws
         return ws
+
+    def quant_buffer(self, ws, name: str, kind: str, rows: int, k: int) -> QuantizedMatrix:
+        """Quantised-activation buffer ``name`` of ``kind`` (int8: per-row scales, fp8: one
+        scale) in the shared workspace, allocated on first use: blocks of one model that
+        share workspaces may store to_out_linear in different kinds (bf16 edge blocks)."""
+        slot = f"{name}_{kind}"
+        buf = ws.get(slot)
+        if buf is None or buf.data.shape[0] < rows or buf.data.shape[1] != k:
+            qdt = torch.int8 if kind == "int8" else torch.float8_e4m3fn
+            dev = self.device
+            buf = QuantizedMatrix(torch.empty(rows, k, device=dev, dtype=qdt),
+                                  torch.empty(rows if kind == "int8" else 1, device=dev, dtype=torch.float32), kind)
+            ws[slot] = buf
+        return buf
 
     # ------------------------------------------------------------------ phases
     def _qkv(self, x, ws, status, stream, q_act=None, rows=None):
@@ -339,11 +399,12 @@ class FusedBlock:
                       aux.stride(0), *qa, status.err_ptr, stream)
             return
         kind = KIND[self.precision]
+        xbuf = self.quant_buffer(ws, "xq", self.precision, ws["qkv"].shape[0], g.hidden)
         if self.precision == "int8":
-            xq = quantize_rows_int8(x, QuantizedMatrix(ws["xq"].data[r0:r1], ws["xq"].scale[r0:r1], "int8"))
+            xq = quantize_rows_int8(x, QuantizedMatrix(xbuf.data[r0:r1], xbuf.scale[r0:r1], "int8"))
             rs, cs, d0, d1 = xq.scale, self.w_qkv_q.scale, None, None
         else:
-            xq = quantize_tensor_fp8(x, ws["xq"], ws["work"])
+            xq = quantize_tensor_fp8(x, QuantizedMatrix(xbuf.data[:S], xbuf.scale, "fp8"), ws["work"])
             rs, cs, d0, d1 = None, None, xq.scale, self.w_qkv_q.scale
         _lib.call("vdn_qkv_gemm", kind, xq.data.data_ptr(), xq.data.stride(0), self.w_qkv_q.data.data_ptr(),
                   self.w_qkv_q.data.stride(0), S, g.hidden, g.inner, 0, g.dim, self.norm_w.data_ptr(), self.eps, 1.0,
@@ -361,30 +422,39 @@ class FusedBlock:
         flat, branch, out = ws["flat"][r0:r1], ws["branch"][r0:r1], out[r0:r1]
         if residual is not None and rows is not None:
             residual = residual.rows(r0, r1 - r0)
-        if self.precision == "bf16":
+        if self.concat_out:
             a2 = branch if with_branch else None
             gemm_block(0, flat, self.w_out_cat, out, a2=a2, k_split=g.inner if with_branch else 0,
                        k=2 * g.inner if with_branch else g.inner, residual=residual, status=status, stream=stream,
                        rows=r1 - r0)
             return
-        self._quantized_out(flat, branch if with_branch else None, ws, out, status, stream, residual=residual)
+        self._two_pass_out(flat, branch if with_branch else None, ws, out, status, stream, residual=residual)
 
-    def _quantized_out(self, flat, branch, ws, out, status, stream, amax_reduce=None,
-                       residual: GatedResidual | None = None):
-        """out = Q(flat) W_out^T (+ Q(branch) W_to^T as an addend pass), quantised
-        activations: int8 per row, fp8 per tensor (``amax_reduce`` combines the amax of
-        the ranks' row blocks).  With a ``residual`` both passes are gated and the first
-        adds the residual stream."""
-        kind = KIND[self.precision]
+    def _two_pass_out(self, flat, branch, ws, out, status, stream, amax_reduce=None,
+                      residual: GatedResidual | None = None):
+        """out = P(flat) W_out^T, then + P'(branch) W_to^T as an addend pass, each in its own
+        arithmetic: out_proj in the block's precision, to_out_linear in the kind its map
+        stores.  Quantised activations are int8 per row (ConvRot for a ConvRot master) or
+        e4m3 per tensor (``amax_reduce`` combines the amax of the ranks' row blocks).  With a
+        ``residual`` both passes are gated and the first adds the residual stream."""
         rows = flat.shape[0]
         K = flat.shape[1]
 
-        def quantized_gemm(src, buf: QuantizedMatrix, w: QuantizedMatrix, addend, first, convrot=None):
-            if rows == 0 and self.precision == "int8":
+        def project_pass(src, name, kind, w, first, convrot=None):
+            res = None
+            if residual is not None:
+                res = residual if first else GatedResidual(out, residual.gate, residual.group)
+            addend = None if (first or res is not None) else out
+            if kind == "bf16":
+                if rows > 0:
+                    gemm_block(0, src, w, out, residual=res, addend=addend, status=status, stream=stream, rows=rows,
+                               k=K)
+                return
+            if rows == 0 and kind == "int8":
                 return  # per-row scales: nothing to combine across ranks
-            buf = QuantizedMatrix(buf.data[:rows], buf.scale[:rows] if self.precision == "int8" else buf.scale,
-                                  self.precision)
-            if self.precision == "int8":
+            buf = self.quant_buffer(ws, name, kind, rows, K)
+            buf = QuantizedMatrix(buf.data[:rows], buf.scale[:rows] if kind == "int8" else buf.scale, kind)
+            if kind == "int8":
                 qa = quantize_rows_int8(src, buf) if convrot is None else \
                     quantize_rows_int8_convrot(src, buf, group=convrot)
                 rs, cs, d0, d1 = qa.scale, w.scale, None, None
@@ -393,15 +463,19 @@ class FusedBlock:
                 rs, cs, d0, d1 = None, None, qa.scale, w.scale
             if rows == 0:
                 return
-            res = None
-            if residual is not None:
-                res = residual if first else GatedResidual(out, residual.gate, residual.group)
-            gemm_block(kind, qa.data, w.data, out, dev_scales=(d0, d1), row_scale=rs, col_scale=cs, residual=res,
-                       addend=None if res is not None else addend, status=status, stream=stream, rows=rows, k=K)
+            gemm_block(KIND[kind], qa.data, w.data, out, dev_scales=(d0, d1), row_scale=rs, col_scale=cs,
+                       residual=res, addend=addend, status=status, stream=stream, rows=rows, k=K)
 
-        quantized_gemm(flat, ws["fq"], self.w_out_q, None, True)
-        if branch is not None and self.w_to_q is not None:
-            quantized_gemm(branch, ws["bq"], self.w_to_q, out, False, self.to_out_convrot)
+        if self.precision == "bf16":
+            project_pass(flat, "fq", "bf16", self.w_out, True)
+        else:
+            project_pass(flat, "fq", self.precision, self.w_out_q, True)
+        if branch is None or self.to_out_kind is None:
+            return
+        if self.to_out_kind == "bf16":
+            project_pass(branch, "bq", "bf16", self.w_to_b16, False)
+        else:
+            project_pass(branch, "bq", self.to_out_kind, self.w_to_q, False, self.to_out_convrot)
 
     def project_rows(self, ws, with_branch, recv, rows, out_rows, status, stream, amax_reduce=None,
                      residual: GatedResidual | None = None):
@@ -410,14 +484,14 @@ class FusedBlock:
         (``residual``: already restricted to those rows)."""
         g = self.geo
         world = recv.shape[0]
-        if self.precision == "bf16":
+        if self.concat_out:
             if rows > 0:
                 gemm_block(0, recv, self.w_out_cat, out_rows, grouped=(world, 2 * g.inner, recv.stride(0)),
                            residual=residual, status=status, stream=stream, rows=rows)
             return
         flat, branch = split_heads_outputs(concat_rows(recv, rows), world, g.inner)
-        self._quantized_out(flat, branch if with_branch else None, ws, out_rows, status, stream,
-                            amax_reduce=amax_reduce, residual=residual)
+        self._two_pass_out(flat, branch if with_branch else None, ws, out_rows, status, stream,
+                           amax_reduce=amax_reduce, residual=residual)
 
     def _out_sharded(self, ws, with_branch, status, stream, residual: GatedResidual | None = None,
                      row_epilogue=None) -> torch.Tensor:
@@ -443,7 +517,7 @@ class FusedBlock:
         return xchg.project_and_gather(project)
 
     def forward(self, x: torch.Tensor, layout: VDNLayout, plans: WindowPlanCache, status: _lib.DeviceStatus,
-                *, linear_enabled=True, bridge="alpha", enable_text_state=True, out=None,
+                *, linear_enabled=True, bridge=None, enable_text_state=None, out=None,
                 residual: GatedResidual | None = None, row_epilogue=None, io: StreamIO | None = None,
                 rope: RopeTable | None = None) -> torch.Tensor:
         """The block output [S, hidden]; with ``residual`` the gated residual stream
@@ -473,12 +547,15 @@ class FusedBlock:
         return out
 
     def forward_heads(self, x: torch.Tensor, layout: VDNLayout, plans: WindowPlanCache, status: _lib.DeviceStatus,
-                      *, linear_enabled=True, bridge="alpha", enable_text_state=True, io: StreamIO | None = None,
+                      *, linear_enabled=True, bridge=None, enable_text_state=None, io: StreamIO | None = None,
                       rope: RopeTable | None = None):
         """Phases 1-3 (QKV, branch, window attention) for this rank's heads; returns the
-        workspace holding the per-head outputs and whether the branch ran."""
+        workspace holding the per-head outputs and whether the branch ran.  ``bridge`` /
+        ``enable_text_state``: None takes the block's own settings."""
         g = self.geo
         S = x.shape[0]
+        bridge = self.bridge if bridge is None else bridge
+        enable_text_state = self.enable_text_state if enable_text_state is None else bool(enable_text_state)
         by_blocks = (io is not None and x.dtype == torch.bfloat16 and x.stride(-1) == 1 and self.shard is None and
                      self.precision != "fp8" and len(io.in_blocks) > 1)
         if io is not None and not by_blocks:
@@ -494,7 +571,8 @@ class FusedBlock:
             tpf = layout.tokens_per_frame
             Fb = layout.num_frames - 2 if skip else layout.num_frames
             r0 = layout.video_start + (tpf if skip else 0)
-            if "q" not in self.short_conv:  # q's features need no conv: the QKV epilogue writes them
+            if "q" not in self.short_conv and ws["bws"].tile_frames is None:
+                # q's features need no conv: the QKV epilogue writes them (untiled branch)
                 q_act = (ws["bws"].qf, r0, Fb * tpf, tpf)
         if by_blocks:
             # project each row block of x as soon as its copy has landed
@@ -514,7 +592,7 @@ class FusedBlock:
                       bridge=bridge, out=ws["branch"], out_row0=r0, status=status, short_conv=self.short_conv,
                       delta_rule=self.delta_rule,
                       q_ready=q_act is not None)
-            if enable_text_state and layout.text_len > 0:
+            if enable_text_state and layout.text_len > 0:  # hybrid.py:449-451
                 ts = slice(layout.text_start, layout.text_start + layout.text_len)
                 kw.update(text_k=qkv[ts, g.inner:2 * g.inner], text_v=qkv[ts, 2 * g.inner:], text_aux=aux[ts])
             run_branch(ws["bws"], self.bw, **kw)
@@ -553,7 +631,8 @@ class B200State:
     Every rank then runs the patched forward on the same x and gets the full output."""
 
     def __init__(self, name, config: Mapping, branches, num_heads, head_dim, *, attention_backend="b200",
-                 projection_precision="bf16", inference=True, weight_maps=None, shard_heads=False, **_ignored):
+                 projection_precision="bf16", inference=True, weight_maps=None, shard_heads=False, tile_frames=0,
+                 **_ignored):
         if attention_backend not in ATTENTION_BACKENDS:
             raise ValueError(f"unsupported attention backend {attention_backend!r}")
         if projection_precision not in ("bf16", "fp8", "int8"):
@@ -565,6 +644,9 @@ class B200State:
         self.attention_backend = attention_backend
         self.projection_precision = projection_precision
         self.inference = bool(inference)
+        if isinstance(tile_frames, bool) or not isinstance(tile_frames, int) or tile_frames < 0:
+            raise ValueError("tile_frames must be a non-negative integer")  # nodes.py:247-248
+        self.tile_frames = tile_frames  # the runtime's frame tiling (hybrid.py:51), for branches without their own
         maps = list(weight_maps) if weight_maps is not None else [
             b if isinstance(b, Mapping) else getattr(b, "w") for b in branches]
         self.branches = list(branches)
@@ -589,16 +671,17 @@ class B200State:
         fb = self.blocks.get(index)
         if fb is None:
             cfg = self.config
-            # the branch object's own rule (LinearBranch.delta_rule), else the node config's
-            # (nodes.py:106)
+            # each setting from the block's branch object, else the node config, else the
+            # reference default (nodes.py:98-116, hybrid.py:449-451)
             owner = self.branches[index] if index < len(self.branches) else None
-            rule = getattr(owner, "delta_rule", None) or cfg.get("delta_rule", "vdn_solve")
+            setting = {name: branch_setting(owner, cfg, name) for name in BRANCH_SETTING_DEFAULTS}
+            tile = getattr(owner, "tile_frames", None) if not isinstance(owner, Mapping) else None
             fb = FusedBlock(_weight_of(attn.qkv_proj), _weight_of(attn.q_norm), _weight_of(attn.k_norm),
                             _weight_of(attn.out_proj), self.weight_maps[index], self.num_heads, self.head_dim,
                             device, precision=self.projection_precision, eps=float(getattr(attn.q_norm, "eps", 1e-6)),
-                            enable_gate=bool(cfg.get("enable_softmax_gate", True)),
-                            short_conv=tuple(cfg.get("short_conv", ("k", "v"))), shard=self.shard,
-                            workspaces=self.workspaces, delta_rule=rule)
+                            enable_gate=bool(cfg.get("enable_softmax_gate", True)), shard=self.shard,
+                            workspaces=self.workspaces, tile_frames=int(self.tile_frames if tile is None else tile),
+                            **setting)
             self.blocks[index] = fb
         return fb
 
@@ -627,10 +710,9 @@ def make_vdn_forward(attn, state: B200State, block_index: int):
         rope = rope_table(rope_freqs, layout.seq_len, head_dim, x.device)
         status = state.device_status(x.device)
         block = state.fused_block(attn, block_index, x.device)
+        # the branch settings were resolved when the block was built (B200State.fused_block)
         out = block.forward(x, layout, state.window_plans, status,
                             linear_enabled=bool(config.get("linear_enabled", True)),
-                            bridge=str(config.get("bridge", "alpha")),
-                            enable_text_state=bool(config.get("enable_text_state", True)),
                             io=(transformer_options or {}).get(STREAM_IO_KEY), rope=rope)
         state.last_attention_backend = "b200_dense" if layout.full_cover else "b200"
         return out.to(x.dtype)
@@ -650,4 +732,5 @@ def run_forward_checked(state: B200State, fn, *args, **kwargs):
     return result
 
 
-__all__ = ["B200State", "FusedBlock", "RopeTable", "make_vdn_forward", "rope_table", "run_forward_checked"]
+__all__ = ["BRANCH_SETTING_DEFAULTS", "B200State", "FusedBlock", "RopeTable", "branch_setting", "make_vdn_forward",
+           "rope_table", "run_forward_checked"]

@@ -6,14 +6,16 @@
  *   - pointers are CUDA device pointers (row-major, pitches in elements), sizes are
  *     plain ints; `stream` is a cudaStream_t passed as void*; all work is stream-ordered;
  *   - the return value is a status: 0 ok, -1 invalid argument, -2 unsupported geometry,
- *     -3 TMA tensor-map encoding failed, -4 launch failed, -5 misaligned pointer/pitch;
+ *     -3 TMA tensor-map encoding failed, -4 launch failed, -5 misaligned pointer/pitch,
+ *     -6 problem larger than a fixed device scratch area;
  *   - `dev_err` (where present) is a device int that receives the first kernel abort
  *     code (1..4: a bounded wait timed out); the host checks it once per forward;
  *   - bf16 = __nv_bfloat16, fp8 = e4m3 (float8_e4m3fn), int8 = signed char.
  *
  * The reference is pure Python/torch; each function below names the reference code it
- * replaces (file:line inside the reference project).  A Python host binds them with
- * ctypes.
+ * replaces (file:line inside the reference project).  The package's Python host binds every
+ * entry point with ctypes (argument types declared per function, int status returned),
+ * mapping the status codes onto the exceptions the reference raises.
  */
 #ifndef VDN_B200_H
 #define VDN_B200_H
@@ -106,9 +108,10 @@ int vdn_fp8_cast(int src_kind, const void* x, long long ldx, int rows, int K, co
  * memory arena it does not own or a host that hands the library a fixed device budget).
  * out[M, N] bf16 = x[M, K] bf16 * W^T with x quantised per tensor to e4m3 in the library's
  * own file-scope device scratch array; W [N, K] e4m3, w_scale one fp32 device scalar.
- * Limit: M * K <= 16,777,216 (else -6, nothing done); K % 16 == 0.  The array (~16 MiB)
- * stays resident on every GPU that loads the library; the first call on a device looks up
- * its address (make it before any stream capture); calls that overlap on the GPU race. */
+ * Limit: M * K <= 16,777,216 (else -6, nothing done); K % 16 == 0; ldx, ldw >= K and
+ * ldo >= N (else -1).  The array (~16 MiB) stays resident on every GPU that loads the
+ * library; the first call on a device looks up its address (make it before any stream
+ * capture); calls that overlap on the GPU race. */
 int vdn_fp8_linear_noalloc(const void* x, long long ldx, int M, int K, const void* w_fp8, long long ldw, int N,
                            const float* w_scale, void* out, long long ldo, int* dev_err, void* stream);
 

@@ -37,6 +37,7 @@ FP8_MAX = 448.0  # fp8.py:30 (float8_e4m3fn max)
 
 
 _COMPUTE = [F64]
+_MATMUL = [None]  # None: GEMM operands in the compute dtype; torch.bfloat16: the reference's bf16 GEMMs
 
 
 def set_compute_dtype(dtype) -> torch.dtype:
@@ -44,6 +45,19 @@ def set_compute_dtype(dtype) -> torch.dtype:
     reference's CPU path for the timed CPU baseline).  Returns the previous dtype."""
     prev = _COMPUTE[0]
     _COMPUTE[0] = dtype
+    return prev
+
+
+def set_matmul_dtype(dtype):
+    """Operand dtype of the block's large products: the bf16 projections (``project``) and
+    the window attention's two products.  None keeps them in the compute dtype (the parity
+    checks); ``torch.bfloat16`` runs them as the reference's bf16 path does on its own
+    torch ops -- bf16 operands, bf16 results (hybrid.py:260-268, window.py:197-216) -- with
+    the statistics, factor and scans still in the compute dtype (branch.py:197-243 keeps
+    them in fp32).  Used to time the reference path at config 1's dtype.  Returns the
+    previous setting."""
+    prev = _MATMUL[0]
+    _MATMUL[0] = dtype
     return prev
 
 
@@ -159,6 +173,68 @@ def window_attention(q, k, v, vs, ve, num_frames, tpf, bounds, scale, anchors="n
     return out
 
 
+def frame_key_sets(num_frames, bounds, anchors):
+    """Runs of consecutive frames whose rows see the same key frames (window.py:248-274):
+    [(first, stop, frames)], ``frames`` None for anchor-frame rows that see every key."""
+    last = num_frames - 1
+    runs = []
+    for f in range(num_frames):
+        if anchors in ("rows", "both") and f in (0, last):
+            sig = None
+        else:
+            sel = set(range(max(bounds[f][0], 0), min(bounds[f][1], last) + 1))
+            if anchors in ("columns", "both"):
+                sel.update((0, last))
+            sig = tuple(sorted(sel))
+        if runs and runs[-1][2] == sig and runs[-1][1] == f:
+            runs[-1] = (runs[-1][0], f + 1, sig)
+        else:
+            runs.append((f, f + 1, sig))
+    return runs
+
+
+def _sdpa_rows(q, k, v, scale):
+    """softmax(q k^T * scale) v for [rows, H, D] operands, in the matmul dtype when set."""
+    md = _MATMUL[0] or q.dtype
+
+    def heads_major(t):  # [rows, H, D] -> contiguous [1, H, rows, D] (the fused CPU kernel's layout)
+        return t.to(md).permute(1, 0, 2).contiguous().unsqueeze(0)
+
+    o = F.scaled_dot_product_attention(heads_major(q), heads_major(k), heads_major(v), scale=scale)
+    return o[0].permute(1, 0, 2).to(q.dtype)
+
+
+def window_attention_grouped(q, k, v, vs, ve, num_frames, tpf, bounds, scale, anchors="none",
+                             rows=None) -> torch.Tensor:
+    """The same exact window softmax as ``window_attention``, computed the way the reference's
+    grouped backend does (window.py:277-313): global rows against every key; each run of
+    frames with one key set against the gathered [global rows, visible frames] keys only, so
+    the work is the allowed pairs rather than the dense square.  ``rows``: restrict the
+    output to these query rows (sorted or not); returns [len(rows), H, D] then."""
+    q, k, v = _t(q), _t(k), _t(v)
+    seq = q.shape[0]
+    want = torch.arange(seq) if rows is None else torch.as_tensor(rows, dtype=torch.long)
+    need = torch.zeros(seq, dtype=torch.bool)
+    need[want] = True
+    out = torch.zeros(seq, q.shape[1], q.shape[2], dtype=q.dtype)
+    glob = torch.cat([torch.arange(0, vs), torch.arange(ve, seq)])
+    g_rows = glob[need[glob]]
+    if len(g_rows):
+        out[g_rows] = _sdpa_rows(q[g_rows], k, v, scale)
+    for first, stop, frames in frame_key_sets(num_frames, bounds, anchors):
+        r = torch.arange(vs + first * tpf, vs + stop * tpf)
+        r = r[need[r]]
+        if not len(r):
+            continue
+        if frames is None:
+            keys = torch.arange(seq)
+        else:
+            vid = torch.cat([torch.arange(vs + f * tpf, vs + (f + 1) * tpf) for f in frames])
+            keys = torch.cat([glob, vid])
+        out[r] = _sdpa_rows(q[r], k[keys], v[keys], scale)
+    return out[want]
+
+
 def key_count_per_row(seq, vs, ve, num_frames, tpf, bounds, anchors) -> np.ndarray:
     """Allowed keys per query row, computed from intervals (no [S,S] mask)."""
     out = np.empty(seq, dtype=np.int64)
@@ -234,9 +310,10 @@ def to_fhsd(tokens, num_frames) -> torch.Tensor:
 def frame_statistics(key, value, beta) -> tuple[torch.Tensor, torch.Tensor]:
     """A = sym((beta*K)^T K), B = (beta*V)^T K per frame/head (branch.py:197-243)."""
     key, value, beta = _t(key), _t(value), _t(beta)
-    a = torch.einsum("fhsk,fhsl,fhs->fhkl", key, key, beta)
+    kb = key * beta[..., None]  # [F, H, S, D]: two-operand products keep memory at the input size
+    a = kb.transpose(-1, -2) @ key
     a = 0.5 * (a + a.transpose(-1, -2))
-    b = torch.einsum("fhsv,fhsk,fhs->fhvk", value, key, beta)
+    b = (value * beta[..., None]).transpose(-1, -2) @ key
     return a, b
 
 
@@ -359,6 +436,13 @@ class BranchConfig:
     bridge: str = "alpha"
     short_conv: tuple = ("k", "v")
     enable_text_state: bool = True
+
+    def node_config(self, **extra) -> dict:
+        """The node config that builds this branch structure (nodes.py:98-116 reads these
+        keys, defaulting to short_conv=() and enable_text_state=False when they are absent),
+        with the softmax gate on."""
+        return dict(enable_softmax_gate=True, delta_rule=self.delta_rule, bridge=self.bridge,
+                    short_conv=tuple(self.short_conv), enable_text_state=self.enable_text_state, **extra)
 
 
 def text_state(weights, text_x, text_k, text_v, heads, dim, cfg: BranchConfig):
@@ -532,6 +616,9 @@ def fp8_quantize_tensor(x) -> tuple[torch.Tensor, float]:
 
 def project(rows, w, precision="bf16"):
     """``rows @ W^T`` under the chosen precision; float64 result (projection.py:259-268)."""
+    if precision == "bf16" and _MATMUL[0] is not None:
+        md = _MATMUL[0]
+        return (_t(rows).to(md) @ _t(w).to(md).T).to(_COMPUTE[0])
     if precision == "bf16" or precision == "fp64":
         return _t(rows) @ _t(w).T
     if precision == "int8":
@@ -563,15 +650,25 @@ class BlockWeights:
 
 def block_forward(x, bw: BlockWeights, lay: Layout, heads, dim, cfg: BranchConfig,
                   *, enable_softmax_gate=True, linear_enabled=True, precision="bf16",
-                  return_parts=False, rope_freqs=None, to_out_convrot=False):
+                  return_parts=False, rope_freqs=None, to_out_convrot=False, to_out_precision=None,
+                  attention="dense", rows=None):
     """VDN hybrid block forward: QKV, branch on raw video q/k/v, q/k RMSNorm, window
     softmax, per-token head gate, out_proj, delta add on video rows (hybrid.py:409-579).
 
     ``precision`` selects the projection arithmetic of qkv/out_proj/to_out_linear
     (``bf16`` = exact float64 here; ``int8``/``fp8`` = the config-2 quantised schemes).
     ``to_out_convrot`` (int8 only): ``to_out_linear`` through ConvRot int8 instead, the
-    reference's INT8 projection (projection.py:243-256).
+    reference's INT8 projection (projection.py:243-256).  ``to_out_precision`` (default:
+    ``precision``) is the arithmetic of ``to_out_linear`` alone: the reference projects it in
+    the representation its map stores (projection.py:259-268), e.g. bf16 for the edge blocks
+    an fp8 model keeps (fp8.py:198).
+    ``attention``: ``dense`` (masked square, ``window_attention``) or ``grouped`` (the
+    reference's gathered-key spelling, ``window_attention_grouped``; same result, a fraction
+    of the work at video sizes).  ``rows``: output only these rows ([len(rows), hidden]):
+    the projections of x and the branch statistics still cover every row (keys and frame
+    states need them), the attention, gate and output projections only the requested ones.
     """
+    to_out_precision = precision if to_out_precision is None else to_out_precision
     x = _t(x)
     seq = x.shape[0]
     inner = heads * dim
@@ -593,31 +690,46 @@ def block_forward(x, bw: BlockWeights, lay: Layout, heads, dim, cfg: BranchConfi
             text_x=x[ta:tb] if text else None, text_k=k_raw[ta:tb] if text else None,
             text_v=v[ta:tb] if text else None, skip_ends=(lay.anchor_frames == "both"),
         )
-        if to_out_convrot and precision == "int8":
-            delta = project_int8_convrot(readout, w["to_out_linear.weight"])
-        else:
-            delta = project(readout, w["to_out_linear.weight"], precision)
         parts["readout"] = readout
+    sel = torch.arange(seq) if rows is None else torch.as_tensor(rows, dtype=torch.long)
+    if linear_active:
+        va, vb = lay.video_start, lay.video_end
+        in_video = (sel >= va) & (sel < vb)
+        r_read = readout if rows is None else readout[sel[in_video] - va]
+        if to_out_convrot and to_out_precision == "int8":
+            d = project_int8_convrot(r_read, w["to_out_linear.weight"])
+        else:
+            d = project(r_read, w["to_out_linear.weight"], to_out_precision)
+        if rows is None:
+            delta = d
+        else:
+            delta = torch.zeros(len(sel), d.shape[1], dtype=d.dtype)
+            delta[in_video] = d
     qn = rms_norm(q_raw, bw.q_norm, 1e-6)
     kn = rms_norm(k_raw, bw.k_norm, 1e-6)
     if rope_freqs is not None:  # after the norm, softmax path only (the branch read q_raw)
         qn, kn = rope_split_half(qn, rope_freqs), rope_split_half(kn, rope_freqs)
     scale = dim ** -0.5
+    attend = window_attention_grouped if attention == "grouped" else window_attention
     if lay.full_cover:
-        soft = window_attention(qn, kn, v, 0, seq, 1, seq, [(0, 0)], scale, "none")
+        soft = attend(qn, kn, v, 0, seq, 1, seq, [(0, 0)], scale, "none", rows=rows)
     else:
-        soft = window_attention(qn, kn, v, lay.video_start, lay.video_end, lay.num_frames,
-                                lay.tokens_per_frame, list(lay.bounds), scale, lay.anchor_frames)
+        soft = attend(qn, kn, v, lay.video_start, lay.video_end, lay.num_frames, lay.tokens_per_frame,
+                      list(lay.bounds), scale, lay.anchor_frames, rows=rows)
     parts["softmax"] = soft
+    xs = x[sel]
     if enable_softmax_gate:
-        g = torch.sigmoid(x @ _t(w["softmax_gate.up.weight"]).T + _t(w["softmax_gate.up.bias"]))
-        flat = (soft * g.reshape(seq, heads, 1)).reshape(seq, inner)
+        g = torch.sigmoid(xs @ _t(w["softmax_gate.up.weight"]).T + _t(w["softmax_gate.up.bias"]))
+        flat = (soft * g.reshape(len(sel), heads, 1)).reshape(len(sel), inner)
         parts["gate"] = g
     else:
-        flat = soft.reshape(seq, inner)
+        flat = soft.reshape(len(sel), inner)
     out = project(flat, bw.out, precision)
     if delta is not None:
-        out[lay.video_start:lay.video_end] += delta
+        if rows is None:
+            out[lay.video_start:lay.video_end] += delta
+        else:
+            out += delta
         parts["delta"] = delta
     return (out, parts) if return_parts else out
 

@@ -26,7 +26,7 @@ def rel_l2(got, want):
 
 
 def _run_block(bw, lay, heads, dim, x, precision="bf16", config=None):
-    state = pkg.B200State("t", config or {"enable_softmax_gate": True}, [bw.branch], heads, dim,
+    state = pkg.B200State("t", config or vo.BranchConfig().node_config(), [bw.branch], heads, dim,
                           projection_precision=precision)
     attn = _Attn(bw, heads, dim)
     fwd = pkg.make_vdn_forward(attn, state, 0)
@@ -98,7 +98,7 @@ def test_block_d128_ragged_frames_matches_oracle(delta_rule):
     lay_o = vo.config_layout(c)
     x = vo.make_x(4, lay_o.seq_len, c["hidden"])
     got = _run_block(bw, _layout(c), c["heads"], c["dim"], x,
-                     config={"enable_softmax_gate": True, "delta_rule": delta_rule})
+                     config=vo.BranchConfig(delta_rule=delta_rule).node_config())
     want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(delta_rule=delta_rule))
     assert rel_l2(got, want) < 2e-2
 
@@ -111,7 +111,7 @@ def test_block_with_rope_matches_oracle():
     lay_o = vo.config_layout(c)
     x = vo.make_x(4, lay_o.seq_len, c["hidden"])
     freqs = vo.make_rope_freqs(lay_o.seq_len, 128)
-    state = pkg.B200State("t", {"enable_softmax_gate": True}, [bw.branch], c["heads"], c["dim"])
+    state = pkg.B200State("t", vo.BranchConfig().node_config(), [bw.branch], c["heads"], c["dim"])
     fwd = pkg.make_vdn_forward(_Attn(bw, c["heads"], c["dim"]), state, 0)
     rope = freqs.reshape(1, lay_o.seq_len, 1, 64, 2, 2).to(DEV)
     with pkg.publish_layout(_layout(c)):
@@ -130,7 +130,7 @@ def test_block_sana_rule_matches_oracle_and_golden():
     lay_o = vo.config_layout(c)
     x = vo.make_x(0, lay_o.seq_len, c["hidden"])
     got = _run_block(bw, _layout(c), c["heads"], c["dim"], x,
-                     config={"enable_softmax_gate": True, "delta_rule": "sana_scaled"})
+                     config=vo.BranchConfig(delta_rule="sana_scaled").node_config())
     want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(delta_rule="sana_scaled"))
     assert rel_l2(got, want) < 2e-2
     golden = dict(np.load(GOLDEN))
@@ -154,7 +154,7 @@ def test_host_streamer_matches_direct_forward():
     c = vo.CONFIG0
     bw = vo.make_block(7, c["hidden"], c["heads"], c["dim"])
     lay = _layout(c)
-    state = pkg.B200State("t", {"enable_softmax_gate": True}, [bw.branch], c["heads"], c["dim"])
+    state = pkg.B200State("t", vo.BranchConfig().node_config(), [bw.branch], c["heads"], c["dim"])
     fwd = pkg.make_vdn_forward(_Attn(bw, c["heads"], c["dim"]), state, 0)
 
     def run(xd):
@@ -179,7 +179,7 @@ def test_host_streamer_by_row_blocks_matches_direct_forward(precision):
     c = dict(vo.CONFIG0, frames=15, grid=(8, 8))  # 992 rows: several 128-row blocks
     bw = vo.make_block(9, c["hidden"], c["heads"], c["dim"])
     lay = _layout(c)
-    state = pkg.B200State("t", {"enable_softmax_gate": True}, [bw.branch], c["heads"], c["dim"],
+    state = pkg.B200State("t", vo.BranchConfig().node_config(), [bw.branch], c["heads"], c["dim"],
                           projection_precision=precision)
     fwd = pkg.make_vdn_forward(_Attn(bw, c["heads"], c["dim"]), state, 0)
 
@@ -219,3 +219,63 @@ def test_block_on_packed_layout_with_global_segments(order):
     got = _run_block(bw, lay, H, D, x)
     want = vo.block_forward(x, bw, lay_o, H, D, vo.BranchConfig())
     assert rel_l2(got, want) < 2e-2
+
+
+def test_fp8_state_edge_block_projects_its_bf16_master_in_bf16():
+    """An fp8 model keeps to_out_linear of its edge blocks in bf16 (fp8.py:35, :198):
+    prepare_projection_maps leaves block 0 of nine with its bf16 weight, and that block's
+    branch delta must come out of the bf16 projection while qkv / out_proj run in fp8."""
+    c = dict(vo.CONFIG0, heads=2, dim=128)
+    bw = vo.make_block(3, c["hidden"], c["heads"], c["dim"])
+    lay_o = vo.config_layout(c)
+    x = vo.make_x(3, lay_o.seq_len, c["hidden"]).to(torch.bfloat16).float()
+    maps, info = pkg.prepare_projection_maps([bw.branch] * 9, DEV, "fp8")
+    assert info["skip_end_blocks"] == 4 and "to_out_linear.weight" in maps[0]
+    assert "to_out_linear.weight_fp8" in maps[4]
+    state = pkg.B200State("t", vo.BranchConfig().node_config(), [bw.branch] * 9, c["heads"], c["dim"],
+                          projection_precision="fp8", weight_maps=maps)
+    fwd = pkg.make_vdn_forward(_Attn(bw, c["heads"], c["dim"]), state, 0)
+    with pkg.publish_layout(_layout(c)):
+        got = pkg.run_forward_checked(state, fwd, x.to(DEV, torch.bfloat16))
+    torch.cuda.synchronize()
+    assert state.blocks[0].to_out_kind == "bf16"
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(), precision="fp8",
+                            to_out_precision="bf16")
+    all_fp8 = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(), precision="fp8")
+    assert rel_l2(got, want) < 3e-2
+    # the edge block's branch delta is the bf16 one: closer to the bf16-to_out oracle than
+    # to one that quantises to_out_linear too
+    assert rel_l2(got, want) < rel_l2(got, all_fp8)
+
+
+def test_spd_failure_in_an_early_block_survives_later_blocks():
+    """Two blocks share one workspace (as a model's blocks do).  A NaN in one video row of
+    block 0's input makes its clip factor fail (the temporal conv carries the NaN two frames
+    each way); block 1 is clean.  The deferred check at the scope's exit still names block 0's
+    factor: factor 1 (block 0 factors its text frame first, branch.py:795-799), batch
+    (first bad frame) * H."""
+    c = dict(text=64, frames=9, grid=(4, 6), heads=2, dim=128, hidden=256)
+    H, D = c["heads"], c["dim"]
+    lay = _layout(c)
+    shared = {}
+    blocks = []
+    for seed in (5, 6):
+        bw = vo.make_block(seed, c["hidden"], H, D)
+        blocks.append(pkg.FusedBlock(bw.qkv, bw.q_norm, bw.k_norm, bw.out, bw.branch, H, D, DEV, workspaces=shared))
+    x = vo.make_x(5, lay.seq_len, c["hidden"]).to(DEV, torch.bfloat16)
+    x_bad = x.clone()
+    bad_frame = 4  # branch frame (video frame 5): branch frames 2..6 see the NaN
+    x_bad[lay.video_start + (bad_frame + 1) * lay.tokens_per_frame + 3] = float("nan")
+    plans, status = pkg.WindowPlanCache(), pkg.DeviceStatus(DEV)
+    with pytest.raises(torch.linalg.LinAlgError,
+                       match=f"factor 1, batch {(bad_frame - 2) * H}: leading minor of order 1 "):
+        with pkg.cholesky_runtime_scope():
+            blocks[0].forward(x_bad, lay, plans, status)
+            blocks[1].forward(x, lay, plans, status)
+    torch.cuda.synchronize()
+    # the same two blocks on clean inputs raise nothing
+    with pkg.cholesky_runtime_scope():
+        blocks[0].forward(x, lay, plans, status)
+        blocks[1].forward(x, lay, plans, status)
+    torch.cuda.synchronize()
+    status.raise_if_failed()

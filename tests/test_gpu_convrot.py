@@ -96,7 +96,7 @@ def _block_case():
 def _run_block_maps(bw, maps, c, x, precision):
     from __graft_entry__ import _Attn
 
-    state = pkg.B200State("t", {"enable_softmax_gate": True}, [bw.branch], c["heads"], c["dim"],
+    state = pkg.B200State("t", vo.BranchConfig().node_config(), [bw.branch], c["heads"], c["dim"],
                           projection_precision=precision, weight_maps=maps)
     fwd = pkg.make_vdn_forward(_Attn(bw, c["heads"], c["dim"]), state, 0)
     with pkg.publish_layout(pkg.make_layout(c["text"], c["frames"], c["grid"])):
@@ -119,24 +119,22 @@ def test_int8_block_runs_a_convrot_to_out_master_as_stored():
     assert rel_l2(got, exact) < 3e-2
 
 
-@pytest.mark.parametrize("stored", ["int8_convrot", "fp8"])
-def test_bf16_block_dequantises_a_stored_master(stored):
-    """A bf16 block given a quantised to_out_linear master runs its dequantised weight (the
-    branch delta is as large as the output at this size, so dropping it would show)."""
+@pytest.mark.parametrize("stored", ["int8", "int8_convrot", "fp8"])
+def test_bf16_block_runs_a_stored_master_as_stored(stored):
+    """A bf16 block given a quantised to_out_linear master projects the branch in that
+    master's arithmetic, as the reference's project() dispatches on the stored weight
+    (projection.py:259-268), while out_proj stays bf16 (the branch delta is as large as the
+    output at this size, so a wrong or missing branch projection would show)."""
     c, bw, lay_o, x = _block_case()
     prec = "int8" if stored.startswith("int8") else "fp8"
     maps, _ = pkg.prepare_projection_maps([bw.branch], DEV, prec, skip_end_blocks=0,
                                           convrot=stored == "int8_convrot")
-    m = maps[0]
-    w_deq = pkg.projection.dequantize_projection_weight(m["to_out_linear.weight_fp8"], m["to_out_linear.weight_scale"],
-                                                        m.get(pkg.projection.CONVROT_KEY))
     got = _run_block_maps(bw, maps, c, x, "bf16")
-    bw_deq = vo.BlockWeights(bw.qkv, bw.q_norm, bw.k_norm, bw.out, dict(bw.branch, **{"to_out_linear.weight": w_deq}))
-    want = vo.block_forward(x, bw_deq, lay_o, c["heads"], c["dim"], vo.BranchConfig())
-    assert rel_l2(got, want) < 2e-2
-    # the dequantised master is the original weight to within its quantisation step
-    w = bw.branch["to_out_linear.weight"].double()
-    assert rel_l2(w_deq, w) < 3e-2
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(), precision="bf16",
+                            to_out_precision=prec, to_out_convrot=stored == "int8_convrot")
+    exact = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig())
+    assert rel_l2(got, want) < (2e-2 if prec == "int8" else 3e-2)
+    assert rel_l2(got, exact) < (3e-2 if prec == "int8" else 8e-2)
 
 
 def test_fp8_block_runs_a_per_tensor_master_as_stored():

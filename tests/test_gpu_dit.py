@@ -221,7 +221,7 @@ def test_fast_block_forward_is_a_drop_in():
     dw = _dit(11, "swiglu")
     mods = [m.to(torch.bfloat16) for m in vo.make_mods(11, 2, hidden)]
     blk = _comfy_block(dw, [_b16(m) for m in mods])
-    state = pkg.B200State("dit", {"enable_softmax_gate": True}, [dw.attn.branch], H, D)
+    state = pkg.B200State("dit", vo.BranchConfig().node_config(), [dw.attn.branch], H, D)
     fwd = pkg.make_fast_block_forward(blk, state, 0)
     x = vo.make_x(11, lay_o.seq_len, hidden).to(torch.bfloat16)
     t_emb = torch.tensor(1.0, device=DEV, dtype=torch.bfloat16)

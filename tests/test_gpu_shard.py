@@ -126,12 +126,12 @@ def _nccl_worker(rank, world, port, q):
         x = vo.make_x(6, lay.seq_len, hidden).to(f"cuda:{rank}", torch.bfloat16)
         res = {}
         for precision in ("bf16", "int8", "fp8"):
-            state = pkg_r.B200State("t", {"enable_softmax_gate": True}, [bw.branch], H, D,
+            state = pkg_r.B200State("t", vo.BranchConfig().node_config(), [bw.branch], H, D,
                                     projection_precision=precision, shard_heads=True)
             fwd = pkg_r.make_vdn_forward(_Attn(bw, H, D), state, 0)
             with pkg_r.publish_layout(lay):
                 got = pkg_r.run_forward_checked(state, fwd, x)
-            single = pkg_r.B200State("t", {"enable_softmax_gate": True}, [bw.branch], H, D,
+            single = pkg_r.B200State("t", vo.BranchConfig().node_config(), [bw.branch], H, D,
                                      projection_precision=precision)
             fwd1 = pkg_r.make_vdn_forward(_Attn(bw, H, D), single, 0)
             with pkg_r.publish_layout(lay):

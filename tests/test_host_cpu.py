@@ -211,14 +211,39 @@ def test_deferred_cholesky_scope_reports_factor_and_batch():
     bad.view(-1)[3] = 7
     with pytest.raises(torch.linalg.LinAlgError, match="factor 1, batch 3: leading minor of order 7"):
         with bbr.cholesky_runtime_scope() as checks:
-            bbr.record_factor_status(good)
-            bbr.record_factor_status(bad)
+            bbr.record_factor_status([good])
+            bbr.record_factor_status([bad])
             assert checks.factor_calls == 2
     with bbr.cholesky_runtime_scope() as checks:
-        bbr.record_factor_status(good)
+        bbr.record_factor_status([good])
     # outside a scope the check is immediate
     with pytest.raises(torch.linalg.LinAlgError):
-        bbr.record_factor_status(bad)
+        bbr.record_factor_status([bad])
+
+
+def test_factor_status_slots_are_per_call_and_survive_later_blocks():
+    """Blocks sharing one workspace each get their own status slot, so a failure in an early
+    block is still reported at the scope's exit with its own factor index (the reference's
+    fresh cholesky_ex info per call, branch.py:62-71); each call records its text factor before
+    its clip factor (branch.py:795-799)."""
+    ring = bbr.InfoRing(3, 2, "cpu")  # 2 clip frames + the text frame, 2 heads
+    with pytest.raises(torch.linalg.LinAlgError, match="factor 1, batch 3: leading minor of order 5"):
+        with bbr.cholesky_runtime_scope() as checks:
+            slots = []
+            for block in range(3):
+                slot = bbr.claim_factor_status(ring)
+                slot.zero_()  # the kernel writes every entry of its slot
+                if block == 0:
+                    slot[1, 1] = 5  # clip frame 1, head 1: batch 1 * 2 + 1 of block 0's clip factor
+                bbr.record_factor_status([slot[2:3], slot[:2]], ring, slot)
+                slots.append(slot)
+            assert len({s.data_ptr() for s in slots}) == 3 and checks.factor_calls == 6
+    assert len(ring.free) == ring.CHUNK  # released at the scope's exit
+    # a slot recorded outside a scope is validated at once and handed back
+    slot = bbr.claim_factor_status(ring)
+    slot.zero_()
+    bbr.record_factor_status([slot[2:3], slot[:2]], ring, slot)
+    assert len(ring.free) == ring.CHUNK
 
 
 def test_delta_rules_mirror_the_reference_and_unknown_rules_raise():
@@ -360,3 +385,56 @@ def test_alpha_parameters_keep_fp32_precision():
     assert bdw.a_log.dtype == torch.float32 and bdw.dt_bias.dtype == torch.float32
     assert torch.equal(bdw.a_log, w["alpha.A_log"]) and torch.equal(bdw.dt_bias, w["alpha.dt_bias"])
     assert bdw.beta_w.dtype == torch.bfloat16  # the projections themselves run in bf16
+
+
+# ------------------------------------------------------------------ branch settings at the operator
+def _fused_block_for(config, branch, maps=None, **state_kw):
+    """The FusedBlock a B200State builds for block 0 (on the CPU: construction moves weights
+    only, no kernel runs)."""
+    from __graft_entry__ import _Attn
+
+    bw_ = vo.make_block(0, 64, 2, 64)
+    branches = [branch if branch is not None else bw_.branch]
+    state = pkg.B200State("t", config, branches, 2, 64, weight_maps=maps, **state_kw)
+    return state.fused_block(_Attn(bw_, 2, 64), 0, "cpu")
+
+
+def test_node_config_without_branch_keys_resolves_like_the_reference():
+    """A config without the keys builds what nodes.py:98-116 builds (short_conv=(),
+    bridge alpha, vdn_solve) and no text state (hybrid.py:449-451 default False)."""
+    fb = _fused_block_for({}, None)
+    assert fb.short_conv == () and fb.enable_text_state is False
+    assert fb.bridge == "alpha" and fb.delta_rule == "vdn_solve" and fb.tile_frames == 0
+    assert fb.bw.conv == {}  # no conv weights loaded for an empty short_conv
+
+
+def test_node_config_keys_set_the_branch_structure():
+    cfg = vo.BranchConfig(delta_rule="sana_scaled", bridge="none").node_config()
+    fb = _fused_block_for(cfg, None, tile_frames=5)
+    assert fb.short_conv == ("k", "v") and fb.enable_text_state is True
+    assert fb.bridge == "none" and fb.delta_rule == "sana_scaled" and fb.tile_frames == 5
+
+
+def test_branch_object_settings_win_over_the_config():
+    """The operator reads the branch object first (hybrid.py:449-451; the branch's own
+    bridge / short_conv / delta_rule / tile_frames drive its readout, runtime.py:545-607)."""
+    w = vo.make_block(0, 64, 2, 64).branch
+    br = pkg.B200LinearBranch(w, 2, 64, delta_rule="sana_scaled", bridge="none", short_conv=("v",),
+                              enable_text_state=False, tile_frames=3)
+    cfg = vo.BranchConfig().node_config()  # says k,v conv, text state on, alpha, vdn_solve
+    fb = _fused_block_for(cfg, br, tile_frames=7)
+    assert fb.short_conv == ("v",) and fb.enable_text_state is False
+    assert fb.bridge == "none" and fb.delta_rule == "sana_scaled" and fb.tile_frames == 3
+
+
+def test_to_out_follows_the_stored_representation():
+    """to_out_linear runs in the representation its map stores (projection.py:259-268): a
+    bf16 master (an fp8 model's edge block, fp8.py:198) stays bf16 in a quantised block, so
+    the block cannot fuse both projections into one K-concat GEMM; a bf16 block with a bf16
+    master can."""
+    w = vo.make_block(0, 64, 2, 64).branch
+    assert "to_out_linear.weight" in w
+    fb = _fused_block_for({}, None, maps=[w])
+    assert fb.to_out_kind == "bf16" and fb.concat_out
+    fb8 = _fused_block_for({}, None, maps=[w], projection_precision="bf16")
+    assert fb8.w_to_b16 is None  # folded into the K-concat weight

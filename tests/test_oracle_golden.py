@@ -278,3 +278,19 @@ def test_branch_with_skip_ends_zeroes_the_end_frames_and_stays_finite():
             assert torch.count_nonzero(rows) == 0, f
         else:
             assert (rows.abs().amax(dim=1) > 0).all(), f
+
+
+@pytest.mark.parametrize("anchors", ["none", "columns", "rows", "both"])
+def test_grouped_attention_and_row_subsets_equal_the_dense_oracle(anchors):
+    """The gathered-key spelling of the window softmax (the reference's grouped backend,
+    window.py:277-313) and a row-restricted block equal the dense masked oracle."""
+    c = vo.CONFIG0
+    lay = vo.config_layout(c, anchor_frames=anchors)
+    bw = vo.make_block(0, c["hidden"], c["heads"], c["dim"])
+    x = vo.make_x(0, lay.seq_len, c["hidden"])
+    dense = vo.block_forward(x, bw, lay, c["heads"], c["dim"], vo.BranchConfig())
+    grouped = vo.block_forward(x, bw, lay, c["heads"], c["dim"], vo.BranchConfig(), attention="grouped")
+    assert float((dense - grouped).abs().max()) < 1e-12
+    rows = torch.tensor([271, 0, 5, 31, 32, 40, 100, 200])  # text, anchors, interior; unsorted
+    sub = vo.block_forward(x, bw, lay, c["heads"], c["dim"], vo.BranchConfig(), attention="grouped", rows=rows)
+    assert float((dense[rows] - sub).abs().max()) < 1e-12

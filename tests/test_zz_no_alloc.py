@@ -62,3 +62,20 @@ def test_noalloc_rejects_problems_larger_than_its_scratch():
     out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="fixed device scratch"):
         _noalloc(x, wq, ws, out)
+
+
+@pytest.mark.parametrize("bad", ["ldx", "ldw", "ldo"])
+def test_noalloc_rejects_row_pitches_shorter_than_a_row(bad):
+    """A pitch below its row length would make rows overlap: rejected before any launch."""
+    dev = torch.device("cuda:0")
+    M, K, N = 64, 256, 128
+    x = torch.zeros(M, K, device=dev, dtype=torch.bfloat16)
+    wq = torch.zeros(N, K, device=dev, dtype=torch.float8_e4m3fn)
+    ws = torch.ones(1, device=dev)
+    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    lib = pkg._lib
+    status = lib.DeviceStatus(dev)
+    ldx, ldw, ldo = (K - 16 if bad == "ldx" else K), (K - 16 if bad == "ldw" else K), (N - 8 if bad == "ldo" else N)
+    with pytest.raises(ValueError, match="invalid argument"):
+        lib.call("vdn_fp8_linear_noalloc", x.data_ptr(), ldx, M, K, wq.data_ptr(), ldw, N, ws.data_ptr(),
+                 out.data_ptr(), ldo, status.err_ptr, lib.stream_handle(dev))
