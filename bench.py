@@ -12,7 +12,10 @@ Printed JSON line: ``value`` is whole-job TFLOP/s over the algorithmic FLOPs of 
 through the public operator (``make_vdn_forward``) with the input copied from pinned host
 memory and the output read back every step.  ``roofline`` covers the dominant kernel,
 timed with CUDA events on its launch stream inside the timed steps.  ``cpu_baseline`` is
-the float32 CPU restatement (oracle port) of the same block on a bounded head sample.
+one full block forward of the same weights and input on the host cores (the reference
+torch path restated: bf16 GEMMs, fp32 branch), and ``parity_rel_l2`` the relative L2
+between its output and the GPU's, over every row.  ``--impl reference`` times that CPU
+block forward as its step.
 
 Kernel-only modes for profiling: ``--only attention [--heads n]`` (the window attention kernel
 on the config geometry) and ``--only quantisers`` (the int8, ConvRot int8 and per-tensor e4m3
@@ -211,33 +214,76 @@ def barrier(world):
         dist.barrier()
 
 
-def cpu_baseline(c, seconds_target=15.0):
-    """Float32 CPU restatement of the block on a bounded head sample; returns TFLOP/s."""
-    from oracle import vdn_oracle as vo
-
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    heads_sample = 2
-    lay = vo.config_layout(c)
-    D, hidden = c["dim"], c["hidden"]
-    gen = torch.Generator().manual_seed(0)
-    inner = heads_sample * D
-    x = torch.randn(lay.seq_len, hidden, generator=gen)
-    bw = vo.BlockWeights(qkv=torch.randn(3 * inner, hidden, generator=gen) * 0.02,
-                         q_norm=torch.ones(D), k_norm=torch.ones(D),
-                         out=torch.randn(hidden, inner, generator=gen) * 0.02,
-                         branch=vo.make_branch_weights(gen, hidden, heads_sample, D))
-    prev = vo.set_compute_dtype(torch.float32)
+def cpu_model() -> str:
     try:
-        t0 = time.perf_counter()
-        vo.block_forward(x, bw, lay, heads_sample, D, vo.BranchConfig())
-        dt = time.perf_counter() - t0
-    finally:
-        vo.set_compute_dtype(prev)
-    fl = vo.block_flops(lay, heads_sample, D, hidden)["total"]
-    return {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"fp32 oracle block forward on {heads_sample} of {c['heads']} heads (QKV/out GEMMs over those "
-                      f"heads' columns, full hidden {hidden}); {dt:.1f} s for {fl / 1e12:.3f} TFLOP"}
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+class ReferenceCPU:
+    """The reference's block forward on the host cores: the CPU restatement of its torch path
+    (hybrid.py:409-579) at config 1's dtype -- bf16 operands and results for the projections
+    and the two attention products (the reference's grouped window backend, window.py:277-313,
+    on gathered keys), the branch statistics, factor and scans in fp32 (branch.py:197-243) --
+    on every head and every row, with all host threads.  Weights are cast to bf16 once, as
+    the reference holds them."""
+
+    def __init__(self, c, weights, x_bf16):
+        from oracle import vdn_oracle as vo
+
+        self.vo = vo
+        self.c = c
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        qkv, qn, kn, out_w, branch = weights
+        br = dict(branch)
+        br["to_out_linear.weight"] = br["to_out_linear.weight"].to(torch.bfloat16)
+        self.bw = vo.BlockWeights(qkv=qkv.cpu().to(torch.bfloat16), q_norm=qn.cpu(), k_norm=kn.cpu(),
+                                  out=out_w.cpu().to(torch.bfloat16), branch=br)
+        self.lay = vo.config_layout(c)
+        self.x = x_bf16.cpu()
+        self.flops = vo.block_flops(self.lay, c["heads"], c["dim"], c["hidden"])["total"]
+
+    def step(self):
+        """One full block forward; returns (output [S, hidden] fp32, seconds)."""
+        vo = self.vo
+        prev_c, prev_m = vo.set_compute_dtype(torch.float32), vo.set_matmul_dtype(torch.bfloat16)
+        try:
+            t0 = time.perf_counter()
+            out = vo.block_forward(self.x, self.bw, self.lay, self.c["heads"], self.c["dim"], vo.BranchConfig(),
+                                   attention="grouped")
+            return out, time.perf_counter() - t0
+        finally:
+            vo.set_compute_dtype(prev_c)
+            vo.set_matmul_dtype(prev_m)
+
+    def describe(self, seconds) -> dict:
+        return {"cores": self.threads, "cpu": cpu_model(), "kind": "port",
+                "sample": f"one full block forward of the config (all {self.c['heads']} heads, {self.lay.seq_len} "
+                          f"rows): oracle port of the reference torch path at bf16 GEMM operands, fp32 branch "
+                          f"statistics; {seconds:.1f} s for {self.flops / 1e12:.2f} TFLOP"}
+
+
+def cpu_baseline(c, weights, x_bf16, out_gpu=None):
+    """One full block forward on the host cores (``ReferenceCPU``), timed; with ``out_gpu``
+    (the GPU block's output for the same weights and input) also the relative L2 between
+    the two, the parity figure of the benchmarked output."""
+    ref = ReferenceCPU(c, weights, x_bf16)
+    out, dt = ref.step()
+    line = dict({"value": ref.flops / dt / 1e12, "unit": "TFLOP/s"}, **ref.describe(dt))
+    parity = None
+    if out_gpu is not None:
+        got = out_gpu.double().cpu()
+        want = out.double()
+        parity = {"rel_l2": float((got - want).norm() / want.norm()), "rows": int(got.shape[0]), "tolerance": 2e-2,
+                  "against": "the reference torch path restated on the CPU (bf16 GEMMs, fp32 branch), same "
+                             "seeded weights and input, every output row"}
+    return line, parity
 
 
 def make_weights(c, device, seed=0, head_slice=None):
@@ -255,25 +301,46 @@ def make_weights(c, device, seed=0, head_slice=None):
     return qkv, qn, kn, out, branch
 
 
+def bench_input(c):
+    """The seed-1 N(0, 1) block input, bf16, on the host."""
+    g = torch.Generator().manual_seed(1)
+    S = c["text"] + c["frames"] * c["grid"][0] * c["grid"][1]
+    return torch.randn(S, c["hidden"], generator=g).to(torch.bfloat16)
+
+
+def config_entry(args, c, world) -> dict:
+    """The ``config`` object of both arms' JSON lines."""
+    H, D, hidden = c["heads"], c["dim"], c["hidden"]
+    S = c["text"] + c["frames"] * c["grid"][0] * c["grid"][1]
+    return {"workload": f"config{args.config}: {c['frames']}x{c['grid'][0] * c['grid'][1]}+{c['text']} tokens, "
+                        f"H={H}, D={D}, hidden={hidden}", "tokens": S,
+            "parallelism": f"heads/{world}" if world > 1 else "none",
+            "l2": f"inputs larger than L2 (x {S * hidden * 2 / 1e6:.0f} MB, weights "
+                  f"{(5 * H * D + 2 * H + 2 * D) * hidden * 2 / 1e9:.2f} GB)",
+            "delta_rule": args.delta_rule, "rope": bool(args.rope)}
+
+
 def run_reference_arm(args, c, world, rank):
+    """The reference arm: every step is one full block forward of the config on the host
+    cores (``ReferenceCPU``), timed by the wall clock; rank 0 alone works and prints."""
     if rank != 0:
         return
-    from oracle import vdn_oracle as vo
-
-    lay = vo.config_layout(c)
-    base = cpu_baseline(c)
-    steps = []
-    for _ in range(args.warmup + args.steps):
-        steps.append(cpu_baseline(c)["value"])
-    val = sorted(steps[args.warmup:])[len(steps[args.warmup:]) // 2] if args.steps else base["value"]
-    fl = vo.block_flops(lay, c["heads"], c["dim"], c["hidden"])["total"]
+    ref = ReferenceCPU(c, make_weights(c, "cpu"), bench_input(c))
+    times = []
+    for i in range(args.warmup + args.steps):
+        _, dt = ref.step()
+        if i >= args.warmup:
+            times.append(dt)
+    times.sort()
+    dt = times[len(times) // 2] if times else float("nan")
+    val = ref.flops / dt / 1e12
     line = {
         "impl": "reference", "metric": metric_name(c), "value": val, "unit": "TFLOP/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": fl / (val * 1e12) * 1e3,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"config{args.config}", "tokens": lay.seq_len, "heads": c["heads"],
-                   "head_dim": c["dim"], "hidden": c["hidden"]},
-        "cpu_baseline": dict(base, value=val),
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "timed_s": sum(times),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) x)", "config": config_entry(args, c, 1),
+        "tflop_per_step": ref.flops / 1e12,
+        "cpu_baseline": dict({"value": val, "unit": "TFLOP/s"}, **ref.describe(dt)),
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -401,6 +468,9 @@ def run_dit_stack(args, c, world, rank, local):
     for _ in range(n_blocks):
         branch = dict(base_branch)
         branch["to_out_linear.weight"] = rn(hidden, H * D)
+        if c["precision"] != "bf16":
+            # the branch projection runs in its stored representation: store it quantised
+            branch = pkg.prepare_projection_maps([branch], dev, c["precision"], skip_end_blocks=0)[0][0]
         fb = pkg.FusedBlock(rn(3 * H * D, hidden), rn(D, s=0.1, mean=1.0), rn(D, s=0.1, mean=1.0), rn(hidden, H * D),
                             branch, H, D, dev, precision=c["precision"], shard=shard, workspaces=ws_attn)
         blocks.append(pkg.B200DiTBlock(fb, rn(hidden, s=0.1, mean=1.0), 1e-6, rn(hidden, s=0.1, mean=1.0), 1e-6,
@@ -570,8 +640,7 @@ def main():
     rope_freqs = rope_freqs_table(lay.seq_len, D, dev) if args.rope else None
     rope = pkg.rope_table(rope_freqs, lay.seq_len, D, dev)
     status = state.device_status(dev)
-    g = torch.Generator().manual_seed(1)
-    x_host = torch.randn(lay.seq_len, hidden, generator=g).to(torch.bfloat16).pin_memory()
+    x_host = bench_input(c).pin_memory()
     x_dev = x_host.to(dev)
     out_dev = torch.empty(lay.seq_len, hidden, device=dev, dtype=torch.bfloat16)
     # ---- device-resident timing (inputs in HBM; x 270 MB and weights ~0.3 GB exceed the 126 MB L2)
@@ -687,11 +756,7 @@ def main():
         "metric": metric_name(c), "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) x)",
-        "config": {"workload": f"config{args.config}: 31x{c['grid'][0] * c['grid'][1]}+512 tokens, H={H}, D={D}, "
-                               f"hidden={hidden}", "tokens": lay.seq_len, "parallelism": f"heads/{world}" if world > 1 else "none",
-                   "l2": f"inputs larger than L2 (x {lay.seq_len * hidden * 2 / 1e6:.0f} MB, weights "
-                         f"{(5 * H * D + 2 * H + 2 * D) * hidden * 2 / 1e9:.2f} GB)",
-                   "delta_rule": args.delta_rule, "rope": bool(args.rope)},
+        "config": config_entry(args, c, world),
         "tflop_per_step": flops["total"] / 1e12,
         "roofline": {"kernel": "window_attention_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": achieved / peak,
@@ -708,7 +773,14 @@ def main():
         "clocks": clock_summary,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(c)
+        # the same block on the host cores: the CPU baseline, and the parity of the benchmarked
+        # output (out_dev holds the last device-resident step's output for x)
+        baseline, parity = cpu_baseline(c, (qkv, qn, kn, out_w, branch), x_host,
+                                        out_dev if not args.rope else None)
+        line["cpu_baseline"] = baseline
+        if parity is not None:
+            line["parity_rel_l2"] = parity["rel_l2"]
+            line["parity"] = parity
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -275,10 +275,17 @@ def temporal_shift(x, w) -> torch.Tensor:
     x, w = _t(x), _t(w)
     taps = w.shape[-1]
     pad = taps // 2
-    xp = F.pad(x, (0, 0, 0, 0, pad, pad))
-    out = torch.zeros_like(x)
-    for dt in range(taps):
-        out += xp[dt:dt + x.shape[0]] * w[:, dt].view(1, 1, -1)
+    T = x.shape[0]
+    # out[t] = sum_j x[t + j - pad] * w[:, j], terms outside [0, T) being zero
+    out = x * w[:, pad].view(1, 1, -1)
+    for j in range(taps):
+        s = j - pad
+        if s == 0 or abs(s) >= T:
+            continue
+        if s > 0:
+            out[:T - s] += x[s:] * w[:, j].view(1, 1, -1)
+        else:
+            out[-s:] += x[:T + s] * w[:, j].view(1, 1, -1)
     return out
 
 
@@ -618,7 +625,11 @@ def project(rows, w, precision="bf16"):
     """``rows @ W^T`` under the chosen precision; float64 result (projection.py:259-268)."""
     if precision == "bf16" and _MATMUL[0] is not None:
         md = _MATMUL[0]
-        return (_t(rows).to(md) @ _t(w).to(md).T).to(_COMPUTE[0])
+
+        def operand(t):  # straight to the matmul dtype (no copy when the tensor already is)
+            return (torch.from_numpy(t) if isinstance(t, np.ndarray) else t).detach().to("cpu", md)
+
+        return (operand(rows) @ operand(w).T).to(_COMPUTE[0])
     if precision == "bf16" or precision == "fp64":
         return _t(rows) @ _t(w).T
     if precision == "int8":

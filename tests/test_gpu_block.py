@@ -74,14 +74,27 @@ def test_block_full_cover_runs_dense_attention_without_branch():
     assert rel_l2(got, want) < 2e-2
 
 
+@pytest.mark.parametrize("to_out", ["stored_bf16", "prepared"])
 @pytest.mark.parametrize("precision", ["int8", "fp8"])
-def test_block_quantised_projections_match_oracle(precision):
+def test_block_quantised_projections_match_oracle(precision, to_out):
+    """Config 2: qkv_proj and out_proj quantised; to_out_linear in its stored representation --
+    bf16 as given, or quantised by prepare_projection_maps (no bf16 edge blocks)."""
     c = dict(vo.CONFIG0, heads=2, dim=128)
     bw = vo.make_block(3, c["hidden"], c["heads"], c["dim"])
     lay_o = vo.config_layout(c)
     x = vo.make_x(3, lay_o.seq_len, c["hidden"]).to(torch.bfloat16).float()
-    got = _run_block(bw, _layout(c), c["heads"], c["dim"], x, precision=precision)
-    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(), precision=precision)
+    if to_out == "prepared":
+        maps, _ = pkg.prepare_projection_maps([bw.branch], DEV, precision, skip_end_blocks=0)
+        state = pkg.B200State("t", vo.BranchConfig().node_config(), [bw.branch], c["heads"], c["dim"],
+                              projection_precision=precision, weight_maps=maps)
+        fwd = pkg.make_vdn_forward(_Attn(bw, c["heads"], c["dim"]), state, 0)
+        with pkg.publish_layout(_layout(c)):
+            got = pkg.run_forward_checked(state, fwd, x.to(DEV, torch.bfloat16))
+        torch.cuda.synchronize()
+    else:
+        got = _run_block(bw, _layout(c), c["heads"], c["dim"], x, precision=precision)
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(), precision=precision,
+                            to_out_precision=precision if to_out == "prepared" else "bf16")
     exact = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig())
     # Quantised block vs its own CPU restatement.  The two pipelines quantise activations
     # that already differ by bf16 rounding, so a few per cent of e4m3 codes land one ulp

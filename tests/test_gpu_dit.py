@@ -159,7 +159,11 @@ def _dit(seed, activation):
 def _device_block(dw, precision, activation, shard=None):
     H, D = CFG["heads"], CFG["dim"]
     bw = dw.attn
-    fb = pkg.FusedBlock(bw.qkv, bw.q_norm, bw.k_norm, bw.out, bw.branch, H, D, DEV, precision=precision, shard=shard)
+    branch = bw.branch
+    if precision != "bf16":
+        # to_out_linear runs in its stored representation: store it quantised too
+        branch = pkg.prepare_projection_maps([branch], DEV, precision, skip_end_blocks=0)[0][0]
+    fb = pkg.FusedBlock(bw.qkv, bw.q_norm, bw.k_norm, bw.out, branch, H, D, DEV, precision=precision, shard=shard)
     return pkg.B200DiTBlock(fb, dw.norm1, dw.eps, dw.norm2, dw.eps, dw.fc1, dw.fc1_b, dw.fc2, dw.fc2_b, DEV,
                             activation=activation, precision=precision)
 
