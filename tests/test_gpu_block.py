@@ -267,9 +267,10 @@ def test_spd_failure_in_an_early_block_survives_later_blocks():
     each way); block 1 is clean.  The deferred check at the scope's exit still names block 0's
     factor: factor 1 (block 0 factors its text frame first, branch.py:795-799), batch
     (first bad frame) * H."""
-    c = dict(text=64, frames=9, grid=(4, 6), heads=2, dim=128, hidden=256)
+    c = dict(text=64, frames=15, grid=(4, 6), heads=2, dim=128, hidden=256)
     H, D = c["heads"], c["dim"]
     lay = _layout(c)
+    assert not lay.full_cover  # the branch runs
     shared = {}
     blocks = []
     for seed in (5, 6):
