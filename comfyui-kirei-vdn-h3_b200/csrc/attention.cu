@@ -15,15 +15,20 @@
 //     from the frame index (never materialised);
 //   * the 256 query rows are two 128-row tiles (a = 0, 1) that share every K/V tile: warp 8
 //     streams Q and a 2-stage K/V ring with TMA, warp 9 issues all tcgen05 MMAs, and two
-//     softmax warpgroups (warps 0-3 for a = 0, 4-7 for a = 1) ping-pong against it;
+//     softmax warpgroups (warps 0-3 for a = 0, 4-7 for a = 1) ping-pong against it; warps
+//     8-11 hand registers to the softmax warpgroups at start-up (setmaxnreg: 80 and 208);
 //   * TMEM (512 columns): S_a in columns [128a, 128a+128), O_a in [256+128a, 384+128a).  The
 //     softmax writes P_a as packed bf16 over the first 64 columns of S_a and the PV MMA reads
 //     it straight from TMEM (A operand in tensor memory), so shared memory holds only Q and
 //     the K/V ring.  The next S_a is issued after PV_a, so the in-order tensor pipe never
-//     overwrites P before it is consumed, and S_a's completion implies PV_a's;
+//     overwrites P before it is consumed, and S_a's completion implies PV_a's.  P goes to the
+//     MMA warp in two parts (keys 0-95, then 96-127), so most of PV_a starts before the
+//     softmax has finished the tile;
 //   * online softmax in registers with exp2 in log2 units; the reference maximum moves only
-//     when a tile exceeds it by more than 2^8, so O is rescaled rarely (the result is exact);
-//     a quarter of the exponentials run as a polynomial on the FMA pipe;
+//     when a tile exceeds it by more than 2^8, so O is rescaled rarely (the result is exact),
+//     and the exponentials start against the current reference while the tile maximum is
+//     still being reduced (a tile is redone when the reference has to move); a quarter of
+//     the exponentials run as a paired-fp32 polynomial on the FMA pipe;
 //   * the epilogue applies 1/l and the gate and writes bf16 rows.
 #include "host_common.h"
 #include "sm100.cuh"
@@ -31,7 +36,24 @@
 namespace vdn {
 namespace attn {
 
-constexpr int kThreads = 320;  // 8 softmax warps, 1 TMA warp, 1 MMA warp
+constexpr int kThreads = 384;  // 8 softmax warps, 1 TMA warp, 1 MMA warp, 2 warps that only give up registers
+// Registers per thread after the start-up reallocation.  The launch holds 168 per thread
+// (65,536 / 384, rounded down to a multiple of 8), and each SM sub-partition (16,384
+// registers) hosts one warp of each warpgroup: two softmax warps and one of warps 8-11.
+// Per sub-partition 2 x 208 + 80 = 496 <= 512 registers per lane; per CTA
+// 256 x 208 + 128 x 80 = 63,488 <= 384 x 168 = 64,512.
+constexpr int kRegsSoftmax = 208;
+constexpr int kRegsIssue = 80;  // warps 8-11: the TMA and MMA warps and two idle warps
+constexpr int kRegsLaunch = 168;
+
+template <int N>
+__device__ __forceinline__ void reg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void reg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
 constexpr int BQ = 128;        // rows per query tile (two per work item)
 constexpr int BKV = 128;
 constexpr int kStages = 2;
@@ -80,19 +102,26 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x for x <= 8 on the FMA/ALU pipes: x = n + f with n = round(x) (added-magic-number
-// rounding) and f in [-0.5, 0.5]; 2^f by a cubic fitted here for minimum relative error
-// (max 1.0e-4, far below the bf16 rounding P receives); 2^n added to the exponent bits.
-// Inputs below -126 (masked keys are -inf) are clamped to 2^-126 instead of 0: the row sum
-// is at least 1 (the key that set the reference maximum has weight 1), so such weights stay
-// below fp32 resolution in every sum, and no select is spent on exact zeros.
-__device__ __forceinline__ float exp2_poly(float x) {
-  const float xc = fmaxf(x, -126.0f);
-  const float t = xc + 12582912.0f;  // 1.5 * 2^23: rounds xc to an integer in the low bits
-  const int n = __float_as_int(t) - 0x4B400000;
-  const float f = xc - (t - 12582912.0f);
-  const float p = fmaf(fmaf(fmaf(0.05500844f, f, 0.24220988f), f, 0.69328284f), f, 1.0f);
-  return __int_as_float(__float_as_int(p) + (n << 23));
+// 2^x for two values x <= 8 on the FMA/ALU pipes, with the paired fp32 instructions (about
+// five instructions per exponential): x = n + f with n = round(x) (added-magic-number
+// rounding, t = x + 1.5 * 2^23 holds n in its low bits) and f in [-0.5, 0.5]; 2^f by a cubic
+// fitted here for minimum relative error (max 1.0e-4, far below the bf16 rounding P
+// receives); 2^n added to the exponent bits as t's bits shifted left by 23 (those of
+// 1.5 * 2^23 vanish modulo 2^32).  Inputs below -126 (masked keys are -inf) are clamped to
+// 2^-126 instead of 0: the row sum is at least 2^-32 (the key that set the reference has
+// weight >= 2^-32), so such weights stay below fp32 resolution in every sum, and no select
+// is spent on exact zeros.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 t = add2(x, make_float2(12582912.0f, 12582912.0f));
+  const float2 r = add2(t, make_float2(-12582912.0f, -12582912.0f));  // round(x)
+  const float2 f = fma2(r, make_float2(-1.0f, -1.0f), x);              // x - round(x) in [-0.5, 0.5]
+  float2 q = fma2(make_float2(0.05500844f, 0.05500844f), f, make_float2(0.24220988f, 0.24220988f));
+  q = fma2(q, f, make_float2(0.69328284f, 0.69328284f));
+  q = fma2(q, f, make_float2(1.0f, 1.0f));
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
 }
 
 __device__ __forceinline__ float max3(float a, float b, float c) {
@@ -100,6 +129,24 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
+
+// Key pairs (of the eight in a 16-key chunk) whose exponentials run on the FMA pipe: a
+// quarter of them, relieving the MUFU unit (16 exponentials per clock per SM, the same rate
+// at which the tensor cores consume scores at head_dim 128).
+constexpr uint32_t kPolyPairs = 0x22u;
+
+// Row maximum of one 128-key score tile: four independent 3-input max chains.
+template <int N>
+__device__ __forceinline__ float row_max(const uint32_t (&sr)[N]) {
+  float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int c = 0; c < N; c += 8) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) mq[u] = max3(mq[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
+  }
+  return max3(mq[0], mq[1], fmaxf(mq[2], mq[3]));
+}
+
 
 // 32 lanes x 32 bit x 8 columns TMEM store.
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
@@ -116,6 +163,36 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
       "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
+}
+
+// P = 2^(s * scale - m) for the keys of 16-key chunks [C0, C1) of this thread's row, packed
+// as bf16 pairs into TMEM over the first columns of the score tile (key 2c in the low half
+// of column c) chunk by chunk, so each chunk's scores die as its P leaves; returns the
+// chunks' row sum as two partial sums.
+template <int C0, int C1, int N>
+__device__ __forceinline__ float2 p_chunks(const uint32_t (&sr)[N], float scale, float m, uint32_t s_tmem) {
+  const float2 scale2 = make_float2(scale, scale);
+  const float2 negm2 = make_float2(-m, -m);
+  float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+  for (int c0 = 16 * C0; c0 < 16 * C1; c0 += 16) {
+    uint32_t pk[8];
+#pragma unroll
+    for (int c = 0; c < 16; c += 2) {
+      const float2 x = fma2(make_float2(__uint_as_float(sr[c0 + c]), __uint_as_float(sr[c0 + c + 1])), scale2, negm2);
+      float2 e;
+      if ((kPolyPairs >> (c / 2)) & 1u) {
+        e = exp2_poly2(x);
+      } else {
+        e.x = ex2(x.x);
+        e.y = ex2(x.y);
+      }
+      rs2[(c >> 1) & 1] = add2(rs2[(c >> 1) & 1], e);
+      pk[c / 2] = pack_bf16(e.x, e.y);
+    }
+    tmem_st8(s_tmem + c0 / 2, pk);
+  }
+  return add2(rs2[0], rs2[1]);
 }
 
 // The MMAs below take shared-memory descriptors as two 32-bit words.  The low word holds the
@@ -168,14 +245,18 @@ struct Layout {
   static constexpr int kSmem = kOffBar + 512 + 1024;
 };
 
+// P of a tile is handed to the MMA warp in two parts: keys [0, kPSplit) (B_PLO) and the rest
+// (B_PHI), so the first PV products run while the softmax finishes the last chunks.
+constexpr int kPSplit = 96;
+
 enum {
   B_QFULL = 0, B_QEMPTY, B_KFULL0, B_KFULL1, B_VFULL0, B_VFULL1, B_KEMPTY0, B_KEMPTY1, B_VEMPTY0, B_VEMPTY1,
-  B_SFULL0, B_SFULL1, B_PFULL0, B_PFULL1, B_ODONE0, B_ODONE1, B_OFREE0, B_OFREE1,
+  B_SFULL0, B_SFULL1, B_PLO0, B_PLO1, B_PHI0, B_PHI1, B_ODONE0, B_ODONE1, B_OFREE0, B_OFREE1,
   B_IFULL0, B_IFULL1, B_IFULL2, B_IFULL3, B_IEMPTY0, B_IEMPTY1, B_IEMPTY2, B_IEMPTY3, B_COUNT
 };
 
-// 320 threads, one CTA per SM.  Registers are allocated per SM sub-partition (16K each) and one
-// sub-partition hosts three of the ten warps, which caps the uniform allocation at 168/thread.
+// 384 threads, one CTA per SM.  The launch gives every thread 168 registers; warps 8-11 hand
+// most of theirs back at start-up (setmaxnreg) and the softmax warps take 208.
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     window_attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -201,7 +282,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(B(B_KEMPTY0 + s), 1);
       mbar_init(B(B_VEMPTY0 + s), 1);
       mbar_init(B(B_SFULL0 + s), 1);
-      mbar_init(B(B_PFULL0 + s), 4);
+      mbar_init(B(B_PLO0 + s), 4);
+      mbar_init(B(B_PHI0 + s), 4);
       mbar_init(B(B_ODONE0 + s), 1);
       mbar_init(B(B_OFREE0 + s), 4);
     }
@@ -228,126 +310,145 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sV = smem_u32(smem + L::kOffV);
   constexpr int kDBlocks = D / 64;  // 64-element (128 B) column blocks per row
 
-  if (warp == 8) {
-    if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      int g = 0;  // global kv tile counter
-      for (int it = 0;; ++it) {
-        // Dynamic schedule: fetch the next item from the global queue and hand it to the
-        // MMA and softmax warps through a small shared-memory ring (-1 ends the loop).
-        const int slot = it % kItemRing;
-        if (!mbar_wait(B(B_IEMPTY0 + slot), ((it / kItemRing) & 1) ^ 1, abort_flag, err, kErrWaitProducer)) break;
-        const int item = atomicAdd(p.work_counter, 1);
-        const int code = item < p.n_items ? p.items[item] : -1;
-        item_ring[slot] = code;
-        mbar_arrive(B(B_IFULL0 + slot));
-        if (code < 0) break;
-        const int h = code >> 20, qt = code & 0xFFFFF;
-        if (!mbar_wait(B(B_QEMPTY), (it & 1) ^ 1, abort_flag, err, kErrWaitProducer)) break;
-        mbar_arrive_expect_tx(B(B_QFULL), 2 * L::kQTile);
-        for (int a = 0; a < 2; ++a)
-          for (int b = 0; b < kDBlocks; ++b)
-            tma_load_2d(sQ + a * L::kQTile + b * (BQ * 128), &tq, B(B_QFULL), h * D + b * 64,
-                        q_half(p, qt, a) >> 8);
-        const int t0 = p.tile_off[qt], t1 = p.tile_off[qt + 1];
-        bool ok = true;
-        for (int t = t0; t < t1; ++t, ++g) {
-          const int st = g & 1;
-          const uint32_t ph = (g >> 1) & 1;
-          const int k0 = p.ktile[t] >> 9;
-          const uint32_t kb = sK + st * L::kKBytes, vb = sV + st * L::kVBytes;
-          if (!mbar_wait(B(B_KEMPTY0 + st), ph ^ 1, abort_flag, err, kErrWaitProducer)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(B(B_KFULL0 + st), L::kKBytes);
-          for (int b = 0; b < kDBlocks; ++b)
-            tma_load_2d(kb + b * (BKV * 128), &tk, B(B_KFULL0 + st), h * D + b * 64, k0);
-          if (!mbar_wait(B(B_VEMPTY0 + st), ph ^ 1, abort_flag, err, kErrWaitProducer)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(B(B_VFULL0 + st), L::kVBytes);
-          for (int b = 0; b < kDBlocks; ++b)
-            tma_load_2d(vb + b * (BKV * 128), &tv, B(B_VFULL0 + st), h * D + b * 64, k0);
-        }
-        if (!ok) break;
-      }
-    }
-  } else if (warp == 9) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc_s = make_idesc(1, 1, 1, 0, 0, BQ, BKV);
-      constexpr uint32_t idesc_o = make_idesc(1, 1, 1, 0, 1, BQ, D);
-      constexpr uint32_t hi_k = sdesc_hi_sw128(1024);  // K-major Q / K, and MN-major V: SBO 1024
-      const uint32_t q_lo = sdesc_lo(sQ, 16), k_lo = sdesc_lo(sK, 16), v_lo = sdesc_lo(sV, BKV * 128);
-      auto issue_s = [&](int a, int st) {
-        const uint32_t qa = q_lo + a * (L::kQTile >> 4), kb = k_lo + st * (L::kKBytes >> 4);
-#pragma unroll
-        for (int s = 0; s < D / 16; ++s) {
-          const uint32_t off = ((s >> 2) * (BQ * 128) + (s & 3) * 32) >> 4;
-          mma_ss(tmem_base + a * 128, qa + off, kb + off, hi_k, idesc_s, s > 0 ? 1u : 0u);
-        }
-        tc_commit(B(B_SFULL0 + a));
-      };
-      int g = 0;
-      int it = 0;
-      bool ok = true;
-      for (; ok; ++it) {
-        const int slot = it % kItemRing;
-        if (!mbar_wait(B(B_IFULL0 + slot), (it / kItemRing) & 1, abort_flag, err, kErrWaitMma)) break;
-        const int code = item_ring[slot];
-        mbar_arrive(B(B_IEMPTY0 + slot));
-        if (code < 0) break;
-        const int qt = code & 0xFFFFF;
-        const int n = p.tile_off[qt + 1] - p.tile_off[qt];
-        if (!mbar_wait(B(B_QFULL), it & 1, abort_flag, err, kErrWaitMma) ||
-            !mbar_wait(B(B_KFULL0 + (g & 1)), (g >> 1) & 1, abort_flag, err, kErrWaitMma)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        issue_s(0, g & 1);
-        issue_s(1, g & 1);
-        tc_commit(B(B_KEMPTY0 + (g & 1)));
-        if (n == 1) tc_commit(B(B_QEMPTY));
-        for (int j = 0; j < n && ok; ++j) {
-          const int gj = g + j, st = gj & 1;
-          const uint32_t ph = (gj >> 1) & 1;
-          for (int a = 0; a < 2; ++a) {
-            if (!mbar_wait(B(B_PFULL0 + a), gj & 1, abort_flag, err, kErrWaitMma) ||
-                (j == 0 && !mbar_wait(B(B_OFREE0 + a), (it & 1) ^ 1, abort_flag, err, kErrWaitMma)) ||
-                (a == 0 && !mbar_wait(B(B_VFULL0 + st), ph, abort_flag, err, kErrWaitMma))) {
+  // Register reallocation, one setmaxnreg instruction per warpgroup and direction: warps 8-11
+  // (TMA, MMA and two idle warps) give registers up at the start and take the launch's
+  // count back at the end; the softmax warpgroups take more and give it back.  Decreases
+  // never wait; an increase waits until enough registers are free, which the decreases that
+  // precede it (in program order of the other warpgroup) always make true.
+  if (warp >= 8) {
+    reg_dec<kRegsIssue>();
+    if (warp == 8) {
+      if (lane == 0) {
+        // ---------------- TMA producer ----------------
+        int g = 0;  // global kv tile counter
+        for (int it = 0;; ++it) {
+          // Dynamic schedule: fetch the next item from the global queue and hand it to the
+          // MMA and softmax warps through a small shared-memory ring (-1 ends the loop).
+          const int slot = it % kItemRing;
+          if (!mbar_wait_inl(B(B_IEMPTY0 + slot), ((it / kItemRing) & 1) ^ 1, abort_flag, err, kErrWaitProducer)) break;
+          const int item = atomicAdd(p.work_counter, 1);
+          const int code = item < p.n_items ? p.items[item] : -1;
+          item_ring[slot] = code;
+          mbar_arrive(B(B_IFULL0 + slot));
+          if (code < 0) break;
+          const int h = code >> 20, qt = code & 0xFFFFF;
+          if (!mbar_wait_inl(B(B_QEMPTY), (it & 1) ^ 1, abort_flag, err, kErrWaitProducer)) break;
+          mbar_arrive_expect_tx(B(B_QFULL), 2 * L::kQTile);
+          for (int a = 0; a < 2; ++a)
+            for (int b = 0; b < kDBlocks; ++b)
+              tma_load_2d(sQ + a * L::kQTile + b * (BQ * 128), &tq, B(B_QFULL), h * D + b * 64,
+                          q_half(p, qt, a) >> 8);
+          const int t0 = p.tile_off[qt], t1 = p.tile_off[qt + 1];
+          bool ok = true;
+          for (int t = t0; t < t1; ++t, ++g) {
+            const int st = g & 1;
+            const uint32_t ph = (g >> 1) & 1;
+            const int k0 = p.ktile[t] >> 9;
+            const uint32_t kb = sK + st * L::kKBytes, vb = sV + st * L::kVBytes;
+            if (!mbar_wait_inl(B(B_KEMPTY0 + st), ph ^ 1, abort_flag, err, kErrWaitProducer)) {
               ok = false;
               break;
             }
-            tc_fence_after();
-            const uint32_t vb = v_lo + st * (L::kVBytes >> 4);
-#pragma unroll
-            for (int s = 0; s < BKV / 16; ++s)
-              mma_ts(tmem_base + 256 + a * 128, tmem_base + a * 128 + s * 8, vb + s * (2048 >> 4), hi_k, idesc_o,
-                     (j > 0 || s > 0) ? 1u : 0u);
-            if (a == 1) tc_commit(B(B_VEMPTY0 + st));
-            if (j == n - 1) tc_commit(B(B_ODONE0 + a));
-            if (j + 1 < n) {
-              const int g1 = gj + 1, st1 = g1 & 1;
-              if (a == 0 && !mbar_wait(B(B_KFULL0 + st1), (g1 >> 1) & 1, abort_flag, err, kErrWaitMma)) {
+            mbar_arrive_expect_tx(B(B_KFULL0 + st), L::kKBytes);
+            for (int b = 0; b < kDBlocks; ++b)
+              tma_load_2d(kb + b * (BKV * 128), &tk, B(B_KFULL0 + st), h * D + b * 64, k0);
+            if (!mbar_wait_inl(B(B_VEMPTY0 + st), ph ^ 1, abort_flag, err, kErrWaitProducer)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(B(B_VFULL0 + st), L::kVBytes);
+            for (int b = 0; b < kDBlocks; ++b)
+              tma_load_2d(vb + b * (BKV * 128), &tv, B(B_VFULL0 + st), h * D + b * 64, k0);
+          }
+          if (!ok) break;
+        }
+      }
+    } else if (warp == 9) {
+      if (lane == 0) {
+        // ---------------- MMA issuer ----------------
+        constexpr uint32_t idesc_s = make_idesc(1, 1, 1, 0, 0, BQ, BKV);
+        constexpr uint32_t idesc_o = make_idesc(1, 1, 1, 0, 1, BQ, D);
+        constexpr uint32_t hi_k = sdesc_hi_sw128(1024);  // K-major Q / K, and MN-major V: SBO 1024
+        const uint32_t q_lo = sdesc_lo(sQ, 16), k_lo = sdesc_lo(sK, 16), v_lo = sdesc_lo(sV, BKV * 128);
+        auto issue_s = [&](int a, int st) {
+          const uint32_t qa = q_lo + a * (L::kQTile >> 4), kb = k_lo + st * (L::kKBytes >> 4);
+  #pragma unroll
+          for (int s = 0; s < D / 16; ++s) {
+            const uint32_t off = ((s >> 2) * (BQ * 128) + (s & 3) * 32) >> 4;
+            mma_ss(tmem_base + a * 128, qa + off, kb + off, hi_k, idesc_s, s > 0 ? 1u : 0u);
+          }
+          tc_commit(B(B_SFULL0 + a));
+        };
+        int g = 0;
+        int it = 0;
+        bool ok = true;
+        for (; ok; ++it) {
+          const int slot = it % kItemRing;
+          if (!mbar_wait_inl(B(B_IFULL0 + slot), (it / kItemRing) & 1, abort_flag, err, kErrWaitMma)) break;
+          const int code = item_ring[slot];
+          mbar_arrive(B(B_IEMPTY0 + slot));
+          if (code < 0) break;
+          const int qt = code & 0xFFFFF;
+          const int n = p.tile_off[qt + 1] - p.tile_off[qt];
+          if (!mbar_wait_inl(B(B_QFULL), it & 1, abort_flag, err, kErrWaitMma) ||
+              !mbar_wait_inl(B(B_KFULL0 + (g & 1)), (g >> 1) & 1, abort_flag, err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(0, g & 1);
+          issue_s(1, g & 1);
+          tc_commit(B(B_KEMPTY0 + (g & 1)));
+          if (n == 1) tc_commit(B(B_QEMPTY));
+          for (int j = 0; j < n && ok; ++j) {
+            const int gj = g + j, st = gj & 1;
+            const uint32_t ph = (gj >> 1) & 1;
+            for (int a = 0; a < 2; ++a) {
+              if (!mbar_wait_inl(B(B_PLO0 + a), gj & 1, abort_flag, err, kErrWaitMma) ||
+                  (j == 0 && !mbar_wait_inl(B(B_OFREE0 + a), (it & 1) ^ 1, abort_flag, err, kErrWaitMma)) ||
+                  (a == 0 && !mbar_wait_inl(B(B_VFULL0 + st), ph, abort_flag, err, kErrWaitMma))) {
                 ok = false;
                 break;
               }
               tc_fence_after();
-              issue_s(a, st1);
-              if (a == 1) {
-                tc_commit(B(B_KEMPTY0 + st1));
-                if (j + 1 == n - 1) tc_commit(B(B_QEMPTY));
+              const uint32_t vb = v_lo + st * (L::kVBytes >> 4);
+  #pragma unroll
+              for (int s = 0; s < kPSplit / 16; ++s)
+                mma_ts(tmem_base + 256 + a * 128, tmem_base + a * 128 + s * 8, vb + s * (2048 >> 4), hi_k, idesc_o,
+                       (j > 0 || s > 0) ? 1u : 0u);
+              if (!mbar_wait_inl(B(B_PHI0 + a), gj & 1, abort_flag, err, kErrWaitMma)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+  #pragma unroll
+              for (int s = kPSplit / 16; s < BKV / 16; ++s)
+                mma_ts(tmem_base + 256 + a * 128, tmem_base + a * 128 + s * 8, vb + s * (2048 >> 4), hi_k, idesc_o, 1u);
+              if (a == 1) tc_commit(B(B_VEMPTY0 + st));
+              if (j == n - 1) tc_commit(B(B_ODONE0 + a));
+              if (j + 1 < n) {
+                const int g1 = gj + 1, st1 = g1 & 1;
+                if (a == 0 && !mbar_wait_inl(B(B_KFULL0 + st1), (g1 >> 1) & 1, abort_flag, err, kErrWaitMma)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                issue_s(a, st1);
+                if (a == 1) {
+                  tc_commit(B(B_KEMPTY0 + st1));
+                  if (j + 1 == n - 1) tc_commit(B(B_QEMPTY));
+                }
               }
             }
           }
+          g += n;
         }
-        g += n;
       }
     }
+    __syncwarp();
+    reg_inc<kRegsLaunch>();
   } else {
+    reg_inc<kRegsSoftmax>();
     // ---------------- softmax / correction / epilogue: warpgroup a = warp / 4 ----------------
     const int a = warp >> 2;
     const int row_in_tile = (warp & 3) * 32 + lane;
@@ -359,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (; ok; ++it) {
       const int slot = it % kItemRing;
-      if (!mbar_wait(B(B_IFULL0 + slot), (it / kItemRing) & 1, abort_flag, err, kErrWaitEpilogue)) break;
+      if (!mbar_wait_inl(B(B_IFULL0 + slot), (it / kItemRing) & 1, abort_flag, err, kErrWaitEpilogue)) break;
       const int code = item_ring[slot];
       __syncwarp();
       if (lane == 0) mbar_arrive(B(B_IEMPTY0 + slot));
@@ -389,96 +490,95 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int gj = g + j;
         const int info = info_next;
         if (j + 1 < n) info_next = p.ktile[t0 + j + 1];  // prefetch the next tile descriptor
-        if (!mbar_wait(B(B_SFULL0 + a), gj & 1, abort_flag, err, kErrWaitEpilogue)) {
+        if (!mbar_wait_inl(B(B_SFULL0 + a), gj & 1, abort_flag, err, kErrWaitEpilogue)) {
           ok = false;
           break;
         }
         tc_fence_after();
         uint32_t sr[BKV];  // raw scores of this row (fp32 bits)
-#pragma unroll
-        for (int c = 0; c < BKV / 32; ++c)
-          tmem_ld32(s_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
-        tmem_ld_wait();
         const int k0 = info >> 9;
         const int valid = (info & 0xFF) + 1;
         const bool masked = (info >> 8) & 1;
-        if (masked || valid < BKV) {
-          // visible keys of this row as four 32-key bit words, then one test + select per key
-          uint32_t vis[BKV / 32];
+        {
 #pragma unroll
-          for (int w = 0; w < BKV / 32; ++w) {
-            const int base = k0 + 32 * w;
-            uint32_t m = bits_below(valid - 32 * w);
-            if (masked) m &= ~(bit_span(x0 - base, x1 - base) | bit_span(x2 - base, x3 - base));
-            vis[w] = m;
+          for (int c = 0; c < BKV / 32; ++c)
+            tmem_ld32(s_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
+          tmem_ld_wait();
+          if (masked || valid < BKV) {
+            // visible keys of this row as four 32-key bit words, then one test + select per key
+            uint32_t vis[BKV / 32];
+#pragma unroll
+            for (int w = 0; w < BKV / 32; ++w) {
+              const int base = k0 + 32 * w;
+              uint32_t m = bits_below(valid - 32 * w);
+              if (masked) m &= ~(bit_span(x0 - base, x1 - base) | bit_span(x2 - base, x3 - base));
+              vis[w] = m;
+            }
+#pragma unroll
+            for (int c = 0; c < BKV; ++c)
+              if (!((vis[c >> 5] >> (c & 31)) & 1u)) sr[c] = __float_as_uint(-INFINITY);
           }
-#pragma unroll
-          for (int c = 0; c < BKV; ++c)
-            if (!((vis[c >> 5] >> (c & 31)) & 1u)) sr[c] = __float_as_uint(-INFINITY);
         }
-        // tile max of the raw scores: four independent 3-input max chains
-        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int c = 0; c < BKV; c += 8) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            mq[u] = max3(mq[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
-        }
-        const float mt = max3(mq[0], mq[1], fmaxf(mq[2], mq[3]));
-        // The reference max only moves when the tile max exceeds it by more than 2^8 (in log2
-        // units), so exponents stay <= 8 and O is rescaled rarely; the result is exact.
+        // The reference max m of a row moves only when a tile's max exceeds it by more than
+        // 2^8 (in log2 units), so exponents stay <= 8 and O is rescaled rarely; the result is
+        // exact.  The exponentials therefore start against the current reference before the
+        // tile max is known (the max chains overlap them), and the tile is redone from the
+        // scores still in registers only when the reference has to move.  A row's first tile
+        // speculates on m = 0 and keeps it when its max lies within [-32, 8] (the row sum
+        // then stays >= 2^-32).
+        const float mt = row_max(sr);
+        const bool first = (m_run == -INFINITY);
+        const float m_spec = first ? 0.f : m_run;
+        const float2 lo = p_chunks<0, kPSplit / 16>(sr, p.scale_log2, m_spec, s_tmem);
         const float mts = mt * p.scale_log2;
-        const bool grow = mts > m_run + 8.0f;
-        const float m_new = grow ? mts : m_run;
-        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        const float corr = grow ? ex2(m_run - m_use) : 1.0f;  // m_run = -inf gives 0
-        const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
-        const float2 negm2 = make_float2(-m_use, -m_use);
-        // two row-sum chains and 16-key P chunks keep this loop within the register budget
-        float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        const bool grow = first ? (mts > 8.0f || mts < -32.0f) : (mts > m_run + 8.0f);
+        if (!__any_sync(0xffffffffu, grow)) {
+          // keys [0, kPSplit) are final: the first PV products start while the rest is computed
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(B(B_PLO0 + a));
+          const float2 hi = p_chunks<kPSplit / 16, BKV / 16>(sr, p.scale_log2, m_spec, s_tmem);
+          const float2 rsum = add2(lo, hi);
+          l_run += rsum.x + rsum.y;
+          m_run = m_spec;
+        } else {
+          // some row of this warp moves its reference: redo the tile (rows that do not move
+          // recompute the same values), then rescale O
+          const float m_new = grow ? mts : m_spec;
+          const float m_use = (m_new == -INFINITY) ? 0.f : m_new;  // a fully masked tile keeps 0
+          const float corr = grow ? ex2(m_spec - m_use) : 1.0f;  // O and l are relative to m_spec
+          tmem_st_wait();  // the speculative stores land before they are overwritten
+          const float2 rsum = p_chunks<0, BKV / 16>(sr, p.scale_log2, m_use, s_tmem);
+          // O_a is stable here: S_j(a) completed, so PV_{j-1}(a) (issued before it) did too;
+          // and PV_j(a) is not issued before this warpgroup signals P_j(a) below.
+          if (j > 0) {
 #pragma unroll
-        for (int c0 = 0; c0 < BKV; c0 += 16) {
-          uint32_t pk[8];
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32(o_tmem + c * 32, o);
+              tmem_ld_wait();
 #pragma unroll
-          for (int c = 0; c < 16; c += 2) {
-            const float2 x = fma2(make_float2(__uint_as_float(sr[c0 + c]), __uint_as_float(sr[c0 + c + 1])), scale2,
-                                  negm2);
-            // a quarter of the exponentials run on the FMA pipe to relieve the MUFU unit
-            float2 e;
-            e.x = ex2(x.x);
-            e.y = ((c & 2) != 0) ? exp2_poly(x.y) : ex2(x.y);
-            rs2[(c >> 1) & 1] = add2(rs2[(c >> 1) & 1], e);
-            pk[c / 2] = pack_bf16(e.x, e.y);
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+              tmem_st32(o_tmem + c * 32, o);
+            }
           }
-          // P over the first 64 columns of S_a: key 2c in the low half of column c
-          tmem_st8(s_tmem + c0 / 2, pk);
-        }
-        const float2 rsum = add2(rs2[0], rs2[1]);
-        const float rs = rsum.x + rsum.y;
-        // O_a is stable here: S_j(a) completed, so PV_{j-1}(a) (issued before it) did too; and
-        // PV_j(a) is not issued before this warpgroup signals P_j(a) below.
-        if (j > 0 && __any_sync(0xffffffffu, grow)) {
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(o_tmem + c * 32, o);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
-            tmem_st32(o_tmem + c * 32, o);
-          }
+          l_run = l_run * corr + (rsum.x + rsum.y);
+          m_run = m_new;  // stays -inf while every key seen so far was masked
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(B(B_PLO0 + a));
         }
         tmem_st_wait();
-        l_run = l_run * corr + rs;
-        m_run = m_new;
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(B(B_PFULL0 + a));
+        if (lane == 0) mbar_arrive(B(B_PHI0 + a));
       }
       if (!ok) break;
       g += n;
       // Epilogue: wait for the last PV of this tile, normalise, gate, store.
-      if (!mbar_wait(B(B_ODONE0 + a), it & 1, abort_flag, err, kErrWaitEpilogue)) break;
+      if (!mbar_wait_inl(B(B_ODONE0 + a), it & 1, abort_flag, err, kErrWaitEpilogue)) break;
       tc_fence_after();
       float gate = 1.f;
       if (p.gate_logits && row_valid) {
@@ -512,7 +612,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    __syncwarp();
+    reg_dec<kRegsLaunch>();
   }
+  // every warp is back at the launch's count here (the decreases above never wait; an
+  // increase waits until the softmax warps have given their share back)
 
   tc_fence_before();
   __syncthreads();

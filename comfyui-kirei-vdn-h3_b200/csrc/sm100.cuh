@@ -91,6 +91,24 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   return mbar_wait_slow(bar, parity, abort_flag, err, code);
 }
 
+// The same bounded wait with its slow path inlined, for kernels that reallocate registers
+// between warps (setmaxnreg): a function call there would need one register budget for
+// warps that run with different ones.
+__device__ __forceinline__ bool mbar_wait_inl(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                              int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      if (err) atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
 // After an abort, give any bulk copy still in flight time to land before the CTA
 // releases its shared memory.
 __device__ __forceinline__ void abort_drain() {

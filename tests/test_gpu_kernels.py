@@ -203,6 +203,31 @@ def test_window_attention_ragged_tiles(geom, cutting):
     assert rel_l2(got[rows], want) < 1e-2
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_window_attention_moving_reference_is_exact(D):
+    """Scores far from the N(0, 1) range exercise every branch of the online softmax: rows
+    whose reference maximum moves by more than 2^8 within and across key tiles (large q), rows
+    whose first tile lies entirely below 2^-32 of the speculative reference (q opposite to
+    every key), and ordinary rows."""
+    lay = vo.make_layout(40, 9, (6, 8), anchor_frames="both")
+    S, H = lay.seq_len, 2
+    g = torch.Generator().manual_seed(50)
+    u = torch.nn.functional.normalize(torch.randn(H, D, generator=g), dim=-1)
+    k = torch.nn.functional.normalize(u + 0.3 * torch.randn(S, H, D, generator=g), dim=-1)
+    q = torch.randn(S, H, D, generator=g)
+    q[0::3] *= 30
+    q[1::3] = -300.0 * u
+    v = torch.randn(S, H, D, generator=g)
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    got = pkg.window_softmax_b200(q.to(DEV), k.to(DEV), v.to(DEV), lay.video_start, lay.video_end, lay.num_frames,
+                                  lay.tokens_per_frame, list(lay.bounds), D ** -0.5, "both")
+    want = vo.window_attention(q.double(), k.double(), v.double(), lay.video_start, lay.video_end, lay.num_frames,
+                               lay.tokens_per_frame, list(lay.bounds), D ** -0.5, "both")
+    assert torch.isfinite(got.float()).all()
+    for name, rows in (("moving", slice(0, S, 3)), ("below", slice(1, S, 3)), ("plain", slice(2, S, 3))):
+        assert rel_l2(got[rows], want[rows]) < 1e-2, name
+
+
 # --------------------------------------------------------------------------- branch kernels
 def _branch_setup(seed=40, Fb=6, grid=(4, 5), H=2, D=64, text=9):
     tpf = grid[0] * grid[1]
