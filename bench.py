@@ -317,7 +317,7 @@ def config_entry(args, c, world) -> dict:
             "parallelism": f"heads/{world}" if world > 1 else "none",
             "l2": f"inputs larger than L2 (x {S * hidden * 2 / 1e6:.0f} MB, weights "
                   f"{(5 * H * D + 2 * H + 2 * D) * hidden * 2 / 1e9:.2f} GB)",
-            "delta_rule": args.delta_rule, "rope": bool(args.rope)}
+            "delta_rule": args.delta_rule, "rope": bool(args.rope), "precision": args.precision}
 
 
 def run_reference_arm(args, c, world, rank):
@@ -587,6 +587,8 @@ def main():
     ap.add_argument("--blocks", type=int, default=None, help="config 4: number of DiT blocks (default 50)")
     ap.add_argument("--delta-rule", choices=["vdn_solve", "sana_scaled"], default="vdn_solve",
                     help="configs 1/3: the branch's delta rule (BASELINE's released lineage is vdn_solve)")
+    ap.add_argument("--precision", choices=["bf16", "int8", "fp8"], default="bf16",
+                    help="configs 1/3: projection arithmetic (config 2 = config 1 with int8 or fp8)")
     ap.add_argument("--rope", action="store_true",
                     help="configs 1/3: apply a rot_dim = head_dim RoPE table to q/k (not in BASELINE's config)")
     args = ap.parse_args()
@@ -635,7 +637,13 @@ def main():
                                  k_norm=types.SimpleNamespace(weight=kn, eps=1e-6), forward=None)
     # N > 1: the heads are sharded over the ranks (H/N each, recurrence kept per head), the
     # per-head outputs exchanged by row block over NCCL and the projected rows all-gathered
-    state = pkg.B200State("bench", node_config(args.delta_rule), [branch], H, D, shard_heads=world > 1)
+    maps = None
+    if args.precision != "bf16":
+        # config 2: qkv_proj / out_proj quantised by the block, to_out_linear stored quantised
+        # (no bf16 edge block: the benchmarked block is an interior one)
+        maps = pkg.prepare_projection_maps([branch], dev, args.precision, skip_end_blocks=0)[0]
+    state = pkg.B200State("bench", node_config(args.delta_rule), [branch], H, D, shard_heads=world > 1,
+                          projection_precision=args.precision, weight_maps=maps)
     block = state.fused_block(attn, 0, dev)
     rope_freqs = rope_freqs_table(lay.seq_len, D, dev) if args.rope else None
     rope = pkg.rope_table(rope_freqs, lay.seq_len, D, dev)
@@ -655,6 +663,20 @@ def main():
         attn_ms.append((e0, e1))
 
     pkg.hybrid.launch_window_attention = timed_launch
+    # the projection GEMMs' own launches, timed the same way (their streams are the current one)
+    gemm_ms = {"vdn_qkv_gemm": [], "vdn_gemm_block": []}
+    orig_call = pkg._lib.call
+
+    def timed_call(name, *a):
+        if name not in gemm_ms:
+            return orig_call(name, *a)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        orig_call(name, *a)
+        e1.record()
+        gemm_ms[name].append((e0, e1))
+
+    pkg._lib.call = timed_call
     clocks = ClockSampler(local).start()  # running through the warm-up, so it samples the timed region
     with pkg.cholesky_runtime_scope():
         for _ in range(args.warmup):
@@ -662,6 +684,8 @@ def main():
     torch.cuda.synchronize()
     status.raise_if_failed()
     attn_ms.clear()
+    for v in gemm_ms.values():
+        v.clear()
     barrier(world)
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -678,14 +702,29 @@ def main():
     barrier(world)
     status.raise_if_failed()
     pkg.hybrid.launch_window_attention = orig_launch
+    pkg._lib.call = orig_call
     ms = e_start.elapsed_time(e_end) / max(args.steps, 1)
     ms = max_over_ranks(ms, world)
     value = flops["total"] / (ms * 1e-3) / 1e12  # one block forward of the whole problem per step
     attn_avg = sum(a.elapsed_time(b) for a, b in attn_ms) / max(len(attn_ms), 1)
     pk, pk_src = peaks()
     achieved = flops["attention"] / world / (attn_avg * 1e-3) / 1e12  # this rank's heads
-    
     peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    # projection GEMMs per forward: the QKV GEMM (its algorithmic q/k/v columns) and the output
+    # projection passes (out_proj + to_out_linear), against the tensor peak of their arithmetic
+    # (int8 / e4m3 run at twice the bf16 rate: the measured bf16 peak doubled)
+    steps_n = max(args.steps, 1)
+    qkv_ms = sum(a.elapsed_time(b) for a, b in gemm_ms["vdn_qkv_gemm"]) / steps_n
+    out_ms = sum(a.elapsed_time(b) for a, b in gemm_ms["vdn_gemm_block"]) / steps_n
+    gemm_peak = peak * (1 if args.precision == "bf16" else 2)
+    gemm_line = {}
+    for name, fl, t in (("qkv", flops["qkv"] / world, qkv_ms),
+                        ("out_proj+to_out_linear", flops["out_proj"] + flops.get("to_out_linear", 0.0), out_ms)):
+        if t > 0:
+            gemm_line[name] = {"ms": t, "achieved": fl / (t * 1e-3) / 1e12, "peak": gemm_peak, "unit": "TFLOP/s",
+                               "frac": fl / (t * 1e-3) / 1e12 / gemm_peak}
+    gemm_line["peak_source"] = (f"{pk_src} sustained bf16" if args.precision == "bf16" else
+                                f"2 x {pk_src} sustained bf16 (dense {args.precision} tensor rate)")
     # ---- end to end through the public operator with host buffers: every step copies its
     # input from pinned host memory and its output back; HostStreamer overlaps the copies of
     # steps i+1 and i-1 with the compute of step i
@@ -755,7 +794,7 @@ def main():
     line = {
         "metric": metric_name(c), "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) x)",
+        "vs_baseline": None, "dtype": args.precision, "data": "synthetic (seeded N(0,0.02) weights, N(0,1) x)",
         "config": config_entry(args, c, world),
         "tflop_per_step": flops["total"] / 1e12,
         "roofline": {"kernel": "window_attention_kernel", "bound": "tensor", "achieved": achieved, "peak": peak,
@@ -770,9 +809,10 @@ def main():
                   f"{E2E_ROW_BLOCKS if world == 1 else 1} row blocks per copy",
                 **copy_ms},
         "gpu_launches": launches,
+        "gemm": gemm_line,
         "clocks": clock_summary,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.precision == "bf16":
         # the same block on the host cores: the CPU baseline, and the parity of the benchmarked
         # output (out_dev holds the last device-resident step's output for x)
         baseline, parity = cpu_baseline(c, (qkv, qn, kn, out_w, branch), x_host,

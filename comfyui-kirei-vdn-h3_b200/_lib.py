@@ -37,6 +37,7 @@ SIGNATURES: dict[str, list] = {
                              _P, _P, _P, _L, _P, _L, _I, _P, _P, _P, _P],
     "vdn_spatial_conv": [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _L, _P],
     "vdn_temporal_act": [_P, _L, _P, _I, _I, _I, _I, _I, _I, _P, _P],
+    "vdn_conv_features": [_P, _L, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P],
     "vdn_alpha_gate": [_P, _L, _I, _I, _I, _P, _P, _P, _I, _I, _P, _P],
     "vdn_frame_stats": [_P, _P, _I, _I, _I, _I, _P, _L, _I, _P, _P, _P],
     "vdn_frame_stats_tc": [_P, _P, _I, _I, _I, _P, _L, _I, _P, _P, _P, _P],

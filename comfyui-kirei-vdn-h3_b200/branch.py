@@ -206,7 +206,8 @@ class BranchWorkspace:
         self.key = (str(dev), Fb, tpf, heads, dim, text_len, tile_frames)
         self.tile_frames = tile_frames
         self.feature_frames = tile
-        self.conv_tmp = torch.empty(rows, inner, **bf)
+        self._conv_shape = (rows, inner)
+        self._conv_tmp = None  # the spatial conv's output, for the two-kernel path only
         self.qf = torch.empty(tile, heads, tpf, dim, **bf)
         self.kf = torch.empty(tile, heads, tpf, dim, **bf)
         self.vf = torch.empty(tile, heads, tpf, dim, **bf)
@@ -229,6 +230,13 @@ class BranchWorkspace:
         self.lohi: dict = {}
         self._side = None
 
+    def conv_buffer(self) -> torch.Tensor:
+        """[rows, H*D] bf16 spatial-conv output of the two-kernel feature path (allocated on
+        first use: the fused path never needs it)."""
+        if self._conv_tmp is None:
+            self._conv_tmp = torch.empty(*self._conv_shape, device=self.alpha.device, dtype=torch.bfloat16)
+        return self._conv_tmp
+
     def side_stream(self) -> torch.cuda.Stream:
         """The stream the text state runs on, beside the frames' kernels."""
         if self._side is None:
@@ -246,6 +254,14 @@ class BranchWorkspace:
 
 
 TILE_HALO = 2  # frames each side: the 5-tap temporal conv's reach (runtime.py:428-430)
+FUSED_CONV = True  # short conv features in one kernel where its geometry allows
+
+
+def fused_conv_ok(src: torch.Tensor, kh: int, kw: int, taps: int, dim: int) -> bool:
+    """Whether ``vdn_conv_features`` takes these features (5x5 spatial, 5-tap temporal, head
+    dim 64 or 128, 16-byte aligned rows); otherwise the spatial and temporal kernels run."""
+    return (FUSED_CONV and kh == 5 and kw == 5 and taps == 5 and dim in (64, 128) and src.data_ptr() % 16 == 0
+            and src.stride(0) % 8 == 0 and src.stride(-1) == 1)
 
 
 def frame_tiles(Fb: int, tile_frames) -> list[tuple[int, int]]:
@@ -307,9 +323,15 @@ def run_branch(ws: BranchWorkspace, bw: BranchDeviceWeights, *, q_raw, k_raw, v_
         nf = hb - ha
         if conv:
             sp, kh, kw, tm, taps = bw.conv[name]
+            if fused_conv_ok(src, kh, kw, taps, D):
+                # spatial + temporal conv, SiLU and L2 in one pass (no intermediate in HBM)
+                call("vdn_conv_features", src.data_ptr(), src.stride(0), sp.data_ptr(), kh, kw, tm.data_ptr(), taps,
+                     nf, gh, gw, H, D, int(l2), dst.data_ptr(), stream)
+                return a - ha
+            conv_tmp = ws.conv_buffer()
             call("vdn_spatial_conv", src.data_ptr(), src.stride(0), sp.data_ptr(), kh, kw, nf, gh, gw, inner,
-                 ws.conv_tmp.data_ptr(), ws.conv_tmp.stride(0), stream)
-            call("vdn_temporal_act", ws.conv_tmp.data_ptr(), ws.conv_tmp.stride(0), tm.data_ptr(), taps, nf, tpf,
+                 conv_tmp.data_ptr(), conv_tmp.stride(0), stream)
+            call("vdn_temporal_act", conv_tmp.data_ptr(), conv_tmp.stride(0), tm.data_ptr(), taps, nf, tpf,
                  H, D, int(l2), dst.data_ptr(), stream)
         else:
             call("vdn_temporal_act", src.data_ptr(), src.stride(0), None, 0, nf, tpf, H, D, int(l2), dst.data_ptr(),

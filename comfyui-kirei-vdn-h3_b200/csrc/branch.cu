@@ -319,6 +319,217 @@ __global__ void __launch_bounds__(256, 3) temporal_act_kernel(const __nv_bfloat1
 }
 
 // ---------------------------------------------------------------------------------
+// 1+2 fused: the short conv features in one pass over the raw projection (branch.py:443-480
+// with kernels.py:99-129): depthwise 5x5 spatial conv per frame (bf16-rounded, as the
+// reference's bf16 conv2d output), 5-tap temporal conv (zero padded at the clip ends),
+// SiLU, optional L2 over the head, FHSD output.  The same arithmetic, in the same order, as
+// vdn_spatial_conv followed by vdn_temporal_act, without the intermediate round trip
+// through HBM.
+//
+// A unit is one head (D channels) x 4 output rows x up to kFeatMaxCols output columns of
+// the frame grid, walked through every frame in order: frame t's input rows (with a 2-pixel
+// zero-padded halo) are staged in shared memory by cp.async while frame t-1 is computed;
+// each thread computes its row's spatial outputs for two channels (the sliding 5x5 window of
+// spatial_conv5_tiled_kernel) into a 5-frame ring in shared memory, which only that thread
+// reads back: the temporal output of frame t-2 combines ring slots t-4 .. t.  Warp w owns
+// row w % 4 and channels 64 (w / 4) + 2 lane, +1; the L2 sum of a position spans the
+// D / 64 warps of its row (exchanged through shared memory) and is reduced in the tree of
+// vdn_temporal_act's 32 lanes of D / 32 channels.  Units are ordered head by head, band by
+// band, so neighbouring bands run at the same time and their shared halo rows come from L2.
+// ---------------------------------------------------------------------------------
+constexpr int kFeatRows = 4;
+constexpr int kFeatMaxCols = 22;  // two staging buffers, the ring and the L2 exchange fit 227 KB at D = 128
+
+template <int D>
+struct FeatLayout {
+  static constexpr int kHalves = D / 64;
+  static constexpr int kThreads = 128 * kHalves;
+  __host__ __device__ static int stage_elems(int wc) { return (kFeatRows + 4) * (wc + 4) * D; }
+  __host__ __device__ static int ring_elems(int wc) { return 5 * kFeatRows * wc * D; }
+  __host__ __device__ static size_t bytes(int wc) {
+    return (size_t)(2 * stage_elems(wc) + ring_elems(wc)) * 2 + (size_t)kFeatRows * kHalves * kFeatMaxCols * 16 * 4;
+  }
+};
+
+template <int D>
+__global__ void __launch_bounds__(FeatLayout<D>::kThreads, 1)
+    conv_features_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in, const float* __restrict__ w_sp,
+                         const float* __restrict__ w_tm, int F, int gh, int gw, int H, int wc, int l2,
+                         __nv_bfloat16* __restrict__ out) {
+  using L = FeatLayout<D>;
+  extern __shared__ __align__(16) __nv_bfloat16 feat_smem[];
+  __nv_bfloat16* stage = feat_smem;                     // [2][rows + 4][wc + 4][D]
+  __nv_bfloat16* ring = feat_smem + 2 * L::stage_elems(wc);  // [5][rows][wc][D]
+  float* part = reinterpret_cast<float*>(ring + L::ring_elems(wc));  // [rows][halves][kFeatMaxCols][16]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = warp & (kFeatRows - 1), hh = warp / kFeatRows;
+  const int T = gh * gw;
+  const int pitch = wc + 4;
+  const int bands = (gh + kFeatRows - 1) / kFeatRows;
+  const int cblocks = (gw + wc - 1) / wc;
+  const int n_units = H * bands * cblocks;
+  const int cl = hh * 64 + 2 * lane;  // this thread's first channel inside the head
+
+  for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
+    const int h = unit / (bands * cblocks);
+    const int rem = unit - h * bands * cblocks;
+    const int band = rem / cblocks, cb = rem - band * cblocks;
+    const int y0 = band * kFeatRows, x0 = cb * wc;
+    const int ncols = min(wc, gw - x0);
+    const bool row_on = y0 + r < gh;
+    const int c = h * D + cl;  // global channel
+    float2 wr[5][5];
+#pragma unroll
+    for (int dy = 0; dy < 5; ++dy)
+#pragma unroll
+      for (int dx = 0; dx < 5; ++dx)
+        wr[dy][dx] = make_float2(w_sp[(long long)c * 25 + dy * 5 + dx], w_sp[(long long)(c + 1) * 25 + dy * 5 + dx]);
+    float2 wt[5];
+#pragma unroll
+    for (int dt = 0; dt < 5; ++dt) wt[dt] = make_float2(w_tm[(long long)c * 5 + dt], w_tm[(long long)(c + 1) * 5 + dt]);
+
+    auto issue = [&](int f, int buf) {
+      __nv_bfloat16* dst0 = stage + buf * L::stage_elems(wc);
+      constexpr int kChunks = D / 8;  // 16-byte pieces of one pixel's D channels
+      const int total = (kFeatRows + 4) * pitch * kChunks;
+      for (int i = tid; i < total; i += L::kThreads) {
+        const int q = i % kChunks, px = i / kChunks;
+        const int row = px / pitch, col = px - row * pitch;
+        const int yy = y0 - 2 + row, xx = x0 + col - 2;
+        __nv_bfloat16* dst = dst0 + px * D + q * 8;
+        if (yy >= 0 && yy < gh && xx >= 0 && xx < gw && col < ncols + 4)
+          cp_async16(smem_u32(dst), in + ((long long)(f * gh + yy) * gw + xx) * ld_in + h * D + q * 8);
+        else
+          *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      cp_async_commit();
+    };
+    // this thread's ring entries: frames before the clip read as zeros
+    __nv_bfloat16* my_ring = ring + (r * wc) * D + cl;  // + slot * rows * wc * D + x * D
+    const int slot_stride = kFeatRows * wc * D;
+    for (int s = 0; s < 5; ++s)
+      for (int x = 0; x < ncols; ++x)
+        *reinterpret_cast<uint32_t*>(my_ring + s * slot_stride + x * D) = 0u;
+
+    issue(0, 0);
+    for (int t = 0; t < F + 2; ++t) {
+      const int slot = t % 5;
+      if (t < F) {
+        if (t + 1 < F) {
+          issue(t + 1, (t + 1) & 1);
+          cp_async_wait<1>();
+        } else {
+          cp_async_wait<0>();
+        }
+        __syncthreads();
+        if (row_on) {
+          // shared row r + dy holds image row y0 + r - 2 + dy; shared column x + k image column x0 + x - 2 + k
+          const __nv_bfloat16* base = stage + (t & 1) * L::stage_elems(wc) + r * pitch * D + cl;
+          __nv_bfloat16* wring = my_ring + slot * slot_stride;
+          float2 win[5][5];  // win[slot][dy]; slot (x + k) % 5 holds shared column x + k
+#pragma unroll
+          for (int s = 0; s < 5; ++s)
+#pragma unroll
+            for (int dy = 0; dy < 5; ++dy) win[s][dy] = lds_bf162(base + (dy * pitch + s) * D);
+          auto step = [&](int u, int x) {
+            float2 a[5];
+#pragma unroll
+            for (int dy = 0; dy < 5; ++dy) a[dy] = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < 5; ++k)
+#pragma unroll
+              for (int dy = 0; dy < 5; ++dy) a[dy] = fma2(wr[dy][k], win[(u + k) % 5][dy], a[dy]);
+            const float2 sum = add2(add2(add2(a[0], a[1]), add2(a[2], a[3])), a[4]);
+            *reinterpret_cast<__nv_bfloat162*>(wring + x * D) = __floats2bfloat162_rn(sum.x, sum.y);
+            if (x + 5 < pitch) {
+#pragma unroll
+              for (int dy = 0; dy < 5; ++dy) win[u][dy] = lds_bf162(base + (dy * pitch + x + 5) * D);
+            }
+          };
+          int x = 0;
+          for (; x + 5 <= ncols; x += 5) {
+#pragma unroll
+            for (int u = 0; u < 5; ++u) step(u, x + u);
+          }
+#pragma unroll
+          for (int u = 0; u < 5; ++u)
+            if (x + u < ncols) step(u, x + u);
+        }
+      } else {
+        // frames past the clip read as zeros
+        for (int x = 0; x < ncols; ++x) *reinterpret_cast<uint32_t*>(my_ring + slot * slot_stride + x * D) = 0u;
+      }
+      if (t >= 2) {
+        // temporal conv of frame fo = t - 2 over slots fo - 2 .. fo + 2, then SiLU and the L2 sum
+        const int fo = t - 2;
+        float2 y[kFeatMaxCols];
+        float ssq[kFeatMaxCols];
+#pragma unroll
+        for (int x = 0; x < kFeatMaxCols; ++x) {
+          if (x < ncols) {
+            float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int dt = 0; dt < 5; ++dt) {
+              const float2 v = lds_bf162(my_ring + ((fo + 3 + dt) % 5) * slot_stride + x * D);  // frame fo - 2 + dt
+              acc.x = fmaf(wt[dt].x, v.x, acc.x);
+              acc.y = fmaf(wt[dt].y, v.y, acc.y);
+            }
+            y[x] = make_float2(silu(acc.x), silu(acc.y));
+            // vdn_temporal_act's lane sum over D / 32 consecutive channels, in order
+            float s = fmaf(y[x].y, y[x].y, y[x].x * y[x].x);
+            if (D == 128) {  // lanes 2m, 2m + 1 hold the four channels of one such sum
+              const float lo = __shfl_xor_sync(0xffffffffu, s, 1);
+              const float2 yo = make_float2(__shfl_xor_sync(0xffffffffu, y[x].x, 1),
+                                            __shfl_xor_sync(0xffffffffu, y[x].y, 1));
+              s = (lane & 1) ? fmaf(y[x].y, y[x].y, fmaf(y[x].x, y[x].x, lo))
+                             : fmaf(yo.y, yo.y, fmaf(yo.x, yo.x, s));
+            }
+            ssq[x] = s;
+          }
+        }
+        if (l2) {
+          if (D == 128) {
+            // the tree's first step pairs sums of the row's two warps (channels c and c + 64):
+            // one value per lane pair and position goes through shared memory
+            float* mine = part + ((r * L::kHalves + hh) * kFeatMaxCols) * 16 + (lane >> 1);
+            const float* theirs = part + ((r * L::kHalves + (hh ^ 1)) * kFeatMaxCols) * 16 + (lane >> 1);
+            if ((lane & 1) == 0) {
+#pragma unroll
+              for (int x = 0; x < kFeatMaxCols; ++x)
+                if (x < ncols) mine[x * 16] = ssq[x];
+            }
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + r), "n"(64) : "memory");  // the row's two warps
+#pragma unroll
+            for (int x = 0; x < kFeatMaxCols; ++x)
+              if (x < ncols) ssq[x] += theirs[x * 16];
+          }
+#pragma unroll
+          for (int x = 0; x < kFeatMaxCols; ++x) {
+            if (x < ncols) {
+              float s = ssq[x];
+#pragma unroll
+              // the remaining steps inside the warp (lane pairs share a value at D = 128)
+              for (int o = 16; o >= (D == 128 ? 2 : 1); o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+              const float inv = 1.0f / fmaxf(sqrtf(s), 1e-6f);
+              y[x].x *= inv;
+              y[x].y *= inv;
+            }
+          }
+        }
+        if (row_on) {
+          const int s0 = (y0 + r) * gw + x0;
+          __nv_bfloat16* orow = out + (((long long)fo * H + h) * T + s0) * D + cl;
+#pragma unroll
+          for (int x = 0; x < kFeatMaxCols; ++x)
+            if (x < ncols) *reinterpret_cast<__nv_bfloat162*>(orow + (long long)x * D) = __floats2bfloat162_rn(y[x].x, y[x].y);
+        }
+      }
+      __syncthreads();  // the stage buffer refilled next is free
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
 // 3. alpha gate.  down[rows, ld_down] fp32 (the x W_down^T columns, computed by the
 // projection GEMM), mean over the T rows of each frame, then up + dt_bias, softplus.
 // grid F, block 256.  alpha out [F, H, D] fp32.
@@ -921,6 +1132,39 @@ int vdn_spatial_conv(const void* in, long long ld_in, const float* w, int kh, in
                                              C, reinterpret_cast<__nv_bfloat16*>(out), ld_out);
     vdn::count_launch();
   }
+  return vdn::launch_status();
+}
+
+// 1+2 fused: short conv features of F frames in one pass (branch.py:443-480 + kernels.py:99-129).
+// in: raw rows (f*gh + y)*gw + x at pitch ld_in, channel h*D + d (bf16); w_sp [H*D, kh*kw]
+// fp32; w_tm [H*D, taps] fp32; out FHSD [F, H, gh*gw, D] bf16.  Same result as
+// vdn_spatial_conv followed by vdn_temporal_act.  kUnsupported unless kh = kw = taps = 5
+// and D is 64 or 128 (the two-kernel path covers the rest).
+int vdn_conv_features(const void* in, long long ld_in, const float* w_sp, int kh, int kw, const float* w_tm, int taps,
+                      int F, int gh, int gw, int H, int D, int l2norm, void* out, void* stream) {
+  using namespace vdn::branch;
+  if (!in || !w_sp || !w_tm || !out || F <= 0 || gh <= 0 || gw <= 0 || H <= 0) return vdn::kBadArgument;
+  if (kh != 5 || kw != 5 || taps != 5 || (D != 64 && D != 128)) return vdn::kUnsupported;
+  if (!vdn::aligned16(in) || (ld_in % 8) || (reinterpret_cast<uintptr_t>(out) % 4)) return vdn::kMisaligned;
+  const int cblocks = (gw + kFeatMaxCols - 1) / kFeatMaxCols;
+  const int wc = (gw + cblocks - 1) / cblocks;
+  const long long units = (long long)H * ((gh + kFeatRows - 1) / kFeatRows) * cblocks;
+  const int grid = (int)std::min<long long>(units, vdn::sm_count());
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  const auto* x = reinterpret_cast<const __nv_bfloat16*>(in);
+  auto* y = reinterpret_cast<__nv_bfloat16*>(out);
+  if (D == 128) {
+    const int smem = (int)FeatLayout<128>::bytes(wc);
+    if (!vdn::smem_optin((const void*)conv_features_kernel<128>, smem)) return vdn::kLaunchFailed;
+    conv_features_kernel<128><<<grid, FeatLayout<128>::kThreads, smem, s>>>(x, ld_in, w_sp, w_tm, F, gh, gw, H, wc,
+                                                                            l2norm, y);
+  } else {
+    const int smem = (int)FeatLayout<64>::bytes(wc);
+    if (!vdn::smem_optin((const void*)conv_features_kernel<64>, smem)) return vdn::kLaunchFailed;
+    conv_features_kernel<64><<<grid, FeatLayout<64>::kThreads, smem, s>>>(x, ld_in, w_sp, w_tm, F, gh, gw, H, wc,
+                                                                          l2norm, y);
+  }
+  vdn::count_launch();
   return vdn::launch_status();
 }
 

@@ -150,6 +150,14 @@ int vdn_spatial_conv(const void* in, long long ld_in, const float* w, int kh, in
 int vdn_temporal_act(const void* in, long long ld_in, const float* w, int taps, int F, int T, int H, int D,
                      int l2norm, void* out, void* stream);
 
+/* The two above in one pass: depthwise 5x5 spatial conv (bf16-rounded), 5-tap temporal conv,
+ * SiLU, optional L2 over D, FHSD output [F, H, gh*gw, D] bf16, with no intermediate in
+ * memory.  w_sp [H*D, 25], w_tm [H*D, 5] fp32; in 16-byte aligned, ld_in % 8 == 0.
+ * -2 unless kh = kw = taps = 5 and D is 64 or 128.  Replaces: branch.py:443-480
+ * (conv_features), runtime.py:311-348 (_feature_one), kernels.py:99-129. */
+int vdn_conv_features(const void* in, long long ld_in, const float* w_sp, int kh, int kw, const float* w_tm,
+                      int taps, int F, int gh, int gw, int H, int D, int l2norm, void* out, void* stream);
+
 /* alpha [F, H, D] = exp(-exp(A_log) * softplus(W_up mean_t(down) + dt_bias)), down being the
  * per-row x W_down^T columns.  Replaces: branch.py:483-491 (alpha_gate), :743-751. */
 int vdn_alpha_gate(const float* down, long long ld_down, int F, int T, int R, const float* w_up,

@@ -249,8 +249,8 @@ def test_conv_features_match_oracle():
     sp, kh, kw, tm, taps = bwt.conv["k"]
     s = pkg._lib.stream_handle(DEV)
     pkg._lib.call("vdn_spatial_conv", kd.data_ptr(), kd.stride(0), sp.data_ptr(), kh, kw, Fb, grid[0], grid[1],
-                  H * D, ws.conv_tmp.data_ptr(), ws.conv_tmp.stride(0), s)
-    pkg._lib.call("vdn_temporal_act", ws.conv_tmp.data_ptr(), ws.conv_tmp.stride(0), tm.data_ptr(), taps, Fb, tpf, H,
+                  H * D, ws.conv_buffer().data_ptr(), ws.conv_buffer().stride(0), s)
+    pkg._lib.call("vdn_temporal_act", ws.conv_buffer().data_ptr(), ws.conv_buffer().stride(0), tm.data_ptr(), taps, Fb, tpf, H,
                   D, 1, ws.kf.data_ptr(), s)
     qd = q.to(DEV)
     pkg._lib.call("vdn_temporal_act", qd.data_ptr(), qd.stride(0), None, 0, Fb, tpf, H, D, 1, ws.qf.data_ptr(), s)
@@ -488,3 +488,42 @@ def test_branch_readout_matches_oracle_with_and_without_text(D, grid, delta_rule
         msg = "; ".join(f"{k}={v:.3e}" for k, v in stages.items())
         assert rel_l2(got, want) < 2e-2, f"text={text} out={rel_l2(got, want):.3e} stages: {msg}"
         assert float(got[:tpf].abs().max()) == 0.0 and float(got[-tpf:].abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("F,grid,H,D,l2,pitch_mult", [
+    (29, (38, 22), 2, 128, True, 3),   # config-1 frame grid (one column block), k features
+    (7, (38, 22), 2, 128, False, 1),   # v features (no L2)
+    (5, (9, 48), 1, 128, True, 1),     # config-3 width: three column blocks
+    (3, (5, 7), 4, 64, True, 2),       # head_dim 64, bands and blocks smaller than a unit
+    (1, (3, 4), 2, 128, True, 1),      # a single frame: both temporal neighbours are padding
+])
+def test_fused_conv_features_equal_the_two_kernel_path(F, grid, H, D, l2, pitch_mult):
+    """vdn_conv_features (spatial 5x5 + temporal 5-tap + SiLU + L2 in one pass) against
+    vdn_spatial_conv followed by vdn_temporal_act on the same rows: the same arithmetic in the
+    same order, so equal up to the contraction of the L2 sum's multiply-adds."""
+    g = torch.Generator().manual_seed(F * 100 + D)
+    gh, gw = grid
+    tpf = gh * gw
+    rows, C = F * tpf, H * D
+    base = (torch.randn(rows, C * pitch_mult, generator=g) * 2).to(torch.bfloat16).to(DEV)
+    x = base[:, :C]
+    w_sp = (torch.randn(C, 25, generator=g) * 0.2).to(DEV)
+    w_tm = (torch.randn(C, 5, generator=g) * 0.45).to(DEV)
+    s = pkg._lib.stream_handle(DEV)
+    tmp = torch.empty(rows, C, device=DEV, dtype=torch.bfloat16)
+    two = torch.empty(F, H, tpf, D, device=DEV, dtype=torch.bfloat16)
+    one = torch.full((F, H, tpf, D), 7.0, device=DEV, dtype=torch.bfloat16)
+    pkg._lib.call("vdn_spatial_conv", x.data_ptr(), x.stride(0), w_sp.data_ptr(), 5, 5, F, gh, gw, C, tmp.data_ptr(),
+                  C, s)
+    pkg._lib.call("vdn_temporal_act", tmp.data_ptr(), C, w_tm.data_ptr(), 5, F, tpf, H, D, int(l2), two.data_ptr(), s)
+    pkg._lib.call("vdn_conv_features", x.data_ptr(), x.stride(0), w_sp.data_ptr(), 5, 5, w_tm.data_ptr(), 5, F, gh, gw,
+                  H, D, int(l2), one.data_ptr(), s)
+    torch.cuda.synchronize()
+    assert torch.isfinite(one.float()).all()
+    diff = (one.float() - two.float()).abs()
+    # every element within one bf16 step of the two-kernel path, nearly all of them equal
+    assert float((diff / two.float().abs().clamp_min(1e-3)).max()) <= 2 ** -7
+    assert float((diff > 0).float().mean()) < 1e-3
+    want = vo.conv_features(x.float().cpu().reshape(rows, H, D), w_sp.cpu().reshape(C, 1, 5, 5),
+                            w_tm.cpu().reshape(C, 1, 5), F, grid, l2)
+    assert rel_l2(one, want) < 1e-2
