@@ -314,7 +314,7 @@ def config_entry(args, c, world) -> dict:
     S = c["text"] + c["frames"] * c["grid"][0] * c["grid"][1]
     return {"workload": f"config{args.config}: {c['frames']}x{c['grid'][0] * c['grid'][1]}+{c['text']} tokens, "
                         f"H={H}, D={D}, hidden={hidden}", "tokens": S,
-            "parallelism": f"heads/{world}" if world > 1 else "none",
+            "parallelism": (f"heads/{world}, exchange {args.exchange}" if world > 1 else "none"),
             "l2": f"inputs larger than L2 (x {S * hidden * 2 / 1e6:.0f} MB, weights "
                   f"{(5 * H * D + 2 * H + 2 * D) * hidden * 2 / 1e9:.2f} GB)",
             "delta_rule": args.delta_rule, "rope": bool(args.rope), "precision": args.precision}
@@ -587,6 +587,9 @@ def main():
     ap.add_argument("--blocks", type=int, default=None, help="config 4: number of DiT blocks (default 50)")
     ap.add_argument("--delta-rule", choices=["vdn_solve", "sana_scaled"], default="vdn_solve",
                     help="configs 1/3: the branch's delta rule (BASELINE's released lineage is vdn_solve)")
+    ap.add_argument("--exchange", choices=["rows", "heads"], default="rows",
+                    help="N > 1: all-to-all by row block + row-split projection (rows) or all-gather of the "
+                         "per-head outputs + projection on every GPU (heads)")
     ap.add_argument("--precision", choices=["bf16", "int8", "fp8"], default="bf16",
                     help="configs 1/3: projection arithmetic (config 2 = config 1 with int8 or fp8)")
     ap.add_argument("--rope", action="store_true",
@@ -643,7 +646,7 @@ def main():
         # (no bf16 edge block: the benchmarked block is an interior one)
         maps = pkg.prepare_projection_maps([branch], dev, args.precision, skip_end_blocks=0)[0]
     state = pkg.B200State("bench", node_config(args.delta_rule), [branch], H, D, shard_heads=world > 1,
-                          projection_precision=args.precision, weight_maps=maps)
+                          projection_precision=args.precision, weight_maps=maps, shard_exchange=args.exchange)
     block = state.fused_block(attn, 0, dev)
     rope_freqs = rope_freqs_table(lay.seq_len, D, dev) if args.rope else None
     rope = pkg.rope_table(rope_freqs, lay.seq_len, D, dev)

@@ -21,8 +21,10 @@ On the device one block forward is four phases, all on the caller's stream:
    arithmetic) with an addend epilogue.
 
 With a ``HeadShard`` (one process per GPU, torch.distributed) phases 1-3 run on this
-rank's heads only and phase 4 becomes all-to-all by row block, the output projection on
-the rank's rows and an all-gather of the rows (shard.py).
+rank's heads only, the attention chunk by chunk of rows with each chunk's exchange queued
+behind it, and phase 4 becomes either all-to-all by row block, the output projection on
+the rank's rows and an all-gather of the rows, or an all-gather of the per-head outputs and
+the whole projection on every rank (shard.py).
 """
 
 from __future__ import annotations
@@ -37,7 +39,7 @@ from .branch import DELTA_RULES, BranchDeviceWeights, BranchWorkspace, cholesky_
 from .layout import VDNLayout, current_layout
 from .projection import (CONVROT_KEY, KIND, QuantizedMatrix, dequantize_projection_weight, quantize_rows_int8,
                          quantize_rows_int8_convrot, quantize_tensor_fp8, quantize_weight)
-from .shard import (HeadShard, RowExchange, concat_rows, default_shard, qkv_row_index, rank_major_out_weight,
+from .shard import (EXCHANGES, HeadShard, RowExchange, concat_rows, default_shard, qkv_row_index, rank_major_out_weight,
                     slice_branch_weights, split_heads_outputs)
 from .window import ATTENTION_BACKENDS, WindowPlanCache, launch_window_attention
 
@@ -209,7 +211,7 @@ class FusedBlock:
     def __init__(self, qkv_w, q_norm_w, k_norm_w, out_w, branch_w: Mapping, heads, dim, device, *,
                  precision="bf16", eps=1e-6, enable_gate=True, short_conv=("k", "v"), shard: HeadShard | None = None,
                  workspaces: dict | None = None, delta_rule="vdn_solve", bridge="alpha", enable_text_state=True,
-                 tile_frames=0):
+                 tile_frames=0, exchange="rows"):
         dev = torch.device(device)
         H_all, D = int(heads), int(dim)
         inner_all = H_all * D
@@ -241,6 +243,9 @@ class FusedBlock:
         self.bridge = bridge
         self.enable_text_state = bool(enable_text_state)
         self.tile_frames = tile_frames
+        if exchange not in EXCHANGES:
+            raise ValueError(f"unknown head-shard exchange {exchange!r}: one of {sorted(EXCHANGES)}")
+        self.exchange = exchange  # head-sharded only: "rows" (all-to-all, row-split projection) or "heads"
         qkv_rows = qkv_row_index(H_all, D, hs)
 
         def f32(t):
@@ -331,7 +336,7 @@ class FusedBlock:
         key = (S, None if layout is None else (layout.num_frames, layout.tokens_per_frame, layout.text_len,
                                                layout.anchor_frames),
                self.geo.heads, self.geo.dim, self.geo.hidden, self.precision, self.n_aux,
-               None if self.shard is None else (self.shard.rank, self.shard.world), self.bw is not None,
+               None if self.shard is None else (self.shard.rank, self.shard.world, self.exchange), self.bw is not None,
                self.tile_frames)
         ws = self._ws.get(key)
         if ws is None:
@@ -349,7 +354,7 @@ class FusedBlock:
                 # of another; the quantised projections need whole-tensor activation scales (fp8)
                 chunks = (EXCHANGE_CHUNKS if self.precision == "bf16" and S >= EXCHANGE_MIN_ROWS * EXCHANGE_CHUNKS *
                           self.shard.world else 1)
-                xchg = RowExchange(self.shard, S, 2 * g.inner, g.hidden, dev, chunks=chunks)
+                xchg = EXCHANGES[self.exchange](self.shard, S, 2 * g.inner, g.hidden, dev, chunks=chunks)
                 ws["xchg"] = xchg
                 ws["flat"] = xchg.send[:S, :g.inner]
                 ws["branch"] = xchg.send[:S, g.inner:]
@@ -495,14 +500,17 @@ class FusedBlock:
 
     def _out_sharded(self, ws, with_branch, status, stream, residual: GatedResidual | None = None,
                      row_epilogue=None) -> torch.Tensor:
-        """All-to-all of the per-head outputs by row block, the output projection on this
-        rank's rows (grouped-K over the receive buffer), ``row_epilogue(rows_view, row0,
-        n)`` on them (the DiT block's token-parallel MLP), all-gather of the rows."""
+        """The exchange of the per-head outputs and the output projection (grouped-K over the
+        receive buffer), ``row_epilogue(rows_view, row0, n)`` on the projected rows (the DiT
+        block's token-parallel MLP): all-to-all by row block, this rank's rows, all-gather of
+        the rows ("rows"); or all-gather of the per-head outputs and every row on every rank
+        ("heads")."""
         sh = self.shard
-        xchg: RowExchange = ws["xchg"]
-        xchg.exchange()
+        xchg = ws["xchg"]
+        xchg.exchange()  # the chunks the attention launches have not queued yet
         amax_reduce = None
-        if self.precision == "fp8":
+        if self.precision == "fp8" and isinstance(xchg, RowExchange):
+            # each rank quantises its row block: the per-tensor amax is the ranks' maximum
             import torch.distributed as dist
 
             def amax_reduce(t):
@@ -526,7 +534,8 @@ class FusedBlock:
         and the output leaves by row blocks (see :class:`StreamIO`).  ``rope``: rotary
         embedding of the normalised q / k (``rope_table``)."""
         ws, linear_active = self.forward_heads(x, layout, plans, status, linear_enabled=linear_enabled,
-                                               bridge=bridge, enable_text_state=enable_text_state, io=io, rope=rope)
+                                               bridge=bridge, enable_text_state=enable_text_state, io=io, rope=rope,
+                                               issue_exchange=self.shard is not None)
         stream = _lib.stream_handle(x.device)
         if self.shard is not None:
             full = self._out_sharded(ws, linear_active, status, stream, residual, row_epilogue)
@@ -548,10 +557,13 @@ class FusedBlock:
 
     def forward_heads(self, x: torch.Tensor, layout: VDNLayout, plans: WindowPlanCache, status: _lib.DeviceStatus,
                       *, linear_enabled=True, bridge=None, enable_text_state=None, io: StreamIO | None = None,
-                      rope: RopeTable | None = None):
+                      rope: RopeTable | None = None, issue_exchange=False):
         """Phases 1-3 (QKV, branch, window attention) for this rank's heads; returns the
         workspace holding the per-head outputs and whether the branch ran.  ``bridge`` /
-        ``enable_text_state``: None takes the block's own settings."""
+        ``enable_text_state``: None takes the block's own settings.  ``issue_exchange``
+        (head-sharded, several exchange chunks): the attention runs chunk by chunk of rows and
+        each chunk's exchange is queued as soon as its rows are written, so it crosses NVLink
+        while the next chunk is computed."""
         g = self.geo
         S = x.shape[0]
         bridge = self.bridge if bridge is None else bridge
@@ -607,17 +619,26 @@ class FusedBlock:
             # after the q / k RMSNorm of the QKV epilogue; the branch read the raw projections
             _lib.call("vdn_rope_split_half", qkn.data_ptr(), qkn.stride(0), S, 2 * g.heads, g.dim, rope.rot,
                       rope.freqs.data_ptr(), rope.ld, stream)
-        launch_window_attention(qkn[:, :g.inner], qkn[:, g.inner:], qkv[:, 2 * g.inner:], ws["flat"], plan, g.heads,
-                                g.dim, g.dim ** -0.5, status,
-                                gate_logits=ws["aux"] if self.enable_gate else None, gate_col0=self.col_gate,
-                                gate_bias=self.gate_bias)
         if self.shard is not None:
-            # the grouped operand of the row-split projection always spans the branch columns
+            # the grouped operand of the sharded projection always spans the branch columns
             if linear_active:
                 ws["branch_written"] = True
             elif ws["branch_written"]:
                 ws["branch"].zero_()
                 ws["branch_written"] = False
+        attend = dict(gate_logits=ws["aux"] if self.enable_gate else None, gate_col0=self.col_gate,
+                      gate_bias=self.gate_bias)
+        operands = (qkn[:, :g.inner], qkn[:, g.inner:], qkv[:, 2 * g.inner:], ws["flat"], plan, g.heads, g.dim,
+                    g.dim ** -0.5, status)
+        xchg = ws.get("xchg") if issue_exchange else None
+        if xchg is not None and xchg.chunks > 1:
+            ends = [xchg.chunk_rows(c)[1] for c in range(xchg.chunks)]
+            for c, items in enumerate(plan.device_chunk_items(x.device, g.heads, ends)):
+                if items.numel():
+                    launch_window_attention(*operands, items=items, **attend)
+                xchg.exchange_chunk(c)
+        else:
+            launch_window_attention(*operands, **attend)
         return ws, linear_active
 
 
@@ -628,11 +649,14 @@ class B200State:
 
     ``shard_heads``: False (one GPU per block), True (shard the heads over the default
     torch.distributed group, one process per GPU) or a process group to shard over.
-    Every rank then runs the patched forward on the same x and gets the full output."""
+    Every rank then runs the patched forward on the same x and gets the full output.
+    ``shard_exchange``: "rows" (all-to-all of the per-head outputs by row block, each rank
+    projects its rows, all-gather of the projected rows) or "heads" (all-gather of the
+    per-head outputs, every rank projects every row)."""
 
     def __init__(self, name, config: Mapping, branches, num_heads, head_dim, *, attention_backend="b200",
                  projection_precision="bf16", inference=True, weight_maps=None, shard_heads=False, tile_frames=0,
-                 **_ignored):
+                 shard_exchange="rows", **_ignored):
         if attention_backend not in ATTENTION_BACKENDS:
             raise ValueError(f"unsupported attention backend {attention_backend!r}")
         if projection_precision not in ("bf16", "fp8", "int8"):
@@ -647,6 +671,7 @@ class B200State:
         if isinstance(tile_frames, bool) or not isinstance(tile_frames, int) or tile_frames < 0:
             raise ValueError("tile_frames must be a non-negative integer")  # nodes.py:247-248
         self.tile_frames = tile_frames  # the runtime's frame tiling (hybrid.py:51), for branches without their own
+        self.shard_exchange = shard_exchange  # "rows" or "heads" (shard.EXCHANGES)
         maps = list(weight_maps) if weight_maps is not None else [
             b if isinstance(b, Mapping) else getattr(b, "w") for b in branches]
         self.branches = list(branches)
@@ -681,7 +706,7 @@ class B200State:
                             device, precision=self.projection_precision, eps=float(getattr(attn.q_norm, "eps", 1e-6)),
                             enable_gate=bool(cfg.get("enable_softmax_gate", True)), shard=self.shard,
                             workspaces=self.workspaces, tile_frames=int(self.tile_frames if tile is None else tile),
-                            **setting)
+                            exchange=self.shard_exchange, **setting)
             self.blocks[index] = fb
         return fb
 

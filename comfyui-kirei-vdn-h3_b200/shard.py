@@ -155,13 +155,29 @@ class RowExchange:
         r0 = (chunk * self.shard.world + r) * self.cs
         return r0, max(0, min(self.cs, self.seq_len - r0))
 
-    def exchange(self):
-        """Queue the all-to-all of every chunk (asynchronous; each is waited on before use)."""
+    def chunk_rows(self, chunk: int) -> tuple[int, int]:
+        """[first, end) rows of ``chunk`` over all ranks (end clipped to the sequence)."""
+        g, cs = self.shard.world, self.cs
+        return chunk * g * cs, min(self.seq_len, (chunk + 1) * g * cs)
+
+    def exchange_chunk(self, chunk: int):
+        """Queue the all-to-all of one chunk (asynchronous; the collective waits for the work
+        queued on the current stream so far, so it can start while later chunks are computed)."""
         import torch.distributed as dist
 
         g, cs = self.shard.world, self.cs
-        self._works = [dist.all_to_all_single(self.recv[c].view(g * cs, -1), self.send[c * g * cs:(c + 1) * g * cs],
-                                              group=self.shard.group, async_op=True) for c in range(self.chunks)]
+        c = chunk
+        if c != len(self._works):
+            raise RuntimeError("exchange chunks must be queued in order")
+        self._works.append(dist.all_to_all_single(self.recv[c].view(g * cs, -1),
+                                                  self.send[c * g * cs:(c + 1) * g * cs], group=self.shard.group,
+                                                  async_op=True))
+
+    def exchange(self):
+        """Queue the all-to-all of every chunk not queued yet (asynchronous; each is waited on
+        before use)."""
+        for c in range(len(self._works), self.chunks):
+            self.exchange_chunk(c)
 
     def project_and_gather(self, project, out: torch.Tensor | None = None) -> torch.Tensor:
         """Run ``project(recv[c], rows, out_rows, row0)`` on this rank's block of every chunk and
@@ -174,8 +190,7 @@ class RowExchange:
         total = g * self.chunks * cs
         if out is None or out.shape != (total, self.hidden):
             out = torch.empty(total, self.hidden, device=self.send.device, dtype=self.send.dtype)
-        if not self._works:
-            self.exchange()
+        self.exchange()
         gathers = []
         for c in range(self.chunks):
             self._works[c].wait()  # the compute stream waits for this chunk's exchange
@@ -188,6 +203,72 @@ class RowExchange:
             w.wait()
         self._works = []
         return out[:self.seq_len]
+
+
+class HeadGather:
+    """The exchange the north star describes: every rank all-gathers the per-head outputs
+    [S, 2*H/g*D] of every rank, chunk by chunk of rows, and projects all S rows itself (the
+    output projection replicated on every rank, so no gather of projected rows follows).
+    Same interface as ``RowExchange``: ``send`` holds this rank's per-head outputs in natural
+    row order, ``recv[c]`` is chunk c as [g][cs][width] (rank-major K, the grouped-K GEMM's
+    operand), and ``project_and_gather(project)`` returns the [S, hidden] output.
+
+    Per rank it receives (g-1)/g * S * 2*H*D values and projects S rows; the row split
+    receives (g-1)/g^2 of that plus the projected rows' all-gather, and projects S/g rows."""
+
+    def __init__(self, shard: HeadShard, seq_len: int, width: int, hidden: int, device, dtype=torch.bfloat16,
+                 chunks: int = 1):
+        self.shard = shard
+        self.seq_len = int(seq_len)
+        g = shard.world
+        self.chunks = max(1, int(chunks))
+        self.cs = -(-self.seq_len // self.chunks)
+        self.send = torch.zeros(self.chunks * self.cs, width, device=device, dtype=dtype)
+        self.recv = torch.empty(self.chunks, g, self.cs, width, device=device, dtype=dtype)
+        self.hidden = int(hidden)
+        self._works = []
+
+    def rows_of(self, chunk: int, rank: int | None = None) -> tuple[int, int]:
+        """(first row, row count) this rank projects in ``chunk``: all of the chunk's rows."""
+        r0 = chunk * self.cs
+        return r0, max(0, min(self.cs, self.seq_len - r0))
+
+    def chunk_rows(self, chunk: int) -> tuple[int, int]:
+        r0 = chunk * self.cs
+        return r0, min(self.seq_len, r0 + self.cs)
+
+    def exchange_chunk(self, chunk: int):
+        """Queue the all-gather of one chunk (asynchronous, ordered after the work queued on the
+        current stream so far)."""
+        import torch.distributed as dist
+
+        g, cs = self.shard.world, self.cs
+        c = chunk
+        if c != len(self._works):
+            raise RuntimeError("exchange chunks must be queued in order")
+        self._works.append(dist.all_gather_into_tensor(self.recv[c].view(g * cs, -1), self.send[c * cs:(c + 1) * cs],
+                                                       group=self.shard.group, async_op=True))
+
+    def exchange(self):
+        for c in range(len(self._works), self.chunks):
+            self.exchange_chunk(c)
+
+    def project_and_gather(self, project, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Run ``project(recv[c], rows, out_rows, row0)`` on every chunk (every rank projects
+        every row); returns the [S, hidden] output."""
+        total = self.chunks * self.cs
+        if out is None or out.shape != (total, self.hidden):
+            out = torch.empty(total, self.hidden, device=self.send.device, dtype=self.send.dtype)
+        self.exchange()
+        for c in range(self.chunks):
+            self._works[c].wait()
+            r0, n = self.rows_of(c)
+            project(self.recv[c], n, out[r0:r0 + self.cs], r0)
+        self._works = []
+        return out[:self.seq_len]
+
+
+EXCHANGES = {"rows": RowExchange, "heads": HeadGather}
 
 
 def concat_rows(recv: torch.Tensor, rows: int) -> torch.Tensor:
@@ -218,5 +299,5 @@ def default_shard(heads: int, group=None) -> HeadShard | None:
     return HeadShard(dist.get_rank(group), world, int(heads), group)
 
 
-__all__ = ["HeadShard", "RowExchange", "concat_rows", "default_shard", "qkv_row_index", "rank_major_out_weight",
-           "slice_branch_weights", "split_heads_outputs"]
+__all__ = ["EXCHANGES", "HeadGather", "HeadShard", "RowExchange", "concat_rows", "default_shard", "qkv_row_index",
+           "rank_major_out_weight", "slice_branch_weights", "split_heads_outputs"]

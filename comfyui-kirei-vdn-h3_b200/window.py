@@ -100,6 +100,18 @@ class WindowPlan:
         rest = [(h << 20) | q for h in hs for q in order if not long_q[q]]
         return np.asarray(first + rest, dtype=np.int64).astype(np.int32)
 
+    def chunk_items(self, heads: int, ends) -> list[np.ndarray]:
+        """``items(heads)`` split into consecutive row chunks ending at ``ends`` (ascending,
+        the last one the sequence length), keeping the claim order inside each: a query tile
+        goes with the chunk of its first row, so once the launches of chunks 0..c are done
+        every row before ``ends[c]`` is final (a tile reaching into a later chunk only
+        finishes those rows early)."""
+        first_row = np.array([min(r0 for r0, _ in self.q_halves(q)) for q in range(self.n_qtiles)], dtype=np.int64)
+        chunk_of = np.searchsorted(np.asarray(ends, dtype=np.int64), first_row, side="right")
+        items = self.items(heads)
+        owner = chunk_of[items & 0xFFFFF]
+        return [items[owner == c] for c in range(len(ends))]
+
     def key_tiles_total(self, heads: int) -> int:
         return int(self.tiles_per_q.sum()) * heads
 
@@ -118,6 +130,15 @@ class WindowPlan:
                 "items": torch.from_numpy(self.items(heads)).to(dev),
             }
         return self._device[key]
+
+    def device_chunk_items(self, device, heads: int, ends) -> list[torch.Tensor]:
+        """``chunk_items`` on the device (cached per chunk boundaries)."""
+        d = self.device_arrays(device, heads)
+        key = ("chunks", tuple(int(e) for e in ends))
+        if key not in d:
+            d[key] = [torch.from_numpy(np.ascontiguousarray(it)).to(torch.device(device))
+                      for it in self.chunk_items(heads, ends)]
+        return d[key]
 
 
 HALF = BQ // 2  # rows per MMA half of a work item
@@ -280,16 +301,19 @@ def _rows_view(t: torch.Tensor, heads: int, dim: int) -> int:
 
 
 def launch_window_attention(q, k, v, out, plan: WindowPlan, heads, dim, scale, status: _lib.DeviceStatus,
-                            gate_logits=None, gate_col0=0, gate_bias=None):
-    """Launch the kernel on the current stream (no validation beyond the C-ABI's)."""
+                            gate_logits=None, gate_col0=0, gate_bias=None, items: torch.Tensor | None = None):
+    """Launch the kernel on the current stream (no validation beyond the C-ABI's).
+    ``items``: a device subset of the work items (one row chunk, ``device_chunk_items``)."""
     d = plan.device_arrays(q.device, heads)
-    n_items = heads * plan.n_qtiles
+    if items is None:
+        items = d["items"]
+    n_items = int(items.numel())
     _lib.call(
         "vdn_window_attention",
         q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
         plan.seq_len, heads, dim, plan.video_start, plan.video_end, plan.num_frames, plan.tokens_per_frame,
         int(plan.anchor_rows), int(plan.anchor_cols), float(scale),
-        d["frame_lo"].data_ptr(), d["frame_hi"].data_ptr(), d["items"].data_ptr(), n_items,
+        d["frame_lo"].data_ptr(), d["frame_hi"].data_ptr(), items.data_ptr(), n_items,
         d["tile_off"].data_ptr(), d["qtile"].data_ptr(), d["ktile"].data_ptr(), out.data_ptr(), out.stride(0),
         _lib.ptr(gate_logits), gate_logits.stride(0) if gate_logits is not None else 0, int(gate_col0),
         _lib.ptr(gate_bias), status.counter_ptr, status.err_ptr, _lib.stream_handle(q.device),

@@ -34,33 +34,42 @@ def rel_l2(got, want):
     return float((got - want).norm() / want.norm())
 
 
-def _block(bw, heads, dim, precision, shard=None):
+def _block(bw, heads, dim, precision, shard=None, exchange="rows"):
     return pkg.FusedBlock(bw.qkv, bw.q_norm, bw.k_norm, bw.out, bw.branch, heads, dim, DEV, precision=precision,
-                          shard=shard)
+                          shard=shard, exchange=exchange)
 
 
-def _emulated_sharded_forward(bw, lay, heads, dim, x, precision, world):
+def _emulated_sharded_forward(bw, lay, heads, dim, x, precision, world, exchange="rows"):
+    """Every rank's phases 1-3, then the chunked exchange replayed by copies between the
+    ranks' buffers and each rank's projection; returns rank 0's rows for "rows" (every rank
+    writes its own row blocks into one output) or, for "heads", checks that all ranks project
+    the same output and returns it."""
     plans = pkg.WindowPlanCache()
     status = pkg.DeviceStatus(DEV)
     stream = torch.cuda.current_stream().cuda_stream
-    blocks = [_block(bw, heads, dim, precision, sh.HeadShard(r, world, heads)) for r in range(world)]
+    blocks = [_block(bw, heads, dim, precision, sh.HeadShard(r, world, heads), exchange) for r in range(world)]
     parts = [b.forward_heads(x, lay, plans, status) for b in blocks]
     S = x.shape[0]
     x0 = parts[0][0]["xchg"]
     cs = x0.cs
-    out = torch.zeros(world * x0.chunks * cs, bw.out.shape[0], device=DEV, dtype=torch.bfloat16)
-    # replay the chunked all-to-all: rank r's block of chunk c is rows (c * world + r) * cs
+    rows_total = x0.send.shape[0]
+    outs = [torch.zeros(rows_total, bw.out.shape[0], device=DEV, dtype=torch.bfloat16)
+            for _ in range(world if exchange == "heads" else 1)]
     for r, b in enumerate(blocks):
         ws, linear_active = parts[r]
         xr = ws["xchg"]
+        out = outs[r if exchange == "heads" else 0]
         for c in range(xr.chunks):
             r0, rows = xr.rows_of(c)
             for src in range(world):
+                # "rows": rank r's block of chunk c from every rank; "heads": chunk c of every rank
                 xr.recv[c][src].copy_(parts[src][0]["xchg"].send[r0:r0 + cs])
             b.project_rows(ws, linear_active, xr.recv[c], rows, out[r0:r0 + cs], status, stream)
     torch.cuda.synchronize()
     status.raise_if_failed()
-    return out[:S]
+    for other in outs[1:]:
+        assert torch.equal(other[:S], outs[0][:S])
+    return outs[0][:S]
 
 
 GEOMETRIES = {
@@ -69,9 +78,10 @@ GEOMETRIES = {
 }
 
 
+@pytest.mark.parametrize("exchange", ["rows", "heads"])
 @pytest.mark.parametrize("precision", ["bf16", "int8"])
 @pytest.mark.parametrize("geom", sorted(GEOMETRIES))
-def test_sharded_block_emulated_on_one_gpu(geom, precision, monkeypatch):
+def test_sharded_block_emulated_on_one_gpu(geom, precision, exchange, monkeypatch):
     monkeypatch.setattr(pkg.hybrid, "EXCHANGE_MIN_ROWS", 1)  # chunked exchange even at test sizes
     c, worlds = GEOMETRIES[geom]
     H, D, hidden = c["heads"], c["dim"], c["hidden"]
@@ -82,7 +92,7 @@ def test_sharded_block_emulated_on_one_gpu(geom, precision, monkeypatch):
     ref = full.forward(x, lay, pkg.WindowPlanCache(), pkg.DeviceStatus(DEV)).clone()
     torch.cuda.synchronize()
     for world in worlds:
-        got = _emulated_sharded_forward(bw, lay, H, D, x, precision, world)
+        got = _emulated_sharded_forward(bw, lay, H, D, x, precision, world, exchange)
         if precision == "int8":
             assert torch.equal(got, ref), f"world {world}: int8 sharded output differs from the unsharded block"
         else:
@@ -125,9 +135,9 @@ def _nccl_worker(rank, world, port, q):
         lay = pkg_r.make_layout(c["text"], c["frames"], c["grid"])
         x = vo.make_x(6, lay.seq_len, hidden).to(f"cuda:{rank}", torch.bfloat16)
         res = {}
-        for precision in ("bf16", "int8", "fp8"):
+        for exchange, precision in [(e, p) for e in ("rows", "heads") for p in ("bf16", "int8", "fp8")]:
             state = pkg_r.B200State("t", vo.BranchConfig().node_config(), [bw.branch], H, D,
-                                    projection_precision=precision, shard_heads=True)
+                                    projection_precision=precision, shard_heads=True, shard_exchange=exchange)
             fwd = pkg_r.make_vdn_forward(_Attn(bw, H, D), state, 0)
             with pkg_r.publish_layout(lay):
                 got = pkg_r.run_forward_checked(state, fwd, x)
@@ -137,10 +147,10 @@ def _nccl_worker(rank, world, port, q):
             with pkg_r.publish_layout(lay):
                 ref = pkg_r.run_forward_checked(single, fwd1, x)
             torch.cuda.synchronize()
-            res[precision] = (bool(torch.equal(got, ref)), rel_l2(got, ref))
+            res[(exchange, precision)] = (bool(torch.equal(got, ref)), rel_l2(got, ref))
             if precision == "bf16":
                 want = vo.block_forward(x.float().cpu(), bw, vo.config_layout(c), H, D, vo.BranchConfig())
-                res["oracle"] = rel_l2(got, want)
+                res[(exchange, "oracle")] = rel_l2(got, want)
         # the DiT block around it: MLP token-parallel on each rank's rows before the gather
         dw = vo.make_dit(8, hidden, H, D, 512, activation="swiglu")
         mods = [m.to(f"cuda:{rank}", torch.bfloat16) for m in vo.make_mods(8, 2, hidden)]
@@ -179,9 +189,12 @@ def test_sharded_block_on_two_gpus_over_nccl():
         p.join(timeout=120)
         assert p.exitcode == 0
     for rank, res in results.items():
-        assert res["int8"][0], (rank, res)
-        assert res["fp8"][0], (rank, res)  # the amax all-reduce restores the whole tensor's scale
-        assert res["bf16"][1] < 2e-3, (rank, res)
-        assert res["oracle"] < 2e-2, (rank, res)
+        for exchange in ("rows", "heads"):
+            assert res[(exchange, "int8")][0], (rank, exchange, res)
+            # fp8: the row split's amax all-reduce restores the whole tensor's scale; the head
+            # gather quantises every row on every rank
+            assert res[(exchange, "fp8")][0], (rank, exchange, res)
+            assert res[(exchange, "bf16")][1] < 2e-3, (rank, exchange, res)
+            assert res[(exchange, "oracle")] < 2e-2, (rank, exchange, res)
         assert res["dit_int8"][0], (rank, res)
         assert res["dit_bf16"][1] < 2e-3, (rank, res)

@@ -438,3 +438,25 @@ def test_to_out_follows_the_stored_representation():
     assert fb.to_out_kind == "bf16" and fb.concat_out
     fb8 = _fused_block_for({}, None, maps=[w], projection_precision="bf16")
     assert fb8.w_to_b16 is None  # folded into the K-concat weight
+
+
+@pytest.mark.parametrize("n_chunks", [1, 3, 4, 9])
+def test_chunk_items_finish_every_row_before_its_chunk_ends(n_chunks):
+    """The head-sharded block launches the attention chunk by chunk of rows and queues each
+    chunk's exchange behind it: every item runs exactly once, and after the launches of
+    chunks 0..c every row before chunk c's end has been computed by them."""
+    lay = vo.config_layout(vo.CONFIG1)
+    plan = bw.build_window_plan(lay.seq_len, lay.video_start, lay.video_end, lay.num_frames,
+                                lay.tokens_per_frame, list(lay.bounds), lay.anchor_frames)
+    S, heads = lay.seq_len, 3
+    step = -(-S // n_chunks)
+    ends = [min(S, (c + 1) * step) for c in range(n_chunks)]
+    chunks = plan.chunk_items(heads, ends)
+    flat = np.concatenate(chunks)
+    assert sorted(flat.tolist()) == sorted(plan.items(heads).tolist())
+    done = np.zeros(S, dtype=bool)
+    for c, its in enumerate(chunks):
+        for code in its.tolist():
+            for r0, n in plan.q_halves(code & 0xFFFFF):
+                done[r0:r0 + n] = True
+        assert done[:ends[c]].all()

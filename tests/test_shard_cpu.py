@@ -47,6 +47,19 @@ def test_exchange_blocks_tile_the_sequence(S, world, chunks):
     assert x.send.shape[0] == world * chunks * x.cs >= S
 
 
+@pytest.mark.parametrize("S", [1, 7, 64, 26428])
+@pytest.mark.parametrize("world,chunks", [(2, 1), (2, 4), (8, 3)])
+def test_head_gather_chunks_tile_the_sequence(S, world, chunks):
+    x = sh.HeadGather(sh.HeadShard(0, world, 24), S, 8, 4, "cpu", dtype=torch.float32, chunks=chunks)
+    covered = []
+    for c in range(chunks):
+        r0, n = x.rows_of(c, 1)
+        assert (r0, r0 + n) == (x.chunk_rows(c)[0], max(x.chunk_rows(c)))
+        covered += list(range(r0, r0 + n))
+    assert covered == list(range(S))
+    assert x.recv.shape == (chunks, world, x.cs, 8)
+
+
 def test_head_shard_rejects_uneven_split():
     with pytest.raises(ValueError):
         sh.HeadShard(0, 3, 40)
@@ -120,7 +133,7 @@ def _heads_outputs(x, bw: vo.BlockWeights, lay, heads, dim, shard: sh.HeadShard,
     return torch.cat([flat, branch], 1)
 
 
-def _worker(rank, world, port, anchors, chunks, q):
+def _worker(rank, world, port, anchors, chunks, q, kind="rows"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -133,8 +146,8 @@ def _worker(rank, world, port, anchors, chunks, q):
         bcfg = vo.BranchConfig()
         shard = sh.default_shard(H)
         assert shard.rank == rank and shard.world == world
-        xchg = sh.RowExchange(shard, lay.seq_len, 2 * shard.heads_local * D, hidden, "cpu", dtype=torch.float64,
-                              chunks=chunks)
+        xchg = sh.EXCHANGES[kind](shard, lay.seq_len, 2 * shard.heads_local * D, hidden, "cpu",
+                                  dtype=torch.float64, chunks=chunks)
         xchg.send[:lay.seq_len] = _heads_outputs(x, bw, lay, H, D, shard, bcfg)
         xchg.exchange()
         w_rm = sh.rank_major_out_weight(bw.out.double(), bw.branch["to_out_linear.weight"].double(), H, D, world)
@@ -151,12 +164,15 @@ def _worker(rank, world, port, anchors, chunks, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,anchors,chunks", [(2, "both", 3), (4, "none", 1)])
-def test_sharded_block_matches_unsharded_oracle_on_gloo_ranks(world, anchors, chunks):
+@pytest.mark.parametrize("world,anchors,chunks,kind", [(2, "both", 3, "rows"), (4, "none", 1, "rows"),
+                                                       (2, "both", 2, "heads"), (4, "none", 3, "heads")])
+def test_sharded_block_matches_unsharded_oracle_on_gloo_ranks(world, anchors, chunks, kind):
+    """Both exchanges: all-to-all by row block + row-split projection + all-gather of the rows,
+    and all-gather of the per-head outputs + the whole projection on every rank."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, anchors, chunks, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, anchors, chunks, q, kind)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in procs]
