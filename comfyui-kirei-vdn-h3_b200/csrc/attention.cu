@@ -44,7 +44,6 @@ constexpr int kThreads = 384;  // 8 softmax warps, 1 TMA warp, 1 MMA warp, 2 war
 // 256 x 208 + 128 x 80 = 63,488 <= 384 x 168 = 64,512.
 constexpr int kRegsSoftmax = 208;
 constexpr int kRegsIssue = 80;  // warps 8-11: the TMA and MMA warps and two idle warps
-constexpr int kRegsLaunch = 168;
 
 template <int N>
 __device__ __forceinline__ void reg_inc() {
@@ -310,11 +309,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sV = smem_u32(smem + L::kOffV);
   constexpr int kDBlocks = D / 64;  // 64-element (128 B) column blocks per row
 
-  // Register reallocation, one setmaxnreg instruction per warpgroup and direction: warps 8-11
-  // (TMA, MMA and two idle warps) give registers up at the start and take the launch's
-  // count back at the end; the softmax warpgroups take more and give it back.  Decreases
-  // never wait; an increase waits until enough registers are free, which the decreases that
-  // precede it (in program order of the other warpgroup) always make true.
+  // Register reallocation, one setmaxnreg instruction per warpgroup: warps 8-11 (TMA, MMA
+  // and two idle warps) give registers up at the start, the softmax warpgroups take them.
+  // Nothing is given back before the CTA exits: an increase waits until the CTA's pool holds
+  // enough registers, and a warp that took back its share early could keep the softmax
+  // warps' increase waiting for good.
   if (warp >= 8) {
     reg_dec<kRegsIssue>();
     if (warp == 8) {
@@ -445,8 +444,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    __syncwarp();
-    reg_inc<kRegsLaunch>();
   } else {
     reg_inc<kRegsSoftmax>();
     // ---------------- softmax / correction / epilogue: warpgroup a = warp / 4 ----------------
@@ -612,11 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    __syncwarp();
-    reg_dec<kRegsLaunch>();
   }
-  // every warp is back at the launch's count here (the decreases above never wait; an
-  // increase waits until the softmax warps have given their share back)
 
   tc_fence_before();
   __syncthreads();
