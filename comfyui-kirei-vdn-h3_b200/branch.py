@@ -254,7 +254,11 @@ class BranchWorkspace:
 
 
 TILE_HALO = 2  # frames each side: the 5-tap temporal conv's reach (runtime.py:428-430)
-FUSED_CONV = True  # short conv features in one kernel where its geometry allows
+# Short conv features in one kernel (vdn_conv_features) where its geometry allows.  Off: on
+# the config-1 clip (38 x 22 frames, H = 40) the fused kernel, bound by its one-frame-deep
+# prefetch and one 256-thread CTA per SM, measured 1.78 ms per forward for k and v against
+# 1.03 ms for the spatial + temporal pair, which stream at a higher fraction of HBM bandwidth.
+FUSED_CONV = False
 
 
 def fused_conv_ok(src: torch.Tensor, kh: int, kw: int, taps: int, dim: int) -> bool:

@@ -14,9 +14,14 @@
 //     row cannot see every key carry a mask flag, and the mask is then rebuilt per element
 //     from the frame index (never materialised);
 //   * the 256 query rows are two 128-row tiles (a = 0, 1) that share every K/V tile: warp 8
-//     streams Q and a 2-stage K/V ring with TMA, warp 9 issues all tcgen05 MMAs, and two
-//     softmax warpgroups (warps 0-3 for a = 0, 4-7 for a = 1) ping-pong against it; warps
-//     8-11 hand registers to the softmax warpgroups at start-up (setmaxnreg: 80 and 208);
+//     streams Q and a 2-stage K/V ring with TMA, warp 9 issues all tcgen05 MMAs (the whole
+//     warp runs the issue loop, one elected lane issues), and two softmax warpgroups (warps
+//     0-3 for a = 0, 4-7 for a = 1) ping-pong against it; warps 8-11 hand registers to the
+//     softmax warpgroups at start-up (setmaxnreg: 80 and 208);
+//   * the score MMAs read Q and K from shared memory (8 KB per 64-cycle M128 N128 K16
+//     product), the PV MMAs read V (4 KB), and TMA writes 64 KB per K/V tile: 256 KB of
+//     shared-memory traffic per 2048 tensor cycles, the shared-memory port's full rate, so
+//     the tensor pipe and every barrier operation wait on shared memory when both run;
 //   * TMEM (512 columns): S_a in columns [128a, 128a+128), O_a in [256+128a, 384+128a).  The
 //     softmax writes P_a as packed bf16 over the first 64 columns of S_a and the PV MMA reads
 //     it straight from TMEM (A operand in tensor memory), so shared memory holds only Q and
@@ -207,15 +212,21 @@ __host__ __device__ constexpr uint32_t sdesc_hi_sw128(uint32_t sbo) {
   return ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);  // version 1 (bit 46), 128-byte swizzle (bits 61-63)
 }
 
+// The MMA warp runs its loop with all 32 lanes (every operand is warp-uniform) and each
+// tcgen05.mma / commit below is issued by the lane elect.sync picks: the lowest lane of the
+// converged warp, the same thread every time, as a commit must come from the thread that
+// issued the MMAs it tracks.  An issue loop confined to one lane by a branch runs at about
+// a third of the rate of the 64-cycle M128 N128 K16 products.
 // S = Q K^T, both operands from shared memory.
 __device__ __forceinline__ void mma_ss(uint32_t d, uint32_t a_lo, uint32_t b_lo, uint32_t hi, uint32_t idesc,
                                        uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 rx;\n\t.reg .b64 da, db;\n\t"
+      "elect.sync rx|e, 0xffffffff;\n\t"
       "setp.ne.b32 p, %5, 0;\n\t"
       "mov.b64 da, {%1, %3};\n\t"
       "mov.b64 db, {%2, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, p;\n\t}" ::"r"(d),
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, p;\n\t}" ::"r"(d),
       "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -224,12 +235,29 @@ __device__ __forceinline__ void mma_ss(uint32_t d, uint32_t a_lo, uint32_t b_lo,
 __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi, uint32_t idesc,
                                        uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 rx;\n\t.reg .b64 db;\n\t"
+      "elect.sync rx|e, 0xffffffff;\n\t"
       "setp.ne.b32 p, %5, 0;\n\t"
       "mov.b64 db, {%2, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d),
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d),
       "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// tcgen05.commit from the elected lane (the one that issued the MMAs).
+__device__ __forceinline__ void commit_elect(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 rx;\n\t"
+      "elect.sync rx|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+      : "memory");
+}
+
+// A bounded wait by every lane of a warp; the lanes agree on the outcome, so the warp stays
+// converged for the elected issues that follow (a lane that gave up makes all of them stop).
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err, int code) {
+  const bool r = mbar_wait_inl(bar, parity, abort_flag, err, code);
+  return __all_sync(0xffffffffu, r);
 }
 
 template <int D>
@@ -363,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else if (warp == 9) {
-      if (lane == 0) {
+      {
         // ---------------- MMA issuer ----------------
         constexpr uint32_t idesc_s = make_idesc(1, 1, 1, 0, 0, BQ, BKV);
         constexpr uint32_t idesc_o = make_idesc(1, 1, 1, 0, 1, BQ, D);
@@ -376,36 +404,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t off = ((s >> 2) * (BQ * 128) + (s & 3) * 32) >> 4;
             mma_ss(tmem_base + a * 128, qa + off, kb + off, hi_k, idesc_s, s > 0 ? 1u : 0u);
           }
-          tc_commit(B(B_SFULL0 + a));
+          commit_elect(B(B_SFULL0 + a));
         };
         int g = 0;
         int it = 0;
         bool ok = true;
         for (; ok; ++it) {
           const int slot = it % kItemRing;
-          if (!mbar_wait_inl(B(B_IFULL0 + slot), (it / kItemRing) & 1, abort_flag, err, kErrWaitMma)) break;
+          if (!warp_wait(B(B_IFULL0 + slot), (it / kItemRing) & 1, abort_flag, err, kErrWaitMma)) break;
           const int code = item_ring[slot];
-          mbar_arrive(B(B_IEMPTY0 + slot));
+          if (lane == 0) mbar_arrive(B(B_IEMPTY0 + slot));
           if (code < 0) break;
           const int qt = code & 0xFFFFF;
           const int n = p.tile_off[qt + 1] - p.tile_off[qt];
-          if (!mbar_wait_inl(B(B_QFULL), it & 1, abort_flag, err, kErrWaitMma) ||
-              !mbar_wait_inl(B(B_KFULL0 + (g & 1)), (g >> 1) & 1, abort_flag, err, kErrWaitMma)) {
+          if (!warp_wait(B(B_QFULL), it & 1, abort_flag, err, kErrWaitMma) ||
+              !warp_wait(B(B_KFULL0 + (g & 1)), (g >> 1) & 1, abort_flag, err, kErrWaitMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
           issue_s(0, g & 1);
           issue_s(1, g & 1);
-          tc_commit(B(B_KEMPTY0 + (g & 1)));
-          if (n == 1) tc_commit(B(B_QEMPTY));
+          commit_elect(B(B_KEMPTY0 + (g & 1)));
+          if (n == 1) commit_elect(B(B_QEMPTY));
           for (int j = 0; j < n && ok; ++j) {
             const int gj = g + j, st = gj & 1;
             const uint32_t ph = (gj >> 1) & 1;
             for (int a = 0; a < 2; ++a) {
-              if (!mbar_wait_inl(B(B_PLO0 + a), gj & 1, abort_flag, err, kErrWaitMma) ||
-                  (j == 0 && !mbar_wait_inl(B(B_OFREE0 + a), (it & 1) ^ 1, abort_flag, err, kErrWaitMma)) ||
-                  (a == 0 && !mbar_wait_inl(B(B_VFULL0 + st), ph, abort_flag, err, kErrWaitMma))) {
+              if (!warp_wait(B(B_PLO0 + a), gj & 1, abort_flag, err, kErrWaitMma) ||
+                  (j == 0 && !warp_wait(B(B_OFREE0 + a), (it & 1) ^ 1, abort_flag, err, kErrWaitMma)) ||
+                  (a == 0 && !warp_wait(B(B_VFULL0 + st), ph, abort_flag, err, kErrWaitMma))) {
                 ok = false;
                 break;
               }
@@ -415,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int s = 0; s < kPSplit / 16; ++s)
                 mma_ts(tmem_base + 256 + a * 128, tmem_base + a * 128 + s * 8, vb + s * (2048 >> 4), hi_k, idesc_o,
                        (j > 0 || s > 0) ? 1u : 0u);
-              if (!mbar_wait_inl(B(B_PHI0 + a), gj & 1, abort_flag, err, kErrWaitMma)) {
+              if (!warp_wait(B(B_PHI0 + a), gj & 1, abort_flag, err, kErrWaitMma)) {
                 ok = false;
                 break;
               }
@@ -423,19 +451,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   #pragma unroll
               for (int s = kPSplit / 16; s < BKV / 16; ++s)
                 mma_ts(tmem_base + 256 + a * 128, tmem_base + a * 128 + s * 8, vb + s * (2048 >> 4), hi_k, idesc_o, 1u);
-              if (a == 1) tc_commit(B(B_VEMPTY0 + st));
-              if (j == n - 1) tc_commit(B(B_ODONE0 + a));
+              if (a == 1) commit_elect(B(B_VEMPTY0 + st));
+              if (j == n - 1) commit_elect(B(B_ODONE0 + a));
               if (j + 1 < n) {
                 const int g1 = gj + 1, st1 = g1 & 1;
-                if (a == 0 && !mbar_wait_inl(B(B_KFULL0 + st1), (g1 >> 1) & 1, abort_flag, err, kErrWaitMma)) {
+                if (a == 0 && !warp_wait(B(B_KFULL0 + st1), (g1 >> 1) & 1, abort_flag, err, kErrWaitMma)) {
                   ok = false;
                   break;
                 }
                 tc_fence_after();
                 issue_s(a, st1);
                 if (a == 1) {
-                  tc_commit(B(B_KEMPTY0 + st1));
-                  if (j + 1 == n - 1) tc_commit(B(B_QEMPTY));
+                  commit_elect(B(B_KEMPTY0 + st1));
+                  if (j + 1 == n - 1) commit_elect(B(B_QEMPTY));
                 }
               }
             }

@@ -153,14 +153,18 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
           break;
         }
         const int s = c * kRows + r;
-        const float beta = s < T ? sigm(beta_logits[((long long)f * T + s) * ld_beta + beta_col0 + h]) : 0.f;
-        const __nv_bfloat162 b2 = __floats2bfloat162_rn(beta, beta);
         uint8_t* kt = smem + StatsSmem::kKV + st * 2 * kTile;
         uint8_t* vt = kt + kTile;
         uint8_t* bk = smem + StatsSmem::kBK + st * kTile;
+        // A row past the frame holds the next unit's tokens: it is zeroed in all three operand
+        // tiles (a zero beta alone would still carry a non-finite token of the next unit into
+        // this unit's sums as 0 * inf), so each frame's statistics see only its own tokens.
+        const bool past = s >= T;
+        const float beta = past ? 0.f : sigm(beta_logits[((long long)f * T + s) * ld_beta + beta_col0 + h]);
+        const __nv_bfloat162 b2 = __floats2bfloat162_rn(beta, beta);
         for (int b = 0; b < 2; ++b) {
           const uint32_t off = b * kBlk + r * 128;
-          const uint4* srck = reinterpret_cast<const uint4*>(kt + off);
+          uint4* srck = reinterpret_cast<uint4*>(kt + off);
           uint4* vv = reinterpret_cast<uint4*>(vt + off);
           uint4* dk = reinterpret_cast<uint4*>(bk + off);
           // the scale is the same for the whole row, so any chunk order works: start each
@@ -170,6 +174,11 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
           for (int i0 = 0; i0 < 8; ++i0) {
             const int i = i0 ^ (r & 7);
             uint4 k4 = srck[i], v4 = vv[i];
+            if (past) {
+              k4 = make_uint4(0u, 0u, 0u, 0u);
+              v4 = k4;
+              srck[i] = k4;
+            }
             __nv_bfloat162* kp = reinterpret_cast<__nv_bfloat162*>(&k4);
             __nv_bfloat162* vp = reinterpret_cast<__nv_bfloat162*>(&v4);
 #pragma unroll
