@@ -18,8 +18,9 @@ between its output and the GPU's, over every row.  ``--impl reference`` times th
 block forward as its step.
 
 Kernel-only modes for profiling: ``--only attention [--heads n]`` (the window attention kernel
-on the config geometry) and ``--only quantisers`` (the int8, ConvRot int8 and per-tensor e4m3
-activation quantisers on the config's branch rows, against the measured HBM bandwidth).
+on the config geometry), ``--only quantisers`` (the int8, ConvRot int8 and per-tensor e4m3
+activation quantisers on the config's branch rows, against the measured HBM bandwidth) and
+``--only gemms --precision bf16|int8|fp8 [--rows m]`` (the block's QKV projection GEMM).
 """
 
 from __future__ import annotations
@@ -439,6 +440,51 @@ def run_quantisers_only(args, c):
                           "gbs": gbs, "frac_of_hbm": gbs / pk["hbm_gbs"], "peak_source": src}), flush=True)
 
 
+def run_gemms_only(args, c):
+    """The block's QKV projection GEMM alone ([rows, hidden] x [3 H D, hidden]^T, bf16 out) in
+    the precision of ``--precision``: bf16 operands (kind 0), per-row int8 codes with row and
+    column scales in the epilogue (kind 2), or per-tensor e4m3 with device scales (kind 1).
+    ``--rows`` takes a smaller row count for profiling; the operands are quantised once,
+    outside the timed launches.  TFLOP/s against the measured bf16 peak (sustained) and, for
+    int8 / fp8, against twice it (the dense 8-bit : bf16 ratio of the part, 4.5 : 2.25)."""
+    from __graft_entry__ import load_package
+
+    pkg = load_package()
+    dev = torch.device("cuda", 0)
+    rows = args.rows or (c["text"] + c["frames"] * c["grid"][0] * c["grid"][1])
+    hidden, N = c["hidden"], 3 * c["heads"] * c["dim"]
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(rows, hidden, generator=g).to(dev, torch.bfloat16)
+    w = (torch.randn(N, hidden, generator=g) * 0.02).to(dev, torch.bfloat16)
+    out = torch.empty(rows, N, device=dev, dtype=torch.bfloat16)
+    if args.precision == "int8":
+        xa, wq = pkg.quantize_rows_int8(x), pkg.quantize_rows_int8(w)
+        fn = lambda: pkg.gemm(xa.data, wq.data, out=out, row_scale=xa.scale, col_scale=wq.scale, kind=2)
+    elif args.precision == "fp8":
+        xa, wq = pkg.quantize_tensor_fp8(x), pkg.quantize_tensor_fp8(w)
+        fn = lambda: pkg.gemm(xa.data, wq.data, out=out, dev_scale0=xa.scale, dev_scale1=wq.scale, kind=1)
+    else:
+        fn = lambda: pkg.gemm(x, w, out=out)
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(args.steps, 1)
+    tflops = 2 * rows * N * hidden / (ms * 1e-3) / 1e12
+    pk, src = peaks()
+    peak = pk["bf16_tflops_sustained"] * (1 if args.precision == "bf16" else 2)
+    print(json.dumps({"kernel": f"gemm_kernel<{ {'bf16': 0, 'fp8': 1, 'int8': 2}[args.precision] }>",
+                      "precision": args.precision, "M": rows, "N": N, "K": hidden, "ms": ms, "tflops": tflops,
+                      "peak": peak, "frac": tflops / peak,
+                      "peak_source": f"{src} bf16 sustained" + ("" if args.precision == "bf16" else " x 2")}),
+          flush=True)
+
+
 def run_dit_stack(args, c, world, rank, local):
     """Config 4: the denoiser forward stack of ``blocks`` DiT blocks (hybrid attention + GELU MLP,
     INT8 projections) over a CFG batch of 2 latent sequences; one step = one sampler step
@@ -581,9 +627,10 @@ def main():
     ap.add_argument("--impl", default="b200")
     ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["attention", "quantisers"], default=None,
+    ap.add_argument("--only", choices=["attention", "quantisers", "gemms"], default=None,
                     help="run one kernel alone on the config geometry (profiling small cases)")
     ap.add_argument("--heads", type=int, default=None, help="override the head count (profiling small cases)")
+    ap.add_argument("--rows", type=int, default=None, help="--only gemms: row count (profiling small cases)")
     ap.add_argument("--blocks", type=int, default=None, help="config 4: number of DiT blocks (default 50)")
     ap.add_argument("--delta-rule", choices=["vdn_solve", "sana_scaled"], default="vdn_solve",
                     help="configs 1/3: the branch's delta rule (BASELINE's released lineage is vdn_solve)")
@@ -605,6 +652,9 @@ def main():
         return
     if args.only == "quantisers":
         run_quantisers_only(args, c)
+        return
+    if args.only == "gemms":
+        run_gemms_only(args, c)
         return
     if args.config == 4 and args.impl != "reference":
         run_dit_stack(args, c, world, rank, local)
