@@ -759,7 +759,10 @@ def main():
     ms = e_start.elapsed_time(e_end) / max(args.steps, 1)
     ms = max_over_ranks(ms, world)
     value = flops["total"] / (ms * 1e-3) / 1e12  # one block forward of the whole problem per step
-    attn_avg = sum(a.elapsed_time(b) for a, b in attn_ms) / max(len(attn_ms), 1)
+    # the attention of one forward may be several launches (one per row chunk when the heads
+    # are sharded and the exchange is chunked): sum them per step
+    attn_avg = sum(a.elapsed_time(b) for a, b in attn_ms) / max(args.steps, 1)
+    attn_launches = len(attn_ms) // max(args.steps, 1)
     pk, pk_src = peaks()
     achieved = flops["attention"] / world / (attn_avg * 1e-3) / 1e12  # this rank's heads
     peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
@@ -854,7 +857,7 @@ def main():
                      "unit": "TFLOP/s", "frac": achieved / peak,
                      "traffic": attention_traffic(H // world, H) if args.config == 1 else None,
                      "algorithmic_bytes": lay.seq_len * (H // world) * D * 2 * 4, "peak_source": f"{pk_src} sustained",
-                     "kernel_ms": attn_avg, "block_frac": value / world / peak},
+                     "kernel_ms": attn_avg, "launches_per_step": attn_launches, "block_frac": value / world / peak},
         # bytes summed over the ranks (at N > 1 each rank moves its own row block)
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": S * hidden * 2, "d2h_bytes_per_step": S * hidden * 2,
