@@ -27,8 +27,8 @@
 //     it straight from TMEM (A operand in tensor memory), so shared memory holds only Q and
 //     the K/V ring.  The next S_a is issued after PV_a, so the in-order tensor pipe never
 //     overwrites P before it is consumed, and S_a's completion implies PV_a's.  P goes to the
-//     MMA warp in two parts (keys 0-95, then 96-127), so most of PV_a starts before the
-//     softmax has finished the tile;
+//     MMA warp in two parts (keys 0-47, then 48-127), so PV_a starts while the softmax is
+//     still on the tile;
 //   * online softmax in registers with exp2 in log2 units; the reference maximum moves only
 //     when a tile exceeds it by more than 2^8, so O is rescaled rarely (the result is exact),
 //     and the exponentials start against the current reference while the tile maximum is
@@ -273,8 +273,9 @@ struct Layout {
 };
 
 // P of a tile is handed to the MMA warp in two parts: keys [0, kPSplit) (B_PLO) and the rest
-// (B_PHI), so the first PV products run while the softmax finishes the last chunks.
-constexpr int kPSplit = 96;
+// (B_PHI), so the first PV products run while the softmax finishes the last chunks.  Measured
+// at config 1, 40 heads (ms per launch): split 96: 7.33, 64: 7.02, 48: 6.84, 32: 7.08.
+constexpr int kPSplit = 48;
 
 enum {
   B_QFULL = 0, B_QEMPTY, B_KFULL0, B_KFULL1, B_VFULL0, B_VFULL1, B_KEMPTY0, B_KEMPTY1, B_VEMPTY0, B_VEMPTY1,

@@ -106,9 +106,10 @@ def test_block_quantised_projections_match_oracle(precision, to_out):
 
 @pytest.mark.parametrize("delta_rule", ["vdn_solve", "sana_scaled"])
 def test_block_d128_ragged_frames_matches_oracle(delta_rule):
-    c = dict(text=64, frames=7, grid=(9, 14), heads=2, dim=128, hidden=512)
+    c = dict(text=64, frames=11, grid=(9, 14), heads=2, dim=128, hidden=512)
     bw = vo.make_block(4, c["hidden"], c["heads"], c["dim"])
     lay_o = vo.config_layout(c)
+    assert not _layout(c).full_cover  # the branch runs
     x = vo.make_x(4, lay_o.seq_len, c["hidden"])
     got = _run_block(bw, _layout(c), c["heads"], c["dim"], x,
                      config=vo.BranchConfig(delta_rule=delta_rule).node_config())
@@ -116,10 +117,28 @@ def test_block_d128_ragged_frames_matches_oracle(delta_rule):
     assert rel_l2(got, want) < 2e-2
 
 
+def test_node_config_without_branch_keys_runs_the_reference_default_block():
+    """A node config that names none of the branch keys (nodes.py:98-116 then builds
+    short_conv=() and no text state, bridge "alpha", delta rule "vdn_solve") runs that block
+    through the drop-in operator: it matches the oracle of that structure, and differs from
+    the released lineage's (short conv on k and v, text state)."""
+    c = dict(text=64, frames=15, grid=(4, 6), heads=2, dim=128, hidden=256)
+    bw = vo.make_block(4, c["hidden"], c["heads"], c["dim"])
+    lay_o = vo.config_layout(c)
+    assert not _layout(c).full_cover  # the branch runs
+    x = vo.make_x(4, lay_o.seq_len, c["hidden"])
+    got = _run_block(bw, _layout(c), c["heads"], c["dim"], x, config={"enable_softmax_gate": True})
+    want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"],
+                            vo.BranchConfig(short_conv=(), enable_text_state=False))
+    lineage = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig())
+    assert rel_l2(got, want) < 2e-2
+    assert rel_l2(got, lineage) > 5 * rel_l2(got, want)
+
+
 def test_block_with_rope_matches_oracle():
     """rope_freqs in ComfyUI's [1, S, 1, rot/2, 2, 2] form through the drop-in operator (RoPE
     parity unpinned: restated, not checked against comfy-kitchen)."""
-    c = dict(text=64, frames=7, grid=(9, 14), heads=2, dim=128, hidden=512)
+    c = dict(text=64, frames=11, grid=(9, 14), heads=2, dim=128, hidden=512)
     bw = vo.make_block(4, c["hidden"], c["heads"], c["dim"])
     lay_o = vo.config_layout(c)
     x = vo.make_x(4, lay_o.seq_len, c["hidden"])
@@ -132,8 +151,9 @@ def test_block_with_rope_matches_oracle():
     torch.cuda.synchronize()
     want = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig(), rope_freqs=freqs)
     plain = vo.block_forward(x, bw, lay_o, c["heads"], c["dim"], vo.BranchConfig())
-    assert rel_l2(got, want) < 2e-2
-    assert rel_l2(want, plain) > 5e-2  # the rotation matters on this input
+    err = rel_l2(got, want)
+    assert err < 2e-2
+    assert rel_l2(want, plain) > max(2e-2, 3 * err)  # the rotation matters on this input
 
 
 def test_block_sana_rule_matches_oracle_and_golden():

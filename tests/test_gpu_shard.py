@@ -74,7 +74,7 @@ def _emulated_sharded_forward(bw, lay, heads, dim, x, precision, world, exchange
 
 GEOMETRIES = {
     "config0": (vo.CONFIG0, (2,)),
-    "d128_ragged": (dict(text=64, frames=7, grid=(9, 14), heads=4, dim=128, hidden=512), (2, 4)),
+    "d128_ragged": (dict(text=64, frames=11, grid=(9, 14), heads=4, dim=128, hidden=512), (2, 4)),
 }
 
 
@@ -129,7 +129,7 @@ def _nccl_worker(rank, world, port, q):
                             device_id=torch.device("cuda", rank))
     try:
         pkg_r = load_package()
-        c = dict(text=64, frames=7, grid=(9, 14), heads=4, dim=128, hidden=512)
+        c = dict(text=64, frames=11, grid=(9, 14), heads=4, dim=128, hidden=512)
         H, D, hidden = c["heads"], c["dim"], c["hidden"]
         bw = vo.make_block(6, hidden, H, D)
         lay = pkg_r.make_layout(c["text"], c["frames"], c["grid"])
