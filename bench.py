@@ -631,6 +631,8 @@ def main():
                     help="run one kernel alone on the config geometry (profiling small cases)")
     ap.add_argument("--heads", type=int, default=None, help="override the head count (profiling small cases)")
     ap.add_argument("--rows", type=int, default=None, help="--only gemms: row count (profiling small cases)")
+    ap.add_argument("--e2e-blocks", type=int, default=E2E_ROW_BLOCKS,
+                    help="row blocks per host copy in the end-to-end leg at N = 1")
     ap.add_argument("--blocks", type=int, default=None, help="config 4: number of DiT blocks (default 50)")
     ap.add_argument("--delta-rule", choices=["vdn_solve", "sana_scaled"], default="vdn_solve",
                     help="configs 1/3: the branch's delta rule (BASELINE's released lineage is vdn_solve)")
@@ -820,7 +822,7 @@ def main():
         # one GPU: inputs copied in and outputs copied back by row blocks, overlapping the
         # first step's QKV and the last step's output projection too
         streamer.run([inputs_host[0]] * k, [outs_host[i & 1] for i in range(k)], prepare=prepare,
-                     chunks=E2E_ROW_BLOCKS if world == 1 else 1)
+                     chunks=args.e2e_blocks if world == 1 else 1)
 
     e2e_run(args.warmup)
     torch.cuda.synchronize()
@@ -862,7 +864,7 @@ def main():
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": S * hidden * 2, "d2h_bytes_per_step": S * hidden * 2,
                 "copies": "pinned host buffers; H2D of step i+1 and D2H of step i-1 overlap step i (HostStreamer); "
-                  f"{E2E_ROW_BLOCKS if world == 1 else 1} row blocks per copy",
+                  f"{args.e2e_blocks if world == 1 else 1} row blocks per copy",
                 **copy_ms},
         "gpu_launches": launches,
         "gemm": gemm_line,
