@@ -347,7 +347,7 @@ def run_reference_arm(args, c, world, rank):
     print(json.dumps(line), flush=True)
 
 
-E2E_ROW_BLOCKS = 4  # row blocks of the end-to-end copies at N = 1
+E2E_ROW_BLOCKS = 8  # row blocks of the end-to-end copies at N = 1 (4: 15.98 ms e2e, 8: 15.81, 16: 16.23)
 
 
 def node_config(delta_rule="vdn_solve") -> dict:
