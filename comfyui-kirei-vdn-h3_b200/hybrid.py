@@ -47,6 +47,20 @@ STREAM_IO_KEY = "vdn_b200_io"  # transformer_options entry carrying a StreamIO (
 AUX_ALIGN = 32  # side columns padded to 32: 128-byte fp32 rows, and no extra 256-column GEMM tile
 EXCHANGE_CHUNKS = 4  # pipelined exchange / projection / gather steps of the head-sharded block
 EXCHANGE_MIN_ROWS = 512  # rows per rank and chunk (one wave of projection tiles); fewer: one step
+# Work items per CTA below which the chunks of a head-sharded block share one attention launch:
+# a persistent launch of few items per CTA loses its tail to the unevenly sized items (at 4 GPUs,
+# config 1, four launches of 260 items made the kernel 1.3x slower per head than one launch).
+ATTN_ITEMS_PER_CTA = 6
+
+
+_SM_COUNT: dict = {}
+
+
+def _sm_count(device) -> int:
+    key = torch.device(device).index
+    if key not in _SM_COUNT:
+        _SM_COUNT[key] = torch.cuda.get_device_properties(device).multi_processor_count
+    return _SM_COUNT[key]
 
 # Branch settings a node config may leave out, with the values the reference falls back to:
 # the node builds each block's branch from the config with these defaults (nodes.py:98-116)
@@ -632,11 +646,16 @@ class FusedBlock:
                     g.dim ** -0.5, status)
         xchg = ws.get("xchg") if issue_exchange else None
         if xchg is not None and xchg.chunks > 1:
+            # the attention of consecutive row chunks in as many launches as keep at least
+            # ATTN_ITEMS_PER_CTA items per CTA; each launch's chunks are exchanged behind it
             ends = [xchg.chunk_rows(c)[1] for c in range(xchg.chunks)]
-            for c, items in enumerate(plan.device_chunk_items(x.device, g.heads, ends)):
+            total = plan.n_qtiles * g.heads
+            launches = max(1, min(xchg.chunks, total // (ATTN_ITEMS_PER_CTA * _sm_count(x.device))))
+            for items, chunks in plan.device_chunk_groups(x.device, g.heads, ends, launches):
                 if items.numel():
                     launch_window_attention(*operands, items=items, **attend)
-                xchg.exchange_chunk(c)
+                for c in chunks:
+                    xchg.exchange_chunk(c)
         else:
             launch_window_attention(*operands, **attend)
         return ws, linear_active

@@ -140,6 +140,27 @@ class WindowPlan:
                       for it in self.chunk_items(heads, ends)]
         return d[key]
 
+    def chunk_groups(self, heads: int, ends, launches: int) -> list[tuple[np.ndarray, range]]:
+        """``chunk_items`` merged into ``launches`` runs of consecutive chunks (as even as the
+        chunk count allows): each run's items, in chunk order, and the chunks it covers.  One
+        launch per run keeps enough items per CTA for the persistent grid to balance its tail,
+        while the collectives of a run's chunks still start as soon as that run is done."""
+        per = self.chunk_items(heads, ends)
+        n = len(per)
+        runs = max(1, min(int(launches), n))
+        bounds = [(n * k) // runs for k in range(runs + 1)]
+        return [(np.concatenate(per[a:b]).astype(np.int32) if b > a else np.zeros(0, np.int32), range(a, b))
+                for a, b in zip(bounds, bounds[1:])]
+
+    def device_chunk_groups(self, device, heads: int, ends, launches: int) -> list[tuple[torch.Tensor, range]]:
+        """``chunk_groups`` on the device (cached per chunk boundaries and launch count)."""
+        d = self.device_arrays(device, heads)
+        key = ("groups", tuple(int(e) for e in ends), int(launches))
+        if key not in d:
+            d[key] = [(torch.from_numpy(np.ascontiguousarray(it)).to(torch.device(device)), r)
+                      for it, r in self.chunk_groups(heads, ends, launches)]
+        return d[key]
+
 
 HALF = BQ // 2  # rows per MMA half of a work item
 

@@ -460,3 +460,23 @@ def test_chunk_items_finish_every_row_before_its_chunk_ends(n_chunks):
             for r0, n in plan.q_halves(code & 0xFFFFF):
                 done[r0:r0 + n] = True
         assert done[:ends[c]].all()
+
+
+@pytest.mark.parametrize("n_chunks,launches", [(4, 1), (4, 2), (4, 3), (4, 4), (8, 3), (3, 5)])
+def test_chunk_groups_cover_the_chunks_in_order(n_chunks, launches):
+    """Chunks merged into fewer attention launches: the runs are consecutive, cover every
+    chunk once, and each run's items are its chunks' items in chunk order."""
+    lay = vo.config_layout(vo.CONFIG1)
+    plan = bw.build_window_plan(lay.seq_len, lay.video_start, lay.video_end, lay.num_frames,
+                                lay.tokens_per_frame, list(lay.bounds), lay.anchor_frames)
+    S, heads = lay.seq_len, 2
+    step = -(-S // n_chunks)
+    ends = [min(S, (c + 1) * step) for c in range(n_chunks)]
+    per = plan.chunk_items(heads, ends)
+    groups = plan.chunk_groups(heads, ends, launches)
+    assert len(groups) == min(launches, n_chunks)
+    covered = [c for _, r in groups for c in r]
+    assert covered == list(range(n_chunks))
+    for items, r in groups:
+        want = np.concatenate([per[c] for c in r]) if len(r) else np.zeros(0, np.int32)
+        assert np.array_equal(items, want)
