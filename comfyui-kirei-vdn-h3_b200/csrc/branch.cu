@@ -19,9 +19,16 @@
 namespace vdn {
 namespace branch {
 
-// x * sigmoid(x) with the fast reciprocal (2 ulp; the result is rounded to bf16); for
-// x -> -inf the denominator overflows to inf and the quotient is -0
-__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+// x * sigmoid(x) = x / (1 + 2^(-x log2 e)) with the hardware's approximate exp2 and
+// reciprocal (2 ulp; the result is rounded to bf16), in their flush-to-zero forms, which
+// skip the subnormal handling (a subnormal intermediate becomes 0); for x -> -inf the
+// denominator overflows to inf, its reciprocal is 0 and the product -0
+__device__ __forceinline__ float silu(float x) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-x * 1.4426950408889634f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return x * r;
+}
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 
@@ -82,69 +89,75 @@ __global__ void __launch_bounds__(128) spatial_conv5_kernel(const __nv_bfloat16*
   }
 }
 
-// Tiled 5x5 depthwise conv.  A persistent CTA walks a contiguous range of tiles (64
-// channels x 8 output rows of one frame, channel-slab-major so the weights change
-// rarely).  Each tile's input rows y0-2 .. y0+9 are staged in shared memory by 16-byte
-// cp.async copies, with the zero padding written in place (two zero columns left and
-// right, zero rows outside the frame), so the inner loop has no bounds checks.  Two CTAs
-// share an SM, so one's copies are in flight while the other computes.
-// Warp w computes output row y0 + w, lane l channels c0 + 2l, 2l + 1: it slides along x
-// keeping the 5x5 window of both channels in registers (5 shared loads per output) and
-// accumulates five independent paired-fp32 chains, one per kernel row.
-constexpr int kConvRows = 8;
-constexpr int kConvCh = 64;
-constexpr int kConvThreads = kConvRows * 32;
+// Tiled 5x5 depthwise conv.  A persistent CTA of four warps walks a contiguous range of
+// tiles (64 channels x 8 output rows of one frame, channel-slab-major so the weights
+// change rarely).  Each tile's input rows y0-2 .. y0+9 are staged in shared memory by
+// 16-byte cp.async copies, the zero padding (two columns left and right, rows outside the
+// frame) by the zero-filling form of the same copy, so the inner loop has no bounds
+// checks.  Several CTAs share an SM (three at the config-1 row width of 38), so the copies
+// of some are in flight while the others compute.
+// Warp w computes output rows y0 + 2w, y0 + 2w + 1, lane l channels c0 + 2l, 2l + 1.  It
+// walks the staged columns left to right: the 6 rows of a column are read once and added
+// into every output they feed (2 rows x 5 columns of running paired-fp32 sums in
+// registers), and the output column that the column completes is stored.  Per output
+// that is 25 paired FMAs, 3 paired shared loads and one 4-byte store, against 5 loads and
+// 4 extra adds when each output gathers its own 5x5 window.  At config 1 (29 frames of
+// 22 x 38, 5120 channels) this runs in 279 us against 313 us for one warp per output row
+// gathering its window; 4 rows per warp (two-warp CTAs, fewer warps per SM) took 402 us.
+constexpr int kConvRows = 8;         // output rows per tile
+constexpr int kConvWarpRows = 2;     // output rows per warp
+constexpr int kConvCh = 64;          // channels per tile: two per lane
+constexpr int kConvThreads = kConvRows / kConvWarpRows * 32;
+constexpr int kConvMaxCtas = 3;      // CTAs per SM the register budget is sized for
 
 __device__ __forceinline__ float2 lds_bf162(const __nv_bfloat16* p) {
   return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
 }
 
-__global__ void __launch_bounds__(kConvThreads, 2)
+__global__ void __launch_bounds__(kConvThreads, kConvMaxCtas)
     spatial_conv5_tiled_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in, const float* __restrict__ w,
-                               int F, int gh, int gw, int C, __nv_bfloat16* __restrict__ out, long long ld_out,
-                               int stages) {
+                               int F, int gh, int gw, int C, __nv_bfloat16* __restrict__ out, long long ld_out) {
   extern __shared__ __align__(16) __nv_bfloat16 conv_smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bands = (gh + kConvRows - 1) / kConvRows;
   const int per_slab = F * bands;
   const int n_tiles = (C / kConvCh) * per_slab;
   const int pitch = gw + 4;  // shared-memory columns per row: image column x sits at x + 2
-  const int buf_elems = (kConvRows + 4) * pitch * kConvCh;
+  const int n_px = (kConvRows + 4) * pitch;
   const int t0 = (int)((long long)blockIdx.x * n_tiles / gridDim.x);
   const int t1 = (int)((long long)(blockIdx.x + 1) * n_tiles / gridDim.x);
   if (t0 >= t1) return;
 
-  auto issue = [&](int t, int buf) {
+  // Thread tid copies the 16-byte chunk q = tid % 8 (8 channels) of the staged pixels
+  // tid / 8, tid / 8 + kPxStep, ...; the pixel's row and column advance without a division.
+  constexpr int kPxStep = kConvThreads / 8;
+  const int q = tid & 7, px0 = tid >> 3;
+  const int row0 = px0 / pitch, col0 = px0 - row0 * pitch;
+  auto issue = [&](int t) {
     const int slab = t / per_slab, r = t - slab * per_slab;
     const int f = r / bands, y0 = (r - f * bands) * kConvRows;
-    const int c0 = slab * kConvCh;
-    __nv_bfloat16* dst0 = conv_smem + buf * buf_elems;
-    const int chunks = (kConvRows + 4) * pitch * (kConvCh / 8);
-    for (int i = tid; i < chunks; i += kConvThreads) {
-      const int q = i & 7, px = i >> 3;
-      const int row = px / pitch, col = px - row * pitch;
+    const __nv_bfloat16* src = in + (long long)f * gh * gw * ld_in + slab * kConvCh + q * 8;
+    int row = row0, col = col0;
+    uint32_t dst = smem_u32(conv_smem + px0 * kConvCh + q * 8);
+    for (int px = px0; px < n_px; px += kPxStep, dst += kPxStep * kConvCh * 2) {
       const int yy = y0 - 2 + row, xx = col - 2;
-      __nv_bfloat16* dst = dst0 + px * kConvCh + q * 8;
-      if (yy >= 0 && yy < gh && xx >= 0 && xx < gw)
-        cp_async16(smem_u32(dst), in + ((long long)(f * gh + yy) * gw + xx) * ld_in + c0 + q * 8);
-      else
-        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+      const bool inside = yy >= 0 && yy < gh && xx >= 0 && xx < gw;
+      // padding positions read nothing (zero fill) from the frame's first pixel
+      cp_async16_zfill(dst, inside ? src + (long long)(yy * gw + xx) * ld_in : src, inside ? 16u : 0u);
+      col += kPxStep;
+      while (col >= pitch) {
+        col -= pitch;
+        ++row;
+      }
     }
     cp_async_commit();
   };
 
   float2 wr[5][5];
   int cur_slab = -1;
-  issue(t0, 0);
   for (int t = t0; t < t1; ++t) {
-    const int buf = stages == 2 ? ((t - t0) & 1) : 0;
-    if (stages == 1 && t > t0) issue(t, 0);
-    if (stages == 2 && t + 1 < t1) {
-      issue(t + 1, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+    issue(t);
+    cp_async_wait<0>();
     __syncthreads();
     const int slab = t / per_slab, r = t - slab * per_slab;
     const int f = r / bands, y0 = (r - f * bands) * kConvRows;
@@ -157,44 +170,52 @@ __global__ void __launch_bounds__(kConvThreads, 2)
           wr[dy][dx] = make_float2(w[(long long)c * 25 + dy * 5 + dx], w[(long long)(c + 1) * 25 + dy * 5 + dx]);
       cur_slab = slab;
     }
-    const int y = y0 + warp;
+    const int y = y0 + warp * kConvWarpRows;
     if (y < gh) {
-      // shared row `warp + dy` holds image row y - 2 + dy
-      const __nv_bfloat16* base = conv_smem + buf * buf_elems + warp * pitch * kConvCh + 2 * lane;
+      const int rows = min(kConvWarpRows, gh - y);
+      // shared row warp * kConvWarpRows + i holds image row y - 2 + i (zeros outside the frame)
+      const __nv_bfloat16* base = conv_smem + warp * kConvWarpRows * pitch * kConvCh + 2 * lane;
       __nv_bfloat16* orow = out + (long long)(f * gh + y) * gw * ld_out + c;
-      float2 win[5][5];  // win[slot][dy]; slot (x + k) % 5 holds shared column x + k
+      float2 acc[5][kConvWarpRows];  // acc[x % 5][o]: the running sum of output (y + o, x)
 #pragma unroll
-      for (int s = 0; s < 5; ++s)
+      for (int k = 0; k < 5; ++k)
 #pragma unroll
-        for (int dy = 0; dy < 5; ++dy) win[s][dy] = lds_bf162(base + (dy * pitch + s) * kConvCh);
-      // one output: five paired-fp32 chains (one per kernel row), then column x + 5 replaces x
-      auto step = [&](int u, int x, bool tail) {
-        float2 a[5];
+        for (int o = 0; o < kConvWarpRows; ++o) acc[k][o] = make_float2(0.f, 0.f);
+      // staged column s (image column s - 2, s % 5 == u) feeds output x = s - dx through
+      // kernel column dx; the sum of x starts at dx = 0 and is complete after dx = 4
+      auto column = [&](int s, int u) {
+        float2 v[kConvWarpRows + 4];
 #pragma unroll
-        for (int dy = 0; dy < 5; ++dy) a[dy] = make_float2(0.f, 0.f);
+        for (int i = 0; i < kConvWarpRows + 4; ++i) v[i] = lds_bf162(base + (i * pitch + s) * kConvCh);
 #pragma unroll
-        for (int k = 0; k < 5; ++k)
+        for (int dx = 0; dx < 5; ++dx) {
+          const int k = (u - dx + 5) % 5;
 #pragma unroll
-          for (int dy = 0; dy < 5; ++dy) a[dy] = fma2(wr[dy][k], win[(u + k) % 5][dy], a[dy]);
-        const float2 sum = add2(add2(add2(a[0], a[1]), add2(a[2], a[3])), a[4]);
-        *reinterpret_cast<__nv_bfloat162*>(orow + (long long)x * ld_out) = __floats2bfloat162_rn(sum.x, sum.y);
-        if (!tail || x + 5 < pitch) {
+          for (int o = 0; o < kConvWarpRows; ++o)
 #pragma unroll
-          for (int dy = 0; dy < 5; ++dy) win[u][dy] = lds_bf162(base + (dy * pitch + x + 5) * kConvCh);
+            for (int dy = 0; dy < 5; ++dy)
+              acc[k][o] = (dx == 0 && dy == 0) ? mul2(wr[0][0], v[o]) : fma2(wr[dy][dx], v[o + dy], acc[k][o]);
+        }
+        const int x = s - 4;
+        if (x >= 0) {
+          const int k = (u + 1) % 5;
+#pragma unroll
+          for (int o = 0; o < kConvWarpRows; ++o)
+            if (o < rows)
+              *reinterpret_cast<__nv_bfloat162*>(orow + ((long long)o * gw + x) * ld_out) =
+                  __floats2bfloat162_rn(acc[k][o].x, acc[k][o].y);
         }
       };
-      int x0 = 0;
-      // main groups: outputs x0 .. x0 + 4 < gw and their column loads x + 5 <= x0 + 9 < pitch
-      for (; x0 + 5 < gw; x0 += 5) {
+      int s0 = 0;
+      for (; s0 + 5 <= pitch; s0 += 5) {
 #pragma unroll
-        for (int u = 0; u < 5; ++u) step(u, x0 + u, false);
+        for (int u = 0; u < 5; ++u) column(s0 + u, u);
       }
-      // the last 1..5 outputs, with both checks
 #pragma unroll
       for (int u = 0; u < 5; ++u)
-        if (x0 + u < gw) step(u, x0 + u, true);
+        if (s0 + u < pitch) column(s0 + u, u);
     }
-    __syncthreads();  // every warp is done with `buf` before it is refilled
+    __syncthreads();  // every warp is done with the buffer before it is refilled
   }
 }
 
@@ -225,95 +246,109 @@ __global__ void spatial_conv_kernel(const __nv_bfloat16* __restrict__ in, long l
 
 // ---------------------------------------------------------------------------------
 // 2. Temporal conv + SiLU + optional L2, output FHSD [F, H, T, D] bf16.
-// One warp per (token s, head h); lane l holds channels h*D + l*D/32 .. +D/32.  Frames
-// are processed in chunks of 12 outputs: the 16 input frames a chunk needs are loaded
-// first (one 8-byte load per lane and frame for D = 128, all independent, so a warp
-// keeps 16 loads in flight instead of one), then the 5-tap conv, SiLU and the L2 norm
-// (a warp reduction) run from registers.  taps == 0 means no temporal conv.
+// One warp per (token s, head h); lane l holds channels h*D + l*D/32 .. +D/32 as fp32
+// pairs.  The warp walks the frames in chunks of 8 outputs: a chunk first loads the 8
+// input frames it brings into the window (one 8-byte load per lane and frame for D = 128,
+// all in flight at once), then for each output unpacks one frame into a sliding window
+// of 5 and runs the 5-tap conv (paired FMAs), SiLU and the L2 norm (a warp reduction)
+// from registers, so every input frame is unpacked once.  taps 0 (no temporal conv), 1
+// and 3 run with a window of 1 or 3.
 // ---------------------------------------------------------------------------------
 template <int V>
 struct PackedBf16;
 template <>
 struct PackedBf16<4> {
   using T = uint2;
-  __device__ static void unpack(T p, float (&v)[4]) {
-    v[0] = __uint_as_float(p.x << 16);
-    v[1] = __uint_as_float(p.x & 0xffff0000u);
-    v[2] = __uint_as_float(p.y << 16);
-    v[3] = __uint_as_float(p.y & 0xffff0000u);
+  __device__ static void unpack2(T p, float2 (&v)[2]) {
+    v[0] = make_float2(__uint_as_float(p.x << 16), __uint_as_float(p.x & 0xffff0000u));
+    v[1] = make_float2(__uint_as_float(p.y << 16), __uint_as_float(p.y & 0xffff0000u));
   }
-  __device__ static T pack(const float (&v)[4]) { return make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3])); }
+  __device__ static T pack2(const float2 (&v)[2]) {
+    return make_uint2(pack_bf16(v[0].x, v[0].y), pack_bf16(v[1].x, v[1].y));
+  }
 };
 template <>
 struct PackedBf16<2> {
   using T = uint32_t;
-  __device__ static void unpack(T p, float (&v)[2]) {
-    v[0] = __uint_as_float(p << 16);
-    v[1] = __uint_as_float(p & 0xffff0000u);
+  __device__ static void unpack2(T p, float2 (&v)[1]) {
+    v[0] = make_float2(__uint_as_float(p << 16), __uint_as_float(p & 0xffff0000u));
   }
-  __device__ static T pack(const float (&v)[2]) { return pack_bf16(v[0], v[1]); }
+  __device__ static T pack2(const float2 (&v)[1]) { return pack_bf16(v[0].x, v[0].y); }
 };
 
-template <int D>
+template <int D, int TAPS>
 __global__ void __launch_bounds__(256, 3) temporal_act_kernel(const __nv_bfloat16* __restrict__ in, long long ld_in,
                                                            const float* __restrict__ w, int taps, int F, int T,
                                                            int H, int l2, __nv_bfloat16* __restrict__ out) {
-  constexpr int V = D / 32;  // channels per lane
-  constexpr int kChunk = 12;
-  constexpr int kLoad = kChunk + 4;
+  constexpr int V = D / 32;    // channels per lane
+  constexpr int NP = V / 2;    // fp32 pairs per lane
+  constexpr int kChunk = 8;    // outputs per chunk = frames loaded per chunk
+  constexpr int kPad = TAPS / 2;
   using P = PackedBf16<V>;
   const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gwarp >= T * H) return;
   const int s = gwarp / H, h = gwarp % H;
   const int c0 = h * D + lane * V;
-  // y_t = sum_dt wt[dt] x_{t - pad + dt}; no conv = one tap of weight 1
-  const int pad = taps / 2;
-  float wt[5][V];
+  // y_t = sum_dt wt[dt] x_{t - pad + dt}, frames outside [0, F) are zero; no conv
+  // (taps == 0) = one tap of weight 1
+  float2 wt[TAPS][NP];
 #pragma unroll
-  for (int dt = 0; dt < 5; ++dt)
+  for (int dt = 0; dt < TAPS; ++dt)
 #pragma unroll
-    for (int i = 0; i < V; ++i)
-      wt[dt][i] = taps == 0 ? (dt == 0 ? 1.f : 0.f) : (dt < taps ? w[(long long)(c0 + i) * taps + dt] : 0.f);
-  const int span = taps == 0 ? 1 : taps;
+    for (int p = 0; p < NP; ++p)
+      wt[dt][p] = taps == 0 ? make_float2(1.f, 1.f)
+                            : make_float2(w[(long long)(c0 + 2 * p) * taps + dt], w[(long long)(c0 + 2 * p + 1) * taps + dt]);
+  const __nv_bfloat16* src = in + (long long)s * ld_in + c0;
+  const long long frame_pitch = (long long)T * ld_in;
+  auto load = [&](int tt) {
+    typename P::T r{};
+    if (tt >= 0 && tt < F) r = *reinterpret_cast<const typename P::T*>(src + tt * frame_pitch);
+    return r;
+  };
+  __nv_bfloat16* dst = out + ((long long)h * T + s) * D + lane * V;
+  const long long out_pitch = (long long)H * T * D;
+  // win[j] = frame t - pad + j while output t is computed; before output 0 the frames
+  // -pad .. pad - 1 sit in win[1 ..], and each output shifts the window by one frame
+  float2 win[TAPS][NP];
+#pragma unroll
+  for (int j = 1; j < TAPS; ++j) P::unpack2(load(j - kPad - 1), win[j]);
   for (int t0 = 0; t0 < F; t0 += kChunk) {
-    typename P::T raw[kLoad];
+    typename P::T raw[kChunk];  // the frames entering the window in this chunk
 #pragma unroll
-    for (int j = 0; j < kLoad; ++j) {
-      const int tt = t0 - pad + j;
-      if (j < kChunk + span - 1 && tt >= 0 && tt < F)
-        raw[j] = *reinterpret_cast<const typename P::T*>(in + ((long long)tt * T + s) * ld_in + c0);
-      else
-        raw[j] = typename P::T{};
-    }
+    for (int i = 0; i < kChunk; ++i) raw[i] = load(t0 + i + kPad);
 #pragma unroll
     for (int i = 0; i < kChunk; ++i) {
       const int t = t0 + i;
       if (t >= F) break;
-      float y[V];
 #pragma unroll
-      for (int v = 0; v < V; ++v) y[v] = 0.f;
+      for (int j = 0; j + 1 < TAPS; ++j)
 #pragma unroll
-      for (int dt = 0; dt < 5; ++dt) {
-        float x[V];
-        P::unpack(raw[i + dt < kLoad ? i + dt : kLoad - 1], x);
+        for (int p = 0; p < NP; ++p) win[j][p] = win[j + 1][p];
+      P::unpack2(raw[i], win[TAPS - 1]);
+      float2 y[NP];
 #pragma unroll
-        for (int v = 0; v < V; ++v) y[v] = fmaf(wt[dt][v], x[v], y[v]);
-      }
+      for (int p = 0; p < NP; ++p) y[p] = fma2(wt[0][p], win[0][p], make_float2(0.f, 0.f));
+#pragma unroll
+      for (int dt = 1; dt < TAPS; ++dt)
+#pragma unroll
+        for (int p = 0; p < NP; ++p) y[p] = fma2(wt[dt][p], win[dt][p], y[p]);
       float ss = 0.f;
 #pragma unroll
-      for (int v = 0; v < V; ++v) {
-        y[v] = silu(y[v]);
-        ss += y[v] * y[v];
+      for (int p = 0; p < NP; ++p) {
+        y[p].x = silu(y[p].x);
+        ss += y[p].x * y[p].x;
+        y[p].y = silu(y[p].y);
+        ss += y[p].y * y[p].y;
       }
       if (l2) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-6f);
 #pragma unroll
-        for (int v = 0; v < V; ++v) y[v] *= inv;
+        for (int p = 0; p < NP; ++p) y[p] = make_float2(y[p].x * inv, y[p].y * inv);
       }
-      *reinterpret_cast<typename P::T*>(out + (((long long)t * H + h) * T + s) * D + lane * V) = P::pack(y);
+      *reinterpret_cast<typename P::T*>(dst + t * out_pitch) = P::pack2(y);
     }
   }
 }
@@ -1109,17 +1144,24 @@ int vdn_spatial_conv(const void* in, long long ld_in, const float* w, int kh, in
   const bool tiled = paired && (C % kConvCh) == 0 && (ld_in % 8) == 0 && vdn::aligned16(in) &&
                      buf_bytes <= kSmemLimit;
   if (tiled) {
-    if (!vdn::smem_optin((const void*)spatial_conv5_tiled_kernel, (int)kSmemLimit)) return vdn::kLaunchFailed;
-    // two CTAs per SM with one buffer each when they fit (one CTA computes while the other
-    // loads); the kernel can also double-buffer inside one CTA (stages = 2), which measured
-    // slower at 8 warps per SM
-    const bool two_ctas = 2 * buf_bytes <= kSmemLimit;
-    const int stages = 1;
+    if (!vdn::smem_optin((const void*)spatial_conv5_tiled_kernel, (int)kSmemLimit) ||
+        !vdn::func_attr((const void*)spatial_conv5_tiled_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                        cudaSharedmemCarveoutMaxShared))
+      return vdn::kLaunchFailed;
+    // one buffer per CTA and as many CTAs per SM as fit: some CTAs' copies are in flight
+    // while the others compute
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, spatial_conv5_tiled_kernel, kConvThreads,
+                                                      (size_t)buf_bytes) != cudaSuccess ||
+        per_sm < 1) {
+      cudaGetLastError();
+      per_sm = 1;
+    }
     const long long n_tiles = (long long)(C / kConvCh) * F * ((gh + kConvRows - 1) / kConvRows);
-    const int grid = (int)std::min<long long>(n_tiles, (two_ctas ? 2 : 1) * vdn::sm_count());
-    spatial_conv5_tiled_kernel<<<grid, kConvThreads, stages * buf_bytes, s>>>(
+    const int grid = (int)std::min<long long>(n_tiles, (long long)per_sm * vdn::sm_count());
+    spatial_conv5_tiled_kernel<<<grid, kConvThreads, buf_bytes, s>>>(
         reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, F, gh, gw, C, reinterpret_cast<__nv_bfloat16*>(out),
-        ld_out, stages);
+        ld_out);
     vdn::count_launch();
   } else if (paired) {
     dim3 grid((C / 2 + 127) / 128, gh, F);
@@ -1182,12 +1224,14 @@ int vdn_temporal_act(const void* in, long long ld_in, const float* w, int taps, 
   const long long warps = (long long)T * H;
   const int blocks = (int)((warps * 32 + 255) / 256);
   auto s = reinterpret_cast<cudaStream_t>(stream);
+  auto launch = [&](auto kernel) {
+    kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, taps, F, T, H, l2norm,
+                                  reinterpret_cast<__nv_bfloat16*>(out));
+  };
   if (D == 128)
-    temporal_act_kernel<128><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, taps, F,
-                                                     T, H, l2norm, reinterpret_cast<__nv_bfloat16*>(out));
+    launch(taps == 5 ? temporal_act_kernel<128, 5> : taps == 3 ? temporal_act_kernel<128, 3> : temporal_act_kernel<128, 1>);
   else
-    temporal_act_kernel<64><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(in), ld_in, w, taps, F, T,
-                                                    H, l2norm, reinterpret_cast<__nv_bfloat16*>(out));
+    launch(taps == 5 ? temporal_act_kernel<64, 5> : taps == 3 ? temporal_act_kernel<64, 3> : temporal_act_kernel<64, 1>);
   vdn::count_launch();
   return vdn::launch_status();
 }

@@ -87,24 +87,29 @@ inline int sm_count() {
   return n[dev] > 0 ? n[dev] : 148;
 }
 
-// Opt `kernel` in to `bytes` of dynamic shared memory on the current device.  The attribute
-// belongs to the device that is current at the call, so each (kernel, device, size) is set
-// once per process -- a process driving several GPUs opts every one of them in -- under a
-// lock, since entry points may be called from several host threads.  False if CUDA refused.
-inline bool smem_optin(const void* kernel, int bytes) {
+// Set a function attribute of `kernel` on the current device (smem_optin: `bytes` of dynamic
+// shared memory).  The attribute belongs to the device that is current at the call, so each
+// (kernel, device, attribute, value) is set once per process -- a process driving several
+// GPUs sets it on every one of them -- under a lock, since entry points may be called from
+// several host threads.  False if CUDA refused.
+inline bool func_attr(const void* kernel, cudaFuncAttribute attr, int value) {
   static std::mutex mu;
-  static std::set<std::tuple<const void*, int, int>> done;
+  static std::set<std::tuple<const void*, int, int, int>> done;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  const auto key = std::make_tuple(kernel, dev, bytes);
+  const auto key = std::make_tuple(kernel, dev, (int)attr, value);
   std::lock_guard<std::mutex> lock(mu);
   if (done.count(key)) return true;
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+  if (cudaFuncSetAttribute(kernel, attr, value) != cudaSuccess) {
     cudaGetLastError();  // the caller reports the failure; later calls must not see it again
     return false;
   }
   done.insert(key);
   return true;
+}
+
+inline bool smem_optin(const void* kernel, int bytes) {
+  return func_attr(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 // Kernel launches made by this library since it was loaded: every <<<>>> site is followed

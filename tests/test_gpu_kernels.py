@@ -499,8 +499,10 @@ def test_branch_readout_matches_oracle_with_and_without_text(D, grid, delta_rule
 ])
 def test_fused_conv_features_equal_the_two_kernel_path(F, grid, H, D, l2, pitch_mult):
     """vdn_conv_features (spatial 5x5 + temporal 5-tap + SiLU + L2 in one pass) against
-    vdn_spatial_conv followed by vdn_temporal_act on the same rows: the same arithmetic in the
-    same order, so equal up to the contraction of the L2 sum's multiply-adds."""
+    vdn_spatial_conv followed by vdn_temporal_act on the same rows: the same arithmetic, but
+    the two kernels add a spatial output's 25 products in different orders, so a spatial
+    output now and then rounds to the neighbouring bf16 value, and the features it feeds
+    differ by about that much."""
     g = torch.Generator().manual_seed(F * 100 + D)
     gh, gw = grid
     tpf = gh * gw
@@ -521,9 +523,10 @@ def test_fused_conv_features_equal_the_two_kernel_path(F, grid, H, D, l2, pitch_
     torch.cuda.synchronize()
     assert torch.isfinite(one.float()).all()
     diff = (one.float() - two.float()).abs()
-    # every element within one bf16 step of the two-kernel path, nearly all of them equal
-    assert float((diff / two.float().abs().clamp_min(1e-3)).max()) <= 2 ** -7
-    assert float((diff > 0).float().mean()) < 1e-3
+    # nearly all elements equal; the rest differ by the rounding of a spatial output
+    assert rel_l2(one, two.float()) < 1e-3
+    assert float(diff.max()) <= 2 ** -6 * float(two.float().abs().max())
+    assert float((diff > 0).float().mean()) < 1e-2
     want = vo.conv_features(x.float().cpu().reshape(rows, H, D), w_sp.cpu().reshape(C, 1, 5, 5),
                             w_tm.cpu().reshape(C, 1, 5), F, grid, l2)
     assert rel_l2(one, want) < 1e-2
