@@ -19,8 +19,9 @@ block forward as its step.
 
 Kernel-only modes for profiling: ``--only attention [--heads n]`` (the window attention kernel
 on the config geometry), ``--only quantisers`` (the int8, ConvRot int8 and per-tensor e4m3
-activation quantisers on the config's branch rows, against the measured HBM bandwidth) and
-``--only gemms --precision bf16|int8|fp8 [--rows m]`` (the block's QKV projection GEMM).
+activation quantisers on the config's branch rows, against the measured HBM bandwidth),
+``--only gemms --precision bf16|int8|fp8 [--rows m]`` (the block's QKV projection GEMM) and
+``--only convs`` (the branch's spatial 5x5 and temporal 5-tap convs of the k features).
 """
 
 from __future__ import annotations
@@ -485,6 +486,53 @@ def run_gemms_only(args, c):
           flush=True)
 
 
+def run_convs_only(args, c):
+    """The branch's k-feature convolutions alone on the config's clip frames (frames - 2
+    frames of the grid, H*D channels): the depthwise 5x5 spatial conv reading the k columns of
+    a [rows, 3 H D] QKV buffer, then the 5-tap temporal conv + SiLU + L2 writing [F, H, T, D].
+    Each is timed by CUDA events over ``--steps`` launches and reported against its
+    algorithmic bytes (2 B read + 2 B written per element) and the measured HBM copy
+    bandwidth."""
+    from __graft_entry__ import load_package
+
+    pkg = load_package()
+    dev = torch.device("cuda", 0)
+    gh, gw = c["grid"]
+    F, H, D = c["frames"] - 2, c["heads"], c["dim"]
+    C, T = H * D, gh * gw
+    rows = F * T
+    g = torch.Generator().manual_seed(0)
+    qkv = torch.randn(rows, 3 * C, generator=g).to(dev, torch.bfloat16)
+    k = qkv[:, C:2 * C]
+    w_sp = (torch.randn(C, 25, generator=g) * 0.2).to(dev)
+    w_tm = (torch.randn(C, 5, generator=g) * 0.45).to(dev)
+    sp = torch.empty(rows, C, device=dev, dtype=torch.bfloat16)
+    feat = torch.empty(F, H, T, D, device=dev, dtype=torch.bfloat16)
+    s = pkg._lib.stream_handle(dev)
+    pk, src = peaks()
+    algo = rows * C * 4
+    for name, fn in (("spatial_conv5_tiled_kernel",
+                      lambda: pkg._lib.call("vdn_spatial_conv", k.data_ptr(), k.stride(0), w_sp.data_ptr(), 5, 5, F,
+                                            gh, gw, C, sp.data_ptr(), C, s)),
+                     ("temporal_act_kernel<128, 5>",
+                      lambda: pkg._lib.call("vdn_temporal_act", sp.data_ptr(), C, w_tm.data_ptr(), 5, F, T, H, D, 1,
+                                            feat.data_ptr(), s))):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / max(args.steps, 1)
+        gbs = algo / (ms * 1e-3) / 1e9
+        print(json.dumps({"kernel": name, "frames": F, "grid": [gh, gw], "channels": C, "ms": ms,
+                          "algorithmic_bytes": algo, "gbs": gbs, "frac_of_hbm": gbs / pk["hbm_gbs"],
+                          "peak_source": src}), flush=True)
+
+
 def run_dit_stack(args, c, world, rank, local):
     """Config 4: the denoiser forward stack of ``blocks`` DiT blocks (hybrid attention + GELU MLP,
     INT8 projections) over a CFG batch of 2 latent sequences; one step = one sampler step
@@ -627,7 +675,7 @@ def main():
     ap.add_argument("--impl", default="b200")
     ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["attention", "quantisers", "gemms"], default=None,
+    ap.add_argument("--only", choices=["attention", "quantisers", "gemms", "convs"], default=None,
                     help="run one kernel alone on the config geometry (profiling small cases)")
     ap.add_argument("--heads", type=int, default=None, help="override the head count (profiling small cases)")
     ap.add_argument("--rows", type=int, default=None, help="--only gemms: row count (profiling small cases)")
@@ -657,6 +705,9 @@ def main():
         return
     if args.only == "gemms":
         run_gemms_only(args, c)
+        return
+    if args.only == "convs":
+        run_convs_only(args, c)
         return
     if args.config == 4 and args.impl != "reference":
         run_dit_stack(args, c, world, rank, local)

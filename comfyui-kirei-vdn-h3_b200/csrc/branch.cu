@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(128) spatial_conv5_kernel(const __nv_bfloat16*
 // change rarely).  Each tile's input rows y0-2 .. y0+9 are staged in shared memory by
 // 16-byte cp.async copies, the zero padding (two columns left and right, rows outside the
 // frame) by the zero-filling form of the same copy, so the inner loop has no bounds
-// checks.  Several CTAs share an SM (three at the config-1 row width of 38), so the copies
+// checks.  Several CTAs share an SM (five at the config-1 row width of 22), so the copies
 // of some are in flight while the others compute.
 // Warp w computes output rows y0 + 2w, y0 + 2w + 1, lane l channels c0 + 2l, 2l + 1.  It
 // walks the staged columns left to right: the 6 rows of a column are read once and added
@@ -102,8 +102,9 @@ __global__ void __launch_bounds__(128) spatial_conv5_kernel(const __nv_bfloat16*
 // registers), and the output column that the column completes is stored.  Per output
 // that is 25 paired FMAs, 3 paired shared loads and one 4-byte store, against 5 loads and
 // 4 extra adds when each output gathers its own 5x5 window.  At config 1 (29 frames of
-// 22 x 38, 5120 channels) this runs in 279 us against 313 us for one warp per output row
-// gathering its window; 4 rows per warp (two-warp CTAs, fewer warps per SM) took 402 us.
+// 38 x 22, 5120 channels) this runs in 281 us against 329 us for one warp per output row
+// gathering its window; on the transposed 22 x 38 grid 4 rows per warp (two-warp CTAs,
+// fewer warps per SM) took 402 us against 279 us for 2.
 constexpr int kConvRows = 8;         // output rows per tile
 constexpr int kConvWarpRows = 2;     // output rows per warp
 constexpr int kConvCh = 64;          // channels per tile: two per lane
