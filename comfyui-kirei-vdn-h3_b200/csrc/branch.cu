@@ -23,12 +23,7 @@ namespace branch {
 // reciprocal (2 ulp; the result is rounded to bf16), in their flush-to-zero forms, which
 // skip the subnormal handling (a subnormal intermediate becomes 0); for x -> -inf the
 // denominator overflows to inf, its reciprocal is 0 and the product -0
-__device__ __forceinline__ float silu(float x) {
-  float e, r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-x * 1.4426950408889634f));
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
-  return x * r;
-}
+__device__ __forceinline__ float silu(float x) { return x * rcp_ftz(1.0f + ex2_ftz(-x * 1.4426950408889634f)); }
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 

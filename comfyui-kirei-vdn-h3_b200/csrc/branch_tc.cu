@@ -524,13 +524,21 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
           if (tok < T) {
 #pragma unroll
             for (int i = 0; i < 32; i += 8) {
+              // norm weights and gate biases of these 8 columns as two 16-byte loads each
+              const int v0 = c2 * 32 + i;
+              const float4 w0 = *reinterpret_cast<const float4*>(nw + v0);
+              const float4 w1 = *reinterpret_cast<const float4*>(nw + v0 + 4);
+              const float4 b0 = *reinterpret_cast<const float4*>(bias + v0);
+              const float4 b1 = *reinterpret_cast<const float4*>(bias + v0 + 4);
+              const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+              const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
               float o[8];
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
-                const int v = c2 * 32 + i + q;
-                const float nv = bf16_round(__uint_as_float(r[v]) * inv * nw[v]);
-                const float e = __expf(-(__uint_as_float(gr[i + q]) + bias[v]));
-                o[q] = __fdividef(nv, 1.0f + e);  // nv * sigmoid(g + b)
+                const float nv = bf16_round(__uint_as_float(r[v0 + q]) * inv * wv[q]);
+                // nv * sigmoid(g + b) = nv / (1 + 2^(-(g + b) log2 e))
+                const float e = ex2_ftz(-(__uint_as_float(gr[i + q]) + bv[q]) * 1.4426950408889634f);
+                o[q] = nv * rcp_ftz(1.0f + e);
               }
               uint4 pk;
               pk.x = pack_bf16(o[0], o[1]);
@@ -814,8 +822,8 @@ int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, cons
     return vdn::kBadArgument;
   if (F <= 0 || f0 < 0 || F_all < f0 + F) return vdn::kBadArgument;
   if ((ld_out * 2) % 16 || !vdn::aligned16(out) || !vdn::aligned16(prefix) || !vdn::aligned16(suffix) ||
-      (s0 && !vdn::aligned16(s0)))
-    return vdn::kMisaligned;  // 16-byte output vectors, float4 state loads
+      (s0 && !vdn::aligned16(s0)) || !vdn::aligned16(norm_w) || !vdn::aligned16(og_bias))
+    return vdn::kMisaligned;  // 16-byte output vectors, float4 state, norm-weight and bias loads
   CUtensorMap tq, tg, tw;
   int rc = vdn::make_tmap_2d(&tq, Q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, (uint64_t)F * H * T, D, 64, 128);
   if (rc) return rc;

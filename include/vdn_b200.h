@@ -220,6 +220,7 @@ int vdn_readout(const void* Q, int F, int H, int T, int D, const float* prefix, 
  * the output-gate up-projection G = og_down og_up^T as tcgen05 MMAs, then RMSNorm(D) x norm_w x
  * sigmoid(G + og_bias) into out[out_row0 + f*T + s, h*128 + v].  og_down [F*T, 128] bf16,
  * og_up [H*128, 128] bf16.  Frames f0 .. f0+F-1 of a clip of F_all, as in vdn_readout.
+ * out, prefix, suffix, s0, norm_w and og_bias must be 16-byte aligned (kMisaligned otherwise).
  * Replaces: branch.py:345-396, :494-530, :754-758, :780. */
 int vdn_readout_tc(const void* Q, int F, int H, int T, const float* prefix, const float* suffix,
                    const float* alpha, const float* s0, const int* lo, const int* hi, int use_alpha,
