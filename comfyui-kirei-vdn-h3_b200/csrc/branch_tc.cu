@@ -592,6 +592,8 @@ __global__ void __launch_bounds__(kScanThreads, 1)
                    const float* __restrict__ alpha, const float* __restrict__ s0, int F, int F_inv, int H,
                    float inj_scale, float* __restrict__ prefix, float* __restrict__ suffix, int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // per row warp, double-buffered by step: the current frame's alpha row
+  __shared__ __align__(16) float alpha_s[4][2][D];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + ScanSmem::kBar);
   uint64_t* inv_full = bar;       // [2]
@@ -679,12 +681,17 @@ __global__ void __launch_bounds__(kScanThreads, 1)
 #pragma unroll
         for (int q = 0; q < 4; ++q) asm volatile("prefetch.global.L2 [%0];" ::"l"(nb + q * 32));
       }
+      // the frame's alpha row, a 16-byte piece per lane, is loaded before the wait too and
+      // shared through this warp's own row of alpha_s after it (warp-synchronous only)
+      const float4 a_piece = __ldg(reinterpret_cast<const float4*>(alpha + ((long long)t * H + h) * D) + lane);
       if (step > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(mma_done), (step - 1) & 1, abort_flag, err, kErrWaitOther));
         if (!ok) break;
         tc_fence_after();
       }
-      const float* al = alpha + ((long long)t * H + h) * D;
+      float* al = alpha_s[warp][step & 1];
+      reinterpret_cast<float4*>(al)[lane] = a_piece;
+      __syncwarp();
       float* prev = step > 0 ? dst_all + (((long long)frame(step - 1) * H + h) * D + i) * D : nullptr;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
