@@ -89,17 +89,19 @@ __global__ void __launch_bounds__(128) spatial_conv5_kernel(const __nv_bfloat16*
 // change rarely).  Each tile's input rows y0-2 .. y0+9 are staged in shared memory by
 // 16-byte cp.async copies, the zero padding (two columns left and right, rows outside the
 // frame) by the zero-filling form of the same copy, so the inner loop has no bounds
-// checks.  Several CTAs share an SM (five at the config-1 row width of 22), so the copies
-// of some are in flight while the others compute.
+// checks.  Several CTAs share an SM (four at config 1, where registers rather than the
+// 40 KB buffers set the count), so the copies of some are in flight while the others
+// compute.
 // Warp w computes output rows y0 + 2w, y0 + 2w + 1, lane l channels c0 + 2l, 2l + 1.  It
 // walks the staged columns left to right: the 6 rows of a column are read once and added
 // into every output they feed (2 rows x 5 columns of running paired-fp32 sums in
 // registers), and the output column that the column completes is stored.  Per output
 // that is 25 paired FMAs, 3 paired shared loads and one 4-byte store, against 5 loads and
 // 4 extra adds when each output gathers its own 5x5 window.  At config 1 (29 frames of
-// 38 x 22, 5120 channels) this runs in 281 us against 329 us for one warp per output row
-// gathering its window; on the transposed 22 x 38 grid 4 rows per warp (two-warp CTAs,
-// fewer warps per SM) took 402 us against 279 us for 2.
+// 38 x 22, 5120 channels) this runs in 253 us against 329 us for one warp per output row
+// gathering its window (281 us with a staging loop that recomputed each copy's row and
+// column); on the transposed 22 x 38 grid 4 rows per warp (two-warp CTAs, fewer warps per
+// SM) took 402 us against 279 us for 2.
 constexpr int kConvRows = 8;         // output rows per tile
 constexpr int kConvWarpRows = 2;     // output rows per warp
 constexpr int kConvCh = 64;          // channels per tile: two per lane
@@ -119,31 +121,31 @@ __global__ void __launch_bounds__(kConvThreads, kConvMaxCtas)
   const int per_slab = F * bands;
   const int n_tiles = (C / kConvCh) * per_slab;
   const int pitch = gw + 4;  // shared-memory columns per row: image column x sits at x + 2
-  const int n_px = (kConvRows + 4) * pitch;
   const int t0 = (int)((long long)blockIdx.x * n_tiles / gridDim.x);
   const int t1 = (int)((long long)(blockIdx.x + 1) * n_tiles / gridDim.x);
   if (t0 >= t1) return;
 
-  // Thread tid copies the 16-byte chunk q = tid % 8 (8 channels) of the staged pixels
-  // tid / 8, tid / 8 + kPxStep, ...; the pixel's row and column advance without a division.
-  constexpr int kPxStep = kConvThreads / 8;
-  const int q = tid & 7, px0 = tid >> 3;
-  const int row0 = px0 / pitch, col0 = px0 - row0 * pitch;
+  // Thread tid copies the (staged column, 16-byte chunk of 8 channels) pairs p = tid,
+  // tid + kConvThreads, ... < pitch * 8, each down all kConvRows + 4 staged rows: per copy
+  // only the row's bounds bit and one address step change.
+  const long long row_pitch = (long long)gw * ld_in;  // one image row down
   auto issue = [&](int t) {
     const int slab = t / per_slab, r = t - slab * per_slab;
     const int f = r / bands, y0 = (r - f * bands) * kConvRows;
-    const __nv_bfloat16* src = in + (long long)f * gh * gw * ld_in + slab * kConvCh + q * 8;
-    int row = row0, col = col0;
-    uint32_t dst = smem_u32(conv_smem + px0 * kConvCh + q * 8);
-    for (int px = px0; px < n_px; px += kPxStep, dst += kPxStep * kConvCh * 2) {
-      const int yy = y0 - 2 + row, xx = col - 2;
-      const bool inside = yy >= 0 && yy < gh && xx >= 0 && xx < gw;
-      // padding positions read nothing (zero fill) from the frame's first pixel
-      cp_async16_zfill(dst, inside ? src + (long long)(yy * gw + xx) * ld_in : src, inside ? 16u : 0u);
-      col += kPxStep;
-      while (col >= pitch) {
-        col -= pitch;
-        ++row;
+    const __nv_bfloat16* frame = in + (long long)f * gh * gw * ld_in + slab * kConvCh;
+    uint32_t rows_in = 0;  // bit i: staged row i lies inside the frame (the same for every thread)
+#pragma unroll
+    for (int i = 0; i < kConvRows + 4; ++i) rows_in |= (y0 - 2 + i >= 0 && y0 - 2 + i < gh) ? 1u << i : 0u;
+    for (int p = tid; p < pitch * 8; p += kConvThreads) {
+      const int col = p >> 3, q = p & 7, xx = col - 2;
+      const bool col_in = xx >= 0 && xx < gw;
+      const __nv_bfloat16* src = frame + ((long long)(y0 - 2) * gw + xx) * ld_in + q * 8;
+      uint32_t dst = smem_u32(conv_smem + col * kConvCh + q * 8);
+#pragma unroll 4
+      for (int i = 0; i < kConvRows + 4; ++i, src += row_pitch, dst += pitch * kConvCh * 2) {
+        const bool inside = col_in && ((rows_in >> i) & 1u);
+        // padding positions read nothing (zero fill) from the frame's first pixel
+        cp_async16_zfill(dst, inside ? src : frame, inside ? 16u : 0u);
       }
     }
     cp_async_commit();
