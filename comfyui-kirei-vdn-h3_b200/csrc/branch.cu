@@ -342,7 +342,9 @@ __global__ void __launch_bounds__(256, 3) temporal_act_kernel(const __nv_bfloat1
       if (l2) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-6f);
+        // 1 / max(|y|, 1e-6) = rsqrt(max(|y|^2, 1e-12)), by the hardware's approximate
+        // reciprocal square root (2 ulp, far below the bf16 rounding of the output)
+        const float inv = rsqrt_ftz(fmaxf(ss, 1e-12f));
 #pragma unroll
         for (int p = 0; p < NP; ++p) y[p] = make_float2(y[p].x * inv, y[p].y * inv);
       }

@@ -274,6 +274,11 @@ __device__ __forceinline__ float rcp_ftz(float x) {
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+__device__ __forceinline__ float rsqrt_ftz(float x) {
+  float y;
+  asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // Ampere-style asynchronous 16-byte global -> shared copies (no TMA descriptor needed).
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
