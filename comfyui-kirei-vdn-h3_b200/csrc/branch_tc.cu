@@ -139,10 +139,22 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
     const int r = tid - 64;
     int g = 0;
     bool ok = true;
+    // this thread's token logit of a chunk (0 for rows past the frame, which read nothing);
+    // the next chunk's is loaded one chunk ahead, so its latency hides behind the waits
+    auto logit_of = [&](int unit, int c) -> float {
+      const int s = c * kRows + r;
+      if (s >= T) return 0.f;
+      return beta_logits[((long long)(unit / H) * T + s) * ld_beta + beta_col0 + unit % H];
+    };
+    float logit_next = u0 < u1 ? logit_of(u0, 0) : 0.f;
     for (int unit = u0; unit < u1 && ok; ++unit) {
-      const int f = unit / H, h = unit % H;
       for (int c = 0; c < nch; ++c, ++g) {
         const int st = g & 1;
+        const float logit = logit_next;
+        if (c + 1 < nch)
+          logit_next = logit_of(unit, c + 1);
+        else if (unit + 1 < u1)
+          logit_next = logit_of(unit + 1, 0);
         // K/V of this chunk landed, and the MMA that read this beta-K buffer two chunks ago is done
         const bool okw = __all_sync(0xffffffffu,
                                     mbar_wait(smem_u32(&kv_full[st]), (g >> 1) & 1, abort_flag, err, kErrWaitOther) &&
@@ -160,7 +172,7 @@ __global__ void __launch_bounds__(kStatsThreads, 1)
         // tiles (a zero beta alone would still carry a non-finite token of the next unit into
         // this unit's sums as 0 * inf), so each frame's statistics see only its own tokens.
         const bool past = s >= T;
-        const float beta = past ? 0.f : sigm(beta_logits[((long long)f * T + s) * ld_beta + beta_col0 + h]);
+        const float beta = past ? 0.f : sigm(logit);
         const __nv_bfloat162 b2 = __floats2bfloat162_rn(beta, beta);
         for (int b = 0; b < 2; ++b) {
           const uint32_t off = b * kBlk + r * 128;
