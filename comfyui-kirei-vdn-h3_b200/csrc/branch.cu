@@ -731,7 +731,7 @@ __global__ void __launch_bounds__(256) spd_inverse_kernel(const float* __restric
         bad = k + 1;
         break;
       }
-      const float ip = 1.0f / p;
+      const float ip = __frcp_rn(p);  // the correctly rounded 1 / p
       float a_i[TB], b_j[TB];
 #pragma unroll
       for (int i = 0; i < TB; ++i) a_i[i] = colk[pb][r0 + i] * ip;
