@@ -245,12 +245,14 @@ __global__ void spatial_conv_kernel(const __nv_bfloat16* __restrict__ in, long l
 // ---------------------------------------------------------------------------------
 // 2. Temporal conv + SiLU + optional L2, output FHSD [F, H, T, D] bf16.
 // One warp per (token s, head h); lane l holds channels h*D + l*D/32 .. +D/32 as fp32
-// pairs.  The warp walks the frames in chunks of 8 outputs: a chunk first loads the 8
-// input frames it brings into the window (one 8-byte load per lane and frame for D = 128,
-// all in flight at once), then for each output unpacks one frame into a sliding window
-// of 5 and runs the 5-tap conv (paired FMAs), SiLU and the L2 norm (a warp reduction)
-// from registers, so every input frame is unpacked once.  taps 0 (no temporal conv), 1
-// and 3 run with a window of 1 or 3.
+// pairs.  The warp walks the frames keeping the next 4 input frames in flight (one 8-byte
+// load per lane and frame for D = 128): each output unpacks one of them into a sliding
+// window of 5, reloads its slot with the frame 4 outputs ahead, and runs the 5-tap conv
+// (paired FMAs), SiLU and the L2 norm (a warp reduction) from registers, so every input
+// frame is unpacked once.  taps 0 (no temporal conv), 1 and 3 run with a window of 1 or 3.
+// Config 1 (k, 5 taps + L2): 136 us with 4 frames in flight, 142 / 152 us with 3 / 2, 177 us
+// with 8 (which spills at this register budget); loading 8 frames per 8-output chunk only
+// after the previous chunk took 152 us.
 // ---------------------------------------------------------------------------------
 template <int V>
 struct PackedBf16;
@@ -280,7 +282,7 @@ __global__ void __launch_bounds__(256, 3) temporal_act_kernel(const __nv_bfloat1
                                                            int H, int l2, __nv_bfloat16* __restrict__ out) {
   constexpr int V = D / 32;    // channels per lane
   constexpr int NP = V / 2;    // fp32 pairs per lane
-  constexpr int kChunk = 8;    // outputs per chunk = frames loaded per chunk
+  constexpr int kChunk = 4;    // input frames in flight (the unroll of the output loop)
   constexpr int kPad = TAPS / 2;
   using P = PackedBf16<V>;
   const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -311,10 +313,12 @@ __global__ void __launch_bounds__(256, 3) temporal_act_kernel(const __nv_bfloat1
   float2 win[TAPS][NP];
 #pragma unroll
   for (int j = 1; j < TAPS; ++j) P::unpack2(load(j - kPad - 1), win[j]);
-  for (int t0 = 0; t0 < F; t0 += kChunk) {
-    typename P::T raw[kChunk];  // the frames entering the window in this chunk
+  // raw[i]: the frame entering the window at output t0 + i; once unpacked, its slot is
+  // refilled with the frame output t0 + i + kChunk needs, so loads stay in flight throughout
+  typename P::T raw[kChunk];
 #pragma unroll
-    for (int i = 0; i < kChunk; ++i) raw[i] = load(t0 + i + kPad);
+  for (int i = 0; i < kChunk; ++i) raw[i] = load(i + kPad);
+  for (int t0 = 0; t0 < F; t0 += kChunk) {
 #pragma unroll
     for (int i = 0; i < kChunk; ++i) {
       const int t = t0 + i;
@@ -324,6 +328,7 @@ __global__ void __launch_bounds__(256, 3) temporal_act_kernel(const __nv_bfloat1
 #pragma unroll
         for (int p = 0; p < NP; ++p) win[j][p] = win[j + 1][p];
       P::unpack2(raw[i], win[TAPS - 1]);
+      raw[i] = load(t + kChunk + kPad);
       float2 y[NP];
 #pragma unroll
       for (int p = 0; p < NP; ++p) y[p] = fma2(wt[0][p], win[0][p], make_float2(0.f, 0.f));
