@@ -257,7 +257,7 @@ TILE_HALO = 2  # frames each side: the 5-tap temporal conv's reach (runtime.py:4
 # Short conv features in one kernel (vdn_conv_features) where its geometry allows.  Off: on
 # the config-1 clip (38 x 22 frames, H = 40) the fused kernel, bound by its one-frame-deep
 # prefetch and one 256-thread CTA per SM, measured 1.78 ms per forward for k and v against
-# 1.03 ms for the spatial + temporal pair (0.89 ms since their rewrite), which keep more
+# 1.03 ms for the spatial + temporal pair (0.78 ms since their rewrite), which keep more
 # warps busy per SM.
 FUSED_CONV = False
 
