@@ -550,7 +550,7 @@ __global__ void __launch_bounds__(FeatLayout<D>::kThreads, 1)
 #pragma unroll
               // the remaining steps inside the warp (lane pairs share a value at D = 128)
               for (int o = 16; o >= (D == 128 ? 2 : 1); o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-              const float inv = 1.0f / fmaxf(sqrtf(s), 1e-6f);
+              const float inv = rsqrt_ftz(fmaxf(s, 1e-12f));  // as temporal_act_kernel
               y[x].x *= inv;
               y[x].y *= inv;
             }
