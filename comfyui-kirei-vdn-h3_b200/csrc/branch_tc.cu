@@ -597,6 +597,7 @@ struct ScanSmem {
   static constexpr int kBytes = kBar + 256 + 1024;
 };
 constexpr int kScanThreads = 160;
+constexpr int kXPitch = 36;  // floats per row of the scan's transpose tiles
 
 template <bool kSana>
 __global__ void __launch_bounds__(kScanThreads, 1)
@@ -606,6 +607,10 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // per row warp, double-buffered by step: the current frame's alpha row
   __shared__ __align__(16) float alpha_s[4][2][D];
+  // per row warp: a 32 x 32 fp32 tile (rows padded to kXPitch floats, so the 16-byte accesses
+  // of a quarter warp hit distinct banks whether it walks a row or a column of rows) that
+  // turns coalesced B pieces into thread rows and thread rows into coalesced state pieces
+  __shared__ __align__(16) float xpose[4][32][kXPitch];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + ScanSmem::kBar);
   uint64_t* inv_full = bar;       // [2]
@@ -683,11 +688,19 @@ __global__ void __launch_bounds__(kScanThreads, 1)
       // this frame's B row (kSana: the previous frame's) does not depend on the previous state:
       // it is in registers before the wait for the previous step's MMA, off the dependent
       // chain of the recurrence
-      const float* brow = Bm + (((long long)(kSana ? frame(step > 0 ? step - 1 : 0) : t) * H + h) * D + i) * D;
-      float4 bv[D / 4];
+      // Loaded coalesced: for chunk c (columns 32c ..) lane l holds columns 32c + 4 (l % 8) .. +3
+      // of the warp's rows 4k + l / 8 (k < 8), so each load instruction reads four whole
+      // 128-byte row pieces; the warp's xpose tile turns them into this thread's own row.
+      const float* bmat = Bm + ((long long)(kSana ? frame(step > 0 ? step - 1 : 0) : t) * H + h) * D * D;
+      const int prow = warp * 32 + (lane >> 3), pcol = (lane & 7) * 4;
+      float4 bv[D / 32][8];
 #pragma unroll
-      for (int q = 0; q < D / 4; ++q)
-        bv[q] = (kSana && step == 0) ? make_float4(0.f, 0.f, 0.f, 0.f) : __ldg(reinterpret_cast<const float4*>(brow) + q);
+      for (int c = 0; c < D / 32; ++c)
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          bv[c][k] = (kSana && step == 0) ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                          : __ldg(reinterpret_cast<const float4*>(bmat + (long long)(prow + 4 * k) * D +
+                                                                                  c * 32 + pcol));
       if (step + 1 < F) {  // the next frame's B row into L2 meanwhile
         const float* nb = Bm + (((long long)frame(step + 1) * H + h) * D + i) * D;
 #pragma unroll
@@ -704,9 +717,19 @@ __global__ void __launch_bounds__(kScanThreads, 1)
       float* al = alpha_s[warp][step & 1];
       reinterpret_cast<float4*>(al)[lane] = a_piece;
       __syncwarp();
-      float* prev = step > 0 ? dst_all + (((long long)frame(step - 1) * H + h) * D + i) * D : nullptr;
+      // the previous frame's state goes out by the same tile, as whole 128-byte row pieces
+      float* prev = step > 0 ? dst_all + ((long long)frame(step - 1) * H + h) * D * D : nullptr;
+      float* xt = &xpose[warp][0][0];
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
+        // this chunk of B: the lanes' pieces into the tile, then this thread's row out of it
+#pragma unroll
+        for (int k = 0; k < 8; ++k) *reinterpret_cast<float4*>(xt + (4 * k + (lane >> 3)) * kXPitch + pcol) = bv[c][k];
+        __syncwarp();
+        float4 bq[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) bq[q] = *reinterpret_cast<const float4*>(xt + lane * kXPitch + 4 * q);
+        __syncwarp();
         float sv[32];
         if (step == 0) {
 #pragma unroll
@@ -720,23 +743,30 @@ __global__ void __launch_bounds__(kScanThreads, 1)
           if (kSana) {
 #pragma unroll
             for (int q = 0; q < 32; q += 4) {
-              const float4 b4 = bv[(c * 32 + q) / 4];
+              const float4 b4 = bq[q / 4];
               sv[q] = fmaf(inj_scale, b4.x, sv[q]);
               sv[q + 1] = fmaf(inj_scale, b4.y, sv[q + 1]);
               sv[q + 2] = fmaf(inj_scale, b4.z, sv[q + 2]);
               sv[q + 3] = fmaf(inj_scale, b4.w, sv[q + 3]);
             }
           }
+          // this thread's row into the tile, then whole row pieces out to the previous frame
 #pragma unroll
           for (int q = 0; q < 32; q += 4)
-            *reinterpret_cast<float4*>(prev + c * 32 + q) = make_float4(sv[q], sv[q + 1], sv[q + 2], sv[q + 3]);
+            *reinterpret_cast<float4*>(xt + lane * kXPitch + q) = make_float4(sv[q], sv[q + 1], sv[q + 2], sv[q + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            *reinterpret_cast<float4*>(prev + (long long)(prow + 4 * k) * D + c * 32 + pcol) =
+                *reinterpret_cast<const float4*>(xt + (4 * k + (lane >> 3)) * kXPitch + pcol);
+          __syncwarp();
         }
         // u = B + s o alpha, split into bf16 hi + lo, written K-major swizzled (8 values per 16 B)
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {
           const int k0 = c * 32 + q8 * 8;
-          const float4 b0 = bv[k0 / 4];
-          const float4 b1 = bv[k0 / 4 + 1];
+          const float4 b0 = bq[q8 * 2];
+          const float4 b1 = bq[q8 * 2 + 1];
           const float4 a0 = *reinterpret_cast<const float4*>(al + k0);
           const float4 a1 = *reinterpret_cast<const float4*>(al + k0 + 4);
           const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
