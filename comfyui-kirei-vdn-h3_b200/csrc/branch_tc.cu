@@ -591,7 +591,9 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
 // vdn_sana_factor) and the injection is added after the product,
 //     u = s o alpha_t,   s = u M_t + inj_scale B_t,
 // so the B row a thread needs at step t is that of the frame whose product it reads back.
-// smem: 2 stages x (inv hi, inv lo) + (u hi, u lo) = 6 x 32 KB.
+// smem: 2 stages x (inv hi, inv lo) + (u hi, u lo) = 6 x 32 KB dynamic, plus 22 KB static per
+// CTA: each state warp's alpha row (double-buffered) and its 32 x 32 transpose tile, through
+// which the B rows arrive and the state rows leave as whole 128-byte row pieces.
 struct ScanSmem {
   static constexpr int kInv = 0, kU = 4 * kTile, kBar = 6 * kTile;
   static constexpr int kBytes = kBar + 256 + 1024;
